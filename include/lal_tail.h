@@ -1,0 +1,197 @@
+/*
+ * lal_tail.h -- C ABI of liblal_tail.so, the B200 (sm_100a) decode tail of LAL.
+ *
+ * The decode tail is the end of every forward() in the LAL servers
+ * (tools/server/qwen7b_server.c:819-851): quantize the final hidden vector to
+ * int8, contract it with the per-row-scaled int8 LM head, apply the
+ * repetition penalty, then top-k select, softmax with temperature, draw.
+ *
+ * Two layers are exported, both plain C: host pointers, sizes, int status.
+ *
+ *  1. Drop-ins.  The functions the reference defines as static inline in
+ *     runtime/lal_q8_kernel.h and runtime/lal_sampling.h, with the same names
+ *     and signatures, computed on the GPU (declared in include/runtime/, the
+ *     drop-in copies of those headers), and their status-returning lal_tail_*
+ *     forms below.  Host pointers in and out; the sampler mutates logits in
+ *     place and consumes glibc rand() exactly where the reference does.  The
+ *     reference-named forms have no error channel (the originals return void
+ *     or a token): on failure they print the reason to stderr and abort().
+ *     There is no CPU fallback.
+ *
+ *  2. The fused decode tail (lal_tail_*): one context per GPU holding its
+ *     vocab slice of the LM head in HBM, the per-stream penalty histories and
+ *     sampling parameters; lal_tail_step() takes B hidden vectors and B draws
+ *     and returns B token ids, in one kernel per step.  Multi-GPU contexts
+ *     each own a contiguous vocab slice and merge the per-slice top-k
+ *     candidates across GPUs.
+ *
+ * Every lal_tail_* function returns LAL_TAIL_OK (0) or an error code;
+ * lal_tail_last_error() gives the calling thread's last message.
+ */
+#ifndef LAL_TAIL_H
+#define LAL_TAIL_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LAL_TAIL_OK              0
+#define LAL_TAIL_ERR_ARG         1   /* bad argument or size                  */
+#define LAL_TAIL_ERR_CUDA        2   /* CUDA runtime error                    */
+#define LAL_TAIL_ERR_NOMEM       3   /* device or pinned allocation failed    */
+#define LAL_TAIL_ERR_TIMEOUT     4   /* a bounded device wait ran out         */
+#define LAL_TAIL_ERR_CAPACITY    5   /* tie set or list above the built limit */
+#define LAL_TAIL_ERR_STATE       6   /* call out of order (e.g. no LM head)   */
+#define LAL_TAIL_ERR_COMM        7   /* multi-GPU exchange failed             */
+#define LAL_TAIL_ERR_UNSUPPORTED 8   /* shape outside what the kernels handle */
+
+/* Sampler semantics.  LIBRARY = runtime/lal_sampling.h:46-125 (greedy check
+ * before the penalty).  SERVER = tools/server/qwen7b_server.c:219-295
+ * (penalty first, k clamped to [1,V], argmax fallback when the kept softmax
+ * mass is not positive). */
+#define LAL_SAMPLER_LIBRARY 0
+#define LAL_SAMPLER_SERVER  1
+
+/* The calling thread's last error message ("" if none). */
+const char *lal_tail_last_error(void);
+/* Library version and build string. */
+const char *lal_tail_version(void);
+
+/* ======================================================================
+ * 1. Status-returning forms of the drop-ins
+ *
+ * The functions with the reference's own names (lal_quantize_x_int8,
+ * lal_lm_head_int8_range, lal_sample_token, ...) are exported by the same
+ * library and declared in include/runtime/lal_q8_kernel.h and
+ * include/runtime/lal_sampling.h, the drop-in copies of the reference
+ * headers.  This header declares only lal_tail_* names, so it can be
+ * included next to the reference's original headers.
+ * ====================================================================== */
+
+
+/* Level-2 filter hook types (tools/server/qwen7b_server.c:175-186). */
+typedef int (*lal_token_decode_fn)(int token_id, char *out_buf, int max_len);
+typedef int (*lal_filter_topk_fn)(int *keep_mask, int n_vocab, int last_token,
+                                  const int *recent_tokens, int n_recent,
+                                  lal_token_decode_fn decode_fn);
+/* A draw source: returns u = (float)rand()/(float)RAND_MAX or equivalent. */
+typedef float (*lal_draw_fn)(void *ctx);
+
+int lal_tail_quantize_x_int8(const float *x, int8_t *xq, int n, float *scale_out);
+int lal_tail_compute_abs_xq(const int8_t *xq, uint8_t *ax, int n);
+int lal_tail_lm_head_int8_range(float *logits, const int8_t *xq, float scale_x,
+                                const int8_t *wte_q, const float *scale_w,
+                                int v_start, int v_end, int n_embd);
+int lal_tail_quantize_q8_per_row(const float *W, int8_t *q8_T, float *scale,
+                                 int in_dim, int out_dim);
+/* lal_sample_token with the draw u supplied (used only on the non-greedy
+ * path).  Writes the token to *token_out and mutates logits like the
+ * reference. */
+int lal_tail_sample_token(float *logits, int vocab_size, float temperature,
+                          int top_k, float rep_penalty, const int *recent,
+                          int n_recent, float u, int *token_out);
+/* tools/server/qwen7b_server.c:219-295 (lal_sample_token_filtered), with the
+ * level-2 filter hook: filter (may be NULL) sees the top-k keep_mask on the
+ * host; draw() is called exactly where the reference calls rand() (only when
+ * the kept softmax mass is positive).  decode is handed to the filter. */
+int lal_tail_sample_token_filtered(float *logits, int vocab_size, float temperature,
+                                   int top_k, float rep_penalty, const int *recent,
+                                   int n_recent, lal_filter_topk_fn filter,
+                                   lal_token_decode_fn decode, lal_draw_fn draw,
+                                   void *draw_ctx, int *token_out);
+/* Register (copy to the device) or drop a host LM head used by the range
+ * drop-ins.  Registration is optional: first use registers on demand. */
+int lal_tail_lm_head_register(const int8_t *wte_q, const float *scale_w,
+                              int vocab_size, int n_embd);
+int lal_tail_lm_head_forget(const int8_t *wte_q);
+
+/* ======================================================================
+ * 2. Fused decode tail
+ * ====================================================================== */
+
+typedef struct lal_tail lal_tail;
+
+typedef struct {
+    int vocab_size;    /* V: the whole vocabulary (all slices)              */
+    int n_embd;        /* d                                                 */
+    int max_streams;   /* B capacity                                        */
+    int max_top_k;     /* largest top_k a step will use                     */
+    int history_cap;   /* per-stream penalty-history capacity (server: 256) */
+    int sampler;       /* LAL_SAMPLER_LIBRARY or LAL_SAMPLER_SERVER         */
+    int device;        /* CUDA device ordinal; -1 = the current device      */
+    int shard_rank;    /* this context owns vocab rows                      */
+    int shard_count;   /*   [rank*V/count, (rank+1)*V/count)                */
+} lal_tail_config;
+
+/* Per-stream outputs of the last step, for inspection and parity tests. */
+typedef struct {
+    float threshold;   /* k-th largest penalised logit                      */
+    float max_l;       /* softmax max, floored at -1e30f                    */
+    float sum;         /* sequential sum of the candidate weights           */
+    float r;           /* u * sum                                           */
+    int   n_cand;      /* candidates {v : l[v] >= threshold}                */
+    int   greedy;      /* 1 if the argmax path was taken                    */
+    int   drew;        /* 1 if the draw u was consumed                      */
+    int   token;
+} lal_tail_diag;
+
+int lal_tail_create(const lal_tail_config *cfg, lal_tail **out);
+int lal_tail_destroy(lal_tail *t);
+/* This context's vocab slice: first row and row count. */
+int lal_tail_shard_rows(const lal_tail *t, int *row0, int *n_rows);
+
+/* Load this slice of the LM head: int8 rows [n_rows, n_embd] + fp32 scales,
+ * from host memory. */
+int lal_tail_load_lm_head_q8(lal_tail *t, const int8_t *wte_q_rows,
+                             const float *scale_w_rows);
+/* Load this slice from fp32 rows and quantize it on the GPU exactly as
+ * lal_quantize_q8_per_row does (runtime/lal_q8_kernel.h:357-372).  rows may
+ * be given in chunks: [row_begin, row_begin + n) of the slice. */
+int lal_tail_load_lm_head_f32(lal_tail *t, const float *W_rows, int row_begin,
+                              int n_rows);
+/* Read back this slice's quantized LM head (n_rows x n_embd, and scales). */
+int lal_tail_read_lm_head(lal_tail *t, int8_t *wte_q_rows, float *scale_w_rows);
+
+/* Per-stream sampling parameters (host arrays of n_streams). */
+int lal_tail_set_sampling(lal_tail *t, int n_streams, const float *temperature,
+                          const int *top_k, const float *rep_penalty);
+/* Replace one stream's penalty history (oldest first; n <= history_cap). */
+int lal_tail_set_history(lal_tail *t, int stream, const int *recent, int n_recent);
+/* Read one stream's history, oldest first; *n_out receives its length. */
+int lal_tail_get_history(lal_tail *t, int stream, int *recent_out, int *n_out);
+
+/* One decode-tail step for n_streams streams.  hidden: host [n_streams,
+ * n_embd] fp32; u: host [n_streams] draws (read only for non-greedy
+ * streams); tokens_out: host [n_streams].  Each sampled token is appended to
+ * its stream's history (FIFO at history_cap, runtime/lal_sampling.h:133-136). */
+int lal_tail_step(lal_tail *t, const float *hidden, int n_streams, const float *u,
+                  int *tokens_out);
+/* The same with device pointers, enqueued on the context's stream without a
+ * host synchronisation (tokens land in d_tokens_out). */
+int lal_tail_step_device(lal_tail *t, const float *d_hidden, int n_streams,
+                         const float *d_u, int *d_tokens_out);
+/* Wait for the context's stream; returns a device-side error if one was
+ * recorded (e.g. LAL_TAIL_ERR_TIMEOUT). */
+int lal_tail_sync(lal_tail *t);
+/* Diagnostics and penalised logits (this slice's rows) of the last step. */
+int lal_tail_get_diag(lal_tail *t, int stream, lal_tail_diag *out);
+int lal_tail_get_logits(lal_tail *t, int stream, float *logits_rows);
+/* Device buffers of the context, for callers that keep inputs on the GPU. */
+int lal_tail_device_buffers(lal_tail *t, float **d_hidden, float **d_u,
+                            int **d_tokens);
+/* Turn on (1) or off (0) CUDA-event timing of each fused-kernel launch. */
+int lal_tail_set_timing(lal_tail *t, int on);
+/* Average duration in milliseconds of the fused kernel over the launches
+ * since the last call (CUDA events on the context's stream), and their
+ * count. */
+int lal_tail_kernel_time(lal_tail *t, double *avg_ms, int *n_launches);
+
+/* Glibc-exact expf as the device computes it (test hook). */
+int lal_tail_debug_expf(const float *x, float *y, int n);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* LAL_TAIL_H */

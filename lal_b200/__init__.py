@@ -1,0 +1,324 @@
+"""lal_b200 -- the LAL decode tail on B200 (sm_100a), Python host mirror.
+
+The product is ``lal_b200/liblal_tail.so`` (C ABI in ``include/lal_tail.h``).
+This module binds it with ctypes and mirrors the reference's interface for
+the path, with the reference's names:
+
+* ``quantize_x_int8``      runtime/lal_q8_kernel.h:375  lal_quantize_x_int8
+* ``compute_abs_xq``       runtime/lal_q8_kernel.h:450  lal_compute_abs_xq
+* ``lm_head_int8_range``   runtime/lal_q8_kernel.h:463  lal_lm_head_int8_range
+* ``quantize_q8_per_row``  runtime/lal_q8_kernel.h:357  lal_quantize_q8_per_row
+* ``sample_token``         runtime/lal_sampling.h:46    lal_sample_token
+* ``sample_token_filtered`` tools/server/qwen7b_server.c:219 (with the level-2
+  filter hook of qwen7b_server.c:175-186)
+* ``DecodeTail``           the fused tail replacing qwen7b_server.c:829-850
+
+Everything computes on the GPU.  There is no CPU fallback: importing works
+without a GPU (so the library can be inspected), but every compute call
+raises ``LalTailError`` when the CUDA library or a GPU is unavailable.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from typing import Callable, Optional, Sequence
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "liblal_tail.so")
+
+LAL_SAMPLER_LIBRARY = 0
+LAL_SAMPLER_SERVER = 1
+
+ERRORS = {0: "OK", 1: "ERR_ARG", 2: "ERR_CUDA", 3: "ERR_NOMEM", 4: "ERR_TIMEOUT",
+          5: "ERR_CAPACITY", 6: "ERR_STATE", 7: "ERR_COMM", 8: "ERR_UNSUPPORTED"}
+
+
+class LalTailError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"{ERRORS.get(code, code)}: {msg}")
+        self.code = code
+
+
+class TailConfig(C.Structure):
+    """Mirror of lal_tail_config."""
+    _fields_ = [("vocab_size", C.c_int), ("n_embd", C.c_int), ("max_streams", C.c_int),
+                ("max_top_k", C.c_int), ("history_cap", C.c_int), ("sampler", C.c_int),
+                ("device", C.c_int), ("shard_rank", C.c_int), ("shard_count", C.c_int)]
+
+
+class TailDiag(C.Structure):
+    """Mirror of lal_tail_diag."""
+    _fields_ = [("threshold", C.c_float), ("max_l", C.c_float), ("sum", C.c_float),
+                ("r", C.c_float), ("n_cand", C.c_int), ("greedy", C.c_int),
+                ("drew", C.c_int), ("token", C.c_int)]
+
+    def as_dict(self):
+        return {k: getattr(self, k) for k, _ in self._fields_}
+
+
+class RecentTokens(C.Structure):
+    """Mirror of LalRecentTokens (runtime/lal_sampling.h:128-131)."""
+    _fields_ = [("tokens", C.c_int * 256), ("n", C.c_int)]
+
+
+DECODE_FN = C.CFUNCTYPE(C.c_int, C.c_int, C.c_char_p, C.c_int)
+FILTER_FN = C.CFUNCTYPE(C.c_int, C.POINTER(C.c_int), C.c_int, C.c_int,
+                        C.POINTER(C.c_int), C.c_int, DECODE_FN)
+DRAW_FN = C.CFUNCTYPE(C.c_float, C.c_void_p)
+
+_f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
+_i8p = np.ctypeslib.ndpointer(np.int8, flags="C_CONTIGUOUS")
+_u8p = np.ctypeslib.ndpointer(np.uint8, flags="C_CONTIGUOUS")
+_i32p = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
+_vp = C.c_void_p
+_ip = C.c_int
+_fp = C.c_float
+
+# name -> (restype, argtypes); every symbol of include/lal_tail.h
+SIGNATURES = {
+    "lal_tail_last_error": (C.c_char_p, []),
+    "lal_tail_version": (C.c_char_p, []),
+    "lal_quantize_x_int8": (C.c_float, [_f32p, _i8p, _ip]),
+    "lal_compute_abs_xq": (None, [_i8p, _u8p, _ip]),
+    "lal_lm_head_int8_range": (None, [_f32p, _i8p, _fp, _i8p, _f32p, _ip, _ip, _ip]),
+    "lal_lm_head_int8_range_abs": (None, [_f32p, _i8p, _u8p, _fp, _i8p, _f32p, _ip, _ip, _ip]),
+    "lal_lm_head_int8_range_abs_8row": (None, [_f32p, _i8p, _u8p, _fp, _i8p, _f32p, _ip, _ip,
+                                               _ip]),
+    "lal_quantize_q8_per_row": (None, [_f32p, _i8p, _f32p, _ip, _ip]),
+    "lal_sample_token": (C.c_int, [_f32p, _ip, _fp, _ip, _fp, _vp, _ip]),
+    "lal_recent_push": (None, [C.POINTER(RecentTokens), _ip]),
+    "lal_tail_quantize_x_int8": (C.c_int, [_f32p, _i8p, _ip, C.POINTER(C.c_float)]),
+    "lal_tail_compute_abs_xq": (C.c_int, [_i8p, _u8p, _ip]),
+    "lal_tail_lm_head_int8_range": (C.c_int, [_f32p, _i8p, _fp, _i8p, _f32p, _ip, _ip, _ip]),
+    "lal_tail_quantize_q8_per_row": (C.c_int, [_f32p, _i8p, _f32p, _ip, _ip]),
+    "lal_tail_sample_token": (C.c_int, [_f32p, _ip, _fp, _ip, _fp, _vp, _ip, _fp,
+                                        C.POINTER(C.c_int)]),
+    "lal_tail_sample_token_filtered": (C.c_int, [_f32p, _ip, _fp, _ip, _fp, _vp, _ip, _vp,
+                                                 _vp, _vp, _vp, C.POINTER(C.c_int)]),
+    "lal_tail_lm_head_register": (C.c_int, [_i8p, _f32p, _ip, _ip]),
+    "lal_tail_lm_head_forget": (C.c_int, [_vp]),
+    "lal_tail_create": (C.c_int, [C.POINTER(TailConfig), C.POINTER(_vp)]),
+    "lal_tail_destroy": (C.c_int, [_vp]),
+    "lal_tail_shard_rows": (C.c_int, [_vp, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
+    "lal_tail_load_lm_head_q8": (C.c_int, [_vp, _i8p, _f32p]),
+    "lal_tail_load_lm_head_f32": (C.c_int, [_vp, _f32p, _ip, _ip]),
+    "lal_tail_read_lm_head": (C.c_int, [_vp, _vp, _vp]),
+    "lal_tail_set_sampling": (C.c_int, [_vp, _ip, _f32p, _i32p, _f32p]),
+    "lal_tail_set_history": (C.c_int, [_vp, _ip, _vp, _ip]),
+    "lal_tail_get_history": (C.c_int, [_vp, _ip, _vp, C.POINTER(C.c_int)]),
+    "lal_tail_step": (C.c_int, [_vp, _f32p, _ip, _f32p, _i32p]),
+    "lal_tail_step_device": (C.c_int, [_vp, _vp, _ip, _vp, _vp]),
+    "lal_tail_sync": (C.c_int, [_vp]),
+    "lal_tail_get_diag": (C.c_int, [_vp, _ip, C.POINTER(TailDiag)]),
+    "lal_tail_get_logits": (C.c_int, [_vp, _ip, _f32p]),
+    "lal_tail_device_buffers": (C.c_int, [_vp, C.POINTER(_vp), C.POINTER(_vp), C.POINTER(_vp)]),
+    "lal_tail_set_timing": (C.c_int, [_vp, _ip]),
+    "lal_tail_kernel_time": (C.c_int, [_vp, C.POINTER(C.c_double), C.POINTER(C.c_int)]),
+    "lal_tail_debug_expf": (C.c_int, [_f32p, _f32p, _ip]),
+}
+
+_lib = None
+
+
+def lib():
+    """The loaded liblal_tail.so (signatures set).  Raises if it was not built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise LalTailError(2, f"{LIB_PATH} is missing: run __graft_entry__.build()")
+        L = C.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def _check(rc: int):
+    if rc != 0:
+        raise LalTailError(rc, lib().lal_tail_last_error().decode(errors="replace"))
+
+
+def _ptr(a):
+    return None if a is None else a.ctypes.data_as(C.c_void_p)
+
+
+# ---- reference-named functions ------------------------------------------------------
+
+def quantize_x_int8(x: np.ndarray):
+    """lal_quantize_x_int8: returns (scale, xq)."""
+    x = np.ascontiguousarray(x, np.float32)
+    xq = np.empty(x.size, np.int8)
+    s = C.c_float()
+    _check(lib().lal_tail_quantize_x_int8(x, xq, x.size, C.byref(s)))
+    return np.float32(s.value), xq
+
+
+def compute_abs_xq(xq: np.ndarray) -> np.ndarray:
+    xq = np.ascontiguousarray(xq, np.int8)
+    ax = np.empty(xq.size, np.uint8)
+    _check(lib().lal_tail_compute_abs_xq(xq, ax, xq.size))
+    return ax
+
+
+def lm_head_int8_range(logits: np.ndarray, xq: np.ndarray, scale_x: float,
+                       wte_q: np.ndarray, scale_w: np.ndarray, v_start: int, v_end: int):
+    """lal_lm_head_int8_range: fills logits[v_start:v_end] in place."""
+    n_embd = wte_q.shape[1]
+    _check(lib().lal_tail_lm_head_int8_range(logits, np.ascontiguousarray(xq, np.int8),
+                                             np.float32(scale_x), wte_q.reshape(-1), scale_w,
+                                             v_start, v_end, n_embd))
+    return logits
+
+
+def lm_head_forget(wte_q: np.ndarray):
+    _check(lib().lal_tail_lm_head_forget(wte_q.ctypes.data_as(C.c_void_p)))
+
+
+def quantize_q8_per_row(W: np.ndarray):
+    """lal_quantize_q8_per_row on the GPU: returns (q8 [V,d], scale [V])."""
+    W = np.ascontiguousarray(W, np.float32)
+    V, d = W.shape
+    q = np.empty((V, d), np.int8)
+    s = np.empty(V, np.float32)
+    _check(lib().lal_tail_quantize_q8_per_row(W.reshape(-1), q.reshape(-1), s, d, V))
+    return q, s
+
+
+def sample_token(logits: np.ndarray, temperature: float, top_k: int, rep_penalty: float,
+                 recent: Optional[np.ndarray], u: float) -> int:
+    """lal_sample_token with the draw u given; mutates logits like the reference."""
+    rec = None if recent is None else np.ascontiguousarray(recent, np.int32)
+    tok = C.c_int()
+    _check(lib().lal_tail_sample_token(logits, logits.size, np.float32(temperature),
+                                       int(top_k), np.float32(rep_penalty), _ptr(rec),
+                                       0 if rec is None else rec.size, np.float32(u),
+                                       C.byref(tok)))
+    return tok.value
+
+
+def sample_token_filtered(logits: np.ndarray, temperature: float, top_k: int,
+                          rep_penalty: float, recent: Optional[np.ndarray],
+                          draw: Callable[[], float], filt=None, decode=None) -> int:
+    """qwen7b_server.c lal_sample_token_filtered; draw() is called only where
+    the reference calls rand()."""
+    rec = None if recent is None else np.ascontiguousarray(recent, np.int32)
+    cdraw = DRAW_FN(lambda _ctx: float(draw()))
+    cf = FILTER_FN(filt) if filt is not None else None
+    cd = DECODE_FN(decode) if decode is not None else None
+    tok = C.c_int()
+    _check(lib().lal_tail_sample_token_filtered(
+        logits, logits.size, np.float32(temperature), int(top_k), np.float32(rep_penalty),
+        _ptr(rec), 0 if rec is None else rec.size,
+        C.cast(cf, C.c_void_p) if cf else None, C.cast(cd, C.c_void_p) if cd else None,
+        C.cast(cdraw, C.c_void_p), None, C.byref(tok)))
+    return tok.value
+
+
+def debug_expf(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, np.float32)
+    y = np.empty_like(x)
+    _check(lib().lal_tail_debug_expf(x, y, x.size))
+    return y
+
+
+# ---- the fused decode tail -----------------------------------------------------------
+
+class DecodeTail:
+    """One GPU's fused decode tail (a vocab slice when shard_count > 1)."""
+
+    def __init__(self, vocab_size: int, n_embd: int, max_streams: int = 1,
+                 max_top_k: int = 64, history_cap: int = 256,
+                 sampler: int = LAL_SAMPLER_LIBRARY, device: int = -1,
+                 shard_rank: int = 0, shard_count: int = 1):
+        self.cfg = TailConfig(vocab_size, n_embd, max_streams, max_top_k, history_cap,
+                              sampler, device, shard_rank, shard_count)
+        h = C.c_void_p()
+        _check(lib().lal_tail_create(C.byref(self.cfg), C.byref(h)))
+        self.h = h
+        r0, n = C.c_int(), C.c_int()
+        _check(lib().lal_tail_shard_rows(self.h, C.byref(r0), C.byref(n)))
+        self.row0, self.n_rows = r0.value, n.value
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().lal_tail_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def load_lm_head_q8(self, wte_q_rows: np.ndarray, scale_w_rows: np.ndarray):
+        _check(lib().lal_tail_load_lm_head_q8(self.h, np.ascontiguousarray(wte_q_rows).reshape(-1),
+                                              np.ascontiguousarray(scale_w_rows, np.float32)))
+
+    def load_lm_head_f32(self, W_rows: np.ndarray, row_begin: int = 0):
+        W_rows = np.ascontiguousarray(W_rows, np.float32)
+        _check(lib().lal_tail_load_lm_head_f32(self.h, W_rows.reshape(-1), row_begin,
+                                               W_rows.shape[0]))
+
+    def read_lm_head(self):
+        q = np.empty((self.n_rows, self.cfg.n_embd), np.int8)
+        s = np.empty(self.n_rows, np.float32)
+        _check(lib().lal_tail_read_lm_head(self.h, _ptr(q), _ptr(s)))
+        return q, s
+
+    def set_sampling(self, temperature: Sequence[float], top_k: Sequence[int],
+                     rep_penalty: Sequence[float]):
+        t = np.ascontiguousarray(temperature, np.float32)
+        k = np.ascontiguousarray(top_k, np.int32)
+        p = np.ascontiguousarray(rep_penalty, np.float32)
+        _check(lib().lal_tail_set_sampling(self.h, t.size, t, k, p))
+
+    def set_history(self, stream: int, recent: Optional[np.ndarray]):
+        rec = np.zeros(0, np.int32) if recent is None else np.ascontiguousarray(recent, np.int32)
+        _check(lib().lal_tail_set_history(self.h, stream, _ptr(rec), rec.size))
+
+    def get_history(self, stream: int) -> np.ndarray:
+        out = np.zeros(max(1, self.cfg.history_cap), np.int32)
+        n = C.c_int()
+        _check(lib().lal_tail_get_history(self.h, stream, _ptr(out), C.byref(n)))
+        return out[:n.value].copy()
+
+    def step(self, hidden: np.ndarray, u: np.ndarray) -> np.ndarray:
+        hidden = np.ascontiguousarray(hidden, np.float32)
+        B = 1 if hidden.ndim == 1 else hidden.shape[0]
+        u = np.ascontiguousarray(u, np.float32).reshape(-1)
+        tok = np.empty(B, np.int32)
+        _check(lib().lal_tail_step(self.h, hidden.reshape(-1), B, u, tok))
+        return tok
+
+    def diag(self, stream: int = 0) -> dict:
+        d = TailDiag()
+        _check(lib().lal_tail_get_diag(self.h, stream, C.byref(d)))
+        return d.as_dict()
+
+    def logits(self, stream: int = 0) -> np.ndarray:
+        out = np.empty(self.n_rows, np.float32)
+        _check(lib().lal_tail_get_logits(self.h, stream, out))
+        return out
+
+    def set_timing(self, on: bool):
+        _check(lib().lal_tail_set_timing(self.h, 1 if on else 0))
+
+    def kernel_time(self):
+        ms, n = C.c_double(), C.c_int()
+        _check(lib().lal_tail_kernel_time(self.h, C.byref(ms), C.byref(n)))
+        return ms.value, n.value
+
+    def device_buffers(self):
+        a, b, c = C.c_void_p(), C.c_void_p(), C.c_void_p()
+        _check(lib().lal_tail_device_buffers(self.h, C.byref(a), C.byref(b), C.byref(c)))
+        return a.value, b.value, c.value
+
+    def step_device(self, d_hidden: int, n_streams: int, d_u: int, d_tokens: int):
+        _check(lib().lal_tail_step_device(self.h, d_hidden, n_streams, d_u, d_tokens))
+
+    def sync(self):
+        _check(lib().lal_tail_sync(self.h))

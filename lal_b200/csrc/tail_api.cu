@@ -1,0 +1,1101 @@
+/*
+ * tail_api.cu -- the C ABI of liblal_tail.so (include/lal_tail.h): contexts,
+ * device memory, streams, the host-LM-head registry of the drop-ins, and the
+ * launch of the kernels in tail_kernels.cu.  Host code only.
+ *
+ * There is no CPU path: every computation is a kernel launch; a missing GPU
+ * or a CUDA error is reported (status-returning functions) or aborts the
+ * process (the void / token-returning drop-ins, which have no error channel).
+ */
+#define LAL_TAIL_BUILDING 1
+#include "../../include/lal_tail.h"
+#include "../../include/runtime/lal_q8_kernel.h"
+#include "../../include/runtime/lal_sampling.h"
+#include "tail_internal.h"
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+/* glibc-expf fix-up table, embedded at build time (expf_blob.S). */
+extern "C" const unsigned char lal_expf_fixups_blob[];
+extern "C" const unsigned char lal_expf_fixups_blob_end[];
+
+using namespace lal;
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_err = buf;
+    return code;
+}
+
+#define CU(call)                                                                       \
+    do {                                                                               \
+        cudaError_t e_ = (call);                                                       \
+        if (e_ != cudaSuccess)                                                         \
+            return fail(LAL_TAIL_ERR_CUDA, "%s: %s (%s:%d)", #call, cudaGetErrorString(e_), \
+                        __FILE__, __LINE__);                                           \
+    } while (0)
+
+#define CHECK(expr)                                                                    \
+    do {                                                                               \
+        int rc_ = (expr);                                                              \
+        if (rc_ != LAL_TAIL_OK) return rc_;                                            \
+    } while (0)
+
+/* Drop-ins without an error channel: report and stop (no CPU fallback). */
+[[noreturn]] void die(const char *where) {
+    fprintf(stderr, "liblal_tail: %s failed: %s\n", where, g_err.c_str());
+    fflush(stderr);
+    abort();
+}
+
+/* ---- per-device state: SM count and the expf fix-up table ------------ */
+struct DeviceState {
+    bool ready = false;
+    int num_sms = 0;
+    uint32_t *d_expf_x = nullptr, *d_expf_y = nullptr;
+    int expf_n = 0;
+};
+std::mutex g_dev_mu;
+DeviceState g_dev[64];
+
+int device_state(int dev, DeviceState **out) {
+    if (dev < 0 || dev >= 64) return fail(LAL_TAIL_ERR_ARG, "device %d out of range", dev);
+    std::lock_guard<std::mutex> lk(g_dev_mu);
+    DeviceState &ds = g_dev[dev];
+    if (!ds.ready) {
+        CU(cudaSetDevice(dev));
+        CU(cudaDeviceGetAttribute(&ds.num_sms, cudaDevAttrMultiProcessorCount, dev));
+        int major = 0;
+        CU(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev));
+        if (major != 10)
+            return fail(LAL_TAIL_ERR_UNSUPPORTED, "device %d is sm_%d0; this library is built for sm_100a",
+                        dev, major);
+        const size_t blob = (size_t)(lal_expf_fixups_blob_end - lal_expf_fixups_blob);
+        uint32_t n = 0;
+        if (blob < 4) return fail(LAL_TAIL_ERR_STATE, "expf fix-up table missing from the build");
+        memcpy(&n, lal_expf_fixups_blob, 4);
+        if (blob < 4 + 8ull * n) return fail(LAL_TAIL_ERR_STATE, "expf fix-up table truncated");
+        CU(cudaMalloc(&ds.d_expf_x, 4ull * n + 4));
+        CU(cudaMalloc(&ds.d_expf_y, 4ull * n + 4));
+        CU(cudaMemcpy(ds.d_expf_x, lal_expf_fixups_blob + 4, 4ull * n, cudaMemcpyHostToDevice));
+        CU(cudaMemcpy(ds.d_expf_y, lal_expf_fixups_blob + 4 + 4ull * n, 4ull * n,
+                      cudaMemcpyHostToDevice));
+        ds.expf_n = (int)n;
+        ds.ready = true;
+    }
+    *out = &ds;
+    return LAL_TAIL_OK;
+}
+
+int current_device(int *dev) {
+    CU(cudaGetDevice(dev));
+    return LAL_TAIL_OK;
+}
+
+int ld_for(int d) { return (d + 15) / 16 * 16; }
+
+/* ---- growable device buffer ------------------------------------------- */
+struct DevBuf {
+    void *p = nullptr;
+    size_t cap = 0;
+    int ensure(size_t bytes) {
+        if (bytes <= cap) return LAL_TAIL_OK;
+        if (p) cudaFree(p);
+        p = nullptr;
+        cap = 0;
+        size_t want = bytes < 256 ? 256 : bytes;
+        CU(cudaMalloc(&p, want));
+        cap = want;
+        return LAL_TAIL_OK;
+    }
+    ~DevBuf() {
+        if (p) cudaFree(p);
+    }
+};
+
+struct PinBuf {
+    void *p = nullptr;
+    size_t cap = 0;
+    int ensure(size_t bytes) {
+        if (bytes <= cap) return LAL_TAIL_OK;
+        if (p) cudaFreeHost(p);
+        p = nullptr;
+        cap = 0;
+        size_t want = bytes < 256 ? 256 : bytes;
+        CU(cudaMallocHost(&p, want));
+        cap = want;
+        return LAL_TAIL_OK;
+    }
+    ~PinBuf() {
+        if (p) cudaFreeHost(p);
+    }
+};
+
+/* Scratch that one launch of the streaming kernel needs for one stream. */
+struct LaunchScratch {
+    DevBuf recs, keys, idx, counter, status, diag, tokens, params, hist, cand_v, cand_i,
+        keep, prefix, u;
+    int grid_cap = 0, list_cap = 0;
+    int ensure(int grid, int list_cap_) {
+        if (grid <= grid_cap && list_cap_ <= list_cap) return LAL_TAIL_OK;
+        grid_cap = std::max(grid, grid_cap);
+        list_cap = std::max(list_cap_, list_cap);
+        CHECK(recs.ensure(sizeof(CtaRecord) * grid_cap));
+        CHECK(keys.ensure(4ull * grid_cap * list_cap));
+        CHECK(idx.ensure(4ull * grid_cap * list_cap));
+        CHECK(counter.ensure(64));
+        CU(cudaMemset(counter.p, 0, 64));
+        CHECK(status.ensure(64));
+        CU(cudaMemset(status.p, 0, 64));
+        CHECK(diag.ensure(sizeof(StreamDiag)));
+        CHECK(tokens.ensure(64));
+        CHECK(params.ensure(64));
+        return LAL_TAIL_OK;
+    }
+};
+
+/* ---- per-thread state of the drop-ins ---------------------------------- */
+struct DropinState {
+    int device = -1;
+    cudaStream_t stream = nullptr;
+    DevBuf x, xq, ax, logits, W, q, s;
+    LaunchScratch ls;
+    PinBuf pin;
+    ~DropinState() {
+        if (stream) cudaStreamDestroy(stream);
+    }
+};
+thread_local std::unique_ptr<DropinState> t_drop;
+
+int dropin(DropinState **out, DeviceState **ds) {
+    int dev;
+    CHECK(current_device(&dev));
+    CHECK(device_state(dev, ds));
+    if (!t_drop || t_drop->device != dev) {
+        t_drop.reset(new DropinState());
+        t_drop->device = dev;
+        CU(cudaStreamCreateWithFlags(&t_drop->stream, cudaStreamNonBlocking));
+    }
+    *out = t_drop.get();
+    return LAL_TAIL_OK;
+}
+
+/* ---- registry of host LM heads used by the range drop-ins -------------- */
+struct LmHead {
+    int device = -1;
+    int d = 0, ld = 0, rows = 0;
+    const float *host_scale = nullptr;
+    int8_t *W = nullptr;
+    float *sw = nullptr;
+};
+std::mutex g_reg_mu;
+std::map<const int8_t *, LmHead> g_reg;
+std::vector<void *> g_retired; /* buffers replaced while a launch may still read them */
+
+int upload_rows(const int8_t *host, int rows, int d, int ld, int8_t *dst, cudaStream_t st) {
+    if (ld == d) {
+        CU(cudaMemcpyAsync(dst, host, (size_t)rows * d, cudaMemcpyHostToDevice, st));
+    } else {
+        CU(cudaMemset2DAsync(dst, ld, 0, ld, rows, st));
+        CU(cudaMemcpy2DAsync(dst, ld, host, d, d, rows, cudaMemcpyHostToDevice, st));
+    }
+    return LAL_TAIL_OK;
+}
+
+/* Look up (registering or growing on demand) a host LM head covering rows
+ * [0, rows_needed).  Called with g_reg_mu held. */
+int registry_get(const int8_t *wte_q, const float *scale_w, int rows_needed, int d, int dev,
+                 LmHead *out) {
+    auto it = g_reg.find(wte_q);
+    if (it != g_reg.end() && it->second.device == dev && it->second.d == d &&
+        it->second.rows >= rows_needed && it->second.host_scale == scale_w) {
+        *out = it->second;
+        return LAL_TAIL_OK;
+    }
+    LmHead h;
+    h.device = dev;
+    h.d = d;
+    h.ld = ld_for(d);
+    h.rows = rows_needed;
+    h.host_scale = scale_w;
+    CU(cudaMalloc(&h.W, (size_t)h.rows * h.ld));
+    CU(cudaMalloc(&h.sw, sizeof(float) * (size_t)h.rows));
+    CHECK(upload_rows(wte_q, h.rows, d, h.ld, h.W, 0));
+    CU(cudaMemcpy(h.sw, scale_w, sizeof(float) * (size_t)h.rows, cudaMemcpyHostToDevice));
+    CU(cudaDeviceSynchronize());
+    if (it != g_reg.end()) {
+        g_retired.push_back(it->second.W);
+        g_retired.push_back(it->second.sw);
+    }
+    g_reg[wte_q] = h;
+    *out = h;
+    return LAL_TAIL_OK;
+}
+
+/* Launch parameters common to the streaming kernel's modes. */
+void base_params(TailParams &p, const DeviceState *ds) {
+    memset(&p, 0, sizeof(p));
+    p.expf_x = ds->d_expf_x;
+    p.expf_y = ds->d_expf_y;
+    p.expf_n = ds->expf_n;
+}
+
+int sample_launch(DropinState *S, DeviceState *ds, float *logits, int V, float temperature,
+                  int top_k, float rep_penalty, const int *recent, int n_recent, float u,
+                  int variant, bool candidates_only, int *token_out, StreamDiag *diag_out,
+                  int *n_cand_out) {
+    if (!logits || V < 1) return fail(LAL_TAIL_ERR_ARG, "sample: bad logits/vocab");
+    if (n_recent < 0 || (n_recent > 0 && !recent)) return fail(LAL_TAIL_ERR_ARG, "sample: bad recent");
+    const bool greedy = temperature <= 0.0f || top_k <= 0;
+    int k = greedy ? 1 : (top_k > V ? V : top_k);
+    cudaStream_t st = S->stream;
+    TailParams p;
+    base_params(p, ds);
+    p.mode = MODE_SAMPLE;
+    p.variant = variant;
+    p.rows = V;
+    p.row_base = 0;
+    p.vocab = V;
+    p.d = p.ld = 16;
+    p.B = 1;
+    p.list_cap = k + kTieExtra;
+    const int grid = plan_launch(p, ds->num_sms, 64);
+    if (grid < 1) return fail(LAL_TAIL_ERR_UNSUPPORTED, "sample: shape unsupported (plan %d)", grid);
+    CHECK(S->ls.ensure(grid, p.list_cap));
+    CHECK(S->logits.ensure(sizeof(float) * (size_t)V));
+    CHECK(S->ls.hist.ensure(sizeof(int) * (size_t)(n_recent + 1)));
+    CHECK(S->ls.cand_v.ensure(sizeof(float) * (size_t)V));
+    CHECK(S->ls.cand_i.ensure(sizeof(int) * (size_t)V));
+    /* param block: temperature, top_k, penalty, u, hist_n */
+    struct {
+        float t;
+        int k;
+        float pen;
+        float u;
+        int hn;
+        int head;
+    } hp = {temperature, top_k, rep_penalty, u, n_recent, 0};
+    CU(cudaMemcpyAsync(S->ls.params.p, &hp, sizeof(hp), cudaMemcpyHostToDevice, st));
+    CU(cudaMemcpyAsync(S->logits.p, logits, sizeof(float) * (size_t)V, cudaMemcpyHostToDevice, st));
+    if (n_recent > 0)
+        CU(cudaMemcpyAsync(S->ls.hist.p, recent, sizeof(int) * (size_t)n_recent,
+                           cudaMemcpyHostToDevice, st));
+    char *pb = (char *)S->ls.params.p;
+    p.logits = (float *)S->logits.p;
+    p.temperature = (const float *)(pb + 0);
+    p.top_k = (const int *)(pb + 4);
+    p.rep_penalty = (const float *)(pb + 8);
+    p.u = (const float *)(pb + 12);
+    p.hist_n = (int *)(pb + 16);
+    p.hist_head = (int *)(pb + 20);
+    p.hist_ids = (int *)S->ls.hist.p;
+    p.hist_cap = n_recent;
+    p.push_history = 0;
+    p.tokens = (int *)S->ls.tokens.p;
+    p.diag = (StreamDiag *)S->ls.diag.p;
+    p.recs = (CtaRecord *)S->ls.recs.p;
+    p.rec_keys = (uint32_t *)S->ls.keys.p;
+    p.rec_idx = (int *)S->ls.idx.p;
+    p.counter = (unsigned *)S->ls.counter.p;
+    p.status = (int *)S->ls.status.p;
+    p.cand_val_out = (float *)S->ls.cand_v.p;
+    p.cand_idx_out = (int *)S->ls.cand_i.p;
+    p.cand_out_cap = V;
+    p.candidates_only = candidates_only ? 1 : 0;
+    CU(launch_tail(p, grid, st));
+    int status = 0;
+    StreamDiag dg;
+    CU(cudaMemcpyAsync(logits, S->logits.p, sizeof(float) * (size_t)V, cudaMemcpyDeviceToHost, st));
+    CU(cudaMemcpyAsync(&dg, S->ls.diag.p, sizeof(dg), cudaMemcpyDeviceToHost, st));
+    CU(cudaMemcpyAsync(&status, S->ls.status.p, sizeof(int), cudaMemcpyDeviceToHost, st));
+    CU(cudaStreamSynchronize(st));
+    if (status != 0) {
+        CU(cudaMemset(S->ls.status.p, 0, sizeof(int)));
+        return fail(status, "sample kernel reported device status %d (%s)", status,
+                    status == LAL_TAIL_ERR_TIMEOUT ? "bounded wait expired"
+                                                   : "candidate set above the built capacity");
+    }
+    if (token_out) *token_out = dg.token;
+    if (diag_out) *diag_out = dg;
+    if (n_cand_out) *n_cand_out = dg.n_cand;
+    return LAL_TAIL_OK;
+}
+
+}  // namespace
+
+/* ======================================================================
+ * 1. drop-ins and their status-returning forms
+ * ====================================================================== */
+extern "C" {
+
+const char *lal_tail_last_error(void) { return g_err.c_str(); }
+
+const char *lal_tail_version(void) {
+    return "liblal_tail 0.1 (sm_100a; int8 GEMV via cp.async.bulk + dp4a; fused top-k sampler)";
+}
+
+int lal_tail_quantize_x_int8(const float *x, int8_t *xq, int n, float *scale_out) {
+    if (!x || !xq || n < 1) return fail(LAL_TAIL_ERR_ARG, "quantize_x: bad arguments");
+    DropinState *S;
+    DeviceState *ds;
+    CHECK(dropin(&S, &ds));
+    cudaStream_t st = S->stream;
+    CHECK(S->x.ensure(4ull * n + 64));
+    CHECK(S->xq.ensure((size_t)n + 64));
+    CU(cudaMemcpyAsync(S->x.p, x, 4ull * n, cudaMemcpyHostToDevice, st));
+    float *d_scale = (float *)((char *)S->x.p + 4ull * n);
+    CU(launch_quantize_x((const float *)S->x.p, (int8_t *)S->xq.p, d_scale, n, st));
+    float sc = 0.0f;
+    CU(cudaMemcpyAsync(xq, S->xq.p, (size_t)n, cudaMemcpyDeviceToHost, st));
+    CU(cudaMemcpyAsync(&sc, d_scale, 4, cudaMemcpyDeviceToHost, st));
+    CU(cudaStreamSynchronize(st));
+    if (scale_out) *scale_out = sc;
+    return LAL_TAIL_OK;
+}
+
+float lal_quantize_x_int8(const float *x, int8_t *xq, int n) {
+    float s = 0.0f;
+    if (lal_tail_quantize_x_int8(x, xq, n, &s) != LAL_TAIL_OK) die("lal_quantize_x_int8");
+    return s;
+}
+
+int lal_tail_compute_abs_xq(const int8_t *xq, uint8_t *ax, int n) {
+    if (!xq || !ax || n < 1) return fail(LAL_TAIL_ERR_ARG, "compute_abs_xq: bad arguments");
+    DropinState *S;
+    DeviceState *ds;
+    CHECK(dropin(&S, &ds));
+    cudaStream_t st = S->stream;
+    CHECK(S->xq.ensure((size_t)n));
+    CHECK(S->ax.ensure((size_t)n));
+    CU(cudaMemcpyAsync(S->xq.p, xq, (size_t)n, cudaMemcpyHostToDevice, st));
+    CU(launch_abs_xq((const int8_t *)S->xq.p, (uint8_t *)S->ax.p, n, st));
+    CU(cudaMemcpyAsync(ax, S->ax.p, (size_t)n, cudaMemcpyDeviceToHost, st));
+    CU(cudaStreamSynchronize(st));
+    return LAL_TAIL_OK;
+}
+
+void lal_compute_abs_xq(const int8_t *xq, uint8_t *ax, int n_embd) {
+    if (lal_tail_compute_abs_xq(xq, ax, n_embd) != LAL_TAIL_OK) die("lal_compute_abs_xq");
+}
+
+int lal_tail_lm_head_register(const int8_t *wte_q, const float *scale_w, int vocab_size,
+                              int n_embd) {
+    if (!wte_q || !scale_w || vocab_size < 1 || n_embd < 1)
+        return fail(LAL_TAIL_ERR_ARG, "lm_head_register: bad arguments");
+    int dev;
+    CHECK(current_device(&dev));
+    DeviceState *ds;
+    CHECK(device_state(dev, &ds));
+    std::lock_guard<std::mutex> lk(g_reg_mu);
+    LmHead h;
+    return registry_get(wte_q, scale_w, vocab_size, n_embd, dev, &h);
+}
+
+int lal_tail_lm_head_forget(const int8_t *wte_q) {
+    std::lock_guard<std::mutex> lk(g_reg_mu);
+    auto it = g_reg.find(wte_q);
+    if (it == g_reg.end()) return LAL_TAIL_OK;
+    CU(cudaDeviceSynchronize());
+    cudaFree(it->second.W);
+    cudaFree(it->second.sw);
+    g_reg.erase(it);
+    for (void *p : g_retired) cudaFree(p);
+    g_retired.clear();
+    return LAL_TAIL_OK;
+}
+
+}  // extern "C"
+
+namespace {
+
+/* The LM-head range drop-ins.  eight_row selects the 8-row form's column
+ * tail behaviour (runtime/lal_q8_kernel.h:562-611): rows in full 8-row groups
+ * from v_start sum only the first n_embd & ~31 columns. */
+int lm_head_range(float *logits, const int8_t *xq, float scale_x, const int8_t *wte_q,
+                  const float *scale_w, int v_start, int v_end, int n_embd, bool eight_row) {
+    if (!logits || !xq || !wte_q || !scale_w || n_embd < 1 || v_start < 0)
+        return fail(LAL_TAIL_ERR_ARG, "lm_head_int8_range: bad arguments");
+    if (v_end <= v_start) return LAL_TAIL_OK;
+    DropinState *S;
+    DeviceState *ds;
+    CHECK(dropin(&S, &ds));
+    LmHead h;
+    {
+        std::lock_guard<std::mutex> lk(g_reg_mu);
+        CHECK(registry_get(wte_q, scale_w, v_end, n_embd, S->device, &h));
+    }
+    cudaStream_t st = S->stream;
+    const int rows = v_end - v_start;
+    TailParams p;
+    base_params(p, ds);
+    p.mode = MODE_LMHEAD;
+    p.W = h.W + (size_t)v_start * h.ld;
+    p.scale_w = h.sw + v_start;
+    p.rows = rows;
+    p.row_base = v_start;
+    p.vocab = v_end;
+    p.d = n_embd;
+    p.ld = h.ld;
+    p.B = 1;
+    p.list_cap = 1;
+    p.trunc_cols = h.ld;
+    p.trunc_rows_end = 0;
+    if (eight_row && (n_embd & 31) != 0) {
+        p.trunc_cols = n_embd & ~31;
+        p.trunc_rows_end = rows / 8 * 8;
+    }
+    const int grid = plan_launch(p, ds->num_sms, 8);
+    if (grid < 1) return fail(LAL_TAIL_ERR_UNSUPPORTED, "lm_head: shape unsupported (plan %d)", grid);
+    CHECK(S->ls.ensure(grid, 1));
+    CHECK(S->xq.ensure((size_t)n_embd));
+    CHECK(S->logits.ensure(4ull * rows));
+    CU(cudaMemcpyAsync(S->xq.p, xq, (size_t)n_embd, cudaMemcpyHostToDevice, st));
+    p.xq_in = (const int8_t *)S->xq.p;
+    p.scale_x_in = scale_x;
+    p.logits = (float *)S->logits.p;
+    p.status = (int *)S->ls.status.p;
+    p.counter = (unsigned *)S->ls.counter.p;
+    CU(launch_tail(p, grid, st));
+    int status = 0;
+    CU(cudaMemcpyAsync(logits + v_start, S->logits.p, 4ull * rows, cudaMemcpyDeviceToHost, st));
+    CU(cudaMemcpyAsync(&status, S->ls.status.p, sizeof(int), cudaMemcpyDeviceToHost, st));
+    CU(cudaStreamSynchronize(st));
+    if (status != 0) {
+        CU(cudaMemset(S->ls.status.p, 0, sizeof(int)));
+        return fail(status, "lm_head kernel reported device status %d", status);
+    }
+    return LAL_TAIL_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int lal_tail_lm_head_int8_range(float *logits, const int8_t *xq, float scale_x,
+                                const int8_t *wte_q, const float *scale_w, int v_start,
+                                int v_end, int n_embd) {
+    return lm_head_range(logits, xq, scale_x, wte_q, scale_w, v_start, v_end, n_embd, false);
+}
+
+void lal_lm_head_int8_range(float *logits, const int8_t *xq, float scale_x,
+                            const int8_t *wte_q, const float *scale_w, int v_start, int v_end,
+                            int n_embd) {
+    if (lal_tail_lm_head_int8_range(logits, xq, scale_x, wte_q, scale_w, v_start, v_end,
+                                    n_embd) != LAL_TAIL_OK)
+        die("lal_lm_head_int8_range");
+}
+
+void lal_lm_head_int8_range_abs(float *logits, const int8_t *xq, const uint8_t *ax,
+                                float scale_x, const int8_t *wte_q, const float *scale_w,
+                                int v_start, int v_end, int n_embd) {
+    (void)ax;
+    if (lal_tail_lm_head_int8_range(logits, xq, scale_x, wte_q, scale_w, v_start, v_end,
+                                    n_embd) != LAL_TAIL_OK)
+        die("lal_lm_head_int8_range_abs");
+}
+
+void lal_lm_head_int8_range_abs_8row(float *logits, const int8_t *xq, const uint8_t *ax,
+                                     float scale_x, const int8_t *wte_q, const float *scale_w,
+                                     int v_start, int v_end, int n_embd) {
+    (void)ax;
+    if (lm_head_range(logits, xq, scale_x, wte_q, scale_w, v_start, v_end, n_embd, true) !=
+        LAL_TAIL_OK)
+        die("lal_lm_head_int8_range_abs_8row");
+}
+
+int lal_tail_quantize_q8_per_row(const float *W, int8_t *q8_T, float *scale, int in_dim,
+                                 int out_dim) {
+    if (!W || !q8_T || !scale || in_dim < 1 || out_dim < 0)
+        return fail(LAL_TAIL_ERR_ARG, "quantize_q8_per_row: bad arguments");
+    DropinState *S;
+    DeviceState *ds;
+    CHECK(dropin(&S, &ds));
+    cudaStream_t st = S->stream;
+    /* chunks of ~64 MB of fp32 input */
+    const int chunk = std::max(1, (int)((64ull << 20) / (4ull * in_dim)));
+    CHECK(S->W.ensure(4ull * chunk * in_dim));
+    CHECK(S->q.ensure((size_t)chunk * in_dim));
+    CHECK(S->s.ensure(4ull * chunk));
+    for (int r0 = 0; r0 < out_dim; r0 += chunk) {
+        const int n = std::min(chunk, out_dim - r0);
+        CU(cudaMemcpyAsync(S->W.p, W + (size_t)r0 * in_dim, 4ull * n * in_dim,
+                           cudaMemcpyHostToDevice, st));
+        CU(launch_quantize_rows((const float *)S->W.p, in_dim, (int8_t *)S->q.p, in_dim,
+                                (float *)S->s.p, n, st));
+        CU(cudaMemcpyAsync(q8_T + (size_t)r0 * in_dim, S->q.p, (size_t)n * in_dim,
+                           cudaMemcpyDeviceToHost, st));
+        CU(cudaMemcpyAsync(scale + r0, S->s.p, 4ull * n, cudaMemcpyDeviceToHost, st));
+        CU(cudaStreamSynchronize(st));
+    }
+    return LAL_TAIL_OK;
+}
+
+void lal_quantize_q8_per_row(const float *W, int8_t *q8_T, float *scale, int in_dim,
+                             int out_dim) {
+    if (lal_tail_quantize_q8_per_row(W, q8_T, scale, in_dim, out_dim) != LAL_TAIL_OK)
+        die("lal_quantize_q8_per_row");
+}
+
+int lal_tail_sample_token(float *logits, int vocab_size, float temperature, int top_k,
+                          float rep_penalty, const int *recent, int n_recent, float u,
+                          int *token_out) {
+    DropinState *S;
+    DeviceState *ds;
+    CHECK(dropin(&S, &ds));
+    return sample_launch(S, ds, logits, vocab_size, temperature, top_k, rep_penalty, recent,
+                         n_recent, u, VARIANT_LIBRARY, false, token_out, nullptr, nullptr);
+}
+
+int lal_sample_token(float *logits, int vocab_size, float temperature, int top_k,
+                     float rep_penalty, const int *recent, int n_recent) {
+    /* runtime/lal_sampling.h:116 draws once on the non-greedy path; no other
+     * rand() call happens inside the function, so drawing first keeps the
+     * caller's global sequence identical. */
+    float u = 0.0f;
+    if (!(temperature <= 0.0f || top_k <= 0)) u = (float)rand() / (float)RAND_MAX;
+    int tok = 0;
+    if (lal_tail_sample_token(logits, vocab_size, temperature, top_k, rep_penalty, recent,
+                              n_recent, u, &tok) != LAL_TAIL_OK)
+        die("lal_sample_token");
+    return tok;
+}
+
+int lal_tail_sample_token_filtered(float *logits, int vocab_size, float temperature,
+                                   int top_k, float rep_penalty, const int *recent,
+                                   int n_recent, lal_filter_topk_fn filter,
+                                   lal_token_decode_fn decode, lal_draw_fn draw,
+                                   void *draw_ctx, int *token_out) {
+    DropinState *S;
+    DeviceState *ds;
+    CHECK(dropin(&S, &ds));
+    const bool greedy = temperature <= 0.0f || top_k <= 0;
+    if (greedy) /* penalty then argmax (qwen7b_server.c:223-234) */
+        return sample_launch(S, ds, logits, vocab_size, temperature, top_k, rep_penalty, recent,
+                             n_recent, 0.0f, VARIANT_SERVER, false, token_out, nullptr, nullptr);
+    /* 1. penalty, threshold and the candidate set on the device */
+    StreamDiag dg;
+    int m = 0;
+    CHECK(sample_launch(S, ds, logits, vocab_size, temperature, top_k, rep_penalty, recent,
+                        n_recent, 0.0f, VARIANT_SERVER, true, nullptr, &dg, &m));
+    cudaStream_t st = S->stream;
+    std::vector<int> cand(m);
+    CU(cudaMemcpyAsync(cand.data(), S->ls.cand_i.p, sizeof(int) * (size_t)m,
+                       cudaMemcpyDeviceToHost, st));
+    CU(cudaStreamSynchronize(st));
+    /* 2. keep_mask and the level-2 filter on the host (qwen7b_server.c:258-270) */
+    std::vector<int> keep_c(m, 1);
+    if (filter) {
+        std::vector<int> mask((size_t)vocab_size, 0);
+        for (int i = 0; i < m; ++i) mask[cand[i]] = 1;
+        const int last = n_recent > 0 ? recent[n_recent - 1] : -1;
+        (void)filter(mask.data(), vocab_size, last, recent, n_recent, decode);
+        bool any = false;
+        for (int v = 0; v < vocab_size && !any; ++v) any = mask[v] != 0;
+        if (any) {
+            /* a filter only clears bits; kept non-candidates never count
+             * because the reference also requires logits[v] >= threshold */
+            for (int i = 0; i < m; ++i) keep_c[i] = mask[cand[i]] ? 1 : 0;
+        }
+    }
+    /* 3. kept softmax on the device; draw only when the mass is positive */
+    CHECK(S->ls.keep.ensure(sizeof(int) * (size_t)(m + 1)));
+    CHECK(S->ls.prefix.ensure(sizeof(float) * (size_t)(m + 1)));
+    CHECK(S->ls.u.ensure(64));
+    CU(cudaMemcpyAsync(S->ls.keep.p, keep_c.data(), sizeof(int) * (size_t)m,
+                       cudaMemcpyHostToDevice, st));
+    FinishParams f;
+    memset(&f, 0, sizeof(f));
+    f.cand_val = (const float *)S->ls.cand_v.p;
+    f.cand_idx = (const int *)S->ls.cand_i.p;
+    f.keep = (const int *)S->ls.keep.p;
+    f.m = m;
+    f.temperature = temperature;
+    f.vocab = vocab_size;
+    f.u = (const float *)S->ls.u.p;
+    f.prefix = (float *)S->ls.prefix.p;
+    f.diag = (StreamDiag *)S->ls.diag.p;
+    f.token = (int *)S->ls.tokens.p;
+    f.expf_x = ds->d_expf_x;
+    f.expf_y = ds->d_expf_y;
+    f.expf_n = ds->expf_n;
+    f.phase = 0;
+    CU(launch_finish(f, st));
+    CU(cudaMemcpyAsync(&dg, S->ls.diag.p, sizeof(dg), cudaMemcpyDeviceToHost, st));
+    CU(cudaStreamSynchronize(st));
+    if (dg.sum <= 0.0f) { /* qwen7b_server.c:285-286 */
+        if (token_out) *token_out = dg.token;
+        return LAL_TAIL_OK;
+    }
+    const float u = draw ? draw(draw_ctx) : 0.0f;
+    CU(cudaMemcpyAsync(S->ls.u.p, &u, sizeof(float), cudaMemcpyHostToDevice, st));
+    f.phase = 1;
+    CU(launch_finish(f, st));
+    int tok = -1;
+    CU(cudaMemcpyAsync(&tok, S->ls.tokens.p, sizeof(int), cudaMemcpyDeviceToHost, st));
+    CU(cudaStreamSynchronize(st));
+    if (token_out) *token_out = tok;
+    return LAL_TAIL_OK;
+}
+
+void lal_recent_push(LalRecentTokens *rt, int tok) {
+    /* runtime/lal_sampling.h:133-136 */
+    if (rt->n < 256) {
+        rt->tokens[rt->n++] = tok;
+    } else {
+        memmove(rt->tokens, rt->tokens + 1, 255 * sizeof(int));
+        rt->tokens[255] = tok;
+    }
+}
+
+int lal_tail_debug_expf(const float *x, float *y, int n) {
+    if (!x || !y || n < 0) return fail(LAL_TAIL_ERR_ARG, "debug_expf: bad arguments");
+    if (n == 0) return LAL_TAIL_OK;
+    DropinState *S;
+    DeviceState *ds;
+    CHECK(dropin(&S, &ds));
+    cudaStream_t st = S->stream;
+    CHECK(S->x.ensure(4ull * n));
+    CHECK(S->logits.ensure(4ull * n));
+    CU(cudaMemcpyAsync(S->x.p, x, 4ull * n, cudaMemcpyHostToDevice, st));
+    CU(launch_debug_expf((const float *)S->x.p, (float *)S->logits.p, n, ds->d_expf_x,
+                         ds->d_expf_y, ds->expf_n, st));
+    CU(cudaMemcpyAsync(y, S->logits.p, 4ull * n, cudaMemcpyDeviceToHost, st));
+    CU(cudaStreamSynchronize(st));
+    return LAL_TAIL_OK;
+}
+
+}  // extern "C"
+
+/* ======================================================================
+ * 2. fused decode-tail contexts
+ * ====================================================================== */
+struct lal_tail {
+    lal_tail_config cfg;
+    int device = 0;
+    DeviceState *ds = nullptr;
+    int row0 = 0, nrows = 0, ld = 0;
+    cudaStream_t stream = nullptr;
+    bool loaded = false;
+    int8_t *W = nullptr;
+    float *sw = nullptr;
+    /* inputs: hidden [B][d] followed by u [B] (one H2D per step) */
+    float *io_in = nullptr;
+    /* outputs: tokens [B] followed by the status word (one D2H per step) */
+    int *io_out = nullptr;
+    float *logits = nullptr;                   /* [B][nrows] */
+    float *temp = nullptr;                     /* [B] */
+    int *topk = nullptr;                       /* [B] */
+    float *pen = nullptr;                      /* [B] */
+    int *hist_ids = nullptr, *hist_n = nullptr, *hist_head = nullptr;
+    StreamDiag *diag = nullptr;                /* [B] */
+    CtaRecord *recs = nullptr;
+    uint32_t *rec_keys = nullptr;
+    int *rec_idx = nullptr;
+    unsigned *counter = nullptr;               /* [B] */
+    int list_cap = 0;
+    float *h_in = nullptr;                     /* pinned staging */
+    int *h_out = nullptr;
+    std::vector<float> h_temp;
+    std::vector<int> h_topk;
+    std::vector<float> h_pen;
+    int n_set = 0;
+    TailParams plan;
+    int grid = 0;
+    bool timing = false;
+    std::vector<cudaEvent_t> ev;
+    int ev_used = 0;
+};
+
+namespace {
+
+void destroy_ctx(lal_tail *t) {
+    if (!t) return;
+    if (t->device >= 0) cudaSetDevice(t->device);
+    if (t->stream) cudaStreamSynchronize(t->stream);
+    void *bufs[] = {t->W, t->sw, t->io_in, t->io_out, t->logits, t->temp, t->topk, t->pen,
+                    t->hist_ids, t->hist_n, t->hist_head, t->diag, t->recs, t->rec_keys,
+                    t->rec_idx, t->counter};
+    for (void *b : bufs)
+        if (b) cudaFree(b);
+    if (t->h_in) cudaFreeHost(t->h_in);
+    if (t->h_out) cudaFreeHost(t->h_out);
+    for (cudaEvent_t e : t->ev) cudaEventDestroy(e);
+    if (t->stream) cudaStreamDestroy(t->stream);
+    delete t;
+}
+
+int ctx_alloc(lal_tail *t) {
+    const lal_tail_config &c = t->cfg;
+    const int B = c.max_streams, d = c.n_embd;
+    CU(cudaStreamCreateWithFlags(&t->stream, cudaStreamNonBlocking));
+    CU(cudaMalloc(&t->W, (size_t)t->nrows * t->ld));
+    CU(cudaMemset(t->W, 0, (size_t)t->nrows * t->ld));
+    CU(cudaMalloc(&t->sw, 4ull * t->nrows));
+    CU(cudaMalloc(&t->io_in, 4ull * ((size_t)B * d + B)));
+    CU(cudaMalloc(&t->io_out, 4ull * (B + 1)));
+    CU(cudaMemset(t->io_out, 0, 4ull * (B + 1)));
+    CU(cudaMalloc(&t->logits, 4ull * B * t->nrows));
+    CU(cudaMalloc(&t->temp, 4ull * B));
+    CU(cudaMalloc(&t->topk, 4ull * B));
+    CU(cudaMalloc(&t->pen, 4ull * B));
+    const int hc = std::max(1, c.history_cap);
+    CU(cudaMalloc(&t->hist_ids, 4ull * B * hc));
+    CU(cudaMalloc(&t->hist_n, 4ull * B));
+    CU(cudaMalloc(&t->hist_head, 4ull * B));
+    CU(cudaMemset(t->hist_n, 0, 4ull * B));
+    CU(cudaMemset(t->hist_head, 0, 4ull * B));
+    CU(cudaMalloc(&t->diag, sizeof(StreamDiag) * B));
+    CU(cudaMemset(t->diag, 0, sizeof(StreamDiag) * B));
+    t->list_cap = c.max_top_k + kTieExtra;
+    CU(cudaMalloc(&t->recs, sizeof(CtaRecord) * kMaxGrid));
+    CU(cudaMalloc(&t->rec_keys, 4ull * kMaxGrid * t->list_cap));
+    CU(cudaMalloc(&t->rec_idx, 4ull * kMaxGrid * t->list_cap));
+    CU(cudaMalloc(&t->counter, 4ull * B));
+    CU(cudaMemset(t->counter, 0, 4ull * B));
+    CU(cudaMallocHost(&t->h_in, 4ull * ((size_t)B * d + B)));
+    CU(cudaMallocHost(&t->h_out, 4ull * (B + 1)));
+    t->h_temp.assign(B, 0.0f);
+    t->h_topk.assign(B, 0);
+    t->h_pen.assign(B, 1.0f);
+    /* plan the fused launch for this slice */
+    TailParams &p = t->plan;
+    base_params(p, t->ds);
+    p.mode = MODE_FUSED;
+    p.variant = c.sampler == LAL_SAMPLER_SERVER ? VARIANT_SERVER : VARIANT_LIBRARY;
+    p.rows = t->nrows;
+    p.row_base = t->row0;
+    p.vocab = c.vocab_size;
+    p.d = d;
+    p.ld = t->ld;
+    p.B = 1;
+    p.list_cap = t->list_cap;
+    t->grid = plan_launch(p, t->ds->num_sms, 8);
+    if (t->grid < 1)
+        return fail(LAL_TAIL_ERR_UNSUPPORTED, "fused tail: shape V=%d d=%d k=%d unsupported (plan %d)",
+                    c.vocab_size, d, c.max_top_k, t->grid);
+    return LAL_TAIL_OK;
+}
+
+int ctx_check(lal_tail *t) {
+    if (!t) return fail(LAL_TAIL_ERR_ARG, "null context");
+    CU(cudaSetDevice(t->device));
+    return LAL_TAIL_OK;
+}
+
+/* Enqueue the fused kernel for streams [0, n) on the context stream. */
+int enqueue_step(lal_tail *t, const float *d_hidden, int n, const float *d_u, int *d_tokens) {
+    if (!t->loaded) return fail(LAL_TAIL_ERR_STATE, "step before the LM head was loaded");
+    if (n < 1 || n > t->cfg.max_streams) return fail(LAL_TAIL_ERR_ARG, "n_streams %d out of range", n);
+    if (t->n_set < n) return fail(LAL_TAIL_ERR_STATE, "sampling parameters not set for %d streams", n);
+    const int hc = std::max(1, t->cfg.history_cap);
+    for (int b = 0; b < n; ++b) {
+        TailParams p = t->plan;
+        p.W = t->W;
+        p.scale_w = t->sw;
+        p.hidden = d_hidden + (size_t)b * t->cfg.n_embd;
+        p.logits = t->logits + (size_t)b * t->nrows;
+        p.temperature = t->temp + b;
+        p.top_k = t->topk + b;
+        p.rep_penalty = t->pen + b;
+        p.u = d_u + b;
+        p.hist_ids = t->hist_ids + (size_t)b * hc;
+        p.hist_n = t->hist_n + b;
+        p.hist_head = t->hist_head + b;
+        p.hist_cap = t->cfg.history_cap;
+        p.push_history = t->cfg.history_cap > 0 ? 1 : 0;
+        p.tokens = d_tokens + b;
+        p.diag = t->diag + b;
+        p.recs = t->recs;
+        p.rec_keys = t->rec_keys;
+        p.rec_idx = t->rec_idx;
+        p.counter = t->counter + b;
+        p.status = t->io_out + t->cfg.max_streams;
+        const bool time_it = t->timing && t->ev_used + 2 <= (int)t->ev.size();
+        if (time_it) CU(cudaEventRecord(t->ev[t->ev_used], t->stream));
+        CU(launch_tail(p, t->grid, t->stream));
+        if (time_it) {
+            CU(cudaEventRecord(t->ev[t->ev_used + 1], t->stream));
+            t->ev_used += 2;
+        }
+    }
+    return LAL_TAIL_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int lal_tail_create(const lal_tail_config *cfg, lal_tail **out) {
+    if (!cfg || !out) return fail(LAL_TAIL_ERR_ARG, "create: null argument");
+    *out = nullptr;
+    const lal_tail_config &c = *cfg;
+    if (c.vocab_size < 1 || c.n_embd < 1 || c.max_streams < 1 || c.max_top_k < 1 ||
+        c.history_cap < 0 || c.shard_count < 1 || c.shard_rank < 0 || c.shard_rank >= c.shard_count)
+        return fail(LAL_TAIL_ERR_ARG, "create: bad config");
+    if (c.sampler != LAL_SAMPLER_LIBRARY && c.sampler != LAL_SAMPLER_SERVER)
+        return fail(LAL_TAIL_ERR_ARG, "create: unknown sampler %d", c.sampler);
+    lal_tail *t = new lal_tail();
+    t->cfg = c;
+    int dev = c.device;
+    if (dev < 0) {
+        int rc = current_device(&dev);
+        if (rc) { delete t; return rc; }
+    }
+    t->device = dev;
+    int rc = device_state(dev, &t->ds);
+    if (rc == LAL_TAIL_OK) {
+        cudaError_t e = cudaSetDevice(dev);
+        if (e != cudaSuccess) rc = fail(LAL_TAIL_ERR_CUDA, "cudaSetDevice: %s", cudaGetErrorString(e));
+    }
+    if (rc == LAL_TAIL_OK) {
+        t->row0 = (int)((long long)c.shard_rank * c.vocab_size / c.shard_count);
+        t->nrows = (int)((long long)(c.shard_rank + 1) * c.vocab_size / c.shard_count) - t->row0;
+        t->ld = ld_for(c.n_embd);
+        if (t->nrows < 1) rc = fail(LAL_TAIL_ERR_ARG, "create: empty vocab slice");
+    }
+    if (rc == LAL_TAIL_OK) rc = ctx_alloc(t);
+    if (rc != LAL_TAIL_OK) {
+        std::string keep = g_err;
+        destroy_ctx(t);
+        g_err = keep;
+        return rc;
+    }
+    *out = t;
+    return LAL_TAIL_OK;
+}
+
+int lal_tail_destroy(lal_tail *t) {
+    destroy_ctx(t);
+    return LAL_TAIL_OK;
+}
+
+int lal_tail_shard_rows(const lal_tail *t, int *row0, int *n_rows) {
+    if (!t) return fail(LAL_TAIL_ERR_ARG, "null context");
+    if (row0) *row0 = t->row0;
+    if (n_rows) *n_rows = t->nrows;
+    return LAL_TAIL_OK;
+}
+
+int lal_tail_load_lm_head_q8(lal_tail *t, const int8_t *wte_q_rows, const float *scale_w_rows) {
+    CHECK(ctx_check(t));
+    if (!wte_q_rows || !scale_w_rows) return fail(LAL_TAIL_ERR_ARG, "load_lm_head_q8: null");
+    CHECK(upload_rows(wte_q_rows, t->nrows, t->cfg.n_embd, t->ld, t->W, t->stream));
+    CU(cudaMemcpyAsync(t->sw, scale_w_rows, 4ull * t->nrows, cudaMemcpyHostToDevice, t->stream));
+    CU(cudaStreamSynchronize(t->stream));
+    t->loaded = true;
+    return LAL_TAIL_OK;
+}
+
+int lal_tail_load_lm_head_f32(lal_tail *t, const float *W_rows, int row_begin, int n_rows) {
+    CHECK(ctx_check(t));
+    if (!W_rows || row_begin < 0 || n_rows < 0 || row_begin + n_rows > t->nrows)
+        return fail(LAL_TAIL_ERR_ARG, "load_lm_head_f32: bad row range");
+    const int d = t->cfg.n_embd;
+    const int chunk = std::max(1, (int)((64ull << 20) / (4ull * d)));
+    float *dW = nullptr;
+    CU(cudaMalloc(&dW, 4ull * std::min(chunk, std::max(1, n_rows)) * d));
+    int rc = LAL_TAIL_OK;
+    for (int r = 0; r < n_rows && rc == LAL_TAIL_OK; r += chunk) {
+        const int n = std::min(chunk, n_rows - r);
+        cudaError_t e = cudaMemcpyAsync(dW, W_rows + (size_t)r * d, 4ull * n * d,
+                                        cudaMemcpyHostToDevice, t->stream);
+        if (e == cudaSuccess)
+            e = launch_quantize_rows(dW, d, t->W + (size_t)(row_begin + r) * t->ld, t->ld,
+                                     t->sw + row_begin + r, n, t->stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(t->stream);
+        if (e != cudaSuccess) rc = fail(LAL_TAIL_ERR_CUDA, "load_lm_head_f32: %s", cudaGetErrorString(e));
+    }
+    cudaFree(dW);
+    if (rc == LAL_TAIL_OK && row_begin + n_rows == t->nrows) t->loaded = true;
+    return rc;
+}
+
+int lal_tail_read_lm_head(lal_tail *t, int8_t *wte_q_rows, float *scale_w_rows) {
+    CHECK(ctx_check(t));
+    if (wte_q_rows)
+        CU(cudaMemcpy2D(wte_q_rows, t->cfg.n_embd, t->W, t->ld, t->cfg.n_embd, t->nrows,
+                        cudaMemcpyDeviceToHost));
+    if (scale_w_rows) CU(cudaMemcpy(scale_w_rows, t->sw, 4ull * t->nrows, cudaMemcpyDeviceToHost));
+    return LAL_TAIL_OK;
+}
+
+int lal_tail_set_sampling(lal_tail *t, int n_streams, const float *temperature,
+                          const int *top_k, const float *rep_penalty) {
+    CHECK(ctx_check(t));
+    if (n_streams < 1 || n_streams > t->cfg.max_streams || !temperature || !top_k || !rep_penalty)
+        return fail(LAL_TAIL_ERR_ARG, "set_sampling: bad arguments");
+    for (int b = 0; b < n_streams; ++b) {
+        const bool greedy = temperature[b] <= 0.0f || top_k[b] <= 0;
+        if (!greedy && top_k[b] > t->cfg.max_top_k)
+            return fail(LAL_TAIL_ERR_ARG, "top_k %d above the context's max_top_k %d", top_k[b],
+                        t->cfg.max_top_k);
+    }
+    CU(cudaMemcpyAsync(t->temp, temperature, 4ull * n_streams, cudaMemcpyHostToDevice, t->stream));
+    CU(cudaMemcpyAsync(t->topk, top_k, 4ull * n_streams, cudaMemcpyHostToDevice, t->stream));
+    CU(cudaMemcpyAsync(t->pen, rep_penalty, 4ull * n_streams, cudaMemcpyHostToDevice, t->stream));
+    CU(cudaStreamSynchronize(t->stream));
+    for (int b = 0; b < n_streams; ++b) {
+        t->h_temp[b] = temperature[b];
+        t->h_topk[b] = top_k[b];
+        t->h_pen[b] = rep_penalty[b];
+    }
+    t->n_set = n_streams;
+    return LAL_TAIL_OK;
+}
+
+int lal_tail_set_history(lal_tail *t, int stream, const int *recent, int n_recent) {
+    CHECK(ctx_check(t));
+    if (stream < 0 || stream >= t->cfg.max_streams || n_recent < 0 ||
+        n_recent > t->cfg.history_cap || (n_recent > 0 && !recent))
+        return fail(LAL_TAIL_ERR_ARG, "set_history: bad arguments");
+    const int hc = std::max(1, t->cfg.history_cap);
+    if (n_recent > 0)
+        CU(cudaMemcpyAsync(t->hist_ids + (size_t)stream * hc, recent, 4ull * n_recent,
+                           cudaMemcpyHostToDevice, t->stream));
+    const int zero = 0;
+    CU(cudaMemcpyAsync(t->hist_n + stream, &n_recent, 4, cudaMemcpyHostToDevice, t->stream));
+    CU(cudaMemcpyAsync(t->hist_head + stream, &zero, 4, cudaMemcpyHostToDevice, t->stream));
+    CU(cudaStreamSynchronize(t->stream));
+    return LAL_TAIL_OK;
+}
+
+int lal_tail_get_history(lal_tail *t, int stream, int *recent_out, int *n_out) {
+    CHECK(ctx_check(t));
+    if (stream < 0 || stream >= t->cfg.max_streams)
+        return fail(LAL_TAIL_ERR_ARG, "get_history: bad stream");
+    const int hc = std::max(1, t->cfg.history_cap);
+    int n = 0, head = 0;
+    CU(cudaStreamSynchronize(t->stream));
+    CU(cudaMemcpy(&n, t->hist_n + stream, 4, cudaMemcpyDeviceToHost));
+    CU(cudaMemcpy(&head, t->hist_head + stream, 4, cudaMemcpyDeviceToHost));
+    std::vector<int> ring(hc);
+    CU(cudaMemcpy(ring.data(), t->hist_ids + (size_t)stream * hc, 4ull * hc, cudaMemcpyDeviceToHost));
+    if (n_out) *n_out = n;
+    if (recent_out) /* oldest first: [head, n) then [0, head) */
+        for (int i = 0; i < n; ++i) recent_out[i] = ring[(head + i) % (n < hc ? std::max(n, 1) : hc)];
+    return LAL_TAIL_OK;
+}
+
+int lal_tail_device_buffers(lal_tail *t, float **d_hidden, float **d_u, int **d_tokens) {
+    if (!t) return fail(LAL_TAIL_ERR_ARG, "null context");
+    if (d_hidden) *d_hidden = t->io_in;
+    if (d_u) *d_u = t->io_in + (size_t)t->cfg.max_streams * t->cfg.n_embd;
+    if (d_tokens) *d_tokens = t->io_out;
+    return LAL_TAIL_OK;
+}
+
+int lal_tail_step_device(lal_tail *t, const float *d_hidden, int n_streams, const float *d_u,
+                         int *d_tokens_out) {
+    CHECK(ctx_check(t));
+    if (!d_hidden || !d_u || !d_tokens_out) return fail(LAL_TAIL_ERR_ARG, "step_device: null");
+    return enqueue_step(t, d_hidden, n_streams, d_u, d_tokens_out);
+}
+
+int lal_tail_sync(lal_tail *t) {
+    CHECK(ctx_check(t));
+    int status = 0;
+    CU(cudaMemcpyAsync(&status, t->io_out + t->cfg.max_streams, 4, cudaMemcpyDeviceToHost, t->stream));
+    CU(cudaStreamSynchronize(t->stream));
+    if (status != 0) {
+        CU(cudaMemset(t->io_out + t->cfg.max_streams, 0, 4));
+        return fail(status, "device status %d (%s)", status,
+                    status == LAL_TAIL_ERR_TIMEOUT ? "bounded wait expired"
+                                                   : "candidate set above the built capacity");
+    }
+    return LAL_TAIL_OK;
+}
+
+int lal_tail_step(lal_tail *t, const float *hidden, int n_streams, const float *u,
+                  int *tokens_out) {
+    CHECK(ctx_check(t));
+    if (!hidden || !u || !tokens_out) return fail(LAL_TAIL_ERR_ARG, "step: null argument");
+    if (n_streams < 1 || n_streams > t->cfg.max_streams)
+        return fail(LAL_TAIL_ERR_ARG, "n_streams %d out of range", n_streams);
+    const int B = t->cfg.max_streams, d = t->cfg.n_embd;
+    /* stage hidden and u contiguously in pinned memory: one H2D copy */
+    memcpy(t->h_in, hidden, 4ull * n_streams * d);
+    float *hu = t->h_in + (size_t)n_streams * d;
+    memcpy(hu, u, 4ull * n_streams);
+    float *d_u = t->io_in + (size_t)B * d;
+    CU(cudaMemcpyAsync(t->io_in, t->h_in, 4ull * n_streams * d, cudaMemcpyHostToDevice, t->stream));
+    CU(cudaMemcpyAsync(d_u, hu, 4ull * n_streams, cudaMemcpyHostToDevice, t->stream));
+    CHECK(enqueue_step(t, t->io_in, n_streams, d_u, t->io_out));
+    /* tokens and the status word in one D2H copy */
+    CU(cudaMemcpyAsync(t->h_out, t->io_out, 4ull * n_streams, cudaMemcpyDeviceToHost, t->stream));
+    CU(cudaMemcpyAsync(t->h_out + B, t->io_out + B, 4, cudaMemcpyDeviceToHost, t->stream));
+    CU(cudaStreamSynchronize(t->stream));
+    const int status = t->h_out[B];
+    if (status != 0) {
+        CU(cudaMemset(t->io_out + B, 0, 4));
+        return fail(status, "device status %d (%s)", status,
+                    status == LAL_TAIL_ERR_TIMEOUT ? "bounded wait expired"
+                                                   : "candidate set above the built capacity");
+    }
+    memcpy(tokens_out, t->h_out, 4ull * n_streams);
+    return LAL_TAIL_OK;
+}
+
+int lal_tail_get_diag(lal_tail *t, int stream, lal_tail_diag *out) {
+    CHECK(ctx_check(t));
+    if (stream < 0 || stream >= t->cfg.max_streams || !out)
+        return fail(LAL_TAIL_ERR_ARG, "get_diag: bad arguments");
+    static_assert(sizeof(StreamDiag) == sizeof(lal_tail_diag), "diag layout");
+    CU(cudaStreamSynchronize(t->stream));
+    CU(cudaMemcpy(out, t->diag + stream, sizeof(StreamDiag), cudaMemcpyDeviceToHost));
+    return LAL_TAIL_OK;
+}
+
+int lal_tail_get_logits(lal_tail *t, int stream, float *logits_rows) {
+    CHECK(ctx_check(t));
+    if (stream < 0 || stream >= t->cfg.max_streams || !logits_rows)
+        return fail(LAL_TAIL_ERR_ARG, "get_logits: bad arguments");
+    CU(cudaStreamSynchronize(t->stream));
+    CU(cudaMemcpy(logits_rows, t->logits + (size_t)stream * t->nrows, 4ull * t->nrows,
+                  cudaMemcpyDeviceToHost));
+    return LAL_TAIL_OK;
+}
+
+int lal_tail_set_timing(lal_tail *t, int on) {
+    CHECK(ctx_check(t));
+    t->timing = on != 0;
+    if (t->timing && t->ev.empty()) {
+        t->ev.resize(8192);
+        for (auto &e : t->ev) CU(cudaEventCreate(&e));
+    }
+    t->ev_used = 0;
+    return LAL_TAIL_OK;
+}
+
+int lal_tail_kernel_time(lal_tail *t, double *avg_ms, int *n_launches) {
+    CHECK(ctx_check(t));
+    CU(cudaStreamSynchronize(t->stream));
+    double tot = 0.0;
+    const int n = t->ev_used / 2;
+    for (int i = 0; i < n; ++i) {
+        float ms = 0.0f;
+        CU(cudaEventElapsedTime(&ms, t->ev[2 * i], t->ev[2 * i + 1]));
+        tot += ms;
+    }
+    if (avg_ms) *avg_ms = n ? tot / n : 0.0;
+    if (n_launches) *n_launches = n;
+    t->ev_used = 0;
+    return LAL_TAIL_OK;
+}
+
+}  // extern "C"

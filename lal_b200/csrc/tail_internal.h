@@ -1,0 +1,129 @@
+/*
+ * tail_internal.h -- structures shared by the sm_100a kernels (tail_kernels.cu)
+ * and the C-ABI implementation (tail_api.cu).  Not installed.
+ */
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace lal {
+
+/* Block shape of the streaming kernel: 8 consumer warps (dp4a) + 1 TMA
+ * producer warp. */
+constexpr int kConsumerWarps = 8;
+constexpr int kThreads = (kConsumerWarps + 1) * 32;
+constexpr int kMaxStages = 8;
+/* Extra list slots per CTA beyond k, so that values tied with a CTA's k-th
+ * largest are all reported (tie-complete candidate sets). */
+constexpr int kTieExtra = 32;
+/* Largest grid the merge supports (one CTA per SM on B200 is 148). */
+constexpr int kMaxGrid = 256;
+/* Largest per-CTA row slice (smem holds its logits, scales, penalty counts). */
+constexpr int kMaxRowsPerCta = 4096;
+
+enum Mode : int { MODE_FUSED = 0, MODE_LMHEAD = 1, MODE_SAMPLE = 2 };
+enum Variant : int { VARIANT_LIBRARY = 0, VARIANT_SERVER = 1 };
+
+/* Device status word values (mirrors LAL_TAIL_ERR_* in include/lal_tail.h). */
+enum DevStatus : int { DEV_OK = 0, DEV_TIMEOUT = 4, DEV_CAPACITY = 5 };
+
+/* One per (stream, CTA): the CTA's candidate list summary. */
+struct CtaRecord {
+    uint32_t cut_key;     /* key of the CTA's k-th largest (valid if n_local >= k) */
+    int n_local;          /* rows in the CTA slice                                 */
+    int n_out;            /* entries written to the list                           */
+    int overflow;         /* 1 if ties at cut_key did not fit the list             */
+};
+
+/* Per-stream outputs of a sampling launch (same layout as lal_tail_diag). */
+struct StreamDiag {
+    float threshold, max_l, sum, r;
+    int n_cand, greedy, drew, token;
+};
+
+struct TailParams {
+    int mode, variant;
+    /* LM head slice: row-major [rows][ld] int8, ld % 16 == 0, zero padded. */
+    const int8_t *W;
+    const float *scale_w;
+    int rows;          /* rows covered by this launch                        */
+    int row_base;      /* vocab index of local row 0                         */
+    int vocab;         /* the whole vocabulary V                             */
+    int d, ld;
+    /* inputs */
+    const float *hidden;     /* FUSED: [B][d]                                 */
+    const int8_t *xq_in;     /* LMHEAD: quantized vector [d]                  */
+    float scale_x_in;        /* LMHEAD                                        */
+    /* LMHEAD: local rows < trunc_rows_end sum only columns < trunc_cols (the
+     * 8-row form's dropped tail, runtime/lal_q8_kernel.h:577-611); otherwise
+     * trunc_cols = ld. */
+    int trunc_cols, trunc_rows_end;
+    float *logits;           /* [B][rows]: written (FUSED/LMHEAD), in/out (SAMPLE) */
+    int B;
+    const float *temperature;
+    const int *top_k;
+    const float *rep_penalty;
+    const float *u;
+    /* penalty history: ids[b*hist_cap + i] for i < hist_n[b] */
+    int *hist_ids, *hist_n, *hist_head;
+    int hist_cap;
+    int push_history;
+    /* outputs */
+    int *tokens;
+    StreamDiag *diag;
+    /* scratch (global memory beyond inputs and outputs) */
+    CtaRecord *recs;         /* [B][grid]                                     */
+    uint32_t *rec_keys;      /* [B][grid][list_cap]                           */
+    int *rec_idx;            /* [B][grid][list_cap]                           */
+    int list_cap;
+    unsigned int *counter;   /* [B] arrival tickets, self-resetting           */
+    int *status;             /* device status word                            */
+    /* optional export of the candidate set (ascending vocab order) */
+    float *cand_val_out;
+    int *cand_idx_out;
+    int cand_out_cap;
+    int candidates_only;     /* stop after exporting candidates (no draw)     */
+    /* glibc expf fix-ups */
+    const uint32_t *expf_x, *expf_y;
+    int expf_n;
+    /* shared-memory layout (bytes) */
+    int stages, rows_per_stage, stage_bytes, area_bytes;
+    int off_bars, off_xq, off_sw, off_lg, off_cnt, off_misc, smem_total;
+    int rows_per_cta_max;
+    int nch;                 /* 512-byte column chunks per row                */
+};
+
+/* Second half of the server sampler with a level-2 filter
+ * (tools/server/qwen7b_server.c:271-294) over an exported candidate list:
+ * phase 0 computes max, weights, running sums and the argmax fallback over
+ * the kept candidates; phase 1 draws with u. */
+struct FinishParams {
+    const float *cand_val;
+    const int *cand_idx;
+    const int *keep;
+    int m;
+    float temperature;
+    int vocab;
+    const float *u;
+    float *prefix;           /* [m] scratch                                    */
+    StreamDiag *diag;
+    int *token;
+    int phase;
+    const uint32_t *expf_x, *expf_y;
+    int expf_n;
+};
+
+/* Host-side launchers (tail_kernels.cu). */
+cudaError_t launch_finish(const FinishParams &f, cudaStream_t st);
+int plan_launch(TailParams &p, int num_sms, int min_rows_per_cta);
+cudaError_t launch_tail(const TailParams &p, int grid, cudaStream_t st);
+cudaError_t launch_quantize_x(const float *x, int8_t *xq, float *scale, int n,
+                              cudaStream_t st);
+cudaError_t launch_abs_xq(const int8_t *xq, uint8_t *ax, int n, cudaStream_t st);
+cudaError_t launch_quantize_rows(const float *W, int d, int8_t *q, int ld,
+                                 float *scale, int n_rows, cudaStream_t st);
+cudaError_t launch_debug_expf(const float *x, float *y, int n, const uint32_t *tx,
+                              const uint32_t *ty, int tn, cudaStream_t st);
+
+}  // namespace lal

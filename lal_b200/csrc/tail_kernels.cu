@@ -1,0 +1,951 @@
+/*
+ * tail_kernels.cu -- sm_100a kernels of the LAL decode tail.
+ *
+ * The streaming kernel (tail_kernel) handles one stream (B = 1) and has three
+ * modes that share one body:
+ *
+ *   MODE_FUSED   hidden fp32 -> int8 quantize (prologue, every CTA) -> int8
+ *                GEMV over this CTA's slice of vocab rows -> logits with the
+ *                reference's scale epilogue -> repetition penalty -> per-CTA
+ *                tie-complete top-k list -> the last CTA to finish merges the
+ *                lists, runs the ordered softmax and the draw, and pushes
+ *                the token into the device-resident history.
+ *   MODE_LMHEAD  the GEMV + scale epilogue only (runtime/lal_q8_kernel.h:463
+ *                drop-in): quantized vector in, logits out.
+ *   MODE_SAMPLE  logits in (host copy), penalty written back, then the same
+ *                select / merge / draw (runtime/lal_sampling.h:46 drop-in).
+ *
+ * Data movement: each CTA owns a contiguous slice of rows, which is one
+ * contiguous byte range of the row-major LM head; a producer warp streams it
+ * into a ring of shared-memory stages with cp.async.bulk (TMA, no
+ * multicast, L2 evict-first) completing on mbarriers, and 8 consumer warps
+ * each take whole rows: every lane holds its 16-byte columns of the quantized
+ * vector in registers and does 4 dp4a per 16 bytes of weights; a warp
+ * reduction (redux.sync) gives the exact int32 dot.
+ *
+ * Exactness: all float steps use explicit round-to-nearest intrinsics in the
+ * reference's order (scale_x*scale_w[v] then *(float)dot; penalty divide or
+ * multiply once per history occurrence; (l-max_l)/T; sequential float sum in
+ * ascending vocab order); the file is compiled with -fmad=false.  The
+ * softmax weights use lal_expf_glibc (lal_expf.h), equal to glibc expf.
+ */
+#include "tail_internal.h"
+#include "lal_expf.h"
+
+#include <cstdio>
+
+namespace lal {
+namespace {
+
+constexpr int NT = kThreads;
+constexpr int NWARP = NT / 32;
+
+/* ---------------------------------------------------------------- PTX --- */
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ uint64_t gtimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ void mbar_init(uint64_t *b, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count)
+                 : "memory");
+}
+__device__ __forceinline__ void mbar_fence_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *b, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)),
+                 "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *b) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint64_t *b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+/* Every wait is bounded: it gives up after kWaitNs of wall time (globaltimer)
+ * or as soon as another warp of the CTA has given up. */
+constexpr uint64_t kWaitNs = 2000000000ull;
+__device__ bool mbar_wait(uint64_t *b, uint32_t parity, volatile int *abort_flag) {
+    if (mbar_try(b, parity)) return true;
+    const uint64_t t0 = gtimer();
+    for (uint32_t it = 1;; ++it) {
+        if (mbar_try(b, parity)) return true;
+        if ((it & 63u) == 0) {
+            if (*abort_flag) return false;
+            if (gtimer() - t0 > kWaitNs) return false;
+        }
+    }
+}
+__device__ __forceinline__ uint64_t policy_evict_first() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+/* Bulk (non-tensor) TMA copy global -> this CTA's shared memory. */
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes,
+                                         uint64_t *bar, uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1], %2, [%3], %4;" ::"r"(smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
+        : "memory");
+}
+
+/* ------------------------------------------------------- order keys --- */
+/* Monotone map float -> uint32 (larger float, larger key).  -0 maps like +0,
+ * so key equality is float equality, as the reference's comparisons treat it. */
+__device__ __forceinline__ uint32_t f2key(float f) {
+    uint32_t u = __float_as_uint(f);
+    if (u == 0x80000000u) u = 0u;
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float key2f(uint32_t k) {
+    return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
+}
+
+/* ------------------------------------------------- block primitives --- */
+struct Misc {
+    uint32_t hist[256];
+    uint32_t scan[NWARP + 1];
+    uint32_t sh[8];
+    float fred[NWARP];
+    float sx;
+    float sum;
+    int abort_flag;
+    int ticket;
+    int found;
+    uint32_t cut[kMaxGrid];
+    int nout[kMaxGrid];
+    int flags[kMaxGrid];
+};
+
+/* Exclusive prefix (thread order) of one value per thread; *total = sum. */
+__device__ __forceinline__ uint32_t block_scan_excl(uint32_t v, Misc *ms, uint32_t *total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    uint32_t x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) ms->scan[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+        uint32_t w = lane < NWARP ? ms->scan[lane] : 0u;
+        uint32_t incl = w;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += y;
+        }
+        if (lane < NWARP) ms->scan[lane] = incl - w;
+        if (lane == NWARP - 1) ms->scan[NWARP] = incl;
+    }
+    __syncthreads();
+    const uint32_t res = ms->scan[warp] + x - v;
+    *total = ms->scan[NWARP];
+    __syncthreads();
+    return res;
+}
+
+__device__ __forceinline__ float block_max_f(float v, Misc *ms) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if (lane == 0) ms->fred[warp] = v;
+    __syncthreads();
+    float r = ms->fred[0];
+#pragma unroll
+    for (int w = 1; w < NWARP; ++w) r = fmaxf(r, ms->fred[w]);
+    __syncthreads();
+    return r;
+}
+
+/* k-th largest key (1 <= k <= n) of get(0..n-1): MSB-first radix select with
+ * 8-bit digits; histogram adds are aggregated per warp (match.any). */
+template <class Get>
+__device__ uint32_t block_kth_largest(Get get, int n, int k, Misc *ms) {
+    uint32_t prefix = 0, mask = 0;
+    int krem = k;
+    for (int shift = 24; shift >= 0; shift -= 8) {
+        for (int i = threadIdx.x; i < 256; i += NT) ms->hist[i] = 0;
+        __syncthreads();
+        for (int i0 = 0; i0 < n; i0 += NT) {
+            const int i = i0 + threadIdx.x;
+            const bool act = i < n;
+            const uint32_t key = act ? get(i) : 0u;
+            const bool m = act && ((key & mask) == prefix);
+            const uint32_t digit = (key >> shift) & 0xFFu;
+            const unsigned voters = __ballot_sync(0xffffffffu, m);
+            if (m) {
+                const unsigned peers = __match_any_sync(voters, digit);
+                if ((int)(threadIdx.x & 31) == __ffs(peers) - 1)
+                    atomicAdd(&ms->hist[digit], (uint32_t)__popc(peers));
+            }
+        }
+        __syncthreads();
+        if (threadIdx.x < 32) {
+            const int lane = threadIdx.x;
+            uint32_t c[8], s = 0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                c[j] = ms->hist[255 - 8 * lane - j];
+                s += c[j];
+            }
+            uint32_t incl = s;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += y;
+            }
+            const uint32_t excl = incl - s;
+            if (excl < (uint32_t)krem && (uint32_t)krem <= incl) {
+                uint32_t run = excl;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    if (run + c[j] >= (uint32_t)krem) {
+                        ms->sh[0] = 255u - 8u * lane - j;
+                        ms->sh[1] = run;
+                        break;
+                    }
+                    run += c[j];
+                }
+            }
+        }
+        __syncthreads();
+        const uint32_t digit = ms->sh[0];
+        krem -= (int)ms->sh[1];
+        prefix |= digit << shift;
+        mask |= 0xFFu << shift;
+        __syncthreads();
+    }
+    return prefix;
+}
+
+/* Penalty for one logit with `count` history occurrences, one step per
+ * occurrence as runtime/lal_sampling.h:63-64 does (not a power). */
+__device__ __forceinline__ float penalise(float l, uint32_t count, float pen) {
+    for (uint32_t c = 0; c < count; ++c) l = (l > 0.0f) ? __fdiv_rn(l, pen) : __fmul_rn(l, pen);
+    return l;
+}
+
+/* ----------------------------------------------------- the kernel --- */
+template <int MODE, int NCH>
+__global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ TailParams p) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int G = gridDim.x, cta = blockIdx.x;
+    const int c0 = (int)((long long)p.rows * cta / G);
+    const int c1 = (int)((long long)p.rows * (cta + 1) / G);
+    const int nloc = c1 - c0;
+
+    uint64_t *full_bar = reinterpret_cast<uint64_t *>(smem + p.off_bars);
+    uint64_t *empty_bar = full_bar + kMaxStages;
+    int8_t *xq_s = reinterpret_cast<int8_t *>(smem + p.off_xq);
+    float *sw_s = reinterpret_cast<float *>(smem + p.off_sw);
+    float *lg_s = reinterpret_cast<float *>(smem + p.off_lg);
+    uint32_t *cnt_s = reinterpret_cast<uint32_t *>(smem + p.off_cnt);
+    Misc *ms = reinterpret_cast<Misc *>(smem + p.off_misc);
+
+    /* stream 0 sampling parameters */
+    float temp = 0.0f, pen = 1.0f;
+    int topk = 0, hn = 0;
+    if (MODE != MODE_LMHEAD) {
+        temp = p.temperature[0];
+        topk = p.top_k[0];
+        pen = p.rep_penalty[0];
+        hn = p.hist_n ? p.hist_n[0] : 0;
+    }
+    const bool greedy = (temp <= 0.0f) || (topk <= 0);
+    const bool use_pen = (MODE != MODE_LMHEAD) && (pen > 1.0f) && hn > 0 &&
+                         (p.variant == VARIANT_SERVER || !greedy);
+
+    /* ---- phase 0: barriers, quantized vector, scales, penalty counts ---- */
+    if (tid == 0) {
+        ms->abort_flag = 0;
+        if (MODE != MODE_SAMPLE) {
+            for (int s = 0; s < p.stages; ++s) {
+                mbar_init(&full_bar[s], 1);
+                mbar_init(&empty_bar[s], kConsumerWarps);
+            }
+            mbar_fence_init();
+        }
+    }
+    if (MODE == MODE_FUSED) {
+        /* lal_quantize_x_int8 (runtime/lal_q8_kernel.h:375-424), redundantly
+         * per CTA: absmax, scale = max/127 floored at 1e-8, inv = 1/scale,
+         * RNE for the first d&~7 elements and truncation for the tail. */
+        const float *h = p.hidden;
+        float m = 0.0f;
+        for (int i = tid; i < p.d; i += NT) m = fmaxf(m, fabsf(h[i]));
+        m = block_max_f(m, ms);
+        float scale = __fdiv_rn(m, 127.0f);
+        if (scale < 1e-8f) scale = 1e-8f;
+        const float inv = __fdiv_rn(1.0f, scale);
+        const int n8 = p.d & ~7;
+        for (int i = tid; i < p.ld; i += NT) {
+            int v = 0;
+            if (i < p.d) {
+                const float s = __fmul_rn(h[i], inv);
+                if (s != s) v = -127;
+                else {
+                    v = (i < n8) ? __float2int_rn(s) : __float2int_rz(s);
+                    v = v > 127 ? 127 : (v < -127 ? -127 : v);
+                }
+            }
+            xq_s[i] = (int8_t)v;
+        }
+        if (tid == 0) ms->sx = scale;
+    } else if (MODE == MODE_LMHEAD) {
+        for (int i = tid; i < p.ld; i += NT) xq_s[i] = i < p.d ? p.xq_in[i] : (int8_t)0;
+        if (tid == 0) ms->sx = p.scale_x_in;
+    }
+    if (MODE != MODE_SAMPLE)
+        for (int i = tid; i < nloc; i += NT) sw_s[i] = p.scale_w[c0 + i];
+    if (MODE != MODE_LMHEAD) {
+        for (int i = tid; i < nloc; i += NT) cnt_s[i] = 0u;
+        __syncthreads();
+        if (use_pen) {
+            /* runtime/lal_sampling.h:60-66: ids outside [0, V) are skipped */
+            for (int i = tid; i < hn; i += NT) {
+                const int t = p.hist_ids[i];
+                if (t < 0 || t >= p.vocab) continue;
+                const int g = t - p.row_base;
+                if (g >= c0 && g < c1) atomicAdd(&cnt_s[g - c0], 1u);
+            }
+        }
+    }
+    __syncthreads();
+
+    /* ---- phase 1: logits of this CTA's rows --------------------------- */
+    if (MODE != MODE_SAMPLE) {
+        const int R = p.rows_per_stage;
+        const int n_chunks = (nloc + R - 1) / R;
+        if (warp == kConsumerWarps) {
+            /* producer: one elected lane streams the slice, chunk by chunk */
+            if (lane == 0) {
+                const uint64_t pol = policy_evict_first();
+                int c = 0;
+                for (; c < n_chunks; ++c) {
+                    const int s = c % p.stages;
+                    const uint32_t use = (uint32_t)(c / p.stages);
+                    if (c >= p.stages && !mbar_wait(&empty_bar[s], (use & 1u) ^ 1u, &ms->abort_flag)) {
+                        ms->abort_flag = 1;
+                        break;
+                    }
+                    const int r0 = c0 + c * R;
+                    const int nr = min(R, c1 - r0);
+                    const uint32_t bytes = (uint32_t)nr * (uint32_t)p.ld;
+                    mbar_expect_tx(&full_bar[s], bytes);
+                    bulk_g2s(smem + (size_t)s * p.stage_bytes, p.W + (size_t)r0 * p.ld, bytes,
+                             &full_bar[s], pol);
+                }
+                /* Do not leave copies in flight: wait (bounded) for the last
+                 * issued stages to land before the CTA may exit. */
+                for (int q = max(0, c - p.stages); q < c; ++q) {
+                    const int s = q % p.stages;
+                    mbar_wait(&full_bar[s], (uint32_t)(q / p.stages) & 1u, &ms->abort_flag);
+                }
+            }
+        } else {
+            const float sx = ms->sx;
+            int4 xr[NCH];
+#pragma unroll
+            for (int j = 0; j < NCH; ++j) {
+                const int col = j * 512 + lane * 16;
+                xr[j] = col < p.ld ? *reinterpret_cast<const int4 *>(xq_s + col)
+                                   : make_int4(0, 0, 0, 0);
+            }
+            for (int c = 0; c < n_chunks; ++c) {
+                const int s = c % p.stages;
+                if (!mbar_wait(&full_bar[s], (uint32_t)(c / p.stages) & 1u, &ms->abort_flag)) {
+                    ms->abort_flag = 1;
+                    break;
+                }
+                const int r0 = c0 + c * R;
+                const int nr = min(R, c1 - r0);
+                const uint8_t *st = smem + (size_t)s * p.stage_bytes;
+                for (int rr = warp; rr < nr; rr += kConsumerWarps) {
+                    const uint8_t *row = st + (size_t)rr * p.ld;
+                    int acc = 0, acc_tail = 0;
+#pragma unroll
+                    for (int j = 0; j < NCH; ++j) {
+                        const int col = j * 512 + lane * 16;
+                        if (col < p.ld) {
+                            const int4 w = *reinterpret_cast<const int4 *>(row + col);
+                            int part = __dp4a(w.x, xr[j].x, 0);
+                            part = __dp4a(w.y, xr[j].y, part);
+                            part = __dp4a(w.z, xr[j].z, part);
+                            part = __dp4a(w.w, xr[j].w, part);
+                            if (MODE == MODE_LMHEAD && col >= p.trunc_cols) acc_tail += part;
+                            else acc += part;
+                        }
+                    }
+                    acc = __reduce_add_sync(0xffffffffu, acc);
+                    if (MODE == MODE_LMHEAD && p.trunc_cols < p.ld) {
+                        acc_tail = __reduce_add_sync(0xffffffffu, acc_tail);
+                        if (r0 + rr >= p.trunc_rows_end) acc += acc_tail;
+                    }
+                    if (lane == 0) {
+                        const int lr = r0 + rr - c0;
+                        /* runtime/lal_q8_kernel.h:489: scale_x*scale_w[v]*(float)dot */
+                        float l = __fmul_rn(__fmul_rn(sx, sw_s[lr]), __int2float_rn(acc));
+                        if (MODE == MODE_FUSED) {
+                            l = penalise(l, cnt_s[lr], pen);
+                            lg_s[lr] = l;
+                        }
+                        p.logits[c0 + lr] = l;
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty_bar[s]);
+            }
+        }
+        __syncthreads();
+        if (MODE == MODE_LMHEAD) {
+            if (tid == 0 && ms->abort_flag) atomicCAS(p.status, 0, (int)DEV_TIMEOUT);
+            return;
+        }
+    } else {
+        for (int i = tid; i < nloc; i += NT) {
+            float l = p.logits[c0 + i];
+            const uint32_t cnt = cnt_s[i];
+            if (cnt) {
+                l = penalise(l, cnt, pen);
+                p.logits[c0 + i] = l; /* the reference mutates logits in place */
+            }
+            lg_s[i] = l;
+        }
+        __syncthreads();
+    }
+
+    /* ---- phase 2: this CTA's candidate list ---------------------------- *
+     * k = min(top_k, V) (runtime/lal_sampling.h:70-71); greedy is k = 1 with
+     * the lowest index among the maxima.  The list holds every local entry
+     * >= the local k-th largest (all ties, up to list_cap), in index order. */
+    int k = greedy ? 1 : topk;
+    if (k > p.vocab) k = p.vocab;
+    if (k < 1) k = 1;
+    const bool tie_complete = !greedy;
+    {
+        const int kloc = min(k, nloc);
+        const uint32_t T = block_kth_largest([&](int i) { return f2key(lg_s[i]); }, nloc, kloc, ms);
+        const int seg = (nloc + NT - 1) / NT;
+        const int i0 = min(nloc, tid * seg), i1 = min(nloc, i0 + seg);
+        uint32_t ngt = 0, neq = 0;
+        for (int i = i0; i < i1; ++i) {
+            const uint32_t key = f2key(lg_s[i]);
+            ngt += key > T;
+            neq += key == T;
+        }
+        uint32_t tot;
+        const uint32_t ex = block_scan_excl((ngt << 16) | neq, ms, &tot);
+        const uint32_t gt_tot = tot >> 16, eq_tot = tot & 0xFFFFu, eq_before = ex & 0xFFFFu;
+        const uint32_t need_eq = tie_complete ? eq_tot : (uint32_t)kloc - gt_tot;
+        const uint32_t my_eq = need_eq > eq_before ? min(neq, need_eq - eq_before) : 0u;
+        uint32_t nsel_tot;
+        uint32_t pos = block_scan_excl(ngt + my_eq, ms, &nsel_tot);
+        uint32_t *out_key = p.rec_keys + (size_t)cta * p.list_cap;
+        int *out_idx = p.rec_idx + (size_t)cta * p.list_cap;
+        uint32_t eqr = eq_before;
+        for (int i = i0; i < i1; ++i) {
+            const uint32_t key = f2key(lg_s[i]);
+            bool sel = key > T;
+            if (key == T) {
+                sel = eqr < need_eq;
+                ++eqr;
+            }
+            if (sel) {
+                if (pos < (uint32_t)p.list_cap) {
+                    out_key[pos] = key;
+                    out_idx[pos] = p.row_base + c0 + i;
+                }
+                ++pos;
+            }
+        }
+        if (tid == 0) {
+            CtaRecord r;
+            r.cut_key = T;
+            r.n_local = nloc;
+            r.n_out = (int)min(nsel_tot, (uint32_t)p.list_cap);
+            r.overflow = nsel_tot > (uint32_t)p.list_cap ? 1 : 0;
+            p.recs[cta] = r;
+            if (ms->abort_flag) atomicCAS(p.status, 0, (int)DEV_TIMEOUT);
+        }
+    }
+
+    /* ---- phase 3: the last CTA to arrive merges ------------------------ */
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) ms->ticket = (int)atomicAdd(&p.counter[0], 1u);
+    __syncthreads();
+    if (ms->ticket != G - 1) return;
+    __threadfence();
+
+    /* merge buffers reuse the stage area */
+    uint32_t *Bk = reinterpret_cast<uint32_t *>(smem);
+    int *Bi = reinterpret_cast<int *>(smem + (size_t)G * p.list_cap * 4);
+    const int cand_cap = (int)((p.area_bytes - (long long)G * p.list_cap * 8) / 12);
+    float *Cv = reinterpret_cast<float *>(smem + (size_t)G * p.list_cap * 8);
+    int *Ci = reinterpret_cast<int *>(Cv + cand_cap);
+    float *Ce = reinterpret_cast<float *>(Ci + cand_cap);
+
+    for (int g = tid; g < G; g += NT) {
+        const int4 raw = __ldcg(reinterpret_cast<const int4 *>(p.recs + g));
+        ms->cut[g] = (uint32_t)raw.x;
+        ms->nout[g] = raw.z;
+        ms->flags[g] = (raw.y >= k ? 1 : 0) | (raw.w ? 2 : 0);
+    }
+    if (tid == 0) ms->sh[4] = 0u;
+    __syncthreads();
+    /* Lower bound: the global k-th largest T is >= every full list's cut. */
+    for (int g = tid; g < G; g += NT)
+        if (ms->flags[g] & 1) atomicMax(&ms->sh[4], ms->cut[g]);
+    __syncthreads();
+    const uint32_t L = ms->sh[4];
+
+    /* gather list entries >= L, preserving (CTA, position) = vocab order */
+    const int Fn = G * p.list_cap;
+    {
+        const int seg = (Fn + NT - 1) / NT;
+        const int e0 = min(Fn, tid * seg), e1 = min(Fn, e0 + seg);
+        uint32_t cnt = 0;
+        for (int e = e0; e < e1; ++e) {
+            const int g = e / p.list_cap, j = e - g * p.list_cap;
+            if (j < ms->nout[g] && __ldcg(p.rec_keys + e) >= L) ++cnt;
+        }
+        uint32_t M;
+        uint32_t pos = block_scan_excl(cnt, ms, &M);
+        for (int e = e0; e < e1; ++e) {
+            const int g = e / p.list_cap, j = e - g * p.list_cap;
+            if (j < ms->nout[g]) {
+                const uint32_t key = __ldcg(p.rec_keys + e);
+                if (key >= L) {
+                    Bk[pos] = key;
+                    Bi[pos] = __ldcg(p.rec_idx + e);
+                    ++pos;
+                }
+            }
+        }
+        if (tid == 0) ms->sh[5] = M;
+    }
+    __syncthreads();
+    const int M = (int)ms->sh[5];
+    const int kk = min(k, M);
+    const uint32_t T = block_kth_largest([&](int i) { return Bk[i]; }, M, kk, ms);
+
+    /* A list whose ties at its cut did not fit is only a problem when that
+     * cut is a candidate value. */
+    if (tid == 0) ms->found = 0;
+    __syncthreads();
+    if (tie_complete)
+        for (int g = tid; g < G; g += NT)
+            if ((ms->flags[g] & 2) && ms->cut[g] >= T) ms->found = 1;
+    __syncthreads();
+    const bool overflow = ms->found != 0;
+
+    /* candidates {v : l[v] >= T} in ascending vocab order */
+    int m;
+    {
+        const int seg = (M + NT - 1) / NT;
+        const int e0 = min(M, tid * seg), e1 = min(M, e0 + seg);
+        uint32_t cnt = 0;
+        for (int e = e0; e < e1; ++e) cnt += Bk[e] >= T;
+        uint32_t mt;
+        uint32_t pos = block_scan_excl(cnt, ms, &mt);
+        m = (int)mt;
+        if (m <= cand_cap) {
+            /* Bk/Bi and Cv/Ci do not overlap; read all before writing is not
+             * needed. */
+            for (int e = e0; e < e1; ++e)
+                if (Bk[e] >= T) {
+                    Cv[pos] = key2f(Bk[e]);
+                    Ci[pos] = Bi[e];
+                    ++pos;
+                }
+        }
+    }
+    __syncthreads();
+
+    StreamDiag dg;
+    dg.threshold = key2f(T);
+    dg.max_l = 0.0f;
+    dg.sum = 0.0f;
+    dg.r = 0.0f;
+    dg.n_cand = m;
+    dg.greedy = greedy ? 1 : 0;
+    dg.drew = 0;
+    dg.token = -1;
+    const int dev_status = __ldcg(p.status);
+    if (dev_status != 0 || overflow || m > cand_cap || m < 1) {
+        if (tid == 0) {
+            if (dev_status == 0) atomicCAS(p.status, 0, (int)DEV_CAPACITY);
+            p.tokens[0] = -1;
+            p.diag[0] = dg;
+            p.counter[0] = 0u;
+        }
+        return;
+    }
+
+    if (p.cand_val_out != nullptr && m <= p.cand_out_cap) {
+        for (int i = tid; i < m; i += NT) {
+            p.cand_val_out[i] = Cv[i];
+            p.cand_idx_out[i] = Ci[i];
+        }
+    }
+    if (p.candidates_only) {
+        if (tid == 0) {
+            p.diag[0] = dg;
+            p.counter[0] = 0u;
+        }
+        return;
+    }
+
+    /* max over candidates, floored at -1e30f (runtime/lal_sampling.h:107-109) */
+    float mx = -1e30f;
+    for (int i = tid; i < m; i += NT) mx = fmaxf(mx, Cv[i]);
+    const float max_l = block_max_f(mx, ms);
+    dg.max_l = max_l;
+    int token;
+    if (greedy) {
+        token = Ci[0];
+    } else {
+        /* weights expf((l - max_l) / T) (runtime/lal_sampling.h:112) */
+        for (int i = tid; i < m; i += NT) {
+            const float x = __fdiv_rn(__fsub_rn(Cv[i], max_l), temp);
+            Ce[i] = lal_expf_glibc(x, p.expf_x, p.expf_y, p.expf_n);
+        }
+        __syncthreads();
+        /* sequential float sum in ascending vocab order; keep the prefix */
+        if (tid == 0) {
+            float acc = 0.0f;
+            for (int i = 0; i < m; ++i) {
+                acc = __fadd_rn(acc, Ce[i]);
+                Ce[i] = acc;
+            }
+            ms->sum = acc;
+            ms->found = 0x7fffffff;
+        }
+        __syncthreads();
+        const float sum = ms->sum;
+        dg.sum = sum;
+        if (p.variant == VARIANT_SERVER && sum <= 0.0f) {
+            /* tools/server/qwen7b_server.c:285-286: argmax over the kept
+             * candidates with '>' from -1e30f, no draw */
+            token = 0;
+            float bv = -1e30f;
+            if (tid == 0)
+                for (int i = 0; i < m; ++i)
+                    if (Cv[i] > bv) {
+                        bv = Cv[i];
+                        token = Ci[i];
+                    }
+        } else {
+            /* r = u * sum; first candidate with r <= running sum
+             * (runtime/lal_sampling.h:116-124) */
+            const float r = __fmul_rn(p.u[0], sum);
+            dg.r = r;
+            dg.drew = 1;
+            int first = 0x7fffffff;
+            for (int i = tid; i < m; i += NT)
+                if (r <= Ce[i]) {
+                    first = i;
+                    break;
+                }
+            if (first != 0x7fffffff) atomicMin(&ms->found, first);
+            __syncthreads();
+            token = ms->found != 0x7fffffff ? Ci[ms->found] : p.vocab - 1;
+        }
+    }
+    if (tid == 0) {
+        dg.token = token;
+        p.tokens[0] = token;
+        p.diag[0] = dg;
+        if (p.push_history && p.hist_cap > 0) {
+            /* runtime/lal_sampling.h:133-136 as a ring: FIFO at hist_cap */
+            const int n = p.hist_n[0];
+            if (n < p.hist_cap) {
+                p.hist_ids[n] = token;
+                p.hist_n[0] = n + 1;
+            } else {
+                const int h = p.hist_head[0];
+                p.hist_ids[h] = token;
+                p.hist_head[0] = (h + 1) % p.hist_cap;
+            }
+        }
+        p.counter[0] = 0u;
+    }
+}
+
+/* ------------------------------------------------- auxiliary kernels --- */
+
+/* lal_quantize_x_int8 for the drop-in: one CTA. */
+__global__ void __launch_bounds__(NT) quantize_x_kernel(const float *x, int8_t *xq,
+                                                        float *scale_out, int n) {
+    __shared__ Misc ms;
+    float m = 0.0f;
+    for (int i = threadIdx.x; i < n; i += NT) m = fmaxf(m, fabsf(x[i]));
+    m = block_max_f(m, &ms);
+    float scale = __fdiv_rn(m, 127.0f);
+    if (scale < 1e-8f) scale = 1e-8f;
+    const float inv = __fdiv_rn(1.0f, scale);
+    const int n8 = n & ~7;
+    for (int i = threadIdx.x; i < n; i += NT) {
+        const float s = __fmul_rn(x[i], inv);
+        int v;
+        if (s != s) v = -127;
+        else {
+            v = (i < n8) ? __float2int_rn(s) : __float2int_rz(s);
+            v = v > 127 ? 127 : (v < -127 ? -127 : v);
+        }
+        xq[i] = (int8_t)v;
+    }
+    if (threadIdx.x == 0) *scale_out = scale;
+}
+
+__global__ void abs_xq_kernel(const int8_t *xq, uint8_t *ax, int n) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) {
+        const int v = xq[i];
+        ax[i] = (uint8_t)(v < 0 ? -v : v);
+    }
+}
+
+/* lroundf without the library: round half away from zero (exact for the
+ * |v| < 2^23 range the quantizer sees; larger values are already integers). */
+__device__ __forceinline__ int round_half_away(float v) {
+    const float t = truncf(v);
+    const float frac = __fsub_rn(v, t);
+    float r = t;
+    if (frac >= 0.5f) r = __fadd_rn(t, 1.0f);
+    else if (frac <= -0.5f) r = __fsub_rn(t, 1.0f);
+    if (r > 2147483520.0f) return 0x7fffffff;
+    if (r < -2147483648.0f) return (int)0x80000000u;
+    return (int)r;
+}
+
+/* lal_quantize_q8_per_row (runtime/lal_q8_kernel.h:357-372): one warp per
+ * row; absmax, scale = max/127 floored at 1e-8, q = clamp(lroundf(w*inv)). */
+__global__ void __launch_bounds__(256) quantize_rows_kernel(const float *W, int d, int8_t *q,
+                                                            int ld, float *scale, int n_rows) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (warp >= n_rows) return;
+    const float *row = W + (size_t)warp * d;
+    float m = 0.0f;
+    for (int i = lane; i < d; i += 32) m = fmaxf(m, fabsf(row[i]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float s = __fdiv_rn(m, 127.0f);
+    if (s < 1e-8f) s = 1e-8f;
+    const float inv = __fdiv_rn(1.0f, s);
+    int8_t *out = q + (size_t)warp * ld;
+    for (int i = lane; i < ld; i += 32) {
+        int v = 0;
+        if (i < d) {
+            v = round_half_away(__fmul_rn(row[i], inv));
+            v = v > 127 ? 127 : (v < -127 ? -127 : v);
+        }
+        out[i] = (int8_t)v;
+    }
+    if (lane == 0) scale[warp] = s;
+}
+
+/* One CTA: the kept-candidate softmax of qwen7b_server.c:271-294. */
+__global__ void __launch_bounds__(NT) finish_kernel(const FinishParams f) {
+    __shared__ Misc ms;
+    const int tid = threadIdx.x;
+    if (f.phase == 0) {
+        float mx = -1e30f;
+        for (int i = tid; i < f.m; i += NT)
+            if (f.keep[i]) mx = fmaxf(mx, f.cand_val[i]);
+        const float max_l = block_max_f(mx, &ms);
+        for (int i = tid; i < f.m; i += NT)
+            f.prefix[i] = f.keep[i] ? lal_expf_glibc(__fdiv_rn(__fsub_rn(f.cand_val[i], max_l),
+                                                               f.temperature),
+                                                     f.expf_x, f.expf_y, f.expf_n)
+                                    : 0.0f;
+        __syncthreads();
+        if (tid == 0) {
+            float acc = 0.0f, bv = -1e30f;
+            int best = 0;
+            for (int i = 0; i < f.m; ++i) {
+                if (!f.keep[i]) continue;
+                acc = __fadd_rn(acc, f.prefix[i]);
+                f.prefix[i] = acc;
+                if (f.cand_val[i] > bv) {
+                    bv = f.cand_val[i];
+                    best = f.cand_idx[i];
+                }
+            }
+            f.diag->max_l = max_l;
+            f.diag->sum = acc;
+            f.diag->token = best; /* argmax fallback, used when sum <= 0 */
+        }
+    } else {
+        if (tid == 0) ms.found = 0x7fffffff;
+        __syncthreads();
+        const float r = __fmul_rn(f.u[0], f.diag->sum);
+        int first = 0x7fffffff;
+        for (int i = tid; i < f.m; i += NT)
+            if (f.keep[i] && r <= f.prefix[i]) {
+                first = i;
+                break;
+            }
+        if (first != 0x7fffffff) atomicMin(&ms.found, first);
+        __syncthreads();
+        if (tid == 0) {
+            const int tok = ms.found != 0x7fffffff ? f.cand_idx[ms.found] : f.vocab - 1;
+            f.diag->r = r;
+            f.diag->drew = 1;
+            f.diag->token = tok;
+            *f.token = tok;
+        }
+    }
+}
+
+__global__ void debug_expf_kernel(const float *x, float *y, int n, const uint32_t *tx,
+                                  const uint32_t *ty, int tn) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) y[i] = lal_expf_glibc(x[i], tx, ty, tn);
+}
+
+/* -------------------------------------------------- host planning --- */
+template <int MODE>
+void *pick_kernel(int nch) {
+    switch (nch) {
+        case 1: return (void *)tail_kernel<MODE, 1>;
+        case 2: return (void *)tail_kernel<MODE, 2>;
+        case 4: return (void *)tail_kernel<MODE, 4>;
+        case 7: return (void *)tail_kernel<MODE, 7>;
+        case 8: return (void *)tail_kernel<MODE, 8>;
+        case 16: return (void *)tail_kernel<MODE, 16>;
+        default: return nullptr;
+    }
+}
+
+int round_nch(int ld) {
+    const int need = (ld + 511) / 512;
+    const int opts[] = {1, 2, 4, 7, 8, 16};
+    for (int o : opts)
+        if (o >= need) return o;
+    return -1;
+}
+
+constexpr int kSmemLimit = 232448; /* 227 KB dynamic per block on sm_100 */
+
+int align_up(int v, int a) { return (v + a - 1) / a * a; }
+
+}  // namespace
+
+/* Fills the launch geometry and shared-memory layout of p; returns the grid
+ * size, or a negative value when the shape is unsupported. */
+int plan_launch(TailParams &p, int num_sms, int min_rows_per_cta) {
+    if (p.rows < 1) return -1;
+    int G = (p.rows + min_rows_per_cta - 1) / min_rows_per_cta;
+    G = std::min(G, std::min(num_sms, kMaxGrid));
+    G = std::max(G, 1);
+    p.rows_per_cta_max = (p.rows + G - 1) / G;
+    if (p.rows_per_cta_max > kMaxRowsPerCta) return -2;
+    p.nch = p.mode == MODE_SAMPLE ? 1 : round_nch(p.ld);
+    if (p.nch < 0) return -3;
+    const int rpc = align_up(p.rows_per_cta_max, 4);
+    int off = 0;
+    const int fixed = 16 * kMaxStages + align_up(p.ld, 16) + 3 * 4 * rpc +
+                      align_up((int)sizeof(Misc), 128) + 3 * 128;
+    const int budget = kSmemLimit - fixed;
+    const int merge_need = G * p.list_cap * 8 + 12 * std::max(2048, 4 * p.list_cap);
+    if (p.mode == MODE_SAMPLE) {
+        p.stages = 0;
+        p.rows_per_stage = 0;
+        p.stage_bytes = 0;
+        p.area_bytes = std::min(budget, merge_need);
+    } else {
+        int R = std::max(1, 32768 / p.ld);
+        if (R >= 8) R = R / 8 * 8;
+        p.rows_per_stage = R;
+        p.stage_bytes = align_up(R * p.ld, 128);
+        p.stages = std::min(kMaxStages, budget / p.stage_bytes);
+        if (p.stages < 2) return -4;
+        p.area_bytes = p.stages * p.stage_bytes;
+        if (p.mode == MODE_FUSED && p.area_bytes < merge_need)
+            p.area_bytes = std::min(budget, merge_need);
+    }
+    if (p.mode != MODE_LMHEAD && p.area_bytes < G * p.list_cap * 8 + 12 * 64) return -5;
+    off = align_up(p.area_bytes, 128);
+    p.off_bars = off;
+    off += 16 * kMaxStages;
+    p.off_xq = off;
+    off += align_up(p.ld, 16);
+    off = align_up(off, 16);
+    p.off_sw = off;
+    off += 4 * rpc;
+    p.off_lg = off;
+    off += 4 * rpc;
+    p.off_cnt = off;
+    off += 4 * rpc;
+    off = align_up(off, 128);
+    p.off_misc = off;
+    off += (int)sizeof(Misc);
+    p.smem_total = align_up(off, 128);
+    if (p.smem_total > kSmemLimit) return -6;
+    return G;
+}
+
+cudaError_t launch_tail(const TailParams &p, int grid, cudaStream_t st) {
+    void *fn = nullptr;
+    if (p.mode == MODE_FUSED) fn = pick_kernel<MODE_FUSED>(p.nch);
+    else if (p.mode == MODE_LMHEAD) fn = pick_kernel<MODE_LMHEAD>(p.nch);
+    else fn = (void *)tail_kernel<MODE_SAMPLE, 1>;
+    if (!fn) return cudaErrorInvalidValue;
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         p.smem_total);
+    if (e != cudaSuccess) return e;
+    void *args[] = {const_cast<TailParams *>(&p)};
+    return cudaLaunchKernel(fn, dim3(grid), dim3(NT), args, (size_t)p.smem_total, st);
+}
+
+cudaError_t launch_quantize_x(const float *x, int8_t *xq, float *scale, int n,
+                              cudaStream_t st) {
+    quantize_x_kernel<<<1, NT, 0, st>>>(x, xq, scale, n);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_abs_xq(const int8_t *xq, uint8_t *ax, int n, cudaStream_t st) {
+    abs_xq_kernel<<<(n + 255) / 256, 256, 0, st>>>(xq, ax, n);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_quantize_rows(const float *W, int d, int8_t *q, int ld, float *scale,
+                                 int n_rows, cudaStream_t st) {
+    const int warps_per_block = 8;
+    const int blocks = (n_rows + warps_per_block - 1) / warps_per_block;
+    quantize_rows_kernel<<<blocks, 32 * warps_per_block, 0, st>>>(W, d, q, ld, scale, n_rows);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_finish(const FinishParams &f, cudaStream_t st) {
+    finish_kernel<<<1, NT, 0, st>>>(f);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_debug_expf(const float *x, float *y, int n, const uint32_t *tx,
+                              const uint32_t *ty, int tn, cudaStream_t st) {
+    debug_expf_kernel<<<(n + 255) / 256, 256, 0, st>>>(x, y, n, tx, ty, tn);
+    return cudaGetLastError();
+}
+
+}  // namespace lal

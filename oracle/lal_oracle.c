@@ -1,0 +1,333 @@
+/*
+ * lal_oracle.c -- CPU restatement of the LAL decode tail.
+ *
+ * TEST INFRASTRUCTURE ONLY (see lal_oracle.h).  Written from the reference's
+ * behaviour, in plain scalar C, so that every arithmetic step is visible:
+ * float32 operations in the reference's order, no FMA contraction (the build
+ * passes -ffp-contract=off), glibc expf for the softmax exactly as the
+ * reference calls it.
+ */
+#include "lal_oracle.h"
+
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+
+/* ---- quantisation of the hidden vector ------------------------------------
+ * runtime/lal_q8_kernel.h:375-424.  The servers build with -march=native, so
+ * the AVX2+FMA branch is the reference: absmax over all n (order-free),
+ * scale = max/127 floored at 1e-8, inv = 1/scale; the first n&~7 elements go
+ * through _mm256_cvtps_epi32 (round to nearest even, :409) and the last n%8
+ * through a C cast (truncation, :418-423); both clamp to [-127, 127].
+ */
+static int cvt_rne(float v) {
+    /* _mm256_cvtps_epi32 on a NaN or out-of-range value yields INT_MIN. */
+    if (!(v > -2147483648.0f && v < 2147483648.0f)) return (int)0x80000000u;
+    return (int)nearbyintf(v); /* default rounding mode: nearest-even */
+}
+
+float orc_quantize_x_int8(const float *x, int8_t *xq, int n) {
+    float max_abs = 0.0f;
+    for (int i = 0; i < n; i++) {
+        float a = fabsf(x[i]);
+        if (a > max_abs) max_abs = a;
+    }
+    float scale = max_abs / 127.0f;
+    if (scale < 1e-8f) scale = 1e-8f;
+    float inv = 1.0f / scale;
+    int n8 = n & ~7;
+    for (int i = 0; i < n; i++) {
+        float s = x[i] * inv;
+        int v = (i < n8) ? cvt_rne(s) : (int)s;
+        if (v > 127) v = 127;
+        if (v < -127) v = -127;
+        xq[i] = (int8_t)v;
+    }
+    return scale;
+}
+
+/* runtime/lal_q8_kernel.h:450-460: |xq| as uint8. */
+void orc_compute_abs_xq(const int8_t *xq, uint8_t *ax, int n) {
+    for (int i = 0; i < n; i++) ax[i] = (uint8_t)(xq[i] < 0 ? -xq[i] : xq[i]);
+}
+
+/* ---- LM head ----------------------------------------------------------------
+ * runtime/lal_q8_kernel.h:463-499 (and the _abs / _abs_8row forms at
+ * :506-543 / :551-640, which produce identical values): an exact int32 dot
+ * per vocab row, then logits[v] = scale_x * scale_w[v] * (float)dot,
+ * evaluated left to right (:489).  The AVX2 sign trick equals the signed dot
+ * whenever |xq| <= 127 and |w| <= 127, which both quantizers guarantee.
+ */
+void orc_lm_head_dots(int32_t *dots, const int8_t *xq, const int8_t *wte_q,
+                      int v_start, int v_end, int n_embd) {
+    for (int v = v_start; v < v_end; v++) {
+        const int8_t *w = wte_q + (size_t)v * n_embd;
+        int32_t acc = 0;
+        for (int i = 0; i < n_embd; i++) acc += (int32_t)xq[i] * (int32_t)w[i];
+        dots[v - v_start] = acc;
+    }
+}
+
+void orc_lm_head_int8_range(float *logits, const int8_t *xq, float scale_x,
+                            const int8_t *wte_q, const float *scale_w,
+                            int v_start, int v_end, int n_embd) {
+    for (int v = v_start; v < v_end; v++) {
+        int32_t dot;
+        orc_lm_head_dots(&dot, xq, wte_q, v, v + 1, n_embd);
+        float s = scale_x * scale_w[v];
+        logits[v] = s * (float)dot;
+    }
+}
+
+/* runtime/lal_q8_kernel.h:551-640.  Rows taken in full groups of 8 from
+ * v_start (:562) sum only the first n_embd & ~31 columns -- the group body
+ * (:577-611) has no scalar tail, unlike the 1-row forms (:488, :532) and the
+ * 1-row remainder (:614-631), which sum all columns. */
+void orc_lm_head_int8_range_abs_8row(float *logits, const int8_t *xq, float scale_x,
+                                     const int8_t *wte_q, const float *scale_w,
+                                     int v_start, int v_end, int n_embd) {
+    int v = v_start;
+    const int n32 = n_embd & ~31;
+    for (; v + 8 <= v_end; v += 8)
+        for (int r = 0; r < 8; r++) {
+            const int8_t *w = wte_q + (size_t)(v + r) * n_embd;
+            int32_t dot = 0;
+            for (int i = 0; i < n32; i++) dot += (int32_t)xq[i] * (int32_t)w[i];
+            float s = scale_x * scale_w[v + r];
+            logits[v + r] = s * (float)dot;
+        }
+    orc_lm_head_int8_range(logits, xq, scale_x, wte_q, scale_w, v, v_end, n_embd);
+}
+
+/* ---- per-row weight quantisation ------------------------------------------
+ * runtime/lal_q8_kernel.h:357-372: scale = max|row|/127 floored at 1e-8,
+ * q = clamp(lroundf(w * (1/scale)), +-127) -- round half AWAY from zero.
+ */
+void orc_quantize_q8_rows(const float *W, int8_t *q8_T, float *scale,
+                          int in_dim, int n_rows) {
+    for (int j = 0; j < n_rows; j++) {
+        const float *row = W + (size_t)j * in_dim;
+        float mx = 0.0f;
+        for (int i = 0; i < in_dim; i++) {
+            float a = fabsf(row[i]);
+            if (a > mx) mx = a;
+        }
+        float s = mx / 127.0f;
+        if (s < 1e-8f) s = 1e-8f;
+        scale[j] = s;
+        float inv = 1.0f / s;
+        for (int i = 0; i < in_dim; i++) {
+            long q = lroundf(row[i] * inv);
+            if (q > 127) q = 127;
+            if (q < -127) q = -127;
+            q8_T[(size_t)j * in_dim + i] = (int8_t)q;
+        }
+    }
+}
+
+void orc_quantize_q8_per_row(const float *W, int8_t *q8_T, float *scale,
+                             int in_dim, int out_dim) {
+    orc_quantize_q8_rows(W, q8_T, scale, in_dim, out_dim);
+}
+
+/* ---- sampling ---------------------------------------------------------------*/
+
+/* Repetition penalty, runtime/lal_sampling.h:59-67 (and the identical loop at
+ * tools/server/qwen7b_server.c:223-230): once per occurrence, in order. */
+static void apply_penalty(float *logits, int vocab_size, float rep_penalty,
+                          const int *recent, int n_recent) {
+    if (!(rep_penalty > 1.0f) || !recent || n_recent <= 0) return;
+    for (int i = 0; i < n_recent; i++) {
+        int t = recent[i];
+        if (t < 0 || t >= vocab_size) continue;
+        if (logits[t] > 0) logits[t] /= rep_penalty;
+        else logits[t] *= rep_penalty;
+    }
+}
+
+/* Greedy argmax with strict '>' (lowest index wins ties):
+ * runtime/lal_sampling.h:51-56. */
+static int argmax_first(const float *logits, int vocab_size) {
+    int best = 0;
+    for (int v = 1; v < vocab_size; v++)
+        if (logits[v] > logits[best]) best = v;
+    return best;
+}
+
+/* Top-k threshold by a min-heap of capacity k (runtime/lal_sampling.h:70-104,
+ * tools/server/qwen7b_server.c:237-256).  The heap takes the first k values,
+ * then replaces its root only on a STRICTLY larger value; its final root is
+ * the k-th largest value counted with multiplicity.  The capacity here is k
+ * itself, so k larger than the reference's static 64 / 512 is defined. */
+static float heap_threshold(const float *logits, int vocab_size, int k) {
+    float *h = (float *)malloc(sizeof(float) * (size_t)k);
+    int hn = 0;
+    for (int v = 0; v < vocab_size; v++) {
+        float val = logits[v];
+        if (hn < k) {
+            int c = hn++;
+            h[c] = val;
+            while (c > 0) {               /* sift up */
+                int p = (c - 1) / 2;
+                if (h[p] <= h[c]) break;
+                float t = h[p]; h[p] = h[c]; h[c] = t;
+                c = p;
+            }
+        } else if (val > h[0]) {
+            h[0] = val;
+            int p = 0;
+            for (;;) {                    /* sift down */
+                int l = 2 * p + 1, r = l + 1, s = p;
+                if (l < hn && h[l] < h[s]) s = l;
+                if (r < hn && h[r] < h[s]) s = r;
+                if (s == p) break;
+                float t = h[p]; h[p] = h[s]; h[s] = t;
+                p = s;
+            }
+        }
+    }
+    float th = h[0];
+    free(h);
+    return th;
+}
+
+int orc_sample_token(float *logits, int vocab_size, float temperature,
+                     int top_k, float rep_penalty, const int *recent,
+                     int n_recent, float u, orc_sample_info *info) {
+    orc_sample_info tmp;
+    if (!info) info = &tmp;
+    memset(info, 0, sizeof(*info));
+    /* lal_sampling.h:51-56: greedy BEFORE the penalty in the library form. */
+    if (temperature <= 0.0f || top_k <= 0) {
+        info->greedy = 1;
+        return argmax_first(logits, vocab_size);
+    }
+    apply_penalty(logits, vocab_size, rep_penalty, recent, n_recent);
+    int k = top_k;
+    if (k > vocab_size) k = vocab_size;                   /* :70-71 */
+    float threshold = heap_threshold(logits, vocab_size, k);
+    float max_l = -1e30f;                                 /* :107-109 */
+    int n_cand = 0;
+    for (int v = 0; v < vocab_size; v++)
+        if (logits[v] >= threshold) {
+            n_cand++;
+            if (logits[v] > max_l) max_l = logits[v];
+        }
+    float sum = 0;                                        /* :110-113 */
+    for (int v = 0; v < vocab_size; v++)
+        if (logits[v] >= threshold) sum += expf((logits[v] - max_l) / temperature);
+    float r = u * sum;                                    /* :116 */
+    info->threshold = threshold; info->max_l = max_l; info->sum = sum;
+    info->r = r; info->n_cand = n_cand; info->drew = 1;
+    float acc = 0;                                        /* :117-123 */
+    for (int v = 0; v < vocab_size; v++) {
+        if (logits[v] >= threshold) {
+            acc += expf((logits[v] - max_l) / temperature);
+            if (r <= acc) return v;
+        }
+    }
+    return vocab_size - 1;                                /* :124 */
+}
+
+int orc_sample_token_filtered(float *logits, int vocab_size, float temperature,
+                              int top_k, float rep_penalty, const int *recent,
+                              int n_recent, orc_filter_fn filter,
+                              orc_decode_fn decode, orc_draw_fn draw,
+                              void *draw_ctx, orc_sample_info *info) {
+    orc_sample_info tmp;
+    if (!info) info = &tmp;
+    memset(info, 0, sizeof(*info));
+    /* qwen7b_server.c:223-230: penalty first, then the greedy check :231-234 */
+    apply_penalty(logits, vocab_size, rep_penalty, recent, n_recent);
+    if (temperature <= 0.0f || top_k <= 0) {
+        info->greedy = 1;
+        return argmax_first(logits, vocab_size);
+    }
+    int k = top_k;                                        /* :236 */
+    if (k < 1) k = 1;
+    if (k > vocab_size) k = vocab_size;
+    float threshold = heap_threshold(logits, vocab_size, k);
+    /* :258-270: keep_mask = candidates, optional filter, restore if empty */
+    int *keep = (int *)malloc(sizeof(int) * (size_t)vocab_size);
+    for (int v = 0; v < vocab_size; v++) keep[v] = (logits[v] >= threshold) ? 1 : 0;
+    if (filter) {
+        int last = (n_recent > 0) ? recent[n_recent - 1] : -1;
+        (void)filter(keep, vocab_size, last, recent, n_recent, decode);
+    }
+    int any = 0;
+    for (int v = 0; v < vocab_size; v++) if (keep[v]) { any = 1; break; }
+    if (!any)
+        for (int v = 0; v < vocab_size; v++) if (logits[v] >= threshold) keep[v] = 1;
+    /* :275-284: max then sum over kept & >= threshold */
+    float max_l = -1e30f, sum = 0;
+    int n_cand = 0;
+    for (int v = 0; v < vocab_size; v++)
+        if (keep[v] && logits[v] >= threshold) {
+            n_cand++;
+            if (logits[v] > max_l) max_l = logits[v];
+        }
+    for (int v = 0; v < vocab_size; v++)
+        if (keep[v] && logits[v] >= threshold)
+            sum += expf((logits[v] - max_l) / temperature);
+    info->threshold = threshold; info->max_l = max_l; info->sum = sum;
+    info->n_cand = n_cand;
+    int tok;
+    if (sum <= 0) {                                        /* :285-286 */
+        int best = 0; float bv = -1e30f;
+        for (int v = 0; v < vocab_size; v++)
+            if (keep[v] && logits[v] > bv) { bv = logits[v]; best = v; }
+        tok = best;
+    } else {
+        float u = draw ? draw(draw_ctx) : 0.0f;            /* :287 */
+        float r = u * sum, acc = 0;
+        info->r = r; info->drew = 1;
+        tok = vocab_size - 1;                              /* :294 */
+        for (int v = 0; v < vocab_size; v++) {
+            if (keep[v] && logits[v] >= threshold) {
+                acc += expf((logits[v] - max_l) / temperature);
+                if (r <= acc) { tok = v; break; }
+            }
+        }
+    }
+    free(keep);
+    return tok;
+}
+
+/* runtime/lal_sampling.h:133-136 (FIFO by memmove), capacity cap. */
+void orc_recent_push(int *tokens, int *n, int cap, int tok) {
+    if (*n < cap) { tokens[(*n)++] = tok; return; }
+    memmove(tokens, tokens + 1, (size_t)(cap - 1) * sizeof(int));
+    tokens[cap - 1] = tok;
+}
+
+/* glibc expf over an array: the softmax weight function of
+ * runtime/lal_sampling.h:112,120, for checking the device's weights. */
+void orc_expf_batch(const float *x, float *y, long n) {
+    for (long i = 0; i < n; i++) y[i] = expf(x[i]);
+}
+
+static float fixed_draw(void *ctx) { return *(const float *)ctx; }
+
+int orc_tail_step(const float *hidden, int n_embd, const int8_t *wte_q,
+                  const float *scale_w, int vocab_size, float temperature,
+                  int top_k, float rep_penalty, int *recent, int *n_recent,
+                  int hist_cap, float u, int variant, float *logits_out,
+                  orc_sample_info *info) {
+    int8_t *xq = (int8_t *)malloc((size_t)n_embd);
+    float *logits = logits_out ? logits_out
+                               : (float *)malloc(sizeof(float) * (size_t)vocab_size);
+    float sx = orc_quantize_x_int8(hidden, xq, n_embd);
+    orc_lm_head_int8_range(logits, xq, sx, wte_q, scale_w, 0, vocab_size, n_embd);
+    int tok;
+    if (variant == 0)
+        tok = orc_sample_token(logits, vocab_size, temperature, top_k, rep_penalty,
+                               recent, *n_recent, u, info);
+    else
+        tok = orc_sample_token_filtered(logits, vocab_size, temperature, top_k,
+                                        rep_penalty, recent, *n_recent, NULL, NULL,
+                                        fixed_draw, &u, info);
+    orc_recent_push(recent, n_recent, hist_cap, tok);
+    free(xq);
+    if (!logits_out) free(logits);
+    return tok;
+}
