@@ -1,0 +1,399 @@
+"""Benchmark of the LAL decode tail on B200 -- prints ONE JSON line (rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2_qwen]
+    python bench.py --impl reference ...
+
+A step is one decode-tail pass (quantize hidden, int8 LM head over all vocab
+rows, repetition penalty, top-k, temperature softmax, draw, history push) for
+the B streams of the config, on seeded synthetic inputs with the BASELINE
+shapes (no real weights exist for this path).  Default workload: c2_qwen, the
+Qwen2.5-7B-shaped tail at B=1 (V=152064, d=3584, 545 MB int8 LM head).
+
+Reported:
+  value      tokens/s with the step's inputs already in HBM (CUDA events on the
+             context's stream around the K timed steps)
+  e2e        tokens/s through the public C ABI (lal_tail_step) from host
+             buffers: H2D of hidden + draws and D2H of tokens + status inside
+             the timed region, host wall clock per call
+  roofline   the fused kernel's algorithmic bytes per launch / its average
+             duration (CUDA events per launch), against MEASURED_PEAKS.json
+  cpu_baseline  the reference's own C (oracle/_ref: quantize, |xq|, OpenMP
+             LM head, lal_sample_token) on the host's cores, bounded sample
+
+Multi-GPU (torchrun, --gpus N): each rank owns a contiguous vocab slice
+(vocab-sharded, strong scaling: a step is the same B tokens at any N).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+from lal_b200 import synth  # noqa: E402
+
+METRIC = "Qwen7B LM-head+top-k tail tokens/s at B=1/64, % HBM BW peak, 1/2/4/8 B200"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--config", default="c2_qwen", choices=sorted(synth.CONFIGS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=12.0,
+                    help="bound of the CPU-baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def algorithmic_bytes(cfg, B, rows=None):
+    """Per step: int8 W + fp32 row scales (this slice) + per stream fp32 hidden,
+    int32 history and the int32 token (logits stay on chip / in L2)."""
+    V = cfg.vocab if rows is None else rows
+    return V * cfg.n_embd + 4 * V + B * (4 * cfg.n_embd + 4 * cfg.hist + 4)
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d, "measured"
+    return FALLBACK_PEAKS, "fallback"
+
+
+def load_traffic(cfg_name, n_gpus):
+    """dram read+write bytes per launch of the fused kernel from the committed
+    ncu summary (profiles/traffic.json), or None."""
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    if not os.path.exists(p):
+        return None
+    with open(p) as f:
+        d = json.load(f)
+    return d.get(f"{cfg_name}@{n_gpus}")
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.out = ""
+        if self.proc:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out = ""
+
+    def summary(self):
+        rows = []
+        for line in (self.out or "").splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                rows.append(dict(sm=float(f[1]), max=float(f[2]), hw=f[5], hwt=f[6], swt=f[7],
+                                 pcap=f[8]))
+            except ValueError:
+                continue
+        if not rows:
+            return None
+        reasons = set()
+        for r in rows:
+            for k, name in (("hw", "hw_slowdown"), ("hwt", "hw_thermal_slowdown"),
+                            ("swt", "sw_thermal_slowdown"), ("pcap", "sw_power_cap")):
+                if r[k].lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(r["sm"] for r in rows),
+                "sm_max_mhz": max(r["max"] for r in rows), "reasons": sorted(reasons),
+                "samples": len(rows)}
+
+
+# ---------------------------------------------------------------- CPU arm ---
+
+def quantized_lm_head_host(cfg, rows=None):
+    """int8 LM head + scales on the host, quantized by the reference's own
+    lal_quantize_q8_per_row (oracle/_ref) when built, else the restatement."""
+    import oracle
+    V = cfg.vocab
+    q = np.empty((V, cfg.n_embd), np.int8)
+    s = np.empty(V, np.float32)
+    which = "ref" if oracle.have_ref() else "port"
+    step = 8192
+    for r0 in range(0, V, step):
+        r1 = min(V, r0 + step)
+        q[r0:r1], s[r0:r1] = oracle.quantize_rows(synth.lm_head_f32(cfg, r0, r1), which)
+    return q, s
+
+
+def cpu_tail(cfg, q, s, steps, threads, seconds):
+    """Time the reference's decode tail (qwen7b_server.c:829-850) on the host:
+    oracle/_ref when built ('reference'), else the C restatement ('port').
+    Runs at most `steps` steps or `seconds` of work per stream.  Returns
+    (tokens/s, kind, steps done, cores)."""
+    import ctypes as C
+
+    import oracle
+    B = cfg.streams
+    V, d = cfg.vocab, cfg.n_embd
+    # lal_sample_token's heap holds 64 (lal_sampling.h:74): larger k runs on
+    # the uncapped restatement
+    kind = "reference" if oracle.have_ref() and min(cfg.top_k, V) <= 64 else "port"
+    temps = synth.temperatures(cfg)
+    draws = synth.Draws(cfg)
+    cap = max(1, cfg.hist)
+    pad = max(32, -(-d // 32) * 32)
+    xq = np.zeros(pad, np.int8)
+    ax = np.zeros(pad, np.uint8)
+    logits = np.zeros(V, np.float32)
+    hists, loops = [], []
+    for b in range(B):
+        h0 = synth.history(cfg, b)
+        rec = np.zeros(cap, np.int32)
+        rec[:h0.size] = h0
+        hists.append((rec, C.c_int(h0.size)))
+        if kind == "port":
+            loops.append(oracle.PortLoop(q, s, h0, cap, float(temps[b]), cfg.top_k,
+                                         cfg.rep_penalty, 0))
+    if kind == "reference":
+        R = oracle.ref()
+        if cfg.draws == "rand":
+            R.ref_srand(cfg.seed)
+    done = 0
+    t_tot = 0.0
+    for step in range(steps):
+        hid = synth.hidden(cfg, step)
+        t0 = time.perf_counter()
+        for b in range(B):
+            if kind == "reference":
+                rec, n = hists[b]
+                R.ref_tail_step(hid[b], xq, ax, logits, q.reshape(-1), s, V, d,
+                                np.float32(temps[b]), cfg.top_k, np.float32(cfg.rep_penalty),
+                                rec, C.byref(n), cap, threads, 0)
+            else:
+                loops[b].step(hid[b], draws.u(b))
+        t_tot += time.perf_counter() - t0
+        done += 1
+        if t_tot > seconds:
+            break
+    return B * done / t_tot, kind, done, threads
+
+
+def run_reference_arm(args, cfg):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    q, s = quantized_lm_head_host(cfg)
+    # warm-up, then the timed steps (each a full step of the workload; bounded
+    # by --cpu-seconds of host time)
+    cpu_tail(cfg, q, s, max(1, min(args.warmup, 2)), threads, 5.0)
+    val, kind, done, cores = cpu_tail(cfg, q, s, args.steps, threads, args.cpu_seconds * 2)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(val, 3), "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": done, "warmup": args.warmup,
+        "ms_per_step": round(1000.0 * cfg.streams / val, 4), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "config": workload(cfg, args.gpus),
+        "cpu_baseline": {"value": round(val, 3), "unit": "tokens/s", "cores": cores,
+                         "kind": kind,
+                         "sample": f"{done} full decode-tail steps of {cfg.name} "
+                                   f"(reference tail sequence of qwen7b_server.c:829-850)"},
+        "e2e": {"value": round(val, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def workload(cfg, n):
+    return {"workload": f"{cfg.name}: V={cfg.vocab} d={cfg.n_embd} B={cfg.streams} "
+                        f"top_k={cfg.top_k} H={cfg.hist} p={cfg.rep_penalty}",
+            "vocab": cfg.vocab, "n_embd": cfg.n_embd, "streams": cfg.streams,
+            "top_k": cfg.top_k, "history": cfg.hist, "parallelism": f"vocab-sharded x{n}",
+            "l2": "LM head (545 MB) streamed each step is larger than L2 (126 MB)"
+            if n == 1 else "L2 flushed between timed steps (256 MB write)"}
+
+
+# ---------------------------------------------------------------- GPU arm ---
+
+def run_ours(args, cfg):
+    import torch
+
+    import lal_b200 as L
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    B = cfg.streams
+    K, W = args.steps, args.warmup
+    t = L.DecodeTail(cfg.vocab, cfg.n_embd, max_streams=B, max_top_k=max(cfg.top_k, 1),
+                     history_cap=cfg.hist, sampler=L.LAL_SAMPLER_LIBRARY, device=local,
+                     shard_rank=rank, shard_count=world)
+    if world > 1:
+        t.connect(dist)
+    # LM head slice: fp32 rows generated in blocks, quantized on the GPU
+    blk = 8192
+    for r in range(0, t.n_rows, blk):
+        n = min(blk, t.n_rows - r)
+        t.load_lm_head_f32(synth.lm_head_f32(cfg, t.row0 + r, t.row0 + r + n), r)
+    temps = synth.temperatures(cfg)
+    t.set_sampling(temps, [cfg.top_k] * B, [cfg.rep_penalty] * B)
+    for b in range(B):
+        t.set_history(b, synth.history(cfg, b))
+    draws = synth.Draws(cfg)
+    nsteps = W + 2 * K
+    hid = np.stack([synth.hidden(cfg, i) for i in range(nsteps)]).astype(np.float32)
+    us = np.array([[draws.u(b) for b in range(B)] for _ in range(nsteps)], np.float32)
+
+    stream = torch.cuda.ExternalStream(t.stream(), device=local)
+    flush = torch.empty(64 << 20, dtype=torch.float32, device=local) if world > 1 else None
+
+    def barrier():
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+
+    # warm-up through the public call
+    for i in range(W):
+        t.step(hid[i], us[i])
+
+    # ---- value: inputs resident in HBM, device-timed ----
+    d_hid = torch.from_numpy(hid[W:W + K]).to(local)
+    d_u = torch.from_numpy(us[W:W + K]).to(local)
+    d_tok = torch.empty((K, B), dtype=torch.int32, device=local)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(K)]
+    t.set_timing(True)
+    barrier()
+    with ClockSampler(local) as clk:
+        for i in range(K):
+            if flush is not None:
+                flush.zero_()       # evict the slice from L2 (not timed)
+                torch.cuda.current_stream().synchronize()
+            ev[i][0].record(stream)
+            t.step_device(d_hid[i].data_ptr(), B, d_u[i].data_ptr(), d_tok[i].data_ptr())
+            ev[i][1].record(stream)
+        t.sync()
+        barrier()
+    if flush is None:   # back-to-back steps: one bracket around all K
+        dev_ms = ev[0][0].elapsed_time(ev[-1][1])
+    else:               # L2 flushed between steps: sum the steps
+        dev_ms = sum(a.elapsed_time(b) for a, b in ev)
+    kern_ms, n_launch = t.kernel_time()
+    t.set_timing(False)
+
+    # ---- e2e: host buffers through lal_tail_step ----
+    barrier()
+    e2e_s = 0.0
+    for i in range(K):
+        if flush is not None:
+            flush.zero_()
+            torch.cuda.synchronize()
+        h = hid[W + K + i]
+        u = us[W + K + i]
+        t0 = time.perf_counter()
+        t.step(h, u)
+        e2e_s += time.perf_counter() - t0
+    barrier()
+
+    # max over ranks
+    vals = torch.tensor([dev_ms, e2e_s * 1000.0, kern_ms], dtype=torch.float64, device=local)
+    if dist is not None:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    dev_ms, e2e_ms, kern_ms = vals.tolist()
+
+    out = None
+    if rank == 0:
+        peaks, pk_kind = load_peaks()
+        rows = t.n_rows
+        alg = algorithmic_bytes(cfg, B, rows)
+        launches_per_step = B
+        achieved = alg / launches_per_step / (kern_ms * 1e-3) / 1e9
+        peak = float(peaks["hbm_gbs"])
+        traffic = load_traffic(cfg.name, world)
+        tokens = K * B
+        out = {
+            "metric": METRIC, "value": round(tokens / (dev_ms * 1e-3), 3), "unit": "tokens/s",
+            "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": round(dev_ms / K, 5),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "int8", "data": "synthetic", "config": workload(cfg, world),
+            "e2e": {"value": round(tokens / (e2e_ms * 1e-3), 3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": int(hid[0].nbytes + us[0].nbytes),
+                    "d2h_bytes_per_step": int(4 * B + 4)},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1),
+                         "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "traffic": traffic,
+                         "note": f"fused kernel; {alg} algorithmic bytes per step on rank 0's "
+                                 f"slice ({rows} rows); peak {pk_kind}"},
+            "gpu_launches": int(K * launches_per_step),
+            "kernel_ms": round(kern_ms / launches_per_step * launches_per_step, 5),
+            "clocks": clk.summary(),
+        }
+    # ---- CPU baseline (rank 0, N=1 only) ----
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        q, s = t.read_lm_head()
+        val, kind, done, cores = cpu_tail(cfg, q, s, 10_000, os.cpu_count() or 1,
+                                          args.cpu_seconds)
+        out["cpu_baseline"] = {"value": round(val, 3), "unit": "tokens/s", "cores": cores,
+                               "kind": kind,
+                               "sample": f"{done} decode-tail steps of {cfg.name} "
+                                         f"(~{args.cpu_seconds:.0f} s bound)"}
+    if out is not None:
+        print(json.dumps(out), flush=True)
+    t.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    cfg = synth.CONFIGS[args.config]
+    if args.impl == "reference":
+        run_reference_arm(args, cfg)
+    else:
+        run_ours(args, cfg)
+
+
+if __name__ == "__main__":
+    main()

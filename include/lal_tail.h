@@ -181,6 +181,9 @@ int lal_tail_get_logits(lal_tail *t, int stream, float *logits_rows);
 /* Device buffers of the context, for callers that keep inputs on the GPU. */
 int lal_tail_device_buffers(lal_tail *t, float **d_hidden, float **d_u,
                             int **d_tokens);
+/* The context's CUDA stream (a cudaStream_t), for callers that order their
+ * own work or timing events with the tail's launches. */
+int lal_tail_get_stream(lal_tail *t, void **stream);
 /* Turn on (1) or off (0) CUDA-event timing of each fused-kernel launch. */
 int lal_tail_set_timing(lal_tail *t, int on);
 /* Average duration in milliseconds of the fused kernel over the launches

@@ -114,6 +114,7 @@ SIGNATURES = {
     "lal_tail_get_diag": (C.c_int, [_vp, _ip, C.POINTER(TailDiag)]),
     "lal_tail_get_logits": (C.c_int, [_vp, _ip, _f32p]),
     "lal_tail_device_buffers": (C.c_int, [_vp, C.POINTER(_vp), C.POINTER(_vp), C.POINTER(_vp)]),
+    "lal_tail_get_stream": (C.c_int, [_vp, C.POINTER(_vp)]),
     "lal_tail_set_timing": (C.c_int, [_vp, _ip]),
     "lal_tail_kernel_time": (C.c_int, [_vp, C.POINTER(C.c_double), C.POINTER(C.c_int)]),
     "lal_tail_debug_expf": (C.c_int, [_f32p, _f32p, _ip]),
@@ -316,6 +317,11 @@ class DecodeTail:
         a, b, c = C.c_void_p(), C.c_void_p(), C.c_void_p()
         _check(lib().lal_tail_device_buffers(self.h, C.byref(a), C.byref(b), C.byref(c)))
         return a.value, b.value, c.value
+
+    def stream(self) -> int:
+        s = C.c_void_p()
+        _check(lib().lal_tail_get_stream(self.h, C.byref(s)))
+        return s.value or 0
 
     def step_device(self, d_hidden: int, n_streams: int, d_u: int, d_tokens: int):
         _check(lib().lal_tail_step_device(self.h, d_hidden, n_streams, d_u, d_tokens))

@@ -1000,6 +1000,12 @@ int lal_tail_device_buffers(lal_tail *t, float **d_hidden, float **d_u, int **d_
     return LAL_TAIL_OK;
 }
 
+int lal_tail_get_stream(lal_tail *t, void **stream) {
+    if (!t || !stream) return fail(LAL_TAIL_ERR_ARG, "get_stream: null argument");
+    *stream = (void *)t->stream;
+    return LAL_TAIL_OK;
+}
+
 int lal_tail_step_device(lal_tail *t, const float *d_hidden, int n_streams, const float *d_u,
                          int *d_tokens_out) {
     CHECK(ctx_check(t));

@@ -174,8 +174,10 @@ __device__ __forceinline__ float block_max_f(float v, Misc *ms) {
     return r;
 }
 
-/* k-th largest key (1 <= k <= n) of get(0..n-1): MSB-first radix select with
- * 8-bit digits; histogram adds are aggregated per warp (match.any). */
+/* k-th largest key of the valid entries among i in [0, n): get(i, key)
+ * returns whether entry i takes part and sets its key; 1 <= k <= the number
+ * of valid entries.  MSB-first radix select with 8-bit digits; histogram adds
+ * are aggregated per warp (match.any). */
 template <class Get>
 __device__ uint32_t block_kth_largest(Get get, int n, int k, Misc *ms) {
     uint32_t prefix = 0, mask = 0;
@@ -185,8 +187,8 @@ __device__ uint32_t block_kth_largest(Get get, int n, int k, Misc *ms) {
         __syncthreads();
         for (int i0 = 0; i0 < n; i0 += NT) {
             const int i = i0 + threadIdx.x;
-            const bool act = i < n;
-            const uint32_t key = act ? get(i) : 0u;
+            uint32_t key = 0u;
+            const bool act = i < n && get(i, key);
             const bool m = act && ((key & mask) == prefix);
             const uint32_t digit = (key >> shift) & 0xFFu;
             const unsigned voters = __ballot_sync(0xffffffffu, m);
@@ -442,7 +444,12 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
     const bool tie_complete = !greedy;
     {
         const int kloc = min(k, nloc);
-        const uint32_t T = block_kth_largest([&](int i) { return f2key(lg_s[i]); }, nloc, kloc, ms);
+        const uint32_t T = block_kth_largest(
+            [&](int i, uint32_t &key) {
+                key = f2key(lg_s[i]);
+                return true;
+            },
+            nloc, kloc, ms);
         const int seg = (nloc + NT - 1) / NT;
         const int i0 = min(nloc, tid * seg), i1 = min(nloc, i0 + seg);
         uint32_t ngt = 0, neq = 0;
@@ -495,11 +502,17 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
     if (ms->ticket != G - 1) return;
     __threadfence();
 
-    /* merge buffers reuse the stage area */
+    /* Merge buffers reuse the stage area.  When every list fits in shared
+     * memory (with room left for candidates) the entries >= L are staged
+     * there first; otherwise (large k) the select and the compaction read the
+     * lists straight from global memory. */
+    const int Fn = G * p.list_cap;
+    const bool staged = (long long)Fn * 8 + 12ll * 4 * p.list_cap <= (long long)p.area_bytes;
+    const size_t b_bytes = staged ? (size_t)Fn * 8 : 0;
     uint32_t *Bk = reinterpret_cast<uint32_t *>(smem);
-    int *Bi = reinterpret_cast<int *>(smem + (size_t)G * p.list_cap * 4);
-    const int cand_cap = (int)((p.area_bytes - (long long)G * p.list_cap * 8) / 12);
-    float *Cv = reinterpret_cast<float *>(smem + (size_t)G * p.list_cap * 8);
+    int *Bi = reinterpret_cast<int *>(smem + (size_t)Fn * 4);
+    const int cand_cap = (int)((p.area_bytes - (long long)b_bytes) / 12);
+    float *Cv = reinterpret_cast<float *>(smem + b_bytes);
     int *Ci = reinterpret_cast<int *>(Cv + cand_cap);
     float *Ce = reinterpret_cast<float *>(Ci + cand_cap);
 
@@ -517,35 +530,40 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
     __syncthreads();
     const uint32_t L = ms->sh[4];
 
-    /* gather list entries >= L, preserving (CTA, position) = vocab order */
-    const int Fn = G * p.list_cap;
+    /* list entry e = (CTA g, position j); (g, j) order is vocab order */
+    auto list_entry = [&](int e, uint32_t &key) {
+        const int g = e / p.list_cap, j = e - g * p.list_cap;
+        if (j >= ms->nout[g]) return false;
+        key = __ldcg(p.rec_keys + e);
+        return key >= L;
+    };
+    /* gather list entries >= L (staged) or count them (global) */
     {
         const int seg = (Fn + NT - 1) / NT;
         const int e0 = min(Fn, tid * seg), e1 = min(Fn, e0 + seg);
-        uint32_t cnt = 0;
-        for (int e = e0; e < e1; ++e) {
-            const int g = e / p.list_cap, j = e - g * p.list_cap;
-            if (j < ms->nout[g] && __ldcg(p.rec_keys + e) >= L) ++cnt;
-        }
-        uint32_t M;
-        uint32_t pos = block_scan_excl(cnt, ms, &M);
-        for (int e = e0; e < e1; ++e) {
-            const int g = e / p.list_cap, j = e - g * p.list_cap;
-            if (j < ms->nout[g]) {
-                const uint32_t key = __ldcg(p.rec_keys + e);
-                if (key >= L) {
+        uint32_t cnt = 0, key;
+        for (int e = e0; e < e1; ++e) cnt += list_entry(e, key) ? 1u : 0u;
+        uint32_t Mt;
+        uint32_t pos = block_scan_excl(cnt, ms, &Mt);
+        if (staged)
+            for (int e = e0; e < e1; ++e)
+                if (list_entry(e, key)) {
                     Bk[pos] = key;
                     Bi[pos] = __ldcg(p.rec_idx + e);
                     ++pos;
                 }
-            }
-        }
-        if (tid == 0) ms->sh[5] = M;
+        if (tid == 0) ms->sh[5] = Mt;
     }
     __syncthreads();
     const int M = (int)ms->sh[5];
     const int kk = min(k, M);
-    const uint32_t T = block_kth_largest([&](int i) { return Bk[i]; }, M, kk, ms);
+    const uint32_t T = staged ? block_kth_largest(
+                                    [&](int i, uint32_t &key) {
+                                        key = Bk[i];
+                                        return true;
+                                    },
+                                    M, kk, ms)
+                              : block_kth_largest(list_entry, Fn, kk, ms);
 
     /* A list whose ties at its cut did not fit is only a problem when that
      * cut is a candidate value. */
@@ -557,26 +575,32 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
     __syncthreads();
     const bool overflow = ms->found != 0;
 
-    /* candidates {v : l[v] >= T} in ascending vocab order */
+    /* candidates {v : l[v] >= T} in ascending vocab order (Bk/Bi and Cv/Ci
+     * do not overlap) */
     int m;
     {
-        const int seg = (M + NT - 1) / NT;
-        const int e0 = min(M, tid * seg), e1 = min(M, e0 + seg);
-        uint32_t cnt = 0;
-        for (int e = e0; e < e1; ++e) cnt += Bk[e] >= T;
+        const int n_src = staged ? M : Fn;
+        const int seg = (n_src + NT - 1) / NT;
+        const int e0 = min(n_src, tid * seg), e1 = min(n_src, e0 + seg);
+        uint32_t cnt = 0, key;
+        for (int e = e0; e < e1; ++e) {
+            if (staged) key = Bk[e];
+            else if (!list_entry(e, key)) continue;
+            cnt += key >= T;
+        }
         uint32_t mt;
         uint32_t pos = block_scan_excl(cnt, ms, &mt);
         m = (int)mt;
-        if (m <= cand_cap) {
-            /* Bk/Bi and Cv/Ci do not overlap; read all before writing is not
-             * needed. */
-            for (int e = e0; e < e1; ++e)
-                if (Bk[e] >= T) {
-                    Cv[pos] = key2f(Bk[e]);
-                    Ci[pos] = Bi[e];
+        if (m <= cand_cap)
+            for (int e = e0; e < e1; ++e) {
+                if (staged) key = Bk[e];
+                else if (!list_entry(e, key)) continue;
+                if (key >= T) {
+                    Cv[pos] = key2f(key);
+                    Ci[pos] = staged ? Bi[e] : __ldcg(p.rec_idx + e);
                     ++pos;
                 }
-        }
+            }
     }
     __syncthreads();
 
@@ -884,7 +908,9 @@ int plan_launch(TailParams &p, int num_sms, int min_rows_per_cta) {
         if (p.mode == MODE_FUSED && p.area_bytes < merge_need)
             p.area_bytes = std::min(budget, merge_need);
     }
-    if (p.mode != MODE_LMHEAD && p.area_bytes < G * p.list_cap * 8 + 12 * 64) return -5;
+    /* the merge needs room for at least the k candidates plus ties; staging
+     * the lists in shared memory is optional (see the kernel's merge) */
+    if (p.mode != MODE_LMHEAD && p.area_bytes < 12 * (p.list_cap + 64)) return -5;
     off = align_up(p.area_bytes, 128);
     p.off_bars = off;
     off += 16 * kMaxStages;
