@@ -125,9 +125,9 @@ def test_stress_k1024_with_duplicate_rows():
         t.set_history(0, hist0)
         port = oracle.PortLoop(q, s, hist0, cfg.hist, cfg.temperature, cfg.top_k,
                                cfg.rep_penalty, variant)
-        draws = synth.Draws(cfg)
+        draws = synth.Draws(cfg, 1)
         for step in range(cfg.steps):
-            h = synth.hidden(cfg, step)
+            h = synth.hidden(cfg, step, 1)
             u = draws.u(0)
             tok = int(t.step(h, np.array([u], np.float32))[0])
             ptok, info = port.step(h[0], u)
