@@ -191,6 +191,14 @@ int lal_tail_set_timing(lal_tail *t, int on);
  * count. */
 int lal_tail_kernel_time(lal_tail *t, double *avg_ms, int *n_launches);
 
+/* Phase timing of the fused kernel (inspection hook).  When on, every launch
+ * writes globaltimer stamps (ns): per CTA c, out[c*8 + 0..3] = start,
+ * prologue done, rows done, candidate list written; for the merge,
+ * out[grid*8 + 0..3] = merge start, threshold found, candidates gathered,
+ * token written.  read copies the last launch's (grid+1)*8 stamps. */
+int lal_tail_debug_phases(lal_tail *t, int on);
+int lal_tail_debug_phase_read(lal_tail *t, unsigned long long *out, int cap, int *grid);
+
 /* Glibc-exact expf as the device computes it (test hook). */
 int lal_tail_debug_expf(const float *x, float *y, int n);
 

@@ -118,6 +118,8 @@ SIGNATURES = {
     "lal_tail_set_timing": (C.c_int, [_vp, _ip]),
     "lal_tail_kernel_time": (C.c_int, [_vp, C.POINTER(C.c_double), C.POINTER(C.c_int)]),
     "lal_tail_debug_expf": (C.c_int, [_f32p, _f32p, _ip]),
+    "lal_tail_debug_phases": (C.c_int, [_vp, _ip]),
+    "lal_tail_debug_phase_read": (C.c_int, [_vp, _vp, _ip, C.POINTER(C.c_int)]),
 }
 
 _lib = None
@@ -317,6 +319,20 @@ class DecodeTail:
         a, b, c = C.c_void_p(), C.c_void_p(), C.c_void_p()
         _check(lib().lal_tail_device_buffers(self.h, C.byref(a), C.byref(b), C.byref(c)))
         return a.value, b.value, c.value
+
+    def debug_phases(self, on: bool):
+        _check(lib().lal_tail_debug_phases(self.h, 1 if on else 0))
+
+    def phase_times(self):
+        """(per-CTA stamps [grid, 4], merge stamps [4]) in ns, relative to the
+        earliest CTA start, of the last launch."""
+        g = C.c_int()
+        _check(lib().lal_tail_debug_phase_read(self.h, None, 0, C.byref(g)))
+        out = np.zeros((g.value + 1) * 8, np.uint64)
+        _check(lib().lal_tail_debug_phase_read(self.h, _ptr(out), out.size, C.byref(g)))
+        st = out.reshape(g.value + 1, 8)[:, :4].astype(np.int64)
+        t0 = st[:-1, 0].min()
+        return st[:-1] - t0, st[-1] - t0
 
     def stream(self) -> int:
         s = C.c_void_p()

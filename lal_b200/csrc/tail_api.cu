@@ -720,6 +720,8 @@ struct lal_tail {
     bool timing = false;
     std::vector<cudaEvent_t> ev;
     int ev_used = 0;
+    unsigned long long *phase_ts = nullptr;    /* [(kMaxGrid+1)*8] when on */
+    bool phases = false;
 };
 
 namespace {
@@ -730,7 +732,7 @@ void destroy_ctx(lal_tail *t) {
     if (t->stream) cudaStreamSynchronize(t->stream);
     void *bufs[] = {t->W, t->sw, t->io_in, t->io_out, t->logits, t->temp, t->topk, t->pen,
                     t->hist_ids, t->hist_n, t->hist_head, t->diag, t->recs, t->rec_keys,
-                    t->rec_idx, t->counter};
+                    t->rec_idx, t->counter, t->phase_ts};
     for (void *b : bufs)
         if (b) cudaFree(b);
     if (t->h_in) cudaFreeHost(t->h_in);
@@ -826,6 +828,7 @@ int enqueue_step(lal_tail *t, const float *d_hidden, int n, const float *d_u, in
         p.rec_idx = t->rec_idx;
         p.counter = t->counter + b;
         p.status = t->io_out + t->cfg.max_streams;
+        p.phase_ts = t->phases ? t->phase_ts : nullptr;
         const bool time_it = t->timing && t->ev_used + 2 <= (int)t->ev.size();
         if (time_it) CU(cudaEventRecord(t->ev[t->ev_used], t->stream));
         CU(launch_tail(p, t->grid, t->stream));
@@ -1085,6 +1088,26 @@ int lal_tail_set_timing(lal_tail *t, int on) {
         for (auto &e : t->ev) CU(cudaEventCreate(&e));
     }
     t->ev_used = 0;
+    return LAL_TAIL_OK;
+}
+
+int lal_tail_debug_phases(lal_tail *t, int on) {
+    CHECK(ctx_check(t));
+    if (on && !t->phase_ts) {
+        CU(cudaMalloc(&t->phase_ts, sizeof(unsigned long long) * (kMaxGrid + 1) * 8));
+        CU(cudaMemset(t->phase_ts, 0, sizeof(unsigned long long) * (kMaxGrid + 1) * 8));
+    }
+    t->phases = on != 0;
+    return LAL_TAIL_OK;
+}
+
+int lal_tail_debug_phase_read(lal_tail *t, unsigned long long *out, int cap, int *grid) {
+    CHECK(ctx_check(t));
+    if (grid) *grid = t->grid;
+    if (!t->phase_ts || !out) return LAL_TAIL_OK;
+    const int n = std::min(cap, (t->grid + 1) * 8);
+    CU(cudaStreamSynchronize(t->stream));
+    CU(cudaMemcpy(out, t->phase_ts, sizeof(unsigned long long) * n, cudaMemcpyDeviceToHost));
     return LAL_TAIL_OK;
 }
 

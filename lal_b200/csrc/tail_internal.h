@@ -87,6 +87,9 @@ struct TailParams {
     /* glibc expf fix-ups */
     const uint32_t *expf_x, *expf_y;
     int expf_n;
+    /* optional globaltimer stamps: [cta*8 + i] per CTA (start, prologue done,
+     * rows done, list written) and [grid*8 + i] for the merge */
+    unsigned long long *phase_ts;
     /* shared-memory layout (bytes) */
     int stages, rows_per_stage, stage_bytes, area_bytes;
     int off_bars, off_xq, off_sw, off_lg, off_cnt, off_misc, smem_total;

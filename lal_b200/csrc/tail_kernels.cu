@@ -32,7 +32,10 @@
 #include "tail_internal.h"
 #include "lal_expf.h"
 
+#include <algorithm>
 #include <cstdio>
+#include <utility>
+#include <vector>
 
 namespace lal {
 namespace {
@@ -161,6 +164,30 @@ __device__ __forceinline__ uint32_t block_scan_excl(uint32_t v, Misc *ms, uint32
     return res;
 }
 
+/* Barrier among the kConsumerWarps consumer warps only (named barrier 1), so
+ * the producer warp can stream while the consumers run the prologue. */
+__device__ __forceinline__ void consumer_sync() {
+    asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+}
+
+/* max over the consumer warps' values (consumer threads only) */
+__device__ __forceinline__ float consumer_max_f(float v, Misc *ms) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if (lane == 0) ms->fred[warp] = v;
+    consumer_sync();
+    float r = ms->fred[0];
+#pragma unroll
+    for (int w = 1; w < kConsumerWarps; ++w) r = fmaxf(r, ms->fred[w]);
+    consumer_sync();
+    return r;
+}
+
+__device__ __forceinline__ void stamp(const TailParams &p, int slot) {
+    if (p.phase_ts) p.phase_ts[slot] = gtimer();
+}
+
 __device__ __forceinline__ float block_max_f(float v, Misc *ms) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll
@@ -275,8 +302,9 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
     const bool use_pen = (MODE != MODE_LMHEAD) && (pen > 1.0f) && hn > 0 &&
                          (p.variant == VARIANT_SERVER || !greedy);
 
-    /* ---- phase 0: barriers, quantized vector, scales, penalty counts ---- */
+    /* ---- phase 0: barriers -------------------------------------------- */
     if (tid == 0) {
+        stamp(p, cta * 8 + 0);
         ms->abort_flag = 0;
         if (MODE != MODE_SAMPLE) {
             for (int s = 0; s < p.stages; ++s) {
@@ -286,51 +314,64 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
             mbar_fence_init();
         }
     }
-    if (MODE == MODE_FUSED) {
-        /* lal_quantize_x_int8 (runtime/lal_q8_kernel.h:375-424), redundantly
-         * per CTA: absmax, scale = max/127 floored at 1e-8, inv = 1/scale,
-         * RNE for the first d&~7 elements and truncation for the tail. */
-        const float *h = p.hidden;
-        float m = 0.0f;
-        for (int i = tid; i < p.d; i += NT) m = fmaxf(m, fabsf(h[i]));
-        m = block_max_f(m, ms);
-        float scale = __fdiv_rn(m, 127.0f);
-        if (scale < 1e-8f) scale = 1e-8f;
-        const float inv = __fdiv_rn(1.0f, scale);
-        const int n8 = p.d & ~7;
-        for (int i = tid; i < p.ld; i += NT) {
-            int v = 0;
-            if (i < p.d) {
-                const float s = __fmul_rn(h[i], inv);
-                if (s != s) v = -127;
-                else {
-                    v = (i < n8) ? __float2int_rn(s) : __float2int_rz(s);
-                    v = v > 127 ? 127 : (v < -127 ? -127 : v);
+    __syncthreads();
+
+    /* ---- the consumer warps' prologue (the producer streams meanwhile):
+     * quantized vector, row scales, penalty counts ------------------------ */
+    if (warp < kConsumerWarps) {
+        const int ctid = tid; /* 0 .. kConsumerWarps*32-1 */
+        constexpr int NC = kConsumerWarps * 32;
+        if (MODE == MODE_FUSED) {
+            /* lal_quantize_x_int8 (runtime/lal_q8_kernel.h:375-424), redundantly
+             * per CTA: absmax, scale = max/127 floored at 1e-8, inv = 1/scale,
+             * RNE for the first d&~7 elements and truncation for the tail. */
+            const float *h = p.hidden;
+            float m = 0.0f;
+#pragma unroll 4
+            for (int i = ctid; i < p.d; i += NC) m = fmaxf(m, fabsf(__ldg(h + i)));
+            m = consumer_max_f(m, ms);
+            float scale = __fdiv_rn(m, 127.0f);
+            if (scale < 1e-8f) scale = 1e-8f;
+            const float inv = __fdiv_rn(1.0f, scale);
+            const int n8 = p.d & ~7;
+#pragma unroll 4
+            for (int i = ctid; i < p.ld; i += NC) {
+                int v = 0;
+                if (i < p.d) {
+                    const float s = __fmul_rn(__ldg(h + i), inv);
+                    if (s != s) v = -127;
+                    else {
+                        v = (i < n8) ? __float2int_rn(s) : __float2int_rz(s);
+                        v = v > 127 ? 127 : (v < -127 ? -127 : v);
+                    }
+                }
+                xq_s[i] = (int8_t)v;
+            }
+            if (ctid == 0) ms->sx = scale;
+        } else if (MODE == MODE_LMHEAD) {
+            for (int i = ctid; i < p.ld; i += NC) xq_s[i] = i < p.d ? p.xq_in[i] : (int8_t)0;
+            if (ctid == 0) ms->sx = p.scale_x_in;
+        }
+        if (MODE != MODE_SAMPLE)
+#pragma unroll 4
+            for (int i = ctid; i < nloc; i += NC) sw_s[i] = __ldg(p.scale_w + c0 + i);
+        if (MODE != MODE_LMHEAD) {
+            for (int i = ctid; i < nloc; i += NC) cnt_s[i] = 0u;
+            consumer_sync();
+            if (use_pen) {
+                /* runtime/lal_sampling.h:60-66: ids outside [0, V) are skipped */
+#pragma unroll 4
+                for (int i = ctid; i < hn; i += NC) {
+                    const int t = p.hist_ids[i];
+                    if (t < 0 || t >= p.vocab) continue;
+                    const int g = t - p.row_base;
+                    if (g >= c0 && g < c1) atomicAdd(&cnt_s[g - c0], 1u);
                 }
             }
-            xq_s[i] = (int8_t)v;
         }
-        if (tid == 0) ms->sx = scale;
-    } else if (MODE == MODE_LMHEAD) {
-        for (int i = tid; i < p.ld; i += NT) xq_s[i] = i < p.d ? p.xq_in[i] : (int8_t)0;
-        if (tid == 0) ms->sx = p.scale_x_in;
+        consumer_sync();
+        if (ctid == 0) stamp(p, cta * 8 + 1);
     }
-    if (MODE != MODE_SAMPLE)
-        for (int i = tid; i < nloc; i += NT) sw_s[i] = p.scale_w[c0 + i];
-    if (MODE != MODE_LMHEAD) {
-        for (int i = tid; i < nloc; i += NT) cnt_s[i] = 0u;
-        __syncthreads();
-        if (use_pen) {
-            /* runtime/lal_sampling.h:60-66: ids outside [0, V) are skipped */
-            for (int i = tid; i < hn; i += NT) {
-                const int t = p.hist_ids[i];
-                if (t < 0 || t >= p.vocab) continue;
-                const int g = t - p.row_base;
-                if (g >= c0 && g < c1) atomicAdd(&cnt_s[g - c0], 1u);
-            }
-        }
-    }
-    __syncthreads();
 
     /* ---- phase 1: logits of this CTA's rows --------------------------- */
     if (MODE != MODE_SAMPLE) {
@@ -417,11 +458,13 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
             }
         }
         __syncthreads();
+        if (tid == 0) stamp(p, cta * 8 + 2);
         if (MODE == MODE_LMHEAD) {
             if (tid == 0 && ms->abort_flag) atomicCAS(p.status, 0, (int)DEV_TIMEOUT);
             return;
         }
     } else {
+        __syncthreads(); /* penalty counts come from the consumers' prologue */
         for (int i = tid; i < nloc; i += NT) {
             float l = p.logits[c0 + i];
             const uint32_t cnt = cnt_s[i];
@@ -491,6 +534,7 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
             r.overflow = nsel_tot > (uint32_t)p.list_cap ? 1 : 0;
             p.recs[cta] = r;
             if (ms->abort_flag) atomicCAS(p.status, 0, (int)DEV_TIMEOUT);
+            stamp(p, cta * 8 + 3);
         }
     }
 
@@ -502,15 +546,18 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
     if (ms->ticket != G - 1) return;
     __threadfence();
 
-    /* Merge buffers reuse the stage area.  When every list fits in shared
-     * memory (with room left for candidates) the entries >= L are staged
-     * there first; otherwise (large k) the select and the compaction read the
-     * lists straight from global memory. */
+    /* Merge buffers reuse the stage area.  When the lists fit in shared
+     * memory (staged), their keys are copied there with coalesced vector
+     * loads, the entries >= L are compacted there (key + list position) and
+     * selected there; otherwise (large k) the select and the compaction read
+     * the lists straight from global memory. */
+    if (tid == 0) stamp(p, G * 8 + 0);
     const int Fn = G * p.list_cap;
-    const bool staged = (long long)Fn * 8 + 12ll * 4 * p.list_cap <= (long long)p.area_bytes;
-    const size_t b_bytes = staged ? (size_t)Fn * 8 : 0;
-    uint32_t *Bk = reinterpret_cast<uint32_t *>(smem);
-    int *Bi = reinterpret_cast<int *>(smem + (size_t)Fn * 4);
+    const bool staged = 12ll * Fn + 12ll * 4 * p.list_cap <= (long long)p.area_bytes;
+    const size_t b_bytes = staged ? (size_t)Fn * 12 : 0;
+    uint32_t *Fk = reinterpret_cast<uint32_t *>(smem);
+    uint32_t *Bk = Fk + Fn;
+    int *Bp = reinterpret_cast<int *>(Bk + Fn);
     const int cand_cap = (int)((p.area_bytes - (long long)b_bytes) / 12);
     float *Cv = reinterpret_cast<float *>(smem + b_bytes);
     int *Ci = reinterpret_cast<int *>(Cv + cand_cap);
@@ -523,6 +570,14 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
         ms->flags[g] = (raw.y >= k ? 1 : 0) | (raw.w ? 2 : 0);
     }
     if (tid == 0) ms->sh[4] = 0u;
+    if (staged) {
+        const int n4 = Fn / 4;
+        const int4 *src = reinterpret_cast<const int4 *>(p.rec_keys);
+        int4 *dst = reinterpret_cast<int4 *>(Fk);
+#pragma unroll 8
+        for (int i = tid; i < n4; i += NT) dst[i] = __ldcg(src + i);
+        for (int i = 4 * n4 + tid; i < Fn; i += NT) Fk[i] = __ldcg(p.rec_keys + i);
+    }
     __syncthreads();
     /* Lower bound: the global k-th largest T is >= every full list's cut. */
     for (int g = tid; g < G; g += NT)
@@ -534,10 +589,10 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
     auto list_entry = [&](int e, uint32_t &key) {
         const int g = e / p.list_cap, j = e - g * p.list_cap;
         if (j >= ms->nout[g]) return false;
-        key = __ldcg(p.rec_keys + e);
+        key = staged ? Fk[e] : __ldcg(p.rec_keys + e);
         return key >= L;
     };
-    /* gather list entries >= L (staged) or count them (global) */
+    /* compact the list entries >= L (staged) or count them (global) */
     {
         const int seg = (Fn + NT - 1) / NT;
         const int e0 = min(Fn, tid * seg), e1 = min(Fn, e0 + seg);
@@ -549,7 +604,7 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
             for (int e = e0; e < e1; ++e)
                 if (list_entry(e, key)) {
                     Bk[pos] = key;
-                    Bi[pos] = __ldcg(p.rec_idx + e);
+                    Bp[pos] = e;
                     ++pos;
                 }
         if (tid == 0) ms->sh[5] = Mt;
@@ -564,6 +619,7 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
                                     },
                                     M, kk, ms)
                               : block_kth_largest(list_entry, Fn, kk, ms);
+    if (tid == 0) stamp(p, G * 8 + 1);
 
     /* A list whose ties at its cut did not fit is only a problem when that
      * cut is a candidate value. */
@@ -575,8 +631,7 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
     __syncthreads();
     const bool overflow = ms->found != 0;
 
-    /* candidates {v : l[v] >= T} in ascending vocab order (Bk/Bi and Cv/Ci
-     * do not overlap) */
+    /* candidates {v : l[v] >= T} in ascending vocab order */
     int m;
     {
         const int n_src = staged ? M : Fn;
@@ -597,13 +652,13 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
                 else if (!list_entry(e, key)) continue;
                 if (key >= T) {
                     Cv[pos] = key2f(key);
-                    Ci[pos] = staged ? Bi[e] : __ldcg(p.rec_idx + e);
+                    Ci[pos] = __ldcg(p.rec_idx + (staged ? Bp[e] : e));
                     ++pos;
                 }
             }
     }
     __syncthreads();
-
+    if (tid == 0) stamp(p, G * 8 + 2);
     StreamDiag dg;
     dg.threshold = key2f(T);
     dg.max_l = 0.0f;
@@ -711,6 +766,7 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
             }
         }
         p.counter[0] = 0u;
+        stamp(p, G * 8 + 3);
     }
 }
 
@@ -937,9 +993,18 @@ cudaError_t launch_tail(const TailParams &p, int grid, cudaStream_t st) {
     else if (p.mode == MODE_LMHEAD) fn = pick_kernel<MODE_LMHEAD>(p.nch);
     else fn = (void *)tail_kernel<MODE_SAMPLE, 1>;
     if (!fn) return cudaErrorInvalidValue;
-    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         p.smem_total);
+    /* raise the dynamic shared-memory limit once per (device, kernel) */
+    thread_local std::vector<std::pair<int, void *>> raised;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
+    bool done = false;
+    for (const auto &r : raised) done |= (r.first == dev && r.second == fn);
+    if (!done) {
+        e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+        if (e != cudaSuccess) return e;
+        raised.emplace_back(dev, fn);
+    }
     void *args[] = {const_cast<TailParams *>(&p)};
     return cudaLaunchKernel(fn, dim3(grid), dim3(NT), args, (size_t)p.smem_total, st);
 }
