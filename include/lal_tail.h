@@ -192,10 +192,12 @@ int lal_tail_set_timing(lal_tail *t, int on);
 int lal_tail_kernel_time(lal_tail *t, double *avg_ms, int *n_launches);
 
 /* Phase timing of the fused kernel (inspection hook).  When on, every launch
- * writes globaltimer stamps (ns): per CTA c, out[c*8 + 0..3] = start,
- * prologue done, rows done, candidate list written; for the merge,
- * out[grid*8 + 0..3] = merge start, threshold found, candidates gathered,
- * token written.  read copies the last launch's (grid+1)*8 stamps. */
+ * writes globaltimer stamps (ns): per CTA c, out[c*8 + 0..7] = start,
+ * prologue done, rows done, histogram levels 0/1/2 merged (grid barriers;
+ * levels 1-2 only when used), -, arrival at the final ticket; for the last
+ * CTA, out[grid*8 + 0..3] = select start, threshold found, candidates in
+ * vocab order, token written.  read copies the last launch's (grid+1)*8
+ * stamps. */
 int lal_tail_debug_phases(lal_tail *t, int on);
 int lal_tail_debug_phase_read(lal_tail *t, unsigned long long *out, int cap, int *grid);
 

@@ -147,25 +147,67 @@ struct PinBuf {
     }
 };
 
-/* Scratch that one launch of the streaming kernel needs for one stream. */
+/* Scratch of the select (global memory beyond inputs and outputs): the key
+ * histogram, grid-barrier words, superset buffer, arrival ticket. */
+struct SelectScratch {
+    unsigned *ghist = nullptr, *gbar = nullptr, *gcount = nullptr, *counter = nullptr;
+    uint32_t *gkey = nullptr;
+    int *gidx = nullptr;
+    int cap = 0;
+    int alloc(int cap_) {
+        CU(cudaMalloc(&ghist, 4ull * (kHistWords + 8)));
+        gbar = ghist + kHistWords;
+        gcount = gbar + 2;
+        counter = gbar + 3;
+        CU(cudaMemset(ghist, 0, 4ull * (kHistWords + 8)));
+        cap = std::max(cap_, 1);
+        CU(cudaMalloc(&gkey, 4ull * cap));
+        CU(cudaMalloc(&gidx, 4ull * cap));
+        return LAL_TAIL_OK;
+    }
+    /* after a device error the words may be mid-update: start clean */
+    int reset(cudaStream_t st) {
+        CU(cudaMemsetAsync(ghist, 0, 4ull * (kHistWords + 8), st));
+        return LAL_TAIL_OK;
+    }
+    void free_all() {
+        if (ghist) cudaFree(ghist);
+        if (gkey) cudaFree(gkey);
+        if (gidx) cudaFree(gidx);
+        ghist = gbar = gcount = counter = nullptr;
+        gkey = nullptr;
+        gidx = nullptr;
+    }
+    void fill(TailParams &p) const {
+        p.ghist = ghist;
+        p.gbar = gbar;
+        p.gcount = gcount;
+        p.counter = counter;
+        p.gcand_key = gkey;
+        p.gcand_idx = gidx;
+        p.gcand_cap = cap;
+    }
+};
+
+/* Scratch of the drop-ins' launches (one set per host thread). */
 struct LaunchScratch {
-    DevBuf recs, keys, idx, counter, status, diag, tokens, params, hist, cand_v, cand_i,
-        keep, prefix, u;
-    int grid_cap = 0, list_cap = 0;
-    int ensure(int grid, int list_cap_) {
-        if (grid <= grid_cap && list_cap_ <= list_cap) return LAL_TAIL_OK;
-        grid_cap = std::max(grid, grid_cap);
-        list_cap = std::max(list_cap_, list_cap);
-        CHECK(recs.ensure(sizeof(CtaRecord) * grid_cap));
-        CHECK(keys.ensure(4ull * grid_cap * list_cap));
-        CHECK(idx.ensure(4ull * grid_cap * list_cap));
-        CHECK(counter.ensure(64));
-        CU(cudaMemset(counter.p, 0, 64));
+    DevBuf status, diag, tokens, params, hist, cand_v, cand_i, keep, prefix, u;
+    SelectScratch sel;
+    bool ready = false;
+    ~LaunchScratch() { sel.free_all(); }
+    int ensure(int vocab) {
+        if (ready && vocab <= sel.cap) return LAL_TAIL_OK;
+        if (sel.ghist) {
+            CU(cudaDeviceSynchronize());
+            sel.free_all();
+        }
+        CHECK(sel.alloc(std::max(vocab, 1 << 16)));
         CHECK(status.ensure(64));
         CU(cudaMemset(status.p, 0, 64));
         CHECK(diag.ensure(sizeof(StreamDiag)));
         CHECK(tokens.ensure(64));
         CHECK(params.ensure(64));
+        ready = true;
         return LAL_TAIL_OK;
     }
 };
@@ -274,10 +316,10 @@ int sample_launch(DropinState *S, DeviceState *ds, float *logits, int V, float t
     p.vocab = V;
     p.d = p.ld = 16;
     p.B = 1;
-    p.list_cap = k + kTieExtra;
+    p.max_k = k;
     const int grid = plan_launch(p, ds->num_sms, 64);
     if (grid < 1) return fail(LAL_TAIL_ERR_UNSUPPORTED, "sample: shape unsupported (plan %d)", grid);
-    CHECK(S->ls.ensure(grid, p.list_cap));
+    CHECK(S->ls.ensure(V));
     CHECK(S->logits.ensure(sizeof(float) * (size_t)V));
     CHECK(S->ls.hist.ensure(sizeof(int) * (size_t)(n_recent + 1)));
     CHECK(S->ls.cand_v.ensure(sizeof(float) * (size_t)V));
@@ -309,10 +351,7 @@ int sample_launch(DropinState *S, DeviceState *ds, float *logits, int V, float t
     p.push_history = 0;
     p.tokens = (int *)S->ls.tokens.p;
     p.diag = (StreamDiag *)S->ls.diag.p;
-    p.recs = (CtaRecord *)S->ls.recs.p;
-    p.rec_keys = (uint32_t *)S->ls.keys.p;
-    p.rec_idx = (int *)S->ls.idx.p;
-    p.counter = (unsigned *)S->ls.counter.p;
+    S->ls.sel.fill(p);
     p.status = (int *)S->ls.status.p;
     p.cand_val_out = (float *)S->ls.cand_v.p;
     p.cand_idx_out = (int *)S->ls.cand_i.p;
@@ -327,6 +366,8 @@ int sample_launch(DropinState *S, DeviceState *ds, float *logits, int V, float t
     CU(cudaStreamSynchronize(st));
     if (status != 0) {
         CU(cudaMemset(S->ls.status.p, 0, sizeof(int)));
+        CHECK(S->ls.sel.reset(st));
+        CU(cudaStreamSynchronize(st));
         return fail(status, "sample kernel reported device status %d (%s)", status,
                     status == LAL_TAIL_ERR_TIMEOUT ? "bounded wait expired"
                                                    : "candidate set above the built capacity");
@@ -453,7 +494,7 @@ int lm_head_range(float *logits, const int8_t *xq, float scale_x, const int8_t *
     p.d = n_embd;
     p.ld = h.ld;
     p.B = 1;
-    p.list_cap = 1;
+    p.max_k = 1;
     p.trunc_cols = h.ld;
     p.trunc_rows_end = 0;
     if (eight_row && (n_embd & 31) != 0) {
@@ -462,7 +503,7 @@ int lm_head_range(float *logits, const int8_t *xq, float scale_x, const int8_t *
     }
     const int grid = plan_launch(p, ds->num_sms, 8);
     if (grid < 1) return fail(LAL_TAIL_ERR_UNSUPPORTED, "lm_head: shape unsupported (plan %d)", grid);
-    CHECK(S->ls.ensure(grid, 1));
+    CHECK(S->ls.ensure(1));
     CHECK(S->xq.ensure((size_t)n_embd));
     CHECK(S->logits.ensure(4ull * rows));
     CU(cudaMemcpyAsync(S->xq.p, xq, (size_t)n_embd, cudaMemcpyHostToDevice, st));
@@ -470,7 +511,6 @@ int lm_head_range(float *logits, const int8_t *xq, float scale_x, const int8_t *
     p.scale_x_in = scale_x;
     p.logits = (float *)S->logits.p;
     p.status = (int *)S->ls.status.p;
-    p.counter = (unsigned *)S->ls.counter.p;
     CU(launch_tail(p, grid, st));
     int status = 0;
     CU(cudaMemcpyAsync(logits + v_start, S->logits.p, 4ull * rows, cudaMemcpyDeviceToHost, st));
@@ -704,11 +744,7 @@ struct lal_tail {
     float *pen = nullptr;                      /* [B] */
     int *hist_ids = nullptr, *hist_n = nullptr, *hist_head = nullptr;
     StreamDiag *diag = nullptr;                /* [B] */
-    CtaRecord *recs = nullptr;
-    uint32_t *rec_keys = nullptr;
-    int *rec_idx = nullptr;
-    unsigned *counter = nullptr;               /* [B] */
-    int list_cap = 0;
+    SelectScratch sel;                         /* shared by the streams' launches */
     float *h_in = nullptr;                     /* pinned staging */
     int *h_out = nullptr;
     std::vector<float> h_temp;
@@ -731,10 +767,10 @@ void destroy_ctx(lal_tail *t) {
     if (t->device >= 0) cudaSetDevice(t->device);
     if (t->stream) cudaStreamSynchronize(t->stream);
     void *bufs[] = {t->W, t->sw, t->io_in, t->io_out, t->logits, t->temp, t->topk, t->pen,
-                    t->hist_ids, t->hist_n, t->hist_head, t->diag, t->recs, t->rec_keys,
-                    t->rec_idx, t->counter, t->phase_ts};
+                    t->hist_ids, t->hist_n, t->hist_head, t->diag, t->phase_ts};
     for (void *b : bufs)
         if (b) cudaFree(b);
+    t->sel.free_all();
     if (t->h_in) cudaFreeHost(t->h_in);
     if (t->h_out) cudaFreeHost(t->h_out);
     for (cudaEvent_t e : t->ev) cudaEventDestroy(e);
@@ -764,12 +800,7 @@ int ctx_alloc(lal_tail *t) {
     CU(cudaMemset(t->hist_head, 0, 4ull * B));
     CU(cudaMalloc(&t->diag, sizeof(StreamDiag) * B));
     CU(cudaMemset(t->diag, 0, sizeof(StreamDiag) * B));
-    t->list_cap = c.max_top_k + kTieExtra;
-    CU(cudaMalloc(&t->recs, sizeof(CtaRecord) * kMaxGrid));
-    CU(cudaMalloc(&t->rec_keys, 4ull * kMaxGrid * t->list_cap));
-    CU(cudaMalloc(&t->rec_idx, 4ull * kMaxGrid * t->list_cap));
-    CU(cudaMalloc(&t->counter, 4ull * B));
-    CU(cudaMemset(t->counter, 0, 4ull * B));
+    CHECK(t->sel.alloc(t->nrows));
     CU(cudaMallocHost(&t->h_in, 4ull * ((size_t)B * d + B)));
     CU(cudaMallocHost(&t->h_out, 4ull * (B + 1)));
     t->h_temp.assign(B, 0.0f);
@@ -786,7 +817,7 @@ int ctx_alloc(lal_tail *t) {
     p.d = d;
     p.ld = t->ld;
     p.B = 1;
-    p.list_cap = t->list_cap;
+    p.max_k = std::min(c.max_top_k, t->nrows);
     t->grid = plan_launch(p, t->ds->num_sms, 8);
     if (t->grid < 1)
         return fail(LAL_TAIL_ERR_UNSUPPORTED, "fused tail: shape V=%d d=%d k=%d unsupported (plan %d)",
@@ -823,10 +854,7 @@ int enqueue_step(lal_tail *t, const float *d_hidden, int n, const float *d_u, in
         p.push_history = t->cfg.history_cap > 0 ? 1 : 0;
         p.tokens = d_tokens + b;
         p.diag = t->diag + b;
-        p.recs = t->recs;
-        p.rec_keys = t->rec_keys;
-        p.rec_idx = t->rec_idx;
-        p.counter = t->counter + b;
+        t->sel.fill(p);
         p.status = t->io_out + t->cfg.max_streams;
         p.phase_ts = t->phases ? t->phase_ts : nullptr;
         const bool time_it = t->timing && t->ev_used + 2 <= (int)t->ev.size();
@@ -1023,6 +1051,8 @@ int lal_tail_sync(lal_tail *t) {
     CU(cudaStreamSynchronize(t->stream));
     if (status != 0) {
         CU(cudaMemset(t->io_out + t->cfg.max_streams, 0, 4));
+        CHECK(t->sel.reset(t->stream));
+        CU(cudaStreamSynchronize(t->stream));
         return fail(status, "device status %d (%s)", status,
                     status == LAL_TAIL_ERR_TIMEOUT ? "bounded wait expired"
                                                    : "candidate set above the built capacity");
@@ -1052,6 +1082,8 @@ int lal_tail_step(lal_tail *t, const float *hidden, int n_streams, const float *
     const int status = t->h_out[B];
     if (status != 0) {
         CU(cudaMemset(t->io_out + B, 0, 4));
+        CHECK(t->sel.reset(t->stream));
+        CU(cudaStreamSynchronize(t->stream));
         return fail(status, "device status %d (%s)", status,
                     status == LAL_TAIL_ERR_TIMEOUT ? "bounded wait expired"
                                                    : "candidate set above the built capacity");

@@ -14,11 +14,13 @@ namespace lal {
 constexpr int kConsumerWarps = 8;
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
 constexpr int kMaxStages = 8;
-/* Extra list slots per CTA beyond k, so that values tied with a CTA's k-th
- * largest are all reported (tie-complete candidate sets). */
-constexpr int kTieExtra = 32;
-/* Largest grid the merge supports (one CTA per SM on B200 is 148). */
+/* Largest grid (one CTA per SM on B200 is 148). */
 constexpr int kMaxGrid = 256;
+/* Global key histogram of the threshold search: level 0 = the top 12 bits
+ * of the order key, levels 1 and 2 = the next 10 + 10 bits, used only while
+ * the boundary bin holds more than kRefineMax keys. */
+constexpr int kHistWords = 4096 + 1024 + 1024;
+constexpr int kRefineMax = 2048;
 /* Largest per-CTA row slice (smem holds its logits, scales, penalty counts). */
 constexpr int kMaxRowsPerCta = 4096;
 
@@ -27,14 +29,6 @@ enum Variant : int { VARIANT_LIBRARY = 0, VARIANT_SERVER = 1 };
 
 /* Device status word values (mirrors LAL_TAIL_ERR_* in include/lal_tail.h). */
 enum DevStatus : int { DEV_OK = 0, DEV_TIMEOUT = 4, DEV_CAPACITY = 5 };
-
-/* One per (stream, CTA): the CTA's candidate list summary. */
-struct CtaRecord {
-    uint32_t cut_key;     /* key of the CTA's k-th largest (valid if n_local >= k) */
-    int n_local;          /* rows in the CTA slice                                 */
-    int n_out;            /* entries written to the list                           */
-    int overflow;         /* 1 if ties at cut_key did not fit the list             */
-};
 
 /* Per-stream outputs of a sampling launch (same layout as lal_tail_diag). */
 struct StreamDiag {
@@ -72,12 +66,16 @@ struct TailParams {
     /* outputs */
     int *tokens;
     StreamDiag *diag;
-    /* scratch (global memory beyond inputs and outputs) */
-    CtaRecord *recs;         /* [B][grid]                                     */
-    uint32_t *rec_keys;      /* [B][grid][list_cap]                           */
-    int *rec_idx;            /* [B][grid][list_cap]                           */
-    int list_cap;
-    unsigned int *counter;   /* [B] arrival tickets, self-resetting           */
+    /* scratch (global memory beyond inputs and outputs); every word returns
+     * to zero (or, for the barrier generation, to a consistent value) by
+     * the end of a launch */
+    unsigned *ghist;         /* [kHistWords] global key histogram             */
+    unsigned *gbar;          /* [2] grid barrier: arrivals, generation        */
+    unsigned *gcount;        /* [1] superset entries appended                 */
+    uint32_t *gcand_key;     /* [gcand_cap] superset {key >= boundary}        */
+    int *gcand_idx;          /* [gcand_cap] their vocab indices               */
+    int gcand_cap;
+    unsigned int *counter;   /* [1] arrival tickets, self-resetting           */
     int *status;             /* device status word                            */
     /* optional export of the candidate set (ascending vocab order) */
     float *cand_val_out;
@@ -95,6 +93,7 @@ struct TailParams {
     int off_bars, off_xq, off_sw, off_lg, off_cnt, off_misc, smem_total;
     int rows_per_cta_max;
     int nch;                 /* 512-byte column chunks per row                */
+    int max_k;               /* largest k a launch may use (planning)         */
 };
 
 /* Second half of the server sampler with a level-2 filter

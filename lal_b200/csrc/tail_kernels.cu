@@ -107,6 +107,15 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
         : "memory");
 }
 
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_gpu(unsigned *p, unsigned v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
 /* ------------------------------------------------------- order keys --- */
 /* Monotone map float -> uint32 (larger float, larger key).  -0 maps like +0,
  * so key equality is float equality, as the reference's comparisons treat it. */
@@ -123,17 +132,46 @@ __device__ __forceinline__ float key2f(uint32_t k) {
 struct Misc {
     uint32_t hist[256];
     uint32_t scan[NWARP + 1];
-    uint32_t sh[8];
+    uint32_t sh[16];
     float fred[NWARP];
     float sx;
     float sum;
     int abort_flag;
     int ticket;
     int found;
-    uint32_t cut[kMaxGrid];
-    int nout[kMaxGrid];
-    int flags[kMaxGrid];
 };
+
+/* Grid-wide barrier of a cooperative launch (every CTA resident).  The
+ * wait is bounded: after kWaitNs it records DEV_TIMEOUT and returns false.
+ * bar[0] counts arrivals, bar[1] is the generation; the last arriver resets
+ * the count before publishing the next generation (release), so the words
+ * are ready for the next barrier and the next launch. */
+__device__ bool grid_sync(unsigned *bar, unsigned G, Misc *ms, int *status) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const unsigned gen = ld_acquire_gpu(bar + 1);
+        __threadfence();
+        const unsigned arrived = atomicAdd(bar, 1u) + 1u;
+        unsigned ok = 1u;
+        if (arrived == G) {
+            bar[0] = 0u;
+            __threadfence();
+            st_release_gpu(bar + 1, gen + 1u);
+        } else {
+            const uint64_t t0 = gtimer();
+            while (ld_acquire_gpu(bar + 1) == gen) {
+                if (gtimer() - t0 > kWaitNs) {
+                    ok = 0u;
+                    atomicCAS(status, 0, (int)DEV_TIMEOUT);
+                    break;
+                }
+            }
+        }
+        ms->sh[15] = ok;
+    }
+    __syncthreads();
+    return ms->sh[15] != 0u;
+}
 
 /* Exclusive prefix (thread order) of one value per thread; *total = sum. */
 __device__ __forceinline__ uint32_t block_scan_excl(uint32_t v, Misc *ms, uint32_t *total) {
@@ -326,27 +364,42 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
              * per CTA: absmax, scale = max/127 floored at 1e-8, inv = 1/scale,
              * RNE for the first d&~7 elements and truncation for the tail. */
             const float *h = p.hidden;
+            /* one batch of loads: up to kHReg values per thread in registers */
+            constexpr int kHReg = 16;
+            float hv[kHReg];
             float m = 0.0f;
-#pragma unroll 4
-            for (int i = ctid; i < p.d; i += NC) m = fmaxf(m, fabsf(__ldg(h + i)));
+#pragma unroll
+            for (int j = 0; j < kHReg; ++j) {
+                const int i = ctid + j * NC;
+                hv[j] = i < p.d ? __ldg(h + i) : 0.0f;
+            }
+#pragma unroll
+            for (int j = 0; j < kHReg; ++j) m = fmaxf(m, fabsf(hv[j]));
+            for (int i = ctid + kHReg * NC; i < p.d; i += NC) m = fmaxf(m, fabsf(__ldg(h + i)));
             m = consumer_max_f(m, ms);
             float scale = __fdiv_rn(m, 127.0f);
             if (scale < 1e-8f) scale = 1e-8f;
             const float inv = __fdiv_rn(1.0f, scale);
             const int n8 = p.d & ~7;
-#pragma unroll 4
-            for (int i = ctid; i < p.ld; i += NC) {
+            auto quant = [&](int i, float x) {
                 int v = 0;
                 if (i < p.d) {
-                    const float s = __fmul_rn(__ldg(h + i), inv);
+                    const float s = __fmul_rn(x, inv);
                     if (s != s) v = -127;
                     else {
                         v = (i < n8) ? __float2int_rn(s) : __float2int_rz(s);
                         v = v > 127 ? 127 : (v < -127 ? -127 : v);
                     }
                 }
-                xq_s[i] = (int8_t)v;
+                return (int8_t)v;
+            };
+#pragma unroll
+            for (int j = 0; j < kHReg; ++j) {
+                const int i = ctid + j * NC;
+                if (i < p.ld) xq_s[i] = quant(i, hv[j]);
             }
+            for (int i = ctid + kHReg * NC; i < p.ld; i += NC)
+                xq_s[i] = quant(i, i < p.d ? __ldg(h + i) : 0.0f);
             if (ctid == 0) ms->sx = scale;
         } else if (MODE == MODE_LMHEAD) {
             for (int i = ctid; i < p.ld; i += NC) xq_s[i] = i < p.d ? p.xq_in[i] : (int8_t)0;
@@ -477,188 +530,168 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
         __syncthreads();
     }
 
-    /* ---- phase 2: this CTA's candidate list ---------------------------- *
-     * k = min(top_k, V) (runtime/lal_sampling.h:70-71); greedy is k = 1 with
-     * the lowest index among the maxima.  The list holds every local entry
-     * >= the local k-th largest (all ties, up to list_cap), in index order. */
+    /* ---- phase 2: the global threshold ---------------------------------- *
+     * k = min(top_k, V) (runtime/lal_sampling.h:70-71); greedy is k = 1 and
+     * takes the lowest index among the maxima.  T, the k-th largest
+     * penalised logit counted with multiplicity, is located with a global
+     * histogram of the order keys, built by all CTAs: a 12-bit level, then 10
+     * + 10 bits only while the boundary bin is large.  Every key >= the
+     * boundary bin's lower edge Lb (a tie-complete superset of {l >= T}) is
+     * appended to a global buffer; the last CTA selects T exactly from it. */
     int k = greedy ? 1 : topk;
     if (k > p.vocab) k = p.vocab;
+    if (k > p.rows) k = p.rows;
     if (k < 1) k = 1;
-    const bool tie_complete = !greedy;
+    uint32_t *lh = reinterpret_cast<uint32_t *>(smem); /* stage area is free now */
+    uint32_t prefix = 0u, pmask = 0u;
+    int above = 0, binc = 0;
+    bool ok = ms->abort_flag == 0;
+    for (int level = 0; level < 3; ++level) {
+        const int bits = level == 0 ? 12 : 10;
+        const int shift = level == 0 ? 20 : (level == 1 ? 10 : 0);
+        const int nb = 1 << bits;
+        unsigned *gh = p.ghist + (level == 0 ? 0 : (level == 1 ? 4096 : 5120));
+        for (int i = tid; i < nb; i += NT) lh[i] = 0u;
+        __syncthreads();
+        for (int i0 = 0; i0 < nloc; i0 += NT) {
+            const int i = i0 + tid;
+            const uint32_t key = i < nloc ? f2key(lg_s[i]) : 0u;
+            const bool m = i < nloc && (key & pmask) == prefix;
+            const uint32_t digit = (key >> shift) & (uint32_t)(nb - 1);
+            const unsigned voters = __ballot_sync(0xffffffffu, m);
+            if (m) {
+                const unsigned peers = __match_any_sync(voters, digit);
+                if ((int)(threadIdx.x & 31) == __ffs(peers) - 1)
+                    atomicAdd(&lh[digit], (uint32_t)__popc(peers));
+            }
+        }
+        __syncthreads();
+        for (int i = tid; i < nb; i += NT) {
+            const uint32_t c = lh[i];
+            if (c) atomicAdd(&gh[i], c);
+        }
+        ok = grid_sync(p.gbar, (unsigned)G, ms, p.status) && ok;
+        if (tid == 0) stamp(p, cta * 8 + 3 + level);
+        /* boundary bin, from the top: every CTA reads the same histogram */
+        for (int i = tid; i < nb; i += NT) lh[i] = __ldcg(gh + i);
+        __syncthreads();
+        const int per = (nb + NT - 1) / NT;
+        const int q0 = tid * per; /* descending positions q <-> bin nb-1-q */
+        uint32_t s = 0;
+        for (int q = q0; q < min(nb, q0 + per); ++q) s += lh[nb - 1 - q];
+        uint32_t tot;
+        const uint32_t ex = block_scan_excl(s, ms, &tot);
+        const uint32_t krem = (uint32_t)(k - above);
+        if (ex < krem && krem <= ex + s) {
+            uint32_t run = ex;
+            for (int q = q0; q < min(nb, q0 + per); ++q) {
+                const uint32_t c = lh[nb - 1 - q];
+                if (run + c >= krem) {
+                    ms->sh[0] = (uint32_t)(nb - 1 - q);
+                    ms->sh[1] = run;
+                    ms->sh[2] = c;
+                    break;
+                }
+                run += c;
+            }
+        }
+        __syncthreads();
+        above += (int)ms->sh[1];
+        binc = (int)ms->sh[2];
+        prefix |= ms->sh[0] << shift;
+        pmask |= (uint32_t)(nb - 1) << shift;
+        __syncthreads();
+        if (binc <= kRefineMax) break;
+    }
+    const uint32_t Lb = prefix; /* lower edge of the boundary bin */
+    const int S = above + binc; /* keys >= Lb over all CTAs */
+
+    /* append this CTA's keys >= Lb */
     {
-        const int kloc = min(k, nloc);
-        const uint32_t T = block_kth_largest(
-            [&](int i, uint32_t &key) {
-                key = f2key(lg_s[i]);
-                return true;
-            },
-            nloc, kloc, ms);
         const int seg = (nloc + NT - 1) / NT;
         const int i0 = min(nloc, tid * seg), i1 = min(nloc, i0 + seg);
-        uint32_t ngt = 0, neq = 0;
-        for (int i = i0; i < i1; ++i) {
-            const uint32_t key = f2key(lg_s[i]);
-            ngt += key > T;
-            neq += key == T;
-        }
+        uint32_t c = 0;
+        for (int i = i0; i < i1; ++i) c += f2key(lg_s[i]) >= Lb;
         uint32_t tot;
-        const uint32_t ex = block_scan_excl((ngt << 16) | neq, ms, &tot);
-        const uint32_t gt_tot = tot >> 16, eq_tot = tot & 0xFFFFu, eq_before = ex & 0xFFFFu;
-        const uint32_t need_eq = tie_complete ? eq_tot : (uint32_t)kloc - gt_tot;
-        const uint32_t my_eq = need_eq > eq_before ? min(neq, need_eq - eq_before) : 0u;
-        uint32_t nsel_tot;
-        uint32_t pos = block_scan_excl(ngt + my_eq, ms, &nsel_tot);
-        uint32_t *out_key = p.rec_keys + (size_t)cta * p.list_cap;
-        int *out_idx = p.rec_idx + (size_t)cta * p.list_cap;
-        uint32_t eqr = eq_before;
+        uint32_t pos = block_scan_excl(c, ms, &tot);
+        if (tid == 0) ms->sh[3] = tot ? atomicAdd(p.gcount, tot) : 0u;
+        __syncthreads();
+        pos += ms->sh[3];
         for (int i = i0; i < i1; ++i) {
             const uint32_t key = f2key(lg_s[i]);
-            bool sel = key > T;
-            if (key == T) {
-                sel = eqr < need_eq;
-                ++eqr;
-            }
-            if (sel) {
-                if (pos < (uint32_t)p.list_cap) {
-                    out_key[pos] = key;
-                    out_idx[pos] = p.row_base + c0 + i;
+            if (key >= Lb) {
+                if (pos < (uint32_t)p.gcand_cap) {
+                    p.gcand_key[pos] = key;
+                    p.gcand_idx[pos] = p.row_base + c0 + i;
                 }
                 ++pos;
             }
         }
-        if (tid == 0) {
-            CtaRecord r;
-            r.cut_key = T;
-            r.n_local = nloc;
-            r.n_out = (int)min(nsel_tot, (uint32_t)p.list_cap);
-            r.overflow = nsel_tot > (uint32_t)p.list_cap ? 1 : 0;
-            p.recs[cta] = r;
-            if (ms->abort_flag) atomicCAS(p.status, 0, (int)DEV_TIMEOUT);
-            stamp(p, cta * 8 + 3);
-        }
     }
 
-    /* ---- phase 3: the last CTA to arrive merges ------------------------ */
+    /* ---- phase 3: the last CTA to arrive selects and samples ------------ */
     __threadfence();
     __syncthreads();
-    if (tid == 0) ms->ticket = (int)atomicAdd(&p.counter[0], 1u);
+    if (tid == 0) {
+        ms->ticket = (int)atomicAdd(&p.counter[0], 1u);
+        stamp(p, cta * 8 + 7);
+    }
     __syncthreads();
     if (ms->ticket != G - 1) return;
     __threadfence();
-
-    /* Merge buffers reuse the stage area.  When the lists fit in shared
-     * memory (staged), their keys are copied there with coalesced vector
-     * loads, the entries >= L are compacted there (key + list position) and
-     * selected there; otherwise (large k) the select and the compaction read
-     * the lists straight from global memory. */
     if (tid == 0) stamp(p, G * 8 + 0);
-    const int Fn = G * p.list_cap;
-    const bool staged = 12ll * Fn + 12ll * 4 * p.list_cap <= (long long)p.area_bytes;
-    const size_t b_bytes = staged ? (size_t)Fn * 12 : 0;
-    uint32_t *Fk = reinterpret_cast<uint32_t *>(smem);
-    uint32_t *Bk = Fk + Fn;
-    int *Bp = reinterpret_cast<int *>(Bk + Fn);
-    const int cand_cap = (int)((p.area_bytes - (long long)b_bytes) / 12);
-    float *Cv = reinterpret_cast<float *>(smem + b_bytes);
-    int *Ci = reinterpret_cast<int *>(Cv + cand_cap);
-    float *Ce = reinterpret_cast<float *>(Ci + cand_cap);
 
-    for (int g = tid; g < G; g += NT) {
-        const int4 raw = __ldcg(reinterpret_cast<const int4 *>(p.recs + g));
-        ms->cut[g] = (uint32_t)raw.x;
-        ms->nout[g] = raw.z;
-        ms->flags[g] = (raw.y >= k ? 1 : 0) | (raw.w ? 2 : 0);
-    }
-    if (tid == 0) ms->sh[4] = 0u;
-    if (staged) {
-        const int n4 = Fn / 4;
-        const int4 *src = reinterpret_cast<const int4 *>(p.rec_keys);
-        int4 *dst = reinterpret_cast<int4 *>(Fk);
-#pragma unroll 8
-        for (int i = tid; i < n4; i += NT) dst[i] = __ldcg(src + i);
-        for (int i = 4 * n4 + tid; i < Fn; i += NT) Fk[i] = __ldcg(p.rec_keys + i);
-    }
-    __syncthreads();
-    /* Lower bound: the global k-th largest T is >= every full list's cut. */
-    for (int g = tid; g < G; g += NT)
-        if (ms->flags[g] & 1) atomicMax(&ms->sh[4], ms->cut[g]);
-    __syncthreads();
-    const uint32_t L = ms->sh[4];
+    /* shared-memory plan of the stage area: superset keys + indices (Sk, Si),
+     * then the candidates (Cv, Ci) and their ascending-index copies (Ov, Oi)
+     * and running sums (Ce), Ccap a power of two */
+    const int s_cap = p.area_bytes / 16;
+    int ccap = 1;
+    while (ccap * 2 * 20 <= p.area_bytes - 8 * s_cap) ccap *= 2;
+    uint32_t *Sk = reinterpret_cast<uint32_t *>(smem);
+    int *Si = reinterpret_cast<int *>(Sk + s_cap);
+    float *Cv = reinterpret_cast<float *>(Si + s_cap);
+    int *Ci = reinterpret_cast<int *>(Cv + ccap);
+    float *Ov = reinterpret_cast<float *>(Ci + ccap);
+    int *Oi = reinterpret_cast<int *>(Ov + ccap);
+    float *Ce = reinterpret_cast<float *>(Oi + ccap);
 
-    /* list entry e = (CTA g, position j); (g, j) order is vocab order */
-    auto list_entry = [&](int e, uint32_t &key) {
-        const int g = e / p.list_cap, j = e - g * p.list_cap;
-        if (j >= ms->nout[g]) return false;
-        key = staged ? Fk[e] : __ldcg(p.rec_keys + e);
-        return key >= L;
-    };
-    /* compact the list entries >= L (staged) or count them (global) */
-    {
-        const int seg = (Fn + NT - 1) / NT;
-        const int e0 = min(Fn, tid * seg), e1 = min(Fn, e0 + seg);
-        uint32_t cnt = 0, key;
-        for (int e = e0; e < e1; ++e) cnt += list_entry(e, key) ? 1u : 0u;
-        uint32_t Mt;
-        uint32_t pos = block_scan_excl(cnt, ms, &Mt);
-        if (staged)
-            for (int e = e0; e < e1; ++e)
-                if (list_entry(e, key)) {
-                    Bk[pos] = key;
-                    Bp[pos] = e;
-                    ++pos;
-                }
-        if (tid == 0) ms->sh[5] = Mt;
-    }
-    __syncthreads();
-    const int M = (int)ms->sh[5];
-    const int kk = min(k, M);
-    const uint32_t T = staged ? block_kth_largest(
-                                    [&](int i, uint32_t &key) {
-                                        key = Bk[i];
-                                        return true;
-                                    },
-                                    M, kk, ms)
-                              : block_kth_largest(list_entry, Fn, kk, ms);
-    if (tid == 0) stamp(p, G * 8 + 1);
-
-    /* A list whose ties at its cut did not fit is only a problem when that
-     * cut is a candidate value. */
-    if (tid == 0) ms->found = 0;
-    __syncthreads();
-    if (tie_complete)
-        for (int g = tid; g < G; g += NT)
-            if ((ms->flags[g] & 2) && ms->cut[g] >= T) ms->found = 1;
-    __syncthreads();
-    const bool overflow = ms->found != 0;
-
-    /* candidates {v : l[v] >= T} in ascending vocab order */
-    int m;
-    {
-        const int n_src = staged ? M : Fn;
-        const int seg = (n_src + NT - 1) / NT;
-        const int e0 = min(n_src, tid * seg), e1 = min(n_src, e0 + seg);
-        uint32_t cnt = 0, key;
-        for (int e = e0; e < e1; ++e) {
-            if (staged) key = Bk[e];
-            else if (!list_entry(e, key)) continue;
-            cnt += key >= T;
+    const int dev_status = __ldcg(p.status);
+    const int Sg = (int)__ldcg(p.gcount);
+    int m = 0;
+    uint32_t T = 0u;
+    bool fine = ok && dev_status == 0 && Sg == S && S <= s_cap && S <= p.gcand_cap && S >= 1;
+    if (fine) {
+        for (int i = tid; i < S; i += NT) {
+            Sk[i] = __ldcg(p.gcand_key + i);
+            Si[i] = __ldcg(p.gcand_idx + i);
         }
+        __syncthreads();
+        T = block_kth_largest(
+            [&](int i, uint32_t &key) {
+                key = Sk[i];
+                return true;
+            },
+            S, min(k, S), ms);
+        if (tid == 0) stamp(p, G * 8 + 1);
+        /* candidates {v : l[v] >= T} (superset order) */
+        const int seg = (S + NT - 1) / NT;
+        const int e0 = min(S, tid * seg), e1 = min(S, e0 + seg);
+        uint32_t c = 0;
+        for (int e = e0; e < e1; ++e) c += Sk[e] >= T;
         uint32_t mt;
-        uint32_t pos = block_scan_excl(cnt, ms, &mt);
+        uint32_t pos = block_scan_excl(c, ms, &mt);
         m = (int)mt;
-        if (m <= cand_cap)
-            for (int e = e0; e < e1; ++e) {
-                if (staged) key = Bk[e];
-                else if (!list_entry(e, key)) continue;
-                if (key >= T) {
-                    Cv[pos] = key2f(key);
-                    Ci[pos] = __ldcg(p.rec_idx + (staged ? Bp[e] : e));
+        if (m <= ccap)
+            for (int e = e0; e < e1; ++e)
+                if (Sk[e] >= T) {
+                    Cv[pos] = key2f(Sk[e]);
+                    Ci[pos] = Si[e];
                     ++pos;
                 }
-            }
+        fine = m >= 1 && m <= ccap;
     }
     __syncthreads();
-    if (tid == 0) stamp(p, G * 8 + 2);
+
     StreamDiag dg;
     dg.threshold = key2f(T);
     dg.max_l = 0.0f;
@@ -668,43 +701,83 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
     dg.greedy = greedy ? 1 : 0;
     dg.drew = 0;
     dg.token = -1;
-    const int dev_status = __ldcg(p.status);
-    if (dev_status != 0 || overflow || m > cand_cap || m < 1) {
+
+    /* leave the scratch clean for the next launch */
+    for (int i = tid; i < kHistWords; i += NT) p.ghist[i] = 0u;
+    if (tid == 0) {
+        *p.gcount = 0u;
+        p.counter[0] = 0u;
+    }
+    if (!fine) {
         if (tid == 0) {
-            if (dev_status == 0) atomicCAS(p.status, 0, (int)DEV_CAPACITY);
+            if (dev_status == 0) atomicCAS(p.status, 0, ok ? (int)DEV_CAPACITY : (int)DEV_TIMEOUT);
             p.tokens[0] = -1;
             p.diag[0] = dg;
-            p.counter[0] = 0u;
         }
         return;
     }
 
+    /* ascending vocab order: rank by counting for small sets, else bitonic */
+    if (m <= 64) {
+        for (int i = tid; i < m; i += NT) {
+            const int me = Ci[i];
+            int r = 0;
+            for (int j = 0; j < m; ++j) r += Ci[j] < me;
+            Oi[r] = me;
+            Ov[r] = Cv[i];
+        }
+    } else {
+        int n2 = 1;
+        while (n2 < m) n2 <<= 1;
+        for (int i = tid; i < n2; i += NT) {
+            Oi[i] = i < m ? Ci[i] : 0x7fffffff;
+            Ov[i] = i < m ? Cv[i] : 0.0f;
+        }
+        __syncthreads();
+        for (int size = 2; size <= n2; size <<= 1)
+            for (int stride = size >> 1; stride > 0; stride >>= 1) {
+                for (int i = tid; i < (n2 >> 1); i += NT) {
+                    const int lo = (i / stride) * stride * 2 + (i % stride);
+                    const int hi = lo + stride;
+                    const bool asc = (lo & size) == 0;
+                    const int a = Oi[lo], b = Oi[hi];
+                    if ((a > b) == asc) {
+                        Oi[lo] = b;
+                        Oi[hi] = a;
+                        const float t = Ov[lo];
+                        Ov[lo] = Ov[hi];
+                        Ov[hi] = t;
+                    }
+                }
+                __syncthreads();
+            }
+    }
+    __syncthreads();
+    if (tid == 0) stamp(p, G * 8 + 2);
+
     if (p.cand_val_out != nullptr && m <= p.cand_out_cap) {
         for (int i = tid; i < m; i += NT) {
-            p.cand_val_out[i] = Cv[i];
-            p.cand_idx_out[i] = Ci[i];
+            p.cand_val_out[i] = Ov[i];
+            p.cand_idx_out[i] = Oi[i];
         }
     }
     if (p.candidates_only) {
-        if (tid == 0) {
-            p.diag[0] = dg;
-            p.counter[0] = 0u;
-        }
+        if (tid == 0) p.diag[0] = dg;
         return;
     }
 
     /* max over candidates, floored at -1e30f (runtime/lal_sampling.h:107-109) */
     float mx = -1e30f;
-    for (int i = tid; i < m; i += NT) mx = fmaxf(mx, Cv[i]);
+    for (int i = tid; i < m; i += NT) mx = fmaxf(mx, Ov[i]);
     const float max_l = block_max_f(mx, ms);
     dg.max_l = max_l;
     int token;
     if (greedy) {
-        token = Ci[0];
+        token = Oi[0];
     } else {
         /* weights expf((l - max_l) / T) (runtime/lal_sampling.h:112) */
         for (int i = tid; i < m; i += NT) {
-            const float x = __fdiv_rn(__fsub_rn(Cv[i], max_l), temp);
+            const float x = __fdiv_rn(__fsub_rn(Ov[i], max_l), temp);
             Ce[i] = lal_expf_glibc(x, p.expf_x, p.expf_y, p.expf_n);
         }
         __syncthreads();
@@ -728,9 +801,9 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
             float bv = -1e30f;
             if (tid == 0)
                 for (int i = 0; i < m; ++i)
-                    if (Cv[i] > bv) {
-                        bv = Cv[i];
-                        token = Ci[i];
+                    if (Ov[i] > bv) {
+                        bv = Ov[i];
+                        token = Oi[i];
                     }
         } else {
             /* r = u * sum; first candidate with r <= running sum
@@ -746,7 +819,7 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
                 }
             if (first != 0x7fffffff) atomicMin(&ms->found, first);
             __syncthreads();
-            token = ms->found != 0x7fffffff ? Ci[ms->found] : p.vocab - 1;
+            token = ms->found != 0x7fffffff ? Oi[ms->found] : p.vocab - 1;
         }
     }
     if (tid == 0) {
@@ -765,7 +838,6 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
                 p.hist_head[0] = (h + 1) % p.hist_cap;
             }
         }
-        p.counter[0] = 0u;
         stamp(p, G * 8 + 3);
     }
 }
@@ -946,13 +1018,12 @@ int plan_launch(TailParams &p, int num_sms, int min_rows_per_cta) {
     int off = 0;
     const int fixed = 16 * kMaxStages + align_up(p.ld, 16) + 3 * 4 * rpc +
                       align_up((int)sizeof(Misc), 128) + 3 * 128;
-    const int budget = kSmemLimit - fixed;
-    const int merge_need = G * p.list_cap * 8 + 12 * std::max(2048, 4 * p.list_cap);
+    const int budget = (kSmemLimit - fixed) / 128 * 128;
     if (p.mode == MODE_SAMPLE) {
         p.stages = 0;
         p.rows_per_stage = 0;
         p.stage_bytes = 0;
-        p.area_bytes = std::min(budget, merge_need);
+        p.area_bytes = budget;
     } else {
         int R = std::max(1, 32768 / p.ld);
         if (R >= 8) R = R / 8 * 8;
@@ -961,12 +1032,14 @@ int plan_launch(TailParams &p, int num_sms, int min_rows_per_cta) {
         p.stages = std::min(kMaxStages, budget / p.stage_bytes);
         if (p.stages < 2) return -4;
         p.area_bytes = p.stages * p.stage_bytes;
-        if (p.mode == MODE_FUSED && p.area_bytes < merge_need)
-            p.area_bytes = std::min(budget, merge_need);
+        /* after the rows, the stage area holds the local key histogram and,
+         * in the last CTA, the superset and the candidates */
+        if (p.mode == MODE_FUSED) p.area_bytes = std::max(p.area_bytes, std::min(budget, 96 << 10));
     }
-    /* the merge needs room for at least the k candidates plus ties; staging
-     * the lists in shared memory is optional (see the kernel's merge) */
-    if (p.mode != MODE_LMHEAD && p.area_bytes < 12 * (p.list_cap + 64)) return -5;
+    /* the last CTA needs room for the candidates (k plus ties) and the key
+     * histogram of 4096 bins */
+    if (p.mode != MODE_LMHEAD && (p.area_bytes < 16384 || p.area_bytes / 2 < 20 * (p.max_k + 64)))
+        return -5;
     off = align_up(p.area_bytes, 128);
     p.off_bars = off;
     off += 16 * kMaxStages;
@@ -1006,7 +1079,11 @@ cudaError_t launch_tail(const TailParams &p, int grid, cudaStream_t st) {
         raised.emplace_back(dev, fn);
     }
     void *args[] = {const_cast<TailParams *>(&p)};
-    return cudaLaunchKernel(fn, dim3(grid), dim3(NT), args, (size_t)p.smem_total, st);
+    /* The select's grid barriers need every CTA resident: a cooperative
+     * launch guarantees it (or fails to launch). */
+    if (p.mode == MODE_LMHEAD)
+        return cudaLaunchKernel(fn, dim3(grid), dim3(NT), args, (size_t)p.smem_total, st);
+    return cudaLaunchCooperativeKernel(fn, dim3(grid), dim3(NT), args, (size_t)p.smem_total, st);
 }
 
 cudaError_t launch_quantize_x(const float *x, int8_t *xq, float *scale, int n,
