@@ -68,7 +68,7 @@ int fail(int code, const char *fmt, ...) {
 struct DeviceState {
     bool ready = false;
     int num_sms = 0;
-    uint32_t *d_expf_x = nullptr, *d_expf_y = nullptr;
+    uint32_t *d_expf_x = nullptr, *d_expf_y = nullptr, *d_expf_bits = nullptr;
     int expf_n = 0;
 };
 std::mutex g_dev_mu;
@@ -96,6 +96,16 @@ int device_state(int dev, DeviceState **out) {
         CU(cudaMemcpy(ds.d_expf_x, lal_expf_fixups_blob + 4, 4ull * n, cudaMemcpyHostToDevice));
         CU(cudaMemcpy(ds.d_expf_y, lal_expf_fixups_blob + 4 + 4ull * n, 4ull * n,
                       cudaMemcpyHostToDevice));
+        /* membership bitmap: most lookups end after one load */
+        std::vector<uint32_t> bits(kExpfBitmapWords, 0u);
+        for (uint32_t i = 0; i < n; ++i) {
+            uint32_t xb;
+            memcpy(&xb, lal_expf_fixups_blob + 4 + 4ull * i, 4);
+            const uint32_t b = (xb - 0x80000000u) >> 8;
+            bits[b >> 5] |= 1u << (b & 31);
+        }
+        CU(cudaMalloc(&ds.d_expf_bits, 4ull * kExpfBitmapWords));
+        CU(cudaMemcpy(ds.d_expf_bits, bits.data(), 4ull * kExpfBitmapWords, cudaMemcpyHostToDevice));
         ds.expf_n = (int)n;
         ds.ready = true;
     }
@@ -296,6 +306,7 @@ void base_params(TailParams &p, const DeviceState *ds) {
     p.expf_x = ds->d_expf_x;
     p.expf_y = ds->d_expf_y;
     p.expf_n = ds->expf_n;
+    p.expf_bits = ds->d_expf_bits;
 }
 
 int sample_launch(DropinState *S, DeviceState *ds, float *logits, int V, float temperature,
@@ -674,6 +685,7 @@ int lal_tail_sample_token_filtered(float *logits, int vocab_size, float temperat
     f.expf_x = ds->d_expf_x;
     f.expf_y = ds->d_expf_y;
     f.expf_n = ds->expf_n;
+    f.expf_bits = ds->d_expf_bits;
     f.phase = 0;
     CU(launch_finish(f, st));
     CU(cudaMemcpyAsync(&dg, S->ls.diag.p, sizeof(dg), cudaMemcpyDeviceToHost, st));
@@ -714,7 +726,7 @@ int lal_tail_debug_expf(const float *x, float *y, int n) {
     CHECK(S->logits.ensure(4ull * n));
     CU(cudaMemcpyAsync(S->x.p, x, 4ull * n, cudaMemcpyHostToDevice, st));
     CU(launch_debug_expf((const float *)S->x.p, (float *)S->logits.p, n, ds->d_expf_x,
-                         ds->d_expf_y, ds->expf_n, st));
+                         ds->d_expf_y, ds->expf_n, ds->d_expf_bits, st));
     CU(cudaMemcpyAsync(y, S->logits.p, 4ull * n, cudaMemcpyDeviceToHost, st));
     CU(cudaStreamSynchronize(st));
     return LAL_TAIL_OK;

@@ -21,6 +21,9 @@ constexpr int kMaxGrid = 256;
  * the boundary bin holds more than kRefineMax keys. */
 constexpr int kHistWords = 4096 + 1024 + 1024;
 constexpr int kRefineMax = 2048;
+/* words of the expf exception bitmap: bit (b >> 8) for b = bits(x) - 2^31,
+ * x from -0 down to -inf (0x7F800000 >> 8 buckets) */
+constexpr int kExpfBitmapWords = ((0x7F800000u >> 8) >> 5) + 1;
 /* Largest per-CTA row slice (smem holds its logits, scales, penalty counts). */
 constexpr int kMaxRowsPerCta = 4096;
 
@@ -82,15 +85,17 @@ struct TailParams {
     int *cand_idx_out;
     int cand_out_cap;
     int candidates_only;     /* stop after exporting candidates (no draw)     */
-    /* glibc expf fix-ups */
+    /* glibc expf fix-ups; expf_bits has one bit per 256 consecutive negative
+     * float bit patterns, set where the table holds an entry */
     const uint32_t *expf_x, *expf_y;
     int expf_n;
+    const uint32_t *expf_bits;
     /* optional globaltimer stamps: [cta*8 + i] per CTA (start, prologue done,
      * rows done, list written) and [grid*8 + i] for the merge */
     unsigned long long *phase_ts;
     /* shared-memory layout (bytes) */
     int stages, rows_per_stage, stage_bytes, area_bytes;
-    int off_bars, off_xq, off_sw, off_lg, off_cnt, off_misc, smem_total;
+    int off_bars, off_xq, off_sw, off_lg, off_cnt, off_hist, off_misc, smem_total;
     int rows_per_cta_max;
     int nch;                 /* 512-byte column chunks per row                */
     int max_k;               /* largest k a launch may use (planning)         */
@@ -114,6 +119,7 @@ struct FinishParams {
     int phase;
     const uint32_t *expf_x, *expf_y;
     int expf_n;
+    const uint32_t *expf_bits;
 };
 
 /* Host-side launchers (tail_kernels.cu). */
@@ -126,6 +132,7 @@ cudaError_t launch_abs_xq(const int8_t *xq, uint8_t *ax, int n, cudaStream_t st)
 cudaError_t launch_quantize_rows(const float *W, int d, int8_t *q, int ld,
                                  float *scale, int n_rows, cudaStream_t st);
 cudaError_t launch_debug_expf(const float *x, float *y, int n, const uint32_t *tx,
-                              const uint32_t *ty, int tn, cudaStream_t st);
+                              const uint32_t *ty, int tn, const uint32_t *bits,
+                              cudaStream_t st);
 
 }  // namespace lal

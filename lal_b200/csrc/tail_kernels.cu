@@ -116,6 +116,18 @@ __device__ __forceinline__ void st_release_gpu(unsigned *p, unsigned v) {
     asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
+/* The sampler's weight function: glibc-exact expf (lal_expf.h) with the
+ * fix-up table gated by a membership bitmap, so that nearly every call costs
+ * one bitmap load instead of a binary search over the table. */
+__device__ __forceinline__ float sampler_expf(float x, const uint32_t *tx, const uint32_t *ty,
+                                              int tn, const uint32_t *bits) {
+    const uint32_t xb = __float_as_uint(x);
+    if (!(xb & 0x80000000u) || !(x <= 0.0f)) return lal_expf_rounded(x);
+    const uint32_t b = (xb - 0x80000000u) >> 8;
+    if (!((__ldg(bits + (b >> 5)) >> (b & 31)) & 1u)) return lal_expf_rounded(x);
+    return lal_expf_glibc(x, tx, ty, tn);
+}
+
 /* ------------------------------------------------------- order keys --- */
 /* Monotone map float -> uint32 (larger float, larger key).  -0 maps like +0,
  * so key equality is float equality, as the reference's comparisons treat it. */
@@ -325,6 +337,7 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
     float *sw_s = reinterpret_cast<float *>(smem + p.off_sw);
     float *lg_s = reinterpret_cast<float *>(smem + p.off_lg);
     uint32_t *cnt_s = reinterpret_cast<uint32_t *>(smem + p.off_cnt);
+    uint32_t *hist_s = reinterpret_cast<uint32_t *>(smem + p.off_hist); /* 4096 bins */
     Misc *ms = reinterpret_cast<Misc *>(smem + p.off_misc);
 
     /* stream 0 sampling parameters */
@@ -359,24 +372,55 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
     if (warp < kConsumerWarps) {
         const int ctid = tid; /* 0 .. kConsumerWarps*32-1 */
         constexpr int NC = kConsumerWarps * 32;
+        /* every global load of the prologue is issued before any result is
+         * used: hidden values and history ids into registers, scales to smem */
+        constexpr int kHReg = 16;
+        const float *h = p.hidden;
+        float hv[kHReg];
+        int ids[kHReg];
         if (MODE == MODE_FUSED) {
-            /* lal_quantize_x_int8 (runtime/lal_q8_kernel.h:375-424), redundantly
-             * per CTA: absmax, scale = max/127 floored at 1e-8, inv = 1/scale,
-             * RNE for the first d&~7 elements and truncation for the tail. */
-            const float *h = p.hidden;
-            /* one batch of loads: up to kHReg values per thread in registers */
-            constexpr int kHReg = 16;
-            float hv[kHReg];
-            float m = 0.0f;
 #pragma unroll
             for (int j = 0; j < kHReg; ++j) {
                 const int i = ctid + j * NC;
                 hv[j] = i < p.d ? __ldg(h + i) : 0.0f;
             }
+        }
+        if (MODE != MODE_LMHEAD) {
+#pragma unroll
+            for (int j = 0; j < kHReg; ++j) {
+                const int i = ctid + j * NC;
+                ids[j] = (use_pen && i < hn) ? __ldg(p.hist_ids + i) : -1;
+            }
+        }
+        if (MODE != MODE_SAMPLE)
+#pragma unroll 4
+            for (int i = ctid; i < nloc; i += NC) sw_s[i] = __ldg(p.scale_w + c0 + i);
+        if (MODE != MODE_LMHEAD) {
+            for (int i = ctid; i < nloc; i += NC) cnt_s[i] = 0u;
+            for (int i = ctid; i < 4096; i += NC) hist_s[i] = 0u;
+        }
+        float m = 0.0f;
+        if (MODE == MODE_FUSED) {
 #pragma unroll
             for (int j = 0; j < kHReg; ++j) m = fmaxf(m, fabsf(hv[j]));
             for (int i = ctid + kHReg * NC; i < p.d; i += NC) m = fmaxf(m, fabsf(__ldg(h + i)));
-            m = consumer_max_f(m, ms);
+        }
+        m = consumer_max_f(m, ms); /* also orders the zeroing before the adds */
+        if (MODE != MODE_LMHEAD && use_pen) {
+            /* runtime/lal_sampling.h:60-66: ids outside [0, V) are skipped */
+            auto count = [&](int t) {
+                if (t < 0 || t >= p.vocab) return;
+                const int g = t - p.row_base;
+                if (g >= c0 && g < c1) atomicAdd(&cnt_s[g - c0], 1u);
+            };
+#pragma unroll
+            for (int j = 0; j < kHReg; ++j) count(ids[j]);
+            for (int i = ctid + kHReg * NC; i < hn; i += NC) count(__ldg(p.hist_ids + i));
+        }
+        if (MODE == MODE_FUSED) {
+            /* lal_quantize_x_int8 (runtime/lal_q8_kernel.h:375-424), redundantly
+             * per CTA: absmax, scale = max/127 floored at 1e-8, inv = 1/scale,
+             * RNE for the first d&~7 elements and truncation for the tail. */
             float scale = __fdiv_rn(m, 127.0f);
             if (scale < 1e-8f) scale = 1e-8f;
             const float inv = __fdiv_rn(1.0f, scale);
@@ -404,23 +448,6 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
         } else if (MODE == MODE_LMHEAD) {
             for (int i = ctid; i < p.ld; i += NC) xq_s[i] = i < p.d ? p.xq_in[i] : (int8_t)0;
             if (ctid == 0) ms->sx = p.scale_x_in;
-        }
-        if (MODE != MODE_SAMPLE)
-#pragma unroll 4
-            for (int i = ctid; i < nloc; i += NC) sw_s[i] = __ldg(p.scale_w + c0 + i);
-        if (MODE != MODE_LMHEAD) {
-            for (int i = ctid; i < nloc; i += NC) cnt_s[i] = 0u;
-            consumer_sync();
-            if (use_pen) {
-                /* runtime/lal_sampling.h:60-66: ids outside [0, V) are skipped */
-#pragma unroll 4
-                for (int i = ctid; i < hn; i += NC) {
-                    const int t = p.hist_ids[i];
-                    if (t < 0 || t >= p.vocab) continue;
-                    const int g = t - p.row_base;
-                    if (g >= c0 && g < c1) atomicAdd(&cnt_s[g - c0], 1u);
-                }
-            }
         }
         consumer_sync();
         if (ctid == 0) stamp(p, cta * 8 + 1);
@@ -502,6 +529,7 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
                         if (MODE == MODE_FUSED) {
                             l = penalise(l, cnt_s[lr], pen);
                             lg_s[lr] = l;
+                            atomicAdd(&hist_s[f2key(l) >> 20], 1u); /* level-0 bins */
                         }
                         p.logits[c0 + lr] = l;
                     }
@@ -526,6 +554,7 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
                 p.logits[c0 + i] = l; /* the reference mutates logits in place */
             }
             lg_s[i] = l;
+            atomicAdd(&hist_s[f2key(l) >> 20], 1u); /* level-0 bins */
         }
         __syncthreads();
     }
@@ -551,23 +580,28 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
         const int shift = level == 0 ? 20 : (level == 1 ? 10 : 0);
         const int nb = 1 << bits;
         unsigned *gh = p.ghist + (level == 0 ? 0 : (level == 1 ? 4096 : 5120));
-        for (int i = tid; i < nb; i += NT) lh[i] = 0u;
-        __syncthreads();
-        for (int i0 = 0; i0 < nloc; i0 += NT) {
-            const int i = i0 + tid;
-            const uint32_t key = i < nloc ? f2key(lg_s[i]) : 0u;
-            const bool m = i < nloc && (key & pmask) == prefix;
-            const uint32_t digit = (key >> shift) & (uint32_t)(nb - 1);
-            const unsigned voters = __ballot_sync(0xffffffffu, m);
-            if (m) {
-                const unsigned peers = __match_any_sync(voters, digit);
-                if ((int)(threadIdx.x & 31) == __ffs(peers) - 1)
-                    atomicAdd(&lh[digit], (uint32_t)__popc(peers));
+        /* this CTA's histogram: level 0 was accumulated as the logits were
+         * produced; deeper levels take a pass over the keys in the bin */
+        uint32_t *loc = level == 0 ? hist_s : lh;
+        if (level > 0) {
+            for (int i = tid; i < nb; i += NT) lh[i] = 0u;
+            __syncthreads();
+            for (int i0 = 0; i0 < nloc; i0 += NT) {
+                const int i = i0 + tid;
+                const uint32_t key = i < nloc ? f2key(lg_s[i]) : 0u;
+                const bool m = i < nloc && (key & pmask) == prefix;
+                const uint32_t digit = (key >> shift) & (uint32_t)(nb - 1);
+                const unsigned voters = __ballot_sync(0xffffffffu, m);
+                if (m) {
+                    const unsigned peers = __match_any_sync(voters, digit);
+                    if ((int)(threadIdx.x & 31) == __ffs(peers) - 1)
+                        atomicAdd(&lh[digit], (uint32_t)__popc(peers));
+                }
             }
         }
         __syncthreads();
         for (int i = tid; i < nb; i += NT) {
-            const uint32_t c = lh[i];
+            const uint32_t c = loc[i];
             if (c) atomicAdd(&gh[i], c);
         }
         ok = grid_sync(p.gbar, (unsigned)G, ms, p.status) && ok;
@@ -666,12 +700,29 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
             Si[i] = __ldcg(p.gcand_idx + i);
         }
         __syncthreads();
-        T = block_kth_largest(
-            [&](int i, uint32_t &key) {
-                key = Sk[i];
-                return true;
-            },
-            S, min(k, S), ms);
+        if (S <= 256) {
+            /* T = min{ key : #{keys > key} < k } -- one pass per element */
+            uint32_t best = 0xffffffffu;
+            for (int t = tid; t < S; t += NT) {
+                const uint32_t me = Sk[t];
+                int gt = 0;
+                for (int j = 0; j < S; ++j) gt += Sk[j] > me;
+                if (gt < k) best = min(best, me);
+            }
+            best = __reduce_min_sync(0xffffffffu, best);
+            if ((tid & 31) == 0) ms->scan[tid >> 5] = best;
+            __syncthreads();
+            T = ms->scan[0];
+            for (int w = 1; w < NWARP; ++w) T = min(T, ms->scan[w]);
+            __syncthreads();
+        } else {
+            T = block_kth_largest(
+                [&](int i, uint32_t &key) {
+                    key = Sk[i];
+                    return true;
+                },
+                S, min(k, S), ms);
+        }
         if (tid == 0) stamp(p, G * 8 + 1);
         /* candidates {v : l[v] >= T} (superset order) */
         const int seg = (S + NT - 1) / NT;
@@ -778,7 +829,7 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
         /* weights expf((l - max_l) / T) (runtime/lal_sampling.h:112) */
         for (int i = tid; i < m; i += NT) {
             const float x = __fdiv_rn(__fsub_rn(Ov[i], max_l), temp);
-            Ce[i] = lal_expf_glibc(x, p.expf_x, p.expf_y, p.expf_n);
+            Ce[i] = sampler_expf(x, p.expf_x, p.expf_y, p.expf_n, p.expf_bits);
         }
         __syncthreads();
         /* sequential float sum in ascending vocab order; keep the prefix */
@@ -926,9 +977,9 @@ __global__ void __launch_bounds__(NT) finish_kernel(const FinishParams f) {
             if (f.keep[i]) mx = fmaxf(mx, f.cand_val[i]);
         const float max_l = block_max_f(mx, &ms);
         for (int i = tid; i < f.m; i += NT)
-            f.prefix[i] = f.keep[i] ? lal_expf_glibc(__fdiv_rn(__fsub_rn(f.cand_val[i], max_l),
-                                                               f.temperature),
-                                                     f.expf_x, f.expf_y, f.expf_n)
+            f.prefix[i] = f.keep[i] ? sampler_expf(__fdiv_rn(__fsub_rn(f.cand_val[i], max_l),
+                                                             f.temperature),
+                                                   f.expf_x, f.expf_y, f.expf_n, f.expf_bits)
                                     : 0.0f;
         __syncthreads();
         if (tid == 0) {
@@ -970,9 +1021,9 @@ __global__ void __launch_bounds__(NT) finish_kernel(const FinishParams f) {
 }
 
 __global__ void debug_expf_kernel(const float *x, float *y, int n, const uint32_t *tx,
-                                  const uint32_t *ty, int tn) {
+                                  const uint32_t *ty, int tn, const uint32_t *bits) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < n) y[i] = lal_expf_glibc(x[i], tx, ty, tn);
+    if (i < n) y[i] = sampler_expf(x[i], tx, ty, tn, bits);
 }
 
 /* -------------------------------------------------- host planning --- */
@@ -1016,7 +1067,8 @@ int plan_launch(TailParams &p, int num_sms, int min_rows_per_cta) {
     if (p.nch < 0) return -3;
     const int rpc = align_up(p.rows_per_cta_max, 4);
     int off = 0;
-    const int fixed = 16 * kMaxStages + align_up(p.ld, 16) + 3 * 4 * rpc +
+    const int hist_bytes = p.mode == MODE_LMHEAD ? 0 : 4 * 4096;
+    const int fixed = 16 * kMaxStages + align_up(p.ld, 16) + 3 * 4 * rpc + hist_bytes +
                       align_up((int)sizeof(Misc), 128) + 3 * 128;
     const int budget = (kSmemLimit - fixed) / 128 * 128;
     if (p.mode == MODE_SAMPLE) {
@@ -1053,6 +1105,8 @@ int plan_launch(TailParams &p, int num_sms, int min_rows_per_cta) {
     p.off_cnt = off;
     off += 4 * rpc;
     off = align_up(off, 128);
+    p.off_hist = off;
+    off += hist_bytes;
     p.off_misc = off;
     off += (int)sizeof(Misc);
     p.smem_total = align_up(off, 128);
@@ -1111,8 +1165,9 @@ cudaError_t launch_finish(const FinishParams &f, cudaStream_t st) {
 }
 
 cudaError_t launch_debug_expf(const float *x, float *y, int n, const uint32_t *tx,
-                              const uint32_t *ty, int tn, cudaStream_t st) {
-    debug_expf_kernel<<<(n + 255) / 256, 256, 0, st>>>(x, y, n, tx, ty, tn);
+                              const uint32_t *ty, int tn, const uint32_t *bits,
+                              cudaStream_t st) {
+    debug_expf_kernel<<<(n + 255) / 256, 256, 0, st>>>(x, y, n, tx, ty, tn, bits);
     return cudaGetLastError();
 }
 
