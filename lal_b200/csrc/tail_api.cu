@@ -160,7 +160,8 @@ struct PinBuf {
 /* Scratch of the select (global memory beyond inputs and outputs): the key
  * histogram, grid-barrier words, superset buffer, arrival ticket. */
 struct SelectScratch {
-    unsigned *ghist = nullptr, *gbar = nullptr, *gcount = nullptr, *counter = nullptr;
+    unsigned *ghist = nullptr, *gbar = nullptr, *gcount = nullptr, *counter = nullptr,
+             *gL = nullptr;
     uint32_t *gkey = nullptr;
     int *gidx = nullptr;
     int cap = 0;
@@ -169,6 +170,7 @@ struct SelectScratch {
         gbar = ghist + kHistWords;
         gcount = gbar + 2;
         counter = gbar + 3;
+        gL = gbar + 4;
         CU(cudaMemset(ghist, 0, 4ull * (kHistWords + 8)));
         cap = std::max(cap_, 1);
         CU(cudaMalloc(&gkey, 4ull * cap));
@@ -184,7 +186,7 @@ struct SelectScratch {
         if (ghist) cudaFree(ghist);
         if (gkey) cudaFree(gkey);
         if (gidx) cudaFree(gidx);
-        ghist = gbar = gcount = counter = nullptr;
+        ghist = gbar = gcount = counter = gL = nullptr;
         gkey = nullptr;
         gidx = nullptr;
     }
@@ -192,6 +194,7 @@ struct SelectScratch {
         p.ghist = ghist;
         p.gbar = gbar;
         p.gcount = gcount;
+        p.gL = gL;
         p.counter = counter;
         p.gcand_key = gkey;
         p.gcand_idx = gidx;

@@ -75,6 +75,7 @@ struct TailParams {
     unsigned *ghist;         /* [kHistWords] global key histogram             */
     unsigned *gbar;          /* [2] grid barrier: arrivals, generation        */
     unsigned *gcount;        /* [1] superset entries appended                 */
+    unsigned *gL;            /* [1] largest per-CTA boundary edge (small k)   */
     uint32_t *gcand_key;     /* [gcand_cap] superset {key >= boundary}        */
     int *gcand_idx;          /* [gcand_cap] their vocab indices               */
     int gcand_cap;

@@ -251,6 +251,40 @@ __device__ __forceinline__ float block_max_f(float v, Misc *ms) {
     return r;
 }
 
+/* Boundary bin of a histogram h[0..nb) scanned from the top bin down: the bin
+ * holding the krem-th largest entry (1 <= krem <= total).  Returns the bin;
+ * *above gets the count in higher bins, *count the bin's own count.  All
+ * threads of the block call it. */
+__device__ uint32_t boundary_bin(const uint32_t *h, int nb, uint32_t krem, Misc *ms,
+                                 uint32_t *above, uint32_t *count) {
+    const int per = (nb + NT - 1) / NT;
+    const int q0 = threadIdx.x * per; /* descending positions q <-> bin nb-1-q */
+    const int q1 = min(nb, q0 + per);
+    uint32_t s = 0;
+    for (int q = q0; q < q1; ++q) s += h[nb - 1 - q];
+    uint32_t tot;
+    const uint32_t ex = block_scan_excl(s, ms, &tot);
+    if (ex < krem && krem <= ex + s) {
+        uint32_t run = ex;
+        for (int q = q0; q < q1; ++q) {
+            const uint32_t c = h[nb - 1 - q];
+            if (run + c >= krem) {
+                ms->sh[0] = (uint32_t)(nb - 1 - q);
+                ms->sh[1] = run;
+                ms->sh[2] = c;
+                break;
+            }
+            run += c;
+        }
+    }
+    __syncthreads();
+    const uint32_t bin = ms->sh[0];
+    *above = ms->sh[1];
+    *count = ms->sh[2];
+    __syncthreads();
+    return bin;
+}
+
 /* k-th largest key of the valid entries among i in [0, n): get(i, key)
  * returns whether entry i takes part and sets its key; 1 <= k <= the number
  * of valid entries.  MSB-first radix select with 8-bit digits; histogram adds
@@ -341,13 +375,16 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
     Misc *ms = reinterpret_cast<Misc *>(smem + p.off_misc);
 
     /* stream 0 sampling parameters */
-    float temp = 0.0f, pen = 1.0f;
-    int topk = 0, hn = 0;
+    float temp = 0.0f, pen = 1.0f, u0 = 0.0f;
+    int topk = 0, hn = 0, hhead = 0;
     if (MODE != MODE_LMHEAD) {
+        /* read early (every CTA): the last CTA uses u0 and the ring words */
         temp = p.temperature[0];
         topk = p.top_k[0];
         pen = p.rep_penalty[0];
         hn = p.hist_n ? p.hist_n[0] : 0;
+        hhead = p.hist_head ? p.hist_head[0] : 0;
+        u0 = p.u[0];
     }
     const bool greedy = (temp <= 0.0f) || (topk <= 0);
     const bool use_pen = (MODE != MODE_LMHEAD) && (pen > 1.0f) && hn > 0 &&
@@ -575,7 +612,21 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
     uint32_t prefix = 0u, pmask = 0u;
     int above = 0, binc = 0;
     bool ok = ms->abort_flag == 0;
-    for (int level = 0; level < 3; ++level) {
+    /* Small k against the slice (the common case): no grid barrier.  Each
+     * CTA's own boundary bin (from its level-0 histogram) has a lower edge
+     * below its local k-th largest, hence below the global T; the union of
+     * every CTA's keys >= its own edge contains {l >= T}, and the largest
+     * edge L is a lower bound of T that the last CTA filters with.  Large k
+     * (k comparable to a slice) takes the global histogram below. */
+    const bool local_edges = 4 * k <= p.rows_per_cta_max;
+    if (local_edges) {
+        /* (a CTA with fewer than k rows would give no bound: it keeps all) */
+        uint32_t ab, cnt;
+        const uint32_t bin = boundary_bin(hist_s, 4096, (uint32_t)min(k, nloc), ms, &ab, &cnt);
+        prefix = nloc >= k ? bin << 20 : 0u;
+        if (tid == 0 && nloc >= k) atomicMax(p.gL, prefix);
+    }
+    for (int level = 0; level < 3 && !local_edges; ++level) {
         const int bits = level == 0 ? 12 : 10;
         const int shift = level == 0 ? 20 : (level == 1 ? 10 : 0);
         const int nb = 1 << bits;
@@ -609,36 +660,16 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
         /* boundary bin, from the top: every CTA reads the same histogram */
         for (int i = tid; i < nb; i += NT) lh[i] = __ldcg(gh + i);
         __syncthreads();
-        const int per = (nb + NT - 1) / NT;
-        const int q0 = tid * per; /* descending positions q <-> bin nb-1-q */
-        uint32_t s = 0;
-        for (int q = q0; q < min(nb, q0 + per); ++q) s += lh[nb - 1 - q];
-        uint32_t tot;
-        const uint32_t ex = block_scan_excl(s, ms, &tot);
-        const uint32_t krem = (uint32_t)(k - above);
-        if (ex < krem && krem <= ex + s) {
-            uint32_t run = ex;
-            for (int q = q0; q < min(nb, q0 + per); ++q) {
-                const uint32_t c = lh[nb - 1 - q];
-                if (run + c >= krem) {
-                    ms->sh[0] = (uint32_t)(nb - 1 - q);
-                    ms->sh[1] = run;
-                    ms->sh[2] = c;
-                    break;
-                }
-                run += c;
-            }
-        }
-        __syncthreads();
-        above += (int)ms->sh[1];
-        binc = (int)ms->sh[2];
-        prefix |= ms->sh[0] << shift;
+        uint32_t ab, cnt;
+        const uint32_t bin = boundary_bin(lh, nb, (uint32_t)(k - above), ms, &ab, &cnt);
+        above += (int)ab;
+        binc = (int)cnt;
+        prefix |= bin << shift;
         pmask |= (uint32_t)(nb - 1) << shift;
-        __syncthreads();
         if (binc <= kRefineMax) break;
     }
-    const uint32_t Lb = prefix; /* lower edge of the boundary bin */
-    const int S = above + binc; /* keys >= Lb over all CTAs */
+    const uint32_t Lb = prefix; /* lower edge of this CTA's (or the global) bin */
+    const int S_hist = above + binc; /* global histogram: keys >= Lb, all CTAs */
 
     /* append this CTA's keys >= Lb */
     {
@@ -693,13 +724,38 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
     const int Sg = (int)__ldcg(p.gcount);
     int m = 0;
     uint32_t T = 0u;
-    bool fine = ok && dev_status == 0 && Sg == S && S <= s_cap && S <= p.gcand_cap && S >= 1;
+    bool fine = ok && dev_status == 0 && Sg <= p.gcand_cap && Sg >= 1;
+    int S = S_hist;
+    if (fine && local_edges) {
+        /* keep the appended keys >= L = the largest CTA edge, in order */
+        const uint32_t L = __ldcg(p.gL);
+        const int seg = (Sg + NT - 1) / NT;
+        const int e0 = min(Sg, tid * seg), e1 = min(Sg, e0 + seg);
+        uint32_t c = 0;
+        for (int e = e0; e < e1; ++e) c += __ldcg(p.gcand_key + e) >= L;
+        uint32_t tot;
+        uint32_t pos = block_scan_excl(c, ms, &tot);
+        S = (int)tot;
+        if (S <= s_cap)
+            for (int e = e0; e < e1; ++e) {
+                const uint32_t key = __ldcg(p.gcand_key + e);
+                if (key >= L) {
+                    Sk[pos] = key;
+                    Si[pos] = __ldcg(p.gcand_idx + e);
+                    ++pos;
+                }
+            }
+        fine = S >= 1 && S <= s_cap;
+    } else if (fine) {
+        fine = Sg == S && S <= s_cap;
+        if (fine)
+            for (int i = tid; i < S; i += NT) {
+                Sk[i] = __ldcg(p.gcand_key + i);
+                Si[i] = __ldcg(p.gcand_idx + i);
+            }
+    }
+    __syncthreads();
     if (fine) {
-        for (int i = tid; i < S; i += NT) {
-            Sk[i] = __ldcg(p.gcand_key + i);
-            Si[i] = __ldcg(p.gcand_idx + i);
-        }
-        __syncthreads();
         if (S <= 256) {
             /* T = min{ key : #{keys > key} < k } -- one pass per element */
             uint32_t best = 0xffffffffu;
@@ -754,9 +810,11 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
     dg.token = -1;
 
     /* leave the scratch clean for the next launch */
-    for (int i = tid; i < kHistWords; i += NT) p.ghist[i] = 0u;
+    if (!local_edges)
+        for (int i = tid; i < kHistWords; i += NT) p.ghist[i] = 0u;
     if (tid == 0) {
         *p.gcount = 0u;
+        *p.gL = 0u;
         p.counter[0] = 0u;
     }
     if (!fine) {
@@ -859,7 +917,7 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
         } else {
             /* r = u * sum; first candidate with r <= running sum
              * (runtime/lal_sampling.h:116-124) */
-            const float r = __fmul_rn(p.u[0], sum);
+            const float r = __fmul_rn(u0, sum);
             dg.r = r;
             dg.drew = 1;
             int first = 0x7fffffff;
@@ -879,12 +937,12 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
         p.diag[0] = dg;
         if (p.push_history && p.hist_cap > 0) {
             /* runtime/lal_sampling.h:133-136 as a ring: FIFO at hist_cap */
-            const int n = p.hist_n[0];
+            const int n = hn;
             if (n < p.hist_cap) {
                 p.hist_ids[n] = token;
                 p.hist_n[0] = n + 1;
             } else {
-                const int h = p.hist_head[0];
+                const int h = hhead;
                 p.hist_ids[h] = token;
                 p.hist_head[0] = (h + 1) % p.hist_cap;
             }
