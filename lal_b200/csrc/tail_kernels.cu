@@ -727,28 +727,43 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
     bool fine = ok && dev_status == 0 && Sg <= p.gcand_cap && Sg >= 1;
     int S = S_hist;
     if (fine && local_edges) {
-        /* keep the appended keys >= L = the largest CTA edge, in order */
+        /* keep the appended keys >= L = the largest CTA edge: stage all keys
+         * in shared memory with batched loads, filter there (positions kept
+         * in Oi), then fetch the indices of the survivors only */
         const uint32_t L = __ldcg(p.gL);
-        const int seg = (Sg + NT - 1) / NT;
-        const int e0 = min(Sg, tid * seg), e1 = min(Sg, e0 + seg);
-        uint32_t c = 0;
-        for (int e = e0; e < e1; ++e) c += __ldcg(p.gcand_key + e) >= L;
-        uint32_t tot;
-        uint32_t pos = block_scan_excl(c, ms, &tot);
-        S = (int)tot;
-        if (S <= s_cap)
-            for (int e = e0; e < e1; ++e) {
-                const uint32_t key = __ldcg(p.gcand_key + e);
-                if (key >= L) {
-                    Sk[pos] = key;
-                    Si[pos] = __ldcg(p.gcand_idx + e);
-                    ++pos;
-                }
+        fine = Sg <= s_cap;
+        if (fine) {
+#pragma unroll 8
+            for (int e = tid; e < Sg; e += NT) Sk[e] = __ldcg(p.gcand_key + e);
+        }
+        __syncthreads();
+        if (fine) {
+            const int seg = (Sg + NT - 1) / NT;
+            const int e0 = min(Sg, tid * seg), e1 = min(Sg, e0 + seg);
+            uint32_t c = 0;
+            for (int e = e0; e < e1; ++e) c += Sk[e] >= L;
+            uint32_t tot;
+            uint32_t pos = block_scan_excl(c, ms, &tot);
+            S = (int)tot;
+            if (S <= ccap)
+                for (int e = e0; e < e1; ++e)
+                    if (Sk[e] >= L) Oi[pos++] = e;
+            fine = S >= 1 && S <= ccap;
+        }
+        __syncthreads();
+        if (fine) {
+            for (int j = tid; j < S; j += NT) {
+                const int e = Oi[j];
+                Ci[j] = (int)Sk[e];
+                Si[j] = __ldcg(p.gcand_idx + e);
             }
-        fine = S >= 1 && S <= s_cap;
+            __syncthreads();
+            for (int j = tid; j < S; j += NT) Sk[j] = (uint32_t)Ci[j];
+        }
     } else if (fine) {
         fine = Sg == S && S <= s_cap;
         if (fine)
+#pragma unroll 4
             for (int i = tid; i < S; i += NT) {
                 Sk[i] = __ldcg(p.gcand_key + i);
                 Si[i] = __ldcg(p.gcand_idx + i);
