@@ -731,34 +731,34 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
          * in shared memory with batched loads, filter there (positions kept
          * in Oi), then fetch the indices of the survivors only */
         const uint32_t L = __ldcg(p.gL);
-        fine = Sg <= s_cap;
-        if (fine) {
+        S = 0;
+        for (int base = 0; base < Sg; base += s_cap) { /* chunks of s_cap keys */
+            const int n = min(s_cap, Sg - base);
 #pragma unroll 8
-            for (int e = tid; e < Sg; e += NT) Sk[e] = __ldcg(p.gcand_key + e);
-        }
-        __syncthreads();
-        if (fine) {
-            const int seg = (Sg + NT - 1) / NT;
-            const int e0 = min(Sg, tid * seg), e1 = min(Sg, e0 + seg);
+            for (int e = tid; e < n; e += NT) Sk[e] = __ldcg(p.gcand_key + base + e);
+            __syncthreads();
+            const int seg = (n + NT - 1) / NT;
+            const int e0 = min(n, tid * seg), e1 = min(n, e0 + seg);
             uint32_t c = 0;
             for (int e = e0; e < e1; ++e) c += Sk[e] >= L;
             uint32_t tot;
-            uint32_t pos = block_scan_excl(c, ms, &tot);
-            S = (int)tot;
-            if (S <= ccap)
+            uint32_t pos = block_scan_excl(c, ms, &tot) + (uint32_t)S;
+            if (S + (int)tot <= ccap)
                 for (int e = e0; e < e1; ++e)
-                    if (Sk[e] >= L) Oi[pos++] = e;
-            fine = S >= 1 && S <= ccap;
+                    if (Sk[e] >= L) {
+                        Oi[pos] = base + e;
+                        Ci[pos] = (int)Sk[e];
+                        ++pos;
+                    }
+            S += (int)tot;
+            __syncthreads();
         }
-        __syncthreads();
+        fine = S >= 1 && S <= ccap;
         if (fine) {
             for (int j = tid; j < S; j += NT) {
-                const int e = Oi[j];
-                Ci[j] = (int)Sk[e];
-                Si[j] = __ldcg(p.gcand_idx + e);
+                Sk[j] = (uint32_t)Ci[j];
+                Si[j] = __ldcg(p.gcand_idx + Oi[j]);
             }
-            __syncthreads();
-            for (int j = tid; j < S; j += NT) Sk[j] = (uint32_t)Ci[j];
         }
     } else if (fine) {
         fine = Sg == S && S <= s_cap;
