@@ -161,17 +161,18 @@ struct PinBuf {
  * histogram, grid-barrier words, superset buffer, arrival ticket. */
 struct SelectScratch {
     unsigned *ghist = nullptr, *gbar = nullptr, *gcount = nullptr, *counter = nullptr,
-             *gL = nullptr;
+             *gL = nullptr, *gmax = nullptr;
     uint32_t *gkey = nullptr;
     int *gidx = nullptr;
     int cap = 0;
     int alloc(int cap_) {
-        CU(cudaMalloc(&ghist, 4ull * (kHistWords + 8)));
+        CU(cudaMalloc(&ghist, 4ull * (kHistWords + 8 + kMaxGrid)));
         gbar = ghist + kHistWords;
         gcount = gbar + 2;
         counter = gbar + 3;
         gL = gbar + 4;
-        CU(cudaMemset(ghist, 0, 4ull * (kHistWords + 8)));
+        gmax = gbar + 8;
+        CU(cudaMemset(ghist, 0, 4ull * (kHistWords + 8 + kMaxGrid)));
         cap = std::max(cap_, 1);
         CU(cudaMalloc(&gkey, 4ull * cap));
         CU(cudaMalloc(&gidx, 4ull * cap));
@@ -179,14 +180,14 @@ struct SelectScratch {
     }
     /* after a device error the words may be mid-update: start clean */
     int reset(cudaStream_t st) {
-        CU(cudaMemsetAsync(ghist, 0, 4ull * (kHistWords + 8), st));
+        CU(cudaMemsetAsync(ghist, 0, 4ull * (kHistWords + 8 + kMaxGrid), st));
         return LAL_TAIL_OK;
     }
     void free_all() {
         if (ghist) cudaFree(ghist);
         if (gkey) cudaFree(gkey);
         if (gidx) cudaFree(gidx);
-        ghist = gbar = gcount = counter = gL = nullptr;
+        ghist = gbar = gcount = counter = gL = gmax = nullptr;
         gkey = nullptr;
         gidx = nullptr;
     }
@@ -195,6 +196,7 @@ struct SelectScratch {
         p.gbar = gbar;
         p.gcount = gcount;
         p.gL = gL;
+        p.gmax = gmax;
         p.counter = counter;
         p.gcand_key = gkey;
         p.gcand_idx = gidx;

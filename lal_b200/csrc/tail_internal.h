@@ -76,6 +76,7 @@ struct TailParams {
     unsigned *gbar;          /* [2] grid barrier: arrivals, generation        */
     unsigned *gcount;        /* [1] superset entries appended                 */
     unsigned *gL;            /* [1] largest per-CTA boundary edge (small k)   */
+    unsigned *gmax;          /* [kMaxGrid] each CTA's largest key (small k)   */
     uint32_t *gcand_key;     /* [gcand_cap] superset {key >= boundary}        */
     int *gcand_idx;          /* [gcand_cap] their vocab indices               */
     int gcand_cap;

@@ -151,6 +151,7 @@ struct Misc {
     int abort_flag;
     int ticket;
     int found;
+    uint32_t gm[kMaxGrid]; /* the last CTA's copy of the per-CTA maxima */
 };
 
 /* Grid-wide barrier of a cooperative launch (every CTA resident).  The
@@ -625,6 +626,19 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
         const uint32_t bin = boundary_bin(hist_s, 4096, (uint32_t)min(k, nloc), ms, &ab, &cnt);
         prefix = nloc >= k ? bin << 20 : 0u;
         if (tid == 0 && nloc >= k) atomicMax(p.gL, prefix);
+        /* this CTA's largest key: the k-th largest of the CTAs' maxima is a
+         * second lower bound of T (distinct elements), usually much tighter */
+        uint32_t mk = 0u;
+        for (int i = tid; i < nloc; i += NT) mk = max(mk, f2key(lg_s[i]));
+        mk = __reduce_max_sync(0xffffffffu, mk);
+        if ((tid & 31) == 0) ms->scan[tid >> 5] = mk;
+        __syncthreads();
+        if (tid == 0) {
+            uint32_t r = ms->scan[0];
+            for (int w = 1; w < NWARP; ++w) r = max(r, ms->scan[w]);
+            p.gmax[cta] = r;
+        }
+        __syncthreads();
     }
     for (int level = 0; level < 3 && !local_edges; ++level) {
         const int bits = level == 0 ? 12 : 10;
@@ -730,7 +744,26 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
         /* keep the appended keys >= L = the largest CTA edge: stage all keys
          * in shared memory with batched loads, filter there (positions kept
          * in Oi), then fetch the indices of the survivors only */
-        const uint32_t L = __ldcg(p.gL);
+        uint32_t L = __ldcg(p.gL);
+        if (k <= G) {
+            /* L2 = k-th largest of the G per-CTA maxima <= T */
+            for (int g = tid; g < G; g += NT) ms->gm[g] = __ldcg(p.gmax + g);
+            __syncthreads();
+            uint32_t best = 0xffffffffu;
+            for (int g = tid; g < G; g += NT) {
+                const uint32_t me = ms->gm[g];
+                int gt = 0;
+                for (int j = 0; j < G; ++j) gt += ms->gm[j] > me;
+                if (gt < k) best = min(best, me);
+            }
+            best = __reduce_min_sync(0xffffffffu, best);
+            if ((tid & 31) == 0) ms->scan[tid >> 5] = best;
+            __syncthreads();
+            uint32_t L2 = ms->scan[0];
+            for (int w = 1; w < NWARP; ++w) L2 = min(L2, ms->scan[w]);
+            L = max(L, L2);
+            __syncthreads();
+        }
         S = 0;
         for (int base = 0; base < Sg; base += s_cap) { /* chunks of s_cap keys */
             const int n = min(s_cap, Sg - base);
