@@ -324,7 +324,7 @@ class DecodeTail:
         _check(lib().lal_tail_debug_phases(self.h, 1 if on else 0))
 
     def phase_times(self):
-        """(per-CTA stamps [grid, 8], last-CTA stamps [4]) in ns, relative to
+        """(per-CTA stamps [grid, 8], last-CTA stamps [8]) in ns, relative to
         the earliest CTA start, of the last launch (0 where not written)."""
         g = C.c_int()
         _check(lib().lal_tail_debug_phase_read(self.h, None, 0, C.byref(g)))
@@ -333,7 +333,7 @@ class DecodeTail:
         st = out.reshape(g.value + 1, 8).astype(np.int64)
         t0 = st[:-1, 0].min()
         rel = np.where(st > 0, st - t0, 0)
-        return rel[:-1], rel[-1, :4]
+        return rel[:-1], rel[-1]
 
     def stream(self) -> int:
         s = C.c_void_p()

@@ -373,6 +373,7 @@ int sample_launch(DropinState *S, DeviceState *ds, float *logits, int V, float t
     p.cand_idx_out = (int *)S->ls.cand_i.p;
     p.cand_out_cap = V;
     p.candidates_only = candidates_only ? 1 : 0;
+    p.local_edges = use_local_edges(effective_k(temperature, top_k, V, V), p.rows_per_cta_max);
     CU(launch_tail(p, grid, st));
     int status = 0;
     StreamDiag dg;
@@ -874,6 +875,8 @@ int enqueue_step(lal_tail *t, const float *d_hidden, int n, const float *d_u, in
         t->sel.fill(p);
         p.status = t->io_out + t->cfg.max_streams;
         p.phase_ts = t->phases ? t->phase_ts : nullptr;
+        p.local_edges = use_local_edges(
+            effective_k(t->h_temp[b], t->h_topk[b], t->cfg.vocab_size, t->nrows), p.rows_per_cta_max);
         const bool time_it = t->timing && t->ev_used + 2 <= (int)t->ev.size();
         if (time_it) CU(cudaEventRecord(t->ev[t->ev_used], t->stream));
         CU(launch_tail(p, t->grid, t->stream));

@@ -101,6 +101,9 @@ struct TailParams {
     int rows_per_cta_max;
     int nch;                 /* 512-byte column chunks per row                */
     int max_k;               /* largest k a launch may use (planning)         */
+    int local_edges;         /* select strategy (use_local_edges); 0 = grid
+                              * histogram with grid barriers, which needs a
+                              * cooperative launch                            */
 };
 
 /* Second half of the server sampler with a level-2 filter
@@ -123,6 +126,17 @@ struct FinishParams {
     int expf_n;
     const uint32_t *expf_bits;
 };
+
+/* The select strategy of a launch whose effective k (greedy: 1; else
+ * min(top_k, V, rows)) is k: per-CTA histogram edges (no grid barrier) when k
+ * is small against a CTA's slice, else the grid-wide histogram. */
+inline int use_local_edges(int k, int rows_per_cta_max) { return 4 * k <= rows_per_cta_max; }
+inline int effective_k(float temperature, int top_k, int vocab, int rows) {
+    int k = (temperature <= 0.0f || top_k <= 0) ? 1 : top_k;
+    if (k > vocab) k = vocab;
+    if (k > rows) k = rows;
+    return k < 1 ? 1 : k;
+}
 
 /* Host-side launchers (tail_kernels.cu). */
 cudaError_t launch_finish(const FinishParams &f, cudaStream_t st);

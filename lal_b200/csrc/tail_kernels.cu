@@ -619,7 +619,7 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
      * every CTA's keys >= its own edge contains {l >= T}, and the largest
      * edge L is a lower bound of T that the last CTA filters with.  Large k
      * (k comparable to a slice) takes the global histogram below. */
-    const bool local_edges = 4 * k <= p.rows_per_cta_max;
+    const bool local_edges = p.local_edges != 0; /* = use_local_edges(k, ...) */
     if (local_edges) {
         /* (a CTA with fewer than k rows would give no bound: it keeps all) */
         uint32_t ab, cnt;
@@ -764,6 +764,7 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
             L = max(L, L2);
             __syncthreads();
         }
+        if (tid == 0) stamp(p, G * 8 + 1);
         S = 0;
         for (int base = 0; base < Sg; base += s_cap) { /* chunks of s_cap keys */
             const int n = min(s_cap, Sg - base);
@@ -787,6 +788,7 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
             __syncthreads();
         }
         fine = S >= 1 && S <= ccap;
+        if (tid == 0) stamp(p, G * 8 + 2);
         if (fine) {
             for (int j = tid; j < S; j += NT) {
                 Sk[j] = (uint32_t)Ci[j];
@@ -827,7 +829,7 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
                 },
                 S, min(k, S), ms);
         }
-        if (tid == 0) stamp(p, G * 8 + 1);
+        if (tid == 0) stamp(p, G * 8 + 3);
         /* candidates {v : l[v] >= T} (superset order) */
         const int seg = (S + NT - 1) / NT;
         const int e0 = min(S, tid * seg), e1 = min(S, e0 + seg);
@@ -910,7 +912,7 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
             }
     }
     __syncthreads();
-    if (tid == 0) stamp(p, G * 8 + 2);
+    if (tid == 0) stamp(p, G * 8 + 4);
 
     if (p.cand_val_out != nullptr && m <= p.cand_out_cap) {
         for (int i = tid; i < m; i += NT) {
@@ -927,6 +929,7 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
     float mx = -1e30f;
     for (int i = tid; i < m; i += NT) mx = fmaxf(mx, Ov[i]);
     const float max_l = block_max_f(mx, ms);
+    if (tid == 0) stamp(p, G * 8 + 5);
     dg.max_l = max_l;
     int token;
     if (greedy) {
@@ -950,6 +953,7 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
         }
         __syncthreads();
         const float sum = ms->sum;
+        if (tid == 0) stamp(p, G * 8 + 6);
         dg.sum = sum;
         if (p.variant == VARIANT_SERVER && sum <= 0.0f) {
             /* tools/server/qwen7b_server.c:285-286: argmax over the kept
@@ -995,7 +999,7 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
                 p.hist_head[0] = (h + 1) % p.hist_cap;
             }
         }
-        stamp(p, G * 8 + 3);
+        stamp(p, G * 8 + 7);
     }
 }
 
@@ -1241,7 +1245,7 @@ cudaError_t launch_tail(const TailParams &p, int grid, cudaStream_t st) {
     void *args[] = {const_cast<TailParams *>(&p)};
     /* The select's grid barriers need every CTA resident: a cooperative
      * launch guarantees it (or fails to launch). */
-    if (p.mode == MODE_LMHEAD)
+    if (p.mode == MODE_LMHEAD || p.local_edges)
         return cudaLaunchKernel(fn, dim3(grid), dim3(NT), args, (size_t)p.smem_total, st);
     return cudaLaunchCooperativeKernel(fn, dim3(grid), dim3(NT), args, (size_t)p.smem_total, st);
 }
