@@ -161,33 +161,36 @@ struct PinBuf {
  * histogram, grid-barrier words, superset buffer, arrival ticket. */
 struct SelectScratch {
     unsigned *ghist = nullptr, *gbar = nullptr, *gcount = nullptr, *counter = nullptr,
-             *gL = nullptr, *gmax = nullptr;
+             *gL = nullptr, *gmax = nullptr, *gslot_n = nullptr;
     uint32_t *gkey = nullptr;
     int *gidx = nullptr;
     int cap = 0;
+    static constexpr size_t kWords = kHistWords + 8 + 2 * kMaxGrid;
     int alloc(int cap_) {
-        CU(cudaMalloc(&ghist, 4ull * (kHistWords + 8 + kMaxGrid)));
+        CU(cudaMalloc(&ghist, 4ull * kWords));
         gbar = ghist + kHistWords;
         gcount = gbar + 2;
         counter = gbar + 3;
         gL = gbar + 4;
         gmax = gbar + 8;
-        CU(cudaMemset(ghist, 0, 4ull * (kHistWords + 8 + kMaxGrid)));
-        cap = std::max(cap_, 1);
+        gslot_n = gmax + kMaxGrid;
+        CU(cudaMemset(ghist, 0, 4ull * kWords));
+        /* the small-k path uses one slot of kSlot entries per CTA */
+        cap = std::max(cap_, kMaxGrid * kSlot);
         CU(cudaMalloc(&gkey, 4ull * cap));
         CU(cudaMalloc(&gidx, 4ull * cap));
         return LAL_TAIL_OK;
     }
     /* after a device error the words may be mid-update: start clean */
     int reset(cudaStream_t st) {
-        CU(cudaMemsetAsync(ghist, 0, 4ull * (kHistWords + 8 + kMaxGrid), st));
+        CU(cudaMemsetAsync(ghist, 0, 4ull * kWords, st));
         return LAL_TAIL_OK;
     }
     void free_all() {
         if (ghist) cudaFree(ghist);
         if (gkey) cudaFree(gkey);
         if (gidx) cudaFree(gidx);
-        ghist = gbar = gcount = counter = gL = gmax = nullptr;
+        ghist = gbar = gcount = counter = gL = gmax = gslot_n = nullptr;
         gkey = nullptr;
         gidx = nullptr;
     }
@@ -197,6 +200,7 @@ struct SelectScratch {
         p.gcount = gcount;
         p.gL = gL;
         p.gmax = gmax;
+        p.gslot_n = gslot_n;
         p.counter = counter;
         p.gcand_key = gkey;
         p.gcand_idx = gidx;

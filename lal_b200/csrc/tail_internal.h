@@ -21,6 +21,10 @@ constexpr int kMaxGrid = 256;
  * the boundary bin holds more than kRefineMax keys. */
 constexpr int kHistWords = 4096 + 1024 + 1024;
 constexpr int kRefineMax = 2048;
+/* Small-k select: per-CTA slot of the sorted local superset; the strategy is
+ * used only for k <= kLocalMaxK (and 4k <= the rows of a CTA). */
+constexpr int kSlot = 128;
+constexpr int kLocalMaxK = 64;
 /* words of the expf exception bitmap: bit (b >> 8) for b = bits(x) - 2^31,
  * x from -0 down to -inf (0x7F800000 >> 8 buckets) */
 constexpr int kExpfBitmapWords = ((0x7F800000u >> 8) >> 5) + 1;
@@ -77,6 +81,7 @@ struct TailParams {
     unsigned *gcount;        /* [1] superset entries appended                 */
     unsigned *gL;            /* [1] largest per-CTA boundary edge (small k)   */
     unsigned *gmax;          /* [kMaxGrid] each CTA's largest key (small k)   */
+    unsigned *gslot_n;       /* [kMaxGrid] each CTA's slot count (small k)    */
     uint32_t *gcand_key;     /* [gcand_cap] superset {key >= boundary}        */
     int *gcand_idx;          /* [gcand_cap] their vocab indices               */
     int gcand_cap;
@@ -130,7 +135,9 @@ struct FinishParams {
 /* The select strategy of a launch whose effective k (greedy: 1; else
  * min(top_k, V, rows)) is k: per-CTA histogram edges (no grid barrier) when k
  * is small against a CTA's slice, else the grid-wide histogram. */
-inline int use_local_edges(int k, int rows_per_cta_max) { return 4 * k <= rows_per_cta_max; }
+inline int use_local_edges(int k, int rows_per_cta_max) {
+    return k <= kLocalMaxK && 4 * k <= rows_per_cta_max;
+}
 inline int effective_k(float temperature, int top_k, int vocab, int rows) {
     int k = (temperature <= 0.0f || top_k <= 0) ? 1 : top_k;
     if (k > vocab) k = vocab;

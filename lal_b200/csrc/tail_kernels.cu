@@ -128,6 +128,23 @@ __device__ __forceinline__ float sampler_expf(float x, const uint32_t *tx, const
     return lal_expf_glibc(x, tx, ty, tn);
 }
 
+/* sampler_expf in two halves, so the bitmap load can be in flight while
+ * other work runs: the first returns the raw bitmap word (0 when x takes no
+ * fix-up), the second finishes with it. */
+__device__ __forceinline__ uint32_t expf_bitmap_word(float x, const uint32_t *bits) {
+    const uint32_t xb = __float_as_uint(x);
+    if (!(xb & 0x80000000u) || !(x <= 0.0f)) return 0u;
+    return __ldg(bits + (((xb - 0x80000000u) >> 8) >> 5));
+}
+__device__ __forceinline__ float expf_with_word(float x, uint32_t word, const uint32_t *tx,
+                                                const uint32_t *ty, int tn) {
+    const uint32_t xb = __float_as_uint(x);
+    const uint32_t b = (xb - 0x80000000u) >> 8;
+    if ((xb & 0x80000000u) && x <= 0.0f && ((word >> (b & 31)) & 1u))
+        return lal_expf_glibc(x, tx, ty, tn);
+    return lal_expf_rounded(x);
+}
+
 /* ------------------------------------------------------- order keys --- */
 /* Monotone map float -> uint32 (larger float, larger key).  -0 maps like +0,
  * so key equality is float equality, as the reference's comparisons treat it. */
@@ -686,7 +703,42 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
     const int S_hist = above + binc; /* global histogram: keys >= Lb, all CTAs */
 
     /* append this CTA's keys >= Lb */
-    {
+    if (local_edges) {
+        /* into this CTA's fixed slot of kSlot entries, in descending key order
+         * (ties by index), so that the last CTA reads only the head of each
+         * slot; the slot count may exceed kSlot (the tail is dropped and the
+         * last CTA checks that nothing dropped can be a candidate) */
+        uint32_t *tk = lh;
+        int *ti = reinterpret_cast<int *>(lh + p.rows_per_cta_max);
+        const int seg = (nloc + NT - 1) / NT;
+        const int i0 = min(nloc, tid * seg), i1 = min(nloc, i0 + seg);
+        uint32_t c = 0;
+        for (int i = i0; i < i1; ++i) c += f2key(lg_s[i]) >= Lb;
+        uint32_t n;
+        uint32_t pos = block_scan_excl(c, ms, &n);
+        for (int i = i0; i < i1; ++i) {
+            const uint32_t key = f2key(lg_s[i]);
+            if (key >= Lb) {
+                tk[pos] = key;
+                ti[pos] = i;
+                ++pos;
+            }
+        }
+        __syncthreads();
+        uint32_t *slot_k = p.gcand_key + (size_t)cta * kSlot;
+        int *slot_i = p.gcand_idx + (size_t)cta * kSlot;
+        for (int j = tid; j < (int)n; j += NT) {
+            const uint32_t me = tk[j];
+            int r = 0;
+#pragma unroll 8
+            for (int q = 0; q < (int)n; ++q) r += (tk[q] > me) || (tk[q] == me && q < j);
+            if (r < kSlot) {
+                slot_k[r] = me;
+                slot_i[r] = p.row_base + c0 + ti[j];
+            }
+        }
+        if (tid == 0) p.gslot_n[cta] = n;
+    } else {
         const int seg = (nloc + NT - 1) / NT;
         const int i0 = min(nloc, tid * seg), i1 = min(nloc, i0 + seg);
         uint32_t c = 0;
@@ -721,16 +773,19 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
     if (tid == 0) stamp(p, G * 8 + 0);
 
     /* shared-memory plan of the stage area: superset keys + indices (Sk, Si),
-     * then the candidates (Cv, Ci) and their ascending-index copies (Ov, Oi)
-     * and running sums (Ce), Ccap a power of two */
+     * then the superset weights (Ws), the candidates (Cv, Ci, Cw) and their
+     * ascending-index copies (Ov, Oi, Ce = weights, then running sums), ccap
+     * a power of two */
     const int s_cap = p.area_bytes / 16;
     int ccap = 1;
-    while (ccap * 2 * 20 <= p.area_bytes - 8 * s_cap) ccap *= 2;
+    while (ccap * 2 * 28 <= p.area_bytes - 8 * s_cap) ccap *= 2;
     uint32_t *Sk = reinterpret_cast<uint32_t *>(smem);
     int *Si = reinterpret_cast<int *>(Sk + s_cap);
-    float *Cv = reinterpret_cast<float *>(Si + s_cap);
+    float *Ws = reinterpret_cast<float *>(Si + s_cap);
+    float *Cv = Ws + ccap;
     int *Ci = reinterpret_cast<int *>(Cv + ccap);
-    float *Ov = reinterpret_cast<float *>(Ci + ccap);
+    float *Cw = reinterpret_cast<float *>(Ci + ccap);
+    float *Ov = Cw + ccap;
     int *Oi = reinterpret_cast<int *>(Ov + ccap);
     float *Ce = reinterpret_cast<float *>(Oi + ccap);
 
@@ -738,12 +793,13 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
     const int Sg = (int)__ldcg(p.gcount);
     int m = 0;
     uint32_t T = 0u;
-    bool fine = ok && dev_status == 0 && Sg <= p.gcand_cap && Sg >= 1;
+    bool fine = ok && dev_status == 0 &&
+                (local_edges || (Sg <= p.gcand_cap && Sg >= 1));
     int S = S_hist;
     if (fine && local_edges) {
-        /* keep the appended keys >= L = the largest CTA edge: stage all keys
-         * in shared memory with batched loads, filter there (positions kept
-         * in Oi), then fetch the indices of the survivors only */
+        /* keep the slot entries >= L* = max(largest CTA edge, k-th largest
+         * CTA maximum): each slot is sorted descending, so only its head is
+         * read */
         uint32_t L = __ldcg(p.gL);
         if (k <= G) {
             /* L2 = k-th largest of the G per-CTA maxima <= T */
@@ -753,6 +809,7 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
             for (int g = tid; g < G; g += NT) {
                 const uint32_t me = ms->gm[g];
                 int gt = 0;
+#pragma unroll 8
                 for (int j = 0; j < G; ++j) gt += ms->gm[j] > me;
                 if (gt < k) best = min(best, me);
             }
@@ -765,36 +822,40 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
             __syncthreads();
         }
         if (tid == 0) stamp(p, G * 8 + 1);
-        S = 0;
-        for (int base = 0; base < Sg; base += s_cap) { /* chunks of s_cap keys */
-            const int n = min(s_cap, Sg - base);
-#pragma unroll 8
-            for (int e = tid; e < n; e += NT) Sk[e] = __ldcg(p.gcand_key + base + e);
-            __syncthreads();
-            const int seg = (n + NT - 1) / NT;
-            const int e0 = min(n, tid * seg), e1 = min(n, e0 + seg);
-            uint32_t c = 0;
-            for (int e = e0; e < e1; ++e) c += Sk[e] >= L;
-            uint32_t tot;
-            uint32_t pos = block_scan_excl(c, ms, &tot) + (uint32_t)S;
-            if (S + (int)tot <= ccap)
-                for (int e = e0; e < e1; ++e)
-                    if (Sk[e] >= L) {
-                        Oi[pos] = base + e;
-                        Ci[pos] = (int)Sk[e];
-                        ++pos;
-                    }
-            S += (int)tot;
-            __syncthreads();
-        }
-        fine = S >= 1 && S <= ccap;
-        if (tid == 0) stamp(p, G * 8 + 2);
-        if (fine) {
-            for (int j = tid; j < S; j += NT) {
-                Sk[j] = (uint32_t)Ci[j];
-                Si[j] = __ldcg(p.gcand_idx + Oi[j]);
+        /* thread g scans slot g's head in groups of 4 keys; gm[g] becomes the
+         * slot's dropped-tail bound (0 if the slot held all of its entries) */
+        uint32_t c = 0;
+        int g_n = 0;
+        const int g = tid;
+        if (g < G) {
+            g_n = (int)__ldcg(p.gslot_n + g);
+            const int lim = min(g_n, kSlot);
+            const uint32_t *sk = p.gcand_key + (size_t)g * kSlot;
+            bool more = true;
+            for (int j = 0; more && j < lim; j += 4) {
+                uint32_t kv[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) kv[q] = j + q < lim ? __ldcg(sk + j + q) : 0u;
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const bool take = more && j + q < lim && kv[q] >= L;
+                    c += take;
+                    more = take;
+                }
             }
         }
+        __syncthreads();
+        if (g < G) ms->gm[g] = g_n > kSlot ? __ldcg(p.gcand_key + (size_t)g * kSlot + kSlot - 1) : 0u;
+        uint32_t tot;
+        uint32_t pos = block_scan_excl(c, ms, &tot);
+        S = (int)tot;
+        fine = S >= 1 && S <= s_cap;
+        if (fine && g < G)
+            for (uint32_t j = 0; j < c; ++j) {
+                Sk[pos + j] = __ldcg(p.gcand_key + (size_t)g * kSlot + j);
+                Si[pos + j] = __ldcg(p.gcand_idx + (size_t)g * kSlot + j);
+            }
+        if (tid == 0) stamp(p, G * 8 + 2);
     } else if (fine) {
         fine = Sg == S && S <= s_cap;
         if (fine)
@@ -805,6 +866,33 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
             }
     }
     __syncthreads();
+    /* Early weights: the superset holds every candidate and the maximum, so
+     * max_l (runtime/lal_sampling.h:107-109) is known before T; the weights'
+     * exception-bitmap loads are issued now and consumed after the select,
+     * hiding their latency behind it. */
+    const bool early = fine && !greedy && S <= 2 * NT && S <= ccap;
+    float max_l = -1e30f;
+    float xw[2] = {0.0f, 0.0f};
+    uint32_t bw[2] = {0u, 0u};
+    if (early) {
+        uint32_t mk = 0u;
+        for (int j = tid; j < S; j += NT) mk = max(mk, Sk[j]);
+        mk = __reduce_max_sync(0xffffffffu, mk);
+        if ((tid & 31) == 0) ms->scan[tid >> 5] = mk;
+        __syncthreads();
+        uint32_t mx = ms->scan[0];
+        for (int w = 1; w < NWARP; ++w) mx = max(mx, ms->scan[w]);
+        __syncthreads();
+        max_l = fmaxf(-1e30f, key2f(mx));
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            const int j = tid + r * NT;
+            if (j < S) {
+                xw[r] = __fdiv_rn(__fsub_rn(key2f(Sk[j]), max_l), temp);
+                bw[r] = expf_bitmap_word(xw[r], p.expf_bits);
+            }
+        }
+    }
     if (fine) {
         if (S <= 256) {
             /* T = min{ key : #{keys > key} < k } -- one pass per element */
@@ -830,6 +918,19 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
                 S, min(k, S), ms);
         }
         if (tid == 0) stamp(p, G * 8 + 3);
+        if (early) {
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+                const int j = tid + r * NT;
+                if (j < S) Ws[j] = expf_with_word(xw[r], bw[r], p.expf_x, p.expf_y, p.expf_n);
+            }
+        }
+        /* a slot whose dropped tail reaches T lost candidates: refuse */
+        if (tid == 0) ms->found = 0;
+        __syncthreads();
+        if (local_edges)
+            for (int g = tid; g < G; g += NT)
+                if (ms->gm[g] != 0u && ms->gm[g] >= T) ms->found = 1;
         /* candidates {v : l[v] >= T} (superset order) */
         const int seg = (S + NT - 1) / NT;
         const int e0 = min(S, tid * seg), e1 = min(S, e0 + seg);
@@ -843,9 +944,10 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
                 if (Sk[e] >= T) {
                     Cv[pos] = key2f(Sk[e]);
                     Ci[pos] = Si[e];
+                    Cw[pos] = early ? Ws[e] : 0.0f;
                     ++pos;
                 }
-        fine = m >= 1 && m <= ccap;
+        fine = m >= 1 && m <= ccap && ms->found == 0;
     }
     __syncthreads();
 
@@ -881,9 +983,11 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
         for (int i = tid; i < m; i += NT) {
             const int me = Ci[i];
             int r = 0;
+#pragma unroll 8
             for (int j = 0; j < m; ++j) r += Ci[j] < me;
             Oi[r] = me;
             Ov[r] = Cv[i];
+            Ce[r] = Cw[i];
         }
     } else {
         int n2 = 1;
@@ -891,6 +995,7 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
         for (int i = tid; i < n2; i += NT) {
             Oi[i] = i < m ? Ci[i] : 0x7fffffff;
             Ov[i] = i < m ? Cv[i] : 0.0f;
+            Ce[i] = i < m ? Cw[i] : 0.0f;
         }
         __syncthreads();
         for (int size = 2; size <= n2; size <<= 1)
@@ -903,9 +1008,12 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
                     if ((a > b) == asc) {
                         Oi[lo] = b;
                         Oi[hi] = a;
-                        const float t = Ov[lo];
+                        float t = Ov[lo];
                         Ov[lo] = Ov[hi];
                         Ov[hi] = t;
+                        t = Ce[lo];
+                        Ce[lo] = Ce[hi];
+                        Ce[hi] = t;
                     }
                 }
                 __syncthreads();
@@ -926,25 +1034,41 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
     }
 
     /* max over candidates, floored at -1e30f (runtime/lal_sampling.h:107-109) */
-    float mx = -1e30f;
-    for (int i = tid; i < m; i += NT) mx = fmaxf(mx, Ov[i]);
-    const float max_l = block_max_f(mx, ms);
+    if (!early) {
+        float mx = -1e30f;
+        for (int i = tid; i < m; i += NT) mx = fmaxf(mx, Ov[i]);
+        max_l = block_max_f(mx, ms);
+    }
     if (tid == 0) stamp(p, G * 8 + 5);
     dg.max_l = max_l;
     int token;
     if (greedy) {
         token = Oi[0];
     } else {
-        /* weights expf((l - max_l) / T) (runtime/lal_sampling.h:112) */
-        for (int i = tid; i < m; i += NT) {
-            const float x = __fdiv_rn(__fsub_rn(Ov[i], max_l), temp);
-            Ce[i] = sampler_expf(x, p.expf_x, p.expf_y, p.expf_n, p.expf_bits);
-        }
+        /* weights expf((l - max_l) / T) (runtime/lal_sampling.h:112), unless
+         * they came with the candidates */
+        if (!early)
+            for (int i = tid; i < m; i += NT) {
+                const float x = __fdiv_rn(__fsub_rn(Ov[i], max_l), temp);
+                Ce[i] = sampler_expf(x, p.expf_x, p.expf_y, p.expf_n, p.expf_bits);
+            }
         __syncthreads();
-        /* sequential float sum in ascending vocab order; keep the prefix */
+        /* sequential float sum in ascending vocab order; keep the prefix
+         * (values fetched eight at a time, the adds stay in order) */
         if (tid == 0) {
             float acc = 0.0f;
-            for (int i = 0; i < m; ++i) {
+            int i = 0;
+            for (; i + 8 <= m; i += 8) {
+                float v[8];
+#pragma unroll
+                for (int q = 0; q < 8; ++q) v[q] = Ce[i + q];
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    acc = __fadd_rn(acc, v[q]);
+                    Ce[i + q] = acc;
+                }
+            }
+            for (; i < m; ++i) {
                 acc = __fadd_rn(acc, Ce[i]);
                 Ce[i] = acc;
             }
@@ -1200,7 +1324,7 @@ int plan_launch(TailParams &p, int num_sms, int min_rows_per_cta) {
     }
     /* the last CTA needs room for the candidates (k plus ties) and the key
      * histogram of 4096 bins */
-    if (p.mode != MODE_LMHEAD && (p.area_bytes < 16384 || p.area_bytes / 2 < 20 * (p.max_k + 64)))
+    if (p.mode != MODE_LMHEAD && (p.area_bytes < 16384 || p.area_bytes / 2 < 56 * (p.max_k + 64)))
         return -5;
     off = align_up(p.area_bytes, 128);
     p.off_bars = off;
