@@ -776,7 +776,10 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
      * then the superset weights (Ws), the candidates (Cv, Ci, Cw) and their
      * ascending-index copies (Ov, Oi, Ce = weights, then running sums), ccap
      * a power of two */
-    const int s_cap = p.area_bytes / 16;
+    /* grid-histogram path: the superset size is known (S_hist); small-k
+     * path: the slot heads are small, a sixteenth of the area suffices */
+    const int s_cap = local_edges ? p.area_bytes / 16
+                                  : max(1, min(S_hist, p.area_bytes / 8 - 28 * 64));
     int ccap = 1;
     while (ccap * 2 * 28 <= p.area_bytes - 8 * s_cap) ccap *= 2;
     uint32_t *Sk = reinterpret_cast<uint32_t *>(smem);
@@ -1324,8 +1327,14 @@ int plan_launch(TailParams &p, int num_sms, int min_rows_per_cta) {
     }
     /* the last CTA needs room for the candidates (k plus ties) and the key
      * histogram of 4096 bins */
-    if (p.mode != MODE_LMHEAD && (p.area_bytes < 16384 || p.area_bytes / 2 < 56 * (p.max_k + 64)))
-        return -5;
+    if (p.mode != MODE_LMHEAD) {
+        /* k plus ties in power-of-two candidate arrays (28 B an entry) next to
+         * a superset of k plus a boundary bin (8 B an entry) */
+        int c2 = 1;
+        while (c2 < p.max_k + 64) c2 <<= 1;
+        if (p.area_bytes < 16384 || 28 * c2 + 8 * (p.max_k + 64 + kRefineMax) > p.area_bytes)
+            return -5;
+    }
     off = align_up(p.area_bytes, 128);
     p.off_bars = off;
     off += 16 * kMaxStages;
