@@ -68,7 +68,8 @@ int fail(int code, const char *fmt, ...) {
 struct DeviceState {
     bool ready = false;
     int num_sms = 0;
-    uint32_t *d_expf_x = nullptr, *d_expf_y = nullptr, *d_expf_bits = nullptr;
+    uint32_t *d_expf_x = nullptr, *d_expf_y = nullptr, *d_expf_bits = nullptr,
+             *d_expf_off = nullptr;
     int expf_n = 0;
 };
 std::mutex g_dev_mu;
@@ -106,6 +107,23 @@ int device_state(int dev, DeviceState **out) {
         }
         CU(cudaMalloc(&ds.d_expf_bits, 4ull * kExpfBitmapWords));
         CU(cudaMemcpy(ds.d_expf_bits, bits.data(), 4ull * kExpfBitmapWords, cudaMemcpyHostToDevice));
+        /* off[w] = first table entry whose bitmap word is >= w (table sorted) */
+        std::vector<uint32_t> off(kExpfBitmapWords + 1, n);
+        {
+            uint32_t i = 0;
+            for (uint32_t w = 0; w <= (uint32_t)kExpfBitmapWords; ++w) {
+                while (i < n) {
+                    uint32_t xb;
+                    memcpy(&xb, lal_expf_fixups_blob + 4 + 4ull * i, 4);
+                    if (((xb - 0x80000000u) >> 13) >= w) break;
+                    ++i;
+                }
+                off[w] = i;
+            }
+        }
+        CU(cudaMalloc(&ds.d_expf_off, 4ull * (kExpfBitmapWords + 1)));
+        CU(cudaMemcpy(ds.d_expf_off, off.data(), 4ull * (kExpfBitmapWords + 1),
+                      cudaMemcpyHostToDevice));
         ds.expf_n = (int)n;
         ds.ready = true;
     }
@@ -316,6 +334,7 @@ void base_params(TailParams &p, const DeviceState *ds) {
     p.expf_y = ds->d_expf_y;
     p.expf_n = ds->expf_n;
     p.expf_bits = ds->d_expf_bits;
+    p.expf_off = ds->d_expf_off;
 }
 
 int sample_launch(DropinState *S, DeviceState *ds, float *logits, int V, float temperature,
@@ -696,6 +715,7 @@ int lal_tail_sample_token_filtered(float *logits, int vocab_size, float temperat
     f.expf_y = ds->d_expf_y;
     f.expf_n = ds->expf_n;
     f.expf_bits = ds->d_expf_bits;
+    f.expf_off = ds->d_expf_off;
     f.phase = 0;
     CU(launch_finish(f, st));
     CU(cudaMemcpyAsync(&dg, S->ls.diag.p, sizeof(dg), cudaMemcpyDeviceToHost, st));
@@ -736,7 +756,7 @@ int lal_tail_debug_expf(const float *x, float *y, int n) {
     CHECK(S->logits.ensure(4ull * n));
     CU(cudaMemcpyAsync(S->x.p, x, 4ull * n, cudaMemcpyHostToDevice, st));
     CU(launch_debug_expf((const float *)S->x.p, (float *)S->logits.p, n, ds->d_expf_x,
-                         ds->d_expf_y, ds->expf_n, ds->d_expf_bits, st));
+                         ds->d_expf_y, ds->expf_n, ds->d_expf_bits, ds->d_expf_off, st));
     CU(cudaMemcpyAsync(y, S->logits.p, 4ull * n, cudaMemcpyDeviceToHost, st));
     CU(cudaStreamSynchronize(st));
     return LAL_TAIL_OK;

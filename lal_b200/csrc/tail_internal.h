@@ -97,6 +97,7 @@ struct TailParams {
     const uint32_t *expf_x, *expf_y;
     int expf_n;
     const uint32_t *expf_bits;
+    const uint32_t *expf_off; /* [words+1]: first table entry of each bitmap word */
     /* optional globaltimer stamps: [cta*8 + i] per CTA (start, prologue done,
      * rows done, list written) and [grid*8 + i] for the merge */
     unsigned long long *phase_ts;
@@ -130,6 +131,7 @@ struct FinishParams {
     const uint32_t *expf_x, *expf_y;
     int expf_n;
     const uint32_t *expf_bits;
+    const uint32_t *expf_off;
 };
 
 /* The select strategy of a launch whose effective k (greedy: 1; else
@@ -156,6 +158,6 @@ cudaError_t launch_quantize_rows(const float *W, int d, int8_t *q, int ld,
                                  float *scale, int n_rows, cudaStream_t st);
 cudaError_t launch_debug_expf(const float *x, float *y, int n, const uint32_t *tx,
                               const uint32_t *ty, int tn, const uint32_t *bits,
-                              cudaStream_t st);
+                              const uint32_t *off, cudaStream_t st);
 
 }  // namespace lal

@@ -116,16 +116,28 @@ __device__ __forceinline__ void st_release_gpu(unsigned *p, unsigned v) {
     asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
+/* The glibc fix-up of x, whose bitmap bit is set: the entries of x's bitmap
+ * word (8192 bit patterns) are tx[off[w] .. off[w+1]), a few at most. */
+__device__ __forceinline__ float expf_fixup(float x, const uint32_t *tx, const uint32_t *ty,
+                                            const uint32_t *off) {
+    const uint32_t xb = __float_as_uint(x);
+    const uint32_t w = (xb - 0x80000000u) >> 13;
+    const uint32_t lo = __ldg(off + w), hi = __ldg(off + w + 1);
+    for (uint32_t i = lo; i < hi; ++i)
+        if (__ldg(tx + i) == xb) return __uint_as_float(__ldg(ty + i));
+    return lal_expf_rounded(x);
+}
+
 /* The sampler's weight function: glibc-exact expf (lal_expf.h) with the
  * fix-up table gated by a membership bitmap, so that nearly every call costs
- * one bitmap load instead of a binary search over the table. */
+ * one bitmap load, and a flagged one two more plus a short scan. */
 __device__ __forceinline__ float sampler_expf(float x, const uint32_t *tx, const uint32_t *ty,
-                                              int tn, const uint32_t *bits) {
+                                              const uint32_t *bits, const uint32_t *off) {
     const uint32_t xb = __float_as_uint(x);
     if (!(xb & 0x80000000u) || !(x <= 0.0f)) return lal_expf_rounded(x);
     const uint32_t b = (xb - 0x80000000u) >> 8;
     if (!((__ldg(bits + (b >> 5)) >> (b & 31)) & 1u)) return lal_expf_rounded(x);
-    return lal_expf_glibc(x, tx, ty, tn);
+    return expf_fixup(x, tx, ty, off);
 }
 
 /* sampler_expf in two halves, so the bitmap load can be in flight while
@@ -137,11 +149,11 @@ __device__ __forceinline__ uint32_t expf_bitmap_word(float x, const uint32_t *bi
     return __ldg(bits + (((xb - 0x80000000u) >> 8) >> 5));
 }
 __device__ __forceinline__ float expf_with_word(float x, uint32_t word, const uint32_t *tx,
-                                                const uint32_t *ty, int tn) {
+                                                const uint32_t *ty, const uint32_t *off) {
     const uint32_t xb = __float_as_uint(x);
     const uint32_t b = (xb - 0x80000000u) >> 8;
     if ((xb & 0x80000000u) && x <= 0.0f && ((word >> (b & 31)) & 1u))
-        return lal_expf_glibc(x, tx, ty, tn);
+        return expf_fixup(x, tx, ty, off);
     return lal_expf_rounded(x);
 }
 
@@ -792,8 +804,25 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
     int *Oi = reinterpret_cast<int *>(Ov + ccap);
     float *Ce = reinterpret_cast<float *>(Oi + ccap);
 
+    /* one batch of global loads: status, counts, the bound words and, on the
+     * small-k path, thread g's slot count, maximum and its slot's first 4
+     * entries (read whatever the count; only the first min(n, kSlot) count) */
     const int dev_status = __ldcg(p.status);
     const int Sg = (int)__ldcg(p.gcount);
+    uint32_t Lg = 0u, gmx = 0u, hk[4] = {0u, 0u, 0u, 0u};
+    int g_n = 0, hi[4] = {0, 0, 0, 0};
+    if (local_edges) {
+        Lg = __ldcg(p.gL);
+        if (tid < G) {
+            gmx = __ldcg(p.gmax + tid);
+            g_n = (int)__ldcg(p.gslot_n + tid);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                hk[q] = __ldcg(p.gcand_key + (size_t)tid * kSlot + q);
+                hi[q] = __ldcg(p.gcand_idx + (size_t)tid * kSlot + q);
+            }
+        }
+    }
     int m = 0;
     uint32_t T = 0u;
     bool fine = ok && dev_status == 0 &&
@@ -803,10 +832,10 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
         /* keep the slot entries >= L* = max(largest CTA edge, k-th largest
          * CTA maximum): each slot is sorted descending, so only its head is
          * read */
-        uint32_t L = __ldcg(p.gL);
+        uint32_t L = Lg;
         if (k <= G) {
             /* L2 = k-th largest of the G per-CTA maxima <= T */
-            for (int g = tid; g < G; g += NT) ms->gm[g] = __ldcg(p.gmax + g);
+            if (tid < G) ms->gm[tid] = gmx;
             __syncthreads();
             uint32_t best = 0xffffffffu;
             for (int g = tid; g < G; g += NT) {
@@ -828,14 +857,19 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
         /* thread g scans slot g's head in groups of 4 keys; gm[g] becomes the
          * slot's dropped-tail bound (0 if the slot held all of its entries) */
         uint32_t c = 0;
-        int g_n = 0;
         const int g = tid;
         if (g < G) {
-            g_n = (int)__ldcg(p.gslot_n + g);
             const int lim = min(g_n, kSlot);
             const uint32_t *sk = p.gcand_key + (size_t)g * kSlot;
             bool more = true;
-            for (int j = 0; more && j < lim; j += 4) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const bool take = more && q < lim && hk[q] >= L;
+                c += take;
+                more = take;
+            }
+            /* rarely more than 4 survivors in one slot: read on */
+            for (int j = 4; more && j < lim; j += 4) {
                 uint32_t kv[4];
 #pragma unroll
                 for (int q = 0; q < 4; ++q) kv[q] = j + q < lim ? __ldcg(sk + j + q) : 0u;
@@ -853,11 +887,18 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
         uint32_t pos = block_scan_excl(c, ms, &tot);
         S = (int)tot;
         fine = S >= 1 && S <= s_cap;
-        if (fine && g < G)
-            for (uint32_t j = 0; j < c; ++j) {
+        if (fine && g < G) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+                if ((uint32_t)q < c) {
+                    Sk[pos + q] = hk[q];
+                    Si[pos + q] = hi[q];
+                }
+            for (uint32_t j = 4; j < c; ++j) {
                 Sk[pos + j] = __ldcg(p.gcand_key + (size_t)g * kSlot + j);
                 Si[pos + j] = __ldcg(p.gcand_idx + (size_t)g * kSlot + j);
             }
+        }
         if (tid == 0) stamp(p, G * 8 + 2);
     } else if (fine) {
         fine = Sg == S && S <= s_cap;
@@ -925,7 +966,7 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
 #pragma unroll
             for (int r = 0; r < 2; ++r) {
                 const int j = tid + r * NT;
-                if (j < S) Ws[j] = expf_with_word(xw[r], bw[r], p.expf_x, p.expf_y, p.expf_n);
+                if (j < S) Ws[j] = expf_with_word(xw[r], bw[r], p.expf_x, p.expf_y, p.expf_off);
             }
         }
         /* a slot whose dropped tail reaches T lost candidates: refuse */
@@ -1053,7 +1094,7 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
         if (!early)
             for (int i = tid; i < m; i += NT) {
                 const float x = __fdiv_rn(__fsub_rn(Ov[i], max_l), temp);
-                Ce[i] = sampler_expf(x, p.expf_x, p.expf_y, p.expf_n, p.expf_bits);
+                Ce[i] = sampler_expf(x, p.expf_x, p.expf_y, p.expf_bits, p.expf_off);
             }
         __syncthreads();
         /* sequential float sum in ascending vocab order; keep the prefix
@@ -1216,7 +1257,7 @@ __global__ void __launch_bounds__(NT) finish_kernel(const FinishParams f) {
         for (int i = tid; i < f.m; i += NT)
             f.prefix[i] = f.keep[i] ? sampler_expf(__fdiv_rn(__fsub_rn(f.cand_val[i], max_l),
                                                              f.temperature),
-                                                   f.expf_x, f.expf_y, f.expf_n, f.expf_bits)
+                                                   f.expf_x, f.expf_y, f.expf_bits, f.expf_off)
                                     : 0.0f;
         __syncthreads();
         if (tid == 0) {
@@ -1258,9 +1299,10 @@ __global__ void __launch_bounds__(NT) finish_kernel(const FinishParams f) {
 }
 
 __global__ void debug_expf_kernel(const float *x, float *y, int n, const uint32_t *tx,
-                                  const uint32_t *ty, int tn, const uint32_t *bits) {
+                                  const uint32_t *ty, const uint32_t *bits,
+                                  const uint32_t *off) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < n) y[i] = sampler_expf(x[i], tx, ty, tn, bits);
+    if (i < n) y[i] = sampler_expf(x[i], tx, ty, bits, off);
 }
 
 /* -------------------------------------------------- host planning --- */
@@ -1409,8 +1451,9 @@ cudaError_t launch_finish(const FinishParams &f, cudaStream_t st) {
 
 cudaError_t launch_debug_expf(const float *x, float *y, int n, const uint32_t *tx,
                               const uint32_t *ty, int tn, const uint32_t *bits,
-                              cudaStream_t st) {
-    debug_expf_kernel<<<(n + 255) / 256, 256, 0, st>>>(x, y, n, tx, ty, tn, bits);
+                              const uint32_t *off, cudaStream_t st) {
+    (void)tn;
+    debug_expf_kernel<<<(n + 255) / 256, 256, 0, st>>>(x, y, n, tx, ty, bits, off);
     return cudaGetLastError();
 }
 
