@@ -837,6 +837,7 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
             /* L2 = k-th largest of the G per-CTA maxima <= T */
             if (tid < G) ms->gm[tid] = gmx;
             __syncthreads();
+            if (tid == 0) stamp(p, cta * 8 + 4);
             uint32_t best = 0xffffffffu;
             for (int g = tid; g < G; g += NT) {
                 const uint32_t me = ms->gm[g];
@@ -848,6 +849,7 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
             best = __reduce_min_sync(0xffffffffu, best);
             if ((tid & 31) == 0) ms->scan[tid >> 5] = best;
             __syncthreads();
+            if (tid == 0) stamp(p, cta * 8 + 5);
             uint32_t L2 = ms->scan[0];
             for (int w = 1; w < NWARP; ++w) L2 = min(L2, ms->scan[w]);
             L = max(L, L2);
@@ -972,6 +974,7 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
         /* a slot whose dropped tail reaches T lost candidates: refuse */
         if (tid == 0) ms->found = 0;
         __syncthreads();
+        if (tid == 0) stamp(p, cta * 8 + 6);
         if (local_edges)
             for (int g = tid; g < G; g += NT)
                 if (ms->gm[g] != 0u && ms->gm[g] >= T) ms->found = 1;
