@@ -281,54 +281,6 @@ __device__ __forceinline__ float block_max_f(float v, Misc *ms) {
     return r;
 }
 
-/* Bitonic sort of 32*R keys held by one warp, element e = lane*R + j in
- * v[j]; ascending, or descending when DESC.  Pairs closer than R swap inside
- * a lane, farther ones are exchanged with shfl.xor.  All loops unroll. */
-template <int R, bool DESC>
-__device__ __forceinline__ void warp_bitonic_sort(uint32_t (&v)[R]) {
-    const int lane = threadIdx.x & 31;
-#pragma unroll
-    for (int size = 2; size <= 32 * R; size <<= 1) {
-#pragma unroll
-        for (int stride = size >> 1; stride > 0; stride >>= 1) {
-            if (stride >= R) {
-#pragma unroll
-                for (int j = 0; j < R; ++j) {
-                    const int e = lane * R + j;
-                    const uint32_t other = __shfl_xor_sync(0xffffffffu, v[j], stride / R);
-                    const bool up = ((e & size) == 0) != DESC;
-                    const bool lower = (e & stride) == 0;
-                    v[j] = (lower == up) ? min(v[j], other) : max(v[j], other);
-                }
-            } else {
-#pragma unroll
-                for (int j = 0; j < R; ++j) {
-                    const int jp = j ^ stride;
-                    if (jp > j) {
-                        const int e = lane * R + j;
-                        const bool up = ((e & size) == 0) != DESC;
-                        const uint32_t a = v[j], b = v[jp];
-                        if (up ? (a > b) : (a < b)) {
-                            v[j] = b;
-                            v[jp] = a;
-                        }
-                    }
-                }
-            }
-        }
-    }
-}
-
-/* Element e (0-based, e < 32*R) of a warp-held array, to every lane. */
-template <int R>
-__device__ __forceinline__ uint32_t warp_element(const uint32_t (&v)[R], int e) {
-    uint32_t mine = 0u;
-#pragma unroll
-    for (int j = 0; j < R; ++j)
-        if (j == (e % R)) mine = v[j];
-    return __shfl_sync(0xffffffffu, mine, e / R);
-}
-
 /* Boundary bin of a histogram h[0..nb) scanned from the top bin down: the bin
  * holding the krem-th largest entry (1 <= krem <= total).  Returns the bin;
  * *above gets the count in higher bins, *count the bin's own count.  All
@@ -853,25 +805,19 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
     float *Ce = reinterpret_cast<float *>(Oi + ccap);
 
     /* one batch of global loads: status, counts, the bound words and, on the
-     * small-k path, thread g's slot count, maximum and its slot's first 8
+     * small-k path, thread g's slot count, maximum and its slot's first 4
      * entries (read whatever the count; only the first min(n, kSlot) count) */
     const int dev_status = __ldcg(p.status);
     const int Sg = (int)__ldcg(p.gcount);
-    constexpr int kHead = 8;
-    uint32_t Lg = 0u, gmx = 0u, hk[kHead];
-    int g_n = 0, hi[kHead];
-#pragma unroll
-    for (int q = 0; q < kHead; ++q) {
-        hk[q] = 0u;
-        hi[q] = 0;
-    }
+    uint32_t Lg = 0u, gmx = 0u, hk[4] = {0u, 0u, 0u, 0u};
+    int g_n = 0, hi[4] = {0, 0, 0, 0};
     if (local_edges) {
         Lg = __ldcg(p.gL);
         if (tid < G) {
             gmx = __ldcg(p.gmax + tid);
             g_n = (int)__ldcg(p.gslot_n + tid);
 #pragma unroll
-            for (int q = 0; q < kHead; ++q) {
+            for (int q = 0; q < 4; ++q) {
                 hk[q] = __ldcg(p.gcand_key + (size_t)tid * kSlot + q);
                 hi[q] = __ldcg(p.gcand_idx + (size_t)tid * kSlot + q);
             }
@@ -888,27 +834,29 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
          * read */
         uint32_t L = Lg;
         if (k <= G) {
-            /* L2 = k-th largest of the G per-CTA maxima <= T (one warp sort) */
+            /* L2 = k-th largest of the G per-CTA maxima <= T */
             if (tid < G) ms->gm[tid] = gmx;
             __syncthreads();
             if (tid == 0) stamp(p, cta * 8 + 4);
-            if (warp == 0) {
-                uint32_t v[8];
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const int e = lane * 8 + j;
-                    v[j] = e < G ? ms->gm[e] : 0u;
-                }
-                warp_bitonic_sort<8, true>(v);
-                const uint32_t L2 = warp_element<8>(v, k - 1);
-                if (lane == 0) ms->sh[9] = L2;
+            uint32_t best = 0xffffffffu;
+            for (int g = tid; g < G; g += NT) {
+                const uint32_t me = ms->gm[g];
+                int gt = 0;
+#pragma unroll 8
+                for (int j = 0; j < G; ++j) gt += ms->gm[j] > me;
+                if (gt < k) best = min(best, me);
             }
+            best = __reduce_min_sync(0xffffffffu, best);
+            if ((tid & 31) == 0) ms->scan[tid >> 5] = best;
             __syncthreads();
-            L = max(L, ms->sh[9]);
             if (tid == 0) stamp(p, cta * 8 + 5);
+            uint32_t L2 = ms->scan[0];
+            for (int w = 1; w < NWARP; ++w) L2 = min(L2, ms->scan[w]);
+            L = max(L, L2);
+            __syncthreads();
         }
         if (tid == 0) stamp(p, G * 8 + 1);
-        /* thread g counts slot g's leading entries >= L; gm[g] becomes the
+        /* thread g scans slot g's head in groups of 4 keys; gm[g] becomes the
          * slot's dropped-tail bound (0 if the slot held all of its entries) */
         uint32_t c = 0;
         const int g = tid;
@@ -917,19 +865,19 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
             const uint32_t *sk = p.gcand_key + (size_t)g * kSlot;
             bool more = true;
 #pragma unroll
-            for (int q = 0; q < kHead; ++q) {
+            for (int q = 0; q < 4; ++q) {
                 const bool take = more && q < lim && hk[q] >= L;
                 c += take;
                 more = take;
             }
-            /* rarely more than kHead survivors in one slot: read on */
-            for (int j = kHead; more && j < lim; j += 4) {
-                uint32_t kv4[4];
+            /* rarely more than 4 survivors in one slot: read on */
+            for (int j = 4; more && j < lim; j += 4) {
+                uint32_t kv[4];
 #pragma unroll
-                for (int q = 0; q < 4; ++q) kv4[q] = j + q < lim ? __ldcg(sk + j + q) : 0u;
+                for (int q = 0; q < 4; ++q) kv[q] = j + q < lim ? __ldcg(sk + j + q) : 0u;
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {
-                    const bool take = more && j + q < lim && kv4[q] >= L;
+                    const bool take = more && j + q < lim && kv[q] >= L;
                     c += take;
                     more = take;
                 }
@@ -943,227 +891,17 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
         fine = S >= 1 && S <= s_cap;
         if (fine && g < G) {
 #pragma unroll
-            for (int q = 0; q < kHead; ++q)
+            for (int q = 0; q < 4; ++q)
                 if ((uint32_t)q < c) {
                     Sk[pos + q] = hk[q];
                     Si[pos + q] = hi[q];
                 }
-            for (uint32_t j = kHead; j < c; ++j) {
+            for (uint32_t j = 4; j < c; ++j) {
                 Sk[pos + j] = __ldcg(p.gcand_key + (size_t)g * kSlot + j);
                 Si[pos + j] = __ldcg(p.gcand_idx + (size_t)g * kSlot + j);
             }
         }
         if (tid == 0) stamp(p, G * 8 + 2);
-        __syncthreads();
-        if (fine && S <= 256 && p.vocab <= (1 << 24)) {
-            /* ---- the common case: one warp finishes, without block barriers:
-             * superset entry e = lane*8 + j in registers ---- */
-            if (warp != 0) return;
-            uint32_t kv[8];
-            int iv[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const int e = lane * 8 + j;
-                kv[j] = e < S ? Sk[e] : 0u; /* 0 sorts below every key */
-                iv[j] = e < S ? Si[e] : 0;
-            }
-            /* the maximum is a candidate: it gives max_l (lal_sampling.h:107-109) */
-            uint32_t mk = 0u;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) mk = max(mk, kv[j]);
-            mk = __reduce_max_sync(0xffffffffu, mk);
-            const float wmax = fmaxf(-1e30f, key2f(mk));
-            /* weights' bitmap loads issued now, consumed after the select */
-            float xv[8];
-            uint32_t bwd[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                xv[j] = 0.0f;
-                bwd[j] = 0u;
-                if (!greedy && lane * 8 + j < S) {
-                    xv[j] = __fdiv_rn(__fsub_rn(key2f(kv[j]), wmax), temp);
-                    bwd[j] = expf_bitmap_word(xv[j], p.expf_bits);
-                }
-            }
-            /* T = the k-th largest superset key */
-            uint32_t sv[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) sv[j] = kv[j];
-            warp_bitonic_sort<8, true>(sv);
-            const uint32_t Tw = warp_element<8>(sv, min(k, S) - 1);
-            if (lane == 0) stamp(p, G * 8 + 3);
-            /* candidates {l >= T}, compacted in superset order, with weights */
-            uint32_t cnt = 0;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) cnt += (lane * 8 + j < S && kv[j] >= Tw) ? 1u : 0u;
-            uint32_t incl = cnt;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
-                if (lane >= o) incl += y;
-            }
-            const int mw = (int)__shfl_sync(0xffffffffu, incl, 31);
-            bool lost = false; /* a slot whose dropped tail reaches T */
-            for (int gg = lane; gg < G; gg += 32) lost |= ms->gm[gg] != 0u && ms->gm[gg] >= Tw;
-            lost = __any_sync(0xffffffffu, lost);
-            const bool okw = mw >= 1 && mw <= 256 && mw <= ccap && !lost;
-            if (okw) {
-                uint32_t q = incl - cnt;
-#pragma unroll
-                for (int j = 0; j < 8; ++j)
-                    if (lane * 8 + j < S && kv[j] >= Tw) {
-                        Cv[q] = key2f(kv[j]);
-                        Ci[q] = iv[j];
-                        Cw[q] = greedy ? 0.0f
-                                       : expf_with_word(xv[j], bwd[j], p.expf_x, p.expf_y,
-                                                        p.expf_off);
-                        ++q;
-                    }
-            }
-            __syncwarp();
-            StreamDiag dw;
-            dw.threshold = key2f(Tw);
-            dw.max_l = greedy ? 0.0f : wmax;
-            dw.sum = 0.0f;
-            dw.r = 0.0f;
-            dw.n_cand = mw;
-            dw.greedy = greedy ? 1 : 0;
-            dw.drew = 0;
-            dw.token = -1;
-            if (lane == 0) { /* leave the scratch clean for the next launch */
-                *p.gcount = 0u;
-                *p.gL = 0u;
-                p.counter[0] = 0u;
-            }
-            if (!okw) {
-                if (lane == 0) {
-                    atomicCAS(p.status, 0, (int)DEV_CAPACITY);
-                    p.tokens[0] = -1;
-                    p.diag[0] = dw;
-                }
-                return;
-            }
-            /* ascending vocab order: sort (index << 8 | position) */
-            if (mw <= 64) {
-                uint32_t o2[2];
-#pragma unroll
-                for (int r = 0; r < 2; ++r) {
-                    const int e = lane * 2 + r;
-                    o2[r] = e < mw ? ((uint32_t)Ci[e] << 8) | (uint32_t)e : 0xffffffffu;
-                }
-                warp_bitonic_sort<2, false>(o2);
-#pragma unroll
-                for (int r = 0; r < 2; ++r) {
-                    const int e = lane * 2 + r;
-                    if (e < mw) {
-                        const int qq = (int)(o2[r] & 255u);
-                        Oi[e] = (int)(o2[r] >> 8);
-                        Ov[e] = Cv[qq];
-                        Ce[e] = Cw[qq];
-                    }
-                }
-            } else {
-                uint32_t o8[8];
-#pragma unroll
-                for (int r = 0; r < 8; ++r) {
-                    const int e = lane * 8 + r;
-                    o8[r] = e < mw ? ((uint32_t)Ci[e] << 8) | (uint32_t)e : 0xffffffffu;
-                }
-                warp_bitonic_sort<8, false>(o8);
-#pragma unroll
-                for (int r = 0; r < 8; ++r) {
-                    const int e = lane * 8 + r;
-                    if (e < mw) {
-                        const int qq = (int)(o8[r] & 255u);
-                        Oi[e] = (int)(o8[r] >> 8);
-                        Ov[e] = Cv[qq];
-                        Ce[e] = Cw[qq];
-                    }
-                }
-            }
-            __syncwarp();
-            if (lane == 0) stamp(p, G * 8 + 4);
-            if (p.cand_val_out != nullptr && mw <= p.cand_out_cap)
-                for (int e = lane; e < mw; e += 32) {
-                    p.cand_val_out[e] = Ov[e];
-                    p.cand_idx_out[e] = Oi[e];
-                }
-            if (p.candidates_only) {
-                if (lane == 0) p.diag[0] = dw;
-                return;
-            }
-            int token;
-            if (greedy) {
-                token = Oi[0];
-            } else {
-                /* sequential float sum in ascending vocab order, prefix kept */
-                float sum = 0.0f;
-                if (lane == 0) {
-                    float acc = 0.0f;
-                    int i = 0;
-                    for (; i + 8 <= mw; i += 8) {
-                        float v[8];
-#pragma unroll
-                        for (int qq = 0; qq < 8; ++qq) v[qq] = Ce[i + qq];
-#pragma unroll
-                        for (int qq = 0; qq < 8; ++qq) {
-                            acc = __fadd_rn(acc, v[qq]);
-                            Ce[i + qq] = acc;
-                        }
-                    }
-                    for (; i < mw; ++i) {
-                        acc = __fadd_rn(acc, Ce[i]);
-                        Ce[i] = acc;
-                    }
-                    sum = acc;
-                }
-                sum = __shfl_sync(0xffffffffu, sum, 0);
-                __syncwarp();
-                dw.sum = sum;
-                if (lane == 0) stamp(p, G * 8 + 6);
-                if (p.variant == VARIANT_SERVER && sum <= 0.0f) {
-                    /* tools/server/qwen7b_server.c:285-286 */
-                    token = 0;
-                    float bv = -1e30f;
-                    for (int i = 0; i < mw; ++i)
-                        if (Ov[i] > bv) {
-                            bv = Ov[i];
-                            token = Oi[i];
-                        }
-                } else {
-                    /* r = u * sum; first candidate with r <= running sum
-                     * (runtime/lal_sampling.h:116-124) */
-                    const float r = __fmul_rn(u0, sum);
-                    dw.r = r;
-                    dw.drew = 1;
-                    int first = 0x7fffffff;
-                    for (int i = lane; i < mw; i += 32)
-                        if (r <= Ce[i]) {
-                            first = i;
-                            break;
-                        }
-                    first = __reduce_min_sync(0xffffffffu, first);
-                    token = first != 0x7fffffff ? Oi[first] : p.vocab - 1;
-                }
-            }
-            if (lane == 0) {
-                dw.token = token;
-                p.tokens[0] = token;
-                p.diag[0] = dw;
-                if (p.push_history && p.hist_cap > 0) {
-                    /* runtime/lal_sampling.h:133-136 as a ring: FIFO at hist_cap */
-                    if (hn < p.hist_cap) {
-                        p.hist_ids[hn] = token;
-                        p.hist_n[0] = hn + 1;
-                    } else {
-                        p.hist_ids[hhead] = token;
-                        p.hist_head[0] = (hhead + 1) % p.hist_cap;
-                    }
-                }
-                stamp(p, G * 8 + 7);
-            }
-            return;
-        }
     } else if (fine) {
         fine = Sg == S && S <= s_cap;
         if (fine)
