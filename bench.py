@@ -266,11 +266,15 @@ def run_ours(args, cfg):
                                 device_id=torch.device("cuda", local))
     B = cfg.streams
     K, W = args.steps, args.warmup
-    t = L.DecodeTail(cfg.vocab, cfg.n_embd, max_streams=B, max_top_k=max(cfg.top_k, 1),
-                     history_cap=cfg.hist, sampler=L.LAL_SAMPLER_LIBRARY, device=local,
-                     shard_rank=rank, shard_count=world)
     if world > 1:
-        t.connect(dist)
+        from lal_b200.sharded import ShardedDecodeTail
+        # vocab slice per rank; records all-gathered over NCCL each step
+        t = ShardedDecodeTail(cfg.vocab, cfg.n_embd, device=local, max_streams=B,
+                              max_top_k=max(cfg.top_k, 1), history_cap=cfg.hist,
+                              sampler=L.LAL_SAMPLER_LIBRARY)
+    else:
+        t = L.DecodeTail(cfg.vocab, cfg.n_embd, max_streams=B, max_top_k=max(cfg.top_k, 1),
+                         history_cap=cfg.hist, sampler=L.LAL_SAMPLER_LIBRARY, device=local)
     # LM head slice: fp32 rows generated in blocks, quantized on the GPU
     blk = 8192
     for r in range(0, t.n_rows, blk):
@@ -301,26 +305,44 @@ def run_ours(args, cfg):
     d_hid = torch.from_numpy(hid[W:W + K]).to(local)
     d_u = torch.from_numpy(us[W:W + K]).to(local)
     d_tok = torch.empty((K, B), dtype=torch.int32, device=local)
+    n_ev = 1 if flush is None else K
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-          for _ in range(K)]
-    t.set_timing(True)
+          for _ in range(n_ev)]
     barrier()
     with ClockSampler(local) as clk:
-        for i in range(K):
-            if flush is not None:
-                flush.zero_()       # evict the slice from L2 (not timed)
-                torch.cuda.current_stream().synchronize()
-            ev[i][0].record(stream)
-            t.step_device(d_hid[i].data_ptr(), B, d_u[i].data_ptr(), d_tok[i].data_ptr())
-            ev[i][1].record(stream)
+        if flush is None:
+            # back-to-back steps (the slice is larger than L2): one bracket
+            ev[0][0].record(stream)
+            for i in range(K):
+                t.step_device(d_hid[i].data_ptr(), B, d_u[i].data_ptr(), d_tok[i].data_ptr())
+            ev[0][1].record(stream)
+        else:
+            # a slice may fit in L2: a 256 MB write on the same stream evicts
+            # it before each step, outside the step's event pair (the host
+            # enqueues the step while the flush runs, so no idle gap is timed)
+            for i in range(K):
+                with torch.cuda.stream(stream):
+                    flush.zero_()
+                ev[i][0].record(stream)
+                t.step_device(d_hid[i].data_ptr(), B, d_u[i].data_ptr(), d_tok[i].data_ptr())
+                ev[i][1].record(stream)
         t.sync()
         barrier()
-    if flush is None:   # back-to-back steps: one bracket around all K
-        dev_ms = ev[0][0].elapsed_time(ev[-1][1])
-    else:               # L2 flushed between steps: sum the steps
         dev_ms = sum(a.elapsed_time(b) for a, b in ev)
-    kern_ms, n_launch = t.kernel_time()
-    t.set_timing(False)
+
+        # ---- kernel duration for the roofline: the same steps again with a
+        # CUDA-event pair around every fused launch on the context's stream ----
+        t.set_timing(True)
+        t.kernel_time()
+        for i in range(K):
+            if flush is not None:
+                with torch.cuda.stream(stream):
+                    flush.zero_()
+            t.step_device(d_hid[i].data_ptr(), B, d_u[i].data_ptr(), d_tok[i].data_ptr())
+        t.sync()
+        kern_ms, n_launch = t.kernel_time()
+        t.set_timing(False)
+        barrier()
 
     # ---- e2e: host buffers through lal_tail_step ----
     barrier()
@@ -347,8 +369,9 @@ def run_ours(args, cfg):
         peaks, pk_kind = load_peaks()
         rows = t.n_rows
         # one fused launch per stream: each streams this slice's W and scales
-        # once and reads / writes one stream's hidden, history and token
-        launches_per_step = B
+        # once and reads / writes one stream's hidden, history and token; a
+        # sharded step adds one merge launch (the NCCL all-gather is not ours)
+        launches_per_step = B + (1 if world > 1 else 0)
         alg = algorithmic_bytes(cfg, 1, rows)
         achieved = alg / (kern_ms * 1e-3) / 1e9
         peak = float(peaks["hbm_gbs"])

@@ -32,6 +32,7 @@
 #define LAL_TAIL_H
 
 #include <stdint.h>
+#include <stddef.h>
 
 #ifdef __cplusplus
 extern "C" {
@@ -175,6 +176,31 @@ int lal_tail_step_device(lal_tail *t, const float *d_hidden, int n_streams,
 /* Wait for the context's stream; returns a device-side error if one was
  * recorded (e.g. LAL_TAIL_ERR_TIMEOUT). */
 int lal_tail_sync(lal_tail *t);
+
+/* Host staging of one step's inputs (pinned copy, then one H2D into the
+ * context's device buffers, see lal_tail_device_buffers) and the matching
+ * read of the tokens (D2H + wait + status check).  lal_tail_step is
+ * stage_inputs + the step on the device buffers + fetch_tokens. */
+int lal_tail_stage_inputs(lal_tail *t, const float *hidden, int n_streams, const float *u);
+int lal_tail_fetch_tokens(lal_tail *t, int n_streams, int *tokens_out);
+
+/* Vocab-sharded step (shard_count > 1; no counterpart in the reference,
+ * which samples from one process).  Per step, on every rank, in order on the
+ * context's stream:
+ *   1. lal_tail_shard_select: the fused kernel over this rank's slice writes,
+ *      per stream, a candidate record (its tie-complete local top-k set, in
+ *      ascending vocab order) into the send buffer;
+ *   2. the caller all-gathers bytes_per_rank bytes of the send buffer of
+ *      every rank into the receive buffer, in rank order, on the context's
+ *      stream (ncclAllGather or any equivalent);
+ *   3. lal_tail_shard_merge: every rank merges the same records and draws
+ *      the same token (the unsharded step's result, bit for bit), pushes it
+ *      into its history copy and writes d_tokens_out.
+ * A failing shard (status in its record) fails the step on every rank. */
+int lal_tail_shard_select(lal_tail *t, const float *d_hidden, int n_streams);
+int lal_tail_exchange_buffers(lal_tail *t, int n_streams, void **d_send, void **d_recv,
+                              size_t *bytes_per_rank);
+int lal_tail_shard_merge(lal_tail *t, int n_streams, const float *d_u, int *d_tokens_out);
 /* Diagnostics and penalised logits (this slice's rows) of the last step. */
 int lal_tail_get_diag(lal_tail *t, int stream, lal_tail_diag *out);
 int lal_tail_get_logits(lal_tail *t, int stream, float *logits_rows);

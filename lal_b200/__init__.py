@@ -111,6 +111,12 @@ SIGNATURES = {
     "lal_tail_step": (C.c_int, [_vp, _f32p, _ip, _f32p, _i32p]),
     "lal_tail_step_device": (C.c_int, [_vp, _vp, _ip, _vp, _vp]),
     "lal_tail_sync": (C.c_int, [_vp]),
+    "lal_tail_stage_inputs": (C.c_int, [_vp, _f32p, _ip, _f32p]),
+    "lal_tail_fetch_tokens": (C.c_int, [_vp, _ip, _i32p]),
+    "lal_tail_shard_select": (C.c_int, [_vp, _vp, _ip]),
+    "lal_tail_exchange_buffers": (C.c_int, [_vp, _ip, C.POINTER(_vp), C.POINTER(_vp),
+                                            C.POINTER(C.c_size_t)]),
+    "lal_tail_shard_merge": (C.c_int, [_vp, _ip, _vp, _vp]),
     "lal_tail_get_diag": (C.c_int, [_vp, _ip, C.POINTER(TailDiag)]),
     "lal_tail_get_logits": (C.c_int, [_vp, _ip, _f32p]),
     "lal_tail_device_buffers": (C.c_int, [_vp, C.POINTER(_vp), C.POINTER(_vp), C.POINTER(_vp)]),
@@ -345,3 +351,29 @@ class DecodeTail:
 
     def sync(self):
         _check(lib().lal_tail_sync(self.h))
+
+    # ---- host staging and the vocab-sharded step ----
+    def stage_inputs(self, hidden: np.ndarray, u: np.ndarray) -> int:
+        hidden = np.ascontiguousarray(hidden, np.float32)
+        B = 1 if hidden.ndim == 1 else hidden.shape[0]
+        u = np.ascontiguousarray(u, np.float32).reshape(-1)
+        _check(lib().lal_tail_stage_inputs(self.h, hidden.reshape(-1), B, u))
+        return B
+
+    def fetch_tokens(self, n_streams: int) -> np.ndarray:
+        tok = np.empty(n_streams, np.int32)
+        _check(lib().lal_tail_fetch_tokens(self.h, n_streams, tok))
+        return tok
+
+    def shard_select(self, d_hidden: int, n_streams: int):
+        _check(lib().lal_tail_shard_select(self.h, d_hidden, n_streams))
+
+    def exchange_buffers(self, n_streams: int):
+        """(send pointer, receive pointer, bytes per rank) of the sharded step."""
+        a, b, n = C.c_void_p(), C.c_void_p(), C.c_size_t()
+        _check(lib().lal_tail_exchange_buffers(self.h, n_streams, C.byref(a), C.byref(b),
+                                               C.byref(n)))
+        return a.value, b.value, n.value
+
+    def shard_merge(self, n_streams: int, d_u: int, d_tokens: int):
+        _check(lib().lal_tail_shard_merge(self.h, n_streams, d_u, d_tokens))

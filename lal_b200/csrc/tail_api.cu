@@ -800,6 +800,10 @@ struct lal_tail {
     int ev_used = 0;
     unsigned long long *phase_ts = nullptr;    /* [(kMaxGrid+1)*8] when on */
     bool phases = false;
+    /* vocab-sharded step: this rank's records [max_streams][rec_bytes] and
+     * the gathered records of all ranks [shard_count][n][rec_bytes] */
+    int rec_cap = 0, rec_bytes = 0, merge_cap = 0;
+    uint8_t *x_send = nullptr, *x_recv = nullptr;
 };
 
 namespace {
@@ -809,7 +813,8 @@ void destroy_ctx(lal_tail *t) {
     if (t->device >= 0) cudaSetDevice(t->device);
     if (t->stream) cudaStreamSynchronize(t->stream);
     void *bufs[] = {t->W, t->sw, t->io_in, t->io_out, t->logits, t->temp, t->topk, t->pen,
-                    t->hist_ids, t->hist_n, t->hist_head, t->diag, t->phase_ts};
+                    t->hist_ids, t->hist_n, t->hist_head, t->diag, t->phase_ts,
+                    t->x_send, t->x_recv};
     for (void *b : bufs)
         if (b) cudaFree(b);
     t->sel.free_all();
@@ -864,6 +869,20 @@ int ctx_alloc(lal_tail *t) {
     if (t->grid < 1)
         return fail(LAL_TAIL_ERR_UNSUPPORTED, "fused tail: shape V=%d d=%d k=%d unsupported (plan %d)",
                     c.vocab_size, d, c.max_top_k, t->grid);
+    /* candidate records of the sharded step: a slice exports its
+     * tie-complete set, k entries plus room for ties at its threshold */
+    const int want = (std::min(c.max_top_k, c.vocab_size) + 64 + 3) / 4 * 4;
+    t->rec_cap = std::min(want, (t->nrows + 3) / 4 * 4);
+    t->rec_bytes = shard_record_bytes(t->rec_cap);
+    t->merge_cap = merge_smem_cap(c.shard_count * t->rec_cap);
+    if (t->merge_cap < 1)
+        return fail(LAL_TAIL_ERR_UNSUPPORTED,
+                    "sharded merge: %d shards x %d candidates exceed shared memory",
+                    c.shard_count, t->rec_cap);
+    CU(cudaMalloc(&t->x_send, (size_t)B * t->rec_bytes));
+    CU(cudaMemset(t->x_send, 0, (size_t)B * t->rec_bytes));
+    CU(cudaMalloc(&t->x_recv, (size_t)c.shard_count * B * t->rec_bytes));
+    CU(cudaMemset(t->x_recv, 0, (size_t)c.shard_count * B * t->rec_bytes));
     return LAL_TAIL_OK;
 }
 
@@ -873,11 +892,18 @@ int ctx_check(lal_tail *t) {
     return LAL_TAIL_OK;
 }
 
-/* Enqueue the fused kernel for streams [0, n) on the context stream. */
-int enqueue_step(lal_tail *t, const float *d_hidden, int n, const float *d_u, int *d_tokens) {
+/* Enqueue the fused kernel for streams [0, n) on the context stream; with
+ * shard_export, each launch writes stream b's candidate record into x_send
+ * instead of sampling (d_u and d_tokens unused). */
+int enqueue_step(lal_tail *t, const float *d_hidden, int n, const float *d_u, int *d_tokens,
+                 bool shard_export = false) {
     if (!t->loaded) return fail(LAL_TAIL_ERR_STATE, "step before the LM head was loaded");
     if (n < 1 || n > t->cfg.max_streams) return fail(LAL_TAIL_ERR_ARG, "n_streams %d out of range", n);
     if (t->n_set < n) return fail(LAL_TAIL_ERR_STATE, "sampling parameters not set for %d streams", n);
+    if (!shard_export && t->cfg.shard_count > 1)
+        return fail(LAL_TAIL_ERR_STATE,
+                    "vocab-sharded context: step with lal_tail_shard_select, an all-gather of "
+                    "the records and lal_tail_shard_merge");
     const int hc = std::max(1, t->cfg.history_cap);
     for (int b = 0; b < n; ++b) {
         TailParams p = t->plan;
@@ -894,8 +920,13 @@ int enqueue_step(lal_tail *t, const float *d_hidden, int n, const float *d_u, in
         p.hist_head = t->hist_head + b;
         p.hist_cap = t->cfg.history_cap;
         p.push_history = t->cfg.history_cap > 0 ? 1 : 0;
-        p.tokens = d_tokens + b;
+        p.tokens = shard_export ? nullptr : d_tokens + b;
+        p.u = shard_export ? t->temp + b : d_u + b; /* read, unused */
         p.diag = t->diag + b;
+        if (shard_export) {
+            p.shard_out = t->x_send + (size_t)b * t->rec_bytes;
+            p.rec_cap = t->rec_cap;
+        }
         t->sel.fill(p);
         p.status = t->io_out + t->cfg.max_streams;
         p.phase_ts = t->phases ? t->phase_ts : nullptr;
@@ -1133,6 +1164,96 @@ int lal_tail_step(lal_tail *t, const float *hidden, int n_streams, const float *
                                                    : "candidate set above the built capacity");
     }
     memcpy(tokens_out, t->h_out, 4ull * n_streams);
+    return LAL_TAIL_OK;
+}
+
+int lal_tail_stage_inputs(lal_tail *t, const float *hidden, int n_streams, const float *u) {
+    CHECK(ctx_check(t));
+    if (!hidden || !u) return fail(LAL_TAIL_ERR_ARG, "stage_inputs: null argument");
+    if (n_streams < 1 || n_streams > t->cfg.max_streams)
+        return fail(LAL_TAIL_ERR_ARG, "n_streams %d out of range", n_streams);
+    const int B = t->cfg.max_streams, d = t->cfg.n_embd;
+    memcpy(t->h_in, hidden, 4ull * n_streams * d);
+    float *hu = t->h_in + (size_t)n_streams * d;
+    memcpy(hu, u, 4ull * n_streams);
+    CU(cudaMemcpyAsync(t->io_in, t->h_in, 4ull * n_streams * d, cudaMemcpyHostToDevice, t->stream));
+    CU(cudaMemcpyAsync(t->io_in + (size_t)B * d, hu, 4ull * n_streams, cudaMemcpyHostToDevice,
+                       t->stream));
+    return LAL_TAIL_OK;
+}
+
+int lal_tail_fetch_tokens(lal_tail *t, int n_streams, int *tokens_out) {
+    CHECK(ctx_check(t));
+    if (!tokens_out || n_streams < 1 || n_streams > t->cfg.max_streams)
+        return fail(LAL_TAIL_ERR_ARG, "fetch_tokens: bad arguments");
+    const int B = t->cfg.max_streams;
+    CU(cudaMemcpyAsync(t->h_out, t->io_out, 4ull * n_streams, cudaMemcpyDeviceToHost, t->stream));
+    CU(cudaMemcpyAsync(t->h_out + B, t->io_out + B, 4, cudaMemcpyDeviceToHost, t->stream));
+    CU(cudaStreamSynchronize(t->stream));
+    const int status = t->h_out[B];
+    if (status != 0) {
+        CU(cudaMemset(t->io_out + B, 0, 4));
+        CHECK(t->sel.reset(t->stream));
+        CU(cudaStreamSynchronize(t->stream));
+        return fail(status, "device status %d (%s)", status,
+                    status == LAL_TAIL_ERR_TIMEOUT ? "bounded wait expired"
+                                                   : "candidate set above the built capacity");
+    }
+    memcpy(tokens_out, t->h_out, 4ull * n_streams);
+    return LAL_TAIL_OK;
+}
+
+int lal_tail_shard_select(lal_tail *t, const float *d_hidden, int n_streams) {
+    CHECK(ctx_check(t));
+    if (!d_hidden) return fail(LAL_TAIL_ERR_ARG, "shard_select: null hidden");
+    return enqueue_step(t, d_hidden, n_streams, nullptr, nullptr, true);
+}
+
+int lal_tail_exchange_buffers(lal_tail *t, int n_streams, void **d_send, void **d_recv,
+                              size_t *bytes_per_rank) {
+    if (!t) return fail(LAL_TAIL_ERR_ARG, "null context");
+    if (n_streams < 1 || n_streams > t->cfg.max_streams)
+        return fail(LAL_TAIL_ERR_ARG, "n_streams %d out of range", n_streams);
+    if (d_send) *d_send = t->x_send;
+    if (d_recv) *d_recv = t->x_recv;
+    if (bytes_per_rank) *bytes_per_rank = (size_t)n_streams * t->rec_bytes;
+    return LAL_TAIL_OK;
+}
+
+int lal_tail_shard_merge(lal_tail *t, int n_streams, const float *d_u, int *d_tokens_out) {
+    CHECK(ctx_check(t));
+    if (!d_u || !d_tokens_out) return fail(LAL_TAIL_ERR_ARG, "shard_merge: null argument");
+    if (n_streams < 1 || n_streams > t->cfg.max_streams)
+        return fail(LAL_TAIL_ERR_ARG, "n_streams %d out of range", n_streams);
+    if (t->n_set < n_streams)
+        return fail(LAL_TAIL_ERR_STATE, "sampling parameters not set for %d streams", n_streams);
+    MergeParams m;
+    memset(&m, 0, sizeof(m));
+    m.recv = t->x_recv;
+    m.rank_stride = (long long)n_streams * t->rec_bytes;
+    m.rec_bytes = t->rec_bytes;
+    m.rec_cap = t->rec_cap;
+    m.n_ranks = t->cfg.shard_count;
+    m.vocab = t->cfg.vocab_size;
+    m.variant = t->cfg.sampler == LAL_SAMPLER_SERVER ? VARIANT_SERVER : VARIANT_LIBRARY;
+    m.temperature = t->temp;
+    m.top_k = t->topk;
+    m.u = d_u;
+    m.hist_ids = t->hist_ids;
+    m.hist_n = t->hist_n;
+    m.hist_head = t->hist_head;
+    m.hist_cap = t->cfg.history_cap;
+    m.push_history = t->cfg.history_cap > 0 ? 1 : 0;
+    m.tokens = d_tokens_out;
+    m.diag = t->diag;
+    m.status = t->io_out + t->cfg.max_streams;
+    m.expf_x = t->ds->d_expf_x;
+    m.expf_y = t->ds->d_expf_y;
+    m.expf_n = t->ds->expf_n;
+    m.expf_bits = t->ds->d_expf_bits;
+    m.expf_off = t->ds->d_expf_off;
+    m.smem_cap = t->merge_cap;
+    CU(launch_merge(m, n_streams, t->stream));
     return LAL_TAIL_OK;
 }
 

@@ -30,6 +30,8 @@ constexpr int kLocalMaxK = 64;
 constexpr int kExpfBitmapWords = ((0x7F800000u >> 8) >> 5) + 1;
 /* Largest per-CTA row slice (smem holds its logits, scales, penalty counts). */
 constexpr int kMaxRowsPerCta = 4096;
+/* Largest shard count of a vocab-sharded context. */
+constexpr int kMaxRanks = 64;
 
 enum Mode : int { MODE_FUSED = 0, MODE_LMHEAD = 1, MODE_SAMPLE = 2 };
 enum Variant : int { VARIANT_LIBRARY = 0, VARIANT_SERVER = 1 };
@@ -41,6 +43,43 @@ enum DevStatus : int { DEV_OK = 0, DEV_TIMEOUT = 4, DEV_CAPACITY = 5 };
 struct StreamDiag {
     float threshold, max_l, sum, r;
     int n_cand, greedy, drew, token;
+};
+
+/* Vocab-sharded step: the candidate record one shard exports per stream.
+ * A 16-byte header, then cap values and cap global vocab indices, ascending
+ * index order: the shard's tie-complete set {l >= T_shard}, T_shard its own
+ * k-th largest penalised logit.  Every global candidate {l >= T} lies in
+ * some shard's set (T >= T_shard), so the union of the records carries the
+ * whole step. */
+struct ShardRecordHead {
+    int count;        /* candidates in the record                             */
+    int status;       /* DEV_* of the shard's launch (0 = ok)                 */
+    unsigned seq;     /* step sequence number (peer exchange)                 */
+    int pad;
+};
+inline int shard_record_bytes(int cap) { return 16 + 8 * cap; }
+
+/* Merge of the gathered records of one stream (one CTA per stream): the
+ * records of stream b from rank r are at recv + (r * rank_stride +
+ * b * rec_bytes). */
+struct MergeParams {
+    const uint8_t *recv;
+    long long rank_stride;
+    int rec_bytes, rec_cap, n_ranks;
+    int vocab, variant;
+    const float *temperature;
+    const int *top_k;
+    const float *u;
+    int *hist_ids, *hist_n, *hist_head;
+    int hist_cap, push_history;
+    int *tokens;
+    StreamDiag *diag;
+    int *status;
+    const uint32_t *expf_x, *expf_y;
+    int expf_n;
+    const uint32_t *expf_bits;
+    const uint32_t *expf_off;
+    int smem_cap;     /* candidates the CTA's shared memory holds             */
 };
 
 struct TailParams {
@@ -92,6 +131,10 @@ struct TailParams {
     int *cand_idx_out;
     int cand_out_cap;
     int candidates_only;     /* stop after exporting candidates (no draw)     */
+    /* vocab-sharded step: write this stream's candidate record (status,
+     * count, ascending-index list of at most rec_cap) and stop */
+    uint8_t *shard_out;
+    int rec_cap;
     /* glibc expf fix-ups; expf_bits has one bit per 256 consecutive negative
      * float bit patterns, set where the table holds an entry */
     const uint32_t *expf_x, *expf_y;
@@ -149,6 +192,10 @@ inline int effective_k(float temperature, int top_k, int vocab, int rows) {
 
 /* Host-side launchers (tail_kernels.cu). */
 cudaError_t launch_finish(const FinishParams &f, cudaStream_t st);
+cudaError_t launch_merge(const MergeParams &m, int n_streams, cudaStream_t st);
+/* candidates a merge CTA can hold (the gathered records of one stream), or
+ * -1 when n_candidates_max does not fit in shared memory */
+int merge_smem_cap(int n_candidates_max);
 int plan_launch(TailParams &p, int num_sms, int min_rows_per_cta);
 cudaError_t launch_tail(const TailParams &p, int grid, cudaStream_t st);
 cudaError_t launch_quantize_x(const float *x, int8_t *xq, float *scale, int n,

@@ -1018,8 +1018,17 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
     }
     if (!fine) {
         if (tid == 0) {
-            if (dev_status == 0) atomicCAS(p.status, 0, ok ? (int)DEV_CAPACITY : (int)DEV_TIMEOUT);
-            p.tokens[0] = -1;
+            const int st = ok ? (int)DEV_CAPACITY : (int)DEV_TIMEOUT;
+            /* a shard reports through its record: the merge fails the step
+             * on every rank alike */
+            if (dev_status == 0 && p.shard_out == nullptr) atomicCAS(p.status, 0, st);
+            if (p.shard_out != nullptr) {
+                ShardRecordHead *h = reinterpret_cast<ShardRecordHead *>(p.shard_out);
+                h->count = 0;
+                h->status = st;
+            } else {
+                p.tokens[0] = -1;
+            }
             p.diag[0] = dg;
         }
         return;
@@ -1074,6 +1083,24 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
             p.cand_val_out[i] = Ov[i];
             p.cand_idx_out[i] = Oi[i];
         }
+    }
+    if (p.shard_out != nullptr) {
+        /* vocab-sharded step: this slice's record; the merge draws */
+        ShardRecordHead *h = reinterpret_cast<ShardRecordHead *>(p.shard_out);
+        float *rv = reinterpret_cast<float *>(p.shard_out + sizeof(ShardRecordHead));
+        int *ri = reinterpret_cast<int *>(rv + p.rec_cap);
+        const bool fits = m <= p.rec_cap;
+        if (fits)
+            for (int i = tid; i < m; i += NT) {
+                rv[i] = Ov[i];
+                ri[i] = Oi[i];
+            }
+        if (tid == 0) {
+            h->count = fits ? m : 0;
+            h->status = fits ? 0 : (int)DEV_CAPACITY;
+            p.diag[0] = dg;
+        }
+        return;
     }
     if (p.candidates_only) {
         if (tid == 0) p.diag[0] = dg;
@@ -1308,6 +1335,171 @@ __global__ void debug_expf_kernel(const float *x, float *y, int n, const uint32_
     if (i < n) y[i] = sampler_expf(x[i], tx, ty, bits, off);
 }
 
+/* Vocab-sharded step, second half: CTA b merges stream b's records from every
+ * rank and samples exactly as the unsharded last CTA does.  The records are
+ * concatenated in rank order; the slices are contiguous and rank-ordered, so
+ * the concatenation is in ascending vocab order, the order of the
+ * reference's sequential softmax sums (runtime/lal_sampling.h:110-124).
+ * Every rank runs the same merge on the same bytes and gets the same token. */
+__global__ void __launch_bounds__(NT) merge_kernel(const MergeParams mp) {
+    extern __shared__ __align__(16) uint8_t msm[];
+    __shared__ Misc msh;
+    __shared__ int roff[kMaxRanks + 1];
+    __shared__ int rbad;
+    Misc *ms = &msh;
+    const int tid = threadIdx.x, b = blockIdx.x;
+    const int cap = mp.smem_cap;
+    uint32_t *Mk = reinterpret_cast<uint32_t *>(msm);
+    int *Mi = reinterpret_cast<int *>(Mk + cap);
+    float *Cv = reinterpret_cast<float *>(Mi + cap);
+    int *Ci = reinterpret_cast<int *>(Cv + cap);
+    float *Ce = reinterpret_cast<float *>(Ci + cap);
+
+    const float temp = mp.temperature[b];
+    const int topk = mp.top_k[b];
+    const float u0 = mp.u[b];
+    const int hn = mp.hist_n ? mp.hist_n[b] : 0;
+    const int hhead = mp.hist_head ? mp.hist_head[b] : 0;
+    const bool greedy = (temp <= 0.0f) || (topk <= 0);
+    auto rec = [&](int r) { return mp.recv + r * mp.rank_stride + (long long)b * mp.rec_bytes; };
+    if (tid == 0) {
+        int acc = 0, st = 0;
+        for (int r = 0; r < mp.n_ranks; ++r) {
+            const ShardRecordHead *h = reinterpret_cast<const ShardRecordHead *>(rec(r));
+            const int c = h->count, s = h->status;
+            if (s != 0 && st == 0) st = s;
+            if ((c < 0 || c > mp.rec_cap) && st == 0) st = DEV_CAPACITY;
+            roff[r] = acc;
+            acc += (c < 0 || c > mp.rec_cap) ? 0 : c;
+        }
+        roff[mp.n_ranks] = acc;
+        if ((acc < 1 || acc > cap) && st == 0) st = DEV_CAPACITY;
+        rbad = st;
+    }
+    __syncthreads();
+    StreamDiag dg;
+    dg.threshold = 0.0f;
+    dg.max_l = 0.0f;
+    dg.sum = 0.0f;
+    dg.r = 0.0f;
+    dg.n_cand = 0;
+    dg.greedy = greedy ? 1 : 0;
+    dg.drew = 0;
+    dg.token = -1;
+    if (rbad != 0) {
+        if (tid == 0) {
+            atomicCAS(mp.status, 0, rbad);
+            mp.tokens[b] = -1;
+            mp.diag[b] = dg;
+        }
+        return;
+    }
+    const int M = roff[mp.n_ranks];
+    for (int r = 0; r < mp.n_ranks; ++r) {
+        const int c = roff[r + 1] - roff[r];
+        const float *rv = reinterpret_cast<const float *>(rec(r) + sizeof(ShardRecordHead));
+        const int *ri = reinterpret_cast<const int *>(rv + mp.rec_cap);
+        for (int i = tid; i < c; i += NT) {
+            Mk[roff[r] + i] = f2key(rv[i]);
+            Mi[roff[r] + i] = ri[i];
+        }
+    }
+    __syncthreads();
+    /* k = min(top_k, V) (runtime/lal_sampling.h:70-71), 1 for greedy; every
+     * shard exported at least min(k, its rows) entries, so M >= k */
+    int k = greedy ? 1 : topk;
+    if (k > mp.vocab) k = mp.vocab;
+    if (k > M) k = M;
+    if (k < 1) k = 1;
+    const uint32_t T = block_kth_largest(
+        [&](int i, uint32_t &key) {
+            key = Mk[i];
+            return true;
+        },
+        M, k, ms);
+    /* candidates {l >= T}, order kept (stable compaction) */
+    const int seg = (M + NT - 1) / NT;
+    const int e0 = min(M, tid * seg), e1 = min(M, e0 + seg);
+    uint32_t c = 0;
+    for (int e = e0; e < e1; ++e) c += Mk[e] >= T;
+    uint32_t mt;
+    uint32_t pos = block_scan_excl(c, ms, &mt);
+    const int m = (int)mt;
+    for (int e = e0; e < e1; ++e)
+        if (Mk[e] >= T) {
+            Cv[pos] = key2f(Mk[e]);
+            Ci[pos] = Mi[e];
+            ++pos;
+        }
+    __syncthreads();
+    dg.threshold = key2f(T);
+    dg.n_cand = m;
+    float mx = -1e30f;
+    for (int i = tid; i < m; i += NT) mx = fmaxf(mx, Cv[i]);
+    const float max_l = block_max_f(mx, ms);
+    dg.max_l = max_l;
+    int token;
+    if (greedy) {
+        token = Ci[0];
+    } else {
+        for (int i = tid; i < m; i += NT) {
+            const float x = __fdiv_rn(__fsub_rn(Cv[i], max_l), temp);
+            Ce[i] = sampler_expf(x, mp.expf_x, mp.expf_y, mp.expf_bits, mp.expf_off);
+        }
+        __syncthreads();
+        if (tid == 0) {
+            float acc = 0.0f;
+            for (int i = 0; i < m; ++i) {
+                acc = __fadd_rn(acc, Ce[i]);
+                Ce[i] = acc;
+            }
+            ms->sum = acc;
+            ms->found = 0x7fffffff;
+        }
+        __syncthreads();
+        const float sum = ms->sum;
+        dg.sum = sum;
+        if (mp.variant == VARIANT_SERVER && sum <= 0.0f) {
+            /* tools/server/qwen7b_server.c:285-286 */
+            token = 0;
+            float bv = -1e30f;
+            for (int i = 0; i < m; ++i)
+                if (Cv[i] > bv) {
+                    bv = Cv[i];
+                    token = Ci[i];
+                }
+        } else {
+            const float r = __fmul_rn(u0, sum);
+            dg.r = r;
+            dg.drew = 1;
+            int first = 0x7fffffff;
+            for (int i = tid; i < m; i += NT)
+                if (r <= Ce[i]) {
+                    first = i;
+                    break;
+                }
+            if (first != 0x7fffffff) atomicMin(&ms->found, first);
+            __syncthreads();
+            token = ms->found != 0x7fffffff ? Ci[ms->found] : mp.vocab - 1;
+        }
+    }
+    if (tid == 0) {
+        dg.token = token;
+        mp.tokens[b] = token;
+        mp.diag[b] = dg;
+        if (mp.push_history && mp.hist_cap > 0) {
+            int *ids = mp.hist_ids + (size_t)b * mp.hist_cap;
+            if (hn < mp.hist_cap) {
+                ids[hn] = token;
+                mp.hist_n[b] = hn + 1;
+            } else {
+                ids[hhead] = token;
+                mp.hist_head[b] = (hhead + 1) % mp.hist_cap;
+            }
+        }
+    }
+}
+
 /* -------------------------------------------------- host planning --- */
 template <int MODE>
 void *pick_kernel(int nch) {
@@ -1402,24 +1594,28 @@ int plan_launch(TailParams &p, int num_sms, int min_rows_per_cta) {
     return G;
 }
 
+/* Raise a kernel's dynamic shared-memory limit once per (device, kernel). */
+cudaError_t raise_smem(const void *fn, int bytes) {
+    thread_local std::vector<std::pair<int, const void *>> raised;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    for (const auto &r : raised)
+        if (r.first == dev && r.second == fn) return cudaSuccess;
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e != cudaSuccess) return e;
+    raised.emplace_back(dev, fn);
+    return cudaSuccess;
+}
+
 cudaError_t launch_tail(const TailParams &p, int grid, cudaStream_t st) {
     void *fn = nullptr;
     if (p.mode == MODE_FUSED) fn = pick_kernel<MODE_FUSED>(p.nch);
     else if (p.mode == MODE_LMHEAD) fn = pick_kernel<MODE_LMHEAD>(p.nch);
     else fn = (void *)tail_kernel<MODE_SAMPLE, 1>;
     if (!fn) return cudaErrorInvalidValue;
-    /* raise the dynamic shared-memory limit once per (device, kernel) */
-    thread_local std::vector<std::pair<int, void *>> raised;
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
+    cudaError_t e = raise_smem(fn, kSmemLimit);
     if (e != cudaSuccess) return e;
-    bool done = false;
-    for (const auto &r : raised) done |= (r.first == dev && r.second == fn);
-    if (!done) {
-        e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
-        if (e != cudaSuccess) return e;
-        raised.emplace_back(dev, fn);
-    }
     void *args[] = {const_cast<TailParams *>(&p)};
     /* The select's grid barriers need every CTA resident: a cooperative
      * launch guarantees it (or fails to launch). */
@@ -1449,6 +1645,24 @@ cudaError_t launch_quantize_rows(const float *W, int d, int8_t *q, int ld, float
 
 cudaError_t launch_finish(const FinishParams &f, cudaStream_t st) {
     finish_kernel<<<1, NT, 0, st>>>(f);
+    return cudaGetLastError();
+}
+
+/* Five words per candidate: gathered key + index, candidate value + index,
+ * weight / running sum; the static part (Misc, rank offsets) stays below 8 KB. */
+constexpr int kMergeDynLimit = kSmemLimit - 8192;
+
+int merge_smem_cap(int n_candidates_max) {
+    return n_candidates_max <= kMergeDynLimit / 20 ? n_candidates_max : -1;
+}
+
+cudaError_t launch_merge(const MergeParams &m, int n_streams, cudaStream_t st) {
+    if (m.smem_cap < 1 || m.smem_cap > kMergeDynLimit / 20 || m.n_ranks < 1 ||
+        m.n_ranks > kMaxRanks)
+        return cudaErrorInvalidValue;
+    cudaError_t e = raise_smem((const void *)merge_kernel, kMergeDynLimit);
+    if (e != cudaSuccess) return e;
+    merge_kernel<<<n_streams, NT, 20ull * (size_t)m.smem_cap, st>>>(m);
     return cudaGetLastError();
 }
 
