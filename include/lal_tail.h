@@ -102,6 +102,21 @@ int lal_tail_sample_token_filtered(float *logits, int vocab_size, float temperat
                                    int n_recent, lal_filter_topk_fn filter,
                                    lal_token_decode_fn decode, lal_draw_fn draw,
                                    void *draw_ctx, int *token_out);
+/* lal_sample_token on logits already in device memory, allocating nothing
+ * (no counterpart in the reference, whose sampler runs on the host).  For
+ * callers that must not allocate device memory inside their decode loop:
+ * all working memory is a fixed static device region (2.1 MB of scratch +
+ * 3.1 MB for the expf table), so vocab_size <= 262144; larger sizes return
+ * LAL_TAIL_ERR_ARG.  d_logits [vocab_size] is penalised in place like the
+ * reference's logits; d_recent [n_recent] are device ids; u is the draw
+ * (used only on the non-greedy path); stream is a cudaStream_t (NULL = the
+ * legacy default stream); the call waits for its stream and writes the token
+ * to *token_out.  The first call on a device does the set-up with that device
+ * current: make it before any stream capture.  Calls that overlap on one
+ * device share the scratch and race: serialise them. */
+int lal_tail_sample_token_noalloc(float *d_logits, int vocab_size, float temperature,
+                                  int top_k, float rep_penalty, const int *d_recent,
+                                  int n_recent, float u, void *stream, int *token_out);
 /* Register (copy to the device) or drop a host LM head used by the range
  * drop-ins.  Registration is optional: first use registers on demand. */
 int lal_tail_lm_head_register(const int8_t *wte_q, const float *scale_w,

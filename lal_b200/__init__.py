@@ -117,6 +117,8 @@ SIGNATURES = {
     "lal_tail_exchange_buffers": (C.c_int, [_vp, _ip, C.POINTER(_vp), C.POINTER(_vp),
                                             C.POINTER(C.c_size_t)]),
     "lal_tail_shard_merge": (C.c_int, [_vp, _ip, _vp, _vp]),
+    "lal_tail_sample_token_noalloc": (C.c_int, [_vp, _ip, _fp, _ip, _fp, _vp, _ip, _fp, _vp,
+                                                C.POINTER(C.c_int)]),
     "lal_tail_get_diag": (C.c_int, [_vp, _ip, C.POINTER(TailDiag)]),
     "lal_tail_get_logits": (C.c_int, [_vp, _ip, _f32p]),
     "lal_tail_device_buffers": (C.c_int, [_vp, C.POINTER(_vp), C.POINTER(_vp), C.POINTER(_vp)]),

@@ -420,6 +420,10 @@ int sample_launch(DropinState *S, DeviceState *ds, float *logits, int V, float t
 
 }  // namespace
 
+namespace lal {
+int set_error(int code, const char *msg) { return fail(code, "%s", msg); }
+}  // namespace lal
+
 /* ======================================================================
  * 1. drop-ins and their status-returning forms
  * ====================================================================== */

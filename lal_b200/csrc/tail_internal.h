@@ -196,6 +196,17 @@ cudaError_t launch_merge(const MergeParams &m, int n_streams, cudaStream_t st);
 /* candidates a merge CTA can hold (the gathered records of one stream), or
  * -1 when n_candidates_max does not fit in shared memory */
 int merge_smem_cap(int n_candidates_max);
+
+/* Allocation-free sampler entry (tail_noalloc.cu): build the expf bitmap and
+ * offset index from a device copy of the sorted fix-up table (kernels, no
+ * host buffers); raise the SAMPLE kernel's shared-memory limit once; launch
+ * the SAMPLE kernel with that limit already raised. */
+cudaError_t launch_expf_index(const uint32_t *tx, int n, uint32_t *bits, uint32_t *off,
+                              cudaStream_t st);
+cudaError_t prepare_sample_kernel();
+cudaError_t launch_sample_prepared(const TailParams &p, int grid, cudaStream_t st);
+/* Records the calling thread's last error message (tail_api.cu). */
+int set_error(int code, const char *msg);
 int plan_launch(TailParams &p, int num_sms, int min_rows_per_cta);
 cudaError_t launch_tail(const TailParams &p, int grid, cudaStream_t st);
 cudaError_t launch_quantize_x(const float *x, int8_t *xq, float *scale, int n,

@@ -1666,6 +1666,56 @@ cudaError_t launch_merge(const MergeParams &m, int n_streams, cudaStream_t st) {
     return cudaGetLastError();
 }
 
+/* ---- support of the allocation-free sampler entry (tail_noalloc.cu) ---- */
+namespace {
+/* bit (b >> 8) of every table entry, b = bits(x) - 2^31 (the table holds
+ * negative x only, so b >> 8 < kExpfBitmapWords * 32) */
+__global__ void expf_bits_kernel(const uint32_t *tx, int n, uint32_t *bits) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) {
+        const uint32_t b = (tx[i] - 0x80000000u) >> 8;
+        atomicOr(bits + (b >> 5), 1u << (b & 31));
+    }
+}
+/* off[w] = first entry whose bitmap word is >= w (the table is sorted by bit
+ * pattern), for w in [0, words] */
+__global__ void expf_off_kernel(const uint32_t *tx, int n, uint32_t *off, int words) {
+    const int w = blockIdx.x * blockDim.x + threadIdx.x;
+    if (w > words) return;
+    int lo = 0, hi = n;
+    while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if (((tx[mid] - 0x80000000u) >> 13) >= (uint32_t)w) hi = mid;
+        else lo = mid + 1;
+    }
+    off[w] = (uint32_t)lo;
+}
+}  // namespace
+
+cudaError_t launch_expf_index(const uint32_t *tx, int n, uint32_t *bits, uint32_t *off,
+                              cudaStream_t st) {
+    cudaError_t e = cudaMemsetAsync(bits, 0, 4ull * kExpfBitmapWords, st);
+    if (e != cudaSuccess) return e;
+    if (n > 0) expf_bits_kernel<<<(n + 255) / 256, 256, 0, st>>>(tx, n, bits);
+    expf_off_kernel<<<(kExpfBitmapWords + 1 + 255) / 256, 256, 0, st>>>(tx, n, off,
+                                                                        kExpfBitmapWords);
+    return cudaGetLastError();
+}
+
+cudaError_t prepare_sample_kernel() {
+    return cudaFuncSetAttribute((const void *)tail_kernel<MODE_SAMPLE, 1>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+}
+
+cudaError_t launch_sample_prepared(const TailParams &p, int grid, cudaStream_t st) {
+    if (p.mode != MODE_SAMPLE) return cudaErrorInvalidValue;
+    void *fn = (void *)tail_kernel<MODE_SAMPLE, 1>;
+    void *args[] = {const_cast<TailParams *>(&p)};
+    if (p.local_edges)
+        return cudaLaunchKernel(fn, dim3(grid), dim3(NT), args, (size_t)p.smem_total, st);
+    return cudaLaunchCooperativeKernel(fn, dim3(grid), dim3(NT), args, (size_t)p.smem_total, st);
+}
+
 cudaError_t launch_debug_expf(const float *x, float *y, int n, const uint32_t *tx,
                               const uint32_t *ty, int tn, const uint32_t *bits,
                               const uint32_t *off, cudaStream_t st) {
