@@ -17,8 +17,9 @@
  *
  * Data movement: each CTA owns a contiguous slice of rows, which is one
  * contiguous byte range of the row-major LM head; a producer warp streams it
- * into a ring of shared-memory stages with cp.async.bulk (TMA, no
- * multicast, L2 evict-first) completing on mbarriers, and 8 consumer warps
+ * into a ring of shared-memory stages with cp.async.bulk (untiled TMA into
+ * this CTA's own shared memory, L2 evict-first) completing on mbarriers, and
+ * 8 consumer warps
  * each take whole rows: every lane holds its 16-byte columns of the quantized
  * vector in registers and does 4 dp4a per 16 bytes of weights; a warp
  * reduction (redux.sync) gives the exact int32 dot.
