@@ -138,6 +138,12 @@ int current_device(int *dev) {
 
 int ld_for(int d) { return (d + 15) / 16 * 16; }
 
+/* an environment switch is on when set to anything but "" or "0" */
+bool getenv_flag(const char *name) {
+    const char *v = getenv(name);
+    return v && v[0] && !(v[0] == '0' && v[1] == 0);
+}
+
 /* ---- growable device buffer ------------------------------------------- */
 struct DevBuf {
     void *p = nullptr;
@@ -808,6 +814,11 @@ struct lal_tail {
      * the gathered records of all ranks [shard_count][n][rec_bytes] */
     int rec_cap = 0, rec_bytes = 0, merge_cap = 0;
     uint8_t *x_send = nullptr, *x_recv = nullptr;
+    /* batched step (B >= 2): quantized vectors, scales, cached descriptors */
+    bool batch_ok = false;
+    int8_t *xq_b = nullptr;
+    float *sx_b = nullptr;
+    BatchPlan bplan;
 };
 
 namespace {
@@ -818,7 +829,7 @@ void destroy_ctx(lal_tail *t) {
     if (t->stream) cudaStreamSynchronize(t->stream);
     void *bufs[] = {t->W, t->sw, t->io_in, t->io_out, t->logits, t->temp, t->topk, t->pen,
                     t->hist_ids, t->hist_n, t->hist_head, t->diag, t->phase_ts,
-                    t->x_send, t->x_recv};
+                    t->x_send, t->x_recv, t->xq_b, t->sx_b};
     for (void *b : bufs)
         if (b) cudaFree(b);
     t->sel.free_all();
@@ -887,6 +898,14 @@ int ctx_alloc(lal_tail *t) {
     CU(cudaMemset(t->x_send, 0, (size_t)B * t->rec_bytes));
     CU(cudaMalloc(&t->x_recv, (size_t)c.shard_count * B * t->rec_bytes));
     CU(cudaMemset(t->x_recv, 0, (size_t)c.shard_count * B * t->rec_bytes));
+    /* batched step: one pass over W for all streams on the tensor cores */
+    if (B >= 2 && B <= 256) {
+        CU(cudaMalloc(&t->xq_b, (size_t)256 * t->ld));
+        CU(cudaMemset(t->xq_b, 0, (size_t)256 * t->ld));
+        CU(cudaMalloc(&t->sx_b, 4ull * 256));
+        t->batch_ok = batch_plan(t->bplan, t->W, t->sw, t->nrows, t->ld, t->ds->num_sms, t->xq_b,
+                                 t->sx_b, B, c.history_cap) == 0;
+    }
     return LAL_TAIL_OK;
 }
 
@@ -909,6 +928,48 @@ int enqueue_step(lal_tail *t, const float *d_hidden, int n, const float *d_u, in
                     "vocab-sharded context: step with lal_tail_shard_select, an all-gather of "
                     "the records and lal_tail_shard_merge");
     const int hc = std::max(1, t->cfg.history_cap);
+    if (t->batch_ok && n >= 2 && !getenv_flag("LAL_TAIL_PER_STREAM")) {
+        BatchStep bs;
+        memset(&bs, 0, sizeof(bs));
+        bs.hidden = d_hidden;
+        bs.d = t->cfg.n_embd;
+        bs.B = n;
+        bs.logits = t->logits;
+        bs.row_base = t->row0;
+        bs.vocab = t->cfg.vocab_size;
+        bs.variant = t->plan.variant;
+        bs.temperature = t->temp;
+        bs.top_k = t->topk;
+        bs.rep_penalty = t->pen;
+        bs.u = shard_export ? nullptr : d_u;
+        bs.hist_ids = t->hist_ids;
+        bs.hist_n = t->hist_n;
+        bs.hist_head = t->hist_head;
+        bs.hist_cap = t->cfg.history_cap;
+        bs.hist_stride = hc;
+        bs.push_history = shard_export ? 0 : (t->cfg.history_cap > 0 ? 1 : 0);
+        bs.tokens = d_tokens;
+        bs.diag = t->diag;
+        bs.status = t->io_out + t->cfg.max_streams;
+        bs.expf_x = t->ds->d_expf_x;
+        bs.expf_y = t->ds->d_expf_y;
+        bs.expf_n = t->ds->expf_n;
+        bs.expf_bits = t->ds->d_expf_bits;
+        bs.expf_off = t->ds->d_expf_off;
+        if (shard_export) {
+            bs.shard_out = t->x_send;
+            bs.rec_cap = t->rec_cap;
+            bs.rec_bytes = t->rec_bytes;
+        }
+        const bool time_it = t->timing && t->ev_used + 2 <= (int)t->ev.size();
+        if (time_it) CU(cudaEventRecord(t->ev[t->ev_used], t->stream));
+        CU(batch_launch(t->bplan, bs, t->stream));
+        if (time_it) {
+            CU(cudaEventRecord(t->ev[t->ev_used + 1], t->stream));
+            t->ev_used += 2;
+        }
+        return LAL_TAIL_OK;
+    }
     for (int b = 0; b < n; ++b) {
         TailParams p = t->plan;
         p.W = t->W;

@@ -1,0 +1,844 @@
+/*
+ * tail_batch.cu -- the batched decode tail (B >= 2 streams) on sm_100a.
+ *
+ * With B streams the LM-head contraction is a GEMM, logits[b][v] =
+ * (scale_x[b] * scale_w[v]) * sum_k xq[b][k] * W[v][k]; one pass over the
+ * 545 MB of W serves every stream.  Three launches per step:
+ *
+ *   quantize_batch_kernel  lal_quantize_x_int8 (runtime/lal_q8_kernel.h:375-442)
+ *                          for each stream: int8 rows X [N][ld] + scale_x [B];
+ *   gemm_i8_kernel         the 5th-gen tensor cores: tcgen05.mma kind::i8
+ *                          with int32 accumulators in tensor memory.  W is
+ *                          the M operand (128 vocab rows a tile), the B
+ *                          streams the N operand (N = B rounded up to 32, at
+ *                          most 256), K = d in 128-byte TMA boxes with the
+ *                          128-byte swizzle.  A persistent CTA per SM walks
+ *                          its tiles: warp 0 issues the TMA loads into a ring
+ *                          of shared-memory stages, warp 1 issues the MMAs
+ *                          (one thread) and owns the tensor memory, warps
+ *                          2-5 read the accumulators (tcgen05.ld), apply the
+ *                          reference's scale expression and store the logits
+ *                          [B][rows] (fp32, L2-resident for the next kernel).
+ *                          Two accumulator buffers let the epilogue of one
+ *                          tile overlap the MMAs of the next.  int8 products
+ *                          accumulate exactly in int32, so the logits equal
+ *                          the reference's bit for bit.
+ *   batch_select_kernel    one CTA per stream: the repetition penalty
+ *                          (runtime/lal_sampling.h:59-67; occurrences counted
+ *                          in a shared-memory hash of the history), a key
+ *                          histogram for a tie-complete superset of the top k,
+ *                          the exact threshold, the candidates in ascending
+ *                          vocab order, then the softmax sums and the draw
+ *                          exactly as the single-stream kernel, the history
+ *                          push, or (vocab-sharded) the stream's record.
+ *
+ * Every wait is bounded (kWaitNs); a wait that runs out sets DEV_TIMEOUT, the
+ * MMA issuer drains its MMAs before the tensor memory is released, and the
+ * producer waits for its copies in flight before the CTA exits.
+ */
+#include "tail_device.cuh"
+
+#include <cuda.h>
+
+#include <algorithm>
+#include <cstring>
+#include <mutex>
+
+namespace lal {
+namespace {
+
+constexpr int kBM = 128;           /* W rows per tile (MMA M)                  */
+constexpr int kBK = 128;           /* K bytes per TMA box = one swizzle row    */
+constexpr int kMmaK = 32;          /* K of one tcgen05.mma kind::i8            */
+constexpr int kGemmThreads = 192;  /* warp 0 TMA, warp 1 MMA, warps 2-5 epilogue */
+constexpr int kGemmStagesMax = 8;
+constexpr int kGemmSmemLimit = 232448;
+
+/* ------------------------------------------------------------ PTX --- */
+__device__ __forceinline__ uint64_t policy_evict_last() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y,
+                                            uint64_t *bar, uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        ".L2::cache_hint [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(pol)
+        : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+/* arrive on bar when every tcgen05.mma this thread issued before has completed */
+__device__ __forceinline__ void tc_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::
+                     "r"(smem_u32(bar))
+                 : "memory");
+}
+/* D[tmem] (+)= A[smem desc] * B[smem desc]^T, int8 x int8 -> int32 */
+__device__ __forceinline__ void tc_mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                          uint32_t idesc, uint32_t accumulate) {
+    const uint32_t mask0 = 0, mask1 = 0, mask2 = 0, mask3 = 0;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(
+            d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(mask0), "r"(mask1),
+        "r"(mask2), "r"(mask3));
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+        "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
+        "%28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+          "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+          "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+          "=r"(r[31])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_wait() {
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+/* Shared-memory matrix descriptor of a K-major tile written by TMA with the
+ * 128-byte swizzle: rows of 128 bytes, 8-row groups 1024 bytes apart (stride
+ * byte offset), leading byte offset unused (1), descriptor version 1, layout
+ * type 2 = 128-byte swizzle.  The tile base is 1024-byte aligned; a K step of
+ * 32 bytes inside the swizzle row advances the start address. */
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t)1u << 16;                 /* leading byte offset (unused) */
+    d |= (uint64_t)(1024u >> 4) << 32;       /* stride byte offset           */
+    d |= (uint64_t)1u << 46;                 /* version                      */
+    d |= (uint64_t)2u << 61;                 /* 128-byte swizzle             */
+    return d;
+}
+/* Instruction descriptor: int32 accumulate, signed int8 A and B, both K-major,
+ * N >> 3 at bit 17, M >> 4 at bit 24. */
+__host__ __device__ constexpr uint32_t idesc_i8(int M, int N) {
+    return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) |
+           ((uint32_t)(M >> 4) << 24);
+}
+
+/* -------------------------------------------------- batch quantize --- */
+__global__ void __launch_bounds__(NT) quantize_batch_kernel(const float *x, int d, int8_t *xq,
+                                                            int ld, float *scale_out) {
+    __shared__ Misc ms;
+    const int b = blockIdx.x;
+    const float *row = x + (size_t)b * d;
+    int8_t *out = xq + (size_t)b * ld;
+    float m = 0.0f;
+    for (int i = threadIdx.x; i < d; i += NT) m = fmaxf(m, fabsf(row[i]));
+    m = block_max_f(m, &ms);
+    float scale = __fdiv_rn(m, 127.0f);
+    if (scale < 1e-8f) scale = 1e-8f;
+    const float inv = __fdiv_rn(1.0f, scale);
+    const int n8 = d & ~7;
+    for (int i = threadIdx.x; i < ld; i += NT) {
+        int v = 0;
+        if (i < d) {
+            const float s = __fmul_rn(row[i], inv);
+            if (s != s) v = -127;
+            else {
+                v = (i < n8) ? __float2int_rn(s) : __float2int_rz(s);
+                v = v > 127 ? 127 : (v < -127 ? -127 : v);
+            }
+        }
+        out[i] = (int8_t)v;
+    }
+    if (threadIdx.x == 0) scale_out[b] = scale;
+}
+
+/* ---------------------------------------------------- the tcgen05 GEMM --- */
+struct GemmParams {
+    CUtensorMap tmW; /* [rows][ld] int8, box 128 x 128, 128-byte swizzle */
+    CUtensorMap tmX; /* [N][ld] int8, box 128 x N, 128-byte swizzle      */
+    const float *scale_w;
+    const float *scale_x;
+    float *logits; /* [B][rows] */
+    int rows, B, N, kblocks, stages, stage_bytes, tmem_cols;
+    int *status;
+};
+
+__device__ __forceinline__ bool bwait(uint64_t *b, uint32_t parity, volatile int *abort_flag) {
+    return mbar_wait(b, parity, abort_flag);
+}
+
+__global__ void __launch_bounds__(kGemmThreads, 1) gemm_i8_kernel(const __grid_constant__ GemmParams p) {
+    extern __shared__ uint8_t gsm_raw[];
+    uint8_t *gsm = gsm_raw + ((1024u - (smem_u32(gsm_raw) & 1023u)) & 1023u);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    uint64_t *full = reinterpret_cast<uint64_t *>(gsm + (size_t)p.stages * p.stage_bytes);
+    uint64_t *empty = full + kGemmStagesMax;
+    uint64_t *tfull = empty + kGemmStagesMax;
+    uint64_t *tempty = tfull + 2;
+    uint64_t *drain = tempty + 2;
+    uint32_t *tholder = reinterpret_cast<uint32_t *>(drain + 1);
+    int *abort_i = reinterpret_cast<int *>(tholder + 1);
+    volatile int *abort_flag = abort_i;
+    /* the drains at exit wait on time alone (never on the abort flag): no
+     * copy or MMA may be in flight when the CTA leaves */
+    volatile int *never = reinterpret_cast<int *>(tholder + 2);
+    float *sx = reinterpret_cast<float *>(tholder + 4);
+    const int n_tiles = (p.rows + kBM - 1) / kBM;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < p.stages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&tfull[a], 1);
+            mbar_init(&tempty[a], 4);
+        }
+        mbar_init(drain, 1);
+        *abort_i = 0;
+        *never = 0;
+        mbar_fence_init();
+    }
+    for (int i = threadIdx.x; i < p.N; i += kGemmThreads) sx[i] = i < p.B ? p.scale_x[i] : 0.0f;
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(tholder)),
+                     "r"(p.tmem_cols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = *tholder;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            /* producer: one W box and one X box per stage */
+            const uint64_t pol_w = policy_evict_first(), pol_x = policy_evict_last();
+            const uint32_t bytes = (uint32_t)(kBM * kBK + p.N * kBK);
+            int it = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x)
+                for (int kb = 0; kb < p.kblocks; ++kb, ++it) {
+                    const int s = it % p.stages;
+                    const uint32_t use = (uint32_t)(it / p.stages);
+                    if (it >= p.stages && !bwait(&empty[s], (use & 1u) ^ 1u, abort_flag)) {
+                        *abort_flag = 1;
+                        ok = false;
+                        break;
+                    }
+                    uint8_t *st = gsm + (size_t)s * p.stage_bytes;
+                    mbar_expect_tx(&full[s], bytes);
+                    tma_load_2d(st, &p.tmW, kb * kBK, tile * kBM, &full[s], pol_w);
+                    tma_load_2d(st + kBM * kBK, &p.tmX, kb * kBK, 0, &full[s], pol_x);
+                }
+            /* no copy may be in flight when the CTA exits */
+            for (int q = max(0, it - p.stages); q < it; ++q)
+                bwait(&full[q % p.stages], (uint32_t)(q / p.stages) & 1u, never);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            /* MMA issuer */
+            const uint32_t idesc = idesc_i8(kBM, p.N);
+            int it = 0, tcount = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x, ++tcount) {
+                const int acc = tcount & 1;
+                const uint32_t ause = (uint32_t)(tcount >> 1);
+                if (tcount >= 2 && !bwait(&tempty[acc], (ause & 1u) ^ 1u, abort_flag)) {
+                    *abort_flag = 1;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_tmem = tbase + (uint32_t)(acc * p.N);
+                for (int kb = 0; kb < p.kblocks; ++kb, ++it) {
+                    const int s = it % p.stages;
+                    if (!bwait(&full[s], (uint32_t)(it / p.stages) & 1u, abort_flag)) {
+                        *abort_flag = 1;
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a0 = smem_u32(gsm + (size_t)s * p.stage_bytes);
+                    const uint32_t b0 = a0 + kBM * kBK;
+#pragma unroll
+                    for (int kk = 0; kk < kBK / kMmaK; ++kk)
+                        tc_mma_i8(d_tmem, sw128_desc(a0 + kk * kMmaK), sw128_desc(b0 + kk * kMmaK),
+                                  idesc, (kb | kk) != 0 ? 1u : 0u);
+                    tc_commit(&empty[s]); /* the stage is free once these MMAs are done */
+                }
+                if (ok) tc_commit(&tfull[acc]);
+            }
+            /* every MMA issued is complete before the tensor memory is freed */
+            tc_commit(drain);
+            if (!bwait(drain, 0u, never)) *abort_flag = 1;
+        }
+    } else {
+        /* epilogue: warp w reads tensor-memory lanes 32*(w%4) .. +31 */
+        const int q = warp & 3;
+        int tcount = 0;
+        for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++tcount) {
+            const int acc = tcount & 1;
+            const uint32_t ause = (uint32_t)(tcount >> 1);
+            if (!bwait(&tfull[acc], ause & 1u, abort_flag)) {
+                *abort_flag = 1;
+                break;
+            }
+            tc_fence_after();
+            const int row = tile * kBM + q * 32 + lane;
+            const float sw = row < p.rows ? __ldg(p.scale_w + row) : 0.0f;
+            for (int c0 = 0; c0 < p.N; c0 += 32) {
+                uint32_t r[32];
+                tmem_ld32(tbase + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * p.N + c0), r);
+                tmem_ld_wait();
+                if (row < p.rows) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const int b = c0 + j;
+                        if (b < p.B)
+                            /* runtime/lal_q8_kernel.h:489: scale_x*scale_w[v]*(float)dot */
+                            p.logits[(size_t)b * p.rows + row] =
+                                __fmul_rn(__fmul_rn(sx[b], sw), __int2float_rn((int)r[j]));
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[acc]);
+        }
+    }
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tbase),
+                     "r"(p.tmem_cols)
+                     : "memory");
+    }
+    if (threadIdx.x == 0 && *abort_flag) atomicCAS(p.status, 0, (int)DEV_TIMEOUT);
+}
+
+/* --------------------------------------------- per-stream select + draw --- */
+struct BatchSelectParams {
+    float *logits; /* [B][rows], penalised in place */
+    int rows, row_base, vocab, variant;
+    const float *temperature;
+    const int *top_k;
+    const float *rep_penalty;
+    const float *u;
+    int *hist_ids, *hist_n, *hist_head;
+    int hist_cap, hist_stride, push_history;
+    int *tokens;
+    StreamDiag *diag;
+    int *status;
+    const uint32_t *expf_x, *expf_y;
+    int expf_n;
+    const uint32_t *expf_bits;
+    const uint32_t *expf_off;
+    uint8_t *shard_out; /* [B][rec_bytes] records, or null */
+    int rec_cap, rec_bytes;
+    int s_cap, c_cap, h_slots; /* superset, candidate and hash capacities */
+};
+
+constexpr uint32_t kEmptySlot = 0xFFFFFFFFu;
+
+__global__ void __launch_bounds__(NT, 1) batch_select_kernel(const __grid_constant__ BatchSelectParams p) {
+    extern __shared__ __align__(16) uint8_t bsm[];
+    __shared__ Misc msh;
+    __shared__ int s_count;
+    Misc *ms = &msh;
+    const int tid = threadIdx.x, b = blockIdx.x;
+    uint32_t *hist = reinterpret_cast<uint32_t *>(bsm);            /* 4096 bins        */
+    uint32_t *Sk = hist + 4096;                                     /* superset keys    */
+    int *Si = reinterpret_cast<int *>(Sk + p.s_cap);                /* superset rows    */
+    float *Cv = reinterpret_cast<float *>(Si + p.s_cap);           /* candidates       */
+    int *Ci = reinterpret_cast<int *>(Cv + p.c_cap);
+    float *Ov = reinterpret_cast<float *>(Ci + p.c_cap);           /* index order      */
+    int *Oi = reinterpret_cast<int *>(Ov + p.c_cap);
+    float *Ce = reinterpret_cast<float *>(Oi + p.c_cap);           /* weights, sums    */
+    uint32_t *hkey = reinterpret_cast<uint32_t *>(Ce + p.c_cap);   /* history hash     */
+    uint32_t *hcnt = hkey + p.h_slots;
+
+    float *lg = p.logits + (size_t)b * p.rows;
+    const float temp = p.temperature[b];
+    const int topk = p.top_k[b];
+    const float pen = p.rep_penalty[b];
+    const float u0 = p.u ? p.u[b] : 0.0f;
+    int *hids = p.hist_ids + (size_t)b * p.hist_stride;
+    const int hn = p.hist_n ? p.hist_n[b] : 0;
+    const int hhead = p.hist_head ? p.hist_head[b] : 0;
+    const bool greedy = (temp <= 0.0f) || (topk <= 0);
+    const bool use_pen = pen > 1.0f && hn > 0 && (p.variant == VARIANT_SERVER || !greedy);
+
+    /* 1. repetition penalty: occurrences of each history id in this slice,
+     * counted in an open-addressing hash, applied once per occurrence
+     * (runtime/lal_sampling.h:60-66; ids outside [0, V) are skipped) */
+    for (int i = tid; i < 4096; i += NT) hist[i] = 0u;
+    if (use_pen) {
+        for (int i = tid; i < p.h_slots; i += NT) {
+            hkey[i] = kEmptySlot;
+            hcnt[i] = 0u;
+        }
+        __syncthreads();
+        const uint32_t mask = (uint32_t)p.h_slots - 1u;
+        for (int i = tid; i < hn; i += NT) {
+            const int id = hids[i];
+            if (id < 0 || id >= p.vocab) continue;
+            const int g = id - p.row_base;
+            if (g < 0 || g >= p.rows) continue;
+            uint32_t slot = ((uint32_t)id * 2654435761u) & mask;
+            for (int probe = 0; probe < p.h_slots; ++probe) {
+                const uint32_t prev = atomicCAS(&hkey[slot], kEmptySlot, (uint32_t)id);
+                if (prev == kEmptySlot || prev == (uint32_t)id) {
+                    atomicAdd(&hcnt[slot], 1u);
+                    break;
+                }
+                slot = (slot + 1u) & mask;
+            }
+        }
+        __syncthreads();
+        for (int i = tid; i < p.h_slots; i += NT) {
+            const uint32_t id = hkey[i];
+            if (id != kEmptySlot) {
+                const int g = (int)id - p.row_base;
+                lg[g] = penalise(lg[g], hcnt[i], pen);
+            }
+        }
+    }
+    __syncthreads();
+
+    /* 2. k = min(top_k, V) (runtime/lal_sampling.h:70-71), 1 for greedy; the
+     * top 12 key bits of every logit into the histogram */
+    int k = greedy ? 1 : topk;
+    if (k > p.vocab) k = p.vocab;
+    if (k > p.rows) k = p.rows;
+    if (k < 1) k = 1;
+    auto hist_add = [&](uint32_t *h, uint32_t digit, bool act) {
+        const unsigned voters = __ballot_sync(0xffffffffu, act);
+        if (act) {
+            const unsigned peers = __match_any_sync(voters, digit);
+            if ((tid & 31) == __ffs(peers) - 1) atomicAdd(&h[digit], (uint32_t)__popc(peers));
+        }
+    };
+    constexpr int U = 8;
+    for (int i0 = 0; i0 < p.rows; i0 += NT * U) {
+        float v[U];
+#pragma unroll
+        for (int j = 0; j < U; ++j) {
+            const int i = i0 + j * NT + tid;
+            v[j] = i < p.rows ? lg[i] : 0.0f;
+        }
+#pragma unroll
+        for (int j = 0; j < U; ++j) {
+            const int i = i0 + j * NT + tid;
+            hist_add(hist, f2key(v[j]) >> 20, i < p.rows);
+        }
+    }
+    __syncthreads();
+    uint32_t ab, cnt;
+    uint32_t bin = boundary_bin(hist, 4096, (uint32_t)k, ms, &ab, &cnt);
+    uint32_t prefix = bin << 20, pmask = 0xFFF00000u;
+    uint32_t above = ab;
+    /* refine (10 + 10 bits) while the boundary bin does not fit the superset */
+    for (int level = 1; level <= 2 && above + cnt > (uint32_t)p.s_cap; ++level) {
+        const int shift = level == 1 ? 10 : 0;
+        for (int i = tid; i < 1024; i += NT) hist[i] = 0u;
+        __syncthreads();
+        for (int i0 = 0; i0 < p.rows; i0 += NT * U) {
+            float v[U];
+#pragma unroll
+            for (int j = 0; j < U; ++j) {
+                const int i = i0 + j * NT + tid;
+                v[j] = i < p.rows ? lg[i] : 0.0f;
+            }
+#pragma unroll
+            for (int j = 0; j < U; ++j) {
+                const int i = i0 + j * NT + tid;
+                const uint32_t key = f2key(v[j]);
+                hist_add(hist, (key >> shift) & 1023u, i < p.rows && (key & pmask) == prefix);
+            }
+        }
+        __syncthreads();
+        uint32_t ab2, cnt2;
+        const uint32_t bin2 = boundary_bin(hist, 1024, (uint32_t)k - above, ms, &ab2, &cnt2);
+        above += ab2;
+        cnt = cnt2;
+        prefix |= bin2 << shift;
+        pmask |= 1023u << shift;
+    }
+    const uint32_t L = prefix;
+    const int S = (int)(above + cnt);
+
+    StreamDiag dg;
+    dg.threshold = 0.0f;
+    dg.max_l = 0.0f;
+    dg.sum = 0.0f;
+    dg.r = 0.0f;
+    dg.n_cand = 0;
+    dg.greedy = greedy ? 1 : 0;
+    dg.drew = 0;
+    dg.token = -1;
+    auto fail_stream = [&](int st) {
+        if (tid == 0) {
+            if (p.shard_out != nullptr) {
+                ShardRecordHead *h =
+                    reinterpret_cast<ShardRecordHead *>(p.shard_out + (size_t)b * p.rec_bytes);
+                h->count = 0;
+                h->status = st;
+            } else {
+                atomicCAS(p.status, 0, st);
+                p.tokens[b] = -1;
+            }
+            p.diag[b] = dg;
+        }
+    };
+    if (S > p.s_cap) {
+        fail_stream((int)DEV_CAPACITY);
+        return;
+    }
+
+    /* 3. the superset {key >= L} (every candidate is in it) */
+    if (tid == 0) s_count = 0;
+    __syncthreads();
+    for (int i0 = 0; i0 < p.rows; i0 += NT * U) {
+        float v[U];
+#pragma unroll
+        for (int j = 0; j < U; ++j) {
+            const int i = i0 + j * NT + tid;
+            v[j] = i < p.rows ? lg[i] : 0.0f;
+        }
+#pragma unroll
+        for (int j = 0; j < U; ++j) {
+            const int i = i0 + j * NT + tid;
+            const uint32_t key = f2key(v[j]);
+            const bool take = i < p.rows && key >= L;
+            const unsigned bal = __ballot_sync(0xffffffffu, take);
+            int base = 0;
+            if ((tid & 31) == 0 && bal) base = atomicAdd(&s_count, __popc(bal));
+            base = __shfl_sync(0xffffffffu, base, 0);
+            if (take) {
+                const int pos = base + __popc(bal & ((1u << (tid & 31)) - 1u));
+                if (pos < p.s_cap) {
+                    Sk[pos] = key;
+                    Si[pos] = i;
+                }
+            }
+        }
+    }
+    __syncthreads();
+
+    /* 4. T exactly: the k-th largest key of the superset */
+    const uint32_t T = block_kth_largest(
+        [&](int i, uint32_t &key) {
+            key = Sk[i];
+            return true;
+        },
+        S, min(k, S), ms);
+    /* candidates {l >= T} */
+    const int seg = (S + NT - 1) / NT;
+    const int e0 = min(S, tid * seg), e1 = min(S, e0 + seg);
+    uint32_t c = 0;
+    for (int e = e0; e < e1; ++e) c += Sk[e] >= T;
+    uint32_t mt;
+    uint32_t pos = block_scan_excl(c, ms, &mt);
+    const int m = (int)mt;
+    dg.threshold = key2f(T);
+    dg.n_cand = m;
+    if (m < 1 || m > p.c_cap) {
+        fail_stream((int)DEV_CAPACITY);
+        return;
+    }
+    for (int e = e0; e < e1; ++e)
+        if (Sk[e] >= T) {
+            Cv[pos] = key2f(Sk[e]);
+            Ci[pos] = p.row_base + Si[e];
+            ++pos;
+        }
+    __syncthreads();
+    /* ascending vocab order */
+    if (m <= 64) {
+        for (int i = tid; i < m; i += NT) {
+            const int me = Ci[i];
+            int r = 0;
+            for (int j = 0; j < m; ++j) r += Ci[j] < me;
+            Oi[r] = me;
+            Ov[r] = Cv[i];
+        }
+    } else {
+        int n2 = 1;
+        while (n2 < m) n2 <<= 1;
+        for (int i = tid; i < n2; i += NT) {
+            Oi[i] = i < m ? Ci[i] : 0x7fffffff;
+            Ov[i] = i < m ? Cv[i] : 0.0f;
+        }
+        __syncthreads();
+        for (int size = 2; size <= n2; size <<= 1)
+            for (int stride = size >> 1; stride > 0; stride >>= 1) {
+                for (int i = tid; i < (n2 >> 1); i += NT) {
+                    const int lo = (i / stride) * stride * 2 + (i % stride);
+                    const int hi = lo + stride;
+                    const bool asc = (lo & size) == 0;
+                    const int a = Oi[lo], bb = Oi[hi];
+                    if ((a > bb) == asc) {
+                        Oi[lo] = bb;
+                        Oi[hi] = a;
+                        const float t = Ov[lo];
+                        Ov[lo] = Ov[hi];
+                        Ov[hi] = t;
+                    }
+                }
+                __syncthreads();
+            }
+    }
+    __syncthreads();
+
+    if (p.shard_out != nullptr) {
+        /* vocab-sharded step: this slice's record for the merge */
+        uint8_t *rec = p.shard_out + (size_t)b * p.rec_bytes;
+        ShardRecordHead *h = reinterpret_cast<ShardRecordHead *>(rec);
+        float *rv = reinterpret_cast<float *>(rec + sizeof(ShardRecordHead));
+        int *ri = reinterpret_cast<int *>(rv + p.rec_cap);
+        const bool fits = m <= p.rec_cap;
+        if (fits)
+            for (int i = tid; i < m; i += NT) {
+                rv[i] = Ov[i];
+                ri[i] = Oi[i];
+            }
+        if (tid == 0) {
+            h->count = fits ? m : 0;
+            h->status = fits ? 0 : (int)DEV_CAPACITY;
+            p.diag[b] = dg;
+        }
+        return;
+    }
+
+    /* 5. max over candidates floored at -1e30 (runtime/lal_sampling.h:107-109),
+     * weights expf((l - max_l)/T), sequential sums in vocab order, draw */
+    float mx = -1e30f;
+    for (int i = tid; i < m; i += NT) mx = fmaxf(mx, Ov[i]);
+    const float max_l = block_max_f(mx, ms);
+    dg.max_l = max_l;
+    int token;
+    if (greedy) {
+        token = Oi[0];
+    } else {
+        for (int i = tid; i < m; i += NT) {
+            const float x = __fdiv_rn(__fsub_rn(Ov[i], max_l), temp);
+            Ce[i] = sampler_expf(x, p.expf_x, p.expf_y, p.expf_bits, p.expf_off);
+        }
+        __syncthreads();
+        if (tid == 0) {
+            float acc = 0.0f;
+            for (int i = 0; i < m; ++i) {
+                acc = __fadd_rn(acc, Ce[i]);
+                Ce[i] = acc;
+            }
+            ms->sum = acc;
+            ms->found = 0x7fffffff;
+        }
+        __syncthreads();
+        const float sum = ms->sum;
+        dg.sum = sum;
+        if (p.variant == VARIANT_SERVER && sum <= 0.0f) {
+            /* tools/server/qwen7b_server.c:285-286 */
+            token = 0;
+            float bv = -1e30f;
+            for (int i = 0; i < m; ++i)
+                if (Ov[i] > bv) {
+                    bv = Ov[i];
+                    token = Oi[i];
+                }
+        } else {
+            const float r = __fmul_rn(u0, sum);
+            dg.r = r;
+            dg.drew = 1;
+            int first = 0x7fffffff;
+            for (int i = tid; i < m; i += NT)
+                if (r <= Ce[i]) {
+                    first = i;
+                    break;
+                }
+            if (first != 0x7fffffff) atomicMin(&ms->found, first);
+            __syncthreads();
+            token = ms->found != 0x7fffffff ? Oi[ms->found] : p.vocab - 1;
+        }
+    }
+    if (tid == 0) {
+        dg.token = token;
+        p.tokens[b] = token;
+        p.diag[b] = dg;
+        if (p.push_history && p.hist_cap > 0) {
+            if (hn < p.hist_cap) {
+                hids[hn] = token;
+                p.hist_n[b] = hn + 1;
+            } else {
+                hids[hhead] = token;
+                p.hist_head[b] = (hhead + 1) % p.hist_cap;
+            }
+        }
+    }
+}
+
+/* ------------------------------------------------------------ host --- */
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                  const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                  const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encoder() {
+    static std::once_flag once;
+    static EncodeTiledFn fn = nullptr;
+    std::call_once(once, [] {
+        void *f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(f);
+    });
+    return fn;
+}
+
+/* 2-D int8 tensor [dim1][dim0] (row pitch `pitch` bytes), box 128 x box1,
+ * 128-byte swizzle; out-of-range rows and columns read as zero. */
+bool encode_i8(CUtensorMap *m, const void *base, int dim0, int dim1, int pitch, int box1) {
+    EncodeTiledFn enc = encoder();
+    if (!enc) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)dim0, (cuuint64_t)dim1};
+    const cuuint64_t strides[1] = {(cuuint64_t)pitch};
+    const cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box1};
+    const cuuint32_t estr[2] = {1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box,
+               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+/* ---- the batched step, as seen by tail_api.cu ---- */
+int batch_n_for(int B) { return (B + 31) / 32 * 32; }
+
+size_t batch_select_smem(int s_cap, int c_cap, int h_slots) {
+    return 4ull * 4096 + 8ull * s_cap + 24ull * c_cap + 8ull * h_slots;
+}
+
+int batch_plan(BatchPlan &bp, const int8_t *W, const float *scale_w, int rows, int ld,
+               int num_sms, int8_t *xq, float *sx, int max_B, int hist_cap) {
+    memset(&bp, 0, sizeof(bp));
+    if (!encoder()) return -3;
+    if (ld < kBK || ld % 16 != 0 || max_B < 2 || max_B > 256 || rows < 1) return -1;
+    bp.W = W;
+    bp.scale_w = scale_w;
+    bp.rows = rows;
+    bp.ld = ld;
+    bp.xq = xq;
+    bp.sx = sx;
+    bp.num_sms = num_sms;
+    bp.kblocks = (ld + kBK - 1) / kBK;
+    /* select capacities: superset, candidates, history hash (>= 2x the
+     * history, a power of two) */
+    bp.s_cap = 8192;
+    bp.c_cap = 2048;
+    int hs = 64;
+    while (hs < 2 * std::max(1, hist_cap)) hs <<= 1;
+    bp.h_slots = hs;
+    if (batch_select_smem(bp.s_cap, bp.c_cap, bp.h_slots) > (size_t)(kGemmSmemLimit - 8192))
+        return -2;
+    return 0;
+}
+
+cudaError_t batch_launch(BatchPlan &bp, const BatchStep &s, cudaStream_t st) {
+    const int N = batch_n_for(s.B);
+    if (s.B < 1 || N > 256) return cudaErrorInvalidValue;
+    static_assert(sizeof(CUtensorMap) == 128, "tensor map size");
+    if (!bp.w_ready) {
+        if (!encode_i8(reinterpret_cast<CUtensorMap *>(bp.tm_w), bp.W, bp.ld, bp.rows, bp.ld, kBM))
+            return cudaErrorInvalidValue;
+        bp.w_ready = 1;
+    }
+    const int xi = N / 32 - 1;
+    if (!(bp.x_ready & (1u << xi))) {
+        if (!encode_i8(reinterpret_cast<CUtensorMap *>(bp.tm_x[xi]), bp.xq, bp.ld, N, bp.ld, N))
+            return cudaErrorInvalidValue;
+        bp.x_ready |= 1u << xi;
+    }
+    /* 1. quantize the B hidden vectors */
+    quantize_batch_kernel<<<s.B, NT, 0, st>>>(s.hidden, s.d, bp.xq, bp.ld, bp.sx);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    /* 2. logits = X W^T on the tensor cores */
+    GemmParams g;
+    memset(&g, 0, sizeof(g));
+    memcpy(&g.tmW, bp.tm_w, sizeof(CUtensorMap));
+    memcpy(&g.tmX, bp.tm_x[xi], sizeof(CUtensorMap));
+    g.scale_w = bp.scale_w;
+    g.scale_x = bp.sx;
+    g.logits = s.logits;
+    g.rows = bp.rows;
+    g.B = s.B;
+    g.N = N;
+    g.kblocks = bp.kblocks;
+    g.stage_bytes = kBM * kBK + N * kBK;
+    const int fixed = 1024 + 64 * 8 + 4 * 256 + 64; /* alignment, barriers, scales */
+    g.stages = std::min(kGemmStagesMax, (kGemmSmemLimit - fixed) / g.stage_bytes);
+    if (g.stages < 2) return cudaErrorInvalidValue;
+    int cols = 32;
+    while (cols < 2 * N) cols <<= 1;
+    g.tmem_cols = cols;
+    g.status = s.status;
+    const size_t gsmem = (size_t)g.stages * g.stage_bytes + fixed;
+    e = raise_smem((const void *)gemm_i8_kernel, kGemmSmemLimit);
+    if (e != cudaSuccess) return e;
+    const int n_tiles = (bp.rows + kBM - 1) / kBM;
+    const int grid = std::min(n_tiles, bp.num_sms);
+    gemm_i8_kernel<<<grid, kGemmThreads, gsmem, st>>>(g);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    /* 3. per stream: penalty, select, draw (or the shard record) */
+    BatchSelectParams q;
+    memset(&q, 0, sizeof(q));
+    q.logits = s.logits;
+    q.rows = bp.rows;
+    q.row_base = s.row_base;
+    q.vocab = s.vocab;
+    q.variant = s.variant;
+    q.temperature = s.temperature;
+    q.top_k = s.top_k;
+    q.rep_penalty = s.rep_penalty;
+    q.u = s.u;
+    q.hist_ids = s.hist_ids;
+    q.hist_n = s.hist_n;
+    q.hist_head = s.hist_head;
+    q.hist_cap = s.hist_cap;
+    q.hist_stride = s.hist_stride;
+    q.push_history = s.push_history;
+    q.tokens = s.tokens;
+    q.diag = s.diag;
+    q.status = s.status;
+    q.expf_x = s.expf_x;
+    q.expf_y = s.expf_y;
+    q.expf_n = s.expf_n;
+    q.expf_bits = s.expf_bits;
+    q.expf_off = s.expf_off;
+    q.shard_out = s.shard_out;
+    q.rec_cap = s.rec_cap;
+    q.rec_bytes = s.rec_bytes;
+    q.s_cap = bp.s_cap;
+    q.c_cap = bp.c_cap;
+    q.h_slots = bp.h_slots;
+    const size_t ssmem = batch_select_smem(bp.s_cap, bp.c_cap, bp.h_slots);
+    e = raise_smem((const void *)batch_select_kernel, kGemmSmemLimit - 8192);
+    if (e != cudaSuccess) return e;
+    batch_select_kernel<<<s.B, NT, ssmem, st>>>(q);
+    return cudaGetLastError();
+}
+
+}  // namespace lal

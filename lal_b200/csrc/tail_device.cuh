@@ -1,0 +1,362 @@
+/*
+ * tail_device.cuh -- device helpers shared by the sm_100a kernels
+ * (tail_kernels.cu, tail_batch.cu): mbarrier and bulk-copy PTX, bounded
+ * waits, the glibc-exact expf lookup, float order keys, block-wide scans,
+ * maxima, histogram boundaries and the radix k-th-largest select.  Every
+ * function has internal linkage (each kernel file gets its own copy).
+ */
+#pragma once
+
+#include "tail_internal.h"
+#include "lal_expf.h"
+
+namespace lal {
+namespace {
+
+constexpr int NT = kThreads;
+constexpr int NWARP = NT / 32;
+
+/* ---------------------------------------------------------------- PTX --- */
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ uint64_t gtimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ void mbar_init(uint64_t *b, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count)
+                 : "memory");
+}
+__device__ __forceinline__ void mbar_fence_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *b, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)),
+                 "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *b) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint64_t *b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+/* Every wait is bounded: it gives up after kWaitNs of wall time (globaltimer)
+ * or as soon as another warp of the CTA has given up. */
+constexpr uint64_t kWaitNs = 2000000000ull;
+__device__ bool mbar_wait(uint64_t *b, uint32_t parity, volatile int *abort_flag) {
+    if (mbar_try(b, parity)) return true;
+    const uint64_t t0 = gtimer();
+    for (uint32_t it = 1;; ++it) {
+        if (mbar_try(b, parity)) return true;
+        if ((it & 63u) == 0) {
+            if (*abort_flag) return false;
+            if (gtimer() - t0 > kWaitNs) return false;
+        }
+    }
+}
+__device__ __forceinline__ uint64_t policy_evict_first() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+/* Bulk (non-tensor) TMA copy global -> this CTA's shared memory. */
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes,
+                                         uint64_t *bar, uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1], %2, [%3], %4;" ::"r"(smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
+        : "memory");
+}
+
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_gpu(unsigned *p, unsigned v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+/* The glibc fix-up of x, whose bitmap bit is set: the entries of x's bitmap
+ * word (8192 bit patterns) are tx[off[w] .. off[w+1]), a few at most. */
+__device__ __forceinline__ float expf_fixup(float x, const uint32_t *tx, const uint32_t *ty,
+                                            const uint32_t *off) {
+    const uint32_t xb = __float_as_uint(x);
+    const uint32_t w = (xb - 0x80000000u) >> 13;
+    const uint32_t lo = __ldg(off + w), hi = __ldg(off + w + 1);
+    for (uint32_t i = lo; i < hi; ++i)
+        if (__ldg(tx + i) == xb) return __uint_as_float(__ldg(ty + i));
+    return lal_expf_rounded(x);
+}
+
+/* The sampler's weight function: glibc-exact expf (lal_expf.h) with the
+ * fix-up table gated by a membership bitmap, so that nearly every call costs
+ * one bitmap load, and a flagged one two more plus a short scan. */
+__device__ __forceinline__ float sampler_expf(float x, const uint32_t *tx, const uint32_t *ty,
+                                              const uint32_t *bits, const uint32_t *off) {
+    const uint32_t xb = __float_as_uint(x);
+    if (!(xb & 0x80000000u) || !(x <= 0.0f)) return lal_expf_rounded(x);
+    const uint32_t b = (xb - 0x80000000u) >> 8;
+    if (!((__ldg(bits + (b >> 5)) >> (b & 31)) & 1u)) return lal_expf_rounded(x);
+    return expf_fixup(x, tx, ty, off);
+}
+
+/* sampler_expf in two halves, so the bitmap load can be in flight while
+ * other work runs: the first returns the raw bitmap word (0 when x takes no
+ * fix-up), the second finishes with it. */
+__device__ __forceinline__ uint32_t expf_bitmap_word(float x, const uint32_t *bits) {
+    const uint32_t xb = __float_as_uint(x);
+    if (!(xb & 0x80000000u) || !(x <= 0.0f)) return 0u;
+    return __ldg(bits + (((xb - 0x80000000u) >> 8) >> 5));
+}
+__device__ __forceinline__ float expf_with_word(float x, uint32_t word, const uint32_t *tx,
+                                                const uint32_t *ty, const uint32_t *off) {
+    const uint32_t xb = __float_as_uint(x);
+    const uint32_t b = (xb - 0x80000000u) >> 8;
+    if ((xb & 0x80000000u) && x <= 0.0f && ((word >> (b & 31)) & 1u))
+        return expf_fixup(x, tx, ty, off);
+    return lal_expf_rounded(x);
+}
+
+/* ------------------------------------------------------- order keys --- */
+/* Monotone map float -> uint32 (larger float, larger key).  -0 maps like +0,
+ * so key equality is float equality, as the reference's comparisons treat it. */
+__device__ __forceinline__ uint32_t f2key(float f) {
+    uint32_t u = __float_as_uint(f);
+    if (u == 0x80000000u) u = 0u;
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float key2f(uint32_t k) {
+    return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
+}
+
+/* ------------------------------------------------- block primitives --- */
+struct Misc {
+    uint32_t hist[256];
+    uint32_t scan[NWARP + 1];
+    uint32_t sh[16];
+    float fred[NWARP];
+    float sx;
+    float sum;
+    int abort_flag;
+    int ticket;
+    int found;
+    uint32_t gm[kMaxGrid]; /* the last CTA's copy of the per-CTA maxima */
+};
+
+/* Grid-wide barrier of a cooperative launch (every CTA resident).  The
+ * wait is bounded: after kWaitNs it records DEV_TIMEOUT and returns false.
+ * bar[0] counts arrivals, bar[1] is the generation; the last arriver resets
+ * the count before publishing the next generation (release), so the words
+ * are ready for the next barrier and the next launch. */
+__device__ bool grid_sync(unsigned *bar, unsigned G, Misc *ms, int *status) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const unsigned gen = ld_acquire_gpu(bar + 1);
+        __threadfence();
+        const unsigned arrived = atomicAdd(bar, 1u) + 1u;
+        unsigned ok = 1u;
+        if (arrived == G) {
+            bar[0] = 0u;
+            __threadfence();
+            st_release_gpu(bar + 1, gen + 1u);
+        } else {
+            const uint64_t t0 = gtimer();
+            while (ld_acquire_gpu(bar + 1) == gen) {
+                if (gtimer() - t0 > kWaitNs) {
+                    ok = 0u;
+                    atomicCAS(status, 0, (int)DEV_TIMEOUT);
+                    break;
+                }
+            }
+        }
+        ms->sh[15] = ok;
+    }
+    __syncthreads();
+    return ms->sh[15] != 0u;
+}
+
+/* Exclusive prefix (thread order) of one value per thread; *total = sum. */
+__device__ __forceinline__ uint32_t block_scan_excl(uint32_t v, Misc *ms, uint32_t *total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    uint32_t x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) ms->scan[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+        uint32_t w = lane < NWARP ? ms->scan[lane] : 0u;
+        uint32_t incl = w;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += y;
+        }
+        if (lane < NWARP) ms->scan[lane] = incl - w;
+        if (lane == NWARP - 1) ms->scan[NWARP] = incl;
+    }
+    __syncthreads();
+    const uint32_t res = ms->scan[warp] + x - v;
+    *total = ms->scan[NWARP];
+    __syncthreads();
+    return res;
+}
+
+/* Barrier among the kConsumerWarps consumer warps only (named barrier 1), so
+ * the producer warp can stream while the consumers run the prologue. */
+__device__ __forceinline__ void consumer_sync() {
+    asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+}
+
+/* max over the consumer warps' values (consumer threads only) */
+__device__ __forceinline__ float consumer_max_f(float v, Misc *ms) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if (lane == 0) ms->fred[warp] = v;
+    consumer_sync();
+    float r = ms->fred[0];
+#pragma unroll
+    for (int w = 1; w < kConsumerWarps; ++w) r = fmaxf(r, ms->fred[w]);
+    consumer_sync();
+    return r;
+}
+
+__device__ __forceinline__ void stamp(const TailParams &p, int slot) {
+    if (p.phase_ts) p.phase_ts[slot] = gtimer();
+}
+
+__device__ __forceinline__ float block_max_f(float v, Misc *ms) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if (lane == 0) ms->fred[warp] = v;
+    __syncthreads();
+    float r = ms->fred[0];
+#pragma unroll
+    for (int w = 1; w < NWARP; ++w) r = fmaxf(r, ms->fred[w]);
+    __syncthreads();
+    return r;
+}
+
+/* Boundary bin of a histogram h[0..nb) scanned from the top bin down: the bin
+ * holding the krem-th largest entry (1 <= krem <= total).  Returns the bin;
+ * *above gets the count in higher bins, *count the bin's own count.  All
+ * threads of the block call it. */
+__device__ uint32_t boundary_bin(const uint32_t *h, int nb, uint32_t krem, Misc *ms,
+                                 uint32_t *above, uint32_t *count) {
+    const int per = (nb + NT - 1) / NT;
+    const int q0 = threadIdx.x * per; /* descending positions q <-> bin nb-1-q */
+    const int q1 = min(nb, q0 + per);
+    uint32_t s = 0;
+    for (int q = q0; q < q1; ++q) s += h[nb - 1 - q];
+    uint32_t tot;
+    const uint32_t ex = block_scan_excl(s, ms, &tot);
+    if (ex < krem && krem <= ex + s) {
+        uint32_t run = ex;
+        for (int q = q0; q < q1; ++q) {
+            const uint32_t c = h[nb - 1 - q];
+            if (run + c >= krem) {
+                ms->sh[0] = (uint32_t)(nb - 1 - q);
+                ms->sh[1] = run;
+                ms->sh[2] = c;
+                break;
+            }
+            run += c;
+        }
+    }
+    __syncthreads();
+    const uint32_t bin = ms->sh[0];
+    *above = ms->sh[1];
+    *count = ms->sh[2];
+    __syncthreads();
+    return bin;
+}
+
+/* k-th largest key of the valid entries among i in [0, n): get(i, key)
+ * returns whether entry i takes part and sets its key; 1 <= k <= the number
+ * of valid entries.  MSB-first radix select with 8-bit digits; histogram adds
+ * are aggregated per warp (match.any). */
+template <class Get>
+__device__ uint32_t block_kth_largest(Get get, int n, int k, Misc *ms) {
+    uint32_t prefix = 0, mask = 0;
+    int krem = k;
+    for (int shift = 24; shift >= 0; shift -= 8) {
+        for (int i = threadIdx.x; i < 256; i += NT) ms->hist[i] = 0;
+        __syncthreads();
+        for (int i0 = 0; i0 < n; i0 += NT) {
+            const int i = i0 + threadIdx.x;
+            uint32_t key = 0u;
+            const bool act = i < n && get(i, key);
+            const bool m = act && ((key & mask) == prefix);
+            const uint32_t digit = (key >> shift) & 0xFFu;
+            const unsigned voters = __ballot_sync(0xffffffffu, m);
+            if (m) {
+                const unsigned peers = __match_any_sync(voters, digit);
+                if ((int)(threadIdx.x & 31) == __ffs(peers) - 1)
+                    atomicAdd(&ms->hist[digit], (uint32_t)__popc(peers));
+            }
+        }
+        __syncthreads();
+        if (threadIdx.x < 32) {
+            const int lane = threadIdx.x;
+            uint32_t c[8], s = 0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                c[j] = ms->hist[255 - 8 * lane - j];
+                s += c[j];
+            }
+            uint32_t incl = s;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += y;
+            }
+            const uint32_t excl = incl - s;
+            if (excl < (uint32_t)krem && (uint32_t)krem <= incl) {
+                uint32_t run = excl;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    if (run + c[j] >= (uint32_t)krem) {
+                        ms->sh[0] = 255u - 8u * lane - j;
+                        ms->sh[1] = run;
+                        break;
+                    }
+                    run += c[j];
+                }
+            }
+        }
+        __syncthreads();
+        const uint32_t digit = ms->sh[0];
+        krem -= (int)ms->sh[1];
+        prefix |= digit << shift;
+        mask |= 0xFFu << shift;
+        __syncthreads();
+    }
+    return prefix;
+}
+
+/* Penalty for one logit with `count` history occurrences, one step per
+ * occurrence as runtime/lal_sampling.h:63-64 does (not a power). */
+__device__ __forceinline__ float penalise(float l, uint32_t count, float pen) {
+    for (uint32_t c = 0; c < count; ++c) l = (l > 0.0f) ? __fdiv_rn(l, pen) : __fmul_rn(l, pen);
+    return l;
+}
+
+}  // namespace
+}  // namespace lal

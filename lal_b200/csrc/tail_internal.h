@@ -207,6 +207,50 @@ cudaError_t prepare_sample_kernel();
 cudaError_t launch_sample_prepared(const TailParams &p, int grid, cudaStream_t st);
 /* Records the calling thread's last error message (tail_api.cu). */
 int set_error(int code, const char *msg);
+/* Raise a kernel's dynamic shared-memory limit once per (device, kernel). */
+cudaError_t raise_smem(const void *fn, int bytes);
+
+/* Batched step (tail_batch.cu): B >= 2 streams share one pass over W on the
+ * tensor cores.  BatchPlan is per context (W, the quantized-vector buffer,
+ * cached TMA descriptors); BatchStep is per launch. */
+struct BatchPlan {
+    const int8_t *W;
+    const float *scale_w;
+    int rows, ld, num_sms, kblocks;
+    int8_t *xq;        /* [256][ld] quantized hidden vectors                     */
+    float *sx;         /* [256] their scales                                     */
+    int s_cap, c_cap, h_slots;
+    /* TMA descriptors (CUtensorMap, 128 bytes each): W, and X for N = 32..256 */
+    alignas(64) unsigned char tm_w[128];
+    alignas(64) unsigned char tm_x[8][128];
+    unsigned x_ready;
+    int w_ready;
+};
+struct BatchStep {
+    const float *hidden;
+    int d, B;
+    float *logits; /* [B][rows] */
+    int row_base, vocab, variant;
+    const float *temperature;
+    const int *top_k;
+    const float *rep_penalty;
+    const float *u;
+    int *hist_ids, *hist_n, *hist_head;
+    int hist_cap, hist_stride, push_history;
+    int *tokens;
+    StreamDiag *diag;
+    int *status;
+    const uint32_t *expf_x, *expf_y;
+    int expf_n;
+    const uint32_t *expf_bits;
+    const uint32_t *expf_off;
+    uint8_t *shard_out; /* per-stream records (vocab-sharded select), or null */
+    int rec_cap, rec_bytes;
+};
+/* 0 when the shape takes the batched path (d >= 128, 2 <= max_B <= 256). */
+int batch_plan(BatchPlan &bp, const int8_t *W, const float *scale_w, int rows, int ld,
+               int num_sms, int8_t *xq, float *sx, int max_B, int hist_cap);
+cudaError_t batch_launch(BatchPlan &bp, const BatchStep &s, cudaStream_t st);
 int plan_launch(TailParams &p, int num_sms, int min_rows_per_cta);
 cudaError_t launch_tail(const TailParams &p, int grid, cudaStream_t st);
 cudaError_t launch_quantize_x(const float *x, int8_t *xq, float *scale, int n,
