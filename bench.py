@@ -42,6 +42,7 @@ from lal_b200 import synth  # noqa: E402
 
 METRIC = "Qwen7B LM-head+top-k tail tokens/s at B=1/64, % HBM BW peak, 1/2/4/8 B200"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+L2_BYTES = 126 << 20
 
 
 def parse():
@@ -62,6 +63,18 @@ def algorithmic_bytes(cfg, B, rows=None):
     int32 history and the int32 token (logits stay on chip / in L2)."""
     V = cfg.vocab if rows is None else rows
     return V * cfg.n_embd + 4 * V + B * (4 * cfg.n_embd + 4 * cfg.hist + 4)
+
+
+INT8_DENSE_TOPS_NOMINAL = 4500.0  # B200 dense int8 (no measured int8 figure)
+
+
+def tensor_roofline(cfg, B, rows, kern_ms):
+    """int8 tensor-core rate of the batched GEMM: 2*B*rows*d ops per launch."""
+    ops = 2.0 * B * rows * cfg.n_embd
+    achieved = ops / (kern_ms * 1e-3) / 1e12
+    return {"achieved": round(achieved, 1), "peak": INT8_DENSE_TOPS_NOMINAL, "unit": "TOPS",
+            "frac": round(achieved / INT8_DENSE_TOPS_NOMINAL, 4),
+            "note": "of nominal dense int8 (MEASURED_PEAKS.json has no int8 figure)"}
 
 
 def load_peaks():
@@ -240,8 +253,16 @@ def workload(cfg, n):
                         f"top_k={cfg.top_k} H={cfg.hist} p={cfg.rep_penalty}",
             "vocab": cfg.vocab, "n_embd": cfg.n_embd, "streams": cfg.streams,
             "top_k": cfg.top_k, "history": cfg.hist, "parallelism": f"vocab-sharded x{n}",
-            "l2": "LM head (545 MB) streamed each step is larger than L2 (126 MB)"
-            if n == 1 else "L2 flushed between timed steps (256 MB write)"}
+            "l2": l2_policy(cfg, n)}
+
+
+def l2_policy(cfg, n):
+    slice_bytes = (cfg.vocab // n) * cfg.n_embd
+    if slice_bytes >= 2 * L2_BYTES:
+        return (f"inputs larger than L2: each rank streams a {slice_bytes / 1e6:.0f} MB LM-head "
+                f"slice per step (L2 126 MB), steps back to back")
+    return (f"L2 flushed before each timed step: a 512 MB read on the tail's stream "
+            f"(the {slice_bytes / 1e6:.0f} MB slice could stay in the 126 MB L2)")
 
 
 # ---------------------------------------------------------------- GPU arm ---
@@ -290,7 +311,12 @@ def run_ours(args, cfg):
     us = np.array([[draws.u(b) for b in range(B)] for _ in range(nsteps)], np.float32)
 
     stream = torch.cuda.ExternalStream(t.stream(), device=local)
-    flush = torch.empty(64 << 20, dtype=torch.float32, device=local) if world > 1 else None
+    # steps run back to back when this rank's slice is at least twice L2
+    # (126 MB); a smaller slice is evicted by a 512 MB read before each step
+    slice_bytes = t.n_rows * cfg.n_embd
+    flush = (torch.ones(128 << 20, dtype=torch.float32, device=local)
+             if slice_bytes < 2 * L2_BYTES else None)
+    flush_out = torch.empty((), dtype=torch.float32, device=local)
 
     def barrier():
         torch.cuda.synchronize()
@@ -317,12 +343,12 @@ def run_ours(args, cfg):
                 t.step_device(d_hid[i].data_ptr(), B, d_u[i].data_ptr(), d_tok[i].data_ptr())
             ev[0][1].record(stream)
         else:
-            # a slice may fit in L2: a 256 MB write on the same stream evicts
-            # it before each step, outside the step's event pair (the host
-            # enqueues the step while the flush runs, so no idle gap is timed)
+            # the slice could stay in L2: a 512 MB read on the same stream
+            # evicts it before each step, outside the step's event pair (the
+            # host enqueues the step while the read runs: no idle gap is timed)
             for i in range(K):
                 with torch.cuda.stream(stream):
-                    flush.zero_()
+                    torch.sum(flush, out=flush_out)
                 ev[i][0].record(stream)
                 t.step_device(d_hid[i].data_ptr(), B, d_u[i].data_ptr(), d_tok[i].data_ptr())
                 ev[i][1].record(stream)
@@ -337,7 +363,7 @@ def run_ours(args, cfg):
         for i in range(K):
             if flush is not None:
                 with torch.cuda.stream(stream):
-                    flush.zero_()
+                    torch.sum(flush, out=flush_out)
             t.step_device(d_hid[i].data_ptr(), B, d_u[i].data_ptr(), d_tok[i].data_ptr())
         t.sync()
         kern_ms, n_launch = t.kernel_time()
@@ -349,7 +375,7 @@ def run_ours(args, cfg):
     e2e_s = 0.0
     for i in range(K):
         if flush is not None:
-            flush.zero_()
+            torch.sum(flush, out=flush_out)
             torch.cuda.synchronize()
         h = hid[W + K + i]
         u = us[W + K + i]
@@ -368,11 +394,21 @@ def run_ours(args, cfg):
     if rank == 0:
         peaks, pk_kind = load_peaks()
         rows = t.n_rows
-        # one fused launch per stream: each streams this slice's W and scales
-        # once and reads / writes one stream's hidden, history and token; a
-        # sharded step adds one merge launch (the NCCL all-gather is not ours)
-        launches_per_step = B + (1 if world > 1 else 0)
-        alg = algorithmic_bytes(cfg, 1, rows)
+        batched = B >= 2
+        if batched:
+            # quantize + tensor-core GEMM + per-stream select: the GEMM streams
+            # the slice once for all B streams (the timed kernel)
+            launches_per_step = 3
+            alg = algorithmic_bytes(cfg, B, rows)
+            kname = "tcgen05 kind::i8 GEMM (gemm_i8_kernel)"
+        else:
+            # one fused launch per stream: it streams this slice's W and scales
+            # once and reads / writes one stream's hidden, history and token
+            launches_per_step = B
+            alg = algorithmic_bytes(cfg, 1, rows)
+            kname = "fused tail kernel (tail_kernel<MODE_FUSED>)"
+        if world > 1:
+            launches_per_step += 1  # the merge (the NCCL all-gather is not ours)
         achieved = alg / (kern_ms * 1e-3) / 1e9
         peak = float(peaks["hbm_gbs"])
         traffic = load_traffic(cfg.name, world)
@@ -388,10 +424,11 @@ def run_ours(args, cfg):
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1),
                          "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "traffic": traffic,
-                         "note": f"fused tail kernel; {alg} algorithmic bytes per launch on "
+                         "note": f"{kname}; {alg} algorithmic bytes per launch on "
                                  f"rank 0's slice ({rows} rows); peak {pk_kind} "
                                  f"(MEASURED_PEAKS.json hbm_gbs)"},
             "gpu_launches": int(K * launches_per_step),
+            **({"tensor": tensor_roofline(cfg, B, rows, kern_ms)} if batched else {}),
             "kernel_ms": round(kern_ms, 5),
             "clocks": clk.summary(),
         }

@@ -225,11 +225,12 @@ int lal_tail_device_buffers(lal_tail *t, float **d_hidden, float **d_u,
 /* The context's CUDA stream (a cudaStream_t), for callers that order their
  * own work or timing events with the tail's launches. */
 int lal_tail_get_stream(lal_tail *t, void **stream);
-/* Turn on (1) or off (0) CUDA-event timing of each fused-kernel launch. */
+/* Turn on (1) or off (0) CUDA-event timing of each step's dominant kernel:
+ * the fused kernel of a single-stream step (one launch per stream), or the
+ * tensor-core GEMM of a batched step (B >= 2 streams). */
 int lal_tail_set_timing(lal_tail *t, int on);
-/* Average duration in milliseconds of the fused kernel over the launches
- * since the last call (CUDA events on the context's stream), and their
- * count. */
+/* Average duration in milliseconds of that kernel over the launches since
+ * the last call (CUDA events on the context's stream), and their count. */
 int lal_tail_kernel_time(lal_tail *t, double *avg_ms, int *n_launches);
 
 /* Phase timing of the fused kernel (inspection hook).  When on, every launch

@@ -166,6 +166,7 @@ struct GemmParams {
     const float *scale_w;
     const float *scale_x;
     float *logits; /* [B][rows] */
+    uint32_t *gmax; /* [rows/32][N] order key of each 32-row group's largest logit */
     int rows, B, N, kblocks, stages, stage_bytes, tmem_cols;
     int *status;
 };
@@ -295,20 +296,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_i8_kernel(const __grid_c
             tc_fence_after();
             const int row = tile * kBM + q * 32 + lane;
             const float sw = row < p.rows ? __ldg(p.scale_w + row) : 0.0f;
+            const int group = tile * 4 + q; /* this warp's 32 rows */
             for (int c0 = 0; c0 < p.N; c0 += 32) {
                 uint32_t r[32];
                 tmem_ld32(tbase + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * p.N + c0), r);
                 tmem_ld_wait();
-                if (row < p.rows) {
+                uint32_t mine = 0u;
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const int b = c0 + j;
-                        if (b < p.B)
-                            /* runtime/lal_q8_kernel.h:489: scale_x*scale_w[v]*(float)dot */
-                            p.logits[(size_t)b * p.rows + row] =
-                                __fmul_rn(__fmul_rn(sx[b], sw), __int2float_rn((int)r[j]));
-                    }
+                for (int j = 0; j < 32; ++j) {
+                    const int b = c0 + j;
+                    /* runtime/lal_q8_kernel.h:489: scale_x*scale_w[v]*(float)dot */
+                    const float l = __fmul_rn(__fmul_rn(sx[b], sw), __int2float_rn((int)r[j]));
+                    if (row < p.rows && b < p.B) p.logits[(size_t)b * p.rows + row] = l;
+                    /* the group maximum of stream b, kept by lane j */
+                    const uint32_t gm = __reduce_max_sync(0xffffffffu, row < p.rows ? f2key(l) : 0u);
+                    if (lane == j) mine = gm;
                 }
+                p.gmax[(size_t)group * p.N + c0 + lane] = mine;
             }
             tc_fence_before();
             __syncwarp();
@@ -345,6 +349,8 @@ struct BatchSelectParams {
     uint8_t *shard_out; /* [B][rec_bytes] records, or null */
     int rec_cap, rec_bytes;
     int s_cap, c_cap, h_slots; /* superset, candidate and hash capacities */
+    const uint32_t *gmax;      /* [n_groups][gstride] raw group maxima (GEMM) */
+    int n_groups, gstride;
 };
 
 constexpr uint32_t kEmptySlot = 0xFFFFFFFFu;
@@ -381,6 +387,8 @@ __global__ void __launch_bounds__(NT, 1) batch_select_kernel(const __grid_consta
      * counted in an open-addressing hash, applied once per occurrence
      * (runtime/lal_sampling.h:60-66; ids outside [0, V) are skipped) */
     for (int i = tid; i < 4096; i += NT) hist[i] = 0u;
+    __shared__ int s_pen; /* distinct history ids inside this slice */
+    if (tid == 0) s_pen = 0;
     if (use_pen) {
         for (int i = tid; i < p.h_slots; i += NT) {
             hkey[i] = kEmptySlot;
@@ -398,6 +406,7 @@ __global__ void __launch_bounds__(NT, 1) batch_select_kernel(const __grid_consta
                 const uint32_t prev = atomicCAS(&hkey[slot], kEmptySlot, (uint32_t)id);
                 if (prev == kEmptySlot || prev == (uint32_t)id) {
                     atomicAdd(&hcnt[slot], 1u);
+                    if (prev == kEmptySlot) atomicAdd(&s_pen, 1);
                     break;
                 }
                 slot = (slot + 1u) & mask;
@@ -414,12 +423,110 @@ __global__ void __launch_bounds__(NT, 1) batch_select_kernel(const __grid_consta
     }
     __syncthreads();
 
-    /* 2. k = min(top_k, V) (runtime/lal_sampling.h:70-71), 1 for greedy; the
-     * top 12 key bits of every logit into the histogram */
+    /* 2. k = min(top_k, V) (runtime/lal_sampling.h:70-71), 1 for greedy */
     int k = greedy ? 1 : topk;
     if (k > p.vocab) k = p.vocab;
     if (k > p.rows) k = p.rows;
     if (k < 1) k = 1;
+    constexpr int U = 8;
+    StreamDiag dg;
+    dg.threshold = 0.0f;
+    dg.max_l = 0.0f;
+    dg.sum = 0.0f;
+    dg.r = 0.0f;
+    dg.n_cand = 0;
+    dg.greedy = greedy ? 1 : 0;
+    dg.drew = 0;
+    dg.token = -1;
+    auto fail_stream = [&](int st) {
+        if (tid == 0) {
+            if (p.shard_out != nullptr) {
+                ShardRecordHead *h =
+                    reinterpret_cast<ShardRecordHead *>(p.shard_out + (size_t)b * p.rec_bytes);
+                h->count = 0;
+                h->status = st;
+            } else {
+                atomicCAS(p.status, 0, st);
+                p.tokens[b] = -1;
+            }
+            p.diag[b] = dg;
+        }
+    };
+
+    /* 3. a tie-complete superset of {l >= T}: keys >= a lower bound L of T.
+     *
+     * Group bound (the GEMM recorded each 32-row group's largest raw logit):
+     * with P distinct penalised ids in the slice, the (k+P)-th largest group
+     * maximum L is <= T -- its k+P groups hold k+P distinct logits >= L, at
+     * most P of them penalised, and a penalty (p > 1) never raises a logit --
+     * and only groups whose raw maximum reaches L can hold a key >= L.  When
+     * that bound is weak the full histogram pass below is used instead. */
+    uint32_t L = 0u;
+    int S = -1;
+    const int kp = k + s_pen;
+    const bool groups = p.gmax != nullptr && kp <= p.n_groups / 8 && p.n_groups <= p.s_cap;
+    if (groups) {
+        uint32_t *Gk = Sk; /* the group maxima, then the superset */
+        for (int g = tid; g < p.n_groups; g += NT) Gk[g] = __ldg(p.gmax + (size_t)g * p.gstride + b);
+        __syncthreads();
+        L = block_kth_largest(
+            [&](int i, uint32_t &key) {
+                key = Gk[i];
+                return true;
+            },
+            p.n_groups, kp, ms);
+        /* the candidate groups, listed in Ci */
+        if (tid == 0) s_count = 0;
+        __syncthreads();
+        for (int g = tid; g < p.n_groups; g += NT)
+            if (Gk[g] >= L) {
+                const int at = atomicAdd(&s_count, 1);
+                if (at < p.c_cap) Ci[at] = g;
+            }
+        __syncthreads();
+        const int ng = s_count;
+        __syncthreads();
+        if (ng <= p.c_cap) {
+            if (tid == 0) s_count = 0;
+            __syncthreads();
+            /* gather the groups' keys >= L (32 consecutive rows a group) */
+            const int total = ng * 32;
+            for (int i0 = 0; i0 < total; i0 += NT * U) {
+                float v[U];
+                int rr[U];
+#pragma unroll
+                for (int j = 0; j < U; ++j) {
+                    const int e = i0 + j * NT + tid;
+                    rr[j] = e < total ? Ci[e >> 5] * 32 + (e & 31) : p.rows;
+                    v[j] = rr[j] < p.rows ? lg[rr[j]] : 0.0f;
+                }
+#pragma unroll
+                for (int j = 0; j < U; ++j) {
+                    const uint32_t key = f2key(v[j]);
+                    const bool take = rr[j] < p.rows && key >= L;
+                    const unsigned bal = __ballot_sync(0xffffffffu, take);
+                    int base = 0;
+                    if ((tid & 31) == 0 && bal) base = atomicAdd(&s_count, __popc(bal));
+                    base = __shfl_sync(0xffffffffu, base, 0);
+                    if (take) {
+                        const int pos = base + __popc(bal & ((1u << (tid & 31)) - 1u));
+                        if (pos < p.s_cap) {
+                            Sk[pos] = key;
+                            Si[pos] = rr[j];
+                        }
+                    }
+                }
+            }
+            __syncthreads();
+            S = s_count;
+            if (S > p.s_cap) {
+                fail_stream((int)DEV_CAPACITY);
+                return;
+            }
+        }
+    }
+    if (S < 0) {
+    /* full pass: the top 12 key bits of every logit into the histogram */
     auto hist_add = [&](uint32_t *h, uint32_t digit, bool act) {
         const unsigned voters = __ballot_sync(0xffffffffu, act);
         if (act) {
@@ -427,7 +534,6 @@ __global__ void __launch_bounds__(NT, 1) batch_select_kernel(const __grid_consta
             if ((tid & 31) == __ffs(peers) - 1) atomicAdd(&h[digit], (uint32_t)__popc(peers));
         }
     };
-    constexpr int U = 8;
     for (int i0 = 0; i0 < p.rows; i0 += NT * U) {
         float v[U];
 #pragma unroll
@@ -473,38 +579,14 @@ __global__ void __launch_bounds__(NT, 1) batch_select_kernel(const __grid_consta
         prefix |= bin2 << shift;
         pmask |= 1023u << shift;
     }
-    const uint32_t L = prefix;
-    const int S = (int)(above + cnt);
-
-    StreamDiag dg;
-    dg.threshold = 0.0f;
-    dg.max_l = 0.0f;
-    dg.sum = 0.0f;
-    dg.r = 0.0f;
-    dg.n_cand = 0;
-    dg.greedy = greedy ? 1 : 0;
-    dg.drew = 0;
-    dg.token = -1;
-    auto fail_stream = [&](int st) {
-        if (tid == 0) {
-            if (p.shard_out != nullptr) {
-                ShardRecordHead *h =
-                    reinterpret_cast<ShardRecordHead *>(p.shard_out + (size_t)b * p.rec_bytes);
-                h->count = 0;
-                h->status = st;
-            } else {
-                atomicCAS(p.status, 0, st);
-                p.tokens[b] = -1;
-            }
-            p.diag[b] = dg;
-        }
-    };
+    L = prefix;
+    S = (int)(above + cnt);
     if (S > p.s_cap) {
         fail_stream((int)DEV_CAPACITY);
         return;
     }
 
-    /* 3. the superset {key >= L} (every candidate is in it) */
+    /* the superset {key >= L} (every candidate is in it) */
     if (tid == 0) s_count = 0;
     __syncthreads();
     for (int i0 = 0; i0 < p.rows; i0 += NT * U) {
@@ -533,6 +615,7 @@ __global__ void __launch_bounds__(NT, 1) batch_select_kernel(const __grid_consta
         }
     }
     __syncthreads();
+    }  /* full pass */
 
     /* 4. T exactly: the k-th largest key of the superset */
     const uint32_t T = block_kth_largest(
@@ -731,7 +814,7 @@ size_t batch_select_smem(int s_cap, int c_cap, int h_slots) {
 }
 
 int batch_plan(BatchPlan &bp, const int8_t *W, const float *scale_w, int rows, int ld,
-               int num_sms, int8_t *xq, float *sx, int max_B, int hist_cap) {
+               int num_sms, int8_t *xq, float *sx, uint32_t *gmax, int max_B, int hist_cap) {
     memset(&bp, 0, sizeof(bp));
     if (!encoder()) return -3;
     if (ld < kBK || ld % 16 != 0 || max_B < 2 || max_B > 256 || rows < 1) return -1;
@@ -741,6 +824,8 @@ int batch_plan(BatchPlan &bp, const int8_t *W, const float *scale_w, int rows, i
     bp.ld = ld;
     bp.xq = xq;
     bp.sx = sx;
+    bp.gmax = gmax;
+    bp.n_groups = batch_groups(rows);
     bp.num_sms = num_sms;
     bp.kblocks = (ld + kBK - 1) / kBK;
     /* select capacities: superset, candidates, history hash (>= 2x the
@@ -782,6 +867,7 @@ cudaError_t batch_launch(BatchPlan &bp, const BatchStep &s, cudaStream_t st) {
     g.scale_w = bp.scale_w;
     g.scale_x = bp.sx;
     g.logits = s.logits;
+    g.gmax = bp.gmax;
     g.rows = bp.rows;
     g.B = s.B;
     g.N = N;
@@ -799,9 +885,17 @@ cudaError_t batch_launch(BatchPlan &bp, const BatchStep &s, cudaStream_t st) {
     if (e != cudaSuccess) return e;
     const int n_tiles = (bp.rows + kBM - 1) / kBM;
     const int grid = std::min(n_tiles, bp.num_sms);
+    if (s.gemm_ev0) {
+        e = cudaEventRecord(s.gemm_ev0, st);
+        if (e != cudaSuccess) return e;
+    }
     gemm_i8_kernel<<<grid, kGemmThreads, gsmem, st>>>(g);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
+    if (s.gemm_ev1) {
+        e = cudaEventRecord(s.gemm_ev1, st);
+        if (e != cudaSuccess) return e;
+    }
     /* 3. per stream: penalty, select, draw (or the shard record) */
     BatchSelectParams q;
     memset(&q, 0, sizeof(q));
@@ -834,6 +928,9 @@ cudaError_t batch_launch(BatchPlan &bp, const BatchStep &s, cudaStream_t st) {
     q.s_cap = bp.s_cap;
     q.c_cap = bp.c_cap;
     q.h_slots = bp.h_slots;
+    q.gmax = bp.gmax;
+    q.n_groups = bp.n_groups;
+    q.gstride = N;
     const size_t ssmem = batch_select_smem(bp.s_cap, bp.c_cap, bp.h_slots);
     e = raise_smem((const void *)batch_select_kernel, kGemmSmemLimit - 8192);
     if (e != cudaSuccess) return e;

@@ -219,6 +219,8 @@ struct BatchPlan {
     int rows, ld, num_sms, kblocks;
     int8_t *xq;        /* [256][ld] quantized hidden vectors                     */
     float *sx;         /* [256] their scales                                     */
+    uint32_t *gmax;    /* [n_groups][256] raw maxima of 32-row groups, per stream */
+    int n_groups;
     int s_cap, c_cap, h_slots;
     /* TMA descriptors (CUtensorMap, 128 bytes each): W, and X for N = 32..256 */
     alignas(64) unsigned char tm_w[128];
@@ -246,10 +248,13 @@ struct BatchStep {
     const uint32_t *expf_off;
     uint8_t *shard_out; /* per-stream records (vocab-sharded select), or null */
     int rec_cap, rec_bytes;
+    cudaEvent_t gemm_ev0, gemm_ev1; /* optional: recorded around the GEMM launch */
 };
 /* 0 when the shape takes the batched path (d >= 128, 2 <= max_B <= 256). */
 int batch_plan(BatchPlan &bp, const int8_t *W, const float *scale_w, int rows, int ld,
-               int num_sms, int8_t *xq, float *sx, int max_B, int hist_cap);
+               int num_sms, int8_t *xq, float *sx, uint32_t *gmax, int max_B, int hist_cap);
+/* 32-row groups of a slice of `rows` rows (the gmax buffer holds 256 words each) */
+inline int batch_groups(int rows) { return (rows + 127) / 128 * 4; }
 cudaError_t batch_launch(BatchPlan &bp, const BatchStep &s, cudaStream_t st);
 int plan_launch(TailParams &p, int num_sms, int min_rows_per_cta);
 cudaError_t launch_tail(const TailParams &p, int grid, cudaStream_t st);

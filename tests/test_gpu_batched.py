@@ -59,11 +59,14 @@ def test_batched_logits_bit_exact(V, d, B):
 
 
 @pytest.mark.parametrize("variant", [0, 1])
-def test_batched_decode_loops_match_oracle(variant):
-    """B = 6 streams, per-stream temperature and history, 6 steps."""
+@pytest.mark.parametrize("vocab,top_k,hist", [(9000, 50, 256), (40000, 20, 64)])
+def test_batched_decode_loops_match_oracle(variant, vocab, top_k, hist):
+    """B = 6 streams, per-stream temperature and history, 6 steps.  The
+    first shape is too small for the group bound (k + history ids above an
+    eighth of the 32-row groups: full histogram pass), the second takes it."""
     base = synth.CONFIGS["c3_batch"]
     B = 6
-    cfg = base.with_(vocab=9000, n_embd=512, streams=B, steps=6)
+    cfg = base.with_(vocab=vocab, n_embd=512, streams=B, steps=6, top_k=top_k, hist=hist)
     W = synth.lm_head_f32(cfg)
     q, s = oracle.quantize_rows(W, "port")
     temps = synth.temperatures(cfg)[:B]
