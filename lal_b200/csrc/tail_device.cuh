@@ -65,6 +65,15 @@ __device__ bool mbar_wait(uint64_t *b, uint32_t parity, volatile int *abort_flag
         }
     }
 }
+/* Programmatic dependent launch: wait until the preceding kernel on the
+ * stream has completed and its writes are visible (returns at once when the
+ * launch did not overlap one); let the next launch begin to schedule. */
+__device__ __forceinline__ void grid_dep_wait() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void grid_dep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
 __device__ __forceinline__ uint64_t policy_evict_first() {
     uint64_t pol;
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
@@ -80,6 +89,11 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
         : "memory");
 }
 
+__device__ __forceinline__ unsigned atom_add_acq_rel_gpu(unsigned *p, unsigned v) {
+    unsigned old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
 __device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned *p) {
     unsigned v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -127,6 +141,31 @@ __device__ __forceinline__ float expf_with_word(float x, uint32_t word, const ui
     const uint32_t b = (xb - 0x80000000u) >> 8;
     if ((xb & 0x80000000u) && x <= 0.0f && ((word >> (b & 31)) & 1u))
         return expf_fixup(x, tx, ty, off);
+    return lal_expf_rounded(x);
+}
+
+/* The table range of x's bitmap word (loaded beside the word itself, so a
+ * flagged x needs one more round trip, not two); 0..0 for x the table never
+ * holds (x > 0, NaN). */
+__device__ __forceinline__ void expf_offsets(float x, const uint32_t *off, uint32_t *lo,
+                                             uint32_t *hi) {
+    const uint32_t xb = __float_as_uint(x);
+    if ((xb & 0x80000000u) && x <= 0.0f) {
+        const uint32_t w = (xb - 0x80000000u) >> 13;
+        *lo = __ldg(off + w);
+        *hi = __ldg(off + w + 1);
+    } else {
+        *lo = 0u;
+        *hi = 0u;
+    }
+}
+__device__ __forceinline__ float expf_with_range(float x, uint32_t word, uint32_t lo, uint32_t hi,
+                                                 const uint32_t *tx, const uint32_t *ty) {
+    const uint32_t xb = __float_as_uint(x);
+    const uint32_t b = (xb - 0x80000000u) >> 8;
+    if ((xb & 0x80000000u) && x <= 0.0f && ((word >> (b & 31)) & 1u))
+        for (uint32_t i = lo; i < hi; ++i)
+            if (__ldg(tx + i) == xb) return __uint_as_float(__ldg(ty + i));
     return lal_expf_rounded(x);
 }
 

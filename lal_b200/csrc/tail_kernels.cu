@@ -34,6 +34,7 @@
 
 #include <algorithm>
 #include <cstdio>
+#include <cstring>
 #include <utility>
 #include <vector>
 
@@ -59,21 +60,25 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
     uint32_t *hist_s = reinterpret_cast<uint32_t *>(smem + p.off_hist); /* 4096 bins */
     Misc *ms = reinterpret_cast<Misc *>(smem + p.off_misc);
 
-    /* stream 0 sampling parameters */
+    /* stream 0 sampling parameters (the last CTA also uses u0 and the ring
+     * words) */
     float temp = 0.0f, pen = 1.0f, u0 = 0.0f;
     int topk = 0, hn = 0, hhead = 0;
-    if (MODE != MODE_LMHEAD) {
-        /* read early (every CTA): the last CTA uses u0 and the ring words */
-        temp = p.temperature[0];
-        topk = p.top_k[0];
-        pen = p.rep_penalty[0];
-        hn = p.hist_n ? p.hist_n[0] : 0;
-        hhead = p.hist_head ? p.hist_head[0] : 0;
-        u0 = p.u[0];
-    }
-    const bool greedy = (temp <= 0.0f) || (topk <= 0);
-    const bool use_pen = (MODE != MODE_LMHEAD) && (pen > 1.0f) && hn > 0 &&
-                         (p.variant == VARIANT_SERVER || !greedy);
+    bool greedy = false, use_pen = false;
+    auto load_params = [&]() {
+        if (MODE != MODE_LMHEAD) {
+            temp = p.temperature[0];
+            topk = p.top_k[0];
+            pen = p.rep_penalty[0];
+            hn = p.hist_n ? p.hist_n[0] : 0;
+            hhead = p.hist_head ? p.hist_head[0] : 0;
+            u0 = p.u[0];
+        }
+        greedy = (temp <= 0.0f) || (topk <= 0);
+        use_pen = (MODE != MODE_LMHEAD) && (pen > 1.0f) && hn > 0 &&
+                  (p.variant == VARIANT_SERVER || !greedy);
+    };
+    const bool stream_warp = MODE != MODE_SAMPLE && warp == kConsumerWarps;
 
     /* ---- phase 0: barriers -------------------------------------------- */
     if (tid == 0) {
@@ -88,6 +93,15 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
         }
     }
     __syncthreads();
+    /* The fused launch may start while the previous kernel on the stream is
+     * still running (programmatic dependent launch).  The LM head is never
+     * written by a step, so the producer warp streams it at once; every
+     * other read (hidden vector, history ring, sampling parameters, select
+     * scratch) waits for the previous kernel to complete. */
+    if (!stream_warp) {
+        grid_dep_wait();
+        load_params();
+    }
 
     /* ---- the consumer warps' prologue (the producer streams meanwhile):
      * quantized vector, row scales, penalty counts ------------------------ */
@@ -262,6 +276,12 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
         }
         __syncthreads();
         if (tid == 0) stamp(p, cta * 8 + 2);
+        /* this CTA's rows are done: the next launch may begin to stream */
+        grid_dep_launch_dependents();
+        if (stream_warp) {
+            grid_dep_wait();
+            load_params();
+        }
         if (MODE == MODE_LMHEAD) {
             if (tid == 0 && ms->abort_flag) atomicCAS(p.status, 0, (int)DEV_TIMEOUT);
             return;
@@ -427,16 +447,18 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
         }
     }
 
-    /* ---- phase 3: the last CTA to arrive selects and samples ------------ */
-    __threadfence();
+    /* ---- phase 3: the last CTA to arrive selects and samples ------------ *
+     * The barrier orders every thread's writes above before thread 0's
+     * acquire-release ticket, which publishes them at GPU scope; in the last
+     * CTA the same atomic acquires every other CTA's writes, and the barrier
+     * after it orders all of its threads' reads behind that. */
     __syncthreads();
     if (tid == 0) {
-        ms->ticket = (int)atomicAdd(&p.counter[0], 1u);
+        ms->ticket = (int)atom_add_acq_rel_gpu(&p.counter[0], 1u);
         stamp(p, cta * 8 + 7);
     }
     __syncthreads();
     if (ms->ticket != G - 1) return;
-    __threadfence();
     if (tid == 0) stamp(p, G * 8 + 0);
 
     /* shared-memory plan of the stage area: superset keys + indices (Sk, Si),
@@ -493,12 +515,19 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
             if (tid < G) ms->gm[tid] = gmx;
             __syncthreads();
             if (tid == 0) stamp(p, cta * 8 + 4);
+            /* (the gm tail up to a multiple of 4 is zero: it never counts) */
+            if (tid >= G && tid < ((G + 3) & ~3)) ms->gm[tid] = 0u;
+            __syncthreads();
             uint32_t best = 0xffffffffu;
+            const uint4 *g4 = reinterpret_cast<const uint4 *>(ms->gm);
             for (int g = tid; g < G; g += NT) {
                 const uint32_t me = ms->gm[g];
                 int gt = 0;
-#pragma unroll 8
-                for (int j = 0; j < G; ++j) gt += ms->gm[j] > me;
+#pragma unroll 4
+                for (int j = 0; j < (G + 3) >> 2; ++j) {
+                    const uint4 v = g4[j];
+                    gt += (v.x > me) + (v.y > me) + (v.z > me) + (v.w > me);
+                }
                 if (gt < k) best = min(best, me);
             }
             best = __reduce_min_sync(0xffffffffu, best);
@@ -574,7 +603,7 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
     const bool early = fine && !greedy && S <= 2 * NT && S <= ccap;
     float max_l = -1e30f;
     float xw[2] = {0.0f, 0.0f};
-    uint32_t bw[2] = {0u, 0u};
+    uint32_t bw[2] = {0u, 0u}, olo[2] = {0u, 0u}, ohi[2] = {0u, 0u};
     if (early) {
         uint32_t mk = 0u;
         for (int j = tid; j < S; j += NT) mk = max(mk, Sk[j]);
@@ -591,6 +620,7 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
             if (j < S) {
                 xw[r] = __fdiv_rn(__fsub_rn(key2f(Sk[j]), max_l), temp);
                 bw[r] = expf_bitmap_word(xw[r], p.expf_bits);
+                expf_offsets(xw[r], p.expf_off, &olo[r], &ohi[r]);
             }
         }
     }
@@ -623,7 +653,7 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
 #pragma unroll
             for (int r = 0; r < 2; ++r) {
                 const int j = tid + r * NT;
-                if (j < S) Ws[j] = expf_with_word(xw[r], bw[r], p.expf_x, p.expf_y, p.expf_off);
+                if (j < S) Ws[j] = expf_with_range(xw[r], bw[r], olo[r], ohi[r], p.expf_x, p.expf_y);
             }
         }
         /* a slot whose dropped tail reaches T lost candidates: refuse */
@@ -1272,6 +1302,23 @@ cudaError_t launch_tail(const TailParams &p, int grid, cudaStream_t st) {
     cudaError_t e = raise_smem(fn, kSmemLimit);
     if (e != cudaSuccess) return e;
     void *args[] = {const_cast<TailParams *>(&p)};
+    if (p.mode == MODE_FUSED && p.local_edges) {
+        /* programmatic dependent launch: the kernel streams W while the
+         * previous kernel on the stream finishes, and waits for it before
+         * any other read */
+        cudaLaunchConfig_t cfg;
+        memset(&cfg, 0, sizeof(cfg));
+        cfg.gridDim = dim3(grid);
+        cfg.blockDim = dim3(NT);
+        cfg.dynamicSmemBytes = (size_t)p.smem_total;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        return cudaLaunchKernelExC(&cfg, fn, args);
+    }
     /* The select's grid barriers need every CTA resident: a cooperative
      * launch guarantees it (or fails to launch). */
     if (p.mode == MODE_LMHEAD || p.local_edges)
