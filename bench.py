@@ -245,7 +245,7 @@ def run_reference_arm(args, cfg):
         "e2e": {"value": round(val, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 def workload(cfg, n):
@@ -407,7 +407,8 @@ def run_ours(args, cfg):
             launches_per_step = B
             alg = algorithmic_bytes(cfg, 1, rows)
             kname = "fused tail kernel (tail_kernel<MODE_FUSED>)"
-        if world > 1:
+        peer = world > 1 and getattr(t, "p2p", False) and B == 1
+        if world > 1 and not peer:
             launches_per_step += 1  # the merge (the NCCL all-gather is not ours)
         achieved = alg / (kern_ms * 1e-3) / 1e9
         peak = float(peaks["hbm_gbs"])
@@ -428,6 +429,10 @@ def run_ours(args, cfg):
                                  f"rank 0's slice ({rows} rows); peak {pk_kind} "
                                  f"(MEASURED_PEAKS.json hbm_gbs)"},
             "gpu_launches": int(K * launches_per_step),
+            **({"exchange": "peer: each rank's last CTA writes its candidate record into every "
+                            "rank's buffer over NVLink and merges (one kernel per step)"
+                if peer else "NCCL all-gather of the candidate records + merge kernel"}
+               if world > 1 else {}),
             **({"tensor": tensor_roofline(cfg, B, rows, kern_ms)} if batched else {}),
             "kernel_ms": round(kern_ms, 5),
             "clocks": clk.summary(),
@@ -442,14 +447,30 @@ def run_ours(args, cfg):
                                "sample": f"{done} decode-tail steps of {cfg.name} "
                                          f"(~{args.cpu_seconds:.0f} s bound)"}
     if out is not None:
-        print(json.dumps(out), flush=True)
+        emit(out)
     t.close()
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
 
 
+_RESULT_OUT = None
+
+
+def emit(line: dict):
+    """The one JSON line, on the process's real stdout."""
+    out = _RESULT_OUT or sys.stdout
+    out.write(json.dumps(line) + "\n")
+    out.flush()
+
+
 def main():
+    global _RESULT_OUT
+    # libraries (NCCL's version banner, ...) may print to fd 1: keep a private
+    # handle on the real stdout for the result line, send fd 1 to stderr
+    sys.stdout.flush()
+    _RESULT_OUT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
     args = parse()
     cfg = synth.CONFIGS[args.config]
     if args.impl == "reference":

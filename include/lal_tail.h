@@ -213,6 +213,19 @@ int lal_tail_fetch_tokens(lal_tail *t, int n_streams, int *tokens_out);
  *      into its history copy and writes d_tokens_out.
  * A failing shard (status in its record) fails the step on every rank. */
 int lal_tail_shard_select(lal_tail *t, const float *d_hidden, int n_streams);
+/* Peer exchange (single-stream steps, one process per GPU): every rank
+ * exports the IPC handle of its receive buffer, gathers all ranks' handles
+ * (rank order) and connects; afterwards lal_tail_step / lal_tail_step_device
+ * with one stream run the whole sharded step in one kernel per rank: the last
+ * CTA writes its record into every rank's buffer over NVLink (plain stores),
+ * waits -- bounded, LAL_TAIL_ERR_TIMEOUT after 2 s -- for every rank's
+ * record of the step, merges them and draws.  Every rank must step in
+ * lockstep (the step's sequence number is counted per context; connecting
+ * again restarts it). */
+#define LAL_TAIL_IPC_HANDLE_BYTES 64
+int lal_tail_exchange_handle(lal_tail *t, void *handle_out);
+int lal_tail_connect_peers(lal_tail *t, const void *handles);
+int lal_tail_disconnect_peers(lal_tail *t);
 int lal_tail_exchange_buffers(lal_tail *t, int n_streams, void **d_send, void **d_recv,
                               size_t *bytes_per_rank);
 int lal_tail_shard_merge(lal_tail *t, int n_streams, const float *d_u, int *d_tokens_out);

@@ -117,6 +117,9 @@ SIGNATURES = {
     "lal_tail_exchange_buffers": (C.c_int, [_vp, _ip, C.POINTER(_vp), C.POINTER(_vp),
                                             C.POINTER(C.c_size_t)]),
     "lal_tail_shard_merge": (C.c_int, [_vp, _ip, _vp, _vp]),
+    "lal_tail_exchange_handle": (C.c_int, [_vp, _vp]),
+    "lal_tail_connect_peers": (C.c_int, [_vp, _vp]),
+    "lal_tail_disconnect_peers": (C.c_int, [_vp]),
     "lal_tail_sample_token_noalloc": (C.c_int, [_vp, _ip, _fp, _ip, _fp, _vp, _ip, _fp, _vp,
                                                 C.POINTER(C.c_int)]),
     "lal_tail_get_diag": (C.c_int, [_vp, _ip, C.POINTER(TailDiag)]),
@@ -379,3 +382,20 @@ class DecodeTail:
 
     def shard_merge(self, n_streams: int, d_u: int, d_tokens: int):
         _check(lib().lal_tail_shard_merge(self.h, n_streams, d_u, d_tokens))
+
+    def exchange_handle(self) -> bytes:
+        """IPC handle (64 bytes) of this rank's peer-exchange receive buffer."""
+        buf = C.create_string_buffer(64)
+        _check(lib().lal_tail_exchange_handle(self.h, buf))
+        return buf.raw
+
+    def connect_peers(self, handles):
+        """handles: every rank's exchange_handle(), in rank order."""
+        blob = b"".join(handles)
+        if len(blob) != 64 * self.cfg.shard_count:
+            raise ValueError("one 64-byte handle per rank expected")
+        buf = C.create_string_buffer(blob, len(blob))
+        _check(lib().lal_tail_connect_peers(self.h, buf))
+
+    def disconnect_peers(self):
+        _check(lib().lal_tail_disconnect_peers(self.h))

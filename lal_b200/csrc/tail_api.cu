@@ -820,17 +820,34 @@ struct lal_tail {
     float *sx_b = nullptr;
     uint32_t *gmax_b = nullptr;
     BatchPlan bplan;
+    /* peer exchange of the sharded step: this rank's receive buffer
+     * [2][shard_count][rec_bytes] (exported by IPC handle), the device array
+     * of every rank's buffer, the peers' opened mappings, the step counter */
+    uint8_t *x_peer = nullptr;
+    uint8_t **d_peer = nullptr;
+    int peer_rec_bytes = 0; /* 64-bit words: 2 header + 2 per candidate */
+    std::vector<void *> peer_open;
+    bool p2p = false;
+    unsigned seq = 1;
 };
 
 namespace {
+
+void close_peers(lal_tail *t) {
+    for (void *q : t->peer_open)
+        if (q) cudaIpcCloseMemHandle(q);
+    t->peer_open.clear();
+    t->p2p = false;
+}
 
 void destroy_ctx(lal_tail *t) {
     if (!t) return;
     if (t->device >= 0) cudaSetDevice(t->device);
     if (t->stream) cudaStreamSynchronize(t->stream);
+    close_peers(t);
     void *bufs[] = {t->W, t->sw, t->io_in, t->io_out, t->logits, t->temp, t->topk, t->pen,
                     t->hist_ids, t->hist_n, t->hist_head, t->diag, t->phase_ts,
-                    t->x_send, t->x_recv, t->xq_b, t->sx_b, t->gmax_b};
+                    t->x_send, t->x_recv, t->xq_b, t->sx_b, t->gmax_b, t->x_peer, t->d_peer};
     for (void *b : bufs)
         if (b) cudaFree(b);
     t->sel.free_all();
@@ -899,6 +916,13 @@ int ctx_alloc(lal_tail *t) {
     CU(cudaMemset(t->x_send, 0, (size_t)B * t->rec_bytes));
     CU(cudaMalloc(&t->x_recv, (size_t)c.shard_count * B * t->rec_bytes));
     CU(cudaMemset(t->x_recv, 0, (size_t)c.shard_count * B * t->rec_bytes));
+    if (c.shard_count > 1) {
+        t->peer_rec_bytes = 16 + 16 * t->rec_cap;
+        const size_t pb = 2ull * c.shard_count * t->peer_rec_bytes;
+        CU(cudaMalloc(&t->x_peer, pb));
+        CU(cudaMemset(t->x_peer, 0, pb));
+        CU(cudaMalloc(&t->d_peer, sizeof(uint8_t *) * c.shard_count));
+    }
     /* batched step: one pass over W for all streams on the tensor cores */
     if (B >= 2 && B <= 256) {
         CU(cudaMalloc(&t->xq_b, (size_t)256 * t->ld));
@@ -925,10 +949,12 @@ int enqueue_step(lal_tail *t, const float *d_hidden, int n, const float *d_u, in
     if (!t->loaded) return fail(LAL_TAIL_ERR_STATE, "step before the LM head was loaded");
     if (n < 1 || n > t->cfg.max_streams) return fail(LAL_TAIL_ERR_ARG, "n_streams %d out of range", n);
     if (t->n_set < n) return fail(LAL_TAIL_ERR_STATE, "sampling parameters not set for %d streams", n);
-    if (!shard_export && t->cfg.shard_count > 1)
+    const bool peer = !shard_export && t->cfg.shard_count > 1 && t->p2p && n == 1;
+    if (!shard_export && t->cfg.shard_count > 1 && !peer)
         return fail(LAL_TAIL_ERR_STATE,
-                    "vocab-sharded context: step with lal_tail_shard_select, an all-gather of "
-                    "the records and lal_tail_shard_merge");
+                    "vocab-sharded context: step one stream after lal_tail_connect_peers, or "
+                    "use lal_tail_shard_select, an all-gather of the records and "
+                    "lal_tail_shard_merge");
     const int hc = std::max(1, t->cfg.history_cap);
     if (t->batch_ok && n >= 2 && !getenv_flag("LAL_TAIL_PER_STREAM")) {
         BatchStep bs;
@@ -994,6 +1020,15 @@ int enqueue_step(lal_tail *t, const float *d_hidden, int n, const float *d_u, in
         if (shard_export) {
             p.shard_out = t->x_send + (size_t)b * t->rec_bytes;
             p.rec_cap = t->rec_cap;
+        }
+        if (peer) {
+            p.peer_recv = t->d_peer;
+            p.n_ranks = t->cfg.shard_count;
+            p.rank = t->cfg.shard_rank;
+            p.rec_bytes = t->peer_rec_bytes;
+            p.rec_cap = t->rec_cap;
+            p.seq = t->seq++;
+            if (t->seq == 0) t->seq = 1; /* 0 never matches: buffers start zeroed */
         }
         t->sel.fill(p);
         p.status = t->io_out + t->cfg.max_streams;
@@ -1322,6 +1357,58 @@ int lal_tail_shard_merge(lal_tail *t, int n_streams, const float *d_u, int *d_to
     m.expf_off = t->ds->d_expf_off;
     m.smem_cap = t->merge_cap;
     CU(launch_merge(m, n_streams, t->stream));
+    return LAL_TAIL_OK;
+}
+
+int lal_tail_exchange_handle(lal_tail *t, void *handle_out) {
+    CHECK(ctx_check(t));
+    if (!handle_out) return fail(LAL_TAIL_ERR_ARG, "exchange_handle: null");
+    if (!t->x_peer) return fail(LAL_TAIL_ERR_STATE, "exchange_handle: context is not sharded");
+    static_assert(sizeof(cudaIpcMemHandle_t) == LAL_TAIL_IPC_HANDLE_BYTES, "IPC handle size");
+    cudaIpcMemHandle_t h;
+    CU(cudaIpcGetMemHandle(&h, t->x_peer));
+    memcpy(handle_out, &h, sizeof(h));
+    return LAL_TAIL_OK;
+}
+
+int lal_tail_connect_peers(lal_tail *t, const void *handles) {
+    CHECK(ctx_check(t));
+    if (!handles) return fail(LAL_TAIL_ERR_ARG, "connect_peers: null");
+    if (!t->x_peer) return fail(LAL_TAIL_ERR_STATE, "connect_peers: context is not sharded");
+    const int N = t->cfg.shard_count;
+    if (peer_merge_cap(t->plan) < N * t->rec_cap)
+        return fail(LAL_TAIL_ERR_UNSUPPORTED, "connect_peers: %d shards x %d candidates exceed "
+                    "the fused kernel's merge area", N, t->rec_cap);
+    CU(cudaStreamSynchronize(t->stream));
+    close_peers(t);
+    std::vector<uint8_t *> ptrs(N, nullptr);
+    for (int r = 0; r < N; ++r) {
+        if (r == t->cfg.shard_rank) {
+            ptrs[r] = t->x_peer;
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        memcpy(&h, (const uint8_t *)handles + (size_t)r * sizeof(h), sizeof(h));
+        void *q = nullptr;
+        cudaError_t e = cudaIpcOpenMemHandle(&q, h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            close_peers(t);
+            return fail(LAL_TAIL_ERR_COMM, "connect_peers: rank %d: %s", r, cudaGetErrorString(e));
+        }
+        t->peer_open.push_back(q);
+        ptrs[r] = (uint8_t *)q;
+    }
+    CU(cudaMemcpy(t->d_peer, ptrs.data(), sizeof(uint8_t *) * N, cudaMemcpyHostToDevice));
+    CU(cudaMemset(t->x_peer, 0, 2ull * N * t->peer_rec_bytes));
+    t->seq = 1;
+    t->p2p = true;
+    return LAL_TAIL_OK;
+}
+
+int lal_tail_disconnect_peers(lal_tail *t) {
+    CHECK(ctx_check(t));
+    CU(cudaStreamSynchronize(t->stream));
+    close_peers(t);
     return LAL_TAIL_OK;
 }
 

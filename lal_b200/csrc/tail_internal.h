@@ -22,7 +22,8 @@ constexpr int kMaxGrid = 256;
 constexpr int kHistWords = 4096 + 1024 + 1024;
 constexpr int kRefineMax = 2048;
 /* Small-k select: per-CTA slot of the sorted local superset; the strategy is
- * used only for k <= kLocalMaxK (and 4k <= the rows of a CTA). */
+ * used only for k <= kLocalMaxK (and 2k <= the rows of a CTA: each CTA's own
+ * boundary then bounds T usefully; correctness never depends on it). */
 constexpr int kSlot = 128;
 constexpr int kLocalMaxK = 64;
 /* words of the expf exception bitmap: bit (b >> 8) for b = bits(x) - 2^31,
@@ -135,6 +136,13 @@ struct TailParams {
      * count, ascending-index list of at most rec_cap) and stop */
     uint8_t *shard_out;
     int rec_cap;
+    /* vocab-sharded step with the peer exchange (one stream): the last CTA
+     * writes its record into every rank's receive buffer peer_recv[r]
+     * ([2 parities][n_ranks][rec_bytes], NVLink stores), publishes seq, waits
+     * (bounded) for every rank's record of this step and merges them */
+    uint8_t *const *peer_recv;
+    int n_ranks, rank, rec_bytes;
+    unsigned seq;
     /* glibc expf fix-ups; expf_bits has one bit per 256 consecutive negative
      * float bit patterns, set where the table holds an entry */
     const uint32_t *expf_x, *expf_y;
@@ -181,7 +189,7 @@ struct FinishParams {
  * min(top_k, V, rows)) is k: per-CTA histogram edges (no grid barrier) when k
  * is small against a CTA's slice, else the grid-wide histogram. */
 inline int use_local_edges(int k, int rows_per_cta_max) {
-    return k <= kLocalMaxK && 4 * k <= rows_per_cta_max;
+    return k <= kLocalMaxK && 2 * k <= rows_per_cta_max;
 }
 inline int effective_k(float temperature, int top_k, int vocab, int rows) {
     int k = (temperature <= 0.0f || top_k <= 0) ? 1 : top_k;
@@ -196,6 +204,8 @@ cudaError_t launch_merge(const MergeParams &m, int n_streams, cudaStream_t st);
 /* candidates a merge CTA can hold (the gathered records of one stream), or
  * -1 when n_candidates_max does not fit in shared memory */
 int merge_smem_cap(int n_candidates_max);
+/* candidates the fused kernel's last CTA can merge in the peer exchange */
+int peer_merge_cap(const TailParams &p);
 
 /* Allocation-free sampler entry (tail_noalloc.cu): build the expf bitmap and
  * offset index from a device copy of the sorted fix-up table (kernels, no

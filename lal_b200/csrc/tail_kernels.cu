@@ -41,6 +41,128 @@
 namespace lal {
 namespace {
 
+constexpr int kMergeHead = 4 * (kMaxRanks + 4);
+template <class Load>
+__device__ void merge_sample(const MergeParams &mp, int b, uint8_t *area, Misc *ms, Load load);
+
+__device__ __forceinline__ void st_release_sys(unsigned *p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void st_relaxed_sys_u64(uint64_t *p, uint64_t v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_relaxed_sys_u64(const uint64_t *p) {
+    uint64_t v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+/* Peer exchange of the sharded step.  A record slot in a rank's receive
+ * buffer ([2 parities][n_ranks][rec_bytes]) is a run of 64-bit words whose
+ * high half is the step's sequence number: [count | seq], [status | seq],
+ * then per candidate [value bits | seq], [vocab id | seq].  A 64-bit store is
+ * single-copy atomic, so a reader that sees seq in a word has that word's
+ * data: no fence orders the data before a flag, and a stale word (a step
+ * two back, same parity) never matches. */
+__device__ void peer_publish(const TailParams &p, int status, int m, const float *Ov,
+                             const int *Oi) {
+    const size_t slot = ((size_t)(p.seq & 1u) * p.n_ranks + p.rank) * p.rec_bytes;
+    const bool fits = status == 0 && m <= p.rec_cap;
+    const uint64_t hi = (uint64_t)p.seq << 32;
+    for (int r = 0; r < p.n_ranks; ++r) {
+        uint64_t *w = reinterpret_cast<uint64_t *>(p.peer_recv[r] + slot);
+        if (fits)
+            for (int i = threadIdx.x; i < m; i += NT) {
+                st_relaxed_sys_u64(w + 2 + 2 * i, hi | __float_as_uint(Ov[i]));
+                st_relaxed_sys_u64(w + 3 + 2 * i, hi | (uint32_t)Oi[i]);
+            }
+        if (threadIdx.x == 0) {
+            st_relaxed_sys_u64(w + 0, hi | (uint32_t)(fits ? m : 0));
+            st_relaxed_sys_u64(w + 1, hi | (uint32_t)(fits ? 0 : (status != 0 ? status
+                                                                          : (int)DEV_CAPACITY)));
+        }
+    }
+}
+
+/* Wait until w carries this step's sequence number (bounded: the deadline
+ * is a globaltimer value); false on timeout. */
+__device__ __forceinline__ bool poll_word(const uint64_t *w, uint32_t seq, uint64_t deadline,
+                                          uint64_t *out) {
+    for (uint32_t it = 0;; ++it) {
+        const uint64_t v = ld_relaxed_sys_u64(w);
+        if ((uint32_t)(v >> 32) == seq) {
+            *out = v;
+            return true;
+        }
+        if ((it & 15u) == 15u && gtimer() > deadline) return false;
+    }
+}
+
+/* Loader of the peers' records in this rank's own receive buffer. */
+struct PeerRecords {
+    const TailParams &p;
+    Misc *ms;
+    __device__ void operator()(int *roff, int &rbad, uint32_t *Mk, int *Mi, int cap,
+                               float *scratch) const {
+        const int tid = threadIdx.x;
+        const uint8_t *base = p.peer_recv[p.rank] + (size_t)(p.seq & 1u) * p.n_ranks * p.rec_bytes;
+        const uint64_t deadline = gtimer() + kWaitNs;
+        int *rstat = reinterpret_cast<int *>(scratch);
+        if (tid == 0) ms->found = 1;
+        __syncthreads();
+        if (tid < p.n_ranks) {
+            const uint64_t *w = reinterpret_cast<const uint64_t *>(base + (size_t)tid * p.rec_bytes);
+            uint64_t v0 = 0, v1 = 0;
+            if (poll_word(w, p.seq, deadline, &v0) && poll_word(w + 1, p.seq, deadline, &v1)) {
+                roff[tid] = (int)(uint32_t)v0;
+                rstat[tid] = (int)(uint32_t)v1;
+            } else {
+                ms->found = 0;
+            }
+        }
+        __syncthreads();
+        if (tid == 0) {
+            int acc = 0, st = ms->found ? 0 : (int)DEV_TIMEOUT;
+            for (int r = 0; r < p.n_ranks && st == 0; ++r) {
+                const int c = roff[r], s = rstat[r];
+                if (s != 0) st = s;
+                else if (c < 0 || c > p.rec_cap) st = DEV_CAPACITY;
+                roff[r] = acc;
+                acc += c;
+            }
+            roff[p.n_ranks] = acc;
+            if ((acc < 1 || acc > cap) && st == 0) st = DEV_CAPACITY;
+            rbad = st;
+        }
+        __syncthreads();
+        if (rbad != 0) return;
+        const int M = roff[p.n_ranks];
+        for (int e = tid; e < M; e += NT) {
+            int r = 0;
+            while (roff[r + 1] <= e) ++r;
+            const int j = e - roff[r];
+            const uint64_t *w = reinterpret_cast<const uint64_t *>(base + (size_t)r * p.rec_bytes);
+            uint64_t v = 0, x = 0;
+            if (poll_word(w + 2 + 2 * j, p.seq, deadline, &v) &&
+                poll_word(w + 3 + 2 * j, p.seq, deadline, &x)) {
+                Mk[e] = f2key(__uint_as_float((uint32_t)v));
+                Mi[e] = (int)(uint32_t)x;
+            } else {
+                ms->found = 0;
+            }
+        }
+        __syncthreads();
+        if (tid == 0 && !ms->found) rbad = DEV_TIMEOUT;
+        __syncthreads();
+    }
+};
+
 /* ----------------------------------------------------- the kernel --- */
 template <int MODE, int NCH>
 __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ TailParams p) {
@@ -702,6 +824,10 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
         p.counter[0] = 0u;
     }
     if (!fine) {
+        /* a failed slice still publishes (a failure record): the peers fail
+         * the step at once instead of waiting */
+        if (p.peer_recv != nullptr) peer_publish(p, ok ? (int)DEV_CAPACITY : (int)DEV_TIMEOUT, 0,
+                                                 nullptr, nullptr);
         if (tid == 0) {
             const int st = ok ? (int)DEV_CAPACITY : (int)DEV_TIMEOUT;
             /* a shard reports through its record: the merge fails the step
@@ -768,6 +894,41 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
             p.cand_val_out[i] = Ov[i];
             p.cand_idx_out[i] = Oi[i];
         }
+    }
+    if (p.peer_recv != nullptr) {
+        /* vocab-sharded step, peer exchange: publish, wait for every rank's
+         * record of this step, merge and draw like merge_kernel */
+        peer_publish(p, 0, m, Ov, Oi);
+        __syncthreads(); /* Ov / Oi are read before the merge reuses the area */
+        if (tid == 0) stamp(p, G * 8 + 5);
+        MergeParams mp;
+        mp.recv = p.peer_recv[p.rank] + (size_t)(p.seq & 1u) * p.n_ranks * p.rec_bytes;
+        mp.rank_stride = p.rec_bytes;
+        mp.rec_bytes = p.rec_bytes;
+        mp.rec_cap = p.rec_cap;
+        mp.n_ranks = p.n_ranks;
+        mp.vocab = p.vocab;
+        mp.variant = p.variant;
+        mp.temperature = p.temperature;
+        mp.top_k = p.top_k;
+        mp.u = p.u;
+        mp.hist_ids = p.hist_ids;
+        mp.hist_n = p.hist_n;
+        mp.hist_head = p.hist_head;
+        mp.hist_cap = p.hist_cap;
+        mp.push_history = p.push_history;
+        mp.tokens = p.tokens;
+        mp.diag = p.diag;
+        mp.status = p.status;
+        mp.expf_x = p.expf_x;
+        mp.expf_y = p.expf_y;
+        mp.expf_n = p.expf_n;
+        mp.expf_bits = p.expf_bits;
+        mp.expf_off = p.expf_off;
+        mp.smem_cap = (p.area_bytes - kMergeHead) / 24;
+        merge_sample(mp, 0, smem, ms, PeerRecords{p, ms});
+        if (tid == 0) stamp(p, G * 8 + 7);
+        return;
     }
     if (p.shard_out != nullptr) {
         /* vocab-sharded step: this slice's record; the merge draws */
@@ -1026,17 +1187,26 @@ __global__ void debug_expf_kernel(const float *x, float *y, int n, const uint32_
  * the concatenation is in ascending vocab order, the order of the
  * reference's sequential softmax sums (runtime/lal_sampling.h:110-124).
  * Every rank runs the same merge on the same bytes and gets the same token. */
-__global__ void __launch_bounds__(NT) merge_kernel(const MergeParams mp) {
-    extern __shared__ __align__(16) uint8_t msm[];
-    __shared__ Misc msh;
-    __shared__ int roff[kMaxRanks + 1];
-    __shared__ int rbad;
-    Misc *ms = &msh;
-    const int tid = threadIdx.x, b = blockIdx.x;
+/* (kMergeHead: bytes of the merge's shared-memory area before its candidate
+ * arrays -- the per-rank offsets and the failure word.) */
+
+/* The merge of stream b's N shard records and its draw, by one CTA (NT
+ * threads): shared by merge_kernel (records all-gathered into global memory)
+ * and the fused kernel's peer exchange (records written by the peers over
+ * NVLink, polled word by word).  load() fills roff[0..n_ranks] (prefix
+ * offsets), rbad (a DEV_* failure or 0) and the keys / vocab ids of the
+ * concatenated records, ascending vocab order, then synchronises the CTA.
+ * area: kMergeHead bytes + 24 bytes per candidate (mp.smem_cap of them). */
+template <class Load>
+__device__ void merge_sample(const MergeParams &mp, int b, uint8_t *area, Misc *ms, Load load) {
+    int *roff = reinterpret_cast<int *>(area);
+    int &rbad = roff[kMaxRanks + 1];
+    const int tid = threadIdx.x;
     const int cap = mp.smem_cap;
-    uint32_t *Mk = reinterpret_cast<uint32_t *>(msm);
+    uint32_t *Mk = reinterpret_cast<uint32_t *>(area + kMergeHead);
     int *Mi = reinterpret_cast<int *>(Mk + cap);
-    float *Cv = reinterpret_cast<float *>(Mi + cap);
+    float *Mw = reinterpret_cast<float *>(Mi + cap);
+    float *Cv = Mw + cap;
     int *Ci = reinterpret_cast<int *>(Cv + cap);
     float *Ce = reinterpret_cast<float *>(Ci + cap);
 
@@ -1046,22 +1216,7 @@ __global__ void __launch_bounds__(NT) merge_kernel(const MergeParams mp) {
     const int hn = mp.hist_n ? mp.hist_n[b] : 0;
     const int hhead = mp.hist_head ? mp.hist_head[b] : 0;
     const bool greedy = (temp <= 0.0f) || (topk <= 0);
-    auto rec = [&](int r) { return mp.recv + r * mp.rank_stride + (long long)b * mp.rec_bytes; };
-    if (tid == 0) {
-        int acc = 0, st = 0;
-        for (int r = 0; r < mp.n_ranks; ++r) {
-            const ShardRecordHead *h = reinterpret_cast<const ShardRecordHead *>(rec(r));
-            const int c = h->count, s = h->status;
-            if (s != 0 && st == 0) st = s;
-            if ((c < 0 || c > mp.rec_cap) && st == 0) st = DEV_CAPACITY;
-            roff[r] = acc;
-            acc += (c < 0 || c > mp.rec_cap) ? 0 : c;
-        }
-        roff[mp.n_ranks] = acc;
-        if ((acc < 1 || acc > cap) && st == 0) st = DEV_CAPACITY;
-        rbad = st;
-    }
-    __syncthreads();
+    load(roff, rbad, Mk, Mi, cap, Ce);
     StreamDiag dg;
     dg.threshold = 0.0f;
     dg.max_l = 0.0f;
@@ -1080,29 +1235,83 @@ __global__ void __launch_bounds__(NT) merge_kernel(const MergeParams mp) {
         return;
     }
     const int M = roff[mp.n_ranks];
-    for (int r = 0; r < mp.n_ranks; ++r) {
-        const int c = roff[r + 1] - roff[r];
-        const float *rv = reinterpret_cast<const float *>(rec(r) + sizeof(ShardRecordHead));
-        const int *ri = reinterpret_cast<const int *>(rv + mp.rec_cap);
-        for (int i = tid; i < c; i += NT) {
-            Mk[roff[r] + i] = f2key(rv[i]);
-            Mi[roff[r] + i] = ri[i];
-        }
-    }
-    __syncthreads();
     /* k = min(top_k, V) (runtime/lal_sampling.h:70-71), 1 for greedy; every
      * shard exported at least min(k, its rows) entries, so M >= k */
     int k = greedy ? 1 : topk;
     if (k > mp.vocab) k = mp.vocab;
     if (k > M) k = M;
     if (k < 1) k = 1;
-    const uint32_t T = block_kth_largest(
-        [&](int i, uint32_t &key) {
-            key = Mk[i];
-            return true;
-        },
-        M, k, ms);
-    /* candidates {l >= T}, order kept (stable compaction) */
+    /* max_l = the largest entry (every shard's record holds its maximum, and
+     * the overall maximum is a candidate), floored at -1e30f
+     * (runtime/lal_sampling.h:107-109): the weights need not wait for T */
+    uint32_t mk = 0u;
+    for (int e = tid; e < M; e += NT) mk = max(mk, Mk[e]);
+    mk = __reduce_max_sync(0xffffffffu, mk);
+    if ((tid & 31) == 0) ms->scan[tid >> 5] = mk;
+    __syncthreads();
+    uint32_t mx = ms->scan[0];
+    for (int w = 1; w < NWARP; ++w) mx = max(mx, ms->scan[w]);
+    __syncthreads();
+    const float max_l = fmaxf(-1e30f, key2f(mx));
+    dg.max_l = max_l;
+    /* weights expf((l - max_l) / T) (runtime/lal_sampling.h:112): the table
+     * loads go out now and complete behind the threshold search */
+    const bool fast = M <= 2 * NT;
+    float xw[2] = {0.0f, 0.0f};
+    uint32_t bw[2] = {0u, 0u}, olo[2] = {0u, 0u}, ohi[2] = {0u, 0u};
+    if (!greedy) {
+        if (fast) {
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+                const int e = tid + r * NT;
+                if (e < M) {
+                    xw[r] = __fdiv_rn(__fsub_rn(key2f(Mk[e]), max_l), temp);
+                    bw[r] = expf_bitmap_word(xw[r], mp.expf_bits);
+                    expf_offsets(xw[r], mp.expf_off, &olo[r], &ohi[r]);
+                }
+            }
+        } else {
+            for (int e = tid; e < M; e += NT)
+                Mw[e] = sampler_expf(__fdiv_rn(__fsub_rn(key2f(Mk[e]), max_l), temp), mp.expf_x,
+                                     mp.expf_y, mp.expf_bits, mp.expf_off);
+        }
+    }
+    /* T = min{ key : #{keys > key} < k }, the k-th largest with multiplicity */
+    uint32_t T;
+    if (fast) {
+        uint32_t best = 0xffffffffu;
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            const int e = tid + r * NT;
+            if (e < M) {
+                const uint32_t me = Mk[e];
+                int gt = 0;
+#pragma unroll 4
+                for (int j = 0; j < M; ++j) gt += Mk[j] > me;
+                if (gt < k) best = min(best, me);
+            }
+        }
+        best = __reduce_min_sync(0xffffffffu, best);
+        if ((tid & 31) == 0) ms->scan[tid >> 5] = best;
+        __syncthreads();
+        T = ms->scan[0];
+        for (int w = 1; w < NWARP; ++w) T = min(T, ms->scan[w]);
+        if (!greedy)
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+                const int e = tid + r * NT;
+                if (e < M) Mw[e] = expf_with_range(xw[r], bw[r], olo[r], ohi[r], mp.expf_x, mp.expf_y);
+            }
+        __syncthreads();
+    } else {
+        T = block_kth_largest(
+            [&](int i, uint32_t &key) {
+                key = Mk[i];
+                return true;
+            },
+            M, k, ms);
+    }
+    /* candidates {l >= T}, order kept (stable compaction), with weights */
     const int seg = (M + NT - 1) / NT;
     const int e0 = min(M, tid * seg), e1 = min(M, e0 + seg);
     uint32_t c = 0;
@@ -1114,24 +1323,17 @@ __global__ void __launch_bounds__(NT) merge_kernel(const MergeParams mp) {
         if (Mk[e] >= T) {
             Cv[pos] = key2f(Mk[e]);
             Ci[pos] = Mi[e];
+            Ce[pos] = greedy ? 0.0f : Mw[e];
             ++pos;
         }
     __syncthreads();
     dg.threshold = key2f(T);
     dg.n_cand = m;
-    float mx = -1e30f;
-    for (int i = tid; i < m; i += NT) mx = fmaxf(mx, Cv[i]);
-    const float max_l = block_max_f(mx, ms);
-    dg.max_l = max_l;
     int token;
     if (greedy) {
         token = Ci[0];
     } else {
-        for (int i = tid; i < m; i += NT) {
-            const float x = __fdiv_rn(__fsub_rn(Cv[i], max_l), temp);
-            Ce[i] = sampler_expf(x, mp.expf_x, mp.expf_y, mp.expf_bits, mp.expf_off);
-        }
-        __syncthreads();
+        /* sequential float sum in ascending vocab order; keep the prefix */
         if (tid == 0) {
             float acc = 0.0f;
             for (int i = 0; i < m; ++i) {
@@ -1154,6 +1356,8 @@ __global__ void __launch_bounds__(NT) merge_kernel(const MergeParams mp) {
                     token = Ci[i];
                 }
         } else {
+            /* r = u * sum; first candidate with r <= running sum
+             * (runtime/lal_sampling.h:116-124) */
             const float r = __fmul_rn(u0, sum);
             dg.r = r;
             dg.drew = 1;
@@ -1183,6 +1387,51 @@ __global__ void __launch_bounds__(NT) merge_kernel(const MergeParams mp) {
             }
         }
     }
+}
+
+/* Loader of all-gathered records (ShardRecordHead + values + ids) in global
+ * memory: records of stream b from rank r at recv + r*rank_stride +
+ * b*rec_bytes. */
+struct GatheredRecords {
+    const MergeParams &mp;
+    int b;
+    __device__ void operator()(int *roff, int &rbad, uint32_t *Mk, int *Mi, int cap,
+                               float *) const {
+        const int tid = threadIdx.x;
+        auto rec = [&](int r) { return mp.recv + r * mp.rank_stride + (long long)b * mp.rec_bytes; };
+        if (tid == 0) {
+            int acc = 0, st = 0;
+            for (int r = 0; r < mp.n_ranks; ++r) {
+                const ShardRecordHead *h = reinterpret_cast<const ShardRecordHead *>(rec(r));
+                const int c = __ldcg(&h->count), s = __ldcg(&h->status);
+                if (s != 0 && st == 0) st = s;
+                if ((c < 0 || c > mp.rec_cap) && st == 0) st = DEV_CAPACITY;
+                roff[r] = acc;
+                acc += (c < 0 || c > mp.rec_cap) ? 0 : c;
+            }
+            roff[mp.n_ranks] = acc;
+            if ((acc < 1 || acc > cap) && st == 0) st = DEV_CAPACITY;
+            rbad = st;
+        }
+        __syncthreads();
+        if (rbad != 0) return;
+        for (int r = 0; r < mp.n_ranks; ++r) {
+            const int c = roff[r + 1] - roff[r];
+            const float *rv = reinterpret_cast<const float *>(rec(r) + sizeof(ShardRecordHead));
+            const int *ri = reinterpret_cast<const int *>(rv + mp.rec_cap);
+            for (int i = tid; i < c; i += NT) {
+                Mk[roff[r] + i] = f2key(__ldcg(rv + i));
+                Mi[roff[r] + i] = __ldcg(ri + i);
+            }
+        }
+        __syncthreads();
+    }
+};
+
+__global__ void __launch_bounds__(NT) merge_kernel(const MergeParams mp) {
+    extern __shared__ __align__(16) uint8_t msm[];
+    __shared__ Misc msh;
+    merge_sample(mp, blockIdx.x, msm, &msh, GatheredRecords{mp, (int)blockIdx.x});
 }
 
 /* -------------------------------------------------- host planning --- */
@@ -1350,21 +1599,23 @@ cudaError_t launch_finish(const FinishParams &f, cudaStream_t st) {
     return cudaGetLastError();
 }
 
-/* Five words per candidate: gathered key + index, candidate value + index,
- * weight / running sum; the static part (Misc, rank offsets) stays below 8 KB. */
+/* Six words per candidate: gathered key + index + weight, candidate value +
+ * index + weight / running sum; the static part (Misc) stays below 8 KB. */
 constexpr int kMergeDynLimit = kSmemLimit - 8192;
 
+int peer_merge_cap(const TailParams &p) { return (p.area_bytes - kMergeHead) / 24; }
+
 int merge_smem_cap(int n_candidates_max) {
-    return n_candidates_max <= kMergeDynLimit / 20 ? n_candidates_max : -1;
+    return n_candidates_max <= (kMergeDynLimit - kMergeHead) / 24 ? n_candidates_max : -1;
 }
 
 cudaError_t launch_merge(const MergeParams &m, int n_streams, cudaStream_t st) {
-    if (m.smem_cap < 1 || m.smem_cap > kMergeDynLimit / 20 || m.n_ranks < 1 ||
+    if (m.smem_cap < 1 || m.smem_cap > (kMergeDynLimit - kMergeHead) / 24 || m.n_ranks < 1 ||
         m.n_ranks > kMaxRanks)
         return cudaErrorInvalidValue;
     cudaError_t e = raise_smem((const void *)merge_kernel, kMergeDynLimit);
     if (e != cudaSuccess) return e;
-    merge_kernel<<<n_streams, NT, 20ull * (size_t)m.smem_cap, st>>>(m);
+    merge_kernel<<<n_streams, NT, kMergeHead + 24ull * (size_t)m.smem_cap, st>>>(m);
     return cudaGetLastError();
 }
 

@@ -44,11 +44,14 @@ class ShardedDecodeTail:
     """DecodeTail for this rank's slice + the record exchange.
 
     group: a torch.distributed process group (None = the default group);
-    its backend must move CUDA tensors (NCCL)."""
+    its backend must move CUDA tensors (NCCL).  p2p: connect the ranks'
+    exchange buffers (CUDA IPC over NVLink) so that a single-stream step is
+    one kernel per rank (lal_tail_connect_peers); batched steps use the
+    all-gather."""
 
     def __init__(self, vocab_size: int, n_embd: int, device: int, max_streams: int = 1,
                  max_top_k: int = 64, history_cap: int = 256,
-                 sampler: int = LAL_SAMPLER_LIBRARY, group=None):
+                 sampler: int = LAL_SAMPLER_LIBRARY, group=None, p2p: bool = True):
         import torch
         import torch.distributed as dist
 
@@ -61,6 +64,12 @@ class ShardedDecodeTail:
                                device=device, shard_rank=self.rank, shard_count=self.world)
         self.torch_stream = torch.cuda.ExternalStream(self.tail.stream(), device=device)
         self._views = {}
+        self.p2p = False
+        if p2p:
+            handles = [None] * self.world
+            dist.all_gather_object(handles, self.tail.exchange_handle(), group=group)
+            self.tail.connect_peers(handles)
+            self.p2p = True
 
     # the slice and the per-stream state live in the wrapped context
     def __getattr__(self, name):
@@ -82,6 +91,9 @@ class ShardedDecodeTail:
 
     def step_device(self, d_hidden: int, n_streams: int, d_u: int, d_tokens: int):
         """Enqueue one sharded step on the tail's stream (no host wait)."""
+        if self.p2p and n_streams == 1:
+            self.tail.step_device(d_hidden, n_streams, d_u, d_tokens)
+            return
         self.tail.shard_select(d_hidden, n_streams)
         vs, vr = self._exchange_views(n_streams)
         with self.torch.cuda.stream(self.torch_stream):
@@ -90,12 +102,18 @@ class ShardedDecodeTail:
 
     def step(self, hidden: np.ndarray, u: np.ndarray) -> np.ndarray:
         """One step from host buffers: the same tokens on every rank."""
+        hidden = np.asarray(hidden)
+        if self.p2p and (hidden.ndim == 1 or hidden.shape[0] == 1):
+            return self.tail.step(hidden, u)
         n = self.tail.stage_inputs(hidden, u)
         d_hid, d_u, d_tok = self.tail.device_buffers()
         self.step_device(d_hid, n, d_u, d_tok)
         return self.tail.fetch_tokens(n)
 
     def close(self):
+        """Collective: every rank's kernels finish before any buffer is freed."""
+        self.tail.sync()
+        self.dist.barrier(group=self.group)
         self._views.clear()
         self.tail.close()
 

@@ -216,7 +216,7 @@ def test_sharded_capacity_error_reaches_every_shard_then_recovers():
 
 # ---- real ranks over NCCL (two or more GPUs) ----------------------------------
 
-def _nccl_worker(rank, world, port, out_dir):
+def _nccl_worker(rank, world, port, out_dir, p2p):
     import datetime
 
     import torch
@@ -234,7 +234,8 @@ def _nccl_worker(rank, world, port, out_dir):
     cfg, W, hist0 = cases.loop_inputs(spec)
     q, s = oracle.quantize_rows(W, "port")
     st = ShardedDecodeTail(cfg.vocab, cfg.n_embd, device=rank, max_top_k=cfg.top_k,
-                           history_cap=cfg.hist, sampler=spec["variant"])
+                           history_cap=cfg.hist, sampler=spec["variant"], p2p=p2p)
+    assert st.p2p == p2p
     st.load_lm_head_q8(q[st.row0:st.row0 + st.n_rows], s[st.row0:st.row0 + st.n_rows])
     st.set_sampling([cfg.temperature], [cfg.top_k], [cfg.rep_penalty])
     st.set_history(0, hist0)
@@ -245,27 +246,95 @@ def _nccl_worker(rank, world, port, out_dir):
         toks.append(int(st.step(h, np.array([g.next_u()], np.float32))[0]))
     hist = st.get_history(0)
     st.close()
-    dist.barrier()
     dist.destroy_process_group()
     np.save(os.path.join(out_dir, f"tok{rank}.npy"), np.array(toks, np.int32))
     np.save(os.path.join(out_dir, f"hist{rank}.npy"), hist)
 
 
-def test_nccl_ranks_match_reference(golden, tmp_path):
-    import torch
-    n = torch.cuda.device_count()
-    if n < 2:
-        pytest.skip("one GPU: the NCCL path runs under a multi-GPU call")
-    import torch.multiprocessing as mp
+def _free_port():
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
     port = s.getsockname()[1]
     s.close()
+    return port
+
+
+@pytest.mark.parametrize("p2p", [False, True])
+def test_nccl_ranks_match_reference(golden, tmp_path, p2p):
+    """Two processes, one GPU each: the all-gather path (p2p=False) and the
+    single-kernel peer exchange (p2p=True) both reproduce the reference's
+    golden decode loop on every rank."""
+    import torch
+    n = torch.cuda.device_count()
+    if n < 2:
+        pytest.skip("one GPU: the multi-GPU paths run under a multi-GPU call")
+    import torch.multiprocessing as mp
     world = 2
-    mp.start_processes(_nccl_worker, args=(world, port, str(tmp_path)), nprocs=world,
-                       join=True, start_method="spawn")
+    mp.start_processes(_nccl_worker, args=(world, _free_port(), str(tmp_path), p2p),
+                       nprocs=world, join=True, start_method="spawn")
     want = golden["loop_c1_gpt2_tokens"]
     for r in range(world):
         np.testing.assert_array_equal(np.load(tmp_path / f"tok{r}.npy"), want)
     np.testing.assert_array_equal(np.load(tmp_path / "hist0.npy"),
                                   np.load(tmp_path / f"hist{world - 1}.npy"))
+
+
+def _p2p_timeout_worker(rank, world, port, out_dir):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from lal_b200.sharded import ShardedDecodeTail
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    spec = cases.loop_cases()["tiny_lib"]
+    cfg, W, hist0 = cases.loop_inputs(spec)
+    q, s = oracle.quantize_rows(W, "port")
+    st = ShardedDecodeTail(cfg.vocab, cfg.n_embd, device=rank, max_top_k=cfg.top_k,
+                           history_cap=cfg.hist, sampler=0, p2p=True)
+    st.load_lm_head_q8(q[st.row0:st.row0 + st.n_rows], s[st.row0:st.row0 + st.n_rows])
+    st.set_sampling([cfg.temperature], [cfg.top_k], [cfg.rep_penalty])
+    st.set_history(0, hist0)
+    h = synth.hidden(cfg, 0)
+    u = np.array([0.25], np.float32)
+    code = 0
+    if rank == 0:
+        # rank 1 never steps: the bounded peer wait runs out (2 s)
+        try:
+            st.step(h, u)
+        except L.LalTailError as e:
+            code = e.code
+    dist.barrier()
+    # both ranks reconnect (fresh sequence numbers) and step together
+    handles = [None] * world
+    dist.all_gather_object(handles, st.tail.exchange_handle())
+    st.tail.connect_peers(handles)
+    tok = int(st.step(h, u)[0])
+    hist = st.get_history(0)
+    st.close()
+    dist.destroy_process_group()
+    np.save(os.path.join(out_dir, f"r{rank}.npy"), np.array([code, tok, hist.size], np.int64))
+
+
+def test_p2p_wait_times_out_then_recovers(tmp_path):
+    """A rank that does not step: the other rank's bounded wait ends with
+    LAL_TAIL_ERR_TIMEOUT (no token pushed); after reconnecting, both ranks
+    step together and agree."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("one GPU: the peer exchange runs under a multi-GPU call")
+    import torch.multiprocessing as mp
+    mp.start_processes(_p2p_timeout_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2,
+                       join=True, start_method="spawn")
+    r0 = np.load(tmp_path / "r0.npy")
+    r1 = np.load(tmp_path / "r1.npy")
+    assert r0[0] == 4          # LAL_TAIL_ERR_TIMEOUT on the rank that stepped alone
+    assert r0[1] == r1[1]      # then the same token on both ranks
+    spec = cases.loop_cases()["tiny_lib"]
+    assert r0[2] == r1[2] == min(spec["hist"], cases.loop_inputs(spec)[2].size + 1)
