@@ -930,7 +930,8 @@ int ctx_alloc(lal_tail *t) {
         CU(cudaMalloc(&t->sx_b, 4ull * 256));
         CU(cudaMalloc(&t->gmax_b, 4ull * 256 * batch_groups(t->nrows)));
         t->batch_ok = batch_plan(t->bplan, t->W, t->sw, t->nrows, t->ld, t->ds->num_sms, t->xq_b,
-                                 t->sx_b, t->gmax_b, B, c.history_cap) == 0;
+                                 t->sx_b, t->gmax_b, B, c.history_cap,
+                                 std::min(c.max_top_k, c.vocab_size)) == 0;
     }
     return LAL_TAIL_OK;
 }

@@ -166,7 +166,8 @@ struct GemmParams {
     const float *scale_w;
     const float *scale_x;
     float *logits; /* [B][rows] */
-    uint32_t *gmax; /* [rows/32][N] order key of each 32-row group's largest logit */
+    uint32_t *gmax; /* [B][n_groups] order key of each 32-row group's largest logit */
+    int n_groups;
     int rows, B, N, kblocks, stages, stage_bytes, tmem_cols;
     int *status;
 };
@@ -312,7 +313,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_i8_kernel(const __grid_c
                     const uint32_t gm = __reduce_max_sync(0xffffffffu, row < p.rows ? f2key(l) : 0u);
                     if (lane == j) mine = gm;
                 }
-                p.gmax[(size_t)group * p.N + c0 + lane] = mine;
+                if (c0 + lane < p.B) p.gmax[(size_t)(c0 + lane) * p.n_groups + group] = mine;
             }
             tc_fence_before();
             __syncwarp();
@@ -349,8 +350,8 @@ struct BatchSelectParams {
     uint8_t *shard_out; /* [B][rec_bytes] records, or null */
     int rec_cap, rec_bytes;
     int s_cap, c_cap, h_slots; /* superset, candidate and hash capacities */
-    const uint32_t *gmax;      /* [n_groups][gstride] raw group maxima (GEMM) */
-    int n_groups, gstride;
+    const uint32_t *gmax;      /* [B][n_groups] raw group maxima (GEMM) */
+    int n_groups;
 };
 
 constexpr uint32_t kEmptySlot = 0xFFFFFFFFu;
@@ -371,6 +372,7 @@ __global__ void __launch_bounds__(NT, 1) batch_select_kernel(const __grid_consta
     float *Ce = reinterpret_cast<float *>(Oi + p.c_cap);           /* weights, sums    */
     uint32_t *hkey = reinterpret_cast<uint32_t *>(Ce + p.c_cap);   /* history hash     */
     uint32_t *hcnt = hkey + p.h_slots;
+    int *Gl = reinterpret_cast<int *>(hcnt + p.h_slots);           /* candidate groups */
 
     float *lg = p.logits + (size_t)b * p.rows;
     const float temp = p.temperature[b];
@@ -461,32 +463,50 @@ __global__ void __launch_bounds__(NT, 1) batch_select_kernel(const __grid_consta
      * most P of them penalised, and a penalty (p > 1) never raises a logit --
      * and only groups whose raw maximum reaches L can hold a key >= L.  When
      * that bound is weak the full histogram pass below is used instead. */
+    auto hist_add = [&](uint32_t *h, uint32_t digit, bool act) {
+        const unsigned voters = __ballot_sync(0xffffffffu, act);
+        if (act) {
+            const unsigned peers = __match_any_sync(voters, digit);
+            if ((tid & 31) == __ffs(peers) - 1) atomicAdd(&h[digit], (uint32_t)__popc(peers));
+        }
+    };
     uint32_t L = 0u;
     int S = -1;
     const int kp = k + s_pen;
     const bool groups = p.gmax != nullptr && kp <= p.n_groups / 8 && p.n_groups <= p.s_cap;
     if (groups) {
+        /* the group maxima (contiguous per stream) into Sk and their top 12
+         * key bits into the histogram; the lower edge of the bin holding the
+         * (k+P)-th largest maximum is <= that maximum, hence a bound of T */
         uint32_t *Gk = Sk; /* the group maxima, then the superset */
-        for (int g = tid; g < p.n_groups; g += NT) Gk[g] = __ldg(p.gmax + (size_t)g * p.gstride + b);
+        const uint32_t *gm = p.gmax + (size_t)b * p.n_groups;
+        for (int g0 = 0; g0 < p.n_groups; g0 += NT * U) {
+            uint32_t v[U];
+#pragma unroll
+            for (int j = 0; j < U; ++j) {
+                const int g = g0 + j * NT + tid;
+                v[j] = g < p.n_groups ? __ldg(gm + g) : 0u;
+            }
+#pragma unroll
+            for (int j = 0; j < U; ++j) {
+                const int g = g0 + j * NT + tid;
+                if (g < p.n_groups) Gk[g] = v[j];
+                hist_add(hist, v[j] >> 20, g < p.n_groups);
+            }
+        }
         __syncthreads();
-        L = block_kth_largest(
-            [&](int i, uint32_t &key) {
-                key = Gk[i];
-                return true;
-            },
-            p.n_groups, kp, ms);
-        /* the candidate groups, listed in Ci */
+        uint32_t gab, gcnt;
+        L = boundary_bin(hist, 4096, (uint32_t)kp, ms, &gab, &gcnt) << 20;
+        for (int i = tid; i < 4096; i += NT) hist[i] = 0u; /* for the fallback */
+        /* the candidate groups, listed in Gl */
         if (tid == 0) s_count = 0;
         __syncthreads();
         for (int g = tid; g < p.n_groups; g += NT)
-            if (Gk[g] >= L) {
-                const int at = atomicAdd(&s_count, 1);
-                if (at < p.c_cap) Ci[at] = g;
-            }
+            if (Gk[g] >= L) Gl[atomicAdd(&s_count, 1)] = g;
         __syncthreads();
         const int ng = s_count;
         __syncthreads();
-        if (ng <= p.c_cap) {
+        if (ng <= p.n_groups / 4) {
             if (tid == 0) s_count = 0;
             __syncthreads();
             /* gather the groups' keys >= L (32 consecutive rows a group) */
@@ -497,7 +517,7 @@ __global__ void __launch_bounds__(NT, 1) batch_select_kernel(const __grid_consta
 #pragma unroll
                 for (int j = 0; j < U; ++j) {
                     const int e = i0 + j * NT + tid;
-                    rr[j] = e < total ? Ci[e >> 5] * 32 + (e & 31) : p.rows;
+                    rr[j] = e < total ? Gl[e >> 5] * 32 + (e & 31) : p.rows;
                     v[j] = rr[j] < p.rows ? lg[rr[j]] : 0.0f;
                 }
 #pragma unroll
@@ -527,13 +547,6 @@ __global__ void __launch_bounds__(NT, 1) batch_select_kernel(const __grid_consta
     }
     if (S < 0) {
     /* full pass: the top 12 key bits of every logit into the histogram */
-    auto hist_add = [&](uint32_t *h, uint32_t digit, bool act) {
-        const unsigned voters = __ballot_sync(0xffffffffu, act);
-        if (act) {
-            const unsigned peers = __match_any_sync(voters, digit);
-            if ((tid & 31) == __ffs(peers) - 1) atomicAdd(&h[digit], (uint32_t)__popc(peers));
-        }
-    };
     for (int i0 = 0; i0 < p.rows; i0 += NT * U) {
         float v[U];
 #pragma unroll
@@ -617,13 +630,37 @@ __global__ void __launch_bounds__(NT, 1) batch_select_kernel(const __grid_consta
     __syncthreads();
     }  /* full pass */
 
-    /* 4. T exactly: the k-th largest key of the superset */
-    const uint32_t T = block_kth_largest(
-        [&](int i, uint32_t &key) {
-            key = Sk[i];
-            return true;
-        },
-        S, min(k, S), ms);
+    /* 4. T exactly: the k-th largest key of the superset (counting for a
+     * small superset: T = min{ key : #{keys > key} < k }) */
+    uint32_t T;
+    if (S <= 2 * NT) {
+        uint32_t best = 0xffffffffu;
+        const int kk = min(k, S);
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            const int e = tid + r * NT;
+            if (e < S) {
+                const uint32_t me = Sk[e];
+                int gt = 0;
+#pragma unroll 4
+                for (int j = 0; j < S; ++j) gt += Sk[j] > me;
+                if (gt < kk) best = min(best, me);
+            }
+        }
+        best = __reduce_min_sync(0xffffffffu, best);
+        if ((tid & 31) == 0) ms->scan[tid >> 5] = best;
+        __syncthreads();
+        T = ms->scan[0];
+        for (int w = 1; w < NWARP; ++w) T = min(T, ms->scan[w]);
+        __syncthreads();
+    } else {
+        T = block_kth_largest(
+            [&](int i, uint32_t &key) {
+                key = Sk[i];
+                return true;
+            },
+            S, min(k, S), ms);
+    }
     /* candidates {l >= T} */
     const int seg = (S + NT - 1) / NT;
     const int e0 = min(S, tid * seg), e1 = min(S, e0 + seg);
@@ -809,12 +846,13 @@ bool encode_i8(CUtensorMap *m, const void *base, int dim0, int dim1, int pitch, 
 /* ---- the batched step, as seen by tail_api.cu ---- */
 int batch_n_for(int B) { return (B + 31) / 32 * 32; }
 
-size_t batch_select_smem(int s_cap, int c_cap, int h_slots) {
-    return 4ull * 4096 + 8ull * s_cap + 24ull * c_cap + 8ull * h_slots;
+size_t batch_select_smem(int s_cap, int c_cap, int h_slots, int n_groups) {
+    return 4ull * 4096 + 8ull * s_cap + 24ull * c_cap + 8ull * h_slots + 4ull * n_groups;
 }
 
 int batch_plan(BatchPlan &bp, const int8_t *W, const float *scale_w, int rows, int ld,
-               int num_sms, int8_t *xq, float *sx, uint32_t *gmax, int max_B, int hist_cap) {
+               int num_sms, int8_t *xq, float *sx, uint32_t *gmax, int max_B, int hist_cap,
+               int max_top_k) {
     memset(&bp, 0, sizeof(bp));
     if (!encoder()) return -3;
     if (ld < kBK || ld % 16 != 0 || max_B < 2 || max_B > 256 || rows < 1) return -1;
@@ -830,12 +868,17 @@ int batch_plan(BatchPlan &bp, const int8_t *W, const float *scale_w, int rows, i
     bp.kblocks = (ld + kBK - 1) / kBK;
     /* select capacities: superset, candidates, history hash (>= 2x the
      * history, a power of two) */
-    bp.s_cap = 8192;
-    bp.c_cap = 2048;
+    /* superset >= the group maxima and 8x the largest k; candidates k plus
+     * ties; small enough for several select CTAs per SM at small k */
+    bp.s_cap = std::max({2048, batch_groups(rows), 8 * max_top_k});
+    bp.s_cap = (bp.s_cap + 31) / 32 * 32;
+    bp.c_cap = 256;
+    while (bp.c_cap < 2 * max_top_k) bp.c_cap <<= 1;
     int hs = 64;
     while (hs < 2 * std::max(1, hist_cap)) hs <<= 1;
     bp.h_slots = hs;
-    if (batch_select_smem(bp.s_cap, bp.c_cap, bp.h_slots) > (size_t)(kGemmSmemLimit - 8192))
+    if (batch_select_smem(bp.s_cap, bp.c_cap, bp.h_slots, bp.n_groups) >
+        (size_t)(kGemmSmemLimit - 8192))
         return -2;
     return 0;
 }
@@ -868,6 +911,7 @@ cudaError_t batch_launch(BatchPlan &bp, const BatchStep &s, cudaStream_t st) {
     g.scale_x = bp.sx;
     g.logits = s.logits;
     g.gmax = bp.gmax;
+    g.n_groups = bp.n_groups;
     g.rows = bp.rows;
     g.B = s.B;
     g.N = N;
@@ -930,8 +974,7 @@ cudaError_t batch_launch(BatchPlan &bp, const BatchStep &s, cudaStream_t st) {
     q.h_slots = bp.h_slots;
     q.gmax = bp.gmax;
     q.n_groups = bp.n_groups;
-    q.gstride = N;
-    const size_t ssmem = batch_select_smem(bp.s_cap, bp.c_cap, bp.h_slots);
+    const size_t ssmem = batch_select_smem(bp.s_cap, bp.c_cap, bp.h_slots, bp.n_groups);
     e = raise_smem((const void *)batch_select_kernel, kGemmSmemLimit - 8192);
     if (e != cudaSuccess) return e;
     batch_select_kernel<<<s.B, NT, ssmem, st>>>(q);

@@ -229,7 +229,7 @@ struct BatchPlan {
     int rows, ld, num_sms, kblocks;
     int8_t *xq;        /* [256][ld] quantized hidden vectors                     */
     float *sx;         /* [256] their scales                                     */
-    uint32_t *gmax;    /* [n_groups][256] raw maxima of 32-row groups, per stream */
+    uint32_t *gmax;    /* [256][n_groups] raw maxima of 32-row groups, per stream */
     int n_groups;
     int s_cap, c_cap, h_slots;
     /* TMA descriptors (CUtensorMap, 128 bytes each): W, and X for N = 32..256 */
@@ -262,8 +262,9 @@ struct BatchStep {
 };
 /* 0 when the shape takes the batched path (d >= 128, 2 <= max_B <= 256). */
 int batch_plan(BatchPlan &bp, const int8_t *W, const float *scale_w, int rows, int ld,
-               int num_sms, int8_t *xq, float *sx, uint32_t *gmax, int max_B, int hist_cap);
-/* 32-row groups of a slice of `rows` rows (the gmax buffer holds 256 words each) */
+               int num_sms, int8_t *xq, float *sx, uint32_t *gmax, int max_B, int hist_cap,
+               int max_top_k);
+/* 32-row groups of a slice of `rows` rows (the gmax buffer holds 256 streams of them) */
 inline int batch_groups(int rows) { return (rows + 127) / 128 * 4; }
 cudaError_t batch_launch(BatchPlan &bp, const BatchStep &s, cudaStream_t st);
 int plan_launch(TailParams &p, int num_sms, int min_rows_per_cta);
