@@ -167,6 +167,26 @@ int lal_tail_load_lm_head_q8(lal_tail *t, const int8_t *wte_q_rows,
  * be given in chunks: [row_begin, row_begin + n) of the slice. */
 int lal_tail_load_lm_head_f32(lal_tail *t, const float *W_rows, int row_begin,
                               int n_rows);
+/* GPQ8 weight files (the Qwen-7B server's format, tools/server/
+ * qwen7b_server.c:499-563).  lal_tail_gpq8_find locates a tensor in a GPQ8
+ * blob (host memory, e.g. an mmap of the file) without touching the GPU;
+ * offsets are from the start of the blob.  lal_tail_load_lm_head_gpq8 loads
+ * this context's slice of the [vocab_size, n_embd] tensor `key` (NULL =
+ * "lm_head.weight"): an F32 tensor is quantized on the GPU exactly as
+ * lal_quantize_q8_per_row does at the server's load, a Q8 tensor (per-row
+ * scales) is copied as it is. */
+typedef struct {
+    int ndim;
+    int shape[4];
+    int qtype;              /* 0 = F32, 1 = Q8                                   */
+    uint64_t data_offset;
+    uint64_t data_len;
+    int n_scale;
+    uint64_t scale_offset;
+} lal_gpq8_tensor;
+int lal_tail_gpq8_find(const void *blob, size_t size, const char *key, lal_gpq8_tensor *out);
+int lal_tail_load_lm_head_gpq8(lal_tail *t, const void *blob, size_t size, const char *key);
+
 /* Read back this slice's quantized LM head (n_rows x n_embd, and scales). */
 int lal_tail_read_lm_head(lal_tail *t, int8_t *wte_q_rows, float *scale_w_rows);
 
@@ -229,6 +249,17 @@ int lal_tail_disconnect_peers(lal_tail *t);
 int lal_tail_exchange_buffers(lal_tail *t, int n_streams, void **d_send, void **d_recv,
                               size_t *bytes_per_rank);
 int lal_tail_shard_merge(lal_tail *t, int n_streams, const float *d_u, int *d_tokens_out);
+/* Level-2 filter hook in the fused context (tools/server/qwen7b_server.c:
+ * 175-186, 257-270).  With a filter or a draw callback set, lal_tail_step
+ * samples each non-greedy stream as the server's lal_sample_token_filtered:
+ * the fused kernel selects the candidates, the host builds the keep mask and
+ * calls filter (restoring the mask if it comes back empty), the GPU finishes
+ * the kept softmax, and draw(draw_ctx) is called only when the kept mass is
+ * positive (with no draw callback, the step's u[b] is used there).  Greedy
+ * streams take the normal path.  Needs LAL_SAMPLER_SERVER and one shard;
+ * lal_tail_step_device is not filtered.  All NULL switches it off. */
+int lal_tail_set_filter(lal_tail *t, lal_filter_topk_fn filter, lal_token_decode_fn decode,
+                        lal_draw_fn draw, void *draw_ctx);
 /* Diagnostics and penalised logits (this slice's rows) of the last step. */
 int lal_tail_get_diag(lal_tail *t, int stream, lal_tail_diag *out);
 int lal_tail_get_logits(lal_tail *t, int stream, float *logits_rows);

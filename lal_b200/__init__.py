@@ -58,6 +58,13 @@ class TailDiag(C.Structure):
         return {k: getattr(self, k) for k, _ in self._fields_}
 
 
+class Gpq8Tensor(C.Structure):
+    """Mirror of ``lal_gpq8_tensor`` (include/lal_tail.h)."""
+    _fields_ = [("ndim", C.c_int), ("shape", C.c_int * 4), ("qtype", C.c_int),
+                ("data_offset", C.c_uint64), ("data_len", C.c_uint64), ("n_scale", C.c_int),
+                ("scale_offset", C.c_uint64)]
+
+
 class RecentTokens(C.Structure):
     """Mirror of LalRecentTokens (runtime/lal_sampling.h:128-131)."""
     _fields_ = [("tokens", C.c_int * 256), ("n", C.c_int)]
@@ -120,6 +127,9 @@ SIGNATURES = {
     "lal_tail_exchange_handle": (C.c_int, [_vp, _vp]),
     "lal_tail_connect_peers": (C.c_int, [_vp, _vp]),
     "lal_tail_disconnect_peers": (C.c_int, [_vp]),
+    "lal_tail_set_filter": (C.c_int, [_vp, _vp, _vp, _vp, _vp]),
+    "lal_tail_gpq8_find": (C.c_int, [_vp, C.c_size_t, C.c_char_p, C.POINTER(Gpq8Tensor)]),
+    "lal_tail_load_lm_head_gpq8": (C.c_int, [_vp, _vp, C.c_size_t, C.c_char_p]),
     "lal_tail_sample_token_noalloc": (C.c_int, [_vp, _ip, _fp, _ip, _fp, _vp, _ip, _fp, _vp,
                                                 C.POINTER(C.c_int)]),
     "lal_tail_get_diag": (C.c_int, [_vp, _ip, C.POINTER(TailDiag)]),
@@ -232,6 +242,16 @@ def sample_token_filtered(logits: np.ndarray, temperature: float, top_k: int,
     return tok.value
 
 
+def gpq8_find(blob: bytes, key: str) -> dict:
+    """Locate a tensor in a GPQ8 blob (host only, no GPU)."""
+    e = Gpq8Tensor()
+    buf = C.create_string_buffer(blob, len(blob))
+    _check(lib().lal_tail_gpq8_find(buf, len(blob), key.encode(), C.byref(e)))
+    return {"ndim": e.ndim, "shape": list(e.shape)[:e.ndim], "qtype": e.qtype,
+            "data_offset": e.data_offset, "data_len": e.data_len, "n_scale": e.n_scale,
+            "scale_offset": e.scale_offset}
+
+
 def debug_expf(x: np.ndarray) -> np.ndarray:
     x = np.ascontiguousarray(x, np.float32)
     y = np.empty_like(x)
@@ -276,6 +296,12 @@ class DecodeTail:
         W_rows = np.ascontiguousarray(W_rows, np.float32)
         _check(lib().lal_tail_load_lm_head_f32(self.h, W_rows.reshape(-1), row_begin,
                                                W_rows.shape[0]))
+
+    def load_lm_head_gpq8(self, blob: bytes, key: Optional[str] = None):
+        """This slice of a [V, d] tensor of a GPQ8 blob (F32: quantized on the GPU)."""
+        buf = C.create_string_buffer(blob, len(blob))
+        _check(lib().lal_tail_load_lm_head_gpq8(self.h, buf, len(blob),
+                                                key.encode() if key else None))
 
     def read_lm_head(self):
         q = np.empty((self.n_rows, self.cfg.n_embd), np.int8)
@@ -399,3 +425,16 @@ class DecodeTail:
 
     def disconnect_peers(self):
         _check(lib().lal_tail_disconnect_peers(self.h))
+
+    def set_filter(self, filt=None, draw: Optional[Callable[[], float]] = None, decode=None):
+        """Level-2 filter hook for step(): filt(keep, n_vocab, last, recent,
+        n_recent, decode) edits the keep mask; draw() is called only where the
+        server calls rand().  set_filter() with no arguments switches it off."""
+        self._filter_refs = (
+            FILTER_FN(filt) if filt is not None else None,
+            DECODE_FN(decode) if decode is not None else None,
+            DRAW_FN(lambda _ctx: float(draw())) if draw is not None else None)
+        cf, cd, cw = self._filter_refs
+        _check(lib().lal_tail_set_filter(
+            self.h, C.cast(cf, C.c_void_p) if cf else None, C.cast(cd, C.c_void_p) if cd else None,
+            C.cast(cw, C.c_void_p) if cw else None, None))

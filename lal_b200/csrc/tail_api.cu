@@ -829,6 +829,18 @@ struct lal_tail {
     std::vector<void *> peer_open;
     bool p2p = false;
     unsigned seq = 1;
+    /* level-2 filter hook (qwen7b_server.c:257-270) for the host-buffer step:
+     * device candidate list, keep flags, prefix scratch, draw and token words;
+     * host keep mask and copies */
+    lal_filter_topk_fn filter = nullptr;
+    lal_token_decode_fn decode = nullptr;
+    lal_draw_fn draw = nullptr;
+    void *draw_ctx = nullptr;
+    bool filtered = false;
+    float *f_cand_v = nullptr, *f_prefix = nullptr, *f_u = nullptr;
+    int *f_cand_i = nullptr, *f_keep = nullptr, *f_tok = nullptr;
+    StreamDiag *f_diag = nullptr;
+    std::vector<int> f_mask, f_ids, f_ring, f_keep_h;
 };
 
 namespace {
@@ -847,7 +859,9 @@ void destroy_ctx(lal_tail *t) {
     close_peers(t);
     void *bufs[] = {t->W, t->sw, t->io_in, t->io_out, t->logits, t->temp, t->topk, t->pen,
                     t->hist_ids, t->hist_n, t->hist_head, t->diag, t->phase_ts,
-                    t->x_send, t->x_recv, t->xq_b, t->sx_b, t->gmax_b, t->x_peer, t->d_peer};
+                    t->x_send, t->x_recv, t->xq_b, t->sx_b, t->gmax_b, t->x_peer, t->d_peer,
+                    t->f_cand_v, t->f_prefix, t->f_u, t->f_cand_i, t->f_keep, t->f_tok,
+                    t->f_diag};
     for (void *b : bufs)
         if (b) cudaFree(b);
     t->sel.free_all();
@@ -1044,6 +1058,149 @@ int enqueue_step(lal_tail *t, const float *d_hidden, int n, const float *d_u, in
             t->ev_used += 2;
         }
     }
+    return LAL_TAIL_OK;
+}
+
+/* The normal fused launch of stream b alone (hidden and u in io_in, the
+ * token into io_out). */
+int enqueue_one(lal_tail *t, int b) {
+    const int B = t->cfg.max_streams, d = t->cfg.n_embd;
+    const int hc = std::max(1, t->cfg.history_cap);
+    TailParams p = t->plan;
+    p.W = t->W;
+    p.scale_w = t->sw;
+    p.hidden = t->io_in + (size_t)b * d;
+    p.logits = t->logits + (size_t)b * t->nrows;
+    p.temperature = t->temp + b;
+    p.top_k = t->topk + b;
+    p.rep_penalty = t->pen + b;
+    p.u = t->io_in + (size_t)B * d + b;
+    p.hist_ids = t->hist_ids + (size_t)b * hc;
+    p.hist_n = t->hist_n + b;
+    p.hist_head = t->hist_head + b;
+    p.hist_cap = t->cfg.history_cap;
+    p.push_history = t->cfg.history_cap > 0 ? 1 : 0;
+    p.tokens = t->io_out + b;
+    p.diag = t->diag + b;
+    t->sel.fill(p);
+    p.status = t->io_out + B;
+    p.local_edges = use_local_edges(
+        effective_k(t->h_temp[b], t->h_topk[b], t->cfg.vocab_size, t->nrows), p.rows_per_cta_max);
+    CU(launch_tail(p, t->grid, t->stream));
+    return LAL_TAIL_OK;
+}
+
+/* One stream's step with the level-2 filter hook: the server's sampler
+ * (tools/server/qwen7b_server.c:219-295) with the candidate set handed to the
+ * host between the select and the draw.  hidden is already on the device;
+ * u_fallback is the draw used when no draw callback is set. */
+int filtered_stream_step(lal_tail *t, int b, const float *d_hidden, float u_fallback,
+                         int *token_out) {
+    const int hc = std::max(1, t->cfg.history_cap);
+    const int V = t->cfg.vocab_size;
+    TailParams p = t->plan;
+    p.W = t->W;
+    p.scale_w = t->sw;
+    p.hidden = d_hidden + (size_t)b * t->cfg.n_embd;
+    p.logits = t->logits + (size_t)b * t->nrows;
+    p.temperature = t->temp + b;
+    p.top_k = t->topk + b;
+    p.rep_penalty = t->pen + b;
+    p.u = t->f_u;
+    p.hist_ids = t->hist_ids + (size_t)b * hc;
+    p.hist_n = t->hist_n + b;
+    p.hist_head = t->hist_head + b;
+    p.hist_cap = t->cfg.history_cap;
+    p.push_history = 0;
+    p.tokens = t->f_tok;
+    p.diag = t->diag + b;
+    p.candidates_only = 1;
+    p.cand_val_out = t->f_cand_v;
+    p.cand_idx_out = t->f_cand_i;
+    p.cand_out_cap = t->nrows;
+    t->sel.fill(p);
+    p.status = t->io_out + t->cfg.max_streams;
+    p.local_edges = use_local_edges(
+        effective_k(t->h_temp[b], t->h_topk[b], V, t->nrows), p.rows_per_cta_max);
+    CU(launch_tail(p, t->grid, t->stream));
+    /* 1. the candidate count, the status and the history ring */
+    StreamDiag dg;
+    int status = 0, n = 0, head = 0;
+    CU(cudaMemcpyAsync(&dg, t->diag + b, sizeof(dg), cudaMemcpyDeviceToHost, t->stream));
+    CU(cudaMemcpyAsync(&status, p.status, 4, cudaMemcpyDeviceToHost, t->stream));
+    CU(cudaMemcpyAsync(&n, t->hist_n + b, 4, cudaMemcpyDeviceToHost, t->stream));
+    CU(cudaMemcpyAsync(&head, t->hist_head + b, 4, cudaMemcpyDeviceToHost, t->stream));
+    CU(cudaStreamSynchronize(t->stream));
+    if (status != 0) {
+        CU(cudaMemset(p.status, 0, 4));
+        CHECK(t->sel.reset(t->stream));
+        CU(cudaStreamSynchronize(t->stream));
+        return fail(status, "device status %d in the filtered step", status);
+    }
+    const int m = dg.n_cand;
+    if (m < 1 || m > t->nrows) return fail(LAL_TAIL_ERR_CAPACITY, "filtered step: %d candidates", m);
+    CU(cudaMemcpyAsync(t->f_ids.data(), t->f_cand_i, 4ull * m, cudaMemcpyDeviceToHost, t->stream));
+    CU(cudaMemcpyAsync(t->f_ring.data(), p.hist_ids, 4ull * hc, cudaMemcpyDeviceToHost, t->stream));
+    CU(cudaStreamSynchronize(t->stream));
+    /* the recent tokens, oldest first, as the server keeps them */
+    std::vector<int> recent((size_t)n);
+    for (int i = 0; i < n; ++i)
+        recent[i] = t->f_ring[(size_t)((n < hc ? 0 : head) + i) % (size_t)hc];
+    /* 2. keep mask, filter, restore when emptied (qwen7b_server.c:258-270) */
+    std::vector<int> &keep = t->f_keep_h;
+    keep.assign((size_t)m, 1);
+    if (t->filter) {
+        std::fill(t->f_mask.begin(), t->f_mask.end(), 0);
+        for (int i = 0; i < m; ++i) t->f_mask[t->f_ids[i]] = 1;
+        const int last = n > 0 ? recent[n - 1] : -1;
+        (void)t->filter(t->f_mask.data(), V, last, recent.data(), n, t->decode);
+        bool any = false;
+        for (int v = 0; v < V && !any; ++v) any = t->f_mask[v] != 0;
+        if (any)
+            for (int i = 0; i < m; ++i) keep[i] = t->f_mask[t->f_ids[i]] ? 1 : 0;
+    }
+    /* 3. kept softmax on the device; the draw only when the mass is positive */
+    CU(cudaMemcpyAsync(t->f_keep, keep.data(), 4ull * m, cudaMemcpyHostToDevice, t->stream));
+    FinishParams f;
+    memset(&f, 0, sizeof(f));
+    f.cand_val = t->f_cand_v;
+    f.cand_idx = t->f_cand_i;
+    f.keep = t->f_keep;
+    f.m = m;
+    f.temperature = t->h_temp[b];
+    f.vocab = V;
+    f.u = t->f_u;
+    f.prefix = t->f_prefix;
+    f.diag = t->f_diag;
+    f.token = t->f_tok;
+    f.expf_x = t->ds->d_expf_x;
+    f.expf_y = t->ds->d_expf_y;
+    f.expf_n = t->ds->expf_n;
+    f.expf_bits = t->ds->d_expf_bits;
+    f.expf_off = t->ds->d_expf_off;
+    f.phase = 0;
+    CU(launch_finish(f, t->stream));
+    StreamDiag fd;
+    CU(cudaMemcpyAsync(&fd, t->f_diag, sizeof(fd), cudaMemcpyDeviceToHost, t->stream));
+    CU(cudaStreamSynchronize(t->stream));
+    int tok = fd.token;
+    if (fd.sum > 0.0f) { /* qwen7b_server.c:285-290 */
+        const float u = t->draw ? t->draw(t->draw_ctx) : u_fallback;
+        CU(cudaMemcpyAsync(t->f_u, &u, 4, cudaMemcpyHostToDevice, t->stream));
+        f.phase = 1;
+        CU(launch_finish(f, t->stream));
+        CU(cudaMemcpyAsync(&tok, t->f_tok, 4, cudaMemcpyDeviceToHost, t->stream));
+        CU(cudaStreamSynchronize(t->stream));
+    }
+    /* 4. the history push (FIFO at history_cap) */
+    if (t->cfg.history_cap > 0) {
+        const int pos = n < hc ? n : head;
+        const int n2 = n < hc ? n + 1 : n, head2 = n < hc ? head : (head + 1) % hc;
+        CU(cudaMemcpy(p.hist_ids + pos, &tok, 4, cudaMemcpyHostToDevice));
+        CU(cudaMemcpy(t->hist_n + b, &n2, 4, cudaMemcpyHostToDevice));
+        CU(cudaMemcpy(t->hist_head + b, &head2, 4, cudaMemcpyHostToDevice));
+    }
+    *token_out = tok;
     return LAL_TAIL_OK;
 }
 
@@ -1245,6 +1402,24 @@ int lal_tail_step(lal_tail *t, const float *hidden, int n_streams, const float *
     if (!hidden || !u || !tokens_out) return fail(LAL_TAIL_ERR_ARG, "step: null argument");
     if (n_streams < 1 || n_streams > t->cfg.max_streams)
         return fail(LAL_TAIL_ERR_ARG, "n_streams %d out of range", n_streams);
+    if (t->filtered) {
+        if (!t->loaded) return fail(LAL_TAIL_ERR_STATE, "step before the LM head was loaded");
+        if (t->n_set < n_streams)
+            return fail(LAL_TAIL_ERR_STATE, "sampling parameters not set for %d streams", n_streams);
+        CHECK(lal_tail_stage_inputs(t, hidden, n_streams, u));
+        for (int b = 0; b < n_streams; ++b) {
+            if (t->h_temp[b] <= 0.0f || t->h_topk[b] <= 0) {
+                /* greedy: penalty then argmax, no filter (qwen7b_server.c:233-234) */
+                CHECK(enqueue_one(t, b));
+                CU(cudaMemcpyAsync(tokens_out + b, t->io_out + b, 4, cudaMemcpyDeviceToHost,
+                                   t->stream));
+                CHECK(lal_tail_sync(t));
+            } else {
+                CHECK(filtered_stream_step(t, b, t->io_in, u[b], tokens_out + b));
+            }
+        }
+        return LAL_TAIL_OK;
+    }
     const int B = t->cfg.max_streams, d = t->cfg.n_embd;
     /* stage hidden and u contiguously in pinned memory: one H2D copy */
     memcpy(t->h_in, hidden, 4ull * n_streams * d);
@@ -1410,6 +1585,128 @@ int lal_tail_disconnect_peers(lal_tail *t) {
     CHECK(ctx_check(t));
     CU(cudaStreamSynchronize(t->stream));
     close_peers(t);
+    return LAL_TAIL_OK;
+}
+
+/* GPQ8 tensor directory (tools/server/qwen7b_server.c:499-505, 524-563):
+ * "GPQ8", int32 count, then per tensor: int32 key length, key bytes, int32
+ * ndim, int32 shape[ndim], uint8 qtype (0 = F32, 1 = Q8), uint64 data length,
+ * data, int32 scale count, float scales (keys up to 127 bytes, the server's
+ * char key[128]).  Every field is bounds-checked against the blob (the server
+ * trusts its file; a library must not). */
+int lal_tail_gpq8_find(const void *blob, size_t size, const char *key, lal_gpq8_tensor *out) {
+    if (!blob || !key || !out) return fail(LAL_TAIL_ERR_ARG, "gpq8: null argument");
+    const unsigned char *b = (const unsigned char *)blob;
+    size_t off = 0;
+    auto take = [&](void *dst, size_t n) {
+        if (n > size || off > size - n) return false;
+        memcpy(dst, b + off, n);
+        off += n;
+        return true;
+    };
+    char magic[4];
+    int32_t count = 0;
+    if (!take(magic, 4) || memcmp(magic, "GPQ8", 4) != 0) return fail(LAL_TAIL_ERR_ARG, "gpq8: bad magic");
+    if (!take(&count, 4) || count < 0) return fail(LAL_TAIL_ERR_ARG, "gpq8: bad tensor count");
+    const size_t klen_want = strlen(key);
+    for (int32_t i = 0; i < count; ++i) {
+        int32_t klen = 0, ndim = 0, n_scale = 0;
+        uint8_t qtype = 0;
+        uint64_t dlen = 0;
+        if (!take(&klen, 4) || klen < 0 || klen > 127 || (size_t)klen > size - off)
+            return fail(LAL_TAIL_ERR_ARG, "gpq8: tensor %d: bad key", (int)i);
+        const bool match = (size_t)klen == klen_want && memcmp(b + off, key, (size_t)klen) == 0;
+        off += (size_t)klen;
+        if (!take(&ndim, 4) || ndim < 0 || ndim > 4)
+            return fail(LAL_TAIL_ERR_ARG, "gpq8: tensor %d: bad ndim", (int)i);
+        int32_t shape[4] = {0, 0, 0, 0};
+        for (int d = 0; d < ndim; ++d)
+            if (!take(&shape[d], 4) || shape[d] < 0)
+                return fail(LAL_TAIL_ERR_ARG, "gpq8: tensor %d: bad shape", (int)i);
+        if (!take(&qtype, 1) || qtype > 1 || !take(&dlen, 8) || dlen > size - off)
+            return fail(LAL_TAIL_ERR_ARG, "gpq8: tensor %d: bad data", (int)i);
+        const uint64_t data_off = off;
+        off += (size_t)dlen;
+        if (!take(&n_scale, 4) || n_scale < 0 || (size_t)n_scale * 4 > size - off)
+            return fail(LAL_TAIL_ERR_ARG, "gpq8: tensor %d: bad scales", (int)i);
+        const uint64_t scale_off = off;
+        off += (size_t)n_scale * 4;
+        if (match) {
+            out->ndim = ndim;
+            for (int d = 0; d < 4; ++d) out->shape[d] = shape[d];
+            out->qtype = qtype;
+            out->data_offset = data_off;
+            out->data_len = dlen;
+            out->n_scale = n_scale;
+            out->scale_offset = scale_off;
+            return LAL_TAIL_OK;
+        }
+    }
+    return fail(LAL_TAIL_ERR_ARG, "gpq8: tensor %s not found", key);
+}
+
+int lal_tail_load_lm_head_gpq8(lal_tail *t, const void *blob, size_t size, const char *key) {
+    CHECK(ctx_check(t));
+    const char *name = key ? key : "lm_head.weight";
+    lal_gpq8_tensor e;
+    CHECK(lal_tail_gpq8_find(blob, size, name, &e));
+    const long long V = t->cfg.vocab_size, d = t->cfg.n_embd;
+    if (e.ndim != 2 || e.shape[0] != V || e.shape[1] != d)
+        return fail(LAL_TAIL_ERR_ARG, "gpq8: %s is not [%lld, %lld]", name, V, d);
+    const unsigned char *b = (const unsigned char *)blob;
+    if (e.qtype == 0) {
+        /* F32: quantized on the GPU as lal_quantize_q8_per_row does at load
+         * (qwen7b_server.c:1106-1112), this context's rows only */
+        if (e.data_len != (uint64_t)(V * d * 4)) return fail(LAL_TAIL_ERR_ARG, "gpq8: F32 size");
+        std::vector<float> rows;
+        const float *src = (const float *)(b + e.data_offset) + (size_t)t->row0 * d;
+        if (((uintptr_t)src & 3u) != 0) { /* the file's float data need not be aligned */
+            rows.resize((size_t)t->nrows * d);
+            memcpy(rows.data(), b + e.data_offset + 4ull * t->row0 * d, 4ull * t->nrows * d);
+            src = rows.data();
+        }
+        return lal_tail_load_lm_head_f32(t, src, 0, t->nrows);
+    }
+    if (e.data_len != (uint64_t)(V * d) || e.n_scale != V)
+        return fail(LAL_TAIL_ERR_ARG, "gpq8: Q8 size");
+    const int8_t *q = (const int8_t *)(b + e.data_offset) + (size_t)t->row0 * d;
+    std::vector<float> sc((size_t)t->nrows);
+    memcpy(sc.data(), b + e.scale_offset + 4ull * t->row0, 4ull * t->nrows);
+    return lal_tail_load_lm_head_q8(t, q, sc.data());
+}
+
+int lal_tail_set_filter(lal_tail *t, lal_filter_topk_fn filter, lal_token_decode_fn decode,
+                        lal_draw_fn draw, void *draw_ctx) {
+    CHECK(ctx_check(t));
+    if (!filter && !draw) {
+        t->filtered = false;
+        t->filter = nullptr;
+        t->decode = nullptr;
+        t->draw = nullptr;
+        t->draw_ctx = nullptr;
+        return LAL_TAIL_OK;
+    }
+    if (t->cfg.sampler != LAL_SAMPLER_SERVER || t->cfg.shard_count != 1)
+        return fail(LAL_TAIL_ERR_UNSUPPORTED,
+                    "set_filter: the filter hook needs the server sampler and one shard");
+    if (!t->f_cand_v) {
+        const size_t r = (size_t)t->nrows;
+        CU(cudaMalloc(&t->f_cand_v, 4 * r));
+        CU(cudaMalloc(&t->f_cand_i, 4 * r));
+        CU(cudaMalloc(&t->f_keep, 4 * r));
+        CU(cudaMalloc(&t->f_prefix, 4 * r));
+        CU(cudaMalloc(&t->f_u, 4));
+        CU(cudaMalloc(&t->f_tok, 4));
+        CU(cudaMalloc(&t->f_diag, sizeof(StreamDiag)));
+        t->f_mask.assign((size_t)t->cfg.vocab_size, 0);
+        t->f_ids.assign(r, 0);
+        t->f_ring.assign((size_t)std::max(1, t->cfg.history_cap), 0);
+    }
+    t->filter = filter;
+    t->decode = decode;
+    t->draw = draw;
+    t->draw_ctx = draw_ctx;
+    t->filtered = true;
     return LAL_TAIL_OK;
 }
 
