@@ -348,7 +348,7 @@ def run_ours(args, cfg):
             # host enqueues the step while the read runs: no idle gap is timed)
             for i in range(K):
                 with torch.cuda.stream(stream):
-                    torch.sum(flush, out=flush_out)
+                    torch.sum(flush, 0, out=flush_out)
                 ev[i][0].record(stream)
                 t.step_device(d_hid[i].data_ptr(), B, d_u[i].data_ptr(), d_tok[i].data_ptr())
                 ev[i][1].record(stream)
@@ -363,7 +363,7 @@ def run_ours(args, cfg):
         for i in range(K):
             if flush is not None:
                 with torch.cuda.stream(stream):
-                    torch.sum(flush, out=flush_out)
+                    torch.sum(flush, 0, out=flush_out)
             t.step_device(d_hid[i].data_ptr(), B, d_u[i].data_ptr(), d_tok[i].data_ptr())
         t.sync()
         kern_ms, n_launch = t.kernel_time()
@@ -375,7 +375,7 @@ def run_ours(args, cfg):
     e2e_s = 0.0
     for i in range(K):
         if flush is not None:
-            torch.sum(flush, out=flush_out)
+            torch.sum(flush, 0, out=flush_out)
             torch.cuda.synchronize()
         h = hid[W + K + i]
         u = us[W + K + i]
