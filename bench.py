@@ -323,6 +323,17 @@ def run_ours(args, cfg):
         if dist is not None:
             dist.barrier()
 
+    align = torch.zeros(1, device=local) if dist is not None else None
+
+    def evict_and_align():
+        """Untimed, on the tail's stream: evict the slice from L2, then (N > 1)
+        a one-element all-reduce so that every rank starts the step together
+        (the host enqueues it all ahead, so no idle time is timed)."""
+        with torch.cuda.stream(stream):
+            torch.sum(flush, 0, out=flush_out)
+            if align is not None:
+                dist.all_reduce(align)
+
     # warm-up through the public call
     for i in range(W):
         t.step(hid[i], us[i])
@@ -344,11 +355,11 @@ def run_ours(args, cfg):
             ev[0][1].record(stream)
         else:
             # the slice could stay in L2: a 512 MB read on the same stream
-            # evicts it before each step, outside the step's event pair (the
-            # host enqueues the step while the read runs: no idle gap is timed)
+            # evicts it before each step, and the ranks line up, outside the
+            # step's event pair (the host enqueues the step meanwhile: no idle
+            # gap is timed)
             for i in range(K):
-                with torch.cuda.stream(stream):
-                    torch.sum(flush, 0, out=flush_out)
+                evict_and_align()
                 ev[i][0].record(stream)
                 t.step_device(d_hid[i].data_ptr(), B, d_u[i].data_ptr(), d_tok[i].data_ptr())
                 ev[i][1].record(stream)
@@ -362,8 +373,7 @@ def run_ours(args, cfg):
         t.kernel_time()
         for i in range(K):
             if flush is not None:
-                with torch.cuda.stream(stream):
-                    torch.sum(flush, 0, out=flush_out)
+                evict_and_align()
             t.step_device(d_hid[i].data_ptr(), B, d_u[i].data_ptr(), d_tok[i].data_ptr())
         t.sync()
         kern_ms, n_launch = t.kernel_time()
@@ -377,6 +387,8 @@ def run_ours(args, cfg):
         if flush is not None:
             torch.sum(flush, 0, out=flush_out)
             torch.cuda.synchronize()
+            if dist is not None:
+                dist.barrier()  # every rank calls the step together (untimed)
         h = hid[W + K + i]
         u = us[W + K + i]
         t0 = time.perf_counter()
