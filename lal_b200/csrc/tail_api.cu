@@ -71,6 +71,8 @@ struct DeviceState {
     uint32_t *d_expf_x = nullptr, *d_expf_y = nullptr, *d_expf_bits = nullptr,
              *d_expf_off = nullptr;
     int expf_n = 0;
+    uint4 *d_expf_hash = nullptr; /* kExpfHashPairs buckets of two (x, y) slots */
+    int expf_hash_probe = 0;
 };
 std::mutex g_dev_mu;
 DeviceState g_dev[64];
@@ -124,6 +126,30 @@ int device_state(int dev, DeviceState **out) {
         CU(cudaMalloc(&ds.d_expf_off, 4ull * (kExpfBitmapWords + 1)));
         CU(cudaMemcpy(ds.d_expf_off, off.data(), 4ull * (kExpfBitmapWords + 1),
                       cudaMemcpyHostToDevice));
+        /* the hash form: linear probing by bucket, the first free slot */
+        std::vector<uint32_t> hash(4ull * kExpfHashPairs, 0u);
+        int probe_max = 1;
+        for (uint32_t i = 0; i < n; ++i) {
+            uint32_t xb, yb;
+            memcpy(&xb, lal_expf_fixups_blob + 4 + 4ull * i, 4);
+            memcpy(&yb, lal_expf_fixups_blob + 4 + 4ull * n + 4ull * i, 4);
+            uint32_t bk = expf_hash_bucket(xb);
+            for (int probe = 1;; ++probe) {
+                uint32_t *slot = &hash[4ull * bk];
+                const int at = slot[0] == 0u ? 0 : (slot[2] == 0u ? 2 : -1);
+                if (at >= 0) {
+                    slot[at] = xb;
+                    slot[at + 1] = yb;
+                    probe_max = std::max(probe_max, probe);
+                    break;
+                }
+                bk = (bk + 1u) & (kExpfHashPairs - 1u);
+            }
+        }
+        CU(cudaMalloc(&ds.d_expf_hash, 16ull * kExpfHashPairs));
+        CU(cudaMemcpy(ds.d_expf_hash, hash.data(), 16ull * kExpfHashPairs,
+                      cudaMemcpyHostToDevice));
+        ds.expf_hash_probe = probe_max;
         ds.expf_n = (int)n;
         ds.ready = true;
     }
@@ -341,6 +367,8 @@ void base_params(TailParams &p, const DeviceState *ds) {
     p.expf_n = ds->expf_n;
     p.expf_bits = ds->d_expf_bits;
     p.expf_off = ds->d_expf_off;
+    p.expf_hash = ds->d_expf_hash;
+    p.expf_hash_probe = ds->expf_hash_probe;
 }
 
 int sample_launch(DropinState *S, DeviceState *ds, float *logits, int V, float temperature,
@@ -766,7 +794,8 @@ int lal_tail_debug_expf(const float *x, float *y, int n) {
     CHECK(S->logits.ensure(4ull * n));
     CU(cudaMemcpyAsync(S->x.p, x, 4ull * n, cudaMemcpyHostToDevice, st));
     CU(launch_debug_expf((const float *)S->x.p, (float *)S->logits.p, n, ds->d_expf_x,
-                         ds->d_expf_y, ds->expf_n, ds->d_expf_bits, ds->d_expf_off, st));
+                         ds->d_expf_y, ds->expf_n, ds->d_expf_bits, ds->d_expf_off,
+                         ds->d_expf_hash, ds->expf_hash_probe, st));
     CU(cudaMemcpyAsync(y, S->logits.p, 4ull * n, cudaMemcpyDeviceToHost, st));
     CU(cudaStreamSynchronize(st));
     return LAL_TAIL_OK;
@@ -1531,6 +1560,8 @@ int lal_tail_shard_merge(lal_tail *t, int n_streams, const float *d_u, int *d_to
     m.expf_n = t->ds->expf_n;
     m.expf_bits = t->ds->d_expf_bits;
     m.expf_off = t->ds->d_expf_off;
+    m.expf_hash = t->ds->d_expf_hash;
+    m.expf_hash_probe = t->ds->expf_hash_probe;
     m.smem_cap = t->merge_cap;
     CU(launch_merge(m, n_streams, t->stream));
     return LAL_TAIL_OK;

@@ -169,6 +169,38 @@ __device__ __forceinline__ float expf_with_range(float x, uint32_t word, uint32_
     return lal_expf_rounded(x);
 }
 
+/* Hash form of the fix-up lookup, in two halves: the first issues the one
+ * 16-byte load of x's bucket (volatile, so it goes out where it is written,
+ * ahead of the work that hides its latency); the second resolves it, probing
+ * further buckets only when x's is full and holds neither x nor a gap. */
+__device__ __forceinline__ uint4 expf_hash_load(float x, const uint4 *hash) {
+    const uint32_t xb = __float_as_uint(x);
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if ((xb & 0x80000000u) && x <= 0.0f) {
+        const uint4 *a = hash + expf_hash_bucket(xb);
+        asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
+                     : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                     : "l"(a));
+    }
+    return v;
+}
+__device__ __forceinline__ float expf_hash_finish(float x, uint4 pr, const uint4 *hash,
+                                                  int max_probe) {
+    const uint32_t xb = __float_as_uint(x);
+    if ((xb & 0x80000000u) && x <= 0.0f) {
+        uint32_t bk = expf_hash_bucket(xb);
+        for (int probe = 0; probe < max_probe; ++probe) {
+            if (pr.x == xb) return __uint_as_float(pr.y);
+            if (pr.x == 0u) break;
+            if (pr.z == xb) return __uint_as_float(pr.w);
+            if (pr.z == 0u) break;
+            bk = (bk + 1u) & (kExpfHashPairs - 1u);
+            pr = __ldg(hash + bk);
+        }
+    }
+    return lal_expf_rounded(x);
+}
+
 /* ------------------------------------------------------- order keys --- */
 /* Monotone map float -> uint32 (larger float, larger key).  -0 maps like +0,
  * so key equality is float equality, as the reference's comparisons treat it. */

@@ -29,6 +29,15 @@ constexpr int kLocalMaxK = 64;
 /* words of the expf exception bitmap: bit (b >> 8) for b = bits(x) - 2^31,
  * x from -0 down to -inf (0x7F800000 >> 8 buckets) */
 constexpr int kExpfBitmapWords = ((0x7F800000u >> 8) >> 5) + 1;
+/* The fix-up table as an open-addressed hash: kExpfHashPairs 16-byte buckets
+ * of two (x bits, y bits) slots, linear probing by bucket from
+ * expf_hash_bucket(x); key 0 (never a fix-up input, all of which are
+ * negative) marks an empty slot.  One aligned 16-byte load resolves most
+ * lookups, and its address depends on x alone. */
+constexpr unsigned kExpfHashPairs = 1u << 18;
+__host__ __device__ inline unsigned expf_hash_bucket(uint32_t xb) {
+    return ((xb * 2654435761u) >> 13) & (kExpfHashPairs - 1u);
+}
 /* Largest per-CTA row slice (smem holds its logits, scales, penalty counts). */
 constexpr int kMaxRowsPerCta = 4096;
 /* Largest shard count of a vocab-sharded context. */
@@ -80,6 +89,8 @@ struct MergeParams {
     int expf_n;
     const uint32_t *expf_bits;
     const uint32_t *expf_off;
+    const uint4 *expf_hash;   /* hash form of the fix-ups, or null            */
+    int expf_hash_probe;
     int smem_cap;     /* candidates the CTA's shared memory holds             */
 };
 
@@ -149,6 +160,9 @@ struct TailParams {
     int expf_n;
     const uint32_t *expf_bits;
     const uint32_t *expf_off; /* [words+1]: first table entry of each bitmap word */
+    /* the same fix-ups as an open-addressed hash (null: use the bitmap) */
+    const uint4 *expf_hash;
+    int expf_hash_probe;     /* longest probe (buckets) of any table entry    */
     /* optional globaltimer stamps: [cta*8 + i] per CTA (start, prologue done,
      * rows done, list written) and [grid*8 + i] for the merge */
     unsigned long long *phase_ts;
@@ -276,6 +290,7 @@ cudaError_t launch_quantize_rows(const float *W, int d, int8_t *q, int ld,
                                  float *scale, int n_rows, cudaStream_t st);
 cudaError_t launch_debug_expf(const float *x, float *y, int n, const uint32_t *tx,
                               const uint32_t *ty, int tn, const uint32_t *bits,
-                              const uint32_t *off, cudaStream_t st);
+                              const uint32_t *off, const uint4 *hash, int hash_probe,
+                              cudaStream_t st);
 
 }  // namespace lal

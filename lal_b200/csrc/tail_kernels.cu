@@ -726,6 +726,7 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
     float max_l = -1e30f;
     float xw[2] = {0.0f, 0.0f};
     uint32_t bw[2] = {0u, 0u}, olo[2] = {0u, 0u}, ohi[2] = {0u, 0u};
+    uint4 hp[2] = {make_uint4(0u, 0u, 0u, 0u), make_uint4(0u, 0u, 0u, 0u)};
     if (early) {
         uint32_t mk = 0u;
         for (int j = tid; j < S; j += NT) mk = max(mk, Sk[j]);
@@ -741,8 +742,12 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
             const int j = tid + r * NT;
             if (j < S) {
                 xw[r] = __fdiv_rn(__fsub_rn(key2f(Sk[j]), max_l), temp);
-                bw[r] = expf_bitmap_word(xw[r], p.expf_bits);
-                expf_offsets(xw[r], p.expf_off, &olo[r], &ohi[r]);
+                if (p.expf_hash) {
+                    hp[r] = expf_hash_load(xw[r], p.expf_hash);
+                } else {
+                    bw[r] = expf_bitmap_word(xw[r], p.expf_bits);
+                    expf_offsets(xw[r], p.expf_off, &olo[r], &ohi[r]);
+                }
             }
         }
     }
@@ -775,7 +780,10 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
 #pragma unroll
             for (int r = 0; r < 2; ++r) {
                 const int j = tid + r * NT;
-                if (j < S) Ws[j] = expf_with_range(xw[r], bw[r], olo[r], ohi[r], p.expf_x, p.expf_y);
+                if (j < S)
+                    Ws[j] = p.expf_hash
+                                ? expf_hash_finish(xw[r], hp[r], p.expf_hash, p.expf_hash_probe)
+                                : expf_with_range(xw[r], bw[r], olo[r], ohi[r], p.expf_x, p.expf_y);
             }
         }
         /* a slot whose dropped tail reaches T lost candidates: refuse */
@@ -925,6 +933,8 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
         mp.expf_n = p.expf_n;
         mp.expf_bits = p.expf_bits;
         mp.expf_off = p.expf_off;
+        mp.expf_hash = p.expf_hash;
+        mp.expf_hash_probe = p.expf_hash_probe;
         mp.smem_cap = (p.area_bytes - kMergeHead) / 24;
         merge_sample(mp, 0, smem, ms, PeerRecords{p, ms});
         if (tid == 0) stamp(p, G * 8 + 7);
@@ -970,7 +980,9 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
         if (!early)
             for (int i = tid; i < m; i += NT) {
                 const float x = __fdiv_rn(__fsub_rn(Ov[i], max_l), temp);
-                Ce[i] = sampler_expf(x, p.expf_x, p.expf_y, p.expf_bits, p.expf_off);
+                Ce[i] = p.expf_hash ? expf_hash_finish(x, expf_hash_load(x, p.expf_hash),
+                                                       p.expf_hash, p.expf_hash_probe)
+                                    : sampler_expf(x, p.expf_x, p.expf_y, p.expf_bits, p.expf_off);
             }
         __syncthreads();
         /* sequential float sum in ascending vocab order; keep the prefix
@@ -1176,9 +1188,11 @@ __global__ void __launch_bounds__(NT) finish_kernel(const FinishParams f) {
 
 __global__ void debug_expf_kernel(const float *x, float *y, int n, const uint32_t *tx,
                                   const uint32_t *ty, const uint32_t *bits,
-                                  const uint32_t *off) {
+                                  const uint32_t *off, const uint4 *hash, int hash_probe) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < n) y[i] = sampler_expf(x[i], tx, ty, bits, off);
+    if (i < n)
+        y[i] = hash ? expf_hash_finish(x[i], expf_hash_load(x[i], hash), hash, hash_probe)
+                    : sampler_expf(x[i], tx, ty, bits, off);
 }
 
 /* Vocab-sharded step, second half: CTA b merges stream b's records from every
@@ -1259,6 +1273,7 @@ __device__ void merge_sample(const MergeParams &mp, int b, uint8_t *area, Misc *
     const bool fast = M <= 2 * NT;
     float xw[2] = {0.0f, 0.0f};
     uint32_t bw[2] = {0u, 0u}, olo[2] = {0u, 0u}, ohi[2] = {0u, 0u};
+    uint4 hp[2] = {make_uint4(0u, 0u, 0u, 0u), make_uint4(0u, 0u, 0u, 0u)};
     if (!greedy) {
         if (fast) {
 #pragma unroll
@@ -1266,14 +1281,22 @@ __device__ void merge_sample(const MergeParams &mp, int b, uint8_t *area, Misc *
                 const int e = tid + r * NT;
                 if (e < M) {
                     xw[r] = __fdiv_rn(__fsub_rn(key2f(Mk[e]), max_l), temp);
-                    bw[r] = expf_bitmap_word(xw[r], mp.expf_bits);
-                    expf_offsets(xw[r], mp.expf_off, &olo[r], &ohi[r]);
+                    if (mp.expf_hash) {
+                        hp[r] = expf_hash_load(xw[r], mp.expf_hash);
+                    } else {
+                        bw[r] = expf_bitmap_word(xw[r], mp.expf_bits);
+                        expf_offsets(xw[r], mp.expf_off, &olo[r], &ohi[r]);
+                    }
                 }
             }
         } else {
-            for (int e = tid; e < M; e += NT)
-                Mw[e] = sampler_expf(__fdiv_rn(__fsub_rn(key2f(Mk[e]), max_l), temp), mp.expf_x,
-                                     mp.expf_y, mp.expf_bits, mp.expf_off);
+            for (int e = tid; e < M; e += NT) {
+                const float x = __fdiv_rn(__fsub_rn(key2f(Mk[e]), max_l), temp);
+                Mw[e] = mp.expf_hash ? expf_hash_finish(x, expf_hash_load(x, mp.expf_hash),
+                                                        mp.expf_hash, mp.expf_hash_probe)
+                                     : sampler_expf(x, mp.expf_x, mp.expf_y, mp.expf_bits,
+                                                    mp.expf_off);
+            }
         }
     }
     /* T = min{ key : #{keys > key} < k }, the k-th largest with multiplicity */
@@ -1300,7 +1323,11 @@ __device__ void merge_sample(const MergeParams &mp, int b, uint8_t *area, Misc *
 #pragma unroll
             for (int r = 0; r < 2; ++r) {
                 const int e = tid + r * NT;
-                if (e < M) Mw[e] = expf_with_range(xw[r], bw[r], olo[r], ohi[r], mp.expf_x, mp.expf_y);
+                if (e < M)
+                    Mw[e] = mp.expf_hash
+                                ? expf_hash_finish(xw[r], hp[r], mp.expf_hash, mp.expf_hash_probe)
+                                : expf_with_range(xw[r], bw[r], olo[r], ohi[r], mp.expf_x,
+                                                  mp.expf_y);
             }
         __syncthreads();
     } else {
@@ -1671,9 +1698,11 @@ cudaError_t launch_sample_prepared(const TailParams &p, int grid, cudaStream_t s
 
 cudaError_t launch_debug_expf(const float *x, float *y, int n, const uint32_t *tx,
                               const uint32_t *ty, int tn, const uint32_t *bits,
-                              const uint32_t *off, cudaStream_t st) {
+                              const uint32_t *off, const uint4 *hash, int hash_probe,
+                              cudaStream_t st) {
     (void)tn;
-    debug_expf_kernel<<<(n + 255) / 256, 256, 0, st>>>(x, y, n, tx, ty, bits, off);
+    debug_expf_kernel<<<(n + 255) / 256, 256, 0, st>>>(x, y, n, tx, ty, bits, off, hash,
+                                                        hash_probe);
     return cudaGetLastError();
 }
 
