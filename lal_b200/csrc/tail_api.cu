@@ -226,7 +226,7 @@ struct SelectScratch {
         gslot_n = gmax + kMaxGrid;
         CU(cudaMemset(ghist, 0, 4ull * kWords));
         /* the small-k path uses one slot of kSlot entries per CTA */
-        cap = std::max(cap_, kMaxGrid * kSlot);
+        cap = std::max(cap_, kSelectCapMin);
         CU(cudaMalloc(&gkey, 4ull * cap));
         CU(cudaMalloc(&gidx, 4ull * cap));
         return LAL_TAIL_OK;

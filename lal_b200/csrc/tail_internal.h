@@ -26,6 +26,12 @@ constexpr int kRefineMax = 2048;
  * boundary then bounds T usefully; correctness never depends on it). */
 constexpr int kSlot = 128;
 constexpr int kLocalMaxK = 64;
+/* Each CTA also publishes a 48-byte head record {max key, slot count, -, -,
+ * the slot's first 4 keys, their 4 vocab ids} at kSlotHeads words into the
+ * superset buffer, so the last CTA reads three 16-byte vectors per CTA. */
+constexpr int kSlotHeads = kMaxGrid * kSlot;
+constexpr int kSlotHeadWords = 12;
+constexpr int kSelectCapMin = kSlotHeads + kMaxGrid * kSlotHeadWords;
 /* words of the expf exception bitmap: bit (b >> 8) for b = bits(x) - 2^31,
  * x from -0 down to -inf (0x7F800000 >> 8 buckets) */
 constexpr int kExpfBitmapWords = ((0x7F800000u >> 8) >> 5) + 1;

@@ -463,6 +463,7 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
             uint32_t r = ms->scan[0];
             for (int w = 1; w < NWARP; ++w) r = max(r, ms->scan[w]);
             p.gmax[cta] = r;
+            p.gcand_key[kSlotHeads + cta * kSlotHeadWords] = r;
         }
         __syncthreads();
     }
@@ -536,6 +537,7 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
         __syncthreads();
         uint32_t *slot_k = p.gcand_key + (size_t)cta * kSlot;
         int *slot_i = p.gcand_idx + (size_t)cta * kSlot;
+        uint32_t *head = p.gcand_key + kSlotHeads + cta * kSlotHeadWords;
         for (int j = tid; j < (int)n; j += NT) {
             const uint32_t me = tk[j];
             int r = 0;
@@ -545,8 +547,15 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
                 slot_k[r] = me;
                 slot_i[r] = p.row_base + c0 + ti[j];
             }
+            if (r < 4) {
+                head[4 + r] = me;
+                head[8 + r] = (uint32_t)(p.row_base + c0 + ti[j]);
+            }
         }
-        if (tid == 0) p.gslot_n[cta] = n;
+        if (tid == 0) {
+            p.gslot_n[cta] = n;
+            head[1] = n;
+        }
     } else {
         const int seg = (nloc + NT - 1) / NT;
         const int i0 = min(nloc, tid * seg), i1 = min(nloc, i0 + seg);
@@ -613,13 +622,19 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
     if (local_edges) {
         Lg = __ldcg(p.gL);
         if (tid < G) {
-            gmx = __ldcg(p.gmax + tid);
-            g_n = (int)__ldcg(p.gslot_n + tid);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                hk[q] = __ldcg(p.gcand_key + (size_t)tid * kSlot + q);
-                hi[q] = __ldcg(p.gcand_idx + (size_t)tid * kSlot + q);
-            }
+            const uint4 *h4 =
+                reinterpret_cast<const uint4 *>(p.gcand_key + kSlotHeads + tid * kSlotHeadWords);
+            const uint4 a = __ldcg(h4), b = __ldcg(h4 + 1), c = __ldcg(h4 + 2);
+            gmx = a.x;
+            g_n = (int)a.y;
+            hk[0] = b.x;
+            hk[1] = b.y;
+            hk[2] = b.z;
+            hk[3] = b.w;
+            hi[0] = (int)c.x;
+            hi[1] = (int)c.y;
+            hi[2] = (int)c.z;
+            hi[3] = (int)c.w;
         }
     }
     int m = 0;

@@ -59,7 +59,7 @@ constexpr int kNaDiag = kNaParams + 8;          /* StreamDiag                  *
 constexpr int kNaKeys = kNaDiag + 8;            /* superset keys [kNaMaxVocab] */
 constexpr int kNaIdx = kNaKeys + kNaMaxVocab;   /* superset ids [kNaMaxVocab]  */
 constexpr int kNaWords = kNaIdx + kNaMaxVocab;
-static_assert(kNaMaxVocab >= kMaxGrid * kSlot, "slot layout of the small-k select");
+static_assert(kNaMaxVocab >= kSelectCapMin, "slot layout of the small-k select");
 
 /* expf table: x [kNaMaxFixups], y [kNaMaxFixups], bitmap, offsets */
 constexpr int kNaExpfY = kNaMaxFixups;
