@@ -201,6 +201,25 @@ __device__ __forceinline__ float expf_hash_finish(float x, uint4 pr, const uint4
     return lal_expf_rounded(x);
 }
 
+/* expf_hash_finish with the rounded value yr = lal_expf_rounded(x) computed
+ * earlier (so its double-precision latency hides behind other work). */
+__device__ __forceinline__ float expf_hash_resolve(float x, float yr, uint4 pr, const uint4 *hash,
+                                                   int max_probe) {
+    const uint32_t xb = __float_as_uint(x);
+    if ((xb & 0x80000000u) && x <= 0.0f) {
+        uint32_t bk = expf_hash_bucket(xb);
+        for (int probe = 0; probe < max_probe; ++probe) {
+            if (pr.x == xb) return __uint_as_float(pr.y);
+            if (pr.x == 0u) break;
+            if (pr.z == xb) return __uint_as_float(pr.w);
+            if (pr.z == 0u) break;
+            bk = (bk + 1u) & (kExpfHashPairs - 1u);
+            pr = __ldg(hash + bk);
+        }
+    }
+    return yr;
+}
+
 /* ------------------------------------------------------- order keys --- */
 /* Monotone map float -> uint32 (larger float, larger key).  -0 maps like +0,
  * so key equality is float equality, as the reference's comparisons treat it. */

@@ -26,8 +26,9 @@ constexpr int kRefineMax = 2048;
  * boundary then bounds T usefully; correctness never depends on it). */
 constexpr int kSlot = 128;
 constexpr int kLocalMaxK = 64;
-/* Each CTA also publishes a 48-byte head record {max key, slot count, -, -,
- * the slot's first 4 keys, their 4 vocab ids} at kSlotHeads words into the
+/* Each CTA also publishes a 48-byte head record {max key, slot count, the
+ * slot's last kept key when its tail was dropped (else 0), -, the slot's
+ * first 4 keys, their 4 vocab ids} at kSlotHeads words into the
  * superset buffer, so the last CTA reads three 16-byte vectors per CTA. */
 constexpr int kSlotHeads = kMaxGrid * kSlot;
 constexpr int kSlotHeadWords = 12;

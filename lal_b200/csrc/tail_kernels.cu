@@ -35,6 +35,7 @@
 #include <algorithm>
 #include <cstdio>
 #include <cstring>
+#include <numeric>
 #include <utility>
 #include <vector>
 
@@ -551,10 +552,12 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
                 head[4 + r] = me;
                 head[8 + r] = (uint32_t)(p.row_base + c0 + ti[j]);
             }
+            if (r == kSlot - 1 && n > (uint32_t)kSlot) head[2] = me;
         }
         if (tid == 0) {
             p.gslot_n[cta] = n;
             head[1] = n;
+            if (n <= (uint32_t)kSlot) head[2] = 0u;
         }
     } else {
         const int seg = (nloc + NT - 1) / NT;
@@ -617,7 +620,7 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
      * entries (read whatever the count; only the first min(n, kSlot) count) */
     const int dev_status = __ldcg(p.status);
     const int Sg = (int)__ldcg(p.gcount);
-    uint32_t Lg = 0u, gmx = 0u, hk[4] = {0u, 0u, 0u, 0u};
+    uint32_t Lg = 0u, gmx = 0u, gdrop = 0u, hk[4] = {0u, 0u, 0u, 0u};
     int g_n = 0, hi[4] = {0, 0, 0, 0};
     if (local_edges) {
         Lg = __ldcg(p.gL);
@@ -627,6 +630,7 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
             const uint4 a = __ldcg(h4), b = __ldcg(h4 + 1), c = __ldcg(h4 + 2);
             gmx = a.x;
             g_n = (int)a.y;
+            gdrop = a.z;
             hk[0] = b.x;
             hk[1] = b.y;
             hk[2] = b.z;
@@ -705,7 +709,7 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
             }
         }
         __syncthreads();
-        if (g < G) ms->gm[g] = g_n > kSlot ? __ldcg(p.gcand_key + (size_t)g * kSlot + kSlot - 1) : 0u;
+        if (g < G) ms->gm[g] = gdrop;
         uint32_t tot;
         uint32_t pos = block_scan_excl(c, ms, &tot);
         S = (int)tot;
@@ -742,6 +746,7 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
     float xw[2] = {0.0f, 0.0f};
     uint32_t bw[2] = {0u, 0u}, olo[2] = {0u, 0u}, ohi[2] = {0u, 0u};
     uint4 hp[2] = {make_uint4(0u, 0u, 0u, 0u), make_uint4(0u, 0u, 0u, 0u)};
+    float yr[2] = {0.0f, 0.0f};
     if (early) {
         uint32_t mk = 0u;
         for (int j = tid; j < S; j += NT) mk = max(mk, Sk[j]);
@@ -759,6 +764,7 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
                 xw[r] = __fdiv_rn(__fsub_rn(key2f(Sk[j]), max_l), temp);
                 if (p.expf_hash) {
                     hp[r] = expf_hash_load(xw[r], p.expf_hash);
+                    yr[r] = lal_expf_rounded(xw[r]);
                 } else {
                     bw[r] = expf_bitmap_word(xw[r], p.expf_bits);
                     expf_offsets(xw[r], p.expf_off, &olo[r], &ohi[r]);
@@ -796,9 +802,10 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
             for (int r = 0; r < 2; ++r) {
                 const int j = tid + r * NT;
                 if (j < S)
-                    Ws[j] = p.expf_hash
-                                ? expf_hash_finish(xw[r], hp[r], p.expf_hash, p.expf_hash_probe)
-                                : expf_with_range(xw[r], bw[r], olo[r], ohi[r], p.expf_x, p.expf_y);
+                    Ws[j] = p.expf_hash ? expf_hash_resolve(xw[r], yr[r], hp[r], p.expf_hash,
+                                                            p.expf_hash_probe)
+                                        : expf_with_range(xw[r], bw[r], olo[r], ohi[r], p.expf_x,
+                                                          p.expf_y);
             }
         }
         /* a slot whose dropped tail reaches T lost candidates: refuse */
@@ -1289,6 +1296,7 @@ __device__ void merge_sample(const MergeParams &mp, int b, uint8_t *area, Misc *
     float xw[2] = {0.0f, 0.0f};
     uint32_t bw[2] = {0u, 0u}, olo[2] = {0u, 0u}, ohi[2] = {0u, 0u};
     uint4 hp[2] = {make_uint4(0u, 0u, 0u, 0u), make_uint4(0u, 0u, 0u, 0u)};
+    float yr[2] = {0.0f, 0.0f};
     if (!greedy) {
         if (fast) {
 #pragma unroll
@@ -1298,6 +1306,7 @@ __device__ void merge_sample(const MergeParams &mp, int b, uint8_t *area, Misc *
                     xw[r] = __fdiv_rn(__fsub_rn(key2f(Mk[e]), max_l), temp);
                     if (mp.expf_hash) {
                         hp[r] = expf_hash_load(xw[r], mp.expf_hash);
+                        yr[r] = lal_expf_rounded(xw[r]);
                     } else {
                         bw[r] = expf_bitmap_word(xw[r], mp.expf_bits);
                         expf_offsets(xw[r], mp.expf_off, &olo[r], &ohi[r]);
@@ -1340,7 +1349,8 @@ __device__ void merge_sample(const MergeParams &mp, int b, uint8_t *area, Misc *
                 const int e = tid + r * NT;
                 if (e < M)
                     Mw[e] = mp.expf_hash
-                                ? expf_hash_finish(xw[r], hp[r], mp.expf_hash, mp.expf_hash_probe)
+                                ? expf_hash_resolve(xw[r], yr[r], hp[r], mp.expf_hash,
+                                                    mp.expf_hash_probe)
                                 : expf_with_range(xw[r], bw[r], olo[r], ohi[r], mp.expf_x,
                                                   mp.expf_y);
             }
@@ -1499,6 +1509,7 @@ int round_nch(int ld) {
 }
 
 constexpr int kSmemLimit = 232448; /* 227 KB dynamic per block on sm_100 */
+constexpr int kStageTargetBytes = 57344; /* bytes of W per bulk-copy stage */
 
 int align_up(int v, int a) { return (v + a - 1) / a * a; }
 
@@ -1527,8 +1538,13 @@ int plan_launch(TailParams &p, int num_sms, int min_rows_per_cta) {
         p.stage_bytes = 0;
         p.area_bytes = budget;
     } else {
-        int R = std::max(1, 32768 / p.ld);
-        if (R >= 8) R = R / 8 * 8;
+        /* Few large stages: on B200 a ring of 3 x 56 KB bulk copies streams a
+         * 545 MB slice in 94 us/step, 6 x 28 KB in 106 us and 14 KB copies
+         * slower still.  A stage is about 56 KB of whole rows, a multiple of
+         * 4 KB where the row length allows it. */
+        const int unit = 4096 / std::gcd(p.ld, 4096);
+        int R = (kStageTargetBytes / p.ld) / unit * unit;
+        if (R < 1) R = std::max(1, kStageTargetBytes / p.ld);
         p.rows_per_stage = R;
         p.stage_bytes = align_up(R * p.ld, 128);
         p.stages = std::min(kMaxStages, budget / p.stage_bytes);
