@@ -7,6 +7,8 @@
  */
 #pragma once
 
+#include <cstddef>
+
 #include "tail_internal.h"
 #include "lal_expf.h"
 
@@ -243,8 +245,12 @@ struct Misc {
     int abort_flag;
     int ticket;
     int found;
-    uint32_t gm[kMaxGrid]; /* the last CTA's copy of the per-CTA maxima */
+    uint32_t cnt;           /* compaction counter of the small-k select */
+    uint32_t wmax[NWARP];   /* per-warp largest key of the CTA's rows */
+    /* the last CTA's copy of the per-CTA maxima (read as 16-byte vectors) */
+    alignas(16) uint32_t gm[kMaxGrid];
 };
+static_assert(offsetof(Misc, gm) % 16 == 0, "Misc::gm must be 16-byte aligned");
 
 /* Grid-wide barrier of a cooperative launch (every CTA resident).  The
  * wait is bounded: after kWaitNs it records DEV_TIMEOUT and returns false.
@@ -376,6 +382,61 @@ __device__ uint32_t boundary_bin(const uint32_t *h, int nb, uint32_t krem, Misc 
     *count = ms->sh[2];
     __syncthreads();
     return bin;
+}
+
+/* boundary_bin for one warp on a 4096-bin histogram whose highest non-empty
+ * bin is top: lanes sum 16 bins each (four 16-byte reads) in windows of 512
+ * bins going down from top, a warp scan finds the window, the lane and the
+ * bin where the count from the top reaches krem (1 <= krem <= the total).
+ * Every lane returns the bin. */
+__device__ __forceinline__ uint32_t warp_boundary_bin_4096(const uint32_t *h, uint32_t top,
+                                                           uint32_t krem) {
+    const int lane = threadIdx.x & 31;
+    uint32_t run = 0u;
+    for (int hi = (int)(top | 15u); hi >= 0; hi -= 512) {
+        const int base = hi - 16 * lane - 15; /* this lane's group [base, base + 15] */
+        uint32_t c[16];
+        uint32_t sum = 0u;
+        if (base >= 0) {
+            const uint4 *g = reinterpret_cast<const uint4 *>(h + base);
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+                const uint4 x = g[v];
+                c[15 - 4 * v] = x.x; /* c[q] = bin base + 15 - q: descending */
+                c[14 - 4 * v] = x.y;
+                c[13 - 4 * v] = x.z;
+                c[12 - 4 * v] = x.w;
+            }
+        } else {
+#pragma unroll
+            for (int q = 0; q < 16; ++q) c[q] = 0u;
+        }
+#pragma unroll
+        for (int q = 0; q < 16; ++q) sum += c[q];
+        uint32_t incl = sum;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += y;
+        }
+        const uint32_t total = __shfl_sync(0xffffffffu, incl, 31);
+        if (run + total >= krem) {
+            const uint32_t ex = run + incl - sum;
+            const unsigned who = __ballot_sync(0xffffffffu, ex < krem && krem <= ex + sum);
+            uint32_t bin = 0u;
+            if (lane == __ffs(who) - 1) {
+                uint32_t r = ex;
+#pragma unroll
+                for (int q = 0; q < 16; ++q) {
+                    if (r < krem && r + c[q] >= krem) bin = (uint32_t)(base + 15 - q);
+                    r += c[q];
+                }
+            }
+            return __shfl_sync(0xffffffffu, bin, __ffs(who) - 1);
+        }
+        run += total;
+    }
+    return 0u;
 }
 
 /* k-th largest key of the valid entries among i in [0, n): get(i, key)

@@ -207,6 +207,8 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
     if (tid == 0) {
         stamp(p, cta * 8 + 0);
         ms->abort_flag = 0;
+        ms->cnt = 0u;
+        for (int w = 0; w < NWARP; ++w) ms->wmax[w] = 0u;
         if (MODE != MODE_SAMPLE) {
             for (int s = 0; s < p.stages; ++s) {
                 mbar_init(&full_bar[s], 1);
@@ -344,6 +346,7 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
             }
         } else {
             const float sx = ms->sx;
+            uint32_t wmax = 0u; /* lane 0: largest key of this warp's rows */
             int4 xr[NCH];
 #pragma unroll
             for (int j = 0; j < NCH; ++j) {
@@ -388,7 +391,9 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
                         if (MODE == MODE_FUSED) {
                             l = penalise(l, cnt_s[lr], pen);
                             lg_s[lr] = l;
-                            atomicAdd(&hist_s[f2key(l) >> 20], 1u); /* level-0 bins */
+                            const uint32_t key = f2key(l);
+                            atomicAdd(&hist_s[key >> 20], 1u); /* level-0 bins */
+                            wmax = max(wmax, key);
                         }
                         p.logits[c0 + lr] = l;
                     }
@@ -396,6 +401,7 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&empty_bar[s]);
             }
+            if (lane == 0) ms->wmax[warp] = wmax;
         }
         __syncthreads();
         if (tid == 0) stamp(p, cta * 8 + 2);
@@ -411,6 +417,7 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
         }
     } else {
         __syncthreads(); /* penalty counts come from the consumers' prologue */
+        uint32_t wmax = 0u;
         for (int i = tid; i < nloc; i += NT) {
             float l = p.logits[c0 + i];
             const uint32_t cnt = cnt_s[i];
@@ -419,8 +426,12 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
                 p.logits[c0 + i] = l; /* the reference mutates logits in place */
             }
             lg_s[i] = l;
-            atomicAdd(&hist_s[f2key(l) >> 20], 1u); /* level-0 bins */
+            const uint32_t key = f2key(l);
+            atomicAdd(&hist_s[key >> 20], 1u); /* level-0 bins */
+            wmax = max(wmax, key);
         }
+        wmax = __reduce_max_sync(0xffffffffu, wmax);
+        if (lane == 0) ms->wmax[warp] = wmax;
         __syncthreads();
     }
 
@@ -448,25 +459,25 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
      * (k comparable to a slice) takes the global histogram below. */
     const bool local_edges = p.local_edges != 0; /* = use_local_edges(k, ...) */
     if (local_edges) {
-        /* (a CTA with fewer than k rows would give no bound: it keeps all) */
-        uint32_t ab, cnt;
-        const uint32_t bin = boundary_bin(hist_s, 4096, (uint32_t)min(k, nloc), ms, &ab, &cnt);
-        prefix = nloc >= k ? bin << 20 : 0u;
-        if (tid == 0 && nloc >= k) atomicMax(p.gL, prefix);
-        /* this CTA's largest key: the k-th largest of the CTAs' maxima is a
-         * second lower bound of T (distinct elements), usually much tighter */
-        uint32_t mk = 0u;
-        for (int i = tid; i < nloc; i += NT) mk = max(mk, f2key(lg_s[i]));
-        mk = __reduce_max_sync(0xffffffffu, mk);
-        if ((tid & 31) == 0) ms->scan[tid >> 5] = mk;
-        __syncthreads();
-        if (tid == 0) {
-            uint32_t r = ms->scan[0];
-            for (int w = 1; w < NWARP; ++w) r = max(r, ms->scan[w]);
-            p.gmax[cta] = r;
-            p.gcand_key[kSlotHeads + cta * kSlotHeadWords] = r;
+        /* warp 0 finds the boundary bin from the top, starting at the bin of
+         * this CTA's largest key (the warps' running maxima of the rows).
+         * That key also goes out with the head record: the k-th largest of
+         * the CTAs' maxima is a second lower bound of T (distinct elements),
+         * usually much tighter.  (A CTA with fewer than k rows would give no
+         * bound: it keeps all.) */
+        if (warp == 0) {
+            uint32_t mx = ms->wmax[0];
+            for (int w = 1; w < NWARP; ++w) mx = max(mx, ms->wmax[w]);
+            const uint32_t bin = warp_boundary_bin_4096(hist_s, mx >> 20, (uint32_t)min(k, nloc));
+            if (lane == 0) {
+                ms->sh[0] = bin;
+                if (nloc >= k) atomicMax(p.gL, bin << 20);
+                p.gmax[cta] = mx;
+                p.gcand_key[kSlotHeads + cta * kSlotHeadWords] = mx;
+            }
         }
         __syncthreads();
+        prefix = nloc >= k ? ms->sh[0] << 20 : 0u;
     }
     for (int level = 0; level < 3 && !local_edges; ++level) {
         const int bits = level == 0 ? 12 : 10;
@@ -519,38 +530,46 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
          * (ties by index), so that the last CTA reads only the head of each
          * slot; the slot count may exceed kSlot (the tail is dropped and the
          * last CTA checks that nothing dropped can be a candidate) */
-        uint32_t *tk = lh;
-        int *ti = reinterpret_cast<int *>(lh + p.rows_per_cta_max);
-        const int seg = (nloc + NT - 1) / NT;
-        const int i0 = min(nloc, tid * seg), i1 = min(nloc, i0 + seg);
-        uint32_t c = 0;
-        for (int i = i0; i < i1; ++i) c += f2key(lg_s[i]) >= Lb;
-        uint32_t n;
-        uint32_t pos = block_scan_excl(c, ms, &n);
-        for (int i = i0; i < i1; ++i) {
-            const uint32_t key = f2key(lg_s[i]);
-            if (key >= Lb) {
-                tk[pos] = key;
-                ti[pos] = i;
-                ++pos;
+        /* gather the keys >= Lb in any order (one shared-memory atomic per
+         * warp and round) as 64-bit words key << 32 | ~row: a larger word is
+         * a larger key, or the same key at a smaller row, so the rank below
+         * is one comparison an element */
+        uint64_t *tw = reinterpret_cast<uint64_t *>(lh);
+        const unsigned below = (1u << lane) - 1u;
+        for (int i0 = 0; i0 < nloc; i0 += NT) {
+            const int i = i0 + tid;
+            const uint32_t key = i < nloc ? f2key(lg_s[i]) : 0u;
+            const bool take = i < nloc && key >= Lb;
+            const unsigned mask = __ballot_sync(0xffffffffu, take);
+            if (mask) {
+                const int lead = __ffs(mask) - 1;
+                uint32_t base = 0u;
+                if (lane == lead) base = atomicAdd(&ms->cnt, (uint32_t)__popc(mask));
+                base = __shfl_sync(0xffffffffu, base, lead);
+                if (take)
+                    tw[base + (uint32_t)__popc(mask & below)] =
+                        ((uint64_t)key << 32) | (uint32_t)~(uint32_t)i;
             }
         }
         __syncthreads();
+        const uint32_t n = ms->cnt;
         uint32_t *slot_k = p.gcand_key + (size_t)cta * kSlot;
         int *slot_i = p.gcand_idx + (size_t)cta * kSlot;
         uint32_t *head = p.gcand_key + kSlotHeads + cta * kSlotHeadWords;
         for (int j = tid; j < (int)n; j += NT) {
-            const uint32_t me = tk[j];
+            const uint64_t w = tw[j];
+            const uint32_t me = (uint32_t)(w >> 32);
+            const int row = p.row_base + c0 + (int)~(uint32_t)w;
             int r = 0;
 #pragma unroll 8
-            for (int q = 0; q < (int)n; ++q) r += (tk[q] > me) || (tk[q] == me && q < j);
+            for (int q = 0; q < (int)n; ++q) r += tw[q] > w;
             if (r < kSlot) {
                 slot_k[r] = me;
-                slot_i[r] = p.row_base + c0 + ti[j];
+                slot_i[r] = row;
             }
             if (r < 4) {
                 head[4 + r] = me;
-                head[8 + r] = (uint32_t)(p.row_base + c0 + ti[j]);
+                head[8 + r] = (uint32_t)row;
             }
             if (r == kSlot - 1 && n > (uint32_t)kSlot) head[2] = me;
         }
@@ -601,8 +620,10 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
      * a power of two */
     /* grid-histogram path: the superset size is known (S_hist); small-k
      * path: the slot heads are small, a sixteenth of the area suffices */
-    const int s_cap = local_edges ? p.area_bytes / 16
-                                  : max(1, min(S_hist, p.area_bytes / 8 - 28 * 64));
+    /* a multiple of 4 entries: Si and the arrays after it start on 16-byte
+     * boundaries */
+    const int s_cap = local_edges ? p.area_bytes / 16 / 4 * 4
+                                  : max(4, min((S_hist + 3) & ~3, (p.area_bytes / 8 - 28 * 64) & ~3));
     int ccap = 1;
     while (ccap * 2 * 28 <= p.area_bytes - 8 * s_cap) ccap *= 2;
     uint32_t *Sk = reinterpret_cast<uint32_t *>(smem);
@@ -643,6 +664,8 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
     }
     int m = 0;
     uint32_t T = 0u;
+    uint32_t top_key = 0u; /* the superset's largest key, when known early */
+    bool top_known = false;
     bool fine = ok && dev_status == 0 &&
                 (local_edges || (Sg <= p.gcand_cap && Sg >= 1));
     int S = S_hist;
@@ -672,12 +695,19 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
                 if (gt < k) best = min(best, me);
             }
             best = __reduce_min_sync(0xffffffffu, best);
-            if ((tid & 31) == 0) ms->scan[tid >> 5] = best;
+            /* with it, the largest of the maxima: the superset's maximum */
+            const uint32_t gw = __reduce_max_sync(0xffffffffu, gmx);
+            if ((tid & 31) == 0) {
+                ms->scan[tid >> 5] = best;
+                ms->wmax[tid >> 5] = gw;
+            }
             __syncthreads();
             if (tid == 0) stamp(p, cta * 8 + 5);
             uint32_t L2 = ms->scan[0];
             for (int w = 1; w < NWARP; ++w) L2 = min(L2, ms->scan[w]);
             L = max(L, L2);
+            for (int w = 0; w < NWARP; ++w) top_key = max(top_key, ms->wmax[w]);
+            top_known = true;
             __syncthreads();
         }
         if (tid == 0) stamp(p, G * 8 + 1);
@@ -748,14 +778,17 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
     uint4 hp[2] = {make_uint4(0u, 0u, 0u, 0u), make_uint4(0u, 0u, 0u, 0u)};
     float yr[2] = {0.0f, 0.0f};
     if (early) {
-        uint32_t mk = 0u;
-        for (int j = tid; j < S; j += NT) mk = max(mk, Sk[j]);
-        mk = __reduce_max_sync(0xffffffffu, mk);
-        if ((tid & 31) == 0) ms->scan[tid >> 5] = mk;
-        __syncthreads();
-        uint32_t mx = ms->scan[0];
-        for (int w = 1; w < NWARP; ++w) mx = max(mx, ms->scan[w]);
-        __syncthreads();
+        uint32_t mx = top_key;
+        if (!top_known) {
+            uint32_t mk = 0u;
+            for (int j = tid; j < S; j += NT) mk = max(mk, Sk[j]);
+            mk = __reduce_max_sync(0xffffffffu, mk);
+            if ((tid & 31) == 0) ms->scan[tid >> 5] = mk;
+            __syncthreads();
+            mx = ms->scan[0];
+            for (int w = 1; w < NWARP; ++w) mx = max(mx, ms->scan[w]);
+            __syncthreads();
+        }
         max_l = fmaxf(-1e30f, key2f(mx));
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
