@@ -766,6 +766,11 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
                 Si[i] = __ldcg(p.gcand_idx + i);
             }
     }
+    /* pad the superset to a multiple of 4 (s_cap is one) */
+    if (fine && tid < ((S + 3) & ~3) - S) {
+        Sk[S + tid] = 0u;
+        Si[S + tid] = 0x7fffffff;
+    }
     __syncthreads();
     /* Early weights: the superset holds every candidate and the maximum, so
      * max_l (runtime/lal_sampling.h:107-109) is known before T; the weights'
@@ -805,14 +810,24 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
             }
         }
     }
+    /* at most one superset entry a thread: the candidates are placed in
+     * ascending vocab order straight from the superset */
+    const bool small = fine && S <= NT;
     if (fine) {
+        /* the superset is padded with zero keys (never greater, never a
+         * candidate) to a multiple of 4 for 16-byte reads */
+        const int S4 = (S + 3) & ~3;
+        const uint4 *K4 = reinterpret_cast<const uint4 *>(Sk);
         if (S <= 256) {
             /* T = min{ key : #{keys > key} < k } -- one pass per element */
             uint32_t best = 0xffffffffu;
             for (int t = tid; t < S; t += NT) {
                 const uint32_t me = Sk[t];
                 int gt = 0;
-                for (int j = 0; j < S; ++j) gt += Sk[j] > me;
+                for (int j = 0; j < S4 / 4; ++j) {
+                    const uint4 v = K4[j];
+                    gt += (v.x > me) + (v.y > me) + (v.z > me) + (v.w > me);
+                }
                 if (gt < k) best = min(best, me);
             }
             best = __reduce_min_sync(0xffffffffu, best);
@@ -820,7 +835,6 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
             __syncthreads();
             T = ms->scan[0];
             for (int w = 1; w < NWARP; ++w) T = min(T, ms->scan[w]);
-            __syncthreads();
         } else {
             T = block_kth_largest(
                 [&](int i, uint32_t &key) {
@@ -829,42 +843,68 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
                 },
                 S, min(k, S), ms);
         }
+        /* a slot whose dropped tail reaches T lost candidates: refuse (the
+         * barrier also keeps ms->scan until every thread has read T) */
+        const uint32_t drop = (local_edges && tid < G) ? ms->gm[tid] : 0u;
+        const bool lost = __syncthreads_or(drop != 0u && drop >= T) != 0;
         if (tid == 0) stamp(p, G * 8 + 3);
-        if (early) {
-#pragma unroll
-            for (int r = 0; r < 2; ++r) {
-                const int j = tid + r * NT;
-                if (j < S)
-                    Ws[j] = p.expf_hash ? expf_hash_resolve(xw[r], yr[r], hp[r], p.expf_hash,
-                                                            p.expf_hash_probe)
-                                        : expf_with_range(xw[r], bw[r], olo[r], ohi[r], p.expf_x,
-                                                          p.expf_y);
-            }
-        }
-        /* a slot whose dropped tail reaches T lost candidates: refuse */
-        if (tid == 0) ms->found = 0;
-        __syncthreads();
-        if (tid == 0) stamp(p, cta * 8 + 6);
-        if (local_edges)
-            for (int g = tid; g < G; g += NT)
-                if (ms->gm[g] != 0u && ms->gm[g] >= T) ms->found = 1;
-        /* candidates {v : l[v] >= T} (superset order) */
-        const int seg = (S + NT - 1) / NT;
-        const int e0 = min(S, tid * seg), e1 = min(S, e0 + seg);
-        uint32_t c = 0;
-        for (int e = e0; e < e1; ++e) c += Sk[e] >= T;
-        uint32_t mt;
-        uint32_t pos = block_scan_excl(c, ms, &mt);
-        m = (int)mt;
-        if (m <= ccap)
-            for (int e = e0; e < e1; ++e)
-                if (Sk[e] >= T) {
-                    Cv[pos] = key2f(Sk[e]);
-                    Ci[pos] = Si[e];
-                    Cw[pos] = early ? Ws[e] : 0.0f;
-                    ++pos;
+        if (small) {
+            /* a candidate's rank by vocab index among the candidates is its
+             * place; the barrier counts them */
+            const bool cand = tid < S && Sk[tid] >= T;
+            if (cand) {
+                const uint32_t me = Sk[tid];
+                const int mi = Si[tid];
+                const int4 *I4 = reinterpret_cast<const int4 *>(Si);
+                int r = 0;
+                for (int j = 0; j < S4 / 4; ++j) {
+                    const uint4 v = K4[j];
+                    const int4 ix = I4[j];
+                    r += (v.x >= T && ix.x < mi) + (v.y >= T && ix.y < mi) +
+                         (v.z >= T && ix.z < mi) + (v.w >= T && ix.w < mi);
                 }
-        fine = m >= 1 && m <= ccap && ms->found == 0;
+                if (r < ccap) {
+                    Oi[r] = mi;
+                    Ov[r] = key2f(me);
+                    Ce[r] = !early ? 0.0f
+                            : p.expf_hash ? expf_hash_resolve(xw[0], yr[0], hp[0], p.expf_hash,
+                                                              p.expf_hash_probe)
+                                          : expf_with_range(xw[0], bw[0], olo[0], ohi[0],
+                                                            p.expf_x, p.expf_y);
+                }
+            }
+            m = __syncthreads_count(cand);
+            fine = m >= 1 && m <= ccap && !lost;
+        } else {
+            if (early) {
+#pragma unroll
+                for (int r = 0; r < 2; ++r) {
+                    const int j = tid + r * NT;
+                    if (j < S)
+                        Ws[j] = p.expf_hash ? expf_hash_resolve(xw[r], yr[r], hp[r], p.expf_hash,
+                                                                p.expf_hash_probe)
+                                            : expf_with_range(xw[r], bw[r], olo[r], ohi[r],
+                                                              p.expf_x, p.expf_y);
+                }
+            }
+            /* candidates {v : l[v] >= T} (superset order) */
+            const int seg = (S + NT - 1) / NT;
+            const int e0 = min(S, tid * seg), e1 = min(S, e0 + seg);
+            uint32_t c = 0;
+            for (int e = e0; e < e1; ++e) c += Sk[e] >= T;
+            uint32_t mt;
+            uint32_t pos = block_scan_excl(c, ms, &mt);
+            m = (int)mt;
+            if (m <= ccap)
+                for (int e = e0; e < e1; ++e)
+                    if (Sk[e] >= T) {
+                        Cv[pos] = key2f(Sk[e]);
+                        Ci[pos] = Si[e];
+                        Cw[pos] = early ? Ws[e] : 0.0f;
+                        ++pos;
+                    }
+            fine = m >= 1 && m <= ccap && !lost;
+        }
     }
     __syncthreads();
 
@@ -908,8 +948,10 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
         return;
     }
 
-    /* ascending vocab order: rank by counting for small sets, else bitonic */
-    if (m <= 64) {
+    /* ascending vocab order (placed already for a small superset): rank by
+     * counting for small sets, else bitonic */
+    if (small) {
+    } else if (m <= 64) {
         for (int i = tid; i < m; i += NT) {
             const int me = Ci[i];
             int r = 0;
