@@ -260,6 +260,17 @@ int lal_tail_shard_merge(lal_tail *t, int n_streams, const float *d_u, int *d_to
  * lal_tail_step_device is not filtered.  All NULL switches it off. */
 int lal_tail_set_filter(lal_tail *t, lal_filter_topk_fn filter, lal_token_decode_fn decode,
                         lal_draw_fn draw, void *draw_ctx);
+/* The model's final RMSNorm fused as the tail's prologue: replaces
+ * qwen7b_rms_norm(g_ln, g_x, g_norm_f_w, N_EMBD) at
+ * tools/server/qwen7b_server.c:820 (runtime/lal_simd_optim.h:32-58, the AVX2
+ * build; eps RMS_EPS = 1e-6f there).  With norm_w set (n_embd floats, copied
+ * to the device), every later step's hidden input is the residual stream x,
+ * and the step quantizes (x * inv_rms) * w with the reference's exact sum
+ * order instead of the hidden itself; the per-stream, batched and sharded
+ * steps all apply it.  NULL switches it off.  n_embd <= 4096 and a multiple of 8
+ * (the reference's scalar tail loop, whose rounding its compiler decides, is
+ * then empty; LAL_TAIL_ERR_UNSUPPORTED otherwise). */
+int lal_tail_set_final_norm(lal_tail *t, const float *norm_w, float eps);
 /* Diagnostics and penalised logits (this slice's rows) of the last step. */
 int lal_tail_get_diag(lal_tail *t, int stream, lal_tail_diag *out);
 int lal_tail_get_logits(lal_tail *t, int stream, float *logits_rows);

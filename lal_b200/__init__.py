@@ -128,6 +128,7 @@ SIGNATURES = {
     "lal_tail_connect_peers": (C.c_int, [_vp, _vp]),
     "lal_tail_disconnect_peers": (C.c_int, [_vp]),
     "lal_tail_set_filter": (C.c_int, [_vp, _vp, _vp, _vp, _vp]),
+    "lal_tail_set_final_norm": (C.c_int, [_vp, _vp, C.c_float]),
     "lal_tail_gpq8_find": (C.c_int, [_vp, C.c_size_t, C.c_char_p, C.POINTER(Gpq8Tensor)]),
     "lal_tail_load_lm_head_gpq8": (C.c_int, [_vp, _vp, C.c_size_t, C.c_char_p]),
     "lal_tail_sample_token_noalloc": (C.c_int, [_vp, _ip, _fp, _ip, _fp, _vp, _ip, _fp, _vp,
@@ -425,6 +426,18 @@ class DecodeTail:
 
     def disconnect_peers(self):
         _check(lib().lal_tail_disconnect_peers(self.h))
+
+    def set_final_norm(self, norm_w: Optional[np.ndarray], eps: float = 1e-6):
+        """Fuse the model's final RMSNorm into the step (qwen7b_server.c:820):
+        later steps take the residual stream x and quantize (x * inv_rms) * w.
+        None switches it off."""
+        if norm_w is None:
+            _check(lib().lal_tail_set_final_norm(self.h, None, C.c_float(0.0)))
+            return
+        w = np.ascontiguousarray(norm_w, np.float32)
+        if w.size != self.cfg.n_embd:
+            raise ValueError(f"norm weights: {w.size} values for n_embd {self.cfg.n_embd}")
+        _check(lib().lal_tail_set_final_norm(self.h, _ptr(w), C.c_float(eps)))
 
     def set_filter(self, filt=None, draw: Optional[Callable[[], float]] = None, decode=None):
         """Level-2 filter hook for step(): filt(keep, n_vocab, last, recent,

@@ -870,6 +870,8 @@ struct lal_tail {
     int *f_cand_i = nullptr, *f_keep = nullptr, *f_tok = nullptr;
     StreamDiag *f_diag = nullptr;
     std::vector<int> f_mask, f_ids, f_ring, f_keep_h;
+    /* the final RMSNorm's weights on the device (lal_tail_set_final_norm) */
+    float *d_norm_w = nullptr;
 };
 
 namespace {
@@ -890,7 +892,7 @@ void destroy_ctx(lal_tail *t) {
                     t->hist_ids, t->hist_n, t->hist_head, t->diag, t->phase_ts,
                     t->x_send, t->x_recv, t->xq_b, t->sx_b, t->gmax_b, t->x_peer, t->d_peer,
                     t->f_cand_v, t->f_prefix, t->f_u, t->f_cand_i, t->f_keep, t->f_tok,
-                    t->f_diag};
+                    t->f_diag, t->d_norm_w};
     for (void *b : bufs)
         if (b) cudaFree(b);
     t->sel.free_all();
@@ -1004,6 +1006,8 @@ int enqueue_step(lal_tail *t, const float *d_hidden, int n, const float *d_u, in
         BatchStep bs;
         memset(&bs, 0, sizeof(bs));
         bs.hidden = d_hidden;
+        bs.norm_w = t->plan.norm_w;
+        bs.norm_eps = t->plan.norm_eps;
         bs.d = t->cfg.n_embd;
         bs.B = n;
         bs.logits = t->logits;
@@ -1704,6 +1708,35 @@ int lal_tail_load_lm_head_gpq8(lal_tail *t, const void *blob, size_t size, const
     std::vector<float> sc((size_t)t->nrows);
     memcpy(sc.data(), b + e.scale_offset + 4ull * t->row0, 4ull * t->nrows);
     return lal_tail_load_lm_head_q8(t, q, sc.data());
+}
+
+int lal_tail_set_final_norm(lal_tail *t, const float *norm_w, float eps) {
+    CHECK(ctx_check(t));
+    if (!norm_w) {
+        CU(cudaStreamSynchronize(t->stream));
+        t->plan.norm_w = nullptr;
+        t->plan.norm_eps = 0.0f;
+        return LAL_TAIL_OK;
+    }
+    const int d = t->cfg.n_embd;
+    /* n_embd % 8 == 0: the reference's SIMD loop then covers every element;
+     * its scalar tail loop (lal_simd_optim.h:45) is compiled by the
+     * reference's compiler into a mix of separately rounded and fused
+     * products, which no fixed rule reproduces */
+    if (d > kNormMaxD || d % 8 != 0)
+        return fail(LAL_TAIL_ERR_UNSUPPORTED,
+                    "set_final_norm: n_embd %d must be a multiple of 8 and <= %d", d, kNormMaxD);
+    if (!(eps >= 0.0f) || eps == INFINITY)
+        return fail(LAL_TAIL_ERR_ARG, "set_final_norm: eps must be finite and >= 0");
+    if (!t->d_norm_w) CU(cudaMalloc(&t->d_norm_w, sizeof(float) * (size_t)d));
+    /* on the context's stream: steps already queued keep reading the old
+     * weights until they finish, later steps see the new ones */
+    CU(cudaMemcpyAsync(t->d_norm_w, norm_w, sizeof(float) * (size_t)d, cudaMemcpyHostToDevice,
+                       t->stream));
+    CU(cudaStreamSynchronize(t->stream));
+    t->plan.norm_w = t->d_norm_w;
+    t->plan.norm_eps = eps;
+    return LAL_TAIL_OK;
 }
 
 int lal_tail_set_filter(lal_tail *t, lal_filter_topk_fn filter, lal_token_decode_fn decode,

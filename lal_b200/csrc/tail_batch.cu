@@ -132,13 +132,30 @@ __host__ __device__ constexpr uint32_t idesc_i8(int M, int N) {
 
 /* -------------------------------------------------- batch quantize --- */
 __global__ void __launch_bounds__(NT) quantize_batch_kernel(const float *x, int d, int8_t *xq,
-                                                            int ld, float *scale_out) {
+                                                            int ld, float *scale_out,
+                                                            const float *norm_w, float norm_eps) {
     __shared__ Misc ms;
+    __shared__ float xs[kNormMaxD];
     const int b = blockIdx.x;
     const float *row = x + (size_t)b * d;
     int8_t *out = xq + (size_t)b * ld;
+    /* the final RMSNorm first when the step takes the residual stream
+     * (runtime/lal_simd_optim.h:32-58): the normalised row replaces x */
+    float inv_rms = 0.0f;
+    if (norm_w != nullptr) {
+        for (int i = threadIdx.x; i < d; i += NT) xs[i] = row[i];
+        __syncthreads();
+        if (threadIdx.x < 8) ms.nrm[threadIdx.x] = rmsnorm_lane(xs, d, threadIdx.x);
+        __syncthreads();
+        if (threadIdx.x == 0) ms.ninv = rmsnorm_inv(ms.nrm, d, norm_eps);
+        __syncthreads();
+        inv_rms = ms.ninv;
+    }
+    auto value = [&](int i) {
+        return norm_w != nullptr ? rmsnorm_apply(xs[i], inv_rms, __ldg(norm_w + i)) : row[i];
+    };
     float m = 0.0f;
-    for (int i = threadIdx.x; i < d; i += NT) m = fmaxf(m, fabsf(row[i]));
+    for (int i = threadIdx.x; i < d; i += NT) m = fmaxf(m, fabsf(value(i)));
     m = block_max_f(m, &ms);
     float scale = __fdiv_rn(m, 127.0f);
     if (scale < 1e-8f) scale = 1e-8f;
@@ -147,7 +164,7 @@ __global__ void __launch_bounds__(NT) quantize_batch_kernel(const float *x, int 
     for (int i = threadIdx.x; i < ld; i += NT) {
         int v = 0;
         if (i < d) {
-            const float s = __fmul_rn(row[i], inv);
+            const float s = __fmul_rn(value(i), inv);
             if (s != s) v = -127;
             else {
                 v = (i < n8) ? __float2int_rn(s) : __float2int_rz(s);
@@ -899,7 +916,8 @@ cudaError_t batch_launch(BatchPlan &bp, const BatchStep &s, cudaStream_t st) {
         bp.x_ready |= 1u << xi;
     }
     /* 1. quantize the B hidden vectors */
-    quantize_batch_kernel<<<s.B, NT, 0, st>>>(s.hidden, s.d, bp.xq, bp.ld, bp.sx);
+    quantize_batch_kernel<<<s.B, NT, 0, st>>>(s.hidden, s.d, bp.xq, bp.ld, bp.sx, s.norm_w,
+                                              s.norm_eps);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     /* 2. logits = X W^T on the tensor cores */

@@ -241,6 +241,8 @@ struct Misc {
     uint32_t sh[16];
     float fred[NWARP];
     float sx;
+    float nrm[8];  /* the RMSNorm lane sums */
+    float ninv;    /* inv_rms */
     float sum;
     int abort_flag;
     int ticket;
@@ -382,6 +384,30 @@ __device__ uint32_t boundary_bin(const uint32_t *h, int nb, uint32_t krem, Misc 
     *count = ms->sh[2];
     __syncthreads();
     return bin;
+}
+
+/* The reference's final RMSNorm (runtime/lal_simd_optim.h:32-58, the
+ * AVX2+FMA build the servers use; called at tools/server/qwen7b_server.c:820),
+ * for n a multiple of 8 (the reference's scalar tail loop is then empty):
+ *   lane j of eight accumulates x[i]^2 for i = j (mod 8) with fused
+ *   multiply-adds in index order (rmsnorm_lane, one thread a lane); the
+ *   lanes combine as ((v0+v4)+(v1+v5)) + ((v2+v6)+(v3+v7)) -- the two 128-bit
+ *   halves added, then two horizontal adds; inv_rms = 1 / sqrtf(ms / n + eps);
+ *   the output is (x[i] * inv_rms) * w[i]. */
+__device__ __forceinline__ float rmsnorm_lane(const float *xs, int n, int j) {
+    float acc = 0.0f;
+#pragma unroll 8
+    for (int i = j; i < n; i += 8) acc = __fmaf_rn(xs[i], xs[i], acc);
+    return acc;
+}
+__device__ __forceinline__ float rmsnorm_inv(const float *v, int n, float eps) {
+    const float s0 = __fadd_rn(v[0], v[4]), s1 = __fadd_rn(v[1], v[5]);
+    const float s2 = __fadd_rn(v[2], v[6]), s3 = __fadd_rn(v[3], v[7]);
+    const float ms = __fadd_rn(__fadd_rn(s0, s1), __fadd_rn(s2, s3));
+    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ms, (float)n), eps)));
+}
+__device__ __forceinline__ float rmsnorm_apply(float x, float inv, float w) {
+    return __fmul_rn(__fmul_rn(x, inv), w);
 }
 
 /* boundary_bin for one warp on a 4096-bin histogram whose highest non-empty

@@ -24,6 +24,9 @@ constexpr int kRefineMax = 2048;
 /* Small-k select: per-CTA slot of the sorted local superset; the strategy is
  * used only for k <= kLocalMaxK (and 2k <= the rows of a CTA: each CTA's own
  * boundary then bounds T usefully; correctness never depends on it). */
+/* the longest hidden vector the fused final RMSNorm accepts (it holds the
+ * vector in the consumer warps' registers, 16 values a thread) */
+constexpr int kNormMaxD = 4096;
 constexpr int kSlot = 128;
 constexpr int kLocalMaxK = 64;
 /* Each CTA also publishes a 48-byte head record {max key, slot count, the
@@ -112,6 +115,10 @@ struct TailParams {
     int d, ld;
     /* inputs */
     const float *hidden;     /* FUSED: [B][d]                                 */
+    /* FUSED: when set, hidden is the residual stream before the final RMSNorm
+     * (weights norm_w [d], epsilon norm_eps), applied in the prologue */
+    const float *norm_w;
+    float norm_eps;
     const int8_t *xq_in;     /* LMHEAD: quantized vector [d]                  */
     float scale_x_in;        /* LMHEAD                                        */
     /* LMHEAD: local rows < trunc_rows_end sum only columns < trunc_cols (the
@@ -261,6 +268,8 @@ struct BatchPlan {
 };
 struct BatchStep {
     const float *hidden;
+    const float *norm_w; /* the final RMSNorm first, when set */
+    float norm_eps;
     int d, B;
     float *logits; /* [B][rows] */
     int row_base, vocab, variant;

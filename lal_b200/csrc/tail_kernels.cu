@@ -253,9 +253,39 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
                 ids[j] = (use_pen && i < hn) ? __ldg(p.hist_ids + i) : -1;
             }
         }
+        /* the final RMSNorm's weights, when the step takes the residual
+         * stream (d <= kHReg * NC: the whole vector sits in registers) */
+        const bool norm = MODE == MODE_FUSED && p.norm_w != nullptr;
+        float wv[kHReg];
+        if (norm) {
+#pragma unroll
+            for (int j = 0; j < kHReg; ++j) {
+                const int i = ctid + j * NC;
+                wv[j] = i < p.d ? __ldg(p.norm_w + i) : 0.0f;
+            }
+        }
         if (MODE != MODE_SAMPLE)
 #pragma unroll 4
             for (int i = ctid; i < nloc; i += NC) sw_s[i] = __ldg(p.scale_w + c0 + i);
+        if (norm) {
+            /* runtime/lal_simd_optim.h:32-58 through the key histogram's
+             * shared memory (zeroed after): eight lane sums, combined and
+             * inverted by one thread, then x * inv_rms * w in registers */
+            float *xs = reinterpret_cast<float *>(hist_s);
+#pragma unroll
+            for (int j = 0; j < kHReg; ++j) {
+                const int i = ctid + j * NC;
+                if (i < p.d) xs[i] = hv[j];
+            }
+            consumer_sync();
+            if (ctid < 8) ms->nrm[ctid] = rmsnorm_lane(xs, p.d, ctid);
+            consumer_sync();
+            if (ctid == 0) ms->ninv = rmsnorm_inv(ms->nrm, p.d, p.norm_eps);
+            consumer_sync();
+            const float inv_rms = ms->ninv;
+#pragma unroll
+            for (int j = 0; j < kHReg; ++j) hv[j] = rmsnorm_apply(hv[j], inv_rms, wv[j]);
+        }
         if (MODE != MODE_LMHEAD) {
             for (int i = ctid; i < nloc; i += NC) cnt_s[i] = 0u;
             for (int i = ctid; i < 4096; i += NC) hist_s[i] = 0u;

@@ -64,6 +64,7 @@ def port():
         if not os.path.exists(PORT_SO):
             build()
         lib = C.CDLL(PORT_SO)
+        lib.orc_rms_norm.argtypes = [_f32p, _f32p, _f32p, C.c_int, C.c_float]
         lib.orc_quantize_x_int8.restype = C.c_float
         lib.orc_quantize_x_int8.argtypes = [_f32p, _i8p, C.c_int]
         lib.orc_compute_abs_xq.argtypes = [_i8p, _u8p, C.c_int]
@@ -107,6 +108,7 @@ def ref():
         lib = C.CDLL(REF_SO)
         lib.ref_vocab_max.restype = C.c_int
         lib.ref_xq_max.restype = C.c_int
+        lib.ref_rms_norm.argtypes = [_f32p, _f32p, _f32p, C.c_int, C.c_float]
         lib.ref_quantize_x_int8.restype = C.c_float
         lib.ref_quantize_x_int8.argtypes = [_f32p, _i8p, C.c_int]
         lib.ref_compute_abs_xq.argtypes = [_i8p, _u8p, C.c_int]
@@ -141,6 +143,18 @@ def _ptr(a):
 
 
 # ---- convenience wrappers (numpy in, numpy out) --------------------------------
+
+def rms_norm(x: np.ndarray, w: np.ndarray, eps: float = 1e-6, lib: str = "port"):
+    """The final RMSNorm (runtime/lal_simd_optim.h:32-58) of one vector whose
+    length is a multiple of 8."""
+    x = np.ascontiguousarray(x, np.float32)
+    if x.size % 8 != 0 or x.size == 0:
+        raise ValueError("rms_norm: the length must be a positive multiple of 8")
+    w = np.ascontiguousarray(w, np.float32)
+    out = np.empty_like(x)
+    (port().orc_rms_norm if lib == "port" else ref().ref_rms_norm)(out, x, w, x.size, eps)
+    return out
+
 
 def quantize_x(x: np.ndarray, lib: str = "port"):
     x = np.ascontiguousarray(x, np.float32)

@@ -26,6 +26,25 @@ static int cvt_rne(float v) {
     return (int)nearbyintf(v); /* default rounding mode: nearest-even */
 }
 
+/* runtime/lal_simd_optim.h:32-58, for n a multiple of 8 (returns without
+ * writing otherwise: the reference's scalar tail loop at :45 is compiled by
+ * its compiler into a mix of separately rounded and fused products that no
+ * fixed rule reproduces).  Eight lane accumulators: lane j takes x[i]^2 for
+ * i = j (mod 8) as fused multiply-adds in index order (_mm256_fmadd_ps,
+ * :39-43); lal_hsum_m256 (:21-28) adds the 128-bit halves (v_j + v_{j+4})
+ * and then two horizontal adds: ((s0+s1)+(s2+s3)).  inv_rms =
+ * 1/sqrtf(ms/n + eps) (:47); the output is (x * inv_rms) * w (:52-56). */
+void orc_rms_norm(float *out, const float *x, const float *w, int n, float eps) {
+    if (n <= 0 || n % 8 != 0) return;
+    float v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int i = 0; i < n; i += 8)
+        for (int j = 0; j < 8; ++j) v[j] = fmaf(x[i + j], x[i + j], v[j]);
+    const float s0 = v[0] + v[4], s1 = v[1] + v[5], s2 = v[2] + v[6], s3 = v[3] + v[7];
+    const float ms = (s0 + s1) + (s2 + s3);
+    const float inv = 1.0f / sqrtf(ms / (float)n + eps);
+    for (int i = 0; i < n; ++i) out[i] = (x[i] * inv) * w[i];
+}
+
 float orc_quantize_x_int8(const float *x, int8_t *xq, int n) {
     float max_abs = 0.0f;
     for (int i = 0; i < n; i++) {

@@ -31,6 +31,9 @@ typedef struct {
     int   drew;        /* 1 when the reference would have called rand()    */
 } orc_sample_info;
 
+/* runtime/lal_simd_optim.h:32-58 (AVX2+FMA build): the final RMSNorm,
+ * tools/server/qwen7b_server.c:820; n a multiple of 8. */
+void  orc_rms_norm(float *out, const float *x, const float *w, int n, float eps);
 /* runtime/lal_q8_kernel.h:375-424 (AVX2+FMA build, the one the servers use). */
 float orc_quantize_x_int8(const float *x, int8_t *xq, int n);
 /* runtime/lal_q8_kernel.h:450-460 */

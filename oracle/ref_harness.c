@@ -23,6 +23,11 @@
 REF_API int ref_vocab_max(void) { return VOCAB_SIZE; }
 REF_API int ref_xq_max(void) { return XQ_MAX; }
 
+/* the server's final RMSNorm (qwen7b_server.c:624-626, 820) */
+REF_API void ref_rms_norm(float *out, const float *x, const float *w, int n, float eps) {
+    lal_rms_norm_simd(out, x, w, n, eps);
+}
+
 REF_API float ref_quantize_x_int8(const float *x, int8_t *xq, int n) {
     return lal_quantize_x_int8(x, xq, n);
 }

@@ -42,6 +42,21 @@ def quantize_x_inputs():
     return xs
 
 
+def rms_norm_inputs():
+    """(x, w, eps) for the final RMSNorm (runtime/lal_simd_optim.h:32-58): both
+    model widths, other multiples of 8 (the only lengths with a fixed sum
+    order: see orc_rms_norm), tiny and large scales, the 4096 limit."""
+    g = _rng(23)
+    out = []
+    for n, scale, eps in ((3584, 1.0, 1e-6), (3584, 40.0, 1e-6), (768, 3.0, 1e-5),
+                          (776, 0.5, 1e-6), (16, 7.0, 1e-6), (8, 2.0, 0.0),
+                          (4096, 1e-3, 1e-6), (64, 1e-20, 1e-6)):
+        x = (g.standard_normal(n) * scale).astype(np.float32)
+        w = (1.0 + 0.25 * g.standard_normal(n)).astype(np.float32)
+        out.append((x, w, np.float32(eps)))
+    return out
+
+
 def lm_head_inputs():
     """(W fp32 [V,d], x fp32 [d], [(v0, v1), ...]) for the LM-head kernels."""
     out = []

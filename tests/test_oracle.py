@@ -141,3 +141,22 @@ def test_uncapped_heap_defines_large_k():
         tok, mut, info = oracle.sample(lg, 0.7, k, 1.0, None, 0.5)
         assert info.threshold == np.sort(lg)[::-1][k - 1]
         assert info.n_cand == int((lg >= info.threshold).sum())
+
+
+def test_rms_norm_matches_golden(golden, golden_meta):
+    for i, (x, w, eps) in enumerate(cases.rms_norm_inputs()):
+        assert h(x) + h(w) == golden_meta["hashes"][f"rn{i}"], "input generator drifted"
+        np.testing.assert_array_equal(bits(oracle.rms_norm(x, w, float(eps), "port")),
+                                      bits(golden[f"rn{i}"]))
+
+
+@pytest.mark.skipif(not oracle.have_ref(), reason="oracle/_ref not built")
+def test_rms_norm_port_matches_reference_on_random_vectors():
+    """Fresh vectors of lengths that are multiples of 8."""
+    g = np.random.default_rng(3)
+    for trial in range(200):
+        n = int(g.choice([8, 16, 776, 768, 3584, 1000, 4096]))
+        x = (g.standard_normal(n) * g.uniform(0.01, 50)).astype(np.float32)
+        w = (1 + 0.2 * g.standard_normal(n)).astype(np.float32)
+        np.testing.assert_array_equal(bits(oracle.rms_norm(x, w, 1e-6, "port")),
+                                      bits(oracle.rms_norm(x, w, 1e-6, "ref")))
