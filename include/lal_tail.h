@@ -54,6 +54,16 @@ extern "C" {
  * mass is not positive). */
 #define LAL_SAMPLER_LIBRARY 0
 #define LAL_SAMPLER_SERVER  1
+/* GPT2 = the GPT-2 server's int8 LM head and sampler, a second drop-in for
+ * lm_head_int8_parallel (tools/server/gpt2_server.c:2125-2214) and its
+ * sampling block (gpt2_server.c:2862-3013, top-p off, no filter hook):
+ * truncating quantizer, int8 logits of every row, the 512 rows the server's
+ * min-heap keeps re-scored in float, then LIBRARY's arithmetic on the
+ * re-scored logits, except that a draw of exactly 0 returns row 0.  u[b] is
+ * the caller's (float)(rand() % 1000000) / 1000000.0f.  One shard, n_embd a
+ * multiple of 8; lal_tail_get_logits returns the re-scored, penalised
+ * logits (the server's g_logits after the step). */
+#define LAL_SAMPLER_GPT2    2
 
 /* The calling thread's last error message ("" if none). */
 const char *lal_tail_last_error(void);
@@ -135,7 +145,7 @@ typedef struct {
     int max_streams;   /* B capacity                                        */
     int max_top_k;     /* largest top_k a step will use                     */
     int history_cap;   /* per-stream penalty-history capacity (server: 256) */
-    int sampler;       /* LAL_SAMPLER_LIBRARY or LAL_SAMPLER_SERVER         */
+    int sampler;       /* LAL_SAMPLER_LIBRARY, _SERVER or _GPT2             */
     int device;        /* CUDA device ordinal; -1 = the current device      */
     int shard_rank;    /* this context owns vocab rows                      */
     int shard_count;   /*   [rank*V/count, (rank+1)*V/count)                */

@@ -30,6 +30,7 @@ LIB_PATH = os.path.join(HERE, "liblal_tail.so")
 
 LAL_SAMPLER_LIBRARY = 0
 LAL_SAMPLER_SERVER = 1
+LAL_SAMPLER_GPT2 = 2
 
 ERRORS = {0: "OK", 1: "ERR_ARG", 2: "ERR_CUDA", 3: "ERR_NOMEM", 4: "ERR_TIMEOUT",
           5: "ERR_CAPACITY", 6: "ERR_STATE", 7: "ERR_COMM", 8: "ERR_UNSUPPORTED"}

@@ -30,7 +30,8 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVFLAGS = ["-O3", "-std=c++17", "-lineinfo", "-fmad=false", "-Xcompiler",
            "-fPIC,-ffp-contract=off", f"-I{INCLUDE}", f"-I{CSRC}"]
 
-CU_SOURCES = ["tail_kernels.cu", "tail_batch.cu", "tail_api.cu", "tail_noalloc.cu"]
+CU_SOURCES = ["tail_kernels.cu", "tail_batch.cu", "tail_gpt2.cu", "tail_api.cu",
+              "tail_noalloc.cu"]
 HEADERS = ["tail_internal.h", "tail_device.cuh", "lal_expf.h", "../../include/lal_tail.h",
            "../../include/runtime/lal_q8_kernel.h", "../../include/runtime/lal_sampling.h"]
 

@@ -872,6 +872,15 @@ struct lal_tail {
     std::vector<int> f_mask, f_ids, f_ring, f_keep_h;
     /* the final RMSNorm's weights on the device (lal_tail_set_final_norm) */
     float *d_norm_w = nullptr;
+    /* LAL_SAMPLER_GPT2: the launch plans of the LM head, the RERANK_N
+     * candidates select and the sampler; the quantized vector and its scale,
+     * the select's parameter block, candidate list and diagnostics */
+    TailParams g2_lm, g2_sel, g2_smp;
+    int g2_grid_lm = 0, g2_grid_sel = 0, g2_grid_smp = 0, g2_cap = 0, g2_n = 0;
+    int8_t *g2_xq = nullptr;
+    float *g2_sx = nullptr, *g2_cand_v = nullptr;
+    int *g2_cand_i = nullptr, *g2_par = nullptr, *g2_tok = nullptr;
+    StreamDiag *g2_diag = nullptr;
 };
 
 namespace {
@@ -892,7 +901,8 @@ void destroy_ctx(lal_tail *t) {
                     t->hist_ids, t->hist_n, t->hist_head, t->diag, t->phase_ts,
                     t->x_send, t->x_recv, t->xq_b, t->sx_b, t->gmax_b, t->x_peer, t->d_peer,
                     t->f_cand_v, t->f_prefix, t->f_u, t->f_cand_i, t->f_keep, t->f_tok,
-                    t->f_diag, t->d_norm_w};
+                    t->f_diag, t->d_norm_w, t->g2_xq, t->g2_sx, t->g2_cand_v, t->g2_cand_i,
+                    t->g2_par, t->g2_tok, t->g2_diag};
     for (void *b : bufs)
         if (b) cudaFree(b);
     t->sel.free_all();
@@ -901,6 +911,132 @@ void destroy_ctx(lal_tail *t) {
     for (cudaEvent_t e : t->ev) cudaEventDestroy(e);
     if (t->stream) cudaStreamDestroy(t->stream);
     delete t;
+}
+
+/* LAL_SAMPLER_GPT2 contexts (one shard): the plans and buffers of the five
+ * launches of a step (tail_gpt2.cu) */
+int gpt2_alloc(lal_tail *t) {
+    const lal_tail_config &c = t->cfg;
+    const int V = c.vocab_size, num_sms = t->ds->num_sms;
+    t->g2_n = std::min(kGpt2RerankN, V);
+    t->g2_cap = std::min(V, t->g2_n + 1024);
+    TailParams &lm = t->g2_lm;
+    base_params(lm, t->ds);
+    lm.mode = MODE_LMHEAD;
+    lm.rows = t->nrows;
+    lm.row_base = 0;
+    lm.vocab = V;
+    lm.d = c.n_embd;
+    lm.ld = t->ld;
+    lm.B = 1;
+    lm.max_k = 1;
+    lm.trunc_cols = t->ld;
+    lm.trunc_rows_end = 0;
+    t->g2_grid_lm = plan_launch(lm, num_sms, 8);
+    auto sample_plan = [&](TailParams &q, int max_k) {
+        base_params(q, t->ds);
+        q.mode = MODE_SAMPLE;
+        q.variant = VARIANT_GPT2;
+        q.rows = V;
+        q.row_base = 0;
+        q.vocab = V;
+        q.d = q.ld = 16;
+        q.B = 1;
+        q.max_k = max_k;
+        return plan_launch(q, num_sms, 64);
+    };
+    t->g2_grid_sel = sample_plan(t->g2_sel, t->g2_n);
+    t->g2_grid_smp = sample_plan(t->g2_smp, std::min(c.max_top_k, V));
+    if (t->g2_grid_lm < 1 || t->g2_grid_sel < 1 || t->g2_grid_smp < 1)
+        return fail(LAL_TAIL_ERR_UNSUPPORTED, "gpt2 tail: shape V=%d d=%d unsupported", V,
+                    c.n_embd);
+    CU(cudaMalloc(&t->g2_xq, (size_t)t->ld));
+    CU(cudaMalloc(&t->g2_sx, sizeof(float)));
+    CU(cudaMalloc(&t->g2_cand_v, sizeof(float) * (size_t)t->g2_cap));
+    CU(cudaMalloc(&t->g2_cand_i, sizeof(int) * (size_t)t->g2_cap));
+    CU(cudaMalloc(&t->g2_tok, sizeof(int)));
+    CU(cudaMalloc(&t->g2_diag, sizeof(StreamDiag)));
+    /* the select's parameters: temperature 1, top_k RERANK_N, no penalty */
+    const struct {
+        float t;
+        int k;
+        float pen;
+        float u;
+        int hn, head;
+    } sp = {1.0f, t->g2_n, 1.0f, 0.0f, 0, 0};
+    CU(cudaMalloc(&t->g2_par, sizeof(sp)));
+    CU(cudaMemcpy(t->g2_par, &sp, sizeof(sp), cudaMemcpyHostToDevice));
+    return LAL_TAIL_OK;
+}
+
+/* One stream of a LAL_SAMPLER_GPT2 step (tail_gpt2.cu has the sequence). */
+int enqueue_gpt2(lal_tail *t, int b, const float *d_hidden, const float *d_u, int *d_tokens) {
+    const int d = t->cfg.n_embd, V = t->cfg.vocab_size;
+    const int hc = std::max(1, t->cfg.history_cap);
+    cudaStream_t st = t->stream;
+    const float *x = d_hidden + (size_t)b * d;
+    float *logits = t->logits + (size_t)b * t->nrows;
+    int *status = t->io_out + t->cfg.max_streams;
+    CU(launch_gpt2_quantize(x, d, t->g2_xq, t->ld, t->g2_sx, st));
+    TailParams lm = t->g2_lm;
+    lm.W = t->W;
+    lm.scale_w = t->sw;
+    lm.xq_in = t->g2_xq;
+    lm.scale_x_dev = t->g2_sx;
+    lm.logits = logits;
+    lm.status = status;
+    const bool time_it = t->timing && t->ev_used + 2 <= (int)t->ev.size();
+    if (time_it) CU(cudaEventRecord(t->ev[t->ev_used], st));
+    CU(launch_tail(lm, t->g2_grid_lm, st));
+    if (time_it) {
+        CU(cudaEventRecord(t->ev[t->ev_used + 1], st));
+        t->ev_used += 2;
+    }
+    /* the RERANK_N largest int8 logits and every tie at the boundary */
+    TailParams q = t->g2_sel;
+    char *pb = reinterpret_cast<char *>(t->g2_par);
+    q.logits = logits;
+    q.temperature = reinterpret_cast<const float *>(pb + 0);
+    q.top_k = reinterpret_cast<const int *>(pb + 4);
+    q.rep_penalty = reinterpret_cast<const float *>(pb + 8);
+    q.u = reinterpret_cast<const float *>(pb + 12);
+    q.hist_n = reinterpret_cast<int *>(pb + 16);
+    q.hist_head = reinterpret_cast<int *>(pb + 20);
+    q.hist_ids = t->hist_ids;
+    q.hist_cap = 0;
+    q.push_history = 0;
+    q.tokens = t->g2_tok;
+    q.diag = t->g2_diag;
+    t->sel.fill(q);
+    q.status = status;
+    q.cand_val_out = t->g2_cand_v;
+    q.cand_idx_out = t->g2_cand_i;
+    q.cand_out_cap = t->g2_cap;
+    q.candidates_only = 1;
+    q.local_edges = use_local_edges(t->g2_n, q.rows_per_cta_max);
+    CU(launch_tail(q, t->g2_grid_sel, st));
+    CU(launch_gpt2_rerank(x, d, t->W, t->ld, t->sw, logits, V, t->g2_cand_i, t->g2_cap,
+                          t->g2_diag, t->g2_n, status, t->ds->num_sms, st));
+    /* the server's sampler on the re-scored logits */
+    TailParams r = t->g2_smp;
+    r.logits = logits;
+    r.temperature = t->temp + b;
+    r.top_k = t->topk + b;
+    r.rep_penalty = t->pen + b;
+    r.u = d_u + b;
+    r.hist_ids = t->hist_ids + (size_t)b * hc;
+    r.hist_n = t->hist_n + b;
+    r.hist_head = t->hist_head + b;
+    r.hist_cap = t->cfg.history_cap;
+    r.push_history = t->cfg.history_cap > 0 ? 1 : 0;
+    r.tokens = d_tokens + b;
+    r.diag = t->diag + b;
+    t->sel.fill(r);
+    r.status = status;
+    r.local_edges =
+        use_local_edges(effective_k(t->h_temp[b], t->h_topk[b], V, V), r.rows_per_cta_max);
+    CU(launch_tail(r, t->g2_grid_smp, st));
+    return LAL_TAIL_OK;
 }
 
 int ctx_alloc(lal_tail *t) {
@@ -935,7 +1071,9 @@ int ctx_alloc(lal_tail *t) {
     TailParams &p = t->plan;
     base_params(p, t->ds);
     p.mode = MODE_FUSED;
-    p.variant = c.sampler == LAL_SAMPLER_SERVER ? VARIANT_SERVER : VARIANT_LIBRARY;
+    p.variant = c.sampler == LAL_SAMPLER_SERVER ? VARIANT_SERVER
+                : c.sampler == LAL_SAMPLER_GPT2 ? VARIANT_GPT2
+                                                : VARIANT_LIBRARY;
     p.rows = t->nrows;
     p.row_base = t->row0;
     p.vocab = c.vocab_size;
@@ -968,6 +1106,7 @@ int ctx_alloc(lal_tail *t) {
         CU(cudaMemset(t->x_peer, 0, pb));
         CU(cudaMalloc(&t->d_peer, sizeof(uint8_t *) * c.shard_count));
     }
+    if (c.sampler == LAL_SAMPLER_GPT2) return gpt2_alloc(t);
     /* batched step: one pass over W for all streams on the tensor cores */
     if (B >= 2 && B <= 256) {
         CU(cudaMalloc(&t->xq_b, (size_t)256 * t->ld));
@@ -1002,6 +1141,12 @@ int enqueue_step(lal_tail *t, const float *d_hidden, int n, const float *d_u, in
                     "use lal_tail_shard_select, an all-gather of the records and "
                     "lal_tail_shard_merge");
     const int hc = std::max(1, t->cfg.history_cap);
+    if (t->cfg.sampler == LAL_SAMPLER_GPT2) {
+        if (shard_export)
+            return fail(LAL_TAIL_ERR_UNSUPPORTED, "the GPT-2 sampler has no sharded step");
+        for (int b = 0; b < n; ++b) CHECK(enqueue_gpt2(t, b, d_hidden, d_u, d_tokens));
+        return LAL_TAIL_OK;
+    }
     if (t->batch_ok && n >= 2 && !getenv_flag("LAL_TAIL_PER_STREAM")) {
         BatchStep bs;
         memset(&bs, 0, sizeof(bs));
@@ -1248,8 +1393,14 @@ int lal_tail_create(const lal_tail_config *cfg, lal_tail **out) {
     if (c.vocab_size < 1 || c.n_embd < 1 || c.max_streams < 1 || c.max_top_k < 1 ||
         c.history_cap < 0 || c.shard_count < 1 || c.shard_rank < 0 || c.shard_rank >= c.shard_count)
         return fail(LAL_TAIL_ERR_ARG, "create: bad config");
-    if (c.sampler != LAL_SAMPLER_LIBRARY && c.sampler != LAL_SAMPLER_SERVER)
+    if (c.sampler != LAL_SAMPLER_LIBRARY && c.sampler != LAL_SAMPLER_SERVER &&
+        c.sampler != LAL_SAMPLER_GPT2)
         return fail(LAL_TAIL_ERR_ARG, "create: unknown sampler %d", c.sampler);
+    /* the GPT-2 tail re-scores rows with eight-lane sums and no scalar tail
+     * (gpt2_server.c:2207-2210 has one, which its compiler may contract) */
+    if (c.sampler == LAL_SAMPLER_GPT2 && (c.shard_count != 1 || c.n_embd % 8 != 0))
+        return fail(LAL_TAIL_ERR_UNSUPPORTED,
+                    "create: the GPT-2 sampler needs one shard and n_embd a multiple of 8");
     lal_tail *t = new lal_tail();
     t->cfg = c;
     int dev = c.device;

@@ -54,7 +54,12 @@ constexpr int kMaxRowsPerCta = 4096;
 constexpr int kMaxRanks = 64;
 
 enum Mode : int { MODE_FUSED = 0, MODE_LMHEAD = 1, MODE_SAMPLE = 2 };
-enum Variant : int { VARIANT_LIBRARY = 0, VARIANT_SERVER = 1 };
+/* LIBRARY: runtime/lal_sampling.h; SERVER: qwen7b_server.c's
+ * lal_sample_token_filtered; GPT2: gpt2_server.c's sampler (LIBRARY's
+ * arithmetic; a draw of r == 0 returns row 0) */
+enum Variant : int { VARIANT_LIBRARY = 0, VARIANT_SERVER = 1, VARIANT_GPT2 = 2 };
+/* rows the GPT-2 server re-scores in float (gpt2_server.c:2123) */
+constexpr int kGpt2RerankN = 512;
 
 /* Device status word values (mirrors LAL_TAIL_ERR_* in include/lal_tail.h). */
 enum DevStatus : int { DEV_OK = 0, DEV_TIMEOUT = 4, DEV_CAPACITY = 5 };
@@ -121,6 +126,7 @@ struct TailParams {
     float norm_eps;
     const int8_t *xq_in;     /* LMHEAD: quantized vector [d]                  */
     float scale_x_in;        /* LMHEAD                                        */
+    const float *scale_x_dev; /* LMHEAD: the scale in device memory, if set    */
     /* LMHEAD: local rows < trunc_rows_end sum only columns < trunc_cols (the
      * 8-row form's dropped tail, runtime/lal_q8_kernel.h:577-611); otherwise
      * trunc_cols = ld. */
@@ -299,6 +305,12 @@ inline int batch_groups(int rows) { return (rows + 127) / 128 * 4; }
 cudaError_t batch_launch(BatchPlan &bp, const BatchStep &s, cudaStream_t st);
 int plan_launch(TailParams &p, int num_sms, int min_rows_per_cta);
 cudaError_t launch_tail(const TailParams &p, int grid, cudaStream_t st);
+cudaError_t launch_gpt2_quantize(const float *x, int d, int8_t *xq, int ld, float *scale_out,
+                                 cudaStream_t st);
+cudaError_t launch_gpt2_rerank(const float *x, int d, const int8_t *W, int ld, const float *sw,
+                               float *logits, int V, const int *cand_i, int cand_cap,
+                               const StreamDiag *sel_diag, int N, const int *status,
+                               int num_sms, cudaStream_t st);
 cudaError_t launch_quantize_x(const float *x, int8_t *xq, float *scale, int n,
                               cudaStream_t st);
 cudaError_t launch_abs_xq(const int8_t *xq, uint8_t *ax, int n, cudaStream_t st);

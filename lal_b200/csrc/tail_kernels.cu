@@ -338,7 +338,7 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
             if (ctid == 0) ms->sx = scale;
         } else if (MODE == MODE_LMHEAD) {
             for (int i = ctid; i < p.ld; i += NC) xq_s[i] = i < p.d ? p.xq_in[i] : (int8_t)0;
-            if (ctid == 0) ms->sx = p.scale_x_in;
+            if (ctid == 0) ms->sx = p.scale_x_dev ? *p.scale_x_dev : p.scale_x_in;
         }
         consumer_sync();
         if (ctid == 0) stamp(p, cta * 8 + 1);
@@ -1164,6 +1164,9 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
             if (first != 0x7fffffff) atomicMin(&ms->found, first);
             __syncthreads();
             token = ms->found != 0x7fffffff ? Oi[ms->found] : p.vocab - 1;
+            /* gpt2_server.c:2996-3001 walks every row, adding zeros below T:
+             * a draw of exactly 0 stops at row 0 */
+            if (p.variant == VARIANT_GPT2 && r == 0.0f) token = 0;
         }
     }
     if (tid == 0) {

@@ -23,6 +23,7 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 PORT_SO = os.path.join(HERE, "liblal_oracle.so")
+REF_GPT2_SO = os.path.join(HERE, "_ref", "liblal_ref_gpt2.so")
 REF_SO = os.path.join(HERE, "_ref", "liblal_ref.so")
 
 _f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
@@ -65,6 +66,13 @@ def port():
             build()
         lib = C.CDLL(PORT_SO)
         lib.orc_rms_norm.argtypes = [_f32p, _f32p, _f32p, C.c_int, C.c_float]
+        lib.orc_gpt2_quantize_x.restype = C.c_float
+        lib.orc_gpt2_quantize_x.argtypes = [_f32p, _i8p, C.c_int]
+        lib.orc_gpt2_lm_head.restype = C.c_int
+        lib.orc_gpt2_lm_head.argtypes = [_f32p, _f32p, _i8p, _f32p, C.c_int, C.c_int, _i32p]
+        lib.orc_gpt2_sample.restype = C.c_int
+        lib.orc_gpt2_sample.argtypes = [_f32p, C.c_int, C.c_float, C.c_int, C.c_float,
+                                        C.c_void_p, C.c_int, C.c_float, C.POINTER(SampleInfo)]
         lib.orc_quantize_x_int8.restype = C.c_float
         lib.orc_quantize_x_int8.argtypes = [_f32p, _i8p, C.c_int]
         lib.orc_compute_abs_xq.argtypes = [_i8p, _u8p, C.c_int]
@@ -136,6 +144,97 @@ def ref():
                                       C.POINTER(C.c_int), C.c_int, C.c_int, C.c_int]
         _ref = lib
     return _ref
+
+
+_ref_gpt2 = None
+
+
+def have_ref_gpt2() -> bool:
+    return os.path.exists(REF_GPT2_SO)
+
+
+def ref_gpt2():
+    """ctypes handle of the GPT-2 server's own LM-head code (oracle/_ref)."""
+    global _ref_gpt2
+    if _ref_gpt2 is None:
+        if not have_ref_gpt2():
+            raise FileNotFoundError(f"{REF_GPT2_SO} not built (needs the reference sources)")
+        lib = C.CDLL(REF_GPT2_SO)
+        lib.ref_gpt2_vocab.restype = C.c_int
+        lib.ref_gpt2_n_embd.restype = C.c_int
+        lib.ref_gpt2_quantize_x.restype = C.c_float
+        lib.ref_gpt2_quantize_x.argtypes = [_f32p, _i8p, C.c_int]
+        lib.ref_gpt2_lm_head.argtypes = [_f32p, _f32p, _i8p, _f32p, C.c_int]
+        _ref_gpt2 = lib
+    return _ref_gpt2
+
+
+def gpt2_quantize_x(x: np.ndarray, lib: str = "port"):
+    """lm_head_quantize_x (gpt2_server.c:1982-1998): (scale, xq)."""
+    x = np.ascontiguousarray(x, np.float32)
+    xq = np.zeros(x.size, np.int8)
+    fn = port().orc_gpt2_quantize_x if lib == "port" else ref_gpt2().ref_gpt2_quantize_x
+    return np.float32(fn(x, xq, x.size)), xq
+
+
+def gpt2_lm_head(x: np.ndarray, wq: np.ndarray, sw: np.ndarray, lib: str = "port",
+                 n_threads: int = 1):
+    """lm_head_int8_parallel (gpt2_server.c:2125-2214): the logits of every
+    row, the 512 kept by the server's heap re-scored in float.  The port also
+    returns the kept rows (heap order)."""
+    x = np.ascontiguousarray(x, np.float32)
+    wq = np.ascontiguousarray(wq, np.int8)
+    sw = np.ascontiguousarray(sw, np.float32)
+    V, d = wq.shape
+    logits = np.zeros(V, np.float32)
+    if lib == "port":
+        kept = np.zeros(512, np.int32)
+        n = port().orc_gpt2_lm_head(logits, x, wq.reshape(-1), sw, V, d, kept)
+        return logits, kept[:n].copy()
+    R = ref_gpt2()
+    if (V, d) != (R.ref_gpt2_vocab(), R.ref_gpt2_n_embd()):
+        raise ValueError("the GPT-2 server is compiled for V=50257, d=768")
+    R.ref_gpt2_lm_head(logits, x, wq.reshape(-1).copy(), sw.copy(), n_threads)
+    return logits, None
+
+
+def gpt2_sample(logits, temperature, top_k, rep_penalty, recent, u):
+    """gpt2_server.c:2862-3013 (top-p off, no filter) on a copy: (token,
+    info, penalised logits)."""
+    lg = np.ascontiguousarray(logits, np.float32).copy()
+    rec = None if recent is None or len(recent) == 0 else np.ascontiguousarray(recent, np.int32)
+    info = SampleInfo()
+    tok = port().orc_gpt2_sample(lg, lg.size, np.float32(temperature), int(top_k),
+                                 np.float32(rep_penalty), _ptr(rec),
+                                 0 if rec is None else rec.size, np.float32(u), C.byref(info))
+    return tok, info, lg
+
+
+class Gpt2PortLoop:
+    """The restated GPT-2 server tail of one stream: LM head with re-score,
+    sampler, then the recent-token ring (gpt2_server.c:3347-3348 as a FIFO of
+    hist_cap)."""
+
+    def __init__(self, wq, sw, hist0, hist_cap, temperature, top_k, rep_penalty):
+        self.wq = np.ascontiguousarray(wq, np.int8)
+        self.sw = np.ascontiguousarray(sw, np.float32)
+        self.cap = max(1, hist_cap)
+        self.rec = np.zeros(self.cap, np.int32)
+        self.rec[:len(hist0)] = hist0
+        self.n = C.c_int(len(hist0))
+        self.T, self.k, self.p = temperature, top_k, rep_penalty
+        self.logits = None
+        self.kept = None
+
+    def step(self, x, u):
+        logits, self.kept = gpt2_lm_head(x, self.wq, self.sw)
+        tok, info, self.logits = gpt2_sample(logits, self.T, self.k, self.p,
+                                             self.rec[:self.n.value], u)
+        port().orc_recent_push(self.rec, C.byref(self.n), self.cap, int(tok))
+        return tok, info
+
+    def history(self):
+        return self.rec[:self.n.value].copy()
 
 
 def _ptr(a):

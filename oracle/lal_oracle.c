@@ -350,3 +350,178 @@ int orc_tail_step(const float *hidden, int n_embd, const int8_t *wte_q,
     if (!logits_out) free(logits);
     return tok;
 }
+
+
+/* ------------------------------------------------------------------ *
+ * The GPT-2 server's LM-head tail (tools/server/gpt2_server.c)       *
+ * ------------------------------------------------------------------ */
+
+/* gpt2_server.c:1982-1998: max |x| kept with '>', scale = max/127 floored at
+ * 1e-8, inv = 1/scale, (int)(x*inv) truncated and clamped to +-127 ((int)NaN
+ * is the x86 integer indefinite: -127 after the clamp). */
+float orc_gpt2_quantize_x(const float *x, int8_t *xq, int n) {
+    float max_abs = 0.0f;
+    for (int i = 0; i < n; i++) {
+        const float a = fabsf(x[i]);
+        if (a > max_abs) max_abs = a;
+    }
+    float scale = max_abs / 127.0f;
+    if (scale < 1e-8f) scale = 1e-8f;
+    const float inv = 1.0f / scale;
+    for (int i = 0; i < n; i++) {
+        const float s = x[i] * inv;
+        int v = (s != s || s >= 2147483648.0f || s < -2147483648.0f) ? INT32_MIN : (int)s;
+        if (v > 127) v = 127;
+        if (v < -127) v = -127;
+        xq[i] = (int8_t)v;
+    }
+    return scale;
+}
+
+#define ORC_GPT2_RERANK_N 512
+
+/* gpt2_server.c:2125-2214.  Pass 1 (:2013-2095): exact int32 dots, logits =
+ * scale_x * scale_w[v] * (float)dot left to right.  Pass 2 (:2160-2197): a
+ * min-heap of RERANK_N (value, row) entries over v = 0..V-1: the first N are
+ * pushed with sift-up (stop when parent <= child); later rows replace the
+ * root only when strictly greater, then sift down to the strictly smaller
+ * child (left first).  Re-score (:2203-2211): w_row[i] = (float)wq[i] *
+ * scale_w[v]; eight lane sums of fused multiply-adds x[i] * w_row[i], lane j
+ * over i = j (mod 8) in index order; v8f_hsum (:110-113) adds the lanes left
+ * to right. */
+int orc_gpt2_lm_head(float *logits, const float *x, const int8_t *wte_q, const float *scale_w,
+                     int vocab_size, int n, int *kept) {
+    int8_t *xq = (int8_t *)malloc((size_t)n);
+    const float sx = orc_gpt2_quantize_x(x, xq, n);
+    for (int v = 0; v < vocab_size; v++) {
+        const int8_t *w = wte_q + (size_t)v * n;
+        int32_t dot = 0;
+        for (int i = 0; i < n; i++) dot += (int32_t)xq[i] * (int32_t)w[i];
+        logits[v] = sx * scale_w[v] * (float)dot;
+    }
+    free(xq);
+    static int heap_idx[ORC_GPT2_RERANK_N];
+    static float heap_val[ORC_GPT2_RERANK_N];
+    int heap_n = 0;
+    for (int v = 0; v < vocab_size; v++) {
+        const float val = logits[v];
+        if (heap_n < ORC_GPT2_RERANK_N) {
+            int c = heap_n++;
+            heap_val[c] = val;
+            heap_idx[c] = v;
+            while (c > 0) {
+                const int p = (c - 1) >> 1;
+                if (heap_val[p] <= heap_val[c]) break;
+                float tv = heap_val[p]; heap_val[p] = heap_val[c]; heap_val[c] = tv;
+                int ti = heap_idx[p]; heap_idx[p] = heap_idx[c]; heap_idx[c] = ti;
+                c = p;
+            }
+        } else if (val > heap_val[0]) {
+            heap_val[0] = val;
+            heap_idx[0] = v;
+            int p = 0;
+            for (;;) {
+                const int l = 2 * p + 1, r = 2 * p + 2;
+                int s = p;
+                if (l < heap_n && heap_val[l] < heap_val[s]) s = l;
+                if (r < heap_n && heap_val[r] < heap_val[s]) s = r;
+                if (s == p) break;
+                float tv = heap_val[p]; heap_val[p] = heap_val[s]; heap_val[s] = tv;
+                int ti = heap_idx[p]; heap_idx[p] = heap_idx[s]; heap_idx[s] = ti;
+                p = s;
+            }
+        }
+    }
+    for (int k = 0; k < heap_n; k++) {
+        const int v = heap_idx[k];
+        const int8_t *wq = wte_q + (size_t)v * n;
+        const float scale = scale_w[v];
+        float lane[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        for (int i = 0; i + 8 <= n; i += 8)
+            for (int j = 0; j < 8; j++) lane[j] = fmaf(x[i + j], (float)wq[i + j] * scale, lane[j]);
+        float s = lane[0];
+        for (int j = 1; j < 8; j++) s = s + lane[j];
+        logits[v] = s;
+        if (kept) kept[k] = v;
+    }
+    return heap_n;
+}
+
+/* gpt2_server.c:2862-3013 with g_top_p = 0 (its default, :2343) and the
+ * weak no-op filter (the keep mask unchanged).  Sampling branch
+ * (temperature > 0 and top_k > 0): the penalty per recent occurrence in order
+ * (l > 0 ? l /= p : l *= p) when p > 1; k = min(top_k, V); k passes of
+ * find-max (strict '>', lowest row) and mask with -1e30f leave threshold =
+ * the k-th largest logit with multiplicity; keep = {l >= threshold};
+ * actual_max over the kept rows with '>' from -1e30f; sum_exp +=
+ * expf((l - actual_max) / T) for kept rows in ascending order (the others add
+ * 0.0f, which leaves the sum unchanged); r = u * sum_exp; the running sum
+ * walks every row (zeros below the threshold) and returns the first row
+ * where it reaches r, else V-1.  Otherwise argmax (strict '>', lowest row),
+ * no penalty. */
+int orc_gpt2_sample(float *logits, int vocab_size, float temperature, int top_k,
+                    float rep_penalty, const int *recent, int n_recent, float u,
+                    orc_sample_info *info) {
+    orc_sample_info loc;
+    if (!info) info = &loc;
+    memset(info, 0, sizeof(*info));
+    if (temperature > 0.0f && top_k > 0) {
+        if (rep_penalty > 1.0f)
+            for (int i = 0; i < n_recent; i++) {
+                const int t = recent[i];
+                if (t >= 0 && t < vocab_size) {
+                    if (logits[t] > 0) logits[t] /= rep_penalty;
+                    else logits[t] *= rep_penalty;
+                }
+            }
+        int k = top_k > vocab_size ? vocab_size : top_k;
+        float *copy = (float *)malloc(sizeof(float) * (size_t)vocab_size);
+        memcpy(copy, logits, sizeof(float) * (size_t)vocab_size);
+        float threshold = -1e30f;
+        for (int sel = 0; sel < k; sel++) {
+            int max_v = 0;
+            float max_val = copy[0];
+            for (int v = 1; v < vocab_size; v++)
+                if (copy[v] > max_val) { max_val = copy[v]; max_v = v; }
+            threshold = max_val;
+            copy[max_v] = -1e30f;
+        }
+        float actual_max = -1e30f;
+        int n_cand = 0;
+        for (int v = 0; v < vocab_size; v++)
+            if (logits[v] >= threshold) {
+                n_cand++;
+                if (logits[v] > actual_max) actual_max = logits[v];
+            }
+        float sum_exp = 0.0f;
+        for (int v = 0; v < vocab_size; v++) {
+            if (logits[v] >= threshold) {
+                copy[v] = expf((logits[v] - actual_max) / temperature);
+                sum_exp += copy[v];
+            } else {
+                copy[v] = 0.0f;
+            }
+        }
+        const float r = u * sum_exp;
+        info->threshold = threshold;
+        info->max_l = actual_max;
+        info->sum = sum_exp;
+        info->r = r;
+        info->n_cand = n_cand;
+        info->drew = 1;
+        float cum = 0.0f;
+        int tok = vocab_size - 1;
+        for (int v = 0; v < vocab_size; v++) {
+            cum += copy[v];
+            if (cum >= r) { tok = v; break; }
+        }
+        free(copy);
+        return tok;
+    }
+    info->greedy = 1;
+    int best = 0;
+    float best_val = logits[0];
+    for (int v = 1; v < vocab_size; v++)
+        if (logits[v] > best_val) { best_val = logits[v]; best = v; }
+    return best;
+}

@@ -34,6 +34,20 @@ typedef struct {
 /* runtime/lal_simd_optim.h:32-58 (AVX2+FMA build): the final RMSNorm,
  * tools/server/qwen7b_server.c:820; n a multiple of 8. */
 void  orc_rms_norm(float *out, const float *x, const float *w, int n, float eps);
+/* tools/server/gpt2_server.c:1982-1998: the GPT-2 server's quantizer
+ * (truncation for every element). */
+float orc_gpt2_quantize_x(const float *x, int8_t *xq, int n);
+/* gpt2_server.c:2125-2214 (AVX2 build, n a multiple of 8): int8 logits of all
+ * V rows, then the rows its 512-entry min-heap keeps re-scored in float.
+ * kept (may be NULL) receives the kept rows in heap order; returns their
+ * count. */
+int   orc_gpt2_lm_head(float *logits, const float *x, const int8_t *wte_q,
+                       const float *scale_w, int vocab_size, int n, int *kept);
+/* gpt2_server.c:2862-3013 with top-p off and no filter: returns the token;
+ * u = (float)(rand() % 1000000) / 1000000.0f. */
+int   orc_gpt2_sample(float *logits, int vocab_size, float temperature, int top_k,
+                      float rep_penalty, const int *recent, int n_recent, float u,
+                      orc_sample_info *info);
 /* runtime/lal_q8_kernel.h:375-424 (AVX2+FMA build, the one the servers use). */
 float orc_quantize_x_int8(const float *x, int8_t *xq, int n);
 /* runtime/lal_q8_kernel.h:450-460 */

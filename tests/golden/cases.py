@@ -57,6 +57,30 @@ def rms_norm_inputs():
     return out
 
 
+def gpt2_lm_inputs():
+    """(name, q, s, x) for the GPT-2 server's LM head (V=50257, d=768, the
+    sizes its source fixes): the synthetic C1 head, and the same head with the
+    row at place 505 copied over 20 rows ranked below it, so that 21 rows tie
+    at the 512th largest logit and the server's heap history decides which 8
+    of them it re-scores."""
+    import oracle
+    from lal_b200 import synth
+    cfg = synth.CONFIGS["c1_gpt2"]
+    q, s = oracle.quantize_rows(synth.lm_head_f32(cfg), "port")
+    x = synth.hidden(cfg, 3)[0]
+    out = [("plain", q, s, x)]
+    sx, xq = oracle.gpt2_quantize_x(x, "port")
+    lg = (sx * s) * (q.astype(np.int32) @ xq.astype(np.int32)).astype(np.float32)
+    order = np.argsort(-lg, kind="stable")
+    src = order[504]
+    q2, s2 = q.copy(), s.copy()
+    for r in order[600:620]:
+        q2[r] = q[src]
+        s2[r] = s[src]
+    out.append(("boundary_ties", q2, s2, x))
+    return out
+
+
 def lm_head_inputs():
     """(W fp32 [V,d], x fp32 [d], [(v0, v1), ...]) for the LM-head kernels."""
     out = []

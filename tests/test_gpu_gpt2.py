@@ -1,0 +1,102 @@
+"""GPU parity of the GPT-2 server's tail as a second drop-in (a context with
+LAL_SAMPLER_GPT2; tools/server/gpt2_server.c:1982-2214 and 2862-3013):
+tokens, diagnostics, the re-scored and penalised logits and the history,
+bit for bit against the oracle's restatement (whose LM head is pinned to the
+server's own compiled code by tests/test_oracle.py)."""
+import numpy as np
+import pytest
+
+import cases
+import lal_b200 as L
+import oracle
+from conftest import bits
+from lal_b200 import synth
+
+pytestmark = pytest.mark.gpu
+
+
+def gpt2_tail(q, s, cfg, max_top_k=40):
+    t = L.DecodeTail(cfg.vocab, cfg.n_embd, max_top_k=max_top_k, history_cap=cfg.hist,
+                     sampler=L.LAL_SAMPLER_GPT2)
+    t.load_lm_head_q8(q, s)
+    return t
+
+
+def draws(n, seed):
+    """(rand() % 1000000) / 1e6, as the server draws; one exact zero."""
+    g = np.random.default_rng(seed)
+    u = (g.integers(0, 1000000, n) / np.float32(1e6)).astype(np.float32)
+    u[min(3, n - 1)] = 0.0
+    return u
+
+
+def test_gpt2_decode_loop_matches_oracle():
+    cfg = synth.CONFIGS["c1_gpt2"]
+    W = synth.lm_head_f32(cfg)
+    q, s = oracle.quantize_rows(W, "port")
+    hist0 = synth.history(cfg, 0)
+    t = gpt2_tail(q, s, cfg)
+    t.set_sampling([cfg.temperature], [cfg.top_k], [cfg.rep_penalty])
+    t.set_history(0, hist0)
+    port = oracle.Gpt2PortLoop(q, s, hist0, cfg.hist, cfg.temperature, cfg.top_k,
+                               cfg.rep_penalty)
+    us = draws(16, 4)
+    for step in range(16):
+        x = synth.hidden(cfg, step)
+        tok = int(t.step(x, us[step:step + 1])[0])
+        ptok, info = port.step(x[0], us[step])
+        assert tok == ptok, step
+        d = t.diag(0)
+        assert bits(d["sum"]) == bits(info.sum) and d["n_cand"] == info.n_cand, step
+        assert bits(d["threshold"]) == bits(info.threshold)
+        np.testing.assert_array_equal(bits(t.logits(0)), bits(port.logits))
+    np.testing.assert_array_equal(t.get_history(0), port.history())
+    # greedy: argmax of the re-scored logits, no penalty
+    t.set_sampling([0.0], [cfg.top_k], [cfg.rep_penalty])
+    port.T = 0.0
+    for step in range(3):
+        x = synth.hidden(cfg, 100 + step)
+        tok = int(t.step(x, np.zeros(1, np.float32))[0])
+        ptok, _ = port.step(x[0], 0.0)
+        assert tok == ptok
+        np.testing.assert_array_equal(bits(t.logits(0)), bits(port.logits))
+    t.close()
+
+
+def test_gpt2_boundary_ties_replay_the_heap():
+    """21 rows tie at the 512th largest int8 logit: the kernel replays the
+    server's heap to re-score the same 8 of them."""
+    cfg = synth.CONFIGS["c1_gpt2"].with_(hist=8)
+    for name, q, s, x in cases.gpt2_lm_inputs():
+        t = gpt2_tail(q, s, cfg, max_top_k=50)
+        t.set_sampling([0.9], [50], [1.0])
+        t.set_history(0, np.zeros(0, np.int32))
+        port = oracle.Gpt2PortLoop(q, s, [], cfg.hist, 0.9, 50, 1.0)
+        tok = int(t.step(x[None, :], np.array([0.25], np.float32))[0])
+        ptok, _ = port.step(x, np.float32(0.25))
+        assert tok == ptok, name
+        np.testing.assert_array_equal(bits(t.logits(0)), bits(port.logits), err_msg=name)
+        t.close()
+
+
+def test_gpt2_small_vocab_rescore_all_rows():
+    """Fewer rows than the re-score window: every row is re-scored."""
+    cfg = synth.CONFIGS["c1_gpt2"].with_(vocab=300, hist=16)
+    rng = np.random.default_rng(9)
+    W = (rng.standard_normal((cfg.vocab, cfg.n_embd)) * 0.02).astype(np.float32)
+    q, s = oracle.quantize_rows(W, "port")
+    t = gpt2_tail(q, s, cfg)
+    t.set_sampling([0.8], [40], [1.1])
+    hist0 = rng.integers(0, cfg.vocab, 16).astype(np.int32)
+    t.set_history(0, hist0)
+    port = oracle.Gpt2PortLoop(q, s, hist0, cfg.hist, 0.8, 40, 1.1)
+    for step, u in enumerate(draws(6, 2)):
+        x = rng.standard_normal((1, cfg.n_embd)).astype(np.float32)
+        assert int(t.step(x, np.array([u], np.float32))[0]) == port.step(x[0], u)[0], step
+        np.testing.assert_array_equal(bits(t.logits(0)), bits(port.logits))
+    t.close()
+
+
+def test_gpt2_context_limits():
+    with pytest.raises(L.LalTailError):
+        L.DecodeTail(1000, 100, max_top_k=8, history_cap=8, sampler=L.LAL_SAMPLER_GPT2)

@@ -160,3 +160,62 @@ def test_rms_norm_port_matches_reference_on_random_vectors():
         w = (1 + 0.2 * g.standard_normal(n)).astype(np.float32)
         np.testing.assert_array_equal(bits(oracle.rms_norm(x, w, 1e-6, "port")),
                                       bits(oracle.rms_norm(x, w, 1e-6, "ref")))
+
+
+def test_gpt2_lm_head_matches_golden(golden, golden_meta):
+    """The GPT-2 server's int8 LM head and float re-score: every logit, and
+    which rows the heap re-scored -- including 21 rows tied at the 512th
+    place, of which the server's heap history keeps 8."""
+    for name, q, s, x in cases.gpt2_lm_inputs():
+        assert h(q) + h(s) + h(x) == golden_meta["hashes"][f"g2_{name}_in"]
+        sx, xq = oracle.gpt2_quantize_x(x, "port")
+        assert bits(sx) == bits(golden[f"g2_{name}_sx"])
+        np.testing.assert_array_equal(xq, golden[f"g2_{name}_xq"])
+        logits, kept = oracle.gpt2_lm_head(x, q, s, "port")
+        assert h(logits) == golden_meta["hashes"][f"g2_{name}_logits"], name
+        rows = golden[f"g2_{name}_rescored_rows"]
+        assert set(rows.tolist()) <= set(kept.tolist())
+        np.testing.assert_array_equal(bits(logits[rows]), bits(golden[f"g2_{name}_rescored_vals"]))
+
+
+@pytest.mark.skipif(not oracle.have_ref_gpt2(), reason="oracle/_ref not built")
+def test_gpt2_quantizer_matches_reference_on_random_vectors():
+    g = np.random.default_rng(17)
+    for trial in range(50):
+        x = (g.standard_normal(768) * g.uniform(1e-9, 30)).astype(np.float32)
+        if trial % 5 == 0:
+            x[g.integers(768)] = np.nan
+        sp, qp = oracle.gpt2_quantize_x(x, "port")
+        sr, qr = oracle.gpt2_quantize_x(x, "ref")
+        assert bits(sp) == bits(sr)
+        np.testing.assert_array_equal(qp, qr)
+
+
+def test_gpt2_sampler_is_the_library_sampler_but_at_r_zero():
+    """gpt2_server.c:2862-3013 restated: its k passes of find-max-and-mask and
+    its kept-row softmax give the library sampler's token (pinned against the
+    reference above) for every draw but r == 0, where its running sum stops
+    at row 0."""
+    g = np.random.default_rng(8)
+    for trial in range(60):
+        V = int(g.integers(50, 3000))
+        logits = (g.standard_normal(V) * 3).astype(np.float32)
+        if trial % 4 == 0:
+            logits[g.integers(V, size=V // 5)] = logits[0]   # ties
+        T = float(g.choice([0.0, 0.7, 1.3]))
+        k = int(g.choice([0, 1, 5, 40, 64]))
+        rec = g.integers(0, V, size=int(g.integers(0, 30))).astype(np.int32)
+        u = np.float32(g.integers(0, 1000000) / 1e6)
+        tg, ig, lg = oracle.gpt2_sample(logits, T, k, 1.1, rec, u)
+        tl, ll, il = oracle.sample(logits, T, k, 1.1, rec, u)
+        if not ig.greedy and ig.r == 0.0:
+            assert tg == 0
+        else:
+            assert tg == tl, trial
+        np.testing.assert_array_equal(bits(lg), bits(ll))
+        if not ig.greedy:
+            assert bits(ig.sum) == bits(il.sum) and ig.n_cand == il.n_cand
+    # a zero draw
+    lg = np.array([1.0, 5.0, 4.0, -2.0], np.float32)
+    assert oracle.gpt2_sample(lg, 0.8, 2, 1.0, None, 0.0)[0] == 0
+    assert oracle.sample(lg, 0.8, 2, 1.0, None, 0.0)[0] == 1
