@@ -53,6 +53,7 @@ constexpr int kMmaK = 32;          /* K of one tcgen05.mma kind::i8            *
 constexpr int kGemmThreads = 192;  /* warp 0 TMA, warp 1 MMA, warps 2-5 epilogue */
 constexpr int kGemmStagesMax = 8;
 constexpr int kGemmSmemLimit = 232448;
+constexpr int kStageGroups = 512;  /* 32-row logit groups staged a round (select) */
 
 /* ------------------------------------------------------------ PTX --- */
 __device__ __forceinline__ uint64_t policy_evict_last() {
@@ -373,6 +374,14 @@ struct BatchSelectParams {
 
 constexpr uint32_t kEmptySlot = 0xFFFFFFFFu;
 
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
 __global__ void __launch_bounds__(NT, 1) batch_select_kernel(const __grid_constant__ BatchSelectParams p) {
     extern __shared__ __align__(16) uint8_t bsm[];
     __shared__ Misc msh;
@@ -390,6 +399,9 @@ __global__ void __launch_bounds__(NT, 1) batch_select_kernel(const __grid_consta
     uint32_t *hkey = reinterpret_cast<uint32_t *>(Ce + p.c_cap);   /* history hash     */
     uint32_t *hcnt = hkey + p.h_slots;
     int *Gl = reinterpret_cast<int *>(hcnt + p.h_slots);           /* candidate groups */
+    /* staging of kStageGroups candidate groups' 32 logits (16-byte aligned) */
+    float *Gv = reinterpret_cast<float *>(
+        (reinterpret_cast<uintptr_t>(Gl + p.n_groups) + 15) & ~static_cast<uintptr_t>(15));
 
     float *lg = p.logits + (size_t)b * p.rows;
     const float temp = p.temperature[b];
@@ -401,6 +413,21 @@ __global__ void __launch_bounds__(NT, 1) batch_select_kernel(const __grid_consta
     const int hhead = p.hist_head ? p.hist_head[b] : 0;
     const bool greedy = (temp <= 0.0f) || (topk <= 0);
     const bool use_pen = pen > 1.0f && hn > 0 && (p.variant == VARIANT_SERVER || !greedy);
+
+    /* this stream's group maxima, loaded now so that their latency overlaps
+     * the penalty (one batch when the slice has at most NT * kGroupRegs
+     * groups) */
+    constexpr int kGroupRegs = 24;
+    uint32_t gpre[kGroupRegs];
+    const bool gpre_ok = p.gmax != nullptr && p.n_groups <= NT * kGroupRegs;
+    if (gpre_ok) {
+        const uint32_t *gm = p.gmax + (size_t)b * p.n_groups;
+#pragma unroll
+        for (int j = 0; j < kGroupRegs; ++j) {
+            const int g = j * NT + tid;
+            gpre[j] = g < p.n_groups ? __ldg(gm + g) : 0u;
+        }
+    }
 
     /* 1. repetition penalty: occurrences of each history id in this slice,
      * counted in an open-addressing hash, applied once per occurrence
@@ -497,6 +524,14 @@ __global__ void __launch_bounds__(NT, 1) batch_select_kernel(const __grid_consta
          * (k+P)-th largest maximum is <= that maximum, hence a bound of T */
         uint32_t *Gk = Sk; /* the group maxima, then the superset */
         const uint32_t *gm = p.gmax + (size_t)b * p.n_groups;
+        if (gpre_ok) {
+#pragma unroll
+            for (int j = 0; j < kGroupRegs; ++j) {
+                const int g = j * NT + tid;
+                if (g < p.n_groups) Gk[g] = gpre[j];
+                hist_add(hist, gpre[j] >> 20, g < p.n_groups);
+            }
+        } else
         for (int g0 = 0; g0 < p.n_groups; g0 += NT * U) {
             uint32_t v[U];
 #pragma unroll
@@ -518,41 +553,68 @@ __global__ void __launch_bounds__(NT, 1) batch_select_kernel(const __grid_consta
         /* the candidate groups, listed in Gl */
         if (tid == 0) s_count = 0;
         __syncthreads();
-        for (int g = tid; g < p.n_groups; g += NT)
-            if (Gk[g] >= L) Gl[atomicAdd(&s_count, 1)] = g;
+        /* one shared-memory atomic per warp and round */
+        for (int g0 = 0; g0 < p.n_groups; g0 += NT) {
+            const int g = g0 + tid;
+            const bool hit = g < p.n_groups && Gk[g] >= L;
+            const unsigned bal = __ballot_sync(0xffffffffu, hit);
+            if (bal) {
+                const int lane = tid & 31;
+                int base = 0;
+                if (lane == 0) base = atomicAdd(&s_count, __popc(bal));
+                base = __shfl_sync(0xffffffffu, base, 0);
+                if (hit) Gl[base + __popc(bal & ((1u << lane) - 1u))] = g;
+            }
+        }
         __syncthreads();
         const int ng = s_count;
         __syncthreads();
         if (ng <= p.n_groups / 4) {
             if (tid == 0) s_count = 0;
-            __syncthreads();
-            /* gather the groups' keys >= L (32 consecutive rows a group) */
-            const int total = ng * 32;
-            for (int i0 = 0; i0 < total; i0 += NT * U) {
-                float v[U];
-                int rr[U];
+            /* gather the groups' keys >= L (32 consecutive rows a group):
+             * each round copies up to kStageGroups groups into shared memory
+             * with 16-byte asynchronous copies, all in flight together (a
+             * piece that is misaligned or crosses the slice end is read one
+             * value at a time), then a warp takes a group a ballot */
+            const bool al16 = (reinterpret_cast<uintptr_t>(lg) & 15u) == 0;
+            for (int c0 = 0; c0 < ng; c0 += kStageGroups) {
+                const int cn = min(kStageGroups, ng - c0);
+                __syncthreads(); /* the previous round's staging is consumed */
+                for (int e = tid; e < cn * 8; e += NT) {
+                    const int r = Gl[c0 + (e >> 3)] * 32 + (e & 7) * 4;
+                    float *dst = Gv + (size_t)(e >> 3) * 32 + (e & 7) * 4;
+                    if (al16 && r + 4 <= p.rows) {
+                        cp_async16(dst, lg + r);
+                    } else {
 #pragma unroll
-                for (int j = 0; j < U; ++j) {
-                    const int e = i0 + j * NT + tid;
-                    rr[j] = e < total ? Gl[e >> 5] * 32 + (e & 31) : p.rows;
-                    v[j] = rr[j] < p.rows ? lg[rr[j]] : 0.0f;
-                }
-#pragma unroll
-                for (int j = 0; j < U; ++j) {
-                    const uint32_t key = f2key(v[j]);
-                    const bool take = rr[j] < p.rows && key >= L;
-                    const unsigned bal = __ballot_sync(0xffffffffu, take);
-                    int base = 0;
-                    if ((tid & 31) == 0 && bal) base = atomicAdd(&s_count, __popc(bal));
-                    base = __shfl_sync(0xffffffffu, base, 0);
-                    if (take) {
-                        const int pos = base + __popc(bal & ((1u << (tid & 31)) - 1u));
-                        if (pos < p.s_cap) {
-                            Sk[pos] = key;
-                            Si[pos] = rr[j];
-                        }
+                        for (int q = 0; q < 4; ++q) dst[q] = r + q < p.rows ? lg[r + q] : 0.0f;
                     }
                 }
+                cp_async_wait_all();
+                __syncthreads();
+                /* a thread a contiguous run of the staged values: count, one
+                 * scan, write (no atomics on the way) */
+                const int tot = cn * 32;
+                const int per = (tot + NT - 1) / NT;
+                const int e0 = min(tot, tid * per), e1 = min(tot, e0 + per);
+                uint32_t c = 0;
+                for (int e = e0; e < e1; ++e)
+                    c += (Gl[c0 + (e >> 5)] * 32 + (e & 31) < p.rows) && f2key(Gv[e]) >= L;
+                uint32_t got;
+                uint32_t pos = block_scan_excl(c, ms, &got) + (uint32_t)s_count;
+                for (int e = e0; e < e1; ++e) {
+                    const int r = Gl[c0 + (e >> 5)] * 32 + (e & 31);
+                    const uint32_t key = f2key(Gv[e]);
+                    if (r < p.rows && key >= L) {
+                        if (pos < (uint32_t)p.s_cap) {
+                            Sk[pos] = key;
+                            Si[pos] = r;
+                        }
+                        ++pos;
+                    }
+                }
+                __syncthreads(); /* every thread read s_count before it moves */
+                if (tid == 0) s_count += (int)got;
             }
             __syncthreads();
             S = s_count;
@@ -650,20 +712,26 @@ __global__ void __launch_bounds__(NT, 1) batch_select_kernel(const __grid_consta
     /* 4. T exactly: the k-th largest key of the superset (counting for a
      * small superset: T = min{ key : #{keys > key} < k }) */
     uint32_t T;
-    if (S <= 2 * NT) {
+    if (S <= 128) {
+        /* pad to a multiple of 4 with zero keys (never greater) and count with
+         * 16-byte reads, two keys a thread in one pass */
+        const int S4 = (S + 3) & ~3;
+        if (tid < S4 - S) Sk[S + tid] = 0u;
+        __syncthreads();
         uint32_t best = 0xffffffffu;
         const int kk = min(k, S);
-#pragma unroll
-        for (int r = 0; r < 2; ++r) {
-            const int e = tid + r * NT;
-            if (e < S) {
-                const uint32_t me = Sk[e];
-                int gt = 0;
+        const uint32_t me0 = tid < S ? Sk[tid] : 0u;
+        const uint32_t me1 = tid + NT < S ? Sk[tid + NT] : 0u;
+        int g0 = 0, g1 = 0;
+        const uint4 *K4 = reinterpret_cast<const uint4 *>(Sk);
 #pragma unroll 4
-                for (int j = 0; j < S; ++j) gt += Sk[j] > me;
-                if (gt < kk) best = min(best, me);
-            }
+        for (int j = 0; j < S4 / 4; ++j) {
+            const uint4 v = K4[j];
+            g0 += (v.x > me0) + (v.y > me0) + (v.z > me0) + (v.w > me0);
+            g1 += (v.x > me1) + (v.y > me1) + (v.z > me1) + (v.w > me1);
         }
+        if (tid < S && g0 < kk) best = me0;
+        if (tid + NT < S && g1 < kk) best = min(best, me1);
         best = __reduce_min_sync(0xffffffffu, best);
         if ((tid & 31) == 0) ms->scan[tid >> 5] = best;
         __syncthreads();
@@ -864,7 +932,8 @@ bool encode_i8(CUtensorMap *m, const void *base, int dim0, int dim1, int pitch, 
 int batch_n_for(int B) { return (B + 31) / 32 * 32; }
 
 size_t batch_select_smem(int s_cap, int c_cap, int h_slots, int n_groups) {
-    return 4ull * 4096 + 8ull * s_cap + 24ull * c_cap + 8ull * h_slots + 4ull * n_groups;
+    const size_t fixed = 4ull * 4096 + 8ull * s_cap + 24ull * c_cap + 8ull * h_slots + 4ull * n_groups;
+    return (fixed + 15) / 16 * 16 + 128ull * kStageGroups;
 }
 
 int batch_plan(BatchPlan &bp, const int8_t *W, const float *scale_w, int rows, int ld,
