@@ -51,6 +51,9 @@ def parse():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--config", default="c2_qwen", choices=sorted(synth.CONFIGS))
+    ap.add_argument("--sampler", default="library", choices=["library", "server", "gpt2"],
+                    help="the fused context's sampler: lal_sampling.h (default), the "
+                         "Qwen server's, or the GPT-2 server's tail (one GPU)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
                     help="bound of the CPU-baseline sample")
@@ -169,7 +172,41 @@ def quantized_lm_head_host(cfg, rows=None):
     return q, s
 
 
-def cpu_tail(cfg, q, s, steps, threads, seconds):
+def cpu_tail_gpt2(cfg, q, s, steps, threads, seconds):
+    """Time the GPT-2 server's tail on the host: its own lm_head_int8_parallel
+    (oracle/_ref, the int8 logits and the float re-score; the server caps its
+    threads at 8) and the restated sampler with the recent-token ring.  The
+    server's sampler sits inside its forward function, so the sampler is
+    always the restatement ('reference' names the LM head's origin)."""
+    import oracle
+    V, d = cfg.vocab, cfg.n_embd
+    ref = oracle.have_ref_gpt2() and (V, d) == (50257, 768)
+    g = np.random.default_rng(cfg.seed)
+    loops = [oracle.Gpt2PortLoop(q, s, synth.history(cfg, b), max(1, cfg.hist),
+                                 float(synth.temperatures(cfg)[b]), cfg.top_k, cfg.rep_penalty)
+             for b in range(cfg.streams)]
+    nt = min(8, threads)
+    done, t_tot = 0, 0.0
+    for step in range(steps):
+        hid = synth.hidden(cfg, step)
+        t0 = time.perf_counter()
+        for b, lp in enumerate(loops):
+            u = np.float32(g.integers(0, 1000000) / 1e6)
+            if ref:
+                logits, _ = oracle.gpt2_lm_head(hid[b], q, s, "ref", n_threads=nt)
+                tok, _, lp.logits = oracle.gpt2_sample(logits, lp.T, lp.k, lp.p,
+                                                       lp.rec[:lp.n.value], u)
+                oracle.port().orc_recent_push(lp.rec, oracle.C.byref(lp.n), lp.cap, int(tok))
+            else:
+                lp.step(hid[b], u)
+        t_tot += time.perf_counter() - t0
+        done += 1
+        if t_tot > seconds:
+            break
+    return cfg.streams * done / t_tot, "reference" if ref else "port", done, nt if ref else 1
+
+
+def cpu_tail(cfg, q, s, steps, threads, seconds, sampler="library"):
     """Time the reference's decode tail (qwen7b_server.c:829-850) on the host:
     oracle/_ref when built ('reference'), else the C restatement ('port').
     Runs at most `steps` steps or `seconds` of work per stream.  Returns
@@ -177,6 +214,8 @@ def cpu_tail(cfg, q, s, steps, threads, seconds):
     import ctypes as C
 
     import oracle
+    if sampler == "gpt2":
+        return cpu_tail_gpt2(cfg, q, s, steps, threads, seconds)
     B = cfg.streams
     V, d = cfg.vocab, cfg.n_embd
     # lal_sample_token's heap holds 64 (lal_sampling.h:74): larger k runs on
@@ -230,18 +269,23 @@ def run_reference_arm(args, cfg):
     q, s = quantized_lm_head_host(cfg)
     # warm-up, then the timed steps (each a full step of the workload; bounded
     # by --cpu-seconds of host time)
-    cpu_tail(cfg, q, s, max(1, min(args.warmup, 2)), threads, 5.0)
-    val, kind, done, cores = cpu_tail(cfg, q, s, args.steps, threads, args.cpu_seconds * 2)
+    cpu_tail(cfg, q, s, max(1, min(args.warmup, 2)), threads, 5.0, args.sampler)
+    val, kind, done, cores = cpu_tail(cfg, q, s, args.steps, threads, args.cpu_seconds * 2,
+                                      args.sampler)
     line = {
         "impl": "reference", "metric": METRIC, "value": round(val, 3), "unit": "tokens/s",
         "n_gpus": args.gpus, "steps": done, "warmup": args.warmup,
         "ms_per_step": round(1000.0 * cfg.streams / val, 4), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-        "config": workload(cfg, args.gpus),
+        "config": {**workload(cfg, args.gpus),
+                   **({"sampler": args.sampler} if args.sampler != "library" else {})},
         "cpu_baseline": {"value": round(val, 3), "unit": "tokens/s", "cores": cores,
                          "kind": kind,
                          "sample": f"{done} full decode-tail steps of {cfg.name} "
-                                   f"(reference tail sequence of qwen7b_server.c:829-850)"},
+                                   + ("(gpt2_server.c's lm_head_int8_parallel and the "
+                                      "restated sampler of :2862-3013)"
+                                      if args.sampler == "gpt2" else
+                                      "(reference tail sequence of qwen7b_server.c:829-850)")},
         "e2e": {"value": round(val, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -287,15 +331,19 @@ def run_ours(args, cfg):
                                 device_id=torch.device("cuda", local))
     B = cfg.streams
     K, W = args.steps, args.warmup
+    sampler = {"library": L.LAL_SAMPLER_LIBRARY, "server": L.LAL_SAMPLER_SERVER,
+               "gpt2": L.LAL_SAMPLER_GPT2}[args.sampler]
+    if args.sampler == "gpt2" and world > 1:
+        raise SystemExit("--sampler gpt2 runs on one GPU (the GPT-2 tail has no sharded step)")
     if world > 1:
         from lal_b200.sharded import ShardedDecodeTail
         # vocab slice per rank; records all-gathered over NCCL each step
         t = ShardedDecodeTail(cfg.vocab, cfg.n_embd, device=local, max_streams=B,
                               max_top_k=max(cfg.top_k, 1), history_cap=cfg.hist,
-                              sampler=L.LAL_SAMPLER_LIBRARY)
+                              sampler=sampler)
     else:
         t = L.DecodeTail(cfg.vocab, cfg.n_embd, max_streams=B, max_top_k=max(cfg.top_k, 1),
-                         history_cap=cfg.hist, sampler=L.LAL_SAMPLER_LIBRARY, device=local)
+                         history_cap=cfg.hist, sampler=sampler, device=local)
     # LM head slice: fp32 rows generated in blocks, quantized on the GPU
     blk = 8192
     for r in range(0, t.n_rows, blk):
@@ -406,8 +454,16 @@ def run_ours(args, cfg):
     if rank == 0:
         peaks, pk_kind = load_peaks()
         rows = t.n_rows
-        batched = B >= 2
-        if batched:
+        gpt2 = args.sampler == "gpt2"
+        batched = B >= 2 and not gpt2
+        if gpt2:
+            # the GPT-2 server's tail: quantize, LM head (the timed kernel),
+            # the 512-candidate select, the float re-score, the sampler
+            launches_per_step = 5 * B
+            alg = algorithmic_bytes(cfg, 1, rows)
+            kname = ("LM-head kernel (tail_kernel<MODE_LMHEAD>), one of the GPT-2 tail's five "
+                     "launches a step")
+        elif batched:
             # quantize + tensor-core GEMM + per-stream select: the GEMM streams
             # the slice once for all B streams (the timed kernel)
             launches_per_step = 3
@@ -430,7 +486,9 @@ def run_ours(args, cfg):
             "metric": METRIC, "value": round(tokens / (dev_ms * 1e-3), 3), "unit": "tokens/s",
             "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": round(dev_ms / K, 5),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "int8", "data": "synthetic", "config": workload(cfg, world),
+            "dtype": "int8", "data": "synthetic",
+            "config": {**workload(cfg, world),
+                       **({"sampler": args.sampler} if args.sampler != "library" else {})},
             "e2e": {"value": round(tokens / (e2e_ms * 1e-3), 3), "unit": "tokens/s",
                     "h2d_bytes_per_step": int(hid[0].nbytes + us[0].nbytes),
                     "d2h_bytes_per_step": int(4 * B + 4)},
@@ -453,7 +511,7 @@ def run_ours(args, cfg):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         q, s = t.read_lm_head()
         val, kind, done, cores = cpu_tail(cfg, q, s, 10_000, os.cpu_count() or 1,
-                                          args.cpu_seconds)
+                                          args.cpu_seconds, args.sampler)
         out["cpu_baseline"] = {"value": round(val, 3), "unit": "tokens/s", "cores": cores,
                                "kind": kind,
                                "sample": f"{done} decode-tail steps of {cfg.name} "

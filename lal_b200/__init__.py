@@ -116,7 +116,7 @@ SIGNATURES = {
     "lal_tail_set_sampling": (C.c_int, [_vp, _ip, _f32p, _i32p, _f32p]),
     "lal_tail_set_history": (C.c_int, [_vp, _ip, _vp, _ip]),
     "lal_tail_get_history": (C.c_int, [_vp, _ip, _vp, C.POINTER(C.c_int)]),
-    "lal_tail_step": (C.c_int, [_vp, _f32p, _ip, _f32p, _i32p]),
+    "lal_tail_step": (C.c_int, [_vp, _vp, _ip, _vp, _vp]),
     "lal_tail_step_device": (C.c_int, [_vp, _vp, _ip, _vp, _vp]),
     "lal_tail_sync": (C.c_int, [_vp]),
     "lal_tail_stage_inputs": (C.c_int, [_vp, _f32p, _ip, _f32p]),
@@ -329,11 +329,17 @@ class DecodeTail:
         return out[:n.value].copy()
 
     def step(self, hidden: np.ndarray, u: np.ndarray) -> np.ndarray:
+        """One decode step from host arrays (hidden [B, d] or [d], u [B])."""
         hidden = np.ascontiguousarray(hidden, np.float32)
         B = 1 if hidden.ndim == 1 else hidden.shape[0]
+        if hidden.size != B * self.cfg.n_embd:
+            raise ValueError(f"hidden: {hidden.size} values for {B} x {self.cfg.n_embd}")
         u = np.ascontiguousarray(u, np.float32).reshape(-1)
+        if u.size < B:
+            raise ValueError(f"u: {u.size} draws for {B} streams")
         tok = np.empty(B, np.int32)
-        _check(lib().lal_tail_step(self.h, hidden.reshape(-1), B, u, tok))
+        # raw pointers: the arrays are checked above, the call is per token
+        _check(lib().lal_tail_step(self.h, hidden.ctypes.data, B, u.ctypes.data, tok.ctypes.data))
         return tok
 
     def diag(self, stream: int = 0) -> dict:

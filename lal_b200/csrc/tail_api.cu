@@ -1580,6 +1580,36 @@ int lal_tail_sync(lal_tail *t) {
     return LAL_TAIL_OK;
 }
 
+}  // extern "C"
+
+namespace {
+/* The step's inputs into io_in ([B][d] hidden, then the B draws) through the
+ * pinned staging buffer: one copy when all B streams step (the two parts are
+ * then contiguous), else one for each part. */
+int upload_inputs(lal_tail *t, const float *hidden, int n, const float *u) {
+    const int B = t->cfg.max_streams, d = t->cfg.n_embd;
+    memcpy(t->h_in, hidden, 4ull * n * d);
+    memcpy(t->h_in + (size_t)B * d, u, 4ull * n);
+    if (n == B) {
+        CU(cudaMemcpyAsync(t->io_in, t->h_in, 4ull * ((size_t)B * d + B), cudaMemcpyHostToDevice,
+                           t->stream));
+    } else {
+        CU(cudaMemcpyAsync(t->io_in, t->h_in, 4ull * n * d, cudaMemcpyHostToDevice, t->stream));
+        CU(cudaMemcpyAsync(t->io_in + (size_t)B * d, t->h_in + (size_t)B * d, 4ull * n,
+                           cudaMemcpyHostToDevice, t->stream));
+    }
+    return LAL_TAIL_OK;
+}
+/* tokens [B] and the status word: one copy of the whole block */
+int download_outputs(lal_tail *t) {
+    CU(cudaMemcpyAsync(t->h_out, t->io_out, 4ull * (t->cfg.max_streams + 1),
+                       cudaMemcpyDeviceToHost, t->stream));
+    return LAL_TAIL_OK;
+}
+}  // namespace
+
+extern "C" {
+
 int lal_tail_step(lal_tail *t, const float *hidden, int n_streams, const float *u,
                   int *tokens_out) {
     CHECK(ctx_check(t));
@@ -1605,17 +1635,9 @@ int lal_tail_step(lal_tail *t, const float *hidden, int n_streams, const float *
         return LAL_TAIL_OK;
     }
     const int B = t->cfg.max_streams, d = t->cfg.n_embd;
-    /* stage hidden and u contiguously in pinned memory: one H2D copy */
-    memcpy(t->h_in, hidden, 4ull * n_streams * d);
-    float *hu = t->h_in + (size_t)n_streams * d;
-    memcpy(hu, u, 4ull * n_streams);
-    float *d_u = t->io_in + (size_t)B * d;
-    CU(cudaMemcpyAsync(t->io_in, t->h_in, 4ull * n_streams * d, cudaMemcpyHostToDevice, t->stream));
-    CU(cudaMemcpyAsync(d_u, hu, 4ull * n_streams, cudaMemcpyHostToDevice, t->stream));
-    CHECK(enqueue_step(t, t->io_in, n_streams, d_u, t->io_out));
-    /* tokens and the status word in one D2H copy */
-    CU(cudaMemcpyAsync(t->h_out, t->io_out, 4ull * n_streams, cudaMemcpyDeviceToHost, t->stream));
-    CU(cudaMemcpyAsync(t->h_out + B, t->io_out + B, 4, cudaMemcpyDeviceToHost, t->stream));
+    CHECK(upload_inputs(t, hidden, n_streams, u));
+    CHECK(enqueue_step(t, t->io_in, n_streams, t->io_in + (size_t)B * d, t->io_out));
+    CHECK(download_outputs(t));
     CU(cudaStreamSynchronize(t->stream));
     const int status = t->h_out[B];
     if (status != 0) {
@@ -1635,14 +1657,7 @@ int lal_tail_stage_inputs(lal_tail *t, const float *hidden, int n_streams, const
     if (!hidden || !u) return fail(LAL_TAIL_ERR_ARG, "stage_inputs: null argument");
     if (n_streams < 1 || n_streams > t->cfg.max_streams)
         return fail(LAL_TAIL_ERR_ARG, "n_streams %d out of range", n_streams);
-    const int B = t->cfg.max_streams, d = t->cfg.n_embd;
-    memcpy(t->h_in, hidden, 4ull * n_streams * d);
-    float *hu = t->h_in + (size_t)n_streams * d;
-    memcpy(hu, u, 4ull * n_streams);
-    CU(cudaMemcpyAsync(t->io_in, t->h_in, 4ull * n_streams * d, cudaMemcpyHostToDevice, t->stream));
-    CU(cudaMemcpyAsync(t->io_in + (size_t)B * d, hu, 4ull * n_streams, cudaMemcpyHostToDevice,
-                       t->stream));
-    return LAL_TAIL_OK;
+    return upload_inputs(t, hidden, n_streams, u);
 }
 
 int lal_tail_fetch_tokens(lal_tail *t, int n_streams, int *tokens_out) {
@@ -1650,8 +1665,7 @@ int lal_tail_fetch_tokens(lal_tail *t, int n_streams, int *tokens_out) {
     if (!tokens_out || n_streams < 1 || n_streams > t->cfg.max_streams)
         return fail(LAL_TAIL_ERR_ARG, "fetch_tokens: bad arguments");
     const int B = t->cfg.max_streams;
-    CU(cudaMemcpyAsync(t->h_out, t->io_out, 4ull * n_streams, cudaMemcpyDeviceToHost, t->stream));
-    CU(cudaMemcpyAsync(t->h_out + B, t->io_out + B, 4, cudaMemcpyDeviceToHost, t->stream));
+    CHECK(download_outputs(t));
     CU(cudaStreamSynchronize(t->stream));
     const int status = t->h_out[B];
     if (status != 0) {

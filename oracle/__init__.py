@@ -194,7 +194,7 @@ def gpt2_lm_head(x: np.ndarray, wq: np.ndarray, sw: np.ndarray, lib: str = "port
     R = ref_gpt2()
     if (V, d) != (R.ref_gpt2_vocab(), R.ref_gpt2_n_embd()):
         raise ValueError("the GPT-2 server is compiled for V=50257, d=768")
-    R.ref_gpt2_lm_head(logits, x, wq.reshape(-1).copy(), sw.copy(), n_threads)
+    R.ref_gpt2_lm_head(logits, x, wq.reshape(-1), sw, n_threads)
     return logits, None
 
 
