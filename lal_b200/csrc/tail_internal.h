@@ -14,6 +14,9 @@ namespace lal {
 constexpr int kConsumerWarps = 8;
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
 constexpr int kMaxStages = 8;
+/* stages the fused kernel's producer issues before waiting for the previous
+ * kernel on the stream (programmatic dependent launch) */
+constexpr int kEarlyStages = 2;
 /* Largest grid (one CTA per SM on B200 is 148). */
 constexpr int kMaxGrid = 256;
 /* Global key histogram of the threshold search: level 0 = the top 12 bits

@@ -366,6 +366,11 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
                     mbar_expect_tx(&full_bar[s], bytes);
                     bulk_g2s(smem + (size_t)s * p.stage_bytes, p.W + (size_t)r0 * p.ld, bytes,
                              &full_bar[s], pol);
+                    /* at most two stages ahead of the previous kernel on the
+                     * stream: a full ring's burst (25 MB over the grid) slows
+                     * that kernel's serial tail; measured 93.0 against 93.4 us
+                     * a step back to back */
+                    if (c == kEarlyStages - 1) grid_dep_wait();
                 }
                 /* Do not leave copies in flight: wait (bounded) for the last
                  * issued stages to land before the CTA may exit. */
