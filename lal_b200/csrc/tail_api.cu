@@ -872,15 +872,13 @@ struct lal_tail {
     std::vector<int> f_mask, f_ids, f_ring, f_keep_h;
     /* the final RMSNorm's weights on the device (lal_tail_set_final_norm) */
     float *d_norm_w = nullptr;
-    /* LAL_SAMPLER_GPT2: the launch plans of the LM head, the RERANK_N
-     * candidates select and the sampler; the quantized vector and its scale,
-     * the select's parameter block, candidate list and diagnostics */
-    TailParams g2_lm, g2_sel, g2_smp;
-    int g2_grid_lm = 0, g2_grid_sel = 0, g2_grid_smp = 0, g2_cap = 0, g2_n = 0;
+    /* LAL_SAMPLER_GPT2: the launch plans of the LM head and the sampler; the
+     * quantized vector and its scale, the re-scored rows and their count */
+    TailParams g2_lm, g2_smp;
+    int g2_grid_lm = 0, g2_grid_smp = 0, g2_n = 0;
     int8_t *g2_xq = nullptr;
-    float *g2_sx = nullptr, *g2_cand_v = nullptr;
-    int *g2_cand_i = nullptr, *g2_par = nullptr, *g2_tok = nullptr;
-    StreamDiag *g2_diag = nullptr;
+    float *g2_sx = nullptr;
+    int *g2_cand_i = nullptr, *g2_count = nullptr;
 };
 
 namespace {
@@ -901,8 +899,7 @@ void destroy_ctx(lal_tail *t) {
                     t->hist_ids, t->hist_n, t->hist_head, t->diag, t->phase_ts,
                     t->x_send, t->x_recv, t->xq_b, t->sx_b, t->gmax_b, t->x_peer, t->d_peer,
                     t->f_cand_v, t->f_prefix, t->f_u, t->f_cand_i, t->f_keep, t->f_tok,
-                    t->f_diag, t->d_norm_w, t->g2_xq, t->g2_sx, t->g2_cand_v, t->g2_cand_i,
-                    t->g2_par, t->g2_tok, t->g2_diag};
+                    t->f_diag, t->d_norm_w, t->g2_xq, t->g2_sx, t->g2_cand_i, t->g2_count};
     for (void *b : bufs)
         if (b) cudaFree(b);
     t->sel.free_all();
@@ -918,8 +915,11 @@ void destroy_ctx(lal_tail *t) {
 int gpt2_alloc(lal_tail *t) {
     const lal_tail_config &c = t->cfg;
     const int V = c.vocab_size, num_sms = t->ds->num_sms;
+    if (V > kGpt2MaxV)
+        return fail(LAL_TAIL_ERR_UNSUPPORTED,
+                    "gpt2 tail: vocab %d above %d (its select holds the vocab's logits in one "
+                    "CTA's shared memory)", V, kGpt2MaxV);
     t->g2_n = std::min(kGpt2RerankN, V);
-    t->g2_cap = std::min(V, t->g2_n + 1024);
     TailParams &lm = t->g2_lm;
     base_params(lm, t->ds);
     lm.mode = MODE_LMHEAD;
@@ -933,39 +933,24 @@ int gpt2_alloc(lal_tail *t) {
     lm.trunc_cols = t->ld;
     lm.trunc_rows_end = 0;
     t->g2_grid_lm = plan_launch(lm, num_sms, 8);
-    auto sample_plan = [&](TailParams &q, int max_k) {
-        base_params(q, t->ds);
-        q.mode = MODE_SAMPLE;
-        q.variant = VARIANT_GPT2;
-        q.rows = V;
-        q.row_base = 0;
-        q.vocab = V;
-        q.d = q.ld = 16;
-        q.B = 1;
-        q.max_k = max_k;
-        return plan_launch(q, num_sms, 64);
-    };
-    t->g2_grid_sel = sample_plan(t->g2_sel, t->g2_n);
-    t->g2_grid_smp = sample_plan(t->g2_smp, std::min(c.max_top_k, V));
-    if (t->g2_grid_lm < 1 || t->g2_grid_sel < 1 || t->g2_grid_smp < 1)
+    TailParams &q = t->g2_smp;
+    base_params(q, t->ds);
+    q.mode = MODE_SAMPLE;
+    q.variant = VARIANT_GPT2;
+    q.rows = V;
+    q.row_base = 0;
+    q.vocab = V;
+    q.d = q.ld = 16;
+    q.B = 1;
+    q.max_k = std::min(c.max_top_k, V);
+    t->g2_grid_smp = plan_launch(q, num_sms, 64);
+    if (t->g2_grid_lm < 1 || t->g2_grid_smp < 1)
         return fail(LAL_TAIL_ERR_UNSUPPORTED, "gpt2 tail: shape V=%d d=%d unsupported", V,
                     c.n_embd);
     CU(cudaMalloc(&t->g2_xq, (size_t)t->ld));
     CU(cudaMalloc(&t->g2_sx, sizeof(float)));
-    CU(cudaMalloc(&t->g2_cand_v, sizeof(float) * (size_t)t->g2_cap));
-    CU(cudaMalloc(&t->g2_cand_i, sizeof(int) * (size_t)t->g2_cap));
-    CU(cudaMalloc(&t->g2_tok, sizeof(int)));
-    CU(cudaMalloc(&t->g2_diag, sizeof(StreamDiag)));
-    /* the select's parameters: temperature 1, top_k RERANK_N, no penalty */
-    const struct {
-        float t;
-        int k;
-        float pen;
-        float u;
-        int hn, head;
-    } sp = {1.0f, t->g2_n, 1.0f, 0.0f, 0, 0};
-    CU(cudaMalloc(&t->g2_par, sizeof(sp)));
-    CU(cudaMemcpy(t->g2_par, &sp, sizeof(sp), cudaMemcpyHostToDevice));
+    CU(cudaMalloc(&t->g2_cand_i, sizeof(int) * (size_t)kGpt2RerankN));
+    CU(cudaMalloc(&t->g2_count, sizeof(int)));
     return LAL_TAIL_OK;
 }
 
@@ -992,31 +977,10 @@ int enqueue_gpt2(lal_tail *t, int b, const float *d_hidden, const float *d_u, in
         CU(cudaEventRecord(t->ev[t->ev_used + 1], st));
         t->ev_used += 2;
     }
-    /* the RERANK_N largest int8 logits and every tie at the boundary */
-    TailParams q = t->g2_sel;
-    char *pb = reinterpret_cast<char *>(t->g2_par);
-    q.logits = logits;
-    q.temperature = reinterpret_cast<const float *>(pb + 0);
-    q.top_k = reinterpret_cast<const int *>(pb + 4);
-    q.rep_penalty = reinterpret_cast<const float *>(pb + 8);
-    q.u = reinterpret_cast<const float *>(pb + 12);
-    q.hist_n = reinterpret_cast<int *>(pb + 16);
-    q.hist_head = reinterpret_cast<int *>(pb + 20);
-    q.hist_ids = t->hist_ids;
-    q.hist_cap = 0;
-    q.push_history = 0;
-    q.tokens = t->g2_tok;
-    q.diag = t->g2_diag;
-    t->sel.fill(q);
-    q.status = status;
-    q.cand_val_out = t->g2_cand_v;
-    q.cand_idx_out = t->g2_cand_i;
-    q.cand_out_cap = t->g2_cap;
-    q.candidates_only = 1;
-    q.local_edges = use_local_edges(t->g2_n, q.rows_per_cta_max);
-    CU(launch_tail(q, t->g2_grid_sel, st));
-    CU(launch_gpt2_rerank(x, d, t->W, t->ld, t->sw, logits, V, t->g2_cand_i, t->g2_cap,
-                          t->g2_diag, t->g2_n, status, t->ds->num_sms, st));
+    /* the rows the server's heap keeps, then their float re-score */
+    CU(launch_gpt2_select(logits, V, t->g2_n, t->g2_cand_i, t->g2_count, status, st));
+    CU(launch_gpt2_rerank(x, d, t->W, t->ld, t->sw, logits, t->g2_cand_i, t->g2_count, t->g2_n,
+                          status, st));
     /* the server's sampler on the re-scored logits */
     TailParams r = t->g2_smp;
     r.logits = logits;

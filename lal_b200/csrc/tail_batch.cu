@@ -374,13 +374,6 @@ struct BatchSelectParams {
 
 constexpr uint32_t kEmptySlot = 0xFFFFFFFFu;
 
-__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
-                 : "memory");
-}
-__device__ __forceinline__ void cp_async_wait_all() {
-    asm volatile("cp.async.wait_all;" ::: "memory");
-}
 
 __global__ void __launch_bounds__(NT, 1) batch_select_kernel(const __grid_constant__ BatchSelectParams p) {
     extern __shared__ __align__(16) uint8_t bsm[];

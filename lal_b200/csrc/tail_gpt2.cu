@@ -9,11 +9,10 @@
  *                          truncation for every element;
  *   tail_kernel<LMHEAD>    the int8 logits of every row (gpt2_server.c:2013-
  *                          2095: exact int32 dots, scale_x*scale_w[v]*dot);
- *   tail_kernel<SAMPLE>    candidates only, k = RERANK_N: the threshold T of
- *                          the RERANK_N largest int8 logits and every row at
- *                          or above it, in ascending vocab order;
- *   gpt2_rerank_kernel     the float re-score of the RERANK_N rows picked by
- *                          the server's min-heap (gpt2_server.c:2160-2212):
+ *   gpt2_select_kernel     one CTA of 1024 threads with the V int8 logits in
+ *                          shared memory: the rows the server's min-heap of
+ *                          RERANK_N = 512 keeps (:2160-2197);
+ *   gpt2_rerank_kernel     their float re-score (gpt2_server.c:2203-2212):
  *                          logits[v] = sum over eight lanes of fused
  *                          multiply-adds x[i] * ((float)wq[i] * scale[v]),
  *                          lane j taking i = j (mod 8) in index order, the
@@ -32,19 +31,17 @@
  *
  * Which rows the heap keeps.  Every row above the RERANK_N-th largest int8
  * logit T is kept.  When more rows than places tie at T, the rows kept among
- * them depend on the heap's history: the candidates launch reports more than
- * RERANK_N rows, and the rerank kernel then replays the server's heap exactly
- * (one thread over the logits in index order, staged through shared memory)
- * before re-scoring -- a slow path (about a millisecond) that only exact
- * logit ties at the boundary take.
+ * them depend on the heap's history: the select kernel then replays the
+ * server's heap exactly (one thread over the keys in shared memory, index
+ * order) -- a slow path that only exact logit ties at the boundary take.
  */
 #include "tail_device.cuh"
 
 namespace lal {
 namespace {
 
-constexpr int kRerankWarps = 8;          /* warps a CTA of the rerank kernel    */
-constexpr int kHeapChunk = 4096;         /* logits staged a round (heap replay)  */
+constexpr int kRerankWarps = 8;          /* warps a CTA of the re-score kernel  */
+constexpr int kRerankRows = 32;          /* rows a CTA of the re-score kernel   */
 
 /* gpt2_server.c:1982-1998 */
 __global__ void __launch_bounds__(NT) gpt2_quantize_kernel(const float *x, int d, int8_t *xq,
@@ -74,111 +71,262 @@ __global__ void __launch_bounds__(NT) gpt2_quantize_kernel(const float *x, int d
     if (threadIdx.x == 0) *scale_out = scale;
 }
 
-/* The float re-score of row v (gpt2_server.c:2203-2211), by the eight lanes
- * sub*8 .. sub*8+7 of the calling warp; returns the score in lane sub*8. */
-__device__ __forceinline__ float rescore_row(const float *x, int d, const int8_t *wrow,
-                                             float scale, int lane8) {
-    float acc = 0.0f;
-#pragma unroll 4
-    for (int i = lane8; i < d; i += 8)
-        acc = __fmaf_rn(x[i], __fmul_rn((float)wrow[i], scale), acc);
-    /* v8f_hsum: t[0]+t[1]+...+t[7], left to right */
-    const int base = (threadIdx.x & 31) & ~7;
-    float s = 0.0f;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-        const float t = __shfl_sync(0xffffffffu, acc, base + j);
-        s = j == 0 ? t : __fadd_rn(s, t);
-    }
-    return s;
-}
-
-/* Re-scores the rows the server's heap keeps.  sel_diag->n_cand is the
- * candidates launch's count of rows at or above the N-th largest logit; the
- * common case (== N) takes the listed rows, all CTAs, four rows a warp; any
- * other count takes the exact heap replay in CTA 0 alone. */
-__global__ void __launch_bounds__(kRerankWarps * 32)
-    gpt2_rerank_kernel(const float *x, int d, const int8_t *W, int ld, const float *sw,
-                       float *logits, int V, const int *cand_i, int cand_cap,
-                       const StreamDiag *sel_diag, int N, const int *status) {
-    __shared__ float heap_val[kGpt2RerankN];
+/* The 512 rows the server's min-heap keeps (gpt2_server.c:2160-2197), from
+ * the int8 logits of all V rows held as order keys in one CTA's shared memory
+ * (V <= kGpt2MaxV): T, the N-th largest key with multiplicity, from a 12-bit
+ * histogram of the keys (the bin where the count from the top reaches N,
+ * searched by one warp down from the largest key's bin) and a count among the
+ * keys of that bin (a radix select over all keys when the bin is crowded).  When
+ * exactly N rows reach T they are the heap's rows, listed in any order;
+ * otherwise rows tie at T across the boundary and thread 0 replays the
+ * heap's pushes and root replacements over the keys in index order (keys
+ * compare as the floats do: -0 and +0 share one).  Writes the rows to
+ * cand_out and their count to *n_out. */
+__global__ void __launch_bounds__(kGpt2SelThreads, 1)
+    gpt2_select_kernel(const float *logits, int V, int N, int *cand_out, int *n_out,
+                       const int *status) {
+    extern __shared__ __align__(16) uint32_t keys[];
+    __shared__ __align__(16) uint32_t hist[4096]; /* then the boundary bin's keys */
+    __shared__ uint32_t sh[4];
+    __shared__ int cnt;
+    __shared__ uint32_t heap_key[kGpt2RerankN];
     __shared__ int heap_idx[kGpt2RerankN];
-    __shared__ float chunk[kHeapChunk];
-    __shared__ int heap_n_s;
-    if (*status != 0) return; /* the select failed: the step reports it */
-    const int m = sel_diag->n_cand;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int sub = lane >> 3, lane8 = lane & 7;
-    if (m == N && m <= cand_cap) {
-        const int gw = blockIdx.x * kRerankWarps + warp;
-        const int nw = gridDim.x * kRerankWarps;
-        for (int j0 = gw * 4; j0 < N; j0 += nw * 4) {
-            const int j = j0 + sub;
-            const bool on = j < N;
-            const int v = on ? cand_i[j] : 0;
-            const float s = rescore_row(x, d, W + (size_t)v * ld, on ? sw[v] : 0.0f, lane8);
-            if (on && lane8 == 0) logits[v] = s;
-        }
-        return;
+    if (*status != 0) return; /* the LM head failed: the step reports it */
+    const int tid = threadIdx.x, lane = tid & 31;
+    const int Vr = (V + kGpt2SelThreads - 1) / kGpt2SelThreads * kGpt2SelThreads;
+    for (int i = tid; i < 4096; i += kGpt2SelThreads) hist[i] = 0u;
+    if (tid == 0) sh[3] = 0u;
+    __syncthreads();
+    /* keys, their 12-bit histogram and the largest key */
+    uint32_t mk = 0u;
+#pragma unroll 4
+    for (int i = tid; i < V; i += kGpt2SelThreads) {
+        const uint32_t key = f2key(__ldcg(logits + i));
+        keys[i] = key;
+        atomicAdd(&hist[key >> 20], 1u);
+        mk = max(mk, key);
     }
-    if (blockIdx.x != 0) return;
-    /* the server's heap (gpt2_server.c:2167-2197), replayed by thread 0 over
-     * the int8 logits in index order; the block stages them */
-    int heap_n = 0;
-    for (int c0 = 0; c0 < V; c0 += kHeapChunk) {
-        const int cn = min(kHeapChunk, V - c0);
-        __syncthreads();
-        for (int i = threadIdx.x; i < cn; i += blockDim.x) chunk[i] = logits[c0 + i];
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            for (int q = 0; q < cn; ++q) {
-                const float val = chunk[q];
-                const int v = c0 + q;
-                if (heap_n < N) {
-                    int c = heap_n++;
-                    heap_val[c] = val;
-                    heap_idx[c] = v;
-                    while (c > 0) {
-                        const int p = (c - 1) >> 1;
-                        if (heap_val[p] <= heap_val[c]) break;
-                        const float tv = heap_val[p];
-                        heap_val[p] = heap_val[c];
-                        heap_val[c] = tv;
-                        const int ti = heap_idx[p];
-                        heap_idx[p] = heap_idx[c];
-                        heap_idx[c] = ti;
-                        c = p;
-                    }
-                } else if (val > heap_val[0]) {
-                    heap_val[0] = val;
-                    heap_idx[0] = v;
-                    int p = 0;
-                    for (;;) {
-                        const int l = 2 * p + 1, r = 2 * p + 2;
-                        int s = p;
-                        if (l < heap_n && heap_val[l] < heap_val[s]) s = l;
-                        if (r < heap_n && heap_val[r] < heap_val[s]) s = r;
-                        if (s == p) break;
-                        const float tv = heap_val[p];
-                        heap_val[p] = heap_val[s];
-                        heap_val[s] = tv;
-                        const int ti = heap_idx[p];
-                        heap_idx[p] = heap_idx[s];
-                        heap_idx[s] = ti;
-                        p = s;
-                    }
-                }
-            }
-            heap_n_s = heap_n;
+    mk = __reduce_max_sync(0xffffffffu, mk);
+    if (lane == 0) atomicMax(&sh[3], mk);
+    __syncthreads();
+    /* the bin holding the N-th largest key, the count above it and its own */
+    if (tid < 32) {
+        const uint32_t bin = warp_boundary_bin_4096(hist, sh[3] >> 20, (uint32_t)N);
+        uint32_t above = 0u;
+        for (int q = (int)bin + 1 + lane; q <= (int)(sh[3] >> 20); q += 32) above += hist[q];
+        above = __reduce_add_sync(0xffffffffu, above);
+        if (lane == 0) {
+            sh[0] = bin;
+            sh[1] = above;
+            sh[2] = hist[bin];
         }
     }
     __syncthreads();
-    const int hn = heap_n_s;
-    for (int j0 = warp * 4; j0 < hn; j0 += kRerankWarps * 4) {
-        const int j = j0 + sub;
-        const bool on = j < hn;
-        const int v = on ? heap_idx[j] : 0;
-        const float s = rescore_row(x, d, W + (size_t)v * ld, on ? sw[v] : 0.0f, lane8);
+    const uint32_t bin = sh[0], above = sh[1], nb = sh[2];
+    uint32_t T;
+    if (nb <= 4096u) {
+        /* the boundary bin's keys (into the histogram's memory), then the
+         * (N - above)-th largest of them by counting */
+        uint32_t *bk = hist;
+        if (tid == 0) cnt = 0;
+        __syncthreads();
+        for (int i = tid; i < Vr; i += kGpt2SelThreads) {
+            const uint32_t key = i < V ? keys[i] : 0u;
+            const bool in = i < V && (key >> 20) == bin;
+            const unsigned bal = __ballot_sync(0xffffffffu, in);
+            if (bal) {
+                int base = 0;
+                if (lane == 0) base = atomicAdd(&cnt, __popc(bal));
+                base = __shfl_sync(0xffffffffu, base, 0);
+                if (in) bk[base + __popc(bal & ((1u << lane) - 1u))] = key;
+            }
+        }
+        __syncthreads();
+        const uint32_t kk = (uint32_t)N - above;
+        uint32_t best = 0xffffffffu;
+        for (int e = tid; e < (int)nb; e += kGpt2SelThreads) {
+            const uint32_t me = bk[e];
+            uint32_t gt = 0u;
+            for (int j = 0; j < (int)nb; ++j) gt += bk[j] > me;
+            if (gt < kk) best = min(best, me);
+        }
+        best = __reduce_min_sync(0xffffffffu, best);
+        if (tid == 0) sh[0] = 0xffffffffu;
+        __syncthreads();
+        if (lane == 0) atomicMin(&sh[0], best);
+        __syncthreads();
+        T = sh[0];
+        __syncthreads();
+    } else {
+        /* a crowded boundary bin: radix select over all keys (8-bit digits) */
+        uint32_t prefix = 0u, mask = 0u;
+        uint32_t krem = (uint32_t)N;
+        for (int shift = 24; shift >= 0; shift -= 8) {
+            if (tid < 256) hist[tid] = 0u;
+            __syncthreads();
+            for (int i = tid; i < Vr; i += kGpt2SelThreads) {
+                const uint32_t key = i < V ? keys[i] : 0u;
+                const bool m = i < V && (key & mask) == prefix;
+                const uint32_t digit = (key >> shift) & 0xFFu;
+                const unsigned voters = __ballot_sync(0xffffffffu, m);
+                if (m) {
+                    const unsigned peers = __match_any_sync(voters, digit);
+                    if (lane == __ffs(peers) - 1) atomicAdd(&hist[digit], (uint32_t)__popc(peers));
+                }
+            }
+            __syncthreads();
+            if (tid < 32) {
+                /* from the top: lane l holds digits 255-8l .. 248-8l */
+                uint32_t c[8], sum = 0u;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    c[j] = hist[255 - 8 * lane - j];
+                    sum += c[j];
+                }
+                uint32_t incl = sum;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+                    if (lane >= o) incl += y;
+                }
+                const uint32_t excl = incl - sum;
+                if (excl < krem && krem <= incl) {
+                    uint32_t run = excl;
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        if (run < krem && run + c[j] >= krem) {
+                            sh[0] = 255u - 8u * (uint32_t)lane - (uint32_t)j;
+                            sh[1] = run;
+                        }
+                        run += c[j];
+                    }
+                }
+            }
+            __syncthreads();
+            prefix |= sh[0] << shift;
+            mask |= 0xFFu << shift;
+            krem -= sh[1];
+            __syncthreads();
+        }
+        T = prefix;
+    }
+    /* rows at or above T */
+    if (tid == 0) cnt = 0;
+    __syncthreads();
+    int c = 0;
+    for (int i = tid; i < V; i += kGpt2SelThreads) c += keys[i] >= T;
+    c = __reduce_add_sync(0xffffffffu, c);
+    if (lane == 0 && c) atomicAdd(&cnt, c);
+    __syncthreads();
+    const int m = cnt;
+    __syncthreads();
+    if (m == N) {
+        if (tid == 0) cnt = 0;
+        __syncthreads();
+        for (int i = tid; i < Vr; i += kGpt2SelThreads) {
+            const bool take = i < V && keys[i] >= T;
+            const unsigned bal = __ballot_sync(0xffffffffu, take);
+            if (bal) {
+                int base = 0;
+                if (lane == 0) base = atomicAdd(&cnt, __popc(bal));
+                base = __shfl_sync(0xffffffffu, base, 0);
+                if (take) cand_out[base + __popc(bal & ((1u << lane) - 1u))] = i;
+            }
+        }
+        if (tid == 0) *n_out = N;
+        return;
+    }
+    if (tid == 0) {
+        int hn = 0;
+        for (int v = 0; v < V; ++v) {
+            const uint32_t val = keys[v];
+            if (hn < N) {
+                int ch = hn++;
+                heap_key[ch] = val;
+                heap_idx[ch] = v;
+                while (ch > 0) {
+                    const int pa = (ch - 1) >> 1;
+                    if (heap_key[pa] <= heap_key[ch]) break;
+                    const uint32_t tk = heap_key[pa];
+                    heap_key[pa] = heap_key[ch];
+                    heap_key[ch] = tk;
+                    const int ti = heap_idx[pa];
+                    heap_idx[pa] = heap_idx[ch];
+                    heap_idx[ch] = ti;
+                    ch = pa;
+                }
+            } else if (val > heap_key[0]) {
+                heap_key[0] = val;
+                heap_idx[0] = v;
+                int pa = 0;
+                for (;;) {
+                    const int l = 2 * pa + 1, r = 2 * pa + 2;
+                    int sm = pa;
+                    if (l < hn && heap_key[l] < heap_key[sm]) sm = l;
+                    if (r < hn && heap_key[r] < heap_key[sm]) sm = r;
+                    if (sm == pa) break;
+                    const uint32_t tk = heap_key[pa];
+                    heap_key[pa] = heap_key[sm];
+                    heap_key[sm] = tk;
+                    const int ti = heap_idx[pa];
+                    heap_idx[pa] = heap_idx[sm];
+                    heap_idx[sm] = ti;
+                    pa = sm;
+                }
+            }
+        }
+        for (int j = 0; j < hn; ++j) cand_out[j] = heap_idx[j];
+        *n_out = hn;
+    }
+}
+
+/* The float re-score (gpt2_server.c:2203-2211) of up to kRerankRows listed
+ * rows a CTA: x and the rows are staged into shared memory with 16-byte
+ * asynchronous copies, then eight lanes a row sum x[i] * ((float)wq[i] *
+ * scale) as fused multiply-adds, lane j over i = j (mod 8) in index order,
+ * and add the lanes left to right (v8f_hsum, :110-113). */
+__global__ void __launch_bounds__(kRerankWarps * 32)
+    gpt2_rerank_kernel(const float *x, int d, const int8_t *W, int ld, const float *sw,
+                       float *logits, const int *cand, const int *n_ptr, const int *status) {
+    extern __shared__ __align__(16) uint8_t rsm[];
+    if (*status != 0) return;
+    const int n = *n_ptr;
+    const int j0 = blockIdx.x * kRerankRows;
+    if (j0 >= n) return;
+    const int rn = min(kRerankRows, n - j0);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    uint8_t *rows = rsm;
+    float *xs = reinterpret_cast<float *>(rsm + (size_t)kRerankRows * ld);
+    if ((reinterpret_cast<uintptr_t>(x) & 15u) == 0) {
+        for (int e = tid; e < d / 4; e += blockDim.x) cp_async16(xs + 4 * e, x + 4 * e);
+    } else {
+        for (int i = tid; i < d; i += blockDim.x) xs[i] = x[i];
+    }
+    const int rp = ld / 16;
+    for (int e = tid; e < rn * rp; e += blockDim.x) {
+        const int r = e / rp, q = e - r * rp;
+        cp_async16(rows + (size_t)r * ld + 16 * q, W + (size_t)cand[j0 + r] * ld + 16 * q);
+    }
+    cp_async_wait_all();
+    __syncthreads();
+    const int sub = lane >> 3, lane8 = lane & 7;
+    for (int r0 = warp * 4; r0 < rn; r0 += kRerankWarps * 4) {
+        const int r = r0 + sub;
+        const bool on = r < rn;
+        const int8_t *wr = reinterpret_cast<const int8_t *>(rows + (size_t)(on ? r : 0) * ld);
+        const int v = on ? cand[j0 + r] : 0;
+        const float scale = on ? sw[v] : 0.0f;
+        float acc = 0.0f;
+#pragma unroll 4
+        for (int i = lane8; i < d; i += 8)
+            acc = __fmaf_rn(xs[i], __fmul_rn((float)wr[i], scale), acc);
+        const int base = lane & ~7;
+        float s = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float t = __shfl_sync(0xffffffffu, acc, base + j);
+            s = j == 0 ? t : __fadd_rn(s, t);
+        }
         if (on && lane8 == 0) logits[v] = s;
     }
 }
@@ -191,13 +339,24 @@ cudaError_t launch_gpt2_quantize(const float *x, int d, int8_t *xq, int ld, floa
     return cudaGetLastError();
 }
 
+cudaError_t launch_gpt2_select(const float *logits, int V, int N, int *cand_out, int *n_out,
+                               const int *status, cudaStream_t st) {
+    const int bytes = 4 * V;
+    cudaError_t e = raise_smem((const void *)gpt2_select_kernel, bytes);
+    if (e != cudaSuccess) return e;
+    gpt2_select_kernel<<<1, kGpt2SelThreads, bytes, st>>>(logits, V, N, cand_out, n_out, status);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_gpt2_rerank(const float *x, int d, const int8_t *W, int ld, const float *sw,
-                               float *logits, int V, const int *cand_i, int cand_cap,
-                               const StreamDiag *sel_diag, int N, const int *status,
-                               int num_sms, cudaStream_t st) {
-    const int grid = std::max(1, std::min(num_sms, (N + kRerankWarps * 4 - 1) / (kRerankWarps * 4)));
-    gpt2_rerank_kernel<<<grid, kRerankWarps * 32, 0, st>>>(x, d, W, ld, sw, logits, V, cand_i,
-                                                          cand_cap, sel_diag, N, status);
+                               float *logits, const int *cand, const int *n_dev, int N,
+                               const int *status, cudaStream_t st) {
+    const int bytes = kRerankRows * ld + 4 * d;
+    cudaError_t e = raise_smem((const void *)gpt2_rerank_kernel, bytes);
+    if (e != cudaSuccess) return e;
+    const int grid = (N + kRerankRows - 1) / kRerankRows;
+    gpt2_rerank_kernel<<<grid, kRerankWarps * 32, bytes, st>>>(x, d, W, ld, sw, logits, cand,
+                                                              n_dev, status);
     return cudaGetLastError();
 }
 

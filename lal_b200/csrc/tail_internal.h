@@ -63,6 +63,9 @@ enum Mode : int { MODE_FUSED = 0, MODE_LMHEAD = 1, MODE_SAMPLE = 2 };
 enum Variant : int { VARIANT_LIBRARY = 0, VARIANT_SERVER = 1, VARIANT_GPT2 = 2 };
 /* rows the GPT-2 server re-scores in float (gpt2_server.c:2123) */
 constexpr int kGpt2RerankN = 512;
+/* the GPT-2 tail's select holds the vocab's keys in one CTA's shared memory */
+constexpr int kGpt2SelThreads = 1024;
+constexpr int kGpt2MaxV = 51200;
 
 /* Device status word values (mirrors LAL_TAIL_ERR_* in include/lal_tail.h). */
 enum DevStatus : int { DEV_OK = 0, DEV_TIMEOUT = 4, DEV_CAPACITY = 5 };
@@ -310,10 +313,11 @@ int plan_launch(TailParams &p, int num_sms, int min_rows_per_cta);
 cudaError_t launch_tail(const TailParams &p, int grid, cudaStream_t st);
 cudaError_t launch_gpt2_quantize(const float *x, int d, int8_t *xq, int ld, float *scale_out,
                                  cudaStream_t st);
+cudaError_t launch_gpt2_select(const float *logits, int V, int N, int *cand_out, int *n_out,
+                               const int *status, cudaStream_t st);
 cudaError_t launch_gpt2_rerank(const float *x, int d, const int8_t *W, int ld, const float *sw,
-                               float *logits, int V, const int *cand_i, int cand_cap,
-                               const StreamDiag *sel_diag, int N, const int *status,
-                               int num_sms, cudaStream_t st);
+                               float *logits, const int *cand, const int *n_dev, int N,
+                               const int *status, cudaStream_t st);
 cudaError_t launch_quantize_x(const float *x, int8_t *xq, float *scale, int n,
                               cudaStream_t st);
 cudaError_t launch_abs_xq(const int8_t *xq, uint8_t *ax, int n, cudaStream_t st);
