@@ -61,7 +61,8 @@ extern "C" {
  * min-heap keeps re-scored in float, then LIBRARY's arithmetic on the
  * re-scored logits, except that a draw of exactly 0 returns row 0.  u[b] is
  * the caller's (float)(rand() % 1000000) / 1000000.0f.  One shard, n_embd a
- * multiple of 8; lal_tail_get_logits returns the re-scored, penalised
+ * multiple of 8, vocab_size <= 51200 (the select holds the vocab's logits in
+ * one CTA's shared memory); lal_tail_get_logits returns the re-scored, penalised
  * logits (the server's g_logits after the step). */
 #define LAL_SAMPLER_GPT2    2
 
