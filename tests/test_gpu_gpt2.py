@@ -100,3 +100,39 @@ def test_gpt2_small_vocab_rescore_all_rows():
 def test_gpt2_context_limits():
     with pytest.raises(L.LalTailError):
         L.DecodeTail(1000, 100, max_top_k=8, history_cap=8, sampler=L.LAL_SAMPLER_GPT2)
+
+
+@pytest.mark.parametrize("kind", ["crowded_bin", "mass_ties"])
+def test_gpt2_crowded_boundary_bin(kind):
+    """More than 4096 logits in the 12-bit bin that holds the 512th largest:
+    the select's radix path.  crowded_bin: nearly equal rows (distinct
+    values, the rows at or above T are exactly 512); mass_ties: 6000 identical
+    rows tie across the boundary (the heap replay decides which are kept)."""
+    cfg = synth.CONFIGS["c1_gpt2"].with_(hist=8)
+    V, d = cfg.vocab, cfg.n_embd
+    rng = np.random.default_rng(21 if kind == "crowded_bin" else 22)
+    base = rng.standard_normal(d).astype(np.float32)
+    if kind == "crowded_bin":
+        W = (base[None, :] + 0.002 * rng.standard_normal((V, d))).astype(np.float32)
+    else:
+        W = (0.05 * rng.standard_normal((V, d))).astype(np.float32)
+        W[rng.choice(V, 6000, replace=False)] = base * 0.05
+    q, s = oracle.quantize_rows(W * 0.02, "port")
+    x = (base * 3.0).astype(np.float32)
+    lg = oracle.gpt2_lm_head(x, q, s)[0]
+    sx, xq = oracle.gpt2_quantize_x(x, "port")
+    plain = (sx * s) * (q.astype(np.int32) @ xq.astype(np.int32)).astype(np.float32)
+    key = plain.view(np.uint32)
+    key = np.where(key >> 31 == 1, ~key, key | 0x80000000).astype(np.uint32)
+    T = np.sort(key)[::-1][511]
+    assert (key >> 20 == T >> 20).sum() > 4096, "the case must crowd the boundary bin"
+    assert ((key >= T).sum() == 512) == (kind == "crowded_bin")
+    t = gpt2_tail(q, s, cfg)
+    t.set_sampling([0.8], [40], [1.0])
+    t.set_history(0, np.zeros(0, np.int32))
+    port = oracle.Gpt2PortLoop(q, s, [], cfg.hist, 0.8, 40, 1.0)
+    tok = int(t.step(x[None, :], np.array([0.4], np.float32))[0])
+    ptok, _ = port.step(x, np.float32(0.4))
+    assert tok == ptok
+    np.testing.assert_array_equal(bits(t.logits(0)), bits(port.logits))
+    t.close()
