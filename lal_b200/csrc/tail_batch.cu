@@ -54,6 +54,7 @@ constexpr int kGemmThreads = 192;  /* warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
 constexpr int kGemmStagesMax = 8;
 constexpr int kGemmSmemLimit = 232448;
 constexpr int kStageGroups = 512;  /* 32-row logit groups staged a round (select) */
+constexpr int kPenGroupWords = 512; /* bitmap words of groups holding a penalised row */
 
 /* ------------------------------------------------------------ PTX --- */
 __device__ __forceinline__ uint64_t policy_evict_last() {
@@ -427,7 +428,16 @@ __global__ void __launch_bounds__(NT, 1) batch_select_kernel(const __grid_consta
      * (runtime/lal_sampling.h:60-66; ids outside [0, V) are skipped) */
     for (int i = tid; i < 4096; i += NT) hist[i] = 0u;
     __shared__ int s_pen; /* distinct history ids inside this slice */
-    if (tid == 0) s_pen = 0;
+    __shared__ int s_pen_groups; /* 32-row groups holding one of them */
+    /* which 32-row groups hold a penalised row (slices of up to
+     * kPenGroupWords * 32 groups) */
+    __shared__ uint32_t pen_groups[kPenGroupWords];
+    const bool mark = p.n_groups <= kPenGroupWords * 32;
+    if (tid == 0) {
+        s_pen = 0;
+        s_pen_groups = 0;
+    }
+    for (int i = tid; i < kPenGroupWords; i += NT) pen_groups[i] = 0u;
     if (use_pen) {
         for (int i = tid; i < p.h_slots; i += NT) {
             hkey[i] = kEmptySlot;
@@ -445,7 +455,15 @@ __global__ void __launch_bounds__(NT, 1) batch_select_kernel(const __grid_consta
                 const uint32_t prev = atomicCAS(&hkey[slot], kEmptySlot, (uint32_t)id);
                 if (prev == kEmptySlot || prev == (uint32_t)id) {
                     atomicAdd(&hcnt[slot], 1u);
-                    if (prev == kEmptySlot) atomicAdd(&s_pen, 1);
+                    if (prev == kEmptySlot) {
+                        atomicAdd(&s_pen, 1);
+                        if (mark) {
+                            const int gi = g >> 5;
+                            const uint32_t bit = 1u << (gi & 31);
+                            if (!(atomicOr(&pen_groups[gi >> 5], bit) & bit))
+                                atomicAdd(&s_pen_groups, 1);
+                        }
+                    }
                     break;
                 }
                 slot = (slot + 1u) & mask;
@@ -509,12 +527,21 @@ __global__ void __launch_bounds__(NT, 1) batch_select_kernel(const __grid_consta
     };
     uint32_t L = 0u;
     int S = -1;
-    const int kp = k + s_pen;
+    /* with the penalised groups marked, only the groups free of penalised
+     * rows count towards the bound: their maxima are unchanged logits of k
+     * distinct rows, so the k-th largest of them is <= T; otherwise every
+     * group counts and the (k+P)-th largest maximum is the bound */
+    const bool excl = mark && p.n_groups - s_pen_groups >= k;
+    const int kp = excl ? k : k + s_pen;
     const bool groups = p.gmax != nullptr && kp <= p.n_groups / 8 && p.n_groups <= p.s_cap;
+    auto counts = [&](int g) {
+        return g < p.n_groups && !(excl && ((pen_groups[g >> 5] >> (g & 31)) & 1u));
+    };
     if (groups) {
-        /* the group maxima (contiguous per stream) into Sk and their top 12
-         * key bits into the histogram; the lower edge of the bin holding the
-         * (k+P)-th largest maximum is <= that maximum, hence a bound of T */
+        /* the group maxima (contiguous per stream) into Sk and the top 12 key
+         * bits of the counted ones into the histogram; the lower edge of the
+         * bin holding the kp-th largest counted maximum is <= that maximum,
+         * hence a bound of T */
         uint32_t *Gk = Sk; /* the group maxima, then the superset */
         const uint32_t *gm = p.gmax + (size_t)b * p.n_groups;
         if (gpre_ok) {
@@ -522,7 +549,7 @@ __global__ void __launch_bounds__(NT, 1) batch_select_kernel(const __grid_consta
             for (int j = 0; j < kGroupRegs; ++j) {
                 const int g = j * NT + tid;
                 if (g < p.n_groups) Gk[g] = gpre[j];
-                hist_add(hist, gpre[j] >> 20, g < p.n_groups);
+                hist_add(hist, gpre[j] >> 20, counts(g));
             }
         } else
         for (int g0 = 0; g0 < p.n_groups; g0 += NT * U) {
@@ -536,7 +563,7 @@ __global__ void __launch_bounds__(NT, 1) batch_select_kernel(const __grid_consta
             for (int j = 0; j < U; ++j) {
                 const int g = g0 + j * NT + tid;
                 if (g < p.n_groups) Gk[g] = v[j];
-                hist_add(hist, v[j] >> 20, g < p.n_groups);
+                hist_add(hist, v[j] >> 20, counts(g));
             }
         }
         __syncthreads();
