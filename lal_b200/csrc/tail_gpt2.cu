@@ -42,6 +42,7 @@ namespace {
 
 constexpr int kRerankWarps = 8;          /* warps a CTA of the re-score kernel  */
 constexpr int kRerankRows = 32;          /* rows a CTA of the re-score kernel   */
+constexpr int kGpt2SelCap = 2048;        /* keys gathered above the bin's edge  */
 
 /* gpt2_server.c:1982-1998 */
 __global__ void __launch_bounds__(NT) gpt2_quantize_kernel(const float *x, int d, int8_t *xq,
@@ -97,15 +98,26 @@ __global__ void __launch_bounds__(kGpt2SelThreads, 1)
     for (int i = tid; i < 4096; i += kGpt2SelThreads) hist[i] = 0u;
     if (tid == 0) sh[3] = 0u;
     __syncthreads();
-    /* keys, their 12-bit histogram and the largest key */
+    /* keys, their 12-bit histogram and the largest key (16-byte reads when
+     * the logits start on a 16-byte boundary) */
     uint32_t mk = 0u;
-#pragma unroll 4
-    for (int i = tid; i < V; i += kGpt2SelThreads) {
-        const uint32_t key = f2key(__ldcg(logits + i));
+    auto take_key = [&](int i, float l) {
+        const uint32_t key = f2key(l);
         keys[i] = key;
         atomicAdd(&hist[key >> 20], 1u);
         mk = max(mk, key);
+    };
+    const bool al16 = (reinterpret_cast<uintptr_t>(logits) & 15u) == 0;
+    const int nv = al16 ? V / 4 : 0;
+#pragma unroll 2
+    for (int e = tid; e < nv; e += kGpt2SelThreads) {
+        const float4 v = __ldcg(reinterpret_cast<const float4 *>(logits) + e);
+        take_key(4 * e, v.x);
+        take_key(4 * e + 1, v.y);
+        take_key(4 * e + 2, v.z);
+        take_key(4 * e + 3, v.w);
     }
+    for (int i = 4 * nv + tid; i < V; i += kGpt2SelThreads) take_key(i, __ldcg(logits + i));
     mk = __reduce_max_sync(0xffffffffu, mk);
     if (lane == 0) atomicMax(&sh[3], mk);
     __syncthreads();
@@ -123,42 +135,76 @@ __global__ void __launch_bounds__(kGpt2SelThreads, 1)
     }
     __syncthreads();
     const uint32_t bin = sh[0], above = sh[1], nb = sh[2];
-    uint32_t T;
-    if (nb <= 4096u) {
-        /* the boundary bin's keys (into the histogram's memory), then the
-         * (N - above)-th largest of them by counting */
-        uint32_t *bk = hist;
+    const uint32_t edge = bin << 20;
+    if (above + nb <= (uint32_t)kGpt2SelCap) {
+        /* one pass: every key at or above the bin's lower edge with its row
+         * (into the histogram's memory); T and the rows come from them */
+        uint32_t *ck = hist;
+        int *ci = reinterpret_cast<int *>(hist + kGpt2SelCap);
         if (tid == 0) cnt = 0;
         __syncthreads();
         for (int i = tid; i < Vr; i += kGpt2SelThreads) {
             const uint32_t key = i < V ? keys[i] : 0u;
-            const bool in = i < V && (key >> 20) == bin;
+            const bool in = i < V && key >= edge;
             const unsigned bal = __ballot_sync(0xffffffffu, in);
             if (bal) {
                 int base = 0;
                 if (lane == 0) base = atomicAdd(&cnt, __popc(bal));
                 base = __shfl_sync(0xffffffffu, base, 0);
-                if (in) bk[base + __popc(bal & ((1u << lane) - 1u))] = key;
+                if (in) {
+                    const int pos = base + __popc(bal & ((1u << lane) - 1u));
+                    ck[pos] = key;
+                    ci[pos] = i;
+                }
             }
         }
         __syncthreads();
-        const uint32_t kk = (uint32_t)N - above;
+        const int na = cnt; /* = above + nb */
+        /* T = min{ key of the bin : #{gathered keys > key} < N } */
         uint32_t best = 0xffffffffu;
-        for (int e = tid; e < (int)nb; e += kGpt2SelThreads) {
-            const uint32_t me = bk[e];
+        for (int e = tid; e < na; e += kGpt2SelThreads) {
+            const uint32_t me = ck[e];
+            if ((me >> 20) != bin) continue;
             uint32_t gt = 0u;
-            for (int j = 0; j < (int)nb; ++j) gt += bk[j] > me;
-            if (gt < kk) best = min(best, me);
+            for (int j = 0; j < na; ++j) gt += ck[j] > me;
+            if (gt < (uint32_t)N) best = min(best, me);
         }
         best = __reduce_min_sync(0xffffffffu, best);
         if (tid == 0) sh[0] = 0xffffffffu;
         __syncthreads();
         if (lane == 0) atomicMin(&sh[0], best);
         __syncthreads();
-        T = sh[0];
+        const uint32_t T = sh[0];
+        /* the rows at or above T: the heap's rows when there are exactly N */
+        int c = 0;
+        for (int e = tid; e < na; e += kGpt2SelThreads) c += ck[e] >= T;
+        if (tid == 0) cnt = 0;
         __syncthreads();
+        c = __reduce_add_sync(0xffffffffu, c);
+        if (lane == 0 && c) atomicAdd(&cnt, c);
+        __syncthreads();
+        const int mt = cnt;
+        if (mt == N) {
+            __syncthreads();
+            if (tid == 0) cnt = 0;
+            __syncthreads();
+            const int nar = (na + kGpt2SelThreads - 1) / kGpt2SelThreads * kGpt2SelThreads;
+            for (int e = tid; e < nar; e += kGpt2SelThreads) {
+                const bool take = e < na && ck[e] >= T;
+                const unsigned bal = __ballot_sync(0xffffffffu, take);
+                if (bal) {
+                    int base = 0;
+                    if (lane == 0) base = atomicAdd(&cnt, __popc(bal));
+                    base = __shfl_sync(0xffffffffu, base, 0);
+                    if (take) cand_out[base + __popc(bal & ((1u << lane) - 1u))] = ci[e];
+                }
+            }
+            if (tid == 0) *n_out = N;
+            return;
+        }
+        /* ties across the boundary: the heap replay below */
     } else {
-        /* a crowded boundary bin: radix select over all keys (8-bit digits) */
+        /* a crowded boundary: radix select over all keys (8-bit digits) */
         uint32_t prefix = 0u, mask = 0u;
         uint32_t krem = (uint32_t)N;
         for (int shift = 24; shift >= 0; shift -= 8) {
@@ -208,34 +254,37 @@ __global__ void __launch_bounds__(kGpt2SelThreads, 1)
             krem -= sh[1];
             __syncthreads();
         }
-        T = prefix;
-    }
-    /* rows at or above T */
-    if (tid == 0) cnt = 0;
-    __syncthreads();
-    int c = 0;
-    for (int i = tid; i < V; i += kGpt2SelThreads) c += keys[i] >= T;
-    c = __reduce_add_sync(0xffffffffu, c);
-    if (lane == 0 && c) atomicAdd(&cnt, c);
-    __syncthreads();
-    const int m = cnt;
-    __syncthreads();
-    if (m == N) {
+        const uint32_t T = prefix;
+        /* rows at or above T */
         if (tid == 0) cnt = 0;
         __syncthreads();
-        for (int i = tid; i < Vr; i += kGpt2SelThreads) {
-            const bool take = i < V && keys[i] >= T;
-            const unsigned bal = __ballot_sync(0xffffffffu, take);
-            if (bal) {
-                int base = 0;
-                if (lane == 0) base = atomicAdd(&cnt, __popc(bal));
-                base = __shfl_sync(0xffffffffu, base, 0);
-                if (take) cand_out[base + __popc(bal & ((1u << lane) - 1u))] = i;
+        int c = 0;
+        for (int i = tid; i < V; i += kGpt2SelThreads) c += keys[i] >= T;
+        c = __reduce_add_sync(0xffffffffu, c);
+        if (lane == 0 && c) atomicAdd(&cnt, c);
+        __syncthreads();
+        const int m = cnt;
+        __syncthreads();
+        if (m == N) {
+            if (tid == 0) cnt = 0;
+            __syncthreads();
+            for (int i = tid; i < Vr; i += kGpt2SelThreads) {
+                const bool take = i < V && keys[i] >= T;
+                const unsigned bal = __ballot_sync(0xffffffffu, take);
+                if (bal) {
+                    int base = 0;
+                    if (lane == 0) base = atomicAdd(&cnt, __popc(bal));
+                    base = __shfl_sync(0xffffffffu, base, 0);
+                    if (take) cand_out[base + __popc(bal & ((1u << lane) - 1u))] = i;
+                }
             }
+            if (tid == 0) *n_out = N;
+            return;
         }
-        if (tid == 0) *n_out = N;
-        return;
     }
+    /* more rows than places tie at T: the server's heap (gpt2_server.c:
+     * 2167-2197) replayed over the keys in index order (keys compare as the
+     * floats do: -0 and +0 share one) */
     if (tid == 0) {
         int hn = 0;
         for (int v = 0; v < V; ++v) {
