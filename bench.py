@@ -101,35 +101,61 @@ def load_traffic(cfg_name, n_gpus):
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 200 ms."""
+    """nvidia-smi clocks and throttle reasons, sampled every `ms` milliseconds.
+    Started (and its first sample awaited, at most 5 s) before the untimed
+    warm-up, so that nvidia-smi's start-up is over before the timed region;
+    mark() at the region's start drops the samples taken before it."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index: int):
+    def __init__(self, gpu_index: int, ms: int = 20):
         self.gpu = gpu_index
+        self.ms = ms
         self.proc = None
+        self.lines = []
+        self.skip = 0
+        self.out = ""
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line)
+
+    def _kill(self):
+        if self.proc and self.proc.poll() is None:
+            self.proc.kill()
 
     def __enter__(self):
+        import atexit
+        import threading
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", str(self.ms)],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except (FileNotFoundError, OSError):
             self.proc = None
+            return self
+        atexit.register(self._kill)
+        threading.Thread(target=self._read, daemon=True).start()
+        t0 = time.time()
+        while not self.lines and time.time() - t0 < 5.0 and self.proc.poll() is None:
+            time.sleep(0.01)
         return self
 
+    def mark(self):
+        """The timed region starts: earlier samples are left out of summary()."""
+        self.skip = len(self.lines)
+
     def __exit__(self, *a):
-        self.out = ""
         if self.proc:
-            time.sleep(0.25)
+            time.sleep(2.5 * self.ms / 1000.0)
             self.proc.terminate()
             try:
-                self.out, _ = self.proc.communicate(timeout=5)
+                self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
-                self.out = ""
+        self.out = "".join(self.lines[self.skip:])
 
     def summary(self):
         rows = []
@@ -382,19 +408,44 @@ def run_ours(args, cfg):
             if align is not None:
                 dist.all_reduce(align)
 
+    # clocks sampled from here on; the summary keeps the timed region's samples
+    clk = ClockSampler(local)
+    clk.__enter__()
+
     # warm-up through the public call
     for i in range(W):
         t.step(hid[i], us[i])
 
-    # ---- value: inputs resident in HBM, device-timed ----
     d_hid = torch.from_numpy(hid[W:W + K]).to(local)
     d_u = torch.from_numpy(us[W:W + K]).to(local)
     d_tok = torch.empty((K, B), dtype=torch.int32, device=local)
+    # Untimed device steps for about WARM_S seconds before the timed region:
+    # the first process on a freshly leased GPU ran its back-to-back steps ~9%
+    # slower without them (C2: 102-103 us a step against 93-94 us; 0.3 s of
+    # steps removed it, later processes never showed it). Rank 0's clock
+    # decides after each chunk and the decision is all-reduced, so every rank
+    # takes the same number of steps (the sharded step exchanges records).
+    WARM_S, chunk = 0.3, 64
+    go = torch.ones(1, dtype=torch.int32, device=local)
+    t_w = time.perf_counter()
+    while True:
+        for j in range(chunk):
+            i = j % K
+            t.step_device(d_hid[i].data_ptr(), B, d_u[i].data_ptr(), d_tok[i].data_ptr())
+        t.sync()
+        go.fill_(int(rank != 0 or time.perf_counter() - t_w < WARM_S))
+        if dist is not None:
+            dist.all_reduce(go, op=dist.ReduceOp.MIN)
+        if not int(go.item()):
+            break
+
+    # ---- value: inputs resident in HBM, device-timed ----
     n_ev = 1 if flush is None else K
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
           for _ in range(n_ev)]
     barrier()
-    with ClockSampler(local) as clk:
+    clk.mark()
+    try:  # the timed region and the roofline pass, clocks sampled throughout
         if flush is None:
             # back-to-back steps (the slice is larger than L2): one bracket
             ev[0][0].record(stream)
@@ -427,6 +478,8 @@ def run_ours(args, cfg):
         kern_ms, n_launch = t.kernel_time()
         t.set_timing(False)
         barrier()
+    finally:
+        clk.__exit__(None, None, None)
 
     # ---- e2e: host buffers through lal_tail_step ----
     barrier()
