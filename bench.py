@@ -20,6 +20,9 @@ Reported:
   cpu_baseline  the reference's own C (oracle/_ref: quantize, |xq|, OpenMP
              LM head, lal_sample_token) on the host's cores, bounded sample
 
+Before the timed region: W warm-up steps through the public call, then about
+0.3 s of untimed device steps (the same count on every rank).
+
 Multi-GPU (torchrun, --gpus N): each rank owns a contiguous vocab slice
 (vocab-sharded, strong scaling: a step is the same B tokens at any N).
 """
