@@ -189,24 +189,6 @@ struct DevBuf {
     }
 };
 
-struct PinBuf {
-    void *p = nullptr;
-    size_t cap = 0;
-    int ensure(size_t bytes) {
-        if (bytes <= cap) return LAL_TAIL_OK;
-        if (p) cudaFreeHost(p);
-        p = nullptr;
-        cap = 0;
-        size_t want = bytes < 256 ? 256 : bytes;
-        CU(cudaMallocHost(&p, want));
-        cap = want;
-        return LAL_TAIL_OK;
-    }
-    ~PinBuf() {
-        if (p) cudaFreeHost(p);
-    }
-};
-
 /* Scratch of the select (global memory beyond inputs and outputs): the key
  * histogram, grid-barrier words, superset buffer, arrival ticket. */
 struct SelectScratch {
@@ -287,7 +269,6 @@ struct DropinState {
     cudaStream_t stream = nullptr;
     DevBuf x, xq, ax, logits, W, q, s;
     LaunchScratch ls;
-    PinBuf pin;
     ~DropinState() {
         if (stream) cudaStreamDestroy(stream);
     }

@@ -46,15 +46,6 @@ constexpr int kMergeHead = 4 * (kMaxRanks + 4);
 template <class Load>
 __device__ void merge_sample(const MergeParams &mp, int b, uint8_t *area, Misc *ms, Load load);
 
-__device__ __forceinline__ void st_release_sys(unsigned *p, unsigned v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p) {
-    unsigned v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-
 __device__ __forceinline__ void st_relaxed_sys_u64(uint64_t *p, uint64_t v) {
     asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
