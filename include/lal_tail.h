@@ -235,7 +235,9 @@ int lal_tail_fetch_tokens(lal_tail *t, int n_streams, int *tokens_out);
  * context's stream:
  *   1. lal_tail_shard_select: the fused kernel over this rank's slice writes,
  *      per stream, a candidate record (its tie-complete local top-k set, in
- *      ascending vocab order) into the send buffer;
+ *      ascending vocab order; when the set outgrows the record, its rows
+ *      above the slice's threshold plus a bitmap of the rows tied at it)
+ *      into the send buffer;
  *   2. the caller all-gathers bytes_per_rank bytes of the send buffer of
  *      every rank into the receive buffer, in rank order, on the context's
  *      stream (ncclAllGather or any equivalent);
@@ -252,7 +254,10 @@ int lal_tail_shard_select(lal_tail *t, const float *d_hidden, int n_streams);
  * waits -- bounded, LAL_TAIL_ERR_TIMEOUT after 2 s -- for every rank's
  * record of the step, merges them and draws.  Every rank must step in
  * lockstep (the step's sequence number is counted per context; connecting
- * again restarts it). */
+ * again restarts it).  lal_tail_exchange_handle clears the receive buffer
+ * before the handle is returned, so every rank must have exported its handle
+ * before any rank steps (gathering the handles is that point); connecting
+ * does not clear it again. */
 #define LAL_TAIL_IPC_HANDLE_BYTES 64
 int lal_tail_exchange_handle(lal_tail *t, void *handle_out);
 int lal_tail_connect_peers(lal_tail *t, const void *handles);

@@ -32,7 +32,7 @@ NVFLAGS = ["-O3", "-std=c++17", "-lineinfo", "-fmad=false", "-Xcompiler",
 
 CU_SOURCES = ["tail_kernels.cu", "tail_batch.cu", "tail_gpt2.cu", "tail_api.cu",
               "tail_noalloc.cu"]
-HEADERS = ["tail_internal.h", "tail_device.cuh", "lal_expf.h", "../../include/lal_tail.h",
+HEADERS = ["tail_internal.h", "tail_device.cuh", "tail_wide.cuh", "lal_expf.h", "../../include/lal_tail.h",
            "../../include/runtime/lal_q8_kernel.h", "../../include/runtime/lal_sampling.h"]
 
 

@@ -835,7 +835,7 @@ struct lal_tail {
      * of every rank's buffer, the peers' opened mappings, the step counter */
     uint8_t *x_peer = nullptr;
     uint8_t **d_peer = nullptr;
-    int peer_rec_bytes = 0; /* 64-bit words: 2 header + 2 per candidate */
+    int peer_rec_bytes = 0; /* peer_record_bytes(rec_cap, largest slice) */
     std::vector<void *> peer_open;
     bool p2p = false;
     unsigned seq = 1;
@@ -1031,10 +1031,12 @@ int ctx_alloc(lal_tail *t) {
         return fail(LAL_TAIL_ERR_UNSUPPORTED, "fused tail: shape V=%d d=%d k=%d unsupported (plan %d)",
                     c.vocab_size, d, c.max_top_k, t->grid);
     /* candidate records of the sharded step: a slice exports its
-     * tie-complete set, k entries plus room for ties at its threshold */
+     * tie-complete set, k entries plus room for ties at its threshold, or in
+     * the wide form its rows above its threshold and a bitmap of its ties */
     const int want = (std::min(c.max_top_k, c.vocab_size) + 64 + 3) / 4 * 4;
     t->rec_cap = std::min(want, (t->nrows + 3) / 4 * 4);
-    t->rec_bytes = shard_record_bytes(t->rec_cap);
+    const int rows_max = shard_rows_max(c.vocab_size, c.shard_count);
+    t->rec_bytes = shard_record_bytes(t->rec_cap, rows_max);
     t->merge_cap = merge_smem_cap(c.shard_count * t->rec_cap);
     if (t->merge_cap < 1)
         return fail(LAL_TAIL_ERR_UNSUPPORTED,
@@ -1045,7 +1047,7 @@ int ctx_alloc(lal_tail *t) {
     CU(cudaMalloc(&t->x_recv, (size_t)c.shard_count * B * t->rec_bytes));
     CU(cudaMemset(t->x_recv, 0, (size_t)c.shard_count * B * t->rec_bytes));
     if (c.shard_count > 1) {
-        t->peer_rec_bytes = 16 + 16 * t->rec_cap;
+        t->peer_rec_bytes = peer_record_bytes(t->rec_cap, rows_max);
         const size_t pb = 2ull * c.shard_count * t->peer_rec_bytes;
         CU(cudaMalloc(&t->x_peer, pb));
         CU(cudaMemset(t->x_peer, 0, pb));
@@ -1686,6 +1688,12 @@ int lal_tail_exchange_handle(lal_tail *t, void *handle_out) {
     if (!handle_out) return fail(LAL_TAIL_ERR_ARG, "exchange_handle: null");
     if (!t->x_peer) return fail(LAL_TAIL_ERR_STATE, "exchange_handle: context is not sharded");
     static_assert(sizeof(cudaIpcMemHandle_t) == LAL_TAIL_IPC_HANDLE_BYTES, "IPC handle size");
+    /* the receive buffer starts clean before any peer can learn its address:
+     * a peer that connects first and steps at once then writes into a buffer
+     * that no later clear can erase */
+    CU(cudaStreamSynchronize(t->stream));
+    CU(cudaMemsetAsync(t->x_peer, 0, 2ull * t->cfg.shard_count * t->peer_rec_bytes, t->stream));
+    CU(cudaStreamSynchronize(t->stream));
     cudaIpcMemHandle_t h;
     CU(cudaIpcGetMemHandle(&h, t->x_peer));
     memcpy(handle_out, &h, sizeof(h));
@@ -1719,8 +1727,11 @@ int lal_tail_connect_peers(lal_tail *t, const void *handles) {
         t->peer_open.push_back(q);
         ptrs[r] = (uint8_t *)q;
     }
-    CU(cudaMemcpy(t->d_peer, ptrs.data(), sizeof(uint8_t *) * N, cudaMemcpyHostToDevice));
-    CU(cudaMemset(t->x_peer, 0, 2ull * N * t->peer_rec_bytes));
+    CU(cudaMemcpyAsync(t->d_peer, ptrs.data(), sizeof(uint8_t *) * N, cudaMemcpyHostToDevice,
+                       t->stream));
+    CU(cudaStreamSynchronize(t->stream));
+    /* (the receive buffer was cleared by lal_tail_exchange_handle, before its
+     * handle left this rank) */
     t->seq = 1;
     t->p2p = true;
     return LAL_TAIL_OK;

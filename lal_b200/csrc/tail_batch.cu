@@ -37,6 +37,7 @@
  * producer waits for its copies in flight before the CTA exits.
  */
 #include "tail_device.cuh"
+#include "tail_wide.cuh"
 
 #include <cuda.h>
 
@@ -371,9 +372,46 @@ struct BatchSelectParams {
     int s_cap, c_cap, h_slots; /* superset, candidate and hash capacities */
     const uint32_t *gmax;      /* [B][n_groups] raw group maxima (GEMM) */
     int n_groups;
+    int wide_cap;              /* explicit rows of the wide path (>= max k - 1) */
 };
 
 constexpr uint32_t kEmptySlot = 0xFFFFFFFFu;
+
+/* The wide path (tail_wide.cuh) of stream b, whose candidates did not fit
+ * the select's shared memory or whose shard set did not fit its record: the
+ * exact select over the stream's penalised logits, then the draw or the
+ * record's wide form. */
+__device__ __noinline__ void batch_wide(const BatchSelectParams &p, int b, int k, bool greedy,
+                                        float temp, float u0, int hn, int hhead, uint8_t *area,
+                                        Misc *ms) {
+    WideDense a = {};
+    a.lg = p.logits + (size_t)b * p.rows;
+    a.rows = p.rows;
+    a.row_base = p.row_base;
+    a.vocab = p.vocab;
+    a.k = k;
+    a.variant = p.variant;
+    a.greedy = greedy ? 1 : 0;
+    a.temp = temp;
+    a.u = u0;
+    a.cap = max(1, p.wide_cap);
+    a.ex = ExpfTables{p.expf_x, p.expf_y, p.expf_bits, p.expf_off, nullptr, 0};
+    a.diag = p.diag + b;
+    if (p.shard_out != nullptr) {
+        a.rec = p.shard_out + (size_t)b * p.rec_bytes;
+        a.rec_cap = p.rec_cap;
+    } else {
+        a.token = p.tokens + b;
+        a.hist_ids = p.hist_ids + (size_t)b * p.hist_stride;
+        a.hist_n = p.hist_n + b;
+        a.hist_head = p.hist_head + b;
+        a.hist_cap = p.hist_cap;
+        a.push_history = p.push_history;
+        a.hn = hn;
+        a.hhead = hhead;
+    }
+    wide_dense(a, area, ms);
+}
 
 
 __global__ void __launch_bounds__(NT, 1) batch_select_kernel(const __grid_constant__ BatchSelectParams p) {
@@ -495,20 +533,6 @@ __global__ void __launch_bounds__(NT, 1) batch_select_kernel(const __grid_consta
     dg.greedy = greedy ? 1 : 0;
     dg.drew = 0;
     dg.token = -1;
-    auto fail_stream = [&](int st) {
-        if (tid == 0) {
-            if (p.shard_out != nullptr) {
-                ShardRecordHead *h =
-                    reinterpret_cast<ShardRecordHead *>(p.shard_out + (size_t)b * p.rec_bytes);
-                h->count = 0;
-                h->status = st;
-            } else {
-                atomicCAS(p.status, 0, st);
-                p.tokens[b] = -1;
-            }
-            p.diag[b] = dg;
-        }
-    };
 
     /* 3. a tie-complete superset of {l >= T}: keys >= a lower bound L of T.
      *
@@ -639,7 +663,7 @@ __global__ void __launch_bounds__(NT, 1) batch_select_kernel(const __grid_consta
             __syncthreads();
             S = s_count;
             if (S > p.s_cap) {
-                fail_stream((int)DEV_CAPACITY);
+                batch_wide(p, b, k, greedy, temp, u0, hn, hhead, bsm, ms);
                 return;
             }
         }
@@ -694,7 +718,7 @@ __global__ void __launch_bounds__(NT, 1) batch_select_kernel(const __grid_consta
     L = prefix;
     S = (int)(above + cnt);
     if (S > p.s_cap) {
-        fail_stream((int)DEV_CAPACITY);
+        batch_wide(p, b, k, greedy, temp, u0, hn, hhead, bsm, ms);
         return;
     }
 
@@ -776,8 +800,8 @@ __global__ void __launch_bounds__(NT, 1) batch_select_kernel(const __grid_consta
     const int m = (int)mt;
     dg.threshold = key2f(T);
     dg.n_cand = m;
-    if (m < 1 || m > p.c_cap) {
-        fail_stream((int)DEV_CAPACITY);
+    if (m < 1 || m > p.c_cap || (p.shard_out != nullptr && m > p.rec_cap)) {
+        batch_wide(p, b, k, greedy, temp, u0, hn, hhead, bsm, ms);
         return;
     }
     for (int e = e0; e < e1; ++e)
@@ -830,15 +854,15 @@ __global__ void __launch_bounds__(NT, 1) batch_select_kernel(const __grid_consta
         ShardRecordHead *h = reinterpret_cast<ShardRecordHead *>(rec);
         float *rv = reinterpret_cast<float *>(rec + sizeof(ShardRecordHead));
         int *ri = reinterpret_cast<int *>(rv + p.rec_cap);
-        const bool fits = m <= p.rec_cap;
-        if (fits)
-            for (int i = tid; i < m; i += NT) {
-                rv[i] = Ov[i];
-                ri[i] = Oi[i];
-            }
+        for (int i = tid; i < m; i += NT) {
+            rv[i] = Ov[i];
+            ri[i] = Oi[i];
+        }
         if (tid == 0) {
-            h->count = fits ? m : 0;
-            h->status = fits ? 0 : (int)DEV_CAPACITY;
+            h->count = m;
+            h->status = 0;
+            h->ties = 0;
+            h->tkey = 0u;
             p.diag[b] = dg;
         }
         return;
@@ -983,8 +1007,11 @@ int batch_plan(BatchPlan &bp, const int8_t *W, const float *scale_w, int rows, i
     int hs = 64;
     while (hs < 2 * std::max(1, hist_cap)) hs <<= 1;
     bp.h_slots = hs;
+    bp.wide_cap = std::max(1, std::min(max_top_k, rows));
     if (batch_select_smem(bp.s_cap, bp.c_cap, bp.h_slots, bp.n_groups) >
-        (size_t)(kGemmSmemLimit - 8192))
+            (size_t)(kGemmSmemLimit - 8192) ||
+        batch_select_smem(bp.s_cap, bp.c_cap, bp.h_slots, bp.n_groups) <
+            (size_t)wide_area_bytes(bp.wide_cap))
         return -2;
     return 0;
 }
@@ -1081,6 +1108,7 @@ cudaError_t batch_launch(BatchPlan &bp, const BatchStep &s, cudaStream_t st) {
     q.h_slots = bp.h_slots;
     q.gmax = bp.gmax;
     q.n_groups = bp.n_groups;
+    q.wide_cap = bp.wide_cap;
     const size_t ssmem = batch_select_smem(bp.s_cap, bp.c_cap, bp.h_slots, bp.n_groups);
     e = raise_smem((const void *)batch_select_kernel, kGemmSmemLimit - 8192);
     if (e != cudaSuccess) return e;

@@ -67,7 +67,10 @@ constexpr int kGpt2RerankN = 512;
 constexpr int kGpt2SelThreads = 1024;
 constexpr int kGpt2MaxV = 51200;
 
-/* Device status word values (mirrors LAL_TAIL_ERR_* in include/lal_tail.h). */
+/* Device status word values (mirrors LAL_TAIL_ERR_* in include/lal_tail.h).
+ * DEV_CAPACITY remains for a merge whose gathered entries exceed the
+ * capacity it was built with (the selects and the merge otherwise take the
+ * wide path, tail_wide.cuh). */
 enum DevStatus : int { DEV_OK = 0, DEV_TIMEOUT = 4, DEV_CAPACITY = 5 };
 
 /* Per-stream outputs of a sampling launch (same layout as lal_tail_diag). */
@@ -77,18 +80,45 @@ struct StreamDiag {
 };
 
 /* Vocab-sharded step: the candidate record one shard exports per stream.
- * A 16-byte header, then cap values and cap global vocab indices, ascending
- * index order: the shard's tie-complete set {l >= T_shard}, T_shard its own
- * k-th largest penalised logit.  Every global candidate {l >= T} lies in
- * some shard's set (T >= T_shard), so the union of the records carries the
- * whole step. */
+ * A 32-byte header, then cap values and cap global vocab indices in
+ * ascending index order, then a bitmap of the shard's rows.  Every global
+ * candidate {l >= T} lies in its shard's set {l >= T_shard} (T >= T_shard,
+ * T_shard the shard's own k-th largest penalised logit), so the union of the
+ * records carries the whole step.  Two forms:
+ *   - list form (ties == 0): the entries are the whole set {l >= T_shard};
+ *   - wide form (ties > 0), when the set does not fit cap entries: the
+ *     entries are the rows l > T_shard (fewer than k), and bit j of the
+ *     bitmap marks local row j when its logit equals T_shard (`ties` rows;
+ *     tkey is T_shard's order key). */
 struct ShardRecordHead {
-    int count;        /* candidates in the record                             */
+    int count;        /* entries in the record                                */
     int status;       /* DEV_* of the shard's launch (0 = ok)                 */
     unsigned seq;     /* step sequence number (peer exchange)                 */
-    int pad;
+    int ties;         /* 0: list form; else the rows equal to T_shard         */
+    uint32_t tkey;    /* wide form: T_shard as an order key                   */
+    int pad[3];
 };
-inline int shard_record_bytes(int cap) { return 16 + 8 * cap; }
+static_assert(sizeof(ShardRecordHead) == 32, "record header layout");
+/* rows of the largest slice of a vocabulary split n ways */
+inline int shard_rows_max(int vocab, int n) {
+    int m = 0;
+    for (int r = 0; r < n; ++r) {
+        const int a = (int)((long long)r * vocab / n), b = (int)((long long)(r + 1) * vocab / n);
+        if (b - a > m) m = b - a;
+    }
+    return m;
+}
+inline int shard_bitmap_words(int rows) { return (rows + 31) / 32; }
+/* bytes of a gathered record (16-byte multiple) */
+inline int shard_record_bytes(int cap, int rows_max) {
+    return (32 + 8 * cap + 4 * shard_bitmap_words(rows_max) + 15) / 16 * 16;
+}
+/* bytes of a peer-exchange record: 64-bit words tagged with the step's
+ * sequence number -- count, status, ties, T_shard key, then (value, vocab
+ * index) per entry, then the bitmap words after cap entries */
+inline int peer_record_bytes(int cap, int rows_max) {
+    return 8 * (4 + 2 * cap + shard_bitmap_words(rows_max));
+}
 
 /* Merge of the gathered records of one stream (one CTA per stream): the
  * records of stream b from rank r are at recv + (r * rank_stride +
@@ -272,6 +302,7 @@ struct BatchPlan {
     uint32_t *gmax;    /* [256][n_groups] raw maxima of 32-row groups, per stream */
     int n_groups;
     int s_cap, c_cap, h_slots;
+    int wide_cap; /* explicit rows of the select's wide path */
     /* TMA descriptors (CUtensorMap, 128 bytes each): W, and X for N = 32..256 */
     alignas(64) unsigned char tm_w[128];
     alignas(64) unsigned char tm_x[8][128];

@@ -31,6 +31,7 @@
  * softmax weights use lal_expf_glibc (lal_expf.h), equal to glibc expf.
  */
 #include "tail_device.cuh"
+#include "tail_wide.cuh"
 
 #include <algorithm>
 #include <cstdio>
@@ -42,7 +43,17 @@
 namespace lal {
 namespace {
 
-constexpr int kMergeHead = 4 * (kMaxRanks + 4);
+/* The head of the merge's shared-memory area: per-rank offsets of the
+ * gathered entries, the load's failure word, and each record's form. */
+struct MergeHead {
+    int roff[kMaxRanks + 1]; /* prefix offsets of the records' entries        */
+    int rbad;                /* DEV_* failure of the load, or 0               */
+    int wide;                /* some record is in the wide form               */
+    int rties[kMaxRanks];    /* each record's ties (0: list form)             */
+    uint32_t rtkey[kMaxRanks]; /* each wide record's T_shard key              */
+    int pad;
+};
+constexpr int kMergeHead = (int)((sizeof(MergeHead) + 15) / 16 * 16);
 template <class Load>
 __device__ void merge_sample(const MergeParams &mp, int b, uint8_t *area, Misc *ms, Load load);
 
@@ -58,10 +69,12 @@ __device__ __forceinline__ uint64_t ld_relaxed_sys_u64(const uint64_t *p) {
 /* Peer exchange of the sharded step.  A record slot in a rank's receive
  * buffer ([2 parities][n_ranks][rec_bytes]) is a run of 64-bit words whose
  * high half is the step's sequence number: [count | seq], [status | seq],
- * then per candidate [value bits | seq], [vocab id | seq].  A 64-bit store is
- * single-copy atomic, so a reader that sees seq in a word has that word's
- * data: no fence orders the data before a flag, and a stale word (a step
- * two back, same parity) never matches. */
+ * [ties | seq], [T_shard key | seq], then per entry [value bits | seq],
+ * [vocab id | seq], and after rec_cap entries the wide form's bitmap words
+ * [word | seq] (peer_record_bytes).  A 64-bit store is single-copy atomic, so
+ * a reader that sees seq in a word has that word's data: no fence orders the
+ * data before a flag, and a stale word (a step two back, same parity) never
+ * matches.  This writes the list form (ties 0), or a failure record. */
 __device__ void peer_publish(const TailParams &p, int status, int m, const float *Ov,
                              const int *Oi) {
     const size_t slot = ((size_t)(p.seq & 1u) * p.n_ranks + p.rank) * p.rec_bytes;
@@ -71,13 +84,15 @@ __device__ void peer_publish(const TailParams &p, int status, int m, const float
         uint64_t *w = reinterpret_cast<uint64_t *>(p.peer_recv[r] + slot);
         if (fits)
             for (int i = threadIdx.x; i < m; i += NT) {
-                st_relaxed_sys_u64(w + 2 + 2 * i, hi | __float_as_uint(Ov[i]));
-                st_relaxed_sys_u64(w + 3 + 2 * i, hi | (uint32_t)Oi[i]);
+                st_relaxed_sys_u64(w + 4 + 2 * i, hi | __float_as_uint(Ov[i]));
+                st_relaxed_sys_u64(w + 5 + 2 * i, hi | (uint32_t)Oi[i]);
             }
         if (threadIdx.x == 0) {
             st_relaxed_sys_u64(w + 0, hi | (uint32_t)(fits ? m : 0));
             st_relaxed_sys_u64(w + 1, hi | (uint32_t)(fits ? 0 : (status != 0 ? status
                                                                           : (int)DEV_CAPACITY)));
+            st_relaxed_sys_u64(w + 2, hi);
+            st_relaxed_sys_u64(w + 3, hi);
         }
     }
 }
@@ -96,53 +111,74 @@ __device__ __forceinline__ bool poll_word(const uint64_t *w, uint32_t seq, uint6
     }
 }
 
+/* The four header words of a peer record, loaded together until every one
+ * carries this step's sequence number (bounded by deadline). */
+__device__ __forceinline__ bool poll_head4(const uint64_t *w, uint32_t seq, uint64_t deadline,
+                                           uint64_t *v) {
+    for (uint32_t it = 0;; ++it) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) v[q] = ld_relaxed_sys_u64(w + q);
+        bool all = true;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) all = all && (uint32_t)(v[q] >> 32) == seq;
+        if (all) return true;
+        if ((it & 15u) == 15u && gtimer() > deadline) return false;
+    }
+}
+
 /* Loader of the peers' records in this rank's own receive buffer. */
 struct PeerRecords {
     const TailParams &p;
     Misc *ms;
-    __device__ void operator()(int *roff, int &rbad, uint32_t *Mk, int *Mi, int cap,
+    __device__ const uint64_t *rec(int r) const {
+        return reinterpret_cast<const uint64_t *>(
+            p.peer_recv[p.rank] + ((size_t)(p.seq & 1u) * p.n_ranks + r) * p.rec_bytes);
+    }
+    __device__ void operator()(MergeHead &hd, uint32_t *Mk, int *Mi, int cap,
                                float *scratch) const {
         const int tid = threadIdx.x;
-        const uint8_t *base = p.peer_recv[p.rank] + (size_t)(p.seq & 1u) * p.n_ranks * p.rec_bytes;
         const uint64_t deadline = gtimer() + kWaitNs;
         int *rstat = reinterpret_cast<int *>(scratch);
         if (tid == 0) ms->found = 1;
         __syncthreads();
         if (tid < p.n_ranks) {
-            const uint64_t *w = reinterpret_cast<const uint64_t *>(base + (size_t)tid * p.rec_bytes);
-            uint64_t v0 = 0, v1 = 0;
-            if (poll_word(w, p.seq, deadline, &v0) && poll_word(w + 1, p.seq, deadline, &v1)) {
-                roff[tid] = (int)(uint32_t)v0;
-                rstat[tid] = (int)(uint32_t)v1;
+            uint64_t v[4];
+            if (poll_head4(rec(tid), p.seq, deadline, v)) {
+                hd.roff[tid] = (int)(uint32_t)v[0];
+                rstat[tid] = (int)(uint32_t)v[1];
+                hd.rties[tid] = (int)(uint32_t)v[2];
+                hd.rtkey[tid] = (uint32_t)v[3];
             } else {
                 ms->found = 0;
             }
         }
         __syncthreads();
         if (tid == 0) {
-            int acc = 0, st = ms->found ? 0 : (int)DEV_TIMEOUT;
+            int acc = 0, st = ms->found ? 0 : (int)DEV_TIMEOUT, wide = 0;
             for (int r = 0; r < p.n_ranks && st == 0; ++r) {
-                const int c = roff[r], s = rstat[r];
+                const int c = hd.roff[r], s = rstat[r];
                 if (s != 0) st = s;
-                else if (c < 0 || c > p.rec_cap) st = DEV_CAPACITY;
-                roff[r] = acc;
+                else if (c < 0 || c > p.rec_cap || hd.rties[r] < 0) st = DEV_CAPACITY;
+                if (hd.rties[r] > 0) wide = 1;
+                hd.roff[r] = acc;
                 acc += c;
             }
-            roff[p.n_ranks] = acc;
-            if ((acc < 1 || acc > cap) && st == 0) st = DEV_CAPACITY;
-            rbad = st;
+            hd.roff[p.n_ranks] = acc;
+            if ((acc > cap || (acc < 1 && !wide)) && st == 0) st = DEV_CAPACITY;
+            hd.rbad = st;
+            hd.wide = wide;
         }
         __syncthreads();
-        if (rbad != 0) return;
-        const int M = roff[p.n_ranks];
+        if (hd.rbad != 0) return;
+        const int M = hd.roff[p.n_ranks];
         for (int e = tid; e < M; e += NT) {
             int r = 0;
-            while (roff[r + 1] <= e) ++r;
-            const int j = e - roff[r];
-            const uint64_t *w = reinterpret_cast<const uint64_t *>(base + (size_t)r * p.rec_bytes);
+            while (hd.roff[r + 1] <= e) ++r;
+            const int j = e - hd.roff[r];
+            const uint64_t *w = rec(r);
             uint64_t v = 0, x = 0;
-            if (poll_word(w + 2 + 2 * j, p.seq, deadline, &v) &&
-                poll_word(w + 3 + 2 * j, p.seq, deadline, &x)) {
+            if (poll_word(w + 4 + 2 * j, p.seq, deadline, &v) &&
+                poll_word(w + 5 + 2 * j, p.seq, deadline, &x)) {
                 Mk[e] = f2key(__uint_as_float((uint32_t)v));
                 Mi[e] = (int)(uint32_t)x;
             } else {
@@ -150,10 +186,101 @@ struct PeerRecords {
             }
         }
         __syncthreads();
-        if (tid == 0 && !ms->found) rbad = DEV_TIMEOUT;
+        if (tid == 0 && !ms->found) hd.rbad = DEV_TIMEOUT;
         __syncthreads();
     }
+    /* nw bitmap words of rank r's wide record from word w0 (every thread);
+     * a word that does not arrive in time clears ms->sh[12] */
+    __device__ void bitmap(int r, int w0, int nw, uint32_t *dst) const {
+        const uint64_t *w = rec(r) + 4 + 2 * p.rec_cap + w0;
+        const uint64_t deadline = gtimer() + kWaitNs;
+        for (int i = threadIdx.x; i < nw; i += NT) {
+            uint64_t v = 0;
+            if (poll_word(w + i, p.seq, deadline, &v)) dst[i] = (uint32_t)v;
+            else {
+                dst[i] = 0u;
+                ms->sh[12] = 0u;
+            }
+        }
+    }
 };
+
+/* The peer exchange's merge of this step (the fused kernel's last CTA, after
+ * it published its record): wait for every rank's record, merge and draw
+ * like merge_kernel. */
+__device__ __noinline__ void peer_merge(const TailParams &p, uint8_t *smem, Misc *ms) {
+    MergeParams mp;
+    mp.recv = p.peer_recv[p.rank] + (size_t)(p.seq & 1u) * p.n_ranks * p.rec_bytes;
+    mp.rank_stride = p.rec_bytes;
+    mp.rec_bytes = p.rec_bytes;
+    mp.rec_cap = p.rec_cap;
+    mp.n_ranks = p.n_ranks;
+    mp.vocab = p.vocab;
+    mp.variant = p.variant;
+    mp.temperature = p.temperature;
+    mp.top_k = p.top_k;
+    mp.u = p.u;
+    mp.hist_ids = p.hist_ids;
+    mp.hist_n = p.hist_n;
+    mp.hist_head = p.hist_head;
+    mp.hist_cap = p.hist_cap;
+    mp.push_history = p.push_history;
+    mp.tokens = p.tokens;
+    mp.diag = p.diag;
+    mp.status = p.status;
+    mp.expf_x = p.expf_x;
+    mp.expf_y = p.expf_y;
+    mp.expf_n = p.expf_n;
+    mp.expf_bits = p.expf_bits;
+    mp.expf_off = p.expf_off;
+    mp.expf_hash = p.expf_hash;
+    mp.expf_hash_probe = p.expf_hash_probe;
+    mp.smem_cap = (p.area_bytes - kMergeHead - kWideWalkBytes) / 24;
+    merge_sample(mp, 0, smem, ms, PeerRecords{p, ms});
+}
+
+/* The wide path (tail_wide.cuh) of a launch whose candidates did not fit the
+ * fast select: the exact select over this launch's logits in global memory
+ * (every CTA wrote its rows before its ticket), then the launch's own output
+ * -- the draw, the shard record in its wide form, or the candidate export.
+ * k is the launch's effective k; hn / hhead the history ring's words. */
+__device__ __noinline__ void tail_wide(const TailParams &p, int k, bool greedy, float temp,
+                                       float u0, int hn, int hhead, uint8_t *smem, Misc *ms) {
+    WideDense a;
+    a.lg = p.logits;
+    a.rows = p.rows;
+    a.row_base = p.row_base;
+    a.vocab = p.vocab;
+    a.k = k;
+    a.variant = p.variant;
+    a.greedy = greedy ? 1 : 0;
+    a.temp = temp;
+    a.u = u0;
+    a.cap = max(1, p.max_k);
+    a.ex = ExpfTables{p.expf_x, p.expf_y, p.expf_bits, p.expf_off, p.expf_hash,
+                      p.expf_hash_probe};
+    a.token = p.tokens;
+    a.diag = p.diag;
+    a.hist_ids = p.hist_ids;
+    a.hist_n = p.hist_n;
+    a.hist_head = p.hist_head;
+    a.hist_cap = p.hist_cap;
+    a.push_history = p.push_history;
+    a.hn = hn;
+    a.hhead = hhead;
+    a.rec = p.shard_out;
+    a.rec_cap = p.rec_cap;
+    a.peer_recv = p.peer_recv;
+    a.n_ranks = p.n_ranks;
+    a.rank = p.rank;
+    a.rec_bytes = p.rec_bytes;
+    a.seq = p.seq;
+    a.cand_val = p.cand_val_out;
+    a.cand_idx = p.cand_idx_out;
+    a.cand_cap = p.cand_val_out ? p.cand_out_cap : 0;
+    a.candidates_only = p.candidates_only;
+    wide_dense(a, smem, ms);
+}
 
 /* ----------------------------------------------------- the kernel --- */
 template <int MODE, int NCH>
@@ -952,6 +1079,18 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
         *p.gL = 0u;
         p.counter[0] = 0u;
     }
+    /* ties (or a superset) beyond the fast path's shared memory, or a
+     * slice's set beyond its record: the exact wide path */
+    const bool shard_wide = fine && (p.peer_recv != nullptr || p.shard_out != nullptr) &&
+                            m > p.rec_cap;
+    if ((!fine && ok && dev_status == 0) || shard_wide) {
+        tail_wide(p, k, greedy, temp, u0, hn, hhead, smem, ms);
+        if (p.peer_recv != nullptr) {
+            __syncthreads();
+            peer_merge(p, smem, ms);
+        }
+        return;
+    }
     if (!fine) {
         /* a failed slice still publishes (a failure record): the peers fail
          * the step at once instead of waiting */
@@ -1032,51 +1171,24 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
         peer_publish(p, 0, m, Ov, Oi);
         __syncthreads(); /* Ov / Oi are read before the merge reuses the area */
         if (tid == 0) stamp(p, G * 8 + 5);
-        MergeParams mp;
-        mp.recv = p.peer_recv[p.rank] + (size_t)(p.seq & 1u) * p.n_ranks * p.rec_bytes;
-        mp.rank_stride = p.rec_bytes;
-        mp.rec_bytes = p.rec_bytes;
-        mp.rec_cap = p.rec_cap;
-        mp.n_ranks = p.n_ranks;
-        mp.vocab = p.vocab;
-        mp.variant = p.variant;
-        mp.temperature = p.temperature;
-        mp.top_k = p.top_k;
-        mp.u = p.u;
-        mp.hist_ids = p.hist_ids;
-        mp.hist_n = p.hist_n;
-        mp.hist_head = p.hist_head;
-        mp.hist_cap = p.hist_cap;
-        mp.push_history = p.push_history;
-        mp.tokens = p.tokens;
-        mp.diag = p.diag;
-        mp.status = p.status;
-        mp.expf_x = p.expf_x;
-        mp.expf_y = p.expf_y;
-        mp.expf_n = p.expf_n;
-        mp.expf_bits = p.expf_bits;
-        mp.expf_off = p.expf_off;
-        mp.expf_hash = p.expf_hash;
-        mp.expf_hash_probe = p.expf_hash_probe;
-        mp.smem_cap = (p.area_bytes - kMergeHead) / 24;
-        merge_sample(mp, 0, smem, ms, PeerRecords{p, ms});
+        peer_merge(p, smem, ms);
         if (tid == 0) stamp(p, G * 8 + 7);
         return;
     }
     if (p.shard_out != nullptr) {
-        /* vocab-sharded step: this slice's record; the merge draws */
+        /* vocab-sharded step: this slice's record (list form); the merge draws */
         ShardRecordHead *h = reinterpret_cast<ShardRecordHead *>(p.shard_out);
         float *rv = reinterpret_cast<float *>(p.shard_out + sizeof(ShardRecordHead));
         int *ri = reinterpret_cast<int *>(rv + p.rec_cap);
-        const bool fits = m <= p.rec_cap;
-        if (fits)
-            for (int i = tid; i < m; i += NT) {
-                rv[i] = Ov[i];
-                ri[i] = Oi[i];
-            }
+        for (int i = tid; i < m; i += NT) {
+            rv[i] = Ov[i];
+            ri[i] = Oi[i];
+        }
         if (tid == 0) {
-            h->count = fits ? m : 0;
-            h->status = fits ? 0 : (int)DEV_CAPACITY;
+            h->count = m;
+            h->status = 0;
+            h->ties = 0;
+            h->tkey = 0u;
             p.diag[0] = dg;
         }
         return;
@@ -1327,20 +1439,120 @@ __global__ void debug_expf_kernel(const float *x, float *y, int n, const uint32_
  * the concatenation is in ascending vocab order, the order of the
  * reference's sequential softmax sums (runtime/lal_sampling.h:110-124).
  * Every rank runs the same merge on the same bytes and gets the same token. */
-/* (kMergeHead: bytes of the merge's shared-memory area before its candidate
- * arrays -- the per-rank offsets and the failure word.) */
+/* The history push of a merged stream (runtime/lal_sampling.h:133-136 as a
+ * ring: FIFO at hist_cap). */
+__device__ __forceinline__ void merge_push(const MergeParams &mp, int b, int token, int hn,
+                                           int hhead) {
+    if (mp.push_history && mp.hist_cap > 0) {
+        int *ids = mp.hist_ids + (size_t)b * mp.hist_cap;
+        if (hn < mp.hist_cap) {
+            ids[hn] = token;
+            mp.hist_n[b] = hn + 1;
+        } else {
+            ids[hhead] = token;
+            mp.hist_head[b] = (hhead + 1) % mp.hist_cap;
+        }
+    }
+}
+
+/* The merge when some record is in the wide form (tail_wide.cuh): T is the
+ * k-th largest of the entries and of every wide record's ties (each T_shard
+ * counted `ties` times); the candidates are the entries >= T and the ties of
+ * the records whose T_shard equals T; the walk adds their weights record by
+ * record in rank order, a record's entries and bitmap rows in ascending
+ * index order. */
+template <class Load>
+__device__ void merge_wide(const MergeParams &mp, int b, MergeHead &hd, const uint32_t *Mk,
+                           const int *Mi, float *Mw, uint8_t *walk, Misc *ms, const Load &load,
+                           StreamDiag dg, bool greedy, float temp, int topk, float u0, int hn,
+                           int hhead) {
+    const int tid = threadIdx.x;
+    const int M = hd.roff[mp.n_ranks];
+    uint32_t total = (uint32_t)M;
+    for (int r = 0; r < mp.n_ranks; ++r) total += (uint32_t)hd.rties[r];
+    uint32_t k = greedy ? 1u : (uint32_t)max(topk, 1);
+    if (k > (uint32_t)mp.vocab) k = (uint32_t)mp.vocab;
+    if (k > total) k = total;
+    if (k < 1u) k = 1u;
+    uint32_t mk = 0u;
+    for (int e = tid; e < M; e += NT) mk = max(mk, Mk[e]);
+    if (tid < mp.n_ranks && hd.rties[tid] > 0) mk = max(mk, hd.rtkey[tid]);
+    const uint32_t top = block_max_u32(mk, ms);
+    const uint32_t T = block_kth_largest_w(
+        [&](int i, uint32_t &key, uint32_t &w) {
+            if (i < M) {
+                key = Mk[i];
+                w = 1u;
+                return true;
+            }
+            key = hd.rtkey[i - M];
+            w = (uint32_t)hd.rties[i - M];
+            return hd.rties[i - M] > 0;
+        },
+        M + mp.n_ranks, k, ms);
+    const float max_l = fmaxf(-1e30f, key2f(top));
+    const ExpfTables ex{mp.expf_x, mp.expf_y, mp.expf_bits, mp.expf_off, mp.expf_hash,
+                        mp.expf_hash_probe};
+    uint32_t c = 0u;
+    for (int e = tid; e < M; e += NT) {
+        Mw[e] = greedy ? 0.0f : ex.weight(key2f(Mk[e]), max_l, temp);
+        c += Mk[e] >= T;
+    }
+    uint32_t n_exp;
+    block_scan_excl(c, ms, &n_exp);
+    uint32_t n_tie = 0u;
+    for (int r = 0; r < mp.n_ranks; ++r)
+        if (hd.rties[r] > 0 && hd.rtkey[r] == T) n_tie += (uint32_t)hd.rties[r];
+    if (tid == 0) ms->fred[0] = greedy ? 0.0f : ex.weight(key2f(T), max_l, temp);
+    __syncthreads();
+    const float wT = ms->fred[0];
+    uint32_t *bm = reinterpret_cast<uint32_t *>(walk);
+    WideChunk *tab = reinterpret_cast<WideChunk *>(bm + kWideChunkWords);
+    const WalkResult res = wide_walk(
+        mp.n_ranks,
+        [&](int r) {
+            const int r0 = (int)((long long)r * mp.vocab / mp.n_ranks);
+            const int r1 = (int)((long long)(r + 1) * mp.vocab / mp.n_ranks);
+            const int o = hd.roff[r];
+            return WalkUnit{Mk + o, Mi + o, Mw + o, hd.roff[r + 1] - o,
+                            hd.rties[r] > 0 && hd.rtkey[r] == T, r0, r1 - r0};
+        },
+        [&](int r, int w0, int nw, uint32_t *dst) { load.bitmap(r, w0, nw, dst); }, T, wT,
+        greedy, u0, mp.variant, bm, tab, ms);
+    dg.threshold = key2f(T);
+    dg.max_l = max_l;
+    dg.n_cand = (int)(n_exp + n_tie);
+    dg.sum = greedy ? 0.0f : res.sum;
+    dg.r = res.r;
+    dg.drew = res.drew;
+    if (tid == 0) {
+        if (!res.ok) {
+            atomicCAS(mp.status, 0, (int)DEV_TIMEOUT);
+            mp.tokens[b] = -1;
+            mp.diag[b] = dg;
+        } else {
+            const int token = res.token >= 0 ? res.token : mp.vocab - 1;
+            dg.token = token;
+            mp.tokens[b] = token;
+            mp.diag[b] = dg;
+            merge_push(mp, b, token, hn, hhead);
+        }
+    }
+    __syncthreads();
+}
 
 /* The merge of stream b's N shard records and its draw, by one CTA (NT
  * threads): shared by merge_kernel (records all-gathered into global memory)
  * and the fused kernel's peer exchange (records written by the peers over
- * NVLink, polled word by word).  load() fills roff[0..n_ranks] (prefix
- * offsets), rbad (a DEV_* failure or 0) and the keys / vocab ids of the
- * concatenated records, ascending vocab order, then synchronises the CTA.
- * area: kMergeHead bytes + 24 bytes per candidate (mp.smem_cap of them). */
+ * NVLink, polled word by word).  load() fills the MergeHead (prefix offsets
+ * of the entries, a DEV_* failure or 0, each record's form) and the keys /
+ * vocab ids of the concatenated records' entries in ascending vocab order,
+ * then synchronises the CTA; load.bitmap() stages a wide record's bitmap.
+ * area: kMergeHead bytes + 24 bytes per entry (mp.smem_cap of them) +
+ * kWideWalkBytes. */
 template <class Load>
 __device__ void merge_sample(const MergeParams &mp, int b, uint8_t *area, Misc *ms, Load load) {
-    int *roff = reinterpret_cast<int *>(area);
-    int &rbad = roff[kMaxRanks + 1];
+    MergeHead &hd = *reinterpret_cast<MergeHead *>(area);
     const int tid = threadIdx.x;
     const int cap = mp.smem_cap;
     uint32_t *Mk = reinterpret_cast<uint32_t *>(area + kMergeHead);
@@ -1356,7 +1568,7 @@ __device__ void merge_sample(const MergeParams &mp, int b, uint8_t *area, Misc *
     const int hn = mp.hist_n ? mp.hist_n[b] : 0;
     const int hhead = mp.hist_head ? mp.hist_head[b] : 0;
     const bool greedy = (temp <= 0.0f) || (topk <= 0);
-    load(roff, rbad, Mk, Mi, cap, Ce);
+    load(hd, Mk, Mi, cap, Ce);
     StreamDiag dg;
     dg.threshold = 0.0f;
     dg.max_l = 0.0f;
@@ -1366,15 +1578,20 @@ __device__ void merge_sample(const MergeParams &mp, int b, uint8_t *area, Misc *
     dg.greedy = greedy ? 1 : 0;
     dg.drew = 0;
     dg.token = -1;
-    if (rbad != 0) {
+    if (hd.rbad != 0) {
         if (tid == 0) {
-            atomicCAS(mp.status, 0, rbad);
+            atomicCAS(mp.status, 0, hd.rbad);
             mp.tokens[b] = -1;
             mp.diag[b] = dg;
         }
         return;
     }
-    const int M = roff[mp.n_ranks];
+    if (hd.wide) {
+        merge_wide(mp, b, hd, Mk, Mi, Mw, area + kMergeHead + 24 * cap, ms, load, dg, greedy, temp,
+                   topk, u0, hn, hhead);
+        return;
+    }
+    const int M = hd.roff[mp.n_ranks];
     /* k = min(top_k, V) (runtime/lal_sampling.h:70-71), 1 for greedy; every
      * shard exported at least min(k, its rows) entries, so M >= k */
     int k = greedy ? 1 : topk;
@@ -1532,55 +1749,59 @@ __device__ void merge_sample(const MergeParams &mp, int b, uint8_t *area, Misc *
         dg.token = token;
         mp.tokens[b] = token;
         mp.diag[b] = dg;
-        if (mp.push_history && mp.hist_cap > 0) {
-            int *ids = mp.hist_ids + (size_t)b * mp.hist_cap;
-            if (hn < mp.hist_cap) {
-                ids[hn] = token;
-                mp.hist_n[b] = hn + 1;
-            } else {
-                ids[hhead] = token;
-                mp.hist_head[b] = (hhead + 1) % mp.hist_cap;
-            }
-        }
+        merge_push(mp, b, token, hn, hhead);
     }
 }
 
-/* Loader of all-gathered records (ShardRecordHead + values + ids) in global
- * memory: records of stream b from rank r at recv + r*rank_stride +
- * b*rec_bytes. */
+/* Loader of all-gathered records (ShardRecordHead + values + ids + bitmap)
+ * in global memory: records of stream b from rank r at recv + r*rank_stride
+ * + b*rec_bytes. */
 struct GatheredRecords {
     const MergeParams &mp;
     int b;
-    __device__ void operator()(int *roff, int &rbad, uint32_t *Mk, int *Mi, int cap,
-                               float *) const {
+    __device__ const uint8_t *rec(int r) const {
+        return mp.recv + r * mp.rank_stride + (long long)b * mp.rec_bytes;
+    }
+    __device__ void operator()(MergeHead &hd, uint32_t *Mk, int *Mi, int cap, float *) const {
         const int tid = threadIdx.x;
-        auto rec = [&](int r) { return mp.recv + r * mp.rank_stride + (long long)b * mp.rec_bytes; };
         if (tid == 0) {
-            int acc = 0, st = 0;
+            int acc = 0, st = 0, wide = 0;
             for (int r = 0; r < mp.n_ranks; ++r) {
                 const ShardRecordHead *h = reinterpret_cast<const ShardRecordHead *>(rec(r));
                 const int c = __ldcg(&h->count), s = __ldcg(&h->status);
+                const int ties = __ldcg(&h->ties);
                 if (s != 0 && st == 0) st = s;
-                if ((c < 0 || c > mp.rec_cap) && st == 0) st = DEV_CAPACITY;
-                roff[r] = acc;
-                acc += (c < 0 || c > mp.rec_cap) ? 0 : c;
+                const bool bad = c < 0 || c > mp.rec_cap || ties < 0;
+                if (bad && st == 0) st = DEV_CAPACITY;
+                hd.rties[r] = bad ? 0 : ties;
+                hd.rtkey[r] = __ldcg(&h->tkey);
+                if (!bad && ties > 0) wide = 1;
+                hd.roff[r] = acc;
+                acc += bad ? 0 : c;
             }
-            roff[mp.n_ranks] = acc;
-            if ((acc < 1 || acc > cap) && st == 0) st = DEV_CAPACITY;
-            rbad = st;
+            hd.roff[mp.n_ranks] = acc;
+            if ((acc > cap || (acc < 1 && !wide)) && st == 0) st = DEV_CAPACITY;
+            hd.rbad = st;
+            hd.wide = wide;
         }
         __syncthreads();
-        if (rbad != 0) return;
+        if (hd.rbad != 0) return;
         for (int r = 0; r < mp.n_ranks; ++r) {
-            const int c = roff[r + 1] - roff[r];
+            const int c = hd.roff[r + 1] - hd.roff[r];
             const float *rv = reinterpret_cast<const float *>(rec(r) + sizeof(ShardRecordHead));
             const int *ri = reinterpret_cast<const int *>(rv + mp.rec_cap);
             for (int i = tid; i < c; i += NT) {
-                Mk[roff[r] + i] = f2key(__ldcg(rv + i));
-                Mi[roff[r] + i] = __ldcg(ri + i);
+                Mk[hd.roff[r] + i] = f2key(__ldcg(rv + i));
+                Mi[hd.roff[r] + i] = __ldcg(ri + i);
             }
         }
         __syncthreads();
+    }
+    /* nw bitmap words of rank r's wide record from word w0 (every thread) */
+    __device__ void bitmap(int r, int w0, int nw, uint32_t *dst) const {
+        const uint32_t *bm = reinterpret_cast<const uint32_t *>(
+            rec(r) + sizeof(ShardRecordHead) + 8 * (size_t)mp.rec_cap);
+        for (int i = threadIdx.x; i < nw; i += NT) dst[i] = __ldcg(bm + w0 + i);
     }
 };
 
@@ -1667,6 +1888,8 @@ int plan_launch(TailParams &p, int num_sms, int min_rows_per_cta) {
         while (c2 < p.max_k + 64) c2 <<= 1;
         if (p.area_bytes < 16384 || 28 * c2 + 8 * (p.max_k + 64 + kRefineMax) > p.area_bytes)
             return -5;
+        /* the wide path's explicit rows (fewer than k) and walk tables */
+        if (wide_area_bytes(std::max(1, p.max_k)) > p.area_bytes) return -7;
     }
     off = align_up(p.area_bytes, 128);
     p.off_bars = off;
@@ -1762,22 +1985,26 @@ cudaError_t launch_finish(const FinishParams &f, cudaStream_t st) {
 }
 
 /* Six words per candidate: gathered key + index + weight, candidate value +
- * index + weight / running sum; the static part (Misc) stays below 8 KB. */
+ * index + weight / running sum; then the wide walk's bitmap stage and chunk
+ * table; the static part (Misc) stays below 8 KB. */
 constexpr int kMergeDynLimit = kSmemLimit - 8192;
+constexpr int kMergeMaxCap = (kMergeDynLimit - kMergeHead - kWideWalkBytes) / 24;
 
-int peer_merge_cap(const TailParams &p) { return (p.area_bytes - kMergeHead) / 24; }
+int peer_merge_cap(const TailParams &p) {
+    return (p.area_bytes - kMergeHead - kWideWalkBytes) / 24;
+}
 
 int merge_smem_cap(int n_candidates_max) {
-    return n_candidates_max <= (kMergeDynLimit - kMergeHead) / 24 ? n_candidates_max : -1;
+    return n_candidates_max <= kMergeMaxCap ? n_candidates_max : -1;
 }
 
 cudaError_t launch_merge(const MergeParams &m, int n_streams, cudaStream_t st) {
-    if (m.smem_cap < 1 || m.smem_cap > (kMergeDynLimit - kMergeHead) / 24 || m.n_ranks < 1 ||
+    if (m.smem_cap < 1 || m.smem_cap > kMergeMaxCap || m.n_ranks < 1 ||
         m.n_ranks > kMaxRanks)
         return cudaErrorInvalidValue;
     cudaError_t e = raise_smem((const void *)merge_kernel, kMergeDynLimit);
     if (e != cudaSuccess) return e;
-    merge_kernel<<<n_streams, NT, kMergeHead + 24ull * (size_t)m.smem_cap, st>>>(m);
+    merge_kernel<<<n_streams, NT, kMergeHead + 24ull * (size_t)m.smem_cap + kWideWalkBytes, st>>>(m);
     return cudaGetLastError();
 }
 

@@ -7,8 +7,10 @@ A step is
   1. lal_tail_shard_select   every rank streams its slice once, applies the
                               penalty to its rows and writes per stream the
                               tie-complete local top-k record;
-  2. all-gather               the records (a few hundred bytes per stream) in
-                              rank order, on the tail's own CUDA stream;
+  2. all-gather               the records (a few hundred bytes per stream and
+                              a bitmap of the slice's rows, which only a
+                              record in its wide form fills) in rank order,
+                              on the tail's own CUDA stream;
   3. lal_tail_shard_merge     every rank merges the same records and draws the
                               same token, pushing it into its history copy.
 
@@ -66,9 +68,14 @@ class ShardedDecodeTail:
         self._views = {}
         self.p2p = False
         if p2p:
+            # exchange_handle clears this rank's receive buffer before its
+            # handle leaves the rank; the gather orders every clear before
+            # any rank's first step, and the barrier keeps a rank from
+            # stepping before every peer has opened its mappings
             handles = [None] * self.world
             dist.all_gather_object(handles, self.tail.exchange_handle(), group=group)
             self.tail.connect_peers(handles)
+            dist.barrier(group=group)
             self.p2p = True
 
     # the slice and the per-stream state live in the wrapped context

@@ -189,27 +189,27 @@ def test_sharded_multi_stream():
         t.close()
 
 
-def test_sharded_capacity_error_reaches_every_shard_then_recovers():
+def test_sharded_tie_set_larger_than_a_record():
     """A tie set larger than a record (an all-zero hidden: every logit 0)
-    fails the step with LAL_TAIL_ERR_CAPACITY on every shard, pushes no
-    token, and the next step runs normally."""
+    goes out in the record's wide form; every shard returns the unsharded
+    step's token and pushes it, and the next step runs the list form."""
     spec = cases.loop_cases()["tiny_lib"]
     cfg, W, hist0 = cases.loop_inputs(spec)
     q, s = oracle.quantize_rows(W, "port")
     tails = _tails(cfg, 0, q, s, 2)
+    port = oracle.PortLoop(q, s, hist0, cfg.hist, cfg.temperature, cfg.top_k,
+                           cfg.rep_penalty, 0)
     for t in tails:
-        t.set_sampling([0.0], [40], [1.1])
+        t.set_sampling([cfg.temperature], [cfg.top_k], [cfg.rep_penalty])
         t.set_history(0, hist0)
-    with pytest.raises(L.LalTailError) as ei:
-        _step(tails, np.zeros((1, cfg.n_embd), np.float32), np.array([0.5], np.float32))
-    assert ei.value.code == 5
-    for t in tails:
-        np.testing.assert_array_equal(t.get_history(0), hist0)
-    h = synth.hidden(cfg, 0)
-    per = _step(tails, h, np.array([0.5], np.float32))
-    sx, xq = oracle.quantize_x(h[0], "port")
-    want = int(np.argmax(oracle.lm_head(xq, sx, q, s)))
-    assert all(int(p[0]) == want for p in per)
+    for step, h in enumerate((np.zeros((1, cfg.n_embd), np.float32), synth.hidden(cfg, 0))):
+        u = np.float32(0.3 + 0.2 * step)
+        per = _step(tails, h, np.array([u], np.float32))
+        want, info = port.step(h[0], u)
+        for r, t in enumerate(tails):
+            assert int(per[r][0]) == want, (step, r)
+            assert t.diag(0)["n_cand"] == info.n_cand
+            np.testing.assert_array_equal(t.get_history(0), port.history())
     for t in tails:
         t.close()
 
@@ -315,6 +315,7 @@ def _p2p_timeout_worker(rank, world, port, out_dir):
     handles = [None] * world
     dist.all_gather_object(handles, st.tail.exchange_handle())
     st.tail.connect_peers(handles)
+    dist.barrier()
     tok = int(st.step(h, u)[0])
     hist = st.get_history(0)
     st.close()

@@ -219,3 +219,36 @@ def test_gpt2_sampler_is_the_library_sampler_but_at_r_zero():
     lg = np.array([1.0, 5.0, 4.0, -2.0], np.float32)
     assert oracle.gpt2_sample(lg, 0.8, 2, 1.0, None, 0.0)[0] == 0
     assert oracle.sample(lg, 0.8, 2, 1.0, None, 0.0)[0] == 1
+
+
+@pytest.mark.skipif(not oracle.have_ref(), reason="oracle/_ref not built (no reference checkout)")
+def test_port_matches_reference_on_exact_ties():
+    """Every logit 0.0 (an all-zero hidden) and 300 rows tied at the 40th
+    place: the candidate set is the whole vocabulary, or k + 300 rows; the
+    restatement returns the reference's token for both samplers and many
+    draws (the GPU's wide path is checked against the same reference)."""
+    rng = np.random.default_rng(21)
+    V = 152064
+    zero = np.zeros(V, np.float32)
+    tied = rng.standard_normal(V).astype(np.float32)
+    order = np.argsort(-tied, kind="stable")
+    rows = rng.choice(order[60:], size=300, replace=False)
+    tied[rows] = tied[order[39]]
+    rec = rng.integers(0, V, size=200).astype(np.int32)
+    R = oracle.ref()
+    for lg in (zero, tied):
+        for seed in range(6):
+            for temp in (0.7, 0.0):
+                R.ref_srand(seed)
+                want, want_lg = oracle.ref_sample(lg, temp, 40, 1.1, rec)
+                u = synth.GlibcStream(seed, private=False).next_u()
+                got, got_lg, info = oracle.sample(lg, temp, 40, 1.1, rec, u)
+                assert got == want, (seed, temp)
+                if temp > 0:  # (the penalty may move a tied or a top row)
+                    assert info.n_cand == V if lg is zero else info.n_cand >= 300
+                np.testing.assert_array_equal(bits(got_lg), bits(want_lg))
+                R.ref_srand(seed)
+                want_s, _ = oracle.ref_sample(lg, temp, 40, 1.1, rec, filtered=True)
+                g = synth.GlibcStream(seed, private=False)
+                got_s, _, _ = oracle.sample_filtered(lg, temp, 40, 1.1, rec, draw=g.next_u)
+                assert got_s == want_s, (seed, temp)

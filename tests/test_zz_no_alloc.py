@@ -1,22 +1,28 @@
 """lal_tail_sample_token_noalloc (device logits, static scratch, no
-allocation) against the existing entry lal_tail_sample_token (host logits,
-buffers grown on demand): the same token and the same penalised logits, bit
-for bit, on two calls in a row with different shapes and parameters.  Named
-to be collected last, so it runs both after the other GPU tests and alone in
-a fresh process (``pytest tests/test_zz_no_alloc.py``)."""
+allocation) against the restated reference sampler (oracle.sample,
+runtime/lal_sampling.h:46-125) and the existing entry lal_tail_sample_token
+(host logits, buffers grown on demand): the same token and the same penalised
+logits, bit for bit, on calls in a row with different shapes and parameters.
+The entry exists for callers that cannot allocate device memory inside their
+decode loop, so one test checks that free device memory does not move across
+its calls.  Named to be collected last, so it runs both after the other GPU
+tests and alone in a fresh process (``pytest tests/test_zz_no_alloc.py``)."""
 import ctypes as C
 
 import numpy as np
 import pytest
 
 import lal_b200 as L
+import oracle
 
 pytestmark = pytest.mark.gpu
 
 
-def _case(seed, V, T, k, pen, n_hist, u):
+def _case(seed, V, T, k, pen, n_hist, u, zero=False):
     rng = np.random.default_rng(seed)
     logits = (rng.standard_normal(V) * 3.0).astype(np.float32)
+    if zero:
+        logits[:] = 0.0
     recent = rng.integers(0, V, size=n_hist).astype(np.int32)
     return logits, recent, T, k, pen, np.float32(u)
 
@@ -31,33 +37,89 @@ def _existing(logits, recent, T, k, pen, u):
     return tok.value, lg
 
 
-def _noalloc(logits, recent, T, k, pen, u):
-    import torch
-    d_lg = torch.from_numpy(logits.copy()).to("cuda:0")
-    d_rec = torch.from_numpy(recent.copy()).to("cuda:0") if recent.size else None
-    torch.cuda.synchronize()
-    tok = C.c_int(-1)
-    rc = L.lib().lal_tail_sample_token_noalloc(
-        d_lg.data_ptr(), logits.size, np.float32(T), k, np.float32(pen),
-        d_rec.data_ptr() if d_rec is not None else None, recent.size, u, None, C.byref(tok))
-    assert rc == 0, L.lib().lal_tail_last_error()
-    return tok.value, d_lg.cpu().numpy()
+def _oracle(logits, recent, T, k, pen, u):
+    tok, lg, _ = oracle.sample(logits, T, k, pen, recent if recent.size else None, u)
+    return tok, lg
 
 
-def test_noalloc_matches_existing_on_two_calls_in_a_row():
+class _Buffers:
+    """Device logits and history allocated once (by torch), refilled in place
+    for every call, so the calls themselves are the only device work that
+    could allocate."""
+
+    def __init__(self, V, H):
+        import torch
+        self.lg = torch.empty(V, dtype=torch.float32, device="cuda:0")
+        self.rec = torch.empty(max(H, 1), dtype=torch.int32, device="cuda:0")
+
+    def call(self, logits, recent, T, k, pen, u, stream=None):
+        import torch
+        V, H = logits.size, recent.size
+        self.lg[:V].copy_(torch.from_numpy(logits))
+        if H:
+            self.rec[:H].copy_(torch.from_numpy(recent))
+        torch.cuda.synchronize()
+        tok = C.c_int(-1)
+        rc = L.lib().lal_tail_sample_token_noalloc(
+            self.lg.data_ptr(), V, np.float32(T), k, np.float32(pen),
+            self.rec.data_ptr() if H else None, H, u,
+            C.c_void_p(stream.cuda_stream) if stream is not None else None, C.byref(tok))
+        assert rc == 0, L.lib().lal_tail_last_error()
+        return tok.value, self.lg[:V].cpu().numpy()
+
+
+def _same(a, b):
+    assert a[0] == b[0]
+    np.testing.assert_array_equal(a[1].view(np.int32), b[1].view(np.int32))
+
+
+def test_noalloc_matches_oracle_and_existing_on_calls_in_a_row():
     cases = [
         _case(11, 152064, 0.7, 40, 1.1, 256, 0.4172),   # Qwen vocab, small-k select
         _case(12, 50257, 0.8, 1024, 1.3, 64, 0.9031),   # GPT-2 vocab, large-k select
+        _case(13, 152064, 0.0, 40, 1.1, 256, 0.5),      # greedy: no penalty, no draw
     ]
-    got = [_noalloc(*c) for c in cases]          # two no-alloc calls in a row
-    want = [_existing(*c) for c in cases]
-    for (tg, lg), (tw, lw) in zip(got, want):
-        assert tg == tw
-        np.testing.assert_array_equal(lg.view(np.int32), lw.view(np.int32))
-    # and interleaved with the existing entry, then greedy
-    g = _case(13, 152064, 0.0, 40, 1.1, 256, 0.5)
-    assert _noalloc(*g)[0] == _existing(*g)[0]
-    assert _noalloc(*cases[0])[0] == want[0][0]
+    buf = _Buffers(152064, 256)
+    got = [buf.call(*c) for c in cases]           # three no-alloc calls in a row
+    for c, g in zip(cases, got):
+        _same(g, _oracle(*c))
+        _same(g, _existing(*c))
+    # interleaved with the existing entry
+    _same(buf.call(*cases[0]), _oracle(*cases[0]))
+
+
+def test_noalloc_leaves_free_device_memory_unchanged_on_a_side_stream():
+    """After the first call on the device (its one-time set-up), calls on a
+    non-blocking stream move no device memory: cudaMemGetInfo's free bytes are
+    the same before and after."""
+    import torch
+    side = torch.cuda.Stream(device=0)
+    cases = [_case(21, 152064, 0.7, 40, 1.1, 256, 0.25), _case(22, 9000, 0.9, 300, 1.2, 100, 0.75)]
+    buf = _Buffers(152064, 256)
+    buf.call(*cases[0], stream=side)              # first call: set-up (if not done yet)
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info(0)
+    out = [buf.call(*c, stream=side) for c in cases for _ in range(2)]
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info(0)
+    assert free1 == free0, (free0, free1)
+    for i, c in enumerate(cases):
+        _same(out[2 * i], _oracle(*c))
+        _same(out[2 * i + 1], _oracle(*c))
+
+
+def test_noalloc_all_tied_logits_then_a_normal_call():
+    """Every logit 0.0: the whole vocabulary ties at T (the select's wide
+    path, which uses the same static scratch); the next call on other logits
+    must still match, so the scratch is left as the next call needs it."""
+    tied = _case(31, 152064, 0.7, 40, 1.1, 256, 0.61, zero=True)
+    normal = _case(32, 152064, 0.7, 40, 1.1, 256, 0.33)
+    buf = _Buffers(152064, 256)
+    a = buf.call(*tied)
+    _same(a, _oracle(*tied))
+    _same(a, _existing(*tied))
+    _same(buf.call(*normal), _oracle(*normal))
+    _same(buf.call(*tied), _oracle(*tied))
 
 
 def test_noalloc_rejects_vocab_above_its_limit():
