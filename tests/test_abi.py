@@ -16,7 +16,9 @@ INCLUDE = os.path.join(ROOT, "include")
 HEADERS = [os.path.join(INCLUDE, "lal_tail.h"),
            os.path.join(INCLUDE, "runtime", "lal_q8_kernel.h"),
            os.path.join(INCLUDE, "runtime", "lal_sampling.h")]
-REF = "/root/reference"
+# the samaidev/lal checkout: $LAL_REF, else a sibling of this repository
+# named "reference" (as oracle/Makefile assumes)
+REF = os.environ.get("LAL_REF", os.path.join(os.path.dirname(ROOT), "reference"))
 
 
 def declared_functions():
