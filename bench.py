@@ -290,6 +290,20 @@ def cpu_tail(cfg, q, s, steps, threads, seconds, sampler="library"):
     return B * done / t_tot, kind, done, threads
 
 
+def host_cpu():
+    """The host CPU's model name and logical CPU count."""
+    model = "unknown"
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    model = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    return {"model": model, "nproc": os.cpu_count()}
+
+
 def run_reference_arm(args, cfg):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -309,7 +323,7 @@ def run_reference_arm(args, cfg):
         "config": {**workload(cfg, args.gpus),
                    **({"sampler": args.sampler} if args.sampler != "library" else {})},
         "cpu_baseline": {"value": round(val, 3), "unit": "tokens/s", "cores": cores,
-                         "kind": kind,
+                         "kind": kind, "host": host_cpu(),
                          "sample": f"{done} full decode-tail steps of {cfg.name} "
                                    + ("(gpt2_server.c's lm_head_int8_parallel and the "
                                       "restated sampler of :2862-3013)"
@@ -329,11 +343,27 @@ def workload(cfg, n):
             "l2": l2_policy(cfg, n)}
 
 
+def lm_head_copies(cfg, n):
+    """Copies of a rank's LM-head slice used in turn so that one rotation
+    covers at least twice L2 (1: the slice alone is that large).  Only the
+    single-stream step rotates; batched steps keep the L2 flush."""
+    slice_bytes = (cfg.vocab // n) * cfg.n_embd
+    if slice_bytes >= 2 * L2_BYTES or cfg.streams > 1:
+        return 1
+    return -(-2 * L2_BYTES // slice_bytes)
+
+
 def l2_policy(cfg, n):
     slice_bytes = (cfg.vocab // n) * cfg.n_embd
     if slice_bytes >= 2 * L2_BYTES:
         return (f"inputs larger than L2: each rank streams a {slice_bytes / 1e6:.0f} MB LM-head "
                 f"slice per step (L2 126 MB), steps back to back")
+    c = lm_head_copies(cfg, n)
+    if c > 1:
+        return (f"inputs larger than L2: each rank steps through {c} identical device copies "
+                f"of its {slice_bytes / 1e6:.0f} MB LM-head slice in turn "
+                f"({c * slice_bytes / 1e6:.0f} MB a rotation against the 126 MB L2), so every "
+                f"step streams its slice from HBM; steps back to back")
     return (f"L2 flushed before each timed step: a 512 MB read on the tail's stream "
             f"(the {slice_bytes / 1e6:.0f} MB slice could stay in the 126 MB L2)")
 
@@ -389,10 +419,15 @@ def run_ours(args, cfg):
 
     stream = torch.cuda.ExternalStream(t.stream(), device=local)
     # steps run back to back when this rank's slice is at least twice L2
-    # (126 MB); a smaller slice is evicted by a 512 MB read before each step
+    # (126 MB), or when the single-stream step rotates copies of a smaller
+    # slice that together are; otherwise a 512 MB read evicts the slice
+    # before each step
     slice_bytes = t.n_rows * cfg.n_embd
+    copies = lm_head_copies(cfg, world)
+    if copies > 1:
+        t.set_lm_head_copies(copies)
     flush = (torch.ones(128 << 20, dtype=torch.float32, device=local)
-             if slice_bytes < 2 * L2_BYTES else None)
+             if slice_bytes * copies < 2 * L2_BYTES else None)
     flush_out = torch.empty((), dtype=torch.float32, device=local)
 
     def barrier():
@@ -484,9 +519,34 @@ def run_ours(args, cfg):
     finally:
         clk.__exit__(None, None, None)
 
-    # ---- e2e: host buffers through lal_tail_step ----
+    # ---- exchange share (N > 1, peer exchange): phase stamps of each step's
+    # last CTA -- its record published, every rank's record arrived, merged
+    # and drawn -- on the same back-to-back steps, read after each step ----
+    peer = world > 1 and getattr(t, "p2p", False) and B == 1
+    exch = None
+    if peer:
+        t.debug_phases(True)
+        wait_us, merge_us = [], []
+        for i in range(min(K, 100)):
+            t.step_device(d_hid[i].data_ptr(), B, d_u[i].data_ptr(), d_tok[i].data_ptr())
+            t.sync()
+            _, last = t.phase_times()
+            if last[5] and last[6] and last[7]:
+                wait_us.append((last[6] - last[5]) / 1e3)
+                merge_us.append((last[7] - last[5]) / 1e3)
+        t.debug_phases(False)
+        barrier()
+        if merge_us:
+            exch = {"publish_to_all_records_us": round(statistics.median(wait_us), 2),
+                    "publish_to_token_us": round(statistics.median(merge_us), 2)}
+
+    # ---- e2e: host buffers through the C ABI's lal_tail_step (bound once;
+    # the step's hidden, draws and tokens are host arrays) ----
     barrier()
     e2e_s = 0.0
+    c_step = L.lib().lal_tail_step if (world == 1 or peer) else None
+    tok_host = np.empty(B, np.int32)
+    ptr = lambda a: a.__array_interface__["data"][0]  # noqa: E731
     for i in range(K):
         if flush is not None:
             torch.sum(flush, 0, out=flush_out)
@@ -495,9 +555,17 @@ def run_ours(args, cfg):
                 dist.barrier()  # every rank calls the step together (untimed)
         h = hid[W + K + i]
         u = us[W + K + i]
-        t0 = time.perf_counter()
-        t.step(h, u)
-        e2e_s += time.perf_counter() - t0
+        hp, up, tp = ptr(h), ptr(u), ptr(tok_host)
+        if c_step is not None:
+            t0 = time.perf_counter()
+            rc = c_step(t.h, hp, B, up, tp)
+            e2e_s += time.perf_counter() - t0
+            if rc:
+                raise L.LalTailError(rc, L.lib().lal_tail_last_error().decode())
+        else:
+            t0 = time.perf_counter()
+            t.step(h, u)
+            e2e_s += time.perf_counter() - t0
     barrier()
 
     # max over ranks
@@ -510,8 +578,9 @@ def run_ours(args, cfg):
     if rank == 0:
         peaks, pk_kind = load_peaks()
         rows = t.n_rows
-        gpt2 = args.sampler == "gpt2"
-        batched = B >= 2 and not gpt2
+        kind = t.step_kind(B)
+        gpt2 = kind == "gpt2"
+        batched = kind == "batched"
         if gpt2:
             # the GPT-2 server's tail: quantize, LM head (the timed kernel),
             # the 512-candidate select, the float re-score, the sampler
@@ -531,7 +600,6 @@ def run_ours(args, cfg):
             launches_per_step = B
             alg = algorithmic_bytes(cfg, 1, rows)
             kname = "fused tail kernel (tail_kernel<MODE_FUSED>)"
-        peer = world > 1 and getattr(t, "p2p", False) and B == 1
         if world > 1 and not peer:
             launches_per_step += 1  # the merge (the NCCL all-gather is not ours)
         achieved = alg / (kern_ms * 1e-3) / 1e9
@@ -546,8 +614,15 @@ def run_ours(args, cfg):
             "config": {**workload(cfg, world),
                        **({"sampler": args.sampler} if args.sampler != "library" else {})},
             "e2e": {"value": round(tokens / (e2e_ms * 1e-3), 3), "unit": "tokens/s",
-                    "h2d_bytes_per_step": int(hid[0].nbytes + us[0].nbytes),
-                    "d2h_bytes_per_step": int(4 * B + 4)},
+                    # unsharded: hidden + draws + the step number pulled from
+                    # pinned memory, one 8-byte completion word per stream
+                    # written back; sharded: the copies of lal_tail_step
+                    "h2d_bytes_per_step": int(hid[0].nbytes + us[0].nbytes
+                                              + (4 if world == 1 else 0)),
+                    "d2h_bytes_per_step": int(8 * B if world == 1 else 4 * B + 4),
+                    "path": "lal_tail_step (C ABI) from host arrays" if c_step is not None
+                            else "ShardedDecodeTail.step (stage, select, NCCL all-gather, "
+                                 "merge, fetch)"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1),
                          "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "traffic": traffic,
@@ -559,8 +634,16 @@ def run_ours(args, cfg):
                             "rank's buffer over NVLink and merges (one kernel per step)"
                 if peer else "NCCL all-gather of the candidate records + merge kernel"}
                if world > 1 else {}),
+            **({"exchange_time": {**exch,
+                                  "share_of_step": round(exch["publish_to_token_us"]
+                                                         / (1e3 * dev_ms / K), 4),
+                                  "what": "rank 0's last CTA, median over steps: from its "
+                                          "record published to every rank's record arrived, "
+                                          "and to its token drawn (the merge)"}}
+               if exch else {}),
             **({"tensor": tensor_roofline(cfg, B, rows, kern_ms)} if batched else {}),
             "kernel_ms": round(kern_ms, 5),
+            "step_kind": kind,
             "clocks": clk.summary(),
         }
     # ---- CPU baseline (rank 0, N=1 only) ----
@@ -568,10 +651,16 @@ def run_ours(args, cfg):
         q, s = t.read_lm_head()
         val, kind, done, cores = cpu_tail(cfg, q, s, 10_000, os.cpu_count() or 1,
                                           args.cpu_seconds, args.sampler)
+        val1, _, done1, _ = cpu_tail(cfg, q, s, 10_000, 1, args.cpu_seconds / 2, args.sampler)
         out["cpu_baseline"] = {"value": round(val, 3), "unit": "tokens/s", "cores": cores,
                                "kind": kind,
                                "sample": f"{done} decode-tail steps of {cfg.name} "
-                                         f"(~{args.cpu_seconds:.0f} s bound)"}
+                                         f"(~{args.cpu_seconds:.0f} s bound)",
+                               "one_thread": {"value": round(val1, 3), "unit": "tokens/s",
+                                              "cores": 1,
+                                              "sample": f"{done1} steps "
+                                                        f"(~{args.cpu_seconds / 2:.0f} s bound)"},
+                               "host": host_cpu()}
     if out is not None:
         emit(out)
     t.close()

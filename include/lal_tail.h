@@ -287,6 +287,25 @@ int lal_tail_set_filter(lal_tail *t, lal_filter_topk_fn filter, lal_token_decode
  * (the reference's scalar tail loop, whose rounding its compiler decides, is
  * then empty; LAL_TAIL_ERR_UNSUPPORTED otherwise). */
 int lal_tail_set_final_norm(lal_tail *t, const float *norm_w, float eps);
+/* How a step of n_streams streams runs on this context (no counterpart in
+ * the reference): one fused launch per stream, the batched tensor-core step
+ * (quantize, one tcgen05 GEMM pass over the LM head for every stream, a
+ * select CTA per stream), or the GPT-2 server's tail.  A batched shape whose
+ * select does not fit shared memory falls back to the per-stream launches.
+ * Returns the kind, or minus an LAL_TAIL_ERR_* code. */
+#define LAL_TAIL_STEP_PER_STREAM 0
+#define LAL_TAIL_STEP_BATCHED 1
+#define LAL_TAIL_STEP_GPT2 2
+int lal_tail_step_kind(lal_tail *t, int n_streams);
+/* Measurement aid (no counterpart in the reference): keep `copies` identical
+ * device copies of this slice's LM head and row scales (the loaded one and
+ * copies - 1 duplicates) and let the single-stream steps use them in turn,
+ * one per step.  A slice smaller than the GPU's L2 cache (the Qwen head split
+ * 4 or 8 ways is 136 or 68 MB against 126 MB of L2) is then read from HBM at
+ * every step, as a full-size head is, so steps can be timed back to back.
+ * Results do not change.  1 drops the duplicates; loading an LM head drops
+ * them too.  Batched (B >= 2) steps always read the loaded copy. */
+int lal_tail_set_lm_head_copies(lal_tail *t, int copies);
 /* Diagnostics and penalised logits (this slice's rows) of the last step. */
 int lal_tail_get_diag(lal_tail *t, int stream, lal_tail_diag *out);
 int lal_tail_get_logits(lal_tail *t, int stream, float *logits_rows);

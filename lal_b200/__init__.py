@@ -130,6 +130,8 @@ SIGNATURES = {
     "lal_tail_disconnect_peers": (C.c_int, [_vp]),
     "lal_tail_set_filter": (C.c_int, [_vp, _vp, _vp, _vp, _vp]),
     "lal_tail_set_final_norm": (C.c_int, [_vp, _vp, C.c_float]),
+    "lal_tail_set_lm_head_copies": (C.c_int, [_vp, _ip]),
+    "lal_tail_step_kind": (C.c_int, [_vp, _ip]),
     "lal_tail_gpq8_find": (C.c_int, [_vp, C.c_size_t, C.c_char_p, C.POINTER(Gpq8Tensor)]),
     "lal_tail_load_lm_head_gpq8": (C.c_int, [_vp, _vp, C.c_size_t, C.c_char_p]),
     "lal_tail_sample_token_noalloc": (C.c_int, [_vp, _ip, _fp, _ip, _fp, _vp, _ip, _fp, _vp,
@@ -161,6 +163,17 @@ def lib():
             fn.argtypes = args
         _lib = L
     return _lib
+
+
+_step = None
+
+
+def _step_fn():
+    """lal_tail_step bound once (the per-token call)."""
+    global _step
+    if _step is None:
+        _step = lib().lal_tail_step
+    return _step
 
 
 def _check(rc: int):
@@ -330,16 +343,22 @@ class DecodeTail:
 
     def step(self, hidden: np.ndarray, u: np.ndarray) -> np.ndarray:
         """One decode step from host arrays (hidden [B, d] or [d], u [B])."""
-        hidden = np.ascontiguousarray(hidden, np.float32)
+        if not (isinstance(hidden, np.ndarray) and hidden.dtype == np.float32
+                and hidden.flags.c_contiguous):
+            hidden = np.ascontiguousarray(hidden, np.float32)
+        if not (isinstance(u, np.ndarray) and u.dtype == np.float32 and u.flags.c_contiguous):
+            u = np.ascontiguousarray(u, np.float32)
         B = 1 if hidden.ndim == 1 else hidden.shape[0]
         if hidden.size != B * self.cfg.n_embd:
             raise ValueError(f"hidden: {hidden.size} values for {B} x {self.cfg.n_embd}")
-        u = np.ascontiguousarray(u, np.float32).reshape(-1)
         if u.size < B:
             raise ValueError(f"u: {u.size} draws for {B} streams")
         tok = np.empty(B, np.int32)
         # raw pointers: the arrays are checked above, the call is per token
-        _check(lib().lal_tail_step(self.h, hidden.ctypes.data, B, u.ctypes.data, tok.ctypes.data))
+        rc = _step_fn()(self.h, hidden.__array_interface__["data"][0], B,
+                        u.__array_interface__["data"][0], tok.__array_interface__["data"][0])
+        if rc:
+            _check(rc)
         return tok
 
     def diag(self, stream: int = 0) -> dict:
@@ -433,6 +452,23 @@ class DecodeTail:
 
     def disconnect_peers(self):
         _check(lib().lal_tail_disconnect_peers(self.h))
+
+    STEP_KINDS = {0: "per_stream", 1: "batched", 2: "gpt2"}
+
+    def step_kind(self, n_streams: int) -> str:
+        """'per_stream' (one fused launch a stream), 'batched' (quantize, one
+        tcgen05 GEMM pass, a select CTA a stream) or 'gpt2' (the GPT-2
+        server's tail)."""
+        k = lib().lal_tail_step_kind(self.h, int(n_streams))
+        if k < 0:
+            _check(-k)
+        return self.STEP_KINDS[k]
+
+    def set_lm_head_copies(self, copies: int):
+        """Measurement aid: single-stream steps use `copies` identical device
+        copies of this slice's LM head in turn, so that a slice smaller than
+        L2 is read from HBM at every step (results do not change)."""
+        _check(lib().lal_tail_set_lm_head_copies(self.h, int(copies)))
 
     def set_final_norm(self, norm_w: Optional[np.ndarray], eps: float = 1e-6):
         """Fuse the model's final RMSNorm into the step (qwen7b_server.c:820):

@@ -13,6 +13,7 @@
 #include "../../include/runtime/lal_sampling.h"
 #include "tail_internal.h"
 
+#include <chrono>
 #include <cstdarg>
 #include <cstdio>
 #include <cstdlib>
@@ -807,8 +808,13 @@ struct lal_tail {
     int *hist_ids = nullptr, *hist_n = nullptr, *hist_head = nullptr;
     StreamDiag *diag = nullptr;                /* [B] */
     SelectScratch sel;                         /* shared by the streams' launches */
-    float *h_in = nullptr;                     /* pinned staging */
+    float *h_in = nullptr;                     /* pinned staging (mapped) */
+    float *d_h_in = nullptr;                   /* its device address */
     int *h_out = nullptr;
+    /* per-stream completion words of lal_tail_step (mapped pinned): the
+     * kernel that draws a stream's token stores [step number | token] */
+    unsigned long long *h_tok = nullptr, *d_h_tok = nullptr;
+    unsigned host_seq = 0;
     std::vector<float> h_temp;
     std::vector<int> h_topk;
     std::vector<float> h_pen;
@@ -853,6 +859,11 @@ struct lal_tail {
     std::vector<int> f_mask, f_ids, f_ring, f_keep_h;
     /* the final RMSNorm's weights on the device (lal_tail_set_final_norm) */
     float *d_norm_w = nullptr;
+    /* lal_tail_set_lm_head_copies: extra device copies of the slice and its
+     * scales, used in turn by the per-stream steps */
+    std::vector<int8_t *> w_copies;
+    std::vector<float *> sw_copies;
+    unsigned rot = 0;
     /* LAL_SAMPLER_GPT2: the launch plans of the LM head and the sampler; the
      * quantized vector and its scale, the re-scored rows and their count */
     TailParams g2_lm, g2_smp;
@@ -871,11 +882,20 @@ void close_peers(lal_tail *t) {
     t->p2p = false;
 }
 
+void free_copies(lal_tail *t) {
+    for (int8_t *w : t->w_copies) cudaFree(w);
+    for (float *f : t->sw_copies) cudaFree(f);
+    t->w_copies.clear();
+    t->sw_copies.clear();
+    t->rot = 0;
+}
+
 void destroy_ctx(lal_tail *t) {
     if (!t) return;
     if (t->device >= 0) cudaSetDevice(t->device);
     if (t->stream) cudaStreamSynchronize(t->stream);
     close_peers(t);
+    free_copies(t);
     void *bufs[] = {t->W, t->sw, t->io_in, t->io_out, t->logits, t->temp, t->topk, t->pen,
                     t->hist_ids, t->hist_n, t->hist_head, t->diag, t->phase_ts,
                     t->x_send, t->x_recv, t->xq_b, t->sx_b, t->gmax_b, t->x_peer, t->d_peer,
@@ -886,6 +906,7 @@ void destroy_ctx(lal_tail *t) {
     t->sel.free_all();
     if (t->h_in) cudaFreeHost(t->h_in);
     if (t->h_out) cudaFreeHost(t->h_out);
+    if (t->h_tok) cudaFreeHost(t->h_tok);
     for (cudaEvent_t e : t->ev) cudaEventDestroy(e);
     if (t->stream) cudaStreamDestroy(t->stream);
     delete t;
@@ -991,7 +1012,8 @@ int ctx_alloc(lal_tail *t) {
     CU(cudaMalloc(&t->W, (size_t)t->nrows * t->ld));
     CU(cudaMemset(t->W, 0, (size_t)t->nrows * t->ld));
     CU(cudaMalloc(&t->sw, 4ull * t->nrows));
-    CU(cudaMalloc(&t->io_in, 4ull * ((size_t)B * d + B)));
+    /* [B][d] hidden, [B] draws, the step number */
+    CU(cudaMalloc(&t->io_in, 4ull * ((size_t)B * d + B + 1)));
     CU(cudaMalloc(&t->io_out, 4ull * (B + 1)));
     CU(cudaMemset(t->io_out, 0, 4ull * (B + 1)));
     CU(cudaMalloc(&t->logits, 4ull * B * t->nrows));
@@ -1007,8 +1029,12 @@ int ctx_alloc(lal_tail *t) {
     CU(cudaMalloc(&t->diag, sizeof(StreamDiag) * B));
     CU(cudaMemset(t->diag, 0, sizeof(StreamDiag) * B));
     CHECK(t->sel.alloc(t->nrows));
-    CU(cudaMallocHost(&t->h_in, 4ull * ((size_t)B * d + B)));
+    CU(cudaHostAlloc(&t->h_in, 4ull * ((size_t)B * d + B + 1), cudaHostAllocMapped));
+    CU(cudaHostGetDevicePointer((void **)&t->d_h_in, t->h_in, 0));
     CU(cudaMallocHost(&t->h_out, 4ull * (B + 1)));
+    CU(cudaHostAlloc(&t->h_tok, 8ull * B, cudaHostAllocMapped));
+    memset(t->h_tok, 0, 8ull * B);
+    CU(cudaHostGetDevicePointer((void **)&t->d_h_tok, t->h_tok, 0));
     t->h_temp.assign(B, 0.0f);
     t->h_topk.assign(B, 0);
     t->h_pen.assign(B, 1.0f);
@@ -1077,7 +1103,10 @@ int ctx_check(lal_tail *t) {
  * shard_export, each launch writes stream b's candidate record into x_send
  * instead of sampling (d_u and d_tokens unused). */
 int enqueue_step(lal_tail *t, const float *d_hidden, int n, const float *d_u, int *d_tokens,
-                 bool shard_export = false) {
+                 bool shard_export = false, bool notify = false) {
+    const unsigned *seq_in =
+        reinterpret_cast<const unsigned *>(t->io_in + (size_t)t->cfg.max_streams * t->cfg.n_embd +
+                                           t->cfg.max_streams);
     if (!t->loaded) return fail(LAL_TAIL_ERR_STATE, "step before the LM head was loaded");
     if (n < 1 || n > t->cfg.max_streams) return fail(LAL_TAIL_ERR_ARG, "n_streams %d out of range", n);
     if (t->n_set < n) return fail(LAL_TAIL_ERR_STATE, "sampling parameters not set for %d streams", n);
@@ -1129,6 +1158,10 @@ int enqueue_step(lal_tail *t, const float *d_hidden, int n, const float *d_u, in
             bs.rec_cap = t->rec_cap;
             bs.rec_bytes = t->rec_bytes;
         }
+        if (notify) {
+            bs.host_tok = t->d_h_tok;
+            bs.seq_in = seq_in;
+        }
         /* timing covers the GEMM launch (the step's dominant kernel) */
         const bool time_it = t->timing && t->ev_used + 2 <= (int)t->ev.size();
         if (time_it) {
@@ -1139,10 +1172,20 @@ int enqueue_step(lal_tail *t, const float *d_hidden, int n, const float *d_u, in
         if (time_it) t->ev_used += 2;
         return LAL_TAIL_OK;
     }
+    /* the LM head copy of this step (lal_tail_set_lm_head_copies) */
+    const int8_t *W = t->W;
+    const float *sw = t->sw;
+    if (!t->w_copies.empty()) {
+        const unsigned c = t->rot++ % (unsigned)(t->w_copies.size() + 1);
+        if (c > 0) {
+            W = t->w_copies[c - 1];
+            sw = t->sw_copies[c - 1];
+        }
+    }
     for (int b = 0; b < n; ++b) {
         TailParams p = t->plan;
-        p.W = t->W;
-        p.scale_w = t->sw;
+        p.W = W;
+        p.scale_w = sw;
         p.hidden = d_hidden + (size_t)b * t->cfg.n_embd;
         p.logits = t->logits + (size_t)b * t->nrows;
         p.temperature = t->temp + b;
@@ -1173,6 +1216,10 @@ int enqueue_step(lal_tail *t, const float *d_hidden, int n, const float *d_u, in
         t->sel.fill(p);
         p.status = t->io_out + t->cfg.max_streams;
         p.phase_ts = t->phases ? t->phase_ts : nullptr;
+        if (notify) {
+            p.host_tok = t->d_h_tok + b;
+            p.seq_in = seq_in;
+        }
         p.local_edges = use_local_edges(
             effective_k(t->h_temp[b], t->h_topk[b], t->cfg.vocab_size, t->nrows), p.rows_per_cta_max);
         const bool time_it = t->timing && t->ev_used + 2 <= (int)t->ev.size();
@@ -1392,6 +1439,8 @@ int lal_tail_shard_rows(const lal_tail *t, int *row0, int *n_rows) {
 
 int lal_tail_load_lm_head_q8(lal_tail *t, const int8_t *wte_q_rows, const float *scale_w_rows) {
     CHECK(ctx_check(t));
+    CU(cudaStreamSynchronize(t->stream));
+    free_copies(t);
     if (!wte_q_rows || !scale_w_rows) return fail(LAL_TAIL_ERR_ARG, "load_lm_head_q8: null");
     CHECK(upload_rows(wte_q_rows, t->nrows, t->cfg.n_embd, t->ld, t->W, t->stream));
     CU(cudaMemcpyAsync(t->sw, scale_w_rows, 4ull * t->nrows, cudaMemcpyHostToDevice, t->stream));
@@ -1402,6 +1451,8 @@ int lal_tail_load_lm_head_q8(lal_tail *t, const int8_t *wte_q_rows, const float 
 
 int lal_tail_load_lm_head_f32(lal_tail *t, const float *W_rows, int row_begin, int n_rows) {
     CHECK(ctx_check(t));
+    CU(cudaStreamSynchronize(t->stream));
+    free_copies(t);
     if (!W_rows || row_begin < 0 || n_rows < 0 || row_begin + n_rows > t->nrows)
         return fail(LAL_TAIL_ERR_ARG, "load_lm_head_f32: bad row range");
     const int d = t->cfg.n_embd;
@@ -1553,6 +1604,66 @@ int download_outputs(lal_tail *t) {
                        cudaMemcpyDeviceToHost, t->stream));
     return LAL_TAIL_OK;
 }
+
+int step_status_error(lal_tail *t, int status) {
+    const int B = t->cfg.max_streams;
+    CU(cudaMemset(t->io_out + B, 0, 4));
+    CHECK(t->sel.reset(t->stream));
+    CU(cudaStreamSynchronize(t->stream));
+    return fail(status, "device status %d (%s)", status,
+                status == LAL_TAIL_ERR_TIMEOUT ? "bounded wait expired"
+                                               : "candidate set above the built capacity");
+}
+
+/* lal_tail_step of an unsharded context: the inputs are staged in mapped
+ * pinned memory and pulled onto the device by a small kernel (the step's
+ * kernel begins streaming the LM head meanwhile), and each stream's kernel
+ * stores [step number | token] into a mapped completion word that this
+ * thread waits on -- no device-to-host copy and no stream synchronisation
+ * on the way.  A stream whose step failed stores -1; its status is then read
+ * the usual way.  If the stream completes without the words (a launch
+ * error), the tokens are read back the usual way too. */
+int notified_step(lal_tail *t, const float *hidden, int n, const float *u, int *tokens_out) {
+    const int B = t->cfg.max_streams, d = t->cfg.n_embd;
+    const unsigned seq = ++t->host_seq == 0 ? ++t->host_seq : t->host_seq;
+    memcpy(t->h_in, hidden, 4ull * n * d);
+    memcpy(t->h_in + (size_t)B * d, u, 4ull * n);
+    memcpy(t->h_in + (size_t)B * d + B, &seq, 4);
+    CU(launch_stage_inputs(t->d_h_in, t->io_in, n * d, B * d, B + 1, t->stream));
+    CHECK(enqueue_step(t, t->io_in, n, t->io_in + (size_t)B * d, t->io_out, false, true));
+    const auto t0 = std::chrono::steady_clock::now();
+    bool done = false, drained = false;
+    for (unsigned it = 1;; ++it) {
+        done = true;
+        for (int b = 0; b < n && done; ++b) {
+            const unsigned long long v = __atomic_load_n(&t->h_tok[b], __ATOMIC_ACQUIRE);
+            done = (unsigned)(v >> 32) == seq;
+        }
+        if (done || drained) break;
+        if ((it & 1023u) == 0) {
+            const cudaError_t q = cudaStreamQuery(t->stream);
+            if (q == cudaSuccess) drained = true; /* one more look at the words */
+            else if (q != cudaErrorNotReady) return fail(LAL_TAIL_ERR_CUDA, "step: %s", cudaGetErrorString(q));
+            else if (std::chrono::steady_clock::now() - t0 > std::chrono::seconds(60))
+                return fail(LAL_TAIL_ERR_TIMEOUT, "step: no completion within 60 s");
+        }
+#if defined(__x86_64__)
+        __builtin_ia32_pause();
+#endif
+    }
+    bool failed = !done;
+    for (int b = 0; b < n && !failed; ++b) {
+        tokens_out[b] = (int)(uint32_t)t->h_tok[b];
+        failed = tokens_out[b] < 0;
+    }
+    if (!failed) return LAL_TAIL_OK;
+    CHECK(download_outputs(t));
+    CU(cudaStreamSynchronize(t->stream));
+    const int status = t->h_out[B];
+    if (status != 0) return step_status_error(t, status);
+    memcpy(tokens_out, t->h_out, 4ull * n);
+    return LAL_TAIL_OK;
+}
 }  // namespace
 
 extern "C" {
@@ -1582,6 +1693,8 @@ int lal_tail_step(lal_tail *t, const float *hidden, int n_streams, const float *
         return LAL_TAIL_OK;
     }
     const int B = t->cfg.max_streams, d = t->cfg.n_embd;
+    if (t->cfg.shard_count == 1 && t->cfg.sampler != LAL_SAMPLER_GPT2)
+        return notified_step(t, hidden, n_streams, u, tokens_out);
     CHECK(upload_inputs(t, hidden, n_streams, u));
     CHECK(enqueue_step(t, t->io_in, n_streams, t->io_in + (size_t)B * d, t->io_out));
     CHECK(download_outputs(t));
@@ -1829,6 +1942,42 @@ int lal_tail_load_lm_head_gpq8(lal_tail *t, const void *blob, size_t size, const
     std::vector<float> sc((size_t)t->nrows);
     memcpy(sc.data(), b + e.scale_offset + 4ull * t->row0, 4ull * t->nrows);
     return lal_tail_load_lm_head_q8(t, q, sc.data());
+}
+
+int lal_tail_step_kind(lal_tail *t, int n_streams) {
+    if (!t) return -fail(LAL_TAIL_ERR_ARG, "null context");
+    if (n_streams < 1 || n_streams > t->cfg.max_streams)
+        return -fail(LAL_TAIL_ERR_ARG, "n_streams %d out of range", n_streams);
+    if (t->cfg.sampler == LAL_SAMPLER_GPT2) return LAL_TAIL_STEP_GPT2;
+    if (t->batch_ok && n_streams >= 2 && !getenv_flag("LAL_TAIL_PER_STREAM"))
+        return LAL_TAIL_STEP_BATCHED;
+    return LAL_TAIL_STEP_PER_STREAM;
+}
+
+int lal_tail_set_lm_head_copies(lal_tail *t, int copies) {
+    CHECK(ctx_check(t));
+    if (copies < 1 || copies > 64) return fail(LAL_TAIL_ERR_ARG, "set_lm_head_copies: 1..64");
+    if (!t->loaded) return fail(LAL_TAIL_ERR_STATE, "set_lm_head_copies before the LM head was loaded");
+    CU(cudaStreamSynchronize(t->stream));
+    free_copies(t);
+    const size_t wb = (size_t)t->nrows * t->ld, sb = 4ull * t->nrows;
+    for (int c = 1; c < copies; ++c) {
+        int8_t *w = nullptr;
+        float *f = nullptr;
+        cudaError_t e = cudaMalloc(&w, wb);
+        if (e == cudaSuccess) e = cudaMalloc(&f, sb);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(w, t->W, wb, cudaMemcpyDeviceToDevice, t->stream);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(f, t->sw, sb, cudaMemcpyDeviceToDevice, t->stream);
+        if (w) t->w_copies.push_back(w);
+        if (f) t->sw_copies.push_back(f);
+        if (e != cudaSuccess) {
+            cudaStreamSynchronize(t->stream);
+            free_copies(t);
+            return fail(LAL_TAIL_ERR_CUDA, "set_lm_head_copies: %s", cudaGetErrorString(e));
+        }
+    }
+    CU(cudaStreamSynchronize(t->stream));
+    return LAL_TAIL_OK;
 }
 
 int lal_tail_set_final_norm(lal_tail *t, const float *norm_w, float eps) {

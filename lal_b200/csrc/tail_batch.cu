@@ -373,6 +373,8 @@ struct BatchSelectParams {
     const uint32_t *gmax;      /* [B][n_groups] raw group maxima (GEMM) */
     int n_groups;
     int wide_cap;              /* explicit rows of the wide path (>= max k - 1) */
+    unsigned long long *host_tok; /* [B] completion words in mapped host memory, or null */
+    const unsigned *seq_in;
 };
 
 constexpr uint32_t kEmptySlot = 0xFFFFFFFFu;
@@ -402,6 +404,10 @@ __device__ __noinline__ void batch_wide(const BatchSelectParams &p, int b, int k
         a.rec_cap = p.rec_cap;
     } else {
         a.token = p.tokens + b;
+        if (p.host_tok) {
+            a.host_tok = p.host_tok + b;
+            a.host_seq = __ldcg(p.seq_in);
+        }
         a.hist_ids = p.hist_ids + (size_t)b * p.hist_stride;
         a.hist_n = p.hist_n + b;
         a.hist_head = p.hist_head + b;
@@ -428,12 +434,15 @@ __global__ void __launch_bounds__(NT, 1) batch_select_kernel(const __grid_consta
     float *Ov = reinterpret_cast<float *>(Ci + p.c_cap);           /* index order      */
     int *Oi = reinterpret_cast<int *>(Ov + p.c_cap);
     float *Ce = reinterpret_cast<float *>(Oi + p.c_cap);           /* weights, sums    */
-    uint32_t *hkey = reinterpret_cast<uint32_t *>(Ce + p.c_cap);   /* history hash     */
-    uint32_t *hcnt = hkey + p.h_slots;
-    int *Gl = reinterpret_cast<int *>(hcnt + p.h_slots);           /* candidate groups */
-    /* staging of kStageGroups candidate groups' 32 logits (16-byte aligned) */
-    float *Gv = reinterpret_cast<float *>(
+    int *Gl = reinterpret_cast<int *>(Ce + p.c_cap);               /* candidate groups */
+    /* one 16-byte aligned region, used twice: the history hash of the
+     * penalty (step 1), then the staging of kStageGroups candidate groups'
+     * 32 logits (step 3) */
+    uint8_t *shared2 = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(Gl + p.n_groups) + 15) & ~static_cast<uintptr_t>(15));
+    uint32_t *hkey = reinterpret_cast<uint32_t *>(shared2);        /* history hash     */
+    uint32_t *hcnt = hkey + p.h_slots;
+    float *Gv = reinterpret_cast<float *>(shared2);
 
     float *lg = p.logits + (size_t)b * p.rows;
     const float temp = p.temperature[b];
@@ -932,6 +941,7 @@ __global__ void __launch_bounds__(NT, 1) batch_select_kernel(const __grid_consta
                 p.hist_head[b] = (hhead + 1) % p.hist_cap;
             }
         }
+        if (p.host_tok) notify_host(p.host_tok + b, __ldcg(p.seq_in), token);
     }
 }
 
@@ -976,8 +986,8 @@ bool encode_i8(CUtensorMap *m, const void *base, int dim0, int dim1, int pitch, 
 int batch_n_for(int B) { return (B + 31) / 32 * 32; }
 
 size_t batch_select_smem(int s_cap, int c_cap, int h_slots, int n_groups) {
-    const size_t fixed = 4ull * 4096 + 8ull * s_cap + 24ull * c_cap + 8ull * h_slots + 4ull * n_groups;
-    return (fixed + 15) / 16 * 16 + 128ull * kStageGroups;
+    const size_t fixed = 4ull * 4096 + 8ull * s_cap + 20ull * c_cap + 4ull * n_groups;
+    return (fixed + 15) / 16 * 16 + std::max(8ull * h_slots, 128ull * kStageGroups);
 }
 
 int batch_plan(BatchPlan &bp, const int8_t *W, const float *scale_w, int rows, int ld,
@@ -1109,6 +1119,8 @@ cudaError_t batch_launch(BatchPlan &bp, const BatchStep &s, cudaStream_t st) {
     q.gmax = bp.gmax;
     q.n_groups = bp.n_groups;
     q.wide_cap = bp.wide_cap;
+    q.host_tok = s.shard_out ? nullptr : s.host_tok;
+    q.seq_in = s.seq_in;
     const size_t ssmem = batch_select_smem(bp.s_cap, bp.c_cap, bp.h_slots, bp.n_groups);
     e = raise_smem((const void *)batch_select_kernel, kGemmSmemLimit - 8192);
     if (e != cudaSuccess) return e;

@@ -538,6 +538,17 @@ __device__ uint32_t block_kth_largest(Get get, int n, int k, Misc *ms) {
     return prefix;
 }
 
+/* The step's token (or -1) into the caller's completion word in mapped
+ * pinned host memory, tagged with the step's sequence number in the high
+ * half; one 64-bit system-scope store after a system fence, so the host
+ * that sees the sequence number has the token and every earlier write. */
+__device__ __forceinline__ void notify_host(unsigned long long *w, unsigned seq, int token) {
+    if (w == nullptr) return;
+    __threadfence_system();
+    const unsigned long long v = ((unsigned long long)seq << 32) | (uint32_t)token;
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(w), "l"(v) : "memory");
+}
+
 /* Penalty for one logit with `count` history occurrences, one step per
  * occurrence as runtime/lal_sampling.h:63-64 does (not a power). */
 __device__ __forceinline__ float penalise(float l, uint32_t count, float pen) {

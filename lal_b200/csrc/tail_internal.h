@@ -222,6 +222,11 @@ struct TailParams {
     /* optional globaltimer stamps: [cta*8 + i] per CTA (start, prologue done,
      * rows done, list written) and [grid*8 + i] for the merge */
     unsigned long long *phase_ts;
+    /* optional completion word in mapped pinned host memory: the step's token
+     * (or -1) in the low half, the step's sequence number (*seq_in, device
+     * memory, read after the previous kernel completes) in the high half */
+    unsigned long long *host_tok;
+    const unsigned *seq_in;
     /* shared-memory layout (bytes) */
     int stages, rows_per_stage, stage_bytes, area_bytes;
     int off_bars, off_xq, off_sw, off_lg, off_cnt, off_hist, off_misc, smem_total;
@@ -332,6 +337,9 @@ struct BatchStep {
     uint8_t *shard_out; /* per-stream records (vocab-sharded select), or null */
     int rec_cap, rec_bytes;
     cudaEvent_t gemm_ev0, gemm_ev1; /* optional: recorded around the GEMM launch */
+    /* optional per-stream completion words in mapped host memory (TailParams) */
+    unsigned long long *host_tok;
+    const unsigned *seq_in;
 };
 /* 0 when the shape takes the batched path (d >= 128, 2 <= max_B <= 256). */
 int batch_plan(BatchPlan &bp, const int8_t *W, const float *scale_w, int rows, int ld,
@@ -351,6 +359,12 @@ cudaError_t launch_gpt2_rerank(const float *x, int d, const int8_t *W, int ld, c
                                const int *status, cudaStream_t st);
 cudaError_t launch_quantize_x(const float *x, int8_t *xq, float *scale, int n,
                               cudaStream_t st);
+/* One step's inputs from mapped pinned host memory into device memory: words
+ * [0, n0) and [off1, off1 + n1) of src to the same offsets of dst, by one
+ * small kernel that lets the next kernel on the stream launch at once
+ * (programmatic dependent launch). */
+cudaError_t launch_stage_inputs(const float *src, float *dst, int n0, int off1, int n1,
+                                cudaStream_t st);
 cudaError_t launch_abs_xq(const int8_t *xq, uint8_t *ax, int n, cudaStream_t st);
 cudaError_t launch_quantize_rows(const float *W, int d, int8_t *q, int ld,
                                  float *scale, int n_rows, cudaStream_t st);

@@ -186,7 +186,10 @@ struct PeerRecords {
             }
         }
         __syncthreads();
-        if (tid == 0 && !ms->found) hd.rbad = DEV_TIMEOUT;
+        if (tid == 0) {
+            if (!ms->found) hd.rbad = DEV_TIMEOUT;
+            stamp(p, (int)gridDim.x * 8 + 6); /* every rank's record is here */
+        }
         __syncthreads();
     }
     /* nw bitmap words of rank r's wide record from word w0 (every thread);
@@ -260,6 +263,8 @@ __device__ __noinline__ void tail_wide(const TailParams &p, int k, bool greedy, 
     a.ex = ExpfTables{p.expf_x, p.expf_y, p.expf_bits, p.expf_off, p.expf_hash,
                       p.expf_hash_probe};
     a.token = p.tokens;
+    a.host_tok = p.host_tok;
+    a.host_seq = p.host_tok ? __ldcg(p.seq_in) : 0u;
     a.diag = p.diag;
     a.hist_ids = p.hist_ids;
     a.hist_n = p.hist_n;
@@ -1087,7 +1092,9 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
         tail_wide(p, k, greedy, temp, u0, hn, hhead, smem, ms);
         if (p.peer_recv != nullptr) {
             __syncthreads();
+            if (tid == 0) stamp(p, G * 8 + 5);
             peer_merge(p, smem, ms);
+            if (tid == 0) stamp(p, G * 8 + 7);
         }
         return;
     }
@@ -1109,6 +1116,7 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
                 p.tokens[0] = -1;
             }
             p.diag[0] = dg;
+            if (p.host_tok) notify_host(p.host_tok, __ldcg(p.seq_in), -1);
         }
         return;
     }
@@ -1293,6 +1301,7 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
                 p.hist_head[0] = (h + 1) % p.hist_cap;
             }
         }
+        if (p.host_tok) notify_host(p.host_tok, __ldcg(p.seq_in), token);
         stamp(p, G * 8 + 7);
     }
 }
@@ -1321,6 +1330,25 @@ __global__ void __launch_bounds__(NT) quantize_x_kernel(const float *x, int8_t *
         xq[i] = (int8_t)v;
     }
     if (threadIdx.x == 0) *scale_out = scale;
+}
+
+/* A step's inputs from mapped pinned host memory (src) into device memory
+ * (dst): words [0, n0) and [off1, off1 + n1).  The next kernel may launch at
+ * once (it streams the LM head, which no step writes) and waits for this
+ * one's completion before it reads the inputs. */
+__global__ void __launch_bounds__(256) stage_inputs_kernel(const float *src, float *dst, int n0,
+                                                           int off1, int n1) {
+    grid_dep_launch_dependents();
+    const int stride = gridDim.x * blockDim.x;
+    const int i0 = blockIdx.x * blockDim.x + threadIdx.x;
+    if (((n0 | off1) & 3) == 0) {
+        const float4 *s4 = reinterpret_cast<const float4 *>(src);
+        float4 *d4 = reinterpret_cast<float4 *>(dst);
+        for (int i = i0; i < n0 / 4; i += stride) d4[i] = s4[i];
+    } else {
+        for (int i = i0; i < n0; i += stride) dst[i] = src[i];
+    }
+    for (int i = i0; i < n1; i += stride) dst[off1 + i] = src[off1 + i];
 }
 
 __global__ void abs_xq_kernel(const int8_t *xq, uint8_t *ax, int n) {
@@ -1963,6 +1991,14 @@ cudaError_t launch_tail(const TailParams &p, int grid, cudaStream_t st) {
 cudaError_t launch_quantize_x(const float *x, int8_t *xq, float *scale, int n,
                               cudaStream_t st) {
     quantize_x_kernel<<<1, NT, 0, st>>>(x, xq, scale, n);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_stage_inputs(const float *src, float *dst, int n0, int off1, int n1,
+                                cudaStream_t st) {
+    /* 16 KB of the first range a CTA (the PCIe reads of one CTA overlap) */
+    const int grid = std::max(1, std::min(64, (n0 + 4095) / 4096));
+    stage_inputs_kernel<<<grid, 256, 0, st>>>(src, dst, n0, off1, n1);
     return cudaGetLastError();
 }
 

@@ -342,6 +342,8 @@ struct WideDense {
     ExpfTables ex;
     /* the draw */
     int *token;
+    unsigned long long *host_tok; /* completion word (notify_host), or null */
+    unsigned host_seq;
     StreamDiag *diag;
     int *hist_ids, *hist_n, *hist_head;
     int hist_cap, push_history, hn, hhead;
@@ -551,6 +553,7 @@ __device__ __noinline__ void wide_dense(const WideDense &a, uint8_t *area, Misc 
                 *a.hist_head = (a.hhead + 1) % a.hist_cap;
             }
         }
+        notify_host(a.host_tok, a.host_seq, token);
     }
     __syncthreads();
 }

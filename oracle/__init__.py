@@ -81,6 +81,8 @@ def port():
         lib.orc_lm_head_int8_range_abs_8row.argtypes = [_f32p, _i8p, C.c_float, _i8p, _f32p,
                                                         C.c_int, C.c_int, C.c_int]
         lib.orc_lm_head_dots.argtypes = [_i32p, _i8p, _i8p, C.c_int, C.c_int, C.c_int]
+        lib.orc_lm_head_multi.argtypes = [_f32p, _i8p, _f32p, _i8p, _f32p, C.c_int, C.c_int,
+                                          C.c_int]
         lib.orc_quantize_q8_per_row.argtypes = [_f32p, _i8p, _f32p, C.c_int, C.c_int]
         lib.orc_quantize_q8_rows.argtypes = [_f32p, _i8p, _f32p, C.c_int, C.c_int]
         lib.orc_sample_token.restype = C.c_int
@@ -378,6 +380,63 @@ class PortLoop:
 
     def history(self):
         return self.rec[:self.n.value].copy()
+
+
+def lm_head_multi(xq, sx, wq, sw):
+    """Restated logits of B quantized vectors at once: [B, V]."""
+    xq = np.ascontiguousarray(xq, np.int8)
+    B, d = xq.shape
+    V = wq.shape[0]
+    out = np.empty((B, V), np.float32)
+    port().orc_lm_head_multi(out.reshape(-1), xq.reshape(-1), np.ascontiguousarray(sx, np.float32),
+                             np.ascontiguousarray(wq).reshape(-1),
+                             np.ascontiguousarray(sw, np.float32), V, d, B)
+    return out
+
+
+class PortBatch:
+    """B independent restated decode tails sharing one LM head (a batched
+    step is B streams, each its own history, temperature, top-k and draws):
+    per stream the quantizer, the 1-row LM head (computed for all streams in
+    one pass), lal_sampling.h's sampler (uncapped heap) or the server's, and
+    the history ring."""
+
+    def __init__(self, wq, sw, hists, hist_cap, temps, top_ks, rep_penalty, variant):
+        self.wq = np.ascontiguousarray(wq, np.int8)
+        self.sw = np.ascontiguousarray(sw, np.float32)
+        self.cap = max(1, hist_cap)
+        self.push = hist_cap > 0
+        self.recs, self.ns = [], []
+        for h in hists:
+            r = np.zeros(self.cap, np.int32)
+            r[:len(h)] = h
+            self.recs.append(r)
+            self.ns.append(C.c_int(len(h)))
+        self.T = [float(x) for x in temps]
+        self.k = [int(x) for x in top_ks]
+        self.p, self.variant = rep_penalty, variant
+
+    def step(self, hidden, u):
+        B = len(self.recs)
+        q = [quantize_x(hidden[b]) for b in range(B)]
+        lg = lm_head_multi(np.stack([x for _, x in q]), np.array([s for s, _ in q], np.float32),
+                           self.wq, self.sw)
+        toks = []
+        for b in range(B):
+            rec = self.recs[b][:self.ns[b].value]
+            if self.variant == 1:
+                tok, _, _ = sample_filtered(lg[b], self.T[b], self.k[b], self.p, rec,
+                                            draw=lambda ub=u[b]: ub)
+            else:
+                tok, _, _ = sample(lg[b], self.T[b], self.k[b], self.p,
+                                   rec if rec.size else None, u[b])
+            if self.push:
+                port().orc_recent_push(self.recs[b], C.byref(self.ns[b]), self.cap, int(tok))
+            toks.append(tok)
+        return np.array(toks, np.int32)
+
+    def history(self, b):
+        return self.recs[b][:self.ns[b].value].copy()
 
 
 def ref_sample(logits, temperature, top_k, rep_penalty, recent, filtered=False):

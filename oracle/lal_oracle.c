@@ -87,14 +87,42 @@ void orc_lm_head_dots(int32_t *dots, const int8_t *xq, const int8_t *wte_q,
     }
 }
 
+/* Rows are independent, so large ranges are split over OpenMP threads (the
+ * reference splits its vocab the same way, qwen7b_server.c:833-845); every
+ * row's dot product and logit are the same whatever the split. */
 void orc_lm_head_int8_range(float *logits, const int8_t *xq, float scale_x,
                             const int8_t *wte_q, const float *scale_w,
                             int v_start, int v_end, int n_embd) {
+    #pragma omp parallel for schedule(static) if ((long)(v_end - v_start) * n_embd > (1L << 22))
     for (int v = v_start; v < v_end; v++) {
         int32_t dot;
         orc_lm_head_dots(&dot, xq, wte_q, v, v + 1, n_embd);
         float s = scale_x * scale_w[v];
         logits[v] = s * (float)dot;
+    }
+}
+
+/* The same logits for B quantized vectors at once (a batched decode step
+ * restated as B calls of the 1-row form above): logits[b][v] for v in
+ * [0, vocab).  Rows are taken in blocks of 16 that every vector visits
+ * while they are in cache; each logit is the 1-row form's
+ * (scale_x[b] * scale_w[v]) * (float)dot, exact int32 dot. */
+void orc_lm_head_multi(float *logits, const int8_t *xq, const float *scale_x,
+                       const int8_t *wte_q, const float *scale_w, int vocab, int n_embd,
+                       int n_vec) {
+    #pragma omp parallel for schedule(static)
+    for (int v0 = 0; v0 < vocab; v0 += 16) {
+        const int v1 = v0 + 16 < vocab ? v0 + 16 : vocab;
+        for (int b = 0; b < n_vec; b++) {
+            const int8_t *x = xq + (size_t)b * n_embd;
+            for (int v = v0; v < v1; v++) {
+                const int8_t *w = wte_q + (size_t)v * n_embd;
+                int32_t acc = 0;
+                for (int i = 0; i < n_embd; i++) acc += (int32_t)x[i] * (int32_t)w[i];
+                float s = scale_x[b] * scale_w[v];
+                logits[(size_t)b * vocab + v] = s * (float)acc;
+            }
+        }
     }
 }
 

@@ -56,6 +56,10 @@ void  orc_compute_abs_xq(const int8_t *xq, uint8_t *ax, int n);
 void  orc_lm_head_int8_range(float *logits, const int8_t *xq, float scale_x,
                              const int8_t *wte_q, const float *scale_w,
                              int v_start, int v_end, int n_embd);
+/* logits[b][v] of n_vec quantized vectors xq[b][n_embd] (scales scale_x[b]) */
+void  orc_lm_head_multi(float *logits, const int8_t *xq, const float *scale_x,
+                        const int8_t *wte_q, const float *scale_w, int vocab, int n_embd,
+                        int n_vec);
 /* runtime/lal_q8_kernel.h:551-640: rows in full 8-row groups from v_start
  * sum only the first n_embd & ~31 columns (no scalar tail in :577-611). */
 void  orc_lm_head_int8_range_abs_8row(float *logits, const int8_t *xq, float scale_x,

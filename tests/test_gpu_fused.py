@@ -160,3 +160,27 @@ def test_multi_stream_context_runs_streams_independently():
         for b in range(4):
             assert int(toks[b]) == ports[b].step(h[b], u[b])[0], (step, b)
     t.close()
+
+
+def test_lm_head_copies_and_partial_streams_keep_results():
+    """Steps that rotate over identical device copies of the LM head
+    (lal_tail_set_lm_head_copies, the bench's way past L2) and steps of fewer
+    streams than the context holds return the oracle's tokens."""
+    spec = cases.loop_cases()["tiny_lib"]
+    cfg, W, hist0 = cases.loop_inputs(spec)
+    q, s = oracle.quantize_rows(W, "port")
+    t = make_tail(cfg, 0, q=q, s=s, streams=3)
+    t.set_lm_head_copies(3)
+    t.set_sampling([cfg.temperature] * 3, [cfg.top_k] * 3, [cfg.rep_penalty] * 3)
+    t.set_history(0, hist0)
+    port = oracle.PortLoop(q, s, hist0, cfg.hist, cfg.temperature, cfg.top_k,
+                           cfg.rep_penalty, 0)
+    g = synth.GlibcStream(cfg.seed, private=False)
+    for step in range(7):
+        h = synth.hidden(cfg, step)
+        u = g.next_u()
+        tok = int(t.step(h, np.array([u], np.float32))[0])   # 1 of 3 streams
+        assert tok == port.step(h[0], u)[0], step
+    np.testing.assert_array_equal(t.get_history(0), port.history())
+    t.set_lm_head_copies(1)
+    t.close()
