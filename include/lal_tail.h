@@ -325,11 +325,13 @@ int lal_tail_kernel_time(lal_tail *t, double *avg_ms, int *n_launches);
 
 /* Phase timing of the fused kernel (inspection hook).  When on, every launch
  * writes globaltimer stamps (ns): per CTA c, out[c*8 + 0..7] = start,
- * prologue done, rows done, histogram levels 0/1/2 merged (grid barriers;
- * levels 1-2 only when used), -, arrival at the final ticket; for the last
- * CTA, out[grid*8 + 0..3] = select start, threshold found, candidates in
- * vocab order, token written.  read copies the last launch's (grid+1)*8
- * stamps. */
+ * prologue done, rows done, the previous kernel complete (small-k select) or
+ * histogram levels 0/1/2 merged (grid select), -, -, -, arrival at the final
+ * ticket; for the last CTA, out[grid*8 + 0..7] = select start, CTA bound,
+ * superset, threshold, candidates in vocab order, (peer exchange) record
+ * published, every rank's record arrived, token written; and for the peer
+ * exchange's merge, out[(grid+1)*8 + 0..4] = maximum, threshold, candidates,
+ * sum, draw.  read copies the last launch's (grid+2)*8 stamps. */
 int lal_tail_debug_phases(lal_tail *t, int on);
 int lal_tail_debug_phase_read(lal_tail *t, unsigned long long *out, int cap, int *grid);
 

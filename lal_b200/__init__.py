@@ -387,17 +387,20 @@ class DecodeTail:
     def debug_phases(self, on: bool):
         _check(lib().lal_tail_debug_phases(self.h, 1 if on else 0))
 
-    def phase_times(self):
+    def phase_times(self, merge: bool = False):
         """(per-CTA stamps [grid, 8], last-CTA stamps [8]) in ns, relative to
-        the earliest CTA start, of the last launch (0 where not written)."""
+        the earliest CTA start, of the last launch (0 where not written);
+        with merge=True also the peer merge's stamps [8]."""
         g = C.c_int()
         _check(lib().lal_tail_debug_phase_read(self.h, None, 0, C.byref(g)))
-        out = np.zeros((g.value + 1) * 8, np.uint64)
+        out = np.zeros((g.value + 2) * 8, np.uint64)
         _check(lib().lal_tail_debug_phase_read(self.h, _ptr(out), out.size, C.byref(g)))
-        st = out.reshape(g.value + 1, 8).astype(np.int64)
-        t0 = st[:-1, 0].min()
+        st = out.reshape(g.value + 2, 8).astype(np.int64)
+        t0 = st[:-2, 0].min()
         rel = np.where(st > 0, st - t0, 0)
-        return rel[:-1], rel[-1]
+        if merge:
+            return rel[:-2], rel[-2], rel[-1]
+        return rel[:-2], rel[-2]
 
     def stream(self) -> int:
         s = C.c_void_p()

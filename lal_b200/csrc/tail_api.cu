@@ -2089,7 +2089,7 @@ int lal_tail_debug_phase_read(lal_tail *t, unsigned long long *out, int cap, int
     CHECK(ctx_check(t));
     if (grid) *grid = t->grid;
     if (!t->phase_ts || !out) return LAL_TAIL_OK;
-    const int n = std::min(cap, (t->grid + 1) * 8);
+    const int n = std::min(cap, (t->grid + 2) * 8);
     CU(cudaStreamSynchronize(t->stream));
     CU(cudaMemcpy(out, t->phase_ts, sizeof(unsigned long long) * n, cudaMemcpyDeviceToHost));
     return LAL_TAIL_OK;

@@ -538,6 +538,28 @@ __device__ uint32_t block_kth_largest(Get get, int n, int k, Misc *ms) {
     return prefix;
 }
 
+/* A pair of 64-bit words of a peer record, stored and loaded as one aligned
+ * 16-byte access (each word single-copy atomic on its own; readers check the
+ * sequence number in both). */
+__device__ __forceinline__ void st_sys_pair(uint64_t *p, uint64_t a, uint64_t b) {
+    asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(a), "l"(b)
+                 : "memory");
+}
+__device__ __forceinline__ void ld_sys_pair(const uint64_t *p, uint64_t &a, uint64_t &b) {
+    asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p)
+                 : "memory");
+}
+/* Wait (bounded by the globaltimer deadline) until both words of a pair
+ * carry sequence number seq. */
+__device__ __forceinline__ bool poll_pair(const uint64_t *w, uint32_t seq, uint64_t deadline,
+                                          uint64_t &a, uint64_t &b) {
+    for (uint32_t it = 0;; ++it) {
+        ld_sys_pair(w, a, b);
+        if ((uint32_t)(a >> 32) == seq && (uint32_t)(b >> 32) == seq) return true;
+        if ((it & 15u) == 15u && gtimer() > deadline) return false;
+    }
+}
+
 /* The step's token (or -1) into the caller's completion word in mapped
  * pinned host memory, tagged with the step's sequence number in the high
  * half; one 64-bit system-scope store after a system fence, so the host

@@ -15,7 +15,8 @@ constexpr int kConsumerWarps = 8;
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
 constexpr int kMaxStages = 8;
 /* stages the fused kernel's producer issues before waiting for the previous
- * kernel on the stream (programmatic dependent launch) */
+ * kernel on the stream (programmatic dependent launch), unless a CTA's slice
+ * is short enough that it prefetches its whole ring (plan_launch) */
 constexpr int kEarlyStages = 2;
 /* Largest grid (one CTA per SM on B200 is 148). */
 constexpr int kMaxGrid = 256;
@@ -115,9 +116,10 @@ inline int shard_record_bytes(int cap, int rows_max) {
 }
 /* bytes of a peer-exchange record: 64-bit words tagged with the step's
  * sequence number -- count, status, ties, T_shard key, then (value, vocab
- * index) per entry, then the bitmap words after cap entries */
+ * index) per entry, then the bitmap words after cap entries; a 16-byte
+ * multiple, so that every pair of words is one aligned 16-byte access */
 inline int peer_record_bytes(int cap, int rows_max) {
-    return 8 * (4 + 2 * cap + shard_bitmap_words(rows_max));
+    return (8 * (4 + 2 * cap + shard_bitmap_words(rows_max)) + 15) / 16 * 16;
 }
 
 /* Merge of the gathered records of one stream (one CTA per stream): the
@@ -143,6 +145,8 @@ struct MergeParams {
     const uint4 *expf_hash;   /* hash form of the fix-ups, or null            */
     int expf_hash_probe;
     int smem_cap;     /* candidates the CTA's shared memory holds             */
+    /* optional globaltimer stamps of the merge's phases ([8], or null) */
+    unsigned long long *phase_ts;
 };
 
 struct TailParams {
@@ -231,6 +235,7 @@ struct TailParams {
     int stages, rows_per_stage, stage_bytes, area_bytes;
     int off_bars, off_xq, off_sw, off_lg, off_cnt, off_hist, off_misc, smem_total;
     int rows_per_cta_max;
+    int early_stages;        /* stages streamed before griddepcontrol.wait    */
     int nch;                 /* 512-byte column chunks per row                */
     int max_k;               /* largest k a launch may use (planning)         */
     int local_edges;         /* select strategy (use_local_edges); 0 = grid

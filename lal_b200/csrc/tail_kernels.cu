@@ -83,16 +83,12 @@ __device__ void peer_publish(const TailParams &p, int status, int m, const float
     for (int r = 0; r < p.n_ranks; ++r) {
         uint64_t *w = reinterpret_cast<uint64_t *>(p.peer_recv[r] + slot);
         if (fits)
-            for (int i = threadIdx.x; i < m; i += NT) {
-                st_relaxed_sys_u64(w + 4 + 2 * i, hi | __float_as_uint(Ov[i]));
-                st_relaxed_sys_u64(w + 5 + 2 * i, hi | (uint32_t)Oi[i]);
-            }
+            for (int i = threadIdx.x; i < m; i += NT)
+                st_sys_pair(w + 4 + 2 * i, hi | __float_as_uint(Ov[i]), hi | (uint32_t)Oi[i]);
         if (threadIdx.x == 0) {
-            st_relaxed_sys_u64(w + 0, hi | (uint32_t)(fits ? m : 0));
-            st_relaxed_sys_u64(w + 1, hi | (uint32_t)(fits ? 0 : (status != 0 ? status
-                                                                          : (int)DEV_CAPACITY)));
-            st_relaxed_sys_u64(w + 2, hi);
-            st_relaxed_sys_u64(w + 3, hi);
+            st_sys_pair(w, hi | (uint32_t)(fits ? m : 0),
+                        hi | (uint32_t)(fits ? 0 : (status != 0 ? status : (int)DEV_CAPACITY)));
+            st_sys_pair(w + 2, hi, hi);
         }
     }
 }
@@ -111,13 +107,14 @@ __device__ __forceinline__ bool poll_word(const uint64_t *w, uint32_t seq, uint6
     }
 }
 
-/* The four header words of a peer record, loaded together until every one
- * carries this step's sequence number (bounded by deadline). */
+/* The four header words of a peer record, loaded together (two 16-byte
+ * loads) until every one carries this step's sequence number (bounded by
+ * deadline). */
 __device__ __forceinline__ bool poll_head4(const uint64_t *w, uint32_t seq, uint64_t deadline,
                                            uint64_t *v) {
     for (uint32_t it = 0;; ++it) {
-#pragma unroll
-        for (int q = 0; q < 4; ++q) v[q] = ld_relaxed_sys_u64(w + q);
+        ld_sys_pair(w, v[0], v[1]);
+        ld_sys_pair(w + 2, v[2], v[3]);
         bool all = true;
 #pragma unroll
         for (int q = 0; q < 4; ++q) all = all && (uint32_t)(v[q] >> 32) == seq;
@@ -177,8 +174,7 @@ struct PeerRecords {
             const int j = e - hd.roff[r];
             const uint64_t *w = rec(r);
             uint64_t v = 0, x = 0;
-            if (poll_word(w + 4 + 2 * j, p.seq, deadline, &v) &&
-                poll_word(w + 5 + 2 * j, p.seq, deadline, &x)) {
+            if (poll_pair(w + 4 + 2 * j, p.seq, deadline, v, x)) {
                 Mk[e] = f2key(__uint_as_float((uint32_t)v));
                 Mi[e] = (int)(uint32_t)x;
             } else {
@@ -239,6 +235,7 @@ __device__ __noinline__ void peer_merge(const TailParams &p, uint8_t *smem, Misc
     mp.expf_hash = p.expf_hash;
     mp.expf_hash_probe = p.expf_hash_probe;
     mp.smem_cap = (p.area_bytes - kMergeHead - kWideWalkBytes) / 24;
+    mp.phase_ts = p.phase_ts ? p.phase_ts + ((size_t)gridDim.x + 1) * 8 : nullptr;
     merge_sample(mp, 0, smem, ms, PeerRecords{p, ms});
 }
 
@@ -342,12 +339,17 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
     }
     __syncthreads();
     /* The fused launch may start while the previous kernel on the stream is
-     * still running (programmatic dependent launch).  The LM head is never
-     * written by a step, so the producer warp streams it at once; every
-     * other read (hidden vector, history ring, sampling parameters, select
-     * scratch) waits for the previous kernel to complete. */
+     * still running (programmatic dependent launch).  The LM head and its row
+     * scales are never written by a step, so the producer warp streams the
+     * rows and the consumer warps load the scales at once; every other read
+     * (hidden vector, history ring, sampling parameters, select scratch)
+     * waits for the previous kernel to complete. */
+    if (MODE != MODE_SAMPLE && warp < kConsumerWarps)
+#pragma unroll 4
+        for (int i = tid; i < nloc; i += kConsumerWarps * 32) sw_s[i] = __ldg(p.scale_w + c0 + i);
     if (!stream_warp) {
         grid_dep_wait();
+        if (tid == 0) stamp(p, cta * 8 + 3); /* the previous kernel is complete */
         load_params();
     }
 
@@ -370,10 +372,13 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
             }
         }
         if (MODE != MODE_LMHEAD) {
+            /* the ring's slots, loaded with the parameters rather than after
+             * them (one round trip): only i < hn count, and only with a
+             * penalty */
 #pragma unroll
             for (int j = 0; j < kHReg; ++j) {
                 const int i = ctid + j * NC;
-                ids[j] = (use_pen && i < hn) ? __ldg(p.hist_ids + i) : -1;
+                ids[j] = i < p.hist_cap ? __ldcg(p.hist_ids + i) : -1;
             }
         }
         /* the final RMSNorm's weights, when the step takes the residual
@@ -387,9 +392,6 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
                 wv[j] = i < p.d ? __ldg(p.norm_w + i) : 0.0f;
             }
         }
-        if (MODE != MODE_SAMPLE)
-#pragma unroll 4
-            for (int i = ctid; i < nloc; i += NC) sw_s[i] = __ldg(p.scale_w + c0 + i);
         if (norm) {
             /* runtime/lal_simd_optim.h:32-58 through the key histogram's
              * shared memory (zeroed after): eight lane sums, combined and
@@ -420,6 +422,7 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
             for (int i = ctid + kHReg * NC; i < p.d; i += NC) m = fmaxf(m, fabsf(__ldg(h + i)));
         }
         m = consumer_max_f(m, ms); /* also orders the zeroing before the adds */
+        if (ctid == 0) stamp(p, cta * 8 + 6); /* the hidden vector's maximum */
         if (MODE != MODE_LMHEAD && use_pen) {
             /* runtime/lal_sampling.h:60-66: ids outside [0, V) are skipped */
             auto count = [&](int t) {
@@ -428,8 +431,9 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
                 if (g >= c0 && g < c1) atomicAdd(&cnt_s[g - c0], 1u);
             };
 #pragma unroll
-            for (int j = 0; j < kHReg; ++j) count(ids[j]);
-            for (int i = ctid + kHReg * NC; i < hn; i += NC) count(__ldg(p.hist_ids + i));
+            for (int j = 0; j < kHReg; ++j)
+                if (ctid + j * NC < hn) count(ids[j]);
+            for (int i = ctid + kHReg * NC; i < hn; i += NC) count(__ldcg(p.hist_ids + i));
         }
         if (MODE == MODE_FUSED) {
             /* lal_quantize_x_int8 (runtime/lal_q8_kernel.h:375-424), redundantly
@@ -493,7 +497,7 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
                      * stream: a full ring's burst (25 MB over the grid) slows
                      * that kernel's serial tail; measured 93.0 against 93.4 us
                      * a step back to back */
-                    if (c == kEarlyStages - 1) grid_dep_wait();
+                    if (c == p.early_stages - 1) grid_dep_wait();
                 }
                 /* Do not leave copies in flight: wait (bounded) for the last
                  * issued stages to land before the CTA may exit. */
@@ -934,7 +938,8 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
      * max_l (runtime/lal_sampling.h:107-109) is known before T; the weights'
      * exception-bitmap loads are issued now and consumed after the select,
      * hiding their latency behind it. */
-    const bool early = fine && !greedy && S <= 2 * NT && S <= ccap;
+    const bool early = fine && !greedy && S <= 2 * NT && S <= ccap && p.peer_recv == nullptr &&
+                       p.shard_out == nullptr;
     float max_l = -1e30f;
     float xw[2] = {0.0f, 0.0f};
     uint32_t bw[2] = {0u, 0u}, olo[2] = {0u, 0u}, ohi[2] = {0u, 0u};
@@ -971,12 +976,25 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
     /* at most one superset entry a thread: the candidates are placed in
      * ascending vocab order straight from the superset */
     const bool small = fine && S <= NT;
+    /* A shard whose slots dropped nothing exports its whole superset (every
+     * key >= the bound L, a set holding {l >= T_shard}) in vocab order: the
+     * merge selects the global T among the records in any case, so this
+     * rank's own threshold search is left out.  Threshold key 1 is below
+     * every real key and above the superset's zero padding. */
+    bool export_all = false;
+    if (small && local_edges && (p.peer_recv != nullptr || p.shard_out != nullptr) &&
+        S <= p.rec_cap) {
+        const uint32_t drop = tid < G ? ms->gm[tid] : 0u;
+        export_all = __syncthreads_or(drop != 0u) == 0;
+    }
     if (fine) {
         /* the superset is padded with zero keys (never greater, never a
          * candidate) to a multiple of 4 for 16-byte reads */
         const int S4 = (S + 3) & ~3;
         const uint4 *K4 = reinterpret_cast<const uint4 *>(Sk);
-        if (S <= 256) {
+        if (export_all) {
+            T = 1u;
+        } else if (S <= 256) {
             /* T = min{ key : #{keys > key} < k } -- one pass per element */
             uint32_t best = 0xffffffffu;
             for (int t = tid; t < S; t += NT) {
@@ -1569,6 +1587,165 @@ __device__ void merge_wide(const MergeParams &mp, int b, MergeHead &hd, const ui
     __syncthreads();
 }
 
+/* The merge when the gathered entries fit two a thread (M <= 2 NT: N
+ * records of about k entries each, the usual case).  Thread t holds entries
+ * t and t + NT; the concatenated records are in ascending vocab order
+ * already, so a candidate's place in the draw order is the number of
+ * candidates before it in entry order.  Five barriers: threshold and
+ * maximum, places, weights in place, the sequential sum (one thread), the
+ * draw. */
+__device__ __noinline__ void merge_small(const MergeParams &mp, int b, int M, const uint32_t *Mk,
+                                         const int *Mi, float *Cw, Misc *ms, StreamDiag dg,
+                                         bool greedy, float temp, int topk, float u0, int hn,
+                                         int hhead) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    auto mstamp = [&](int i) {
+        if (mp.phase_ts && tid == 0) mp.phase_ts[i] = gtimer();
+    };
+    bool have[2];
+    uint32_t me[2];
+    int mi[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int e = tid + h * NT;
+        have[h] = e < M;
+        me[h] = have[h] ? Mk[e] : 0u;
+        mi[h] = have[h] ? Mi[e] : 0;
+    }
+    /* k = min(top_k, V) (runtime/lal_sampling.h:70-71), 1 for greedy; every
+     * shard exported at least min(k, its rows) entries */
+    int k = greedy ? 1 : topk;
+    if (k > mp.vocab) k = mp.vocab;
+    if (k > M) k = M;
+    if (k < 1) k = 1;
+    /* T = min{ key : #{keys > key} < k } (the k-th largest with
+     * multiplicity), and the largest key (max_l) */
+    int gt[2] = {0, 0};
+    {
+        const uint4 *K4 = reinterpret_cast<const uint4 *>(Mk);
+        int j = 0;
+        if ((reinterpret_cast<uintptr_t>(Mk) & 15u) == 0)
+            for (; j + 4 <= M; j += 4) {
+                const uint4 v = K4[j >> 2];
+#pragma unroll
+                for (int h = 0; h < 2; ++h)
+                    gt[h] += (v.x > me[h]) + (v.y > me[h]) + (v.z > me[h]) + (v.w > me[h]);
+            }
+        for (; j < M; ++j)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) gt[h] += Mk[j] > me[h];
+    }
+    uint32_t best = 0xffffffffu;
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+        if (have[h] && gt[h] < k) best = min(best, me[h]);
+    best = __reduce_min_sync(0xffffffffu, best);
+    const uint32_t wmx = __reduce_max_sync(0xffffffffu, max(me[0], me[1]));
+    if (lane == 0) {
+        ms->scan[warp] = best;
+        ms->wmax[warp] = wmx;
+    }
+    if (tid == 0) ms->found = -1;
+    __syncthreads();
+    uint32_t T = ms->scan[0], mx = ms->wmax[0];
+    for (int w = 1; w < NWARP; ++w) {
+        T = min(T, ms->scan[w]);
+        mx = max(mx, ms->wmax[w]);
+    }
+    mstamp(0);
+    const float max_l = fmaxf(-1e30f, key2f(mx));
+    /* candidates {l >= T} and their places; each one's weight
+     * expf((l - max_l) / T) (runtime/lal_sampling.h:107-112) */
+    const ExpfTables ex{mp.expf_x, mp.expf_y, mp.expf_bits, mp.expf_off, mp.expf_hash,
+                        mp.expf_hash_probe};
+    bool cand[2];
+    unsigned bal[2];
+    float w[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        cand[h] = have[h] && me[h] >= T;
+        bal[h] = __ballot_sync(0xffffffffu, cand[h]);
+        if (lane == 0) ms->hist[h * NWARP + warp] = (uint32_t)__popc(bal[h]);
+        w[h] = cand[h] && !greedy ? ex.weight(key2f(me[h]), max_l, temp) : 0.0f;
+    }
+    __syncthreads();
+    int off[2] = {0, 0}, m = 0;
+    for (int v = 0; v < 2 * NWARP; ++v) {
+        const int c = (int)ms->hist[v];
+        off[0] += v < warp ? c : 0;
+        off[1] += v < NWARP + warp ? c : 0;
+        m += c;
+    }
+    int pos[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        pos[h] = off[h] + __popc(bal[h] & ((1u << lane) - 1u));
+        if (cand[h]) Cw[pos[h]] = w[h];
+        if (cand[h] && pos[h] == 0) ms->sh[15] = (uint32_t)mi[h]; /* the first candidate */
+    }
+    __syncthreads();
+    mstamp(1);
+    dg.threshold = key2f(T);
+    dg.max_l = max_l;
+    dg.n_cand = m;
+    int token = (int)ms->sh[15];
+    if (!greedy) {
+        /* sequential float sum in ascending vocab order, the running sums in
+         * place (values fetched eight at a time, the adds in order) */
+        if (tid == 0) {
+            float acc = 0.0f;
+            int i = 0;
+            for (; i + 8 <= m; i += 8) {
+                float v[8];
+#pragma unroll
+                for (int q = 0; q < 8; ++q) v[q] = Cw[i + q];
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    acc = __fadd_rn(acc, v[q]);
+                    Cw[i + q] = acc;
+                }
+            }
+            for (; i < m; ++i) {
+                acc = __fadd_rn(acc, Cw[i]);
+                Cw[i] = acc;
+            }
+            ms->sum = acc;
+        }
+        __syncthreads();
+        mstamp(2);
+        const float sum = ms->sum;
+        dg.sum = sum;
+        if (mp.variant == VARIANT_SERVER && sum <= 0.0f) {
+            /* tools/server/qwen7b_server.c:285-286, the argmax over the kept
+             * candidates with '>' from -1e30f: the sum is 0 only when every
+             * candidate lies at or below -1e30 (the largest one weighs
+             * expf(0) = 1 otherwise), so that argmax keeps row 0 */
+            token = 0;
+        } else {
+            /* r = u * sum; the first candidate with r <= its running sum
+             * (runtime/lal_sampling.h:116-124): the sums do not decrease, so
+             * it is the one whose predecessor's sum is below r */
+            const float r = __fmul_rn(u0, sum);
+            dg.r = r;
+            dg.drew = 1;
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+                if (cand[h] && r <= Cw[pos[h]] && !(pos[h] > 0 && r <= Cw[pos[h] - 1]))
+                    ms->found = mi[h];
+            __syncthreads();
+            token = ms->found >= 0 ? ms->found : mp.vocab - 1;
+            if (mp.variant == VARIANT_GPT2 && r == 0.0f) token = 0;
+        }
+    }
+    mstamp(4);
+    if (tid == 0) {
+        dg.token = token;
+        mp.tokens[b] = token;
+        mp.diag[b] = dg;
+        merge_push(mp, b, token, hn, hhead);
+    }
+}
+
 /* The merge of stream b's N shard records and its draw, by one CTA (NT
  * threads): shared by merge_kernel (records all-gathered into global memory)
  * and the fused kernel's peer exchange (records written by the peers over
@@ -1620,6 +1797,10 @@ __device__ void merge_sample(const MergeParams &mp, int b, uint8_t *area, Misc *
         return;
     }
     const int M = hd.roff[mp.n_ranks];
+    if (M <= 2 * NT) {
+        merge_small(mp, b, M, Mk, Mi, Ce, ms, dg, greedy, temp, topk, u0, hn, hhead);
+        return;
+    }
     /* k = min(top_k, V) (runtime/lal_sampling.h:70-71), 1 for greedy; every
      * shard exported at least min(k, its rows) entries, so M >= k */
     int k = greedy ? 1 : topk;
@@ -1639,79 +1820,27 @@ __device__ void merge_sample(const MergeParams &mp, int b, uint8_t *area, Misc *
     __syncthreads();
     const float max_l = fmaxf(-1e30f, key2f(mx));
     dg.max_l = max_l;
-    /* weights expf((l - max_l) / T) (runtime/lal_sampling.h:112): the table
-     * loads go out now and complete behind the threshold search */
-    const bool fast = M <= 2 * NT;
-    float xw[2] = {0.0f, 0.0f};
-    uint32_t bw[2] = {0u, 0u}, olo[2] = {0u, 0u}, ohi[2] = {0u, 0u};
-    uint4 hp[2] = {make_uint4(0u, 0u, 0u, 0u), make_uint4(0u, 0u, 0u, 0u)};
-    float yr[2] = {0.0f, 0.0f};
-    if (!greedy) {
-        if (fast) {
-#pragma unroll
-            for (int r = 0; r < 2; ++r) {
-                const int e = tid + r * NT;
-                if (e < M) {
-                    xw[r] = __fdiv_rn(__fsub_rn(key2f(Mk[e]), max_l), temp);
-                    if (mp.expf_hash) {
-                        hp[r] = expf_hash_load(xw[r], mp.expf_hash);
-                        yr[r] = lal_expf_rounded(xw[r]);
-                    } else {
-                        bw[r] = expf_bitmap_word(xw[r], mp.expf_bits);
-                        expf_offsets(xw[r], mp.expf_off, &olo[r], &ohi[r]);
-                    }
-                }
-            }
-        } else {
-            for (int e = tid; e < M; e += NT) {
-                const float x = __fdiv_rn(__fsub_rn(key2f(Mk[e]), max_l), temp);
-                Mw[e] = mp.expf_hash ? expf_hash_finish(x, expf_hash_load(x, mp.expf_hash),
-                                                        mp.expf_hash, mp.expf_hash_probe)
-                                     : sampler_expf(x, mp.expf_x, mp.expf_y, mp.expf_bits,
-                                                    mp.expf_off);
-            }
+    auto mstamp = [&](int i) {
+        if (mp.phase_ts && tid == 0) mp.phase_ts[i] = gtimer();
+    };
+    mstamp(0);
+    /* weights expf((l - max_l) / T) (runtime/lal_sampling.h:112) of every
+     * entry, then T by the radix select (more than 2 NT entries) */
+    if (!greedy)
+        for (int e = tid; e < M; e += NT) {
+            const float x = __fdiv_rn(__fsub_rn(key2f(Mk[e]), max_l), temp);
+            Mw[e] = mp.expf_hash ? expf_hash_finish(x, expf_hash_load(x, mp.expf_hash),
+                                                    mp.expf_hash, mp.expf_hash_probe)
+                                 : sampler_expf(x, mp.expf_x, mp.expf_y, mp.expf_bits,
+                                                mp.expf_off);
         }
-    }
-    /* T = min{ key : #{keys > key} < k }, the k-th largest with multiplicity */
-    uint32_t T;
-    if (fast) {
-        uint32_t best = 0xffffffffu;
-#pragma unroll
-        for (int r = 0; r < 2; ++r) {
-            const int e = tid + r * NT;
-            if (e < M) {
-                const uint32_t me = Mk[e];
-                int gt = 0;
-#pragma unroll 4
-                for (int j = 0; j < M; ++j) gt += Mk[j] > me;
-                if (gt < k) best = min(best, me);
-            }
-        }
-        best = __reduce_min_sync(0xffffffffu, best);
-        if ((tid & 31) == 0) ms->scan[tid >> 5] = best;
-        __syncthreads();
-        T = ms->scan[0];
-        for (int w = 1; w < NWARP; ++w) T = min(T, ms->scan[w]);
-        if (!greedy)
-#pragma unroll
-            for (int r = 0; r < 2; ++r) {
-                const int e = tid + r * NT;
-                if (e < M)
-                    Mw[e] = mp.expf_hash
-                                ? expf_hash_resolve(xw[r], yr[r], hp[r], mp.expf_hash,
-                                                    mp.expf_hash_probe)
-                                : expf_with_range(xw[r], bw[r], olo[r], ohi[r], mp.expf_x,
-                                                  mp.expf_y);
-            }
-        __syncthreads();
-    } else {
-        T = block_kth_largest(
-            [&](int i, uint32_t &key) {
-                key = Mk[i];
-                return true;
-            },
-            M, k, ms);
-    }
+    const uint32_t T = block_kth_largest(
+        [&](int i, uint32_t &key) {
+            key = Mk[i];
+            return true;
+        },
+        M, k, ms);
+    mstamp(1);
     /* candidates {l >= T}, order kept (stable compaction), with weights */
     const int seg = (M + NT - 1) / NT;
     const int e0 = min(M, tid * seg), e1 = min(M, e0 + seg);
@@ -1728,6 +1857,7 @@ __device__ void merge_sample(const MergeParams &mp, int b, uint8_t *area, Misc *
             ++pos;
         }
     __syncthreads();
+    mstamp(2);
     dg.threshold = key2f(T);
     dg.n_cand = m;
     int token;
@@ -1745,6 +1875,7 @@ __device__ void merge_sample(const MergeParams &mp, int b, uint8_t *area, Misc *
             ms->found = 0x7fffffff;
         }
         __syncthreads();
+        mstamp(3);
         const float sum = ms->sum;
         dg.sum = sum;
         if (mp.variant == VARIANT_SERVER && sum <= 0.0f) {
@@ -1773,6 +1904,7 @@ __device__ void merge_sample(const MergeParams &mp, int b, uint8_t *area, Misc *
             token = ms->found != 0x7fffffff ? Ci[ms->found] : mp.vocab - 1;
         }
     }
+    mstamp(4);
     if (tid == 0) {
         dg.token = token;
         mp.tokens[b] = token;
@@ -1902,6 +2034,11 @@ int plan_launch(TailParams &p, int num_sms, int min_rows_per_cta) {
         p.stage_bytes = align_up(R * p.ld, 128);
         p.stages = std::min(kMaxStages, budget / p.stage_bytes);
         if (p.stages < 2) return -4;
+        /* stages issued before the previous kernel completes: two, or the
+         * whole ring when a CTA's slice is short (a vocab shard), where the
+         * prefetched part is a large share of its rows */
+        p.early_stages = (long long)p.rows_per_cta_max * p.ld <= 12ll * p.stage_bytes
+                             ? p.stages : std::min(kEarlyStages, p.stages);
         p.area_bytes = p.stages * p.stage_bytes;
         /* after the rows, the stage area holds the local key histogram and,
          * in the last CTA, the superset and the candidates */

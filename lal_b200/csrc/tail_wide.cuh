@@ -467,19 +467,16 @@ __device__ __noinline__ void wide_dense(const WideDense &a, uint8_t *area, Misc 
         const uint64_t hi = (uint64_t)a.seq << 32;
         for (int r = 0; r < a.n_ranks; ++r) {
             uint64_t *w64 = reinterpret_cast<uint64_t *>(a.peer_recv[r] + slot);
-            for (int i = tid; i < ne; i += NT) {
-                st_sys_u64(w64 + 4 + 2 * i, hi | __float_as_uint(key2f(Xk[i])));
-                st_sys_u64(w64 + 5 + 2 * i, hi | (uint32_t)Xi[i]);
-            }
+            for (int i = tid; i < ne; i += NT)
+                st_sys_pair(w64 + 4 + 2 * i, hi | __float_as_uint(key2f(Xk[i])),
+                            hi | (uint32_t)Xi[i]);
             for (int w = warp; w < words; w += NWARP) {
                 const uint32_t b = tie_word(lg, rows, w, T);
                 if (lane == 0) st_sys_u64(w64 + 4 + 2 * a.rec_cap + w, hi | b);
             }
             if (tid == 0) {
-                st_sys_u64(w64 + 0, hi | (uint32_t)ne);
-                st_sys_u64(w64 + 1, hi);
-                st_sys_u64(w64 + 2, hi | ties);
-                st_sys_u64(w64 + 3, hi | T);
+                st_sys_pair(w64, hi | (uint32_t)ne, hi);
+                st_sys_pair(w64 + 2, hi | ties, hi | T);
             }
         }
         if (tid == 0 && a.diag) *a.diag = dg;

@@ -279,6 +279,64 @@ def test_nccl_ranks_match_reference(golden, tmp_path, p2p):
                                   np.load(tmp_path / f"hist{world - 1}.npy"))
 
 
+def _wide_worker(rank, world, port, out_dir, p2p):
+    """Steps whose tie set outgrows a record (all-zero hidden vectors: every
+    logit 0.0) between normal ones, on real ranks: the record's wide form
+    through the peer exchange (p2p) or the NCCL all-gather."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from lal_b200.sharded import ShardedDecodeTail
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    spec = cases.loop_cases()["c1_gpt2"]
+    cfg, W, hist0 = cases.loop_inputs(spec)
+    q, s = oracle.quantize_rows(W, "port")
+    st = ShardedDecodeTail(cfg.vocab, cfg.n_embd, device=rank, max_top_k=cfg.top_k,
+                           history_cap=cfg.hist, sampler=0, p2p=p2p)
+    st.load_lm_head_q8(q[st.row0:st.row0 + st.n_rows], s[st.row0:st.row0 + st.n_rows])
+    st.set_sampling([cfg.temperature], [cfg.top_k], [cfg.rep_penalty])
+    st.set_history(0, hist0)
+    port = oracle.PortLoop(q, s, hist0, cfg.hist, cfg.temperature, cfg.top_k,
+                           cfg.rep_penalty, 0)
+    got, want = [], []
+    for step in range(6):
+        h = (np.zeros((1, cfg.n_embd), np.float32) if step % 2 == 0
+             else synth.hidden(cfg, step))
+        u = np.float32(0.15 + 0.13 * step)
+        got.append(int(st.step(h, np.array([u], np.float32))[0]))
+        want.append(port.step(h[0], u)[0])
+    hist = st.get_history(0)
+    st.close()
+    dist.destroy_process_group()
+    np.save(os.path.join(out_dir, f"w{rank}.npy"), np.array([got, want], np.int32))
+    np.save(os.path.join(out_dir, f"wh{rank}.npy"), np.stack([hist, port.history()]))
+
+
+@pytest.mark.parametrize("p2p", [False, True])
+def test_ranks_exchange_wide_records(tmp_path, p2p):
+    """Two processes, one GPU each: all-zero hidden vectors (every logit tied
+    at 0.0) between normal steps return the oracle's tokens on both ranks."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("one GPU: the multi-GPU paths run under a multi-GPU call")
+    import torch.multiprocessing as mp
+    mp.start_processes(_wide_worker, args=(2, _free_port(), str(tmp_path), p2p), nprocs=2,
+                       join=True, start_method="spawn")
+    for r in range(2):
+        got, want = np.load(tmp_path / f"w{r}.npy")
+        np.testing.assert_array_equal(got, want)
+        h = np.load(tmp_path / f"wh{r}.npy")
+        np.testing.assert_array_equal(h[0], h[1])
+
+
 def _p2p_timeout_worker(rank, world, port, out_dir):
     import datetime
 
