@@ -287,6 +287,13 @@ int lal_tail_set_filter(lal_tail *t, lal_filter_topk_fn filter, lal_token_decode
  * (the reference's scalar tail loop, whose rounding its compiler decides, is
  * then empty; LAL_TAIL_ERR_UNSUPPORTED otherwise). */
 int lal_tail_set_final_norm(lal_tail *t, const float *norm_w, float eps);
+/* The GPT-2 server's nucleus (top-p) step, applied after top-k and before
+ * the softmax (tools/server/gpt2_server.c:2895-2960, its --top-p; 0 = off,
+ * the server's default, :2343): the top-k pool's temperature softmax,
+ * sorted by descending probability (ties by ascending row), keeps rows until
+ * the running probability reaches top_p.  Values are clamped to [0, 1] as
+ * the server clamps them (:3147-3148).  Only LAL_SAMPLER_GPT2 contexts. */
+int lal_tail_set_top_p(lal_tail *t, float top_p);
 /* How a step of n_streams streams runs on this context (no counterpart in
  * the reference): one fused launch per stream, the batched tensor-core step
  * (quantize, one tcgen05 GEMM pass over the LM head for every stream, a

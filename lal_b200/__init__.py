@@ -132,6 +132,7 @@ SIGNATURES = {
     "lal_tail_set_final_norm": (C.c_int, [_vp, _vp, C.c_float]),
     "lal_tail_set_lm_head_copies": (C.c_int, [_vp, _ip]),
     "lal_tail_step_kind": (C.c_int, [_vp, _ip]),
+    "lal_tail_set_top_p": (C.c_int, [_vp, C.c_float]),
     "lal_tail_gpq8_find": (C.c_int, [_vp, C.c_size_t, C.c_char_p, C.POINTER(Gpq8Tensor)]),
     "lal_tail_load_lm_head_gpq8": (C.c_int, [_vp, _vp, C.c_size_t, C.c_char_p]),
     "lal_tail_sample_token_noalloc": (C.c_int, [_vp, _ip, _fp, _ip, _fp, _vp, _ip, _fp, _vp,
@@ -455,6 +456,11 @@ class DecodeTail:
 
     def disconnect_peers(self):
         _check(lib().lal_tail_disconnect_peers(self.h))
+
+    def set_top_p(self, top_p: float):
+        """The GPT-2 server's nucleus step (gpt2_server.c:2895-2960), after
+        top-k; 0 switches it off.  LAL_SAMPLER_GPT2 contexts only."""
+        _check(lib().lal_tail_set_top_p(self.h, C.c_float(top_p)))
 
     STEP_KINDS = {0: "per_stream", 1: "batched", 2: "gpt2"}
 

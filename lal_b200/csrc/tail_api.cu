@@ -1944,6 +1944,21 @@ int lal_tail_load_lm_head_gpq8(lal_tail *t, const void *blob, size_t size, const
     return lal_tail_load_lm_head_q8(t, q, sc.data());
 }
 
+int lal_tail_set_top_p(lal_tail *t, float top_p) {
+    CHECK(ctx_check(t));
+    if (t->cfg.sampler != LAL_SAMPLER_GPT2)
+        return fail(LAL_TAIL_ERR_UNSUPPORTED,
+                    "set_top_p: only the GPT-2 server's sampler has a nucleus step");
+    if (top_p != top_p) return fail(LAL_TAIL_ERR_ARG, "set_top_p: NaN");
+    /* gpt2_server.c:3147-3148 clamps the request to [0, 1]; 0 and 1 keep the
+     * whole top-k pool */
+    if (top_p < 0.0f) top_p = 0.0f;
+    if (top_p > 1.0f) top_p = 1.0f;
+    CU(cudaStreamSynchronize(t->stream));
+    t->g2_smp.top_p = top_p;
+    return LAL_TAIL_OK;
+}
+
 int lal_tail_step_kind(lal_tail *t, int n_streams) {
     if (!t) return -fail(LAL_TAIL_ERR_ARG, "null context");
     if (n_streams < 1 || n_streams > t->cfg.max_streams)

@@ -475,14 +475,12 @@ __global__ void __launch_bounds__(NT, 1) batch_select_kernel(const __grid_consta
      * (runtime/lal_sampling.h:60-66; ids outside [0, V) are skipped) */
     for (int i = tid; i < 4096; i += NT) hist[i] = 0u;
     __shared__ int s_pen; /* distinct history ids inside this slice */
-    __shared__ int s_pen_groups; /* 32-row groups holding one of them */
     /* which 32-row groups hold a penalised row (slices of up to
      * kPenGroupWords * 32 groups) */
     __shared__ uint32_t pen_groups[kPenGroupWords];
     const bool mark = p.n_groups <= kPenGroupWords * 32;
     if (tid == 0) {
         s_pen = 0;
-        s_pen_groups = 0;
     }
     for (int i = tid; i < kPenGroupWords; i += NT) pen_groups[i] = 0u;
     if (use_pen) {
@@ -507,8 +505,7 @@ __global__ void __launch_bounds__(NT, 1) batch_select_kernel(const __grid_consta
                         if (mark) {
                             const int gi = g >> 5;
                             const uint32_t bit = 1u << (gi & 31);
-                            if (!(atomicOr(&pen_groups[gi >> 5], bit) & bit))
-                                atomicAdd(&s_pen_groups, 1);
+                            atomicOr(&pen_groups[gi >> 5], bit);
                         }
                     }
                     break;
@@ -546,11 +543,15 @@ __global__ void __launch_bounds__(NT, 1) batch_select_kernel(const __grid_consta
     /* 3. a tie-complete superset of {l >= T}: keys >= a lower bound L of T.
      *
      * Group bound (the GEMM recorded each 32-row group's largest raw logit):
-     * with P distinct penalised ids in the slice, the (k+P)-th largest group
-     * maximum L is <= T -- its k+P groups hold k+P distinct logits >= L, at
-     * most P of them penalised, and a penalty (p > 1) never raises a logit --
-     * and only groups whose raw maximum reaches L can hold a key >= L.  When
-     * that bound is weak the full histogram pass below is used instead. */
+     * with every group's maximum a logit of the step (the penalised groups'
+     * taken again below), the k-th largest group maximum L is <= T -- k
+     * groups hold k distinct logits >= L -- and only groups whose maximum
+     * reaches L can hold a key >= L.  Without the group marks (a slice of
+     * more than kPenGroupWords * 32 groups), with P distinct penalised ids,
+     * the (k+P)-th largest raw maximum is: its k+P groups hold k+P distinct
+     * logits >= L, at most P of them penalised, and a penalty (p > 1) never
+     * raises a logit.  When the bound is weak the full histogram pass below
+     * is used instead. */
     auto hist_add = [&](uint32_t *h, uint32_t digit, bool act) {
         const unsigned voters = __ballot_sync(0xffffffffu, act);
         if (act) {
@@ -564,12 +565,15 @@ __global__ void __launch_bounds__(NT, 1) batch_select_kernel(const __grid_consta
      * rows count towards the bound: their maxima are unchanged logits of k
      * distinct rows, so the k-th largest of them is <= T; otherwise every
      * group counts and the (k+P)-th largest maximum is the bound */
-    const bool excl = mark && p.n_groups - s_pen_groups >= k;
-    const int kp = excl ? k : k + s_pen;
-    const bool groups = p.gmax != nullptr && kp <= p.n_groups / 8 && p.n_groups <= p.s_cap;
-    auto counts = [&](int g) {
-        return g < p.n_groups && !(excl && ((pen_groups[g >> 5] >> (g & 31)) & 1u));
-    };
+    /* With the penalised groups marked, each one's maximum is taken again
+     * after the penalty (the GEMM's is of the raw logits): every group
+     * maximum is then a logit of the step, k groups reach their k-th largest,
+     * and that maximum bounds T from below.  Without the marks, the (k+P)-th
+     * largest raw maximum does (see above). */
+    const bool exact = mark;
+    const int kp = exact ? k : k + s_pen;
+    const bool groups = p.gmax != nullptr && kp <= p.n_groups / 2 && p.n_groups <= p.s_cap;
+    auto counts = [&](int g) { return g < p.n_groups; };
     if (groups) {
         /* the group maxima (contiguous per stream) into Sk and the top 12 key
          * bits of the counted ones into the histogram; the lower edge of the
@@ -582,22 +586,63 @@ __global__ void __launch_bounds__(NT, 1) batch_select_kernel(const __grid_consta
             for (int j = 0; j < kGroupRegs; ++j) {
                 const int g = j * NT + tid;
                 if (g < p.n_groups) Gk[g] = gpre[j];
-                hist_add(hist, gpre[j] >> 20, counts(g));
             }
-        } else
-        for (int g0 = 0; g0 < p.n_groups; g0 += NT * U) {
-            uint32_t v[U];
+        } else {
+            for (int g = tid; g < p.n_groups; g += NT) Gk[g] = __ldg(gm + g);
+        }
+        if (exact && use_pen) {
+            /* the marked groups, listed in Gl (free until the candidate
+             * groups), then each one's maximum after the penalty, one group a
+             * thread with eight 16-byte loads */
+            if (tid == 0) s_count = 0;
+            __syncthreads();
+            const int words = (p.n_groups + 31) >> 5;
+            for (int w0 = 0; w0 < words; w0 += NT) {
+                const int w = w0 + tid;
+                const uint32_t bits = w < words ? pen_groups[w] : 0u;
+                const int c = __popc(bits);
+                const int lane = tid & 31;
+                int incl = c;
 #pragma unroll
-            for (int j = 0; j < U; ++j) {
-                const int g = g0 + j * NT + tid;
-                v[j] = g < p.n_groups ? __ldg(gm + g) : 0u;
+                for (int o = 1; o < 32; o <<= 1) {
+                    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+                    if (lane >= o) incl += y;
+                }
+                int base = 0;
+                if (lane == 31) base = atomicAdd(&s_count, incl);
+                base = __shfl_sync(0xffffffffu, base, 31) + incl - c;
+                uint32_t rest = bits;
+                while (rest) {
+                    Gl[base++] = 32 * w + __ffs(rest) - 1;
+                    rest &= rest - 1u;
+                }
             }
+            __syncthreads();
+            const int nm = s_count;
+            const bool lg16 = (reinterpret_cast<uintptr_t>(lg) & 15u) == 0;
+            for (int i = tid; i < nm; i += NT) {
+                const int g = Gl[i];
+                const int r0 = g * 32, r1 = min(p.rows, r0 + 32);
+                uint32_t mx = 0u;
+                if (lg16 && r1 == r0 + 32) {
+                    const float4 *v4 = reinterpret_cast<const float4 *>(lg + r0);
+                    float4 v[8];
 #pragma unroll
-            for (int j = 0; j < U; ++j) {
-                const int g = g0 + j * NT + tid;
-                if (g < p.n_groups) Gk[g] = v[j];
-                hist_add(hist, v[j] >> 20, counts(g));
+                    for (int q = 0; q < 8; ++q) v[q] = __ldcg(v4 + q);
+#pragma unroll
+                    for (int q = 0; q < 8; ++q)
+                        mx = max(max(max(mx, f2key(v[q].x)), f2key(v[q].y)),
+                                 max(f2key(v[q].z), f2key(v[q].w)));
+                } else {
+                    for (int r = r0; r < r1; ++r) mx = max(mx, f2key(__ldcg(lg + r)));
+                }
+                Gk[g] = mx;
             }
+        }
+        __syncthreads();
+        for (int g0 = 0; g0 < p.n_groups; g0 += NT) {
+            const int g = g0 + tid;
+            hist_add(hist, g < p.n_groups ? Gk[g] >> 20 : 0u, counts(g));
         }
         __syncthreads();
         uint32_t gab, gcnt;
@@ -622,7 +667,7 @@ __global__ void __launch_bounds__(NT, 1) batch_select_kernel(const __grid_consta
         __syncthreads();
         const int ng = s_count;
         __syncthreads();
-        if (ng <= p.n_groups / 4) {
+        if (ng <= p.n_groups / 2) {
             if (tid == 0) s_count = 0;
             /* gather the groups' keys >= L (32 consecutive rows a group):
              * each round copies up to kStageGroups groups into shared memory
@@ -893,8 +938,20 @@ __global__ void __launch_bounds__(NT, 1) batch_select_kernel(const __grid_consta
         }
         __syncthreads();
         if (tid == 0) {
+            /* values fetched eight at a time, the adds in order */
             float acc = 0.0f;
-            for (int i = 0; i < m; ++i) {
+            int i = 0;
+            for (; i + 8 <= m; i += 8) {
+                float v[8];
+#pragma unroll
+                for (int q = 0; q < 8; ++q) v[q] = Ce[i + q];
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    acc = __fadd_rn(acc, v[q]);
+                    Ce[i + q] = acc;
+                }
+            }
+            for (; i < m; ++i) {
                 acc = __fadd_rn(acc, Ce[i]);
                 Ce[i] = acc;
             }

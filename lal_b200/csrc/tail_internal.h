@@ -203,6 +203,9 @@ struct TailParams {
     int *cand_idx_out;
     int cand_out_cap;
     int candidates_only;     /* stop after exporting candidates (no draw)     */
+    /* VARIANT_GPT2: the server's nucleus over the candidates when
+     * 0 < top_p < 1 (gpt2_server.c:2908-2955), else off */
+    float top_p;
     /* vocab-sharded step: write this stream's candidate record (status,
      * count, ascending-index list of at most rec_cap) and stop */
     uint8_t *shard_out;

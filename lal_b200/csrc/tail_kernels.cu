@@ -204,6 +204,57 @@ struct PeerRecords {
     }
 };
 
+/* The GPT-2 server's nucleus (gpt2_server.c:2908-2955) over the m
+ * candidates of a step: Oi their rows in ascending order, Ce their terms
+ * expf((l - max_l) / T).  Every thread calls it.  The terms are summed in row
+ * order, inv = 1 / (sum + 1e-12f), each probability is term * inv; the rows
+ * are taken in the order of the server's insertion sort (descending
+ * probability, equal probabilities by ascending row) until the running
+ * probability reaches top_p, the row that reaches it included.  The largest
+ * term stays (it is first in that order), so the kept rows' softmax over
+ * their own maximum has the same terms: on return Ce holds them for kept rows
+ * and 0 for the rest.  P, R, Q: scratch of m entries.  Returns the count
+ * kept. */
+__device__ __noinline__ int gpt2_nucleus(float top_p, int m, float *Ce, float *P, int *R,
+                                         float *Q, Misc *ms) {
+    const int tid = threadIdx.x;
+    if (tid == 0) {
+        float acc = 0.0f;
+        for (int i = 0; i < m; ++i) acc = __fadd_rn(acc, Ce[i]);
+        ms->sum = acc;
+    }
+    __syncthreads();
+    const float inv = __fdiv_rn(1.0f, __fadd_rn(ms->sum, 1e-12f));
+    for (int i = tid; i < m; i += NT) P[i] = __fmul_rn(Ce[i], inv);
+    __syncthreads();
+    for (int i = tid; i < m; i += NT) {
+        const float pi = P[i];
+        int r = 0;
+        for (int j = 0; j < m; ++j) r += (P[j] > pi) || (P[j] == pi && j < i);
+        R[i] = r;
+        Q[r] = pi;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        float cum = 0.0f;
+        int n = m;
+        for (int j = 0; j < m; ++j) {
+            cum = __fadd_rn(cum, Q[j]);
+            if (cum >= top_p) {
+                n = j + 1;
+                break;
+            }
+        }
+        ms->sh[0] = (uint32_t)n;
+    }
+    __syncthreads();
+    const int n_keep = (int)ms->sh[0];
+    for (int i = tid; i < m; i += NT)
+        if (R[i] >= n_keep) Ce[i] = 0.0f;
+    __syncthreads();
+    return n_keep;
+}
+
 /* The peer exchange's merge of this step (the fused kernel's last CTA, after
  * it published its record): wait for every rank's record, merge and draw
  * like merge_kernel. */
@@ -281,6 +332,7 @@ __device__ __noinline__ void tail_wide(const TailParams &p, int k, bool greedy, 
     a.cand_idx = p.cand_idx_out;
     a.cand_cap = p.cand_val_out ? p.cand_out_cap : 0;
     a.candidates_only = p.candidates_only;
+    a.top_p = p.variant == VARIANT_GPT2 ? p.top_p : 0.0f;
     wide_dense(a, smem, ms);
 }
 
@@ -1246,6 +1298,10 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
                                     : sampler_expf(x, p.expf_x, p.expf_y, p.expf_bits, p.expf_off);
             }
         __syncthreads();
+        /* the GPT-2 server's nucleus: the dropped rows' terms become 0 (its
+         * draw walks every row, zeros included) */
+        if (p.variant == VARIANT_GPT2 && p.top_p > 0.0f && p.top_p < 1.0f)
+            dg.n_cand = gpt2_nucleus(p.top_p, m, Ce, Cv, Ci, Cw, ms);
         /* sequential float sum in ascending vocab order; keep the prefix
          * (values fetched eight at a time, the adds stay in order) */
         if (tid == 0) {

@@ -206,7 +206,7 @@ struct WalkResult {
 template <class UnitOf, class Fill>
 __device__ WalkResult wide_walk(int n_units, UnitOf unit_of, Fill fill, uint32_t T, float wT,
                                 bool greedy, float u, int variant, uint32_t *bm, WideChunk *tab,
-                                Misc *ms) {
+                                Misc *ms, float r_direct = -1.0f) {
     const int tid = threadIdx.x;
     float acc = 0.0f;
     int ntab = 0, tok = -1;
@@ -258,11 +258,12 @@ __device__ WalkResult wide_walk(int n_units, UnitOf unit_of, Fill fill, uint32_t
     res.drew = 0;
     res.token = -1;
     if (!res.ok) return res;
-    if (!greedy && variant == VARIANT_SERVER && res.sum <= 0.0f) {
+    if (!greedy && r_direct < 0.0f && variant == VARIANT_SERVER && res.sum <= 0.0f) {
         res.token = 0;
         return res;
     }
-    const float r = greedy ? -1.0f : __fmul_rn(u, res.sum);
+    /* r_direct >= 0: find the first row whose running sum reaches it */
+    const float r = greedy ? -1.0f : r_direct >= 0.0f ? r_direct : __fmul_rn(u, res.sum);
     if (!greedy) {
         res.r = r;
         res.drew = 1;
@@ -357,6 +358,8 @@ struct WideDense {
     float *cand_val;
     int *cand_idx;
     int cand_cap, candidates_only;
+    /* VARIANT_GPT2: the server's nucleus when 0 < top_p < 1 */
+    float top_p;
 };
 
 /* bitmap word w of a slice: bit j set when row 32w + j equals T (warp-wide) */
@@ -517,17 +520,91 @@ __device__ __noinline__ void wide_dense(const WideDense &a, uint8_t *area, Misc 
         for (int i = tid; i < ne; i += NT) Xw[i] = a.ex.weight(key2f(Xk[i]), max_l, a.temp);
         if (tid == 0) ms->fred[0] = a.ex.weight(key2f(T), max_l, a.temp);
         __syncthreads();
-        const float wT = ms->fred[0];
-        const WalkUnit U{Xk, Xi, Xw, ne, 1, a.row_base, rows};
-        res = wide_walk(
-            1, [&](int) { return U; },
-            [&](int, int w0, int nw, uint32_t *dst) {
-                for (int w = warp; w < nw; w += NWARP) {
-                    const uint32_t b = tie_word(lg, rows, w0 + w, T);
-                    if (lane == 0) dst[w] = b;
+        float wT = ms->fred[0];
+        /* ties count only up to row tie_end (the nucleus may cut them) */
+        int tie_end = rows;
+        auto fill = [&](int, int w0, int nw, uint32_t *dst) {
+            for (int w = warp; w < nw; w += NWARP) {
+                uint32_t b = tie_word(lg, rows, w0 + w, T);
+                const int lo = 32 * (w0 + w);
+                if (lo + 32 > tie_end) b &= lo >= tie_end ? 0u : (1u << (tie_end - lo)) - 1u;
+                if (lane == 0) dst[w] = b;
+            }
+        };
+        WalkUnit U{Xk, Xi, Xw, ne, 1, a.row_base, rows};
+        if (a.variant == VARIANT_GPT2 && a.top_p > 0.0f && a.top_p < 1.0f) {
+            /* gpt2_server.c:2908-2955 with every tie sharing one probability
+             * pT: the explicit rows' probabilities are >= pT (a larger logit
+             * never weighs less), so the server's order is the rows above pT
+             * (descending, equal ones by row), then every row at exactly pT
+             * by row -- the ties and the explicit rows that round to pT */
+            const WalkResult s1 = wide_walk(1, [&](int) { return U; }, fill, T, wT, false, 0.0f,
+                                            VARIANT_LIBRARY, bm, tab, ms, 0.0f);
+            const float inv = __fdiv_rn(1.0f, __fadd_rn(s1.sum, 1e-12f));
+            const float pT = __fmul_rn(wT, inv);
+            float *P = reinterpret_cast<float *>(tk); /* free after the sort */
+            int *ord = ti;
+            for (int i = tid; i < ne; i += NT) P[i] = __fmul_rn(Xw[i], inv);
+            __syncthreads();
+            for (int i = tid; i < ne; i += NT)
+                if (P[i] > pT) {
+                    int r = 0;
+                    for (int j = 0; j < ne; ++j) r += P[j] > P[i] || (P[j] == P[i] && j < i);
+                    ord[r] = i;
                 }
-            },
-            T, wT, false, a.u, a.variant, bm, tab, ms);
+            __syncthreads();
+            if (tid == 0) {
+                int nA = 0;
+                for (int i = 0; i < ne; ++i) nA += P[i] > pT;
+                float cum = 0.0f;
+                int cut = -1; /* rows of the first group kept: ranks < cut */
+                for (int j = 0; j < nA && cut < 0; ++j) {
+                    cum = __fadd_rn(cum, P[ord[j]]);
+                    if (cum >= a.top_p) cut = j + 1;
+                }
+                /* c rows at pT, in row order, complete the nucleus */
+                int nE = (int)ties;
+                for (int i = 0; i < ne; ++i) nE += P[i] == pT;
+                int c = 0;
+                if (cut < 0)
+                    while (c < nE) {
+                        cum = __fadd_rn(cum, pT);
+                        ++c;
+                        if (cum >= a.top_p) break;
+                    }
+                ms->sh[0] = (uint32_t)(cut < 0 ? nA : cut);
+                ms->sh[1] = (uint32_t)c;
+            }
+            __syncthreads();
+            const int keepA = (int)ms->sh[0], c = (int)ms->sh[1];
+            /* the row of the c-th row at pT: a walk counting those rows */
+            int cut_row = a.row_base - 1;
+            if (c > 0) {
+                for (int i = tid; i < ne; i += NT) P[i] = P[i] == pT ? 1.0f : 0.0f;
+                __syncthreads();
+                const WalkUnit Uc{Xk, Xi, P, ne, 1, a.row_base, rows};
+                const WalkResult cw = wide_walk(1, [&](int) { return Uc; }, fill, T, 1.0f, false,
+                                                0.0f, VARIANT_LIBRARY, bm, tab, ms, (float)c);
+                cut_row = cw.token >= 0 ? cw.token : a.row_base + rows - 1;
+                __syncthreads();
+                for (int i = tid; i < ne; i += NT) P[i] = __fmul_rn(Xw[i], inv);
+                __syncthreads();
+            }
+            /* the kept rows' terms (the largest stays, so they are unchanged) */
+            for (int i = tid; i < ne; i += NT) {
+                const bool inA = P[i] > pT;
+                int r = 0;
+                if (inA)
+                    for (int j = 0; j < ne; ++j) r += P[j] > P[i] || (P[j] == P[i] && j < i);
+                const bool kept = inA ? r < keepA : (c > 0 && Xi[i] <= cut_row);
+                if (!kept) Xw[i] = 0.0f;
+            }
+            tie_end = c > 0 ? cut_row - a.row_base + 1 : 0;
+            __syncthreads();
+            dg.n_cand = keepA + c;
+        }
+        res = wide_walk(1, [&](int) { return U; }, fill, T, wT, false, a.u, a.variant, bm, tab,
+                        ms);
         token = res.token >= 0 ? res.token : a.vocab - 1;
         /* gpt2_server.c:2996-3001 walks every row: a draw of exactly 0 stops
          * at row 0 */

@@ -490,6 +490,22 @@ int orc_gpt2_lm_head(float *logits, const float *x, const int8_t *wte_q, const f
 int orc_gpt2_sample(float *logits, int vocab_size, float temperature, int top_k,
                     float rep_penalty, const int *recent, int n_recent, float u,
                     orc_sample_info *info) {
+    return orc_gpt2_sample_p(logits, vocab_size, temperature, top_k, 0.0f, rep_penalty, recent,
+                             n_recent, u, info);
+}
+
+/* The same with the server's nucleus branch (gpt2_server.c:2895-2960, on
+ * when 0 < top_p < 1): the rows l >= threshold (ascending index), their
+ * temperature softmax over the largest of them -- expf terms summed in that
+ * order, inv = 1 / (sum + 1e-12f), each term times inv -- an insertion sort
+ * descending by probability (stable: equal probabilities keep ascending
+ * index), and rows kept in that order until the running probability sum
+ * reaches top_p (the row that reaches it is kept).  No level-2 filter is
+ * linked (the weak lal_filter_topk keeps the mask, :2969-2979).  The softmax
+ * and draw then run over the kept rows (:2981-3002). */
+int orc_gpt2_sample_p(float *logits, int vocab_size, float temperature, int top_k, float top_p,
+                      float rep_penalty, const int *recent, int n_recent, float u,
+                      orc_sample_info *info) {
     orc_sample_info loc;
     if (!info) info = &loc;
     memset(info, 0, sizeof(*info));
@@ -514,22 +530,68 @@ int orc_gpt2_sample(float *logits, int vocab_size, float temperature, int top_k,
             threshold = max_val;
             copy[max_v] = -1e30f;
         }
+        unsigned char *keep = (unsigned char *)calloc((size_t)vocab_size, 1);
+        if (top_p > 0.0f && top_p < 1.0f) {
+            int *top_idx = (int *)malloc(sizeof(int) * (size_t)vocab_size);
+            float *top_val = (float *)malloc(sizeof(float) * (size_t)vocab_size);
+            int n_top = 0;
+            for (int v = 0; v < vocab_size; v++)
+                if (logits[v] >= threshold) {
+                    top_idx[n_top] = v;
+                    top_val[n_top] = logits[v];
+                    n_top++;
+                }
+            float top_max = -1e30f;
+            for (int i = 0; i < n_top; i++)
+                if (top_val[i] > top_max) top_max = top_val[i];
+            float top_sum = 0.0f;
+            for (int i = 0; i < n_top; i++) {
+                top_val[i] = expf((top_val[i] - top_max) / temperature);
+                top_sum += top_val[i];
+            }
+            const float inv = 1.0f / (top_sum + 1e-12f);
+            for (int i = 0; i < n_top; i++) top_val[i] *= inv;
+            for (int i = 1; i < n_top; i++) {
+                const float vp = top_val[i];
+                const int vi = top_idx[i];
+                int j = i - 1;
+                while (j >= 0 && top_val[j] < vp) {
+                    top_val[j + 1] = top_val[j];
+                    top_idx[j + 1] = top_idx[j];
+                    j--;
+                }
+                top_val[j + 1] = vp;
+                top_idx[j + 1] = vi;
+            }
+            float cum = 0.0f;
+            for (int i = 0; i < n_top; i++) {
+                keep[top_idx[i]] = 1;
+                cum += top_val[i];
+                if (cum >= top_p) break;
+            }
+            free(top_idx);
+            free(top_val);
+        } else {
+            for (int v = 0; v < vocab_size; v++)
+                if (logits[v] >= threshold) keep[v] = 1;
+        }
         float actual_max = -1e30f;
         int n_cand = 0;
         for (int v = 0; v < vocab_size; v++)
-            if (logits[v] >= threshold) {
+            if (keep[v]) {
                 n_cand++;
                 if (logits[v] > actual_max) actual_max = logits[v];
             }
         float sum_exp = 0.0f;
         for (int v = 0; v < vocab_size; v++) {
-            if (logits[v] >= threshold) {
+            if (keep[v]) {
                 copy[v] = expf((logits[v] - actual_max) / temperature);
                 sum_exp += copy[v];
             } else {
                 copy[v] = 0.0f;
             }
         }
+        free(keep);
         const float r = u * sum_exp;
         info->threshold = threshold;
         info->max_l = actual_max;

@@ -48,6 +48,11 @@ int   orc_gpt2_lm_head(float *logits, const float *x, const int8_t *wte_q,
 int   orc_gpt2_sample(float *logits, int vocab_size, float temperature, int top_k,
                       float rep_penalty, const int *recent, int n_recent, float u,
                       orc_sample_info *info);
+/* with the server's top-p branch (gpt2_server.c:2895-2960); top_p outside
+ * (0, 1) keeps every row of the top-k pool */
+int   orc_gpt2_sample_p(float *logits, int vocab_size, float temperature, int top_k,
+                        float top_p, float rep_penalty, const int *recent, int n_recent,
+                        float u, orc_sample_info *info);
 /* runtime/lal_q8_kernel.h:375-424 (AVX2+FMA build, the one the servers use). */
 float orc_quantize_x_int8(const float *x, int8_t *xq, int n);
 /* runtime/lal_q8_kernel.h:450-460 */

@@ -136,3 +136,58 @@ def test_gpt2_crowded_boundary_bin(kind):
     assert tok == ptok
     np.testing.assert_array_equal(bits(t.logits(0)), bits(port.logits))
     t.close()
+
+
+@pytest.mark.parametrize("top_p", [0.3, 0.9])
+def test_gpt2_top_p_loop_matches_oracle(top_p):
+    """The server's nucleus step after top-k (gpt2_server.c:2895-2960):
+    tokens, kept count, sums and history of a C1 loop against the
+    restatement of that branch."""
+    cfg = synth.CONFIGS["c1_gpt2"]
+    W = synth.lm_head_f32(cfg)
+    q, s = oracle.quantize_rows(W, "port")
+    hist0 = synth.history(cfg, 0)
+    t = gpt2_tail(q, s, cfg)
+    t.set_top_p(top_p)
+    t.set_sampling([cfg.temperature], [cfg.top_k], [cfg.rep_penalty])
+    t.set_history(0, hist0)
+    port = oracle.Gpt2PortLoop(q, s, hist0, cfg.hist, cfg.temperature, cfg.top_k,
+                               cfg.rep_penalty, top_p=top_p)
+    us = draws(12, 9)
+    kept = []
+    for step in range(12):
+        x = synth.hidden(cfg, step)
+        tok = int(t.step(x, us[step:step + 1])[0])
+        ptok, info = port.step(x[0], us[step])
+        assert tok == ptok, (top_p, step)
+        d = t.diag(0)
+        assert d["n_cand"] == info.n_cand and bits(d["sum"]) == bits(info.sum), (top_p, step)
+        kept.append(info.n_cand)
+    assert min(kept) < cfg.top_k  # the nucleus really cut the pool
+    np.testing.assert_array_equal(t.get_history(0), port.history())
+    t.close()
+
+
+def test_gpt2_top_p_over_an_all_tied_vocabulary():
+    """An all-zero hidden vector: every row's logit is 0.0 (the re-scored rows
+    too), so the top-k pool is the whole vocabulary at one probability and the
+    nucleus keeps its first rows by index -- the select's wide path."""
+    cfg = synth.CONFIGS["c1_gpt2"]
+    W = synth.lm_head_f32(cfg)
+    q, s = oracle.quantize_rows(W, "port")
+    t = gpt2_tail(q, s, cfg)
+    t.set_sampling([cfg.temperature], [cfg.top_k], [cfg.rep_penalty])
+    t.set_history(0, np.zeros(0, np.int32))
+    x = np.zeros((1, cfg.n_embd), np.float32)
+    for top_p in (0.0, 0.25, 0.75):
+        t.set_top_p(top_p)
+        port = oracle.Gpt2PortLoop(q, s, np.zeros(0, np.int32), cfg.hist, cfg.temperature,
+                                   cfg.top_k, cfg.rep_penalty, top_p=top_p)
+        for u in (0.1, 0.6, 0.999):
+            t.set_history(0, np.zeros(0, np.int32))
+            port.n.value = 0
+            tok = int(t.step(x, np.array([u], np.float32))[0])
+            ptok, info = port.step(x[0], np.float32(u))
+            assert tok == ptok, (top_p, u)
+            assert t.diag(0)["n_cand"] == info.n_cand, (top_p, u)
+    t.close()
