@@ -582,11 +582,11 @@ def run_ours(args, cfg):
         gpt2 = kind == "gpt2"
         batched = kind == "batched"
         if gpt2:
-            # the GPT-2 server's tail: quantize, LM head (the timed kernel),
-            # the 512-candidate select, the float re-score, the sampler
-            launches_per_step = 5 * B
+            # the GPT-2 server's tail: LM head with its quantizer (the timed
+            # kernel), the 512-candidate select, the float re-score + sampler
+            launches_per_step = 3 * B
             alg = algorithmic_bytes(cfg, 1, rows)
-            kname = ("LM-head kernel (tail_kernel<MODE_LMHEAD>), one of the GPT-2 tail's five "
+            kname = ("LM-head kernel (tail_kernel<MODE_LMHEAD>), one of the GPT-2 tail's three "
                      "launches a step")
         elif batched:
             # quantize + tensor-core GEMM + per-stream select: the GEMM streams

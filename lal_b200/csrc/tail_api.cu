@@ -866,11 +866,12 @@ struct lal_tail {
     unsigned rot = 0;
     /* LAL_SAMPLER_GPT2: the launch plans of the LM head and the sampler; the
      * quantized vector and its scale, the re-scored rows and their count */
-    TailParams g2_lm, g2_smp;
-    int g2_grid_lm = 0, g2_grid_smp = 0, g2_n = 0;
-    int8_t *g2_xq = nullptr;
-    float *g2_sx = nullptr;
+    TailParams g2_lm;
+    int g2_grid_lm = 0, g2_n = 0, g2_h_slots = 0;
+    float g2_top_p = 0.0f;
     int *g2_cand_i = nullptr, *g2_count = nullptr;
+    uint32_t *g2_bound = nullptr;
+    unsigned *g2_ticket = nullptr;
 };
 
 namespace {
@@ -900,7 +901,8 @@ void destroy_ctx(lal_tail *t) {
                     t->hist_ids, t->hist_n, t->hist_head, t->diag, t->phase_ts,
                     t->x_send, t->x_recv, t->xq_b, t->sx_b, t->gmax_b, t->x_peer, t->d_peer,
                     t->f_cand_v, t->f_prefix, t->f_u, t->f_cand_i, t->f_keep, t->f_tok,
-                    t->f_diag, t->d_norm_w, t->g2_xq, t->g2_sx, t->g2_cand_i, t->g2_count};
+                    t->f_diag, t->d_norm_w, t->g2_cand_i, t->g2_count,
+                    t->g2_bound, t->g2_ticket};
     for (void *b : bufs)
         if (b) cudaFree(b);
     t->sel.free_all();
@@ -935,24 +937,22 @@ int gpt2_alloc(lal_tail *t) {
     lm.trunc_cols = t->ld;
     lm.trunc_rows_end = 0;
     t->g2_grid_lm = plan_launch(lm, num_sms, 8);
-    TailParams &q = t->g2_smp;
-    base_params(q, t->ds);
-    q.mode = MODE_SAMPLE;
-    q.variant = VARIANT_GPT2;
-    q.rows = V;
-    q.row_base = 0;
-    q.vocab = V;
-    q.d = q.ld = 16;
-    q.B = 1;
-    q.max_k = std::min(c.max_top_k, V);
-    t->g2_grid_smp = plan_launch(q, num_sms, 64);
-    if (t->g2_grid_lm < 1 || t->g2_grid_smp < 1)
+    if (t->g2_grid_lm < 1)
         return fail(LAL_TAIL_ERR_UNSUPPORTED, "gpt2 tail: shape V=%d d=%d unsupported", V,
                     c.n_embd);
-    CU(cudaMalloc(&t->g2_xq, (size_t)t->ld));
-    CU(cudaMalloc(&t->g2_sx, sizeof(float)));
+    /* the sampler's history hash: a power of two >= twice the history */
+    int hs = 64;
+    while (hs < 2 * std::max(1, c.history_cap)) hs <<= 1;
+    t->g2_h_slots = hs;
+    if (gpt2_finish_smem(std::max(1, std::min(c.max_top_k, V)), hs) > (size_t)200 * 1024)
+        return fail(LAL_TAIL_ERR_UNSUPPORTED,
+                    "gpt2 tail: history_cap %d / max_top_k %d beyond the sampler's shared memory",
+                    c.history_cap, c.max_top_k);
     CU(cudaMalloc(&t->g2_cand_i, sizeof(int) * (size_t)kGpt2RerankN));
     CU(cudaMalloc(&t->g2_count, sizeof(int)));
+    CU(cudaMalloc(&t->g2_bound, sizeof(uint32_t)));
+    CU(cudaMalloc(&t->g2_ticket, sizeof(unsigned)));
+    CU(cudaMemset(t->g2_ticket, 0, sizeof(unsigned)));
     return LAL_TAIL_OK;
 }
 
@@ -964,12 +964,11 @@ int enqueue_gpt2(lal_tail *t, int b, const float *d_hidden, const float *d_u, in
     const float *x = d_hidden + (size_t)b * d;
     float *logits = t->logits + (size_t)b * t->nrows;
     int *status = t->io_out + t->cfg.max_streams;
-    CU(launch_gpt2_quantize(x, d, t->g2_xq, t->ld, t->g2_sx, st));
+    /* the LM head (its launch quantizes x: gpt2_server.c:1982-1998) */
     TailParams lm = t->g2_lm;
     lm.W = t->W;
     lm.scale_w = t->sw;
-    lm.xq_in = t->g2_xq;
-    lm.scale_x_dev = t->g2_sx;
+    lm.hidden = x;
     lm.logits = logits;
     lm.status = status;
     const bool time_it = t->timing && t->ev_used + 2 <= (int)t->ev.size();
@@ -979,29 +978,40 @@ int enqueue_gpt2(lal_tail *t, int b, const float *d_hidden, const float *d_u, in
         CU(cudaEventRecord(t->ev[t->ev_used + 1], st));
         t->ev_used += 2;
     }
-    /* the rows the server's heap keeps, then their float re-score */
-    CU(launch_gpt2_select(logits, V, t->g2_n, t->g2_cand_i, t->g2_count, status, st));
-    CU(launch_gpt2_rerank(x, d, t->W, t->ld, t->sw, logits, t->g2_cand_i, t->g2_count, t->g2_n,
-                          status, st));
-    /* the server's sampler on the re-scored logits */
-    TailParams r = t->g2_smp;
-    r.logits = logits;
-    r.temperature = t->temp + b;
-    r.top_k = t->topk + b;
-    r.rep_penalty = t->pen + b;
-    r.u = d_u + b;
-    r.hist_ids = t->hist_ids + (size_t)b * hc;
-    r.hist_n = t->hist_n + b;
-    r.hist_head = t->hist_head + b;
-    r.hist_cap = t->cfg.history_cap;
-    r.push_history = t->cfg.history_cap > 0 ? 1 : 0;
-    r.tokens = d_tokens + b;
-    r.diag = t->diag + b;
-    t->sel.fill(r);
-    r.status = status;
-    r.local_edges =
-        use_local_edges(effective_k(t->h_temp[b], t->h_topk[b], V, V), r.rows_per_cta_max);
-    CU(launch_tail(r, t->g2_grid_smp, st));
+    /* the rows the server's heap keeps, then their float re-score and the
+     * server's sampler (the re-score launch's last CTA) */
+    CU(launch_gpt2_select(logits, V, t->g2_n, t->g2_cand_i, t->g2_count, t->g2_bound, status,
+                          st));
+    Gpt2Finish f;
+    memset(&f, 0, sizeof(f));
+    f.logits = logits;
+    f.V = V;
+    f.cand = t->g2_cand_i;
+    f.n_ptr = t->g2_count;
+    f.bound = t->g2_bound;
+    f.temperature = t->temp + b;
+    f.rep_penalty = t->pen + b;
+    f.u = d_u + b;
+    f.top_k = t->topk + b;
+    f.top_p = t->g2_top_p;
+    f.hist_ids = t->hist_ids + (size_t)b * hc;
+    f.hist_n = t->hist_n + b;
+    f.hist_head = t->hist_head + b;
+    f.hist_cap = t->cfg.history_cap;
+    f.push_history = t->cfg.history_cap > 0 ? 1 : 0;
+    f.tokens = d_tokens + b;
+    f.diag = t->diag + b;
+    f.expf_x = t->ds->d_expf_x;
+    f.expf_y = t->ds->d_expf_y;
+    f.expf_bits = t->ds->d_expf_bits;
+    f.expf_off = t->ds->d_expf_off;
+    f.expf_hash = t->ds->d_expf_hash;
+    f.expf_hash_probe = t->ds->expf_hash_probe;
+    f.cap = std::max(1, std::min(t->cfg.max_top_k, V));
+    f.h_slots = t->g2_h_slots;
+    f.ticket = t->g2_ticket;
+    f.status = status;
+    CU(launch_gpt2_rerank(x, d, t->W, t->ld, t->sw, f, t->g2_n, st));
     return LAL_TAIL_OK;
 }
 
@@ -1955,7 +1965,7 @@ int lal_tail_set_top_p(lal_tail *t, float top_p) {
     if (top_p < 0.0f) top_p = 0.0f;
     if (top_p > 1.0f) top_p = 1.0f;
     CU(cudaStreamSynchronize(t->stream));
-    t->g2_smp.top_p = top_p;
+    t->g2_top_p = top_p;
     return LAL_TAIL_OK;
 }
 

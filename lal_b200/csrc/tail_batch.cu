@@ -139,6 +139,9 @@ __global__ void __launch_bounds__(NT) quantize_batch_kernel(const float *x, int 
                                                             const float *norm_w, float norm_eps) {
     __shared__ Misc ms;
     __shared__ float xs[kNormMaxD];
+    /* the GEMM may launch now: it streams the LM head and waits for this
+     * kernel's completion before it reads X */
+    grid_dep_launch_dependents();
     const int b = blockIdx.x;
     const float *row = x + (size_t)b * d;
     int8_t *out = xq + (size_t)b * ld;
@@ -228,7 +231,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_i8_kernel(const __grid_c
         *never = 0;
         mbar_fence_init();
     }
-    for (int i = threadIdx.x; i < p.N; i += kGemmThreads) sx[i] = i < p.B ? p.scale_x[i] : 0.0f;
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                          smem_u32(tholder)),
@@ -241,23 +243,48 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_i8_kernel(const __grid_c
     tc_fence_after();
     const uint32_t tbase = *tholder;
 
+    /* Programmatic dependent launch: the LM head is written by no step, so
+     * the first W boxes are requested while the previous kernel on the
+     * stream (the quantizer) still runs; X, the scales and every output wait
+     * for that kernel's completion.  Two boxes only: X's first boxes queue
+     * behind this burst when the launches do not overlap (measured: a full
+     * ring of W first cost 5 us a launch at B=64). */
+    const uint32_t bytes = (uint32_t)(kBM * kBK + p.N * kBK);
+    const uint64_t pol_w = policy_evict_first(), pol_x = policy_evict_last();
+    const int my_iters = ((n_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1) * p.kblocks;
+    const int pre = min(2, my_iters);
+    if (warp == 0 && lane == 0)
+        for (int it = 0; it < pre; ++it) {
+            const int tile = blockIdx.x + (it / p.kblocks) * (int)gridDim.x;
+            mbar_expect_tx(&full[it], bytes);
+            tma_load_2d(gsm + (size_t)it * p.stage_bytes, &p.tmW, (it % p.kblocks) * kBK,
+                        tile * kBM, &full[it], pol_w);
+        }
+    grid_dep_wait();
+    grid_dep_launch_dependents();
+    for (int i = threadIdx.x; i < p.N; i += kGemmThreads) sx[i] = i < p.B ? p.scale_x[i] : 0.0f;
+    __syncthreads();
+
     if (warp == 0) {
         if (lane == 0) {
-            /* producer: one W box and one X box per stage */
-            const uint64_t pol_w = policy_evict_first(), pol_x = policy_evict_last();
-            const uint32_t bytes = (uint32_t)(kBM * kBK + p.N * kBK);
+            /* producer: one W box and one X box per stage (the first `pre`
+             * stages' W boxes are on their way already) */
             int it = 0;
             bool ok = true;
             for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x)
                 for (int kb = 0; kb < p.kblocks; ++kb, ++it) {
                     const int s = it % p.stages;
                     const uint32_t use = (uint32_t)(it / p.stages);
-                    if (it >= p.stages && !bwait(&empty[s], (use & 1u) ^ 1u, abort_flag)) {
+                    uint8_t *st = gsm + (size_t)s * p.stage_bytes;
+                    if (it < pre) {
+                        tma_load_2d(st + kBM * kBK, &p.tmX, kb * kBK, 0, &full[s], pol_x);
+                        continue;
+                    }
+                    if (!bwait(&empty[s], (use & 1u) ^ 1u, abort_flag)) {
                         *abort_flag = 1;
                         ok = false;
                         break;
                     }
-                    uint8_t *st = gsm + (size_t)s * p.stage_bytes;
                     mbar_expect_tx(&full[s], bytes);
                     tma_load_2d(st, &p.tmW, kb * kBK, tile * kBM, &full[s], pol_w);
                     tma_load_2d(st + kBM * kBK, &p.tmX, kb * kBK, 0, &full[s], pol_x);
@@ -304,7 +331,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_i8_kernel(const __grid_c
             if (!bwait(drain, 0u, never)) *abort_flag = 1;
         }
     } else {
-        /* epilogue: warp w reads tensor-memory lanes 32*(w%4) .. +31 */
+        /* epilogue (warps 2-5): warp w reads tensor-memory lanes
+         * 32*(w%4) .. +31 */
         const int q = warp & 3;
         int tcount = 0;
         for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++tcount) {
@@ -455,24 +483,17 @@ __global__ void __launch_bounds__(NT, 1) batch_select_kernel(const __grid_consta
     const bool greedy = (temp <= 0.0f) || (topk <= 0);
     const bool use_pen = pen > 1.0f && hn > 0 && (p.variant == VARIANT_SERVER || !greedy);
 
-    /* this stream's group maxima, loaded now so that their latency overlaps
-     * the penalty (one batch when the slice has at most NT * kGroupRegs
-     * groups) */
     constexpr int kGroupRegs = 24;
     uint32_t gpre[kGroupRegs];
     const bool gpre_ok = p.gmax != nullptr && p.n_groups <= NT * kGroupRegs;
-    if (gpre_ok) {
-        const uint32_t *gm = p.gmax + (size_t)b * p.n_groups;
-#pragma unroll
-        for (int j = 0; j < kGroupRegs; ++j) {
-            const int g = j * NT + tid;
-            gpre[j] = g < p.n_groups ? __ldg(gm + g) : 0u;
-        }
-    }
 
     /* 1. repetition penalty: occurrences of each history id in this slice,
      * counted in an open-addressing hash, applied once per occurrence
-     * (runtime/lal_sampling.h:60-66; ids outside [0, V) are skipped) */
+     * (runtime/lal_sampling.h:60-66; ids outside [0, V) are skipped).
+     *
+     * Programmatic dependent launch: the history (the previous step's
+     * select, complete before this step's quantizer ran) is hashed while the
+     * GEMM finishes; the wait comes before the first read of its outputs. */
     for (int i = tid; i < 4096; i += NT) hist[i] = 0u;
     __shared__ int s_pen; /* distinct history ids inside this slice */
     /* which 32-row groups hold a penalised row (slices of up to
@@ -514,6 +535,20 @@ __global__ void __launch_bounds__(NT, 1) batch_select_kernel(const __grid_consta
             }
         }
         __syncthreads();
+    }
+    grid_dep_wait();
+    /* this stream's group maxima, loaded now so that their latency overlaps
+     * the penalty (one batch when the slice has at most NT * kGroupRegs
+     * groups) */
+    if (gpre_ok) {
+        const uint32_t *gm = p.gmax + (size_t)b * p.n_groups;
+#pragma unroll
+        for (int j = 0; j < kGroupRegs; ++j) {
+            const int g = j * NT + tid;
+            gpre[j] = g < p.n_groups ? __ldcg(gm + g) : 0u;
+        }
+    }
+    if (use_pen) {
         for (int i = tid; i < p.h_slots; i += NT) {
             const uint32_t id = hkey[i];
             if (id != kEmptySlot) {
@@ -588,7 +623,7 @@ __global__ void __launch_bounds__(NT, 1) batch_select_kernel(const __grid_consta
                 if (g < p.n_groups) Gk[g] = gpre[j];
             }
         } else {
-            for (int g = tid; g < p.n_groups; g += NT) Gk[g] = __ldg(gm + g);
+            for (int g = tid; g < p.n_groups; g += NT) Gk[g] = __ldcg(gm + g);
         }
         if (exact && use_pen) {
             /* the marked groups, listed in Gl (free until the candidate
@@ -1022,6 +1057,25 @@ EncodeTiledFn encoder() {
     return fn;
 }
 
+/* A launch that may begin while the previous kernel on the stream runs
+ * (programmatic stream serialization); the kernel calls griddepcontrol.wait
+ * before it reads anything that kernel writes. */
+cudaError_t launch_dependent(const void *fn, int grid, int block, size_t smem, cudaStream_t st,
+                             void **args) {
+    cudaLaunchConfig_t cfg;
+    memset(&cfg, 0, sizeof(cfg));
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(block);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelExC(&cfg, fn, args);
+}
+
 /* 2-D int8 tensor [dim1][dim0] (row pitch `pitch` bytes), box 128 x box1,
  * 128-byte swizzle; out-of-range rows and columns read as zero. */
 bool encode_i8(CUtensorMap *m, const void *base, int dim0, int dim1, int pitch, int box1) {
@@ -1134,9 +1188,11 @@ cudaError_t batch_launch(BatchPlan &bp, const BatchStep &s, cudaStream_t st) {
         e = cudaEventRecord(s.gemm_ev0, st);
         if (e != cudaSuccess) return e;
     }
-    gemm_i8_kernel<<<grid, kGemmThreads, gsmem, st>>>(g);
-    e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
+    {
+        void *args[] = {&g};
+        e = launch_dependent((const void *)gemm_i8_kernel, grid, kGemmThreads, gsmem, st, args);
+        if (e != cudaSuccess) return e;
+    }
     if (s.gemm_ev1) {
         e = cudaEventRecord(s.gemm_ev1, st);
         if (e != cudaSuccess) return e;
@@ -1181,8 +1237,8 @@ cudaError_t batch_launch(BatchPlan &bp, const BatchStep &s, cudaStream_t st) {
     const size_t ssmem = batch_select_smem(bp.s_cap, bp.c_cap, bp.h_slots, bp.n_groups);
     e = raise_smem((const void *)batch_select_kernel, kGemmSmemLimit - 8192);
     if (e != cudaSuccess) return e;
-    batch_select_kernel<<<s.B, NT, ssmem, st>>>(q);
-    return cudaGetLastError();
+    void *args[] = {&q};
+    return launch_dependent((const void *)batch_select_kernel, s.B, NT, ssmem, st, args);
 }
 
 }  // namespace lal

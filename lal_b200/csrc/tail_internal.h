@@ -80,6 +80,30 @@ struct StreamDiag {
     int n_cand, greedy, drew, token;
 };
 
+/* The GPT-2 tail's re-score launch: its last CTA runs the server's sampler
+ * (tail_gpt2.cu). */
+struct Gpt2Finish {
+    float *logits; /* [V]: int8 logits, the re-scored rows written by the launch */
+    int V;
+    const int *cand;        /* the rows the heap kept, any order */
+    const int *n_ptr;       /* their count */
+    const uint32_t *bound;  /* order key: every row left out has a logit <= it */
+    const float *temperature, *rep_penalty, *u;
+    const int *top_k;
+    float top_p;
+    int *hist_ids, *hist_n, *hist_head;
+    int hist_cap, push_history;
+    int *tokens;
+    StreamDiag *diag;
+    const uint32_t *expf_x, *expf_y, *expf_bits, *expf_off;
+    const uint4 *expf_hash;
+    int expf_hash_probe;
+    int cap;      /* explicit rows of the wide path: >= the largest k */
+    int h_slots;  /* history hash slots: a power of two >= 2 * hist_cap */
+    unsigned *ticket;
+    int *status;
+};
+
 /* Vocab-sharded step: the candidate record one shard exports per stream.
  * A 32-byte header, then cap values and cap global vocab indices in
  * ascending index order, then a bitmap of the shard's rows.  Every global
@@ -358,13 +382,12 @@ inline int batch_groups(int rows) { return (rows + 127) / 128 * 4; }
 cudaError_t batch_launch(BatchPlan &bp, const BatchStep &s, cudaStream_t st);
 int plan_launch(TailParams &p, int num_sms, int min_rows_per_cta);
 cudaError_t launch_tail(const TailParams &p, int grid, cudaStream_t st);
-cudaError_t launch_gpt2_quantize(const float *x, int d, int8_t *xq, int ld, float *scale_out,
-                                 cudaStream_t st);
 cudaError_t launch_gpt2_select(const float *logits, int V, int N, int *cand_out, int *n_out,
-                               const int *status, cudaStream_t st);
+                               uint32_t *bound_out, int *status, cudaStream_t st);
+/* the re-score of the kept rows, then the sampler in the launch's last CTA */
 cudaError_t launch_gpt2_rerank(const float *x, int d, const int8_t *W, int ld, const float *sw,
-                               float *logits, const int *cand, const int *n_dev, int N,
-                               const int *status, cudaStream_t st);
+                               const Gpt2Finish &f, int N, cudaStream_t st);
+size_t gpt2_finish_smem(int cap, int h_slots);
 cudaError_t launch_quantize_x(const float *x, int8_t *xq, float *scale, int n,
                               cudaStream_t st);
 /* One step's inputs from mapped pinned host memory into device memory: words

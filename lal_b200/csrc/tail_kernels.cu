@@ -204,57 +204,6 @@ struct PeerRecords {
     }
 };
 
-/* The GPT-2 server's nucleus (gpt2_server.c:2908-2955) over the m
- * candidates of a step: Oi their rows in ascending order, Ce their terms
- * expf((l - max_l) / T).  Every thread calls it.  The terms are summed in row
- * order, inv = 1 / (sum + 1e-12f), each probability is term * inv; the rows
- * are taken in the order of the server's insertion sort (descending
- * probability, equal probabilities by ascending row) until the running
- * probability reaches top_p, the row that reaches it included.  The largest
- * term stays (it is first in that order), so the kept rows' softmax over
- * their own maximum has the same terms: on return Ce holds them for kept rows
- * and 0 for the rest.  P, R, Q: scratch of m entries.  Returns the count
- * kept. */
-__device__ __noinline__ int gpt2_nucleus(float top_p, int m, float *Ce, float *P, int *R,
-                                         float *Q, Misc *ms) {
-    const int tid = threadIdx.x;
-    if (tid == 0) {
-        float acc = 0.0f;
-        for (int i = 0; i < m; ++i) acc = __fadd_rn(acc, Ce[i]);
-        ms->sum = acc;
-    }
-    __syncthreads();
-    const float inv = __fdiv_rn(1.0f, __fadd_rn(ms->sum, 1e-12f));
-    for (int i = tid; i < m; i += NT) P[i] = __fmul_rn(Ce[i], inv);
-    __syncthreads();
-    for (int i = tid; i < m; i += NT) {
-        const float pi = P[i];
-        int r = 0;
-        for (int j = 0; j < m; ++j) r += (P[j] > pi) || (P[j] == pi && j < i);
-        R[i] = r;
-        Q[r] = pi;
-    }
-    __syncthreads();
-    if (tid == 0) {
-        float cum = 0.0f;
-        int n = m;
-        for (int j = 0; j < m; ++j) {
-            cum = __fadd_rn(cum, Q[j]);
-            if (cum >= top_p) {
-                n = j + 1;
-                break;
-            }
-        }
-        ms->sh[0] = (uint32_t)n;
-    }
-    __syncthreads();
-    const int n_keep = (int)ms->sh[0];
-    for (int i = tid; i < m; i += NT)
-        if (R[i] >= n_keep) Ce[i] = 0.0f;
-    __syncthreads();
-    return n_keep;
-}
-
 /* The peer exchange's merge of this step (the fused kernel's last CTA, after
  * it published its record): wait for every rank's record, merge and draw
  * like merge_kernel. */
@@ -416,7 +365,11 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
         const float *h = p.hidden;
         float hv[kHReg];
         int ids[kHReg];
-        if (MODE == MODE_FUSED) {
+        /* the hidden vector is quantized here (per CTA) by the fused launch,
+         * and by an LM-head launch given the hidden vector (the GPT-2 tail:
+         * its server's truncating quantizer) */
+        const bool qin = MODE == MODE_FUSED || (MODE == MODE_LMHEAD && p.hidden != nullptr);
+        if (qin) {
 #pragma unroll
             for (int j = 0; j < kHReg; ++j) {
                 const int i = ctid + j * NC;
@@ -468,7 +421,7 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
             for (int i = ctid; i < 4096; i += NC) hist_s[i] = 0u;
         }
         float m = 0.0f;
-        if (MODE == MODE_FUSED) {
+        if (qin) {
 #pragma unroll
             for (int j = 0; j < kHReg; ++j) m = fmaxf(m, fabsf(hv[j]));
             for (int i = ctid + kHReg * NC; i < p.d; i += NC) m = fmaxf(m, fabsf(__ldg(h + i)));
@@ -487,14 +440,16 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
                 if (ctid + j * NC < hn) count(ids[j]);
             for (int i = ctid + kHReg * NC; i < hn; i += NC) count(__ldcg(p.hist_ids + i));
         }
-        if (MODE == MODE_FUSED) {
+        if (qin) {
             /* lal_quantize_x_int8 (runtime/lal_q8_kernel.h:375-424), redundantly
              * per CTA: absmax, scale = max/127 floored at 1e-8, inv = 1/scale,
-             * RNE for the first d&~7 elements and truncation for the tail. */
+             * RNE for the first d&~7 elements and truncation for the tail; the
+             * GPT-2 server's lm_head_quantize_x (gpt2_server.c:1982-1998)
+             * truncates every element. */
             float scale = __fdiv_rn(m, 127.0f);
             if (scale < 1e-8f) scale = 1e-8f;
             const float inv = __fdiv_rn(1.0f, scale);
-            const int n8 = p.d & ~7;
+            const int n8 = MODE == MODE_LMHEAD ? 0 : p.d & ~7;
             auto quant = [&](int i, float x) {
                 int v = 0;
                 if (i < p.d) {
@@ -2157,7 +2112,7 @@ cudaError_t launch_tail(const TailParams &p, int grid, cudaStream_t st) {
     cudaError_t e = raise_smem(fn, kSmemLimit);
     if (e != cudaSuccess) return e;
     void *args[] = {const_cast<TailParams *>(&p)};
-    if (p.mode == MODE_FUSED && p.local_edges) {
+    if ((p.mode == MODE_FUSED && p.local_edges) || (p.mode == MODE_LMHEAD && p.hidden)) {
         /* programmatic dependent launch: the kernel streams W while the
          * previous kernel on the stream finishes, and waits for it before
          * any other read */

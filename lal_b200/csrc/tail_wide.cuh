@@ -362,6 +362,57 @@ struct WideDense {
     float top_p;
 };
 
+/* The GPT-2 server's nucleus (gpt2_server.c:2908-2955) over the m
+ * candidates of a step: Oi their rows in ascending order, Ce their terms
+ * expf((l - max_l) / T).  Every thread calls it.  The terms are summed in row
+ * order, inv = 1 / (sum + 1e-12f), each probability is term * inv; the rows
+ * are taken in the order of the server's insertion sort (descending
+ * probability, equal probabilities by ascending row) until the running
+ * probability reaches top_p, the row that reaches it included.  The largest
+ * term stays (it is first in that order), so the kept rows' softmax over
+ * their own maximum has the same terms: on return Ce holds them for kept rows
+ * and 0 for the rest.  P, R, Q: scratch of m entries.  Returns the count
+ * kept. */
+__device__ __noinline__ int gpt2_nucleus(float top_p, int m, float *Ce, float *P, int *R,
+                                         float *Q, Misc *ms) {
+    const int tid = threadIdx.x;
+    if (tid == 0) {
+        float acc = 0.0f;
+        for (int i = 0; i < m; ++i) acc = __fadd_rn(acc, Ce[i]);
+        ms->sum = acc;
+    }
+    __syncthreads();
+    const float inv = __fdiv_rn(1.0f, __fadd_rn(ms->sum, 1e-12f));
+    for (int i = tid; i < m; i += NT) P[i] = __fmul_rn(Ce[i], inv);
+    __syncthreads();
+    for (int i = tid; i < m; i += NT) {
+        const float pi = P[i];
+        int r = 0;
+        for (int j = 0; j < m; ++j) r += (P[j] > pi) || (P[j] == pi && j < i);
+        R[i] = r;
+        Q[r] = pi;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        float cum = 0.0f;
+        int n = m;
+        for (int j = 0; j < m; ++j) {
+            cum = __fadd_rn(cum, Q[j]);
+            if (cum >= top_p) {
+                n = j + 1;
+                break;
+            }
+        }
+        ms->sh[0] = (uint32_t)n;
+    }
+    __syncthreads();
+    const int n_keep = (int)ms->sh[0];
+    for (int i = tid; i < m; i += NT)
+        if (R[i] >= n_keep) Ce[i] = 0.0f;
+    __syncthreads();
+    return n_keep;
+}
+
 /* bitmap word w of a slice: bit j set when row 32w + j equals T (warp-wide) */
 __device__ __forceinline__ uint32_t tie_word(const float *lg, int rows, int w, uint32_t T) {
     const int row = 32 * w + (int)(threadIdx.x & 31);
