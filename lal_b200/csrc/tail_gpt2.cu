@@ -114,9 +114,9 @@ __global__ void __launch_bounds__(kGpt2SelThreads, 1)
     /* The N-th largest of a multiset of keys that the threads hold (each
      * thread's each(f) calls f(key) for its keys; 1 <= krem <= the count): an
      * MSB-first radix select, 8-bit digits counted in aux. */
-    auto kth_largest = [&](auto each, uint32_t krem) {
+    auto kth_largest = [&](auto each, uint32_t krem, int top_shift) {
         uint32_t prefix = 0u, mask = 0u;
-        for (int shift = 24; shift >= 0; shift -= 8) {
+        for (int shift = top_shift; shift >= 0; shift -= 8) {
             if (tid < 256) aux[tid] = 0u;
             __syncthreads();
             each([&](uint32_t key) {
@@ -213,10 +213,26 @@ __global__ void __launch_bounds__(kGpt2SelThreads, 1)
         }
     }
     __syncthreads();
-    /* L, the N-th largest of the group maxima (empty groups count 0): N
-     * distinct rows reach L, so T >= L and every row at or above T has a key
-     * >= L -- few rows, gathered in one pass */
-    const uint32_t L = kth_largest([&](auto f) { f(gmx); }, (uint32_t)N);
+    /* L, the lower edge of the 12-bit bin holding the N-th largest group
+     * maximum (empty groups count 0): N distinct rows reach L, so T >= L and
+     * every row at or above T has a key >= L -- few rows, gathered in one
+     * pass.  One histogram pass (in the gather area, free until then). */
+    for (int i = tid; i < 4096; i += kGpt2SelThreads) gat[i] = 0u;
+    if (tid == 0) sh[3] = 0u;
+    __syncthreads();
+    atomicAdd(&gat[gmx >> 20], 1u);
+    {
+        const uint32_t wm = __reduce_max_sync(0xffffffffu, gmx);
+        if (lane == 0) atomicMax(&sh[3], wm);
+    }
+    __syncthreads();
+    if (tid < 32) {
+        const uint32_t b = warp_boundary_bin_4096(gat, sh[3] >> 20, (uint32_t)N);
+        if (lane == 0) sh[2] = b;
+    }
+    __syncthreads();
+    const uint32_t L = sh[2] << 20, top_key = sh[3];
+    __syncthreads();
     /* the keys >= L: counted per thread, placed by a block scan (thread
      * order, then row order within a thread) */
     uint32_t *ck = gat;
@@ -257,11 +273,16 @@ __global__ void __launch_bounds__(kGpt2SelThreads, 1)
     const int na = cnt;
     uint32_t T;
     if (na <= kGpt2SelCap) {
+        /* every gathered key lies in [L, top_key]: the digits above the
+         * first byte where the two differ are known */
+        const uint32_t diff = L ^ top_key;
+        const int top_shift = diff == 0u ? 0 : (31 - __clz(diff)) / 8 * 8;
         T = kth_largest(
             [&](auto f) {
                 for (int e = tid; e < na; e += kGpt2SelThreads) f(ck[e]);
             },
-            (uint32_t)N);
+            (uint32_t)N, top_shift);
+        T |= L & (top_shift >= 24 ? 0u : 0xFFFFFFFFu << (top_shift + 8));
         if (list_if_n([&](int e) { return ck[e]; }, [&](int e) { return ci[e]; }, na, T)) return;
     } else {
         /* a crowded boundary: the radix select over all keys */
@@ -269,7 +290,7 @@ __global__ void __launch_bounds__(kGpt2SelThreads, 1)
             [&](auto f) {
                 for (int i = tid; i < V; i += kGpt2SelThreads) f(keys[i]);
             },
-            (uint32_t)N);
+            (uint32_t)N, 24);
         if (list_if_n([&](int i) { return keys[i]; }, [&](int i) { return i; }, V, T)) return;
     }
     __syncthreads(); /* the refinement bins are read before the heap reuses them */
