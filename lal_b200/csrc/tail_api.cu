@@ -871,6 +871,7 @@ struct lal_tail {
     float g2_top_p = 0.0f;
     int *g2_cand_i = nullptr, *g2_count = nullptr;
     uint32_t *g2_bound = nullptr;
+    float *g2_kept_v = nullptr;
     unsigned *g2_ticket = nullptr;
 };
 
@@ -902,7 +903,7 @@ void destroy_ctx(lal_tail *t) {
                     t->x_send, t->x_recv, t->xq_b, t->sx_b, t->gmax_b, t->x_peer, t->d_peer,
                     t->f_cand_v, t->f_prefix, t->f_u, t->f_cand_i, t->f_keep, t->f_tok,
                     t->f_diag, t->d_norm_w, t->g2_cand_i, t->g2_count,
-                    t->g2_bound, t->g2_ticket};
+                    t->g2_bound, t->g2_ticket, t->g2_kept_v};
     for (void *b : bufs)
         if (b) cudaFree(b);
     t->sel.free_all();
@@ -951,6 +952,7 @@ int gpt2_alloc(lal_tail *t) {
     CU(cudaMalloc(&t->g2_cand_i, sizeof(int) * (size_t)kGpt2RerankN));
     CU(cudaMalloc(&t->g2_count, sizeof(int)));
     CU(cudaMalloc(&t->g2_bound, sizeof(uint32_t)));
+    CU(cudaMalloc(&t->g2_kept_v, sizeof(float) * (size_t)kGpt2RerankN));
     CU(cudaMalloc(&t->g2_ticket, sizeof(unsigned)));
     CU(cudaMemset(t->g2_ticket, 0, sizeof(unsigned)));
     return LAL_TAIL_OK;
@@ -987,6 +989,7 @@ int enqueue_gpt2(lal_tail *t, int b, const float *d_hidden, const float *d_u, in
     f.logits = logits;
     f.V = V;
     f.cand = t->g2_cand_i;
+    f.kept_val = t->g2_kept_v;
     f.n_ptr = t->g2_count;
     f.bound = t->g2_bound;
     f.temperature = t->temp + b;

@@ -345,12 +345,14 @@ __global__ void __launch_bounds__(kGpt2SelThreads, 1)
 /* k-th largest (with multiplicity) of the keys the block's threads hold --
  * each thread's each(f) calls f(key) for its keys; 1 <= krem <= their count
  * -- by an MSB-first radix select of 8-bit digits with plain shared-memory
- * counters (a few hundred keys: little contention). */
+ * counters (a few hundred keys: little contention), from the digit at
+ * top_shift down: the caller passes keys whose bits above it are all equal,
+ * and the result holds only the bits from top_shift + 7 down. */
 template <class Each>
-__device__ uint32_t kth_largest_small(Each each, uint32_t krem, Misc *ms) {
+__device__ uint32_t kth_largest_small(Each each, uint32_t krem, int top_shift, Misc *ms) {
     const int tid = threadIdx.x, lane = tid & 31;
     uint32_t prefix = 0u, mask = 0u;
-    for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int shift = top_shift; shift >= 0; shift -= 8) {
         for (int i = tid; i < 256; i += NT) ms->hist[i] = 0u;
         __syncthreads();
         each([&](uint32_t key) {
@@ -441,8 +443,15 @@ __device__ __noinline__ void gpt2_finish(const Gpt2Finish &f, uint8_t *smem, Mis
     int *Rk = reinterpret_cast<int *>(P + kGpt2RerankN);
     float *Q = reinterpret_cast<float *>(Rk + kGpt2RerankN);
 
-    /* 1. the kept rows and their re-scored logits; the history ids' loads
-     * go out with them */
+    /* 1. the kept rows and their re-scored logits (written in list order by
+     * the re-score), the history ids and the history rows' logits: every
+     * load goes out before any is used */
+    const uint32_t mask = (uint32_t)f.h_slots - 1u;
+    if (use_pen)
+        for (int i = tid; i < f.h_slots; i += NT) {
+            hkey[i] = kHashEmpty;
+            hcnt[i] = 0u;
+        }
     constexpr int kHReg = 4;
     int hid[kHReg];
 #pragma unroll
@@ -450,48 +459,62 @@ __device__ __noinline__ void gpt2_finish(const Gpt2Finish &f, uint8_t *smem, Mis
         const int i = tid + q * NT;
         hid[q] = use_pen && i < hn ? __ldcg(f.hist_ids + i) : -1;
     }
-    int rrow[kFinishPer];
-#pragma unroll
-    for (int q = 0; q < kFinishPer; ++q) {
-        const int j = tid + q * NT;
-        rrow[q] = j < n ? __ldcg(f.cand + j) : 0;
-    }
 #pragma unroll
     for (int q = 0; q < kFinishPer; ++q) {
         const int j = tid + q * NT;
         if (j < n) {
-            Ri[j] = rrow[q];
-            Rv[j] = __ldcg(f.logits + rrow[q]);
+            Ri[j] = __ldcg(f.cand + j);
+            Rv[j] = __ldcg(f.kept_val + j);
         }
     }
+    float hl[kHReg];
+#pragma unroll
+    for (int q = 0; q < kHReg; ++q)
+        hl[q] = hid[q] >= 0 && hid[q] < V ? __ldcg(f.logits + hid[q]) : 0.0f;
     /* 2. the penalty (gpt2_server.c:2868-2876): each history id in [0, V)
-     * once per occurrence, on the vocabulary's logits and on the kept copies */
+     * once per occurrence, on the vocabulary's logits and on the kept copies;
+     * the thread that inserts an id first writes its row back */
     if (use_pen) {
-        const uint32_t mask = (uint32_t)f.h_slots - 1u;
-        for (int i = tid; i < f.h_slots; i += NT) {
-            hkey[i] = kHashEmpty;
-            hcnt[i] = 0u;
-        }
         __syncthreads();
         auto insert = [&](int id) {
-            if (id < 0 || id >= V) return;
+            if (id < 0 || id >= V) return false;
             uint32_t slot = ((uint32_t)id * 2654435761u) & mask;
             for (int probe = 0; probe < f.h_slots; ++probe) {
                 const uint32_t prev = atomicCAS(&hkey[slot], kHashEmpty, (uint32_t)id);
                 if (prev == kHashEmpty || prev == (uint32_t)id) {
                     atomicAdd(&hcnt[slot], 1u);
-                    return;
+                    return prev == kHashEmpty;
                 }
                 slot = (slot + 1u) & mask;
             }
+            return false;
         };
+        auto count_of = [&](uint32_t id) {
+            uint32_t slot = (id * 2654435761u) & mask;
+            for (int probe = 0; probe < f.h_slots; ++probe) {
+                const uint32_t kk = hkey[slot];
+                if (kk == id) return hcnt[slot];
+                if (kk == kHashEmpty) break;
+                slot = (slot + 1u) & mask;
+            }
+            return 0u;
+        };
+        bool owner[kHReg];
 #pragma unroll
-        for (int q = 0; q < kHReg; ++q) insert(hid[q]);
+        for (int q = 0; q < kHReg; ++q) owner[q] = insert(hid[q]);
         for (int i = tid + kHReg * NT; i < hn; i += NT) insert(__ldcg(f.hist_ids + i));
         __syncthreads();
-        for (int i = tid; i < f.h_slots; i += NT) {
-            const uint32_t id = hkey[i];
-            if (id != kHashEmpty) f.logits[id] = penalise(__ldcg(f.logits + id), hcnt[i], pen);
+        if (hn <= kHReg * NT) {
+#pragma unroll
+            for (int q = 0; q < kHReg; ++q)
+                if (owner[q]) f.logits[hid[q]] = penalise(hl[q], count_of((uint32_t)hid[q]), pen);
+        } else {
+            /* a history past the registers' reach: every distinct id's row
+             * with a load of its own */
+            for (int i = tid; i < f.h_slots; i += NT) {
+                const uint32_t id = hkey[i];
+                if (id != kHashEmpty) f.logits[id] = penalise(__ldcg(f.logits + id), hcnt[i], pen);
+            }
         }
         for (int j = tid; j < n; j += NT) {
             const uint32_t id = (uint32_t)Ri[j];
@@ -587,13 +610,22 @@ __device__ __noinline__ void gpt2_finish(const Gpt2Finish &f, uint8_t *smem, Mis
         }
         /* 4. T, the k-th largest of the kept rows' logits with multiplicity
          * (the server's k passes of find-max-and-mask) */
-        const uint32_t T = kth_largest_small(
+        /* Unless every row was kept, T > B: only the keys above B take part
+         * (at least k of them), and their digits above the first byte where
+         * B + 1 and the largest key differ are known. */
+        const uint32_t lo = all_rows ? 0u : B + 1u;
+        const uint32_t diff = lo ^ top;
+        const int top_shift = diff == 0u ? 0 : (31 - __clz(diff)) / 8 * 8;
+        uint32_t T = kth_largest_small(
             [&](auto add) {
 #pragma unroll
-                for (int q = 0; q < kFinishPer; ++q)
-                    if (tid + q * NT < n) add(f2key(rv[q]));
+                for (int q = 0; q < kFinishPer; ++q) {
+                    const uint32_t key = f2key(rv[q]);
+                    if (tid + q * NT < n && key >= lo) add(key);
+                }
             },
-            (uint32_t)k, ms);
+            (uint32_t)k, top_shift, ms);
+        T |= top & (top_shift >= 24 ? 0u : 0xFFFFFFFFu << (top_shift + 8));
         /* the candidates {l >= T} with their weights: listed (Rk, Q, P),
          * then placed in ascending row order by their rank among themselves */
         int *Ci = Rk;
@@ -731,7 +763,10 @@ __global__ void __launch_bounds__(NT)
                 const float t = __shfl_sync(0xffffffffu, acc, base + j);
                 s = j == 0 ? t : __fadd_rn(s, t);
             }
-            if (on && lane8 == 0) f.logits[v] = s;
+            if (on && lane8 == 0) {
+                f.logits[v] = s;
+                f.kept_val[j0 + r] = s; /* list order, for the sampler */
+            }
         }
     }
     /* the barrier orders this CTA's logit writes before thread 0's

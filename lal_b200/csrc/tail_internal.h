@@ -86,6 +86,7 @@ struct Gpt2Finish {
     float *logits; /* [V]: int8 logits, the re-scored rows written by the launch */
     int V;
     const int *cand;        /* the rows the heap kept, any order */
+    float *kept_val;        /* their re-scored logits, in the same order */
     const int *n_ptr;       /* their count */
     const uint32_t *bound;  /* order key: every row left out has a logit <= it */
     const float *temperature, *rep_penalty, *u;
