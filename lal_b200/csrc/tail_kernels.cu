@@ -416,9 +416,22 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
 #pragma unroll
             for (int j = 0; j < kHReg; ++j) hv[j] = rmsnorm_apply(hv[j], inv_rms, wv[j]);
         }
+        /* The fused launch stages x in the key histogram's words (zeroed
+         * after the quantizer), so that the quantizer takes four consecutive
+         * elements a thread and writes them as one word. */
+        const bool stage_x = MODE == MODE_FUSED && p.d <= 4096 && (p.ld & 3) == 0;
+        float *xs_q = reinterpret_cast<float *>(hist_s);
+        if (stage_x) {
+#pragma unroll
+            for (int j = 0; j < kHReg; ++j) {
+                const int i = ctid + j * NC;
+                if (i < p.d) xs_q[i] = hv[j];
+            }
+        }
         if (MODE != MODE_LMHEAD) {
             for (int i = ctid; i < nloc; i += NC) cnt_s[i] = 0u;
-            for (int i = ctid; i < 4096; i += NC) hist_s[i] = 0u;
+            if (!stage_x)
+                for (int i = ctid; i < 4096; i += NC) hist_s[i] = 0u;
         }
         float m = 0.0f;
         if (qin) {
@@ -462,13 +475,28 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
                 }
                 return (int8_t)v;
             };
+            if (stage_x) {
+                uint32_t *xq32 = reinterpret_cast<uint32_t *>(xq_s);
+                const float4 *xs4 = reinterpret_cast<const float4 *>(xs_q);
+                for (int e = ctid; e < p.ld / 4; e += NC) {
+                    const int i = 4 * e;
+                    const float4 v = xs4[e]; /* elements >= d quantize to 0 */
+                    xq32[e] = (uint32_t)(uint8_t)quant(i, v.x) |
+                              (uint32_t)(uint8_t)quant(i + 1, v.y) << 8 |
+                              (uint32_t)(uint8_t)quant(i + 2, v.z) << 16 |
+                              (uint32_t)(uint8_t)quant(i + 3, v.w) << 24;
+                }
+                consumer_sync(); /* x is read before its words are zeroed */
+                for (int i = ctid; i < 4096; i += NC) hist_s[i] = 0u;
+            } else {
 #pragma unroll
-            for (int j = 0; j < kHReg; ++j) {
-                const int i = ctid + j * NC;
-                if (i < p.ld) xq_s[i] = quant(i, hv[j]);
+                for (int j = 0; j < kHReg; ++j) {
+                    const int i = ctid + j * NC;
+                    if (i < p.ld) xq_s[i] = quant(i, hv[j]);
+                }
+                for (int i = ctid + kHReg * NC; i < p.ld; i += NC)
+                    xq_s[i] = quant(i, i < p.d ? __ldg(h + i) : 0.0f);
             }
-            for (int i = ctid + kHReg * NC; i < p.ld; i += NC)
-                xq_s[i] = quant(i, i < p.d ? __ldg(h + i) : 0.0f);
             if (ctid == 0) ms->sx = scale;
         } else if (MODE == MODE_LMHEAD) {
             for (int i = ctid; i < p.ld; i += NC) xq_s[i] = i < p.d ? p.xq_in[i] : (int8_t)0;
