@@ -56,7 +56,8 @@ extern "C" {
 #define LAL_SAMPLER_SERVER  1
 /* GPT2 = the GPT-2 server's int8 LM head and sampler, a second drop-in for
  * lm_head_int8_parallel (tools/server/gpt2_server.c:2125-2214) and its
- * sampling block (gpt2_server.c:2862-3013, top-p off, no filter hook):
+ * sampling block (gpt2_server.c:2862-3013; top-p with lal_tail_set_top_p,
+ * the level-2 filter call with lal_tail_set_filter):
  * truncating quantizer, int8 logits of every row, the 512 rows the server's
  * min-heap keeps re-scored in float, then LIBRARY's arithmetic on the
  * re-scored logits, except that a draw of exactly 0 returns row 0.  u[b] is
@@ -272,8 +273,13 @@ int lal_tail_shard_merge(lal_tail *t, int n_streams, const float *d_u, int *d_to
  * calls filter (restoring the mask if it comes back empty), the GPU finishes
  * the kept softmax, and draw(draw_ctx) is called only when the kept mass is
  * positive (with no draw callback, the step's u[b] is used there).  Greedy
- * streams take the normal path.  Needs LAL_SAMPLER_SERVER and one shard;
- * lal_tail_step_device is not filtered.  All NULL switches it off. */
+ * streams take the normal path.  Needs LAL_SAMPLER_SERVER or LAL_SAMPLER_GPT2
+ * and one shard; lal_tail_step_device is not filtered.  All NULL switches it
+ * off.  With LAL_SAMPLER_GPT2 it is the GPT-2 server's call
+ * (tools/server/gpt2_server.c:2962-2978): the mask holds the top-k pool
+ * narrowed by top-p, an empty mask gets the whole top-k pool back, the
+ * softmax runs over every row the mask keeps (rows the filter adds too), and
+ * the draw is taken every non-greedy step. */
 int lal_tail_set_filter(lal_tail *t, lal_filter_topk_fn filter, lal_token_decode_fn decode,
                         lal_draw_fn draw, void *draw_ctx);
 /* The model's final RMSNorm fused as the tail's prologue: replaces

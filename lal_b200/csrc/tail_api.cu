@@ -959,7 +959,8 @@ int gpt2_alloc(lal_tail *t) {
 }
 
 /* One stream of a LAL_SAMPLER_GPT2 step (tail_gpt2.cu has the sequence). */
-int enqueue_gpt2(lal_tail *t, int b, const float *d_hidden, const float *d_u, int *d_tokens) {
+int enqueue_gpt2(lal_tail *t, int b, const float *d_hidden, const float *d_u, int *d_tokens,
+                 bool candidates_only = false) {
     const int d = t->cfg.n_embd, V = t->cfg.vocab_size;
     const int hc = std::max(1, t->cfg.history_cap);
     cudaStream_t st = t->stream;
@@ -1014,6 +1015,14 @@ int enqueue_gpt2(lal_tail *t, int b, const float *d_hidden, const float *d_u, in
     f.h_slots = t->g2_h_slots;
     f.ticket = t->g2_ticket;
     f.status = status;
+    if (candidates_only) {
+        f.candidates_only = 1;
+        f.pool_val = t->f_cand_v;
+        f.pool_idx = t->f_cand_i;
+        f.pool_keep = t->f_keep;
+        f.pool_cap = t->nrows;
+        f.push_history = 0;
+    }
     CU(launch_gpt2_rerank(x, d, t->W, t->ld, t->sw, f, t->g2_n, st));
     return LAL_TAIL_OK;
 }
@@ -1389,6 +1398,102 @@ int filtered_stream_step(lal_tail *t, int b, const float *d_hidden, float u_fall
     return LAL_TAIL_OK;
 }
 
+/* One stream's GPT-2 step with the level-2 filter hook (gpt2_server.c:
+ * 2962-2978): the device exports the top-k pool with the nucleus's marks, the
+ * host builds the keep mask over the vocabulary, calls the filter and restores
+ * the pool when the mask comes back empty; the device then runs the softmax
+ * and the draw over every row the mask keeps, in ascending order (rows the
+ * filter added included, at their penalised logits).  Non-greedy only. */
+int gpt2_filtered_step(lal_tail *t, int b, const float *d_hidden, const float *d_u,
+                       float u_fallback, int *token_out) {
+    const int hc = std::max(1, t->cfg.history_cap);
+    const int V = t->cfg.vocab_size;
+    int *status_p = t->io_out + t->cfg.max_streams;
+    CHECK(enqueue_gpt2(t, b, d_hidden, d_u, t->f_tok, true));
+    /* 1. the pool size, the status and the history ring */
+    StreamDiag dg;
+    int status = 0, n = 0, head = 0;
+    CU(cudaMemcpyAsync(&dg, t->diag + b, sizeof(dg), cudaMemcpyDeviceToHost, t->stream));
+    CU(cudaMemcpyAsync(&status, status_p, 4, cudaMemcpyDeviceToHost, t->stream));
+    CU(cudaMemcpyAsync(&n, t->hist_n + b, 4, cudaMemcpyDeviceToHost, t->stream));
+    CU(cudaMemcpyAsync(&head, t->hist_head + b, 4, cudaMemcpyDeviceToHost, t->stream));
+    CU(cudaStreamSynchronize(t->stream));
+    if (status != 0) {
+        CU(cudaMemset(status_p, 0, 4));
+        CU(cudaStreamSynchronize(t->stream));
+        return fail(status, "device status %d in the filtered GPT-2 step", status);
+    }
+    const int m = dg.n_cand;
+    if (m < 1 || m > t->nrows) return fail(LAL_TAIL_ERR_CAPACITY, "filtered step: %d candidates", m);
+    std::vector<int> pool_keep((size_t)m);
+    CU(cudaMemcpyAsync(t->f_ids.data(), t->f_cand_i, 4ull * m, cudaMemcpyDeviceToHost, t->stream));
+    CU(cudaMemcpyAsync(pool_keep.data(), t->f_keep, 4ull * m, cudaMemcpyDeviceToHost, t->stream));
+    CU(cudaMemcpyAsync(t->f_ring.data(), t->hist_ids + (size_t)b * hc, 4ull * hc,
+                       cudaMemcpyDeviceToHost, t->stream));
+    CU(cudaStreamSynchronize(t->stream));
+    std::vector<int> recent((size_t)n);
+    for (int i = 0; i < n; ++i)
+        recent[i] = t->f_ring[(size_t)((n < hc ? 0 : head) + i) % (size_t)hc];
+    /* 2. keep mask (top-k, narrowed by top-p), the filter, the restore of
+     * the top-k pool when it keeps nothing */
+    std::fill(t->f_mask.begin(), t->f_mask.end(), 0);
+    for (int i = 0; i < m; ++i) t->f_mask[t->f_ids[i]] = pool_keep[i];
+    if (t->filter) {
+        const int last = n > 0 ? recent[n - 1] : -1;
+        (void)t->filter(t->f_mask.data(), V, last, recent.data(), n, t->decode);
+    }
+    bool any = false;
+    for (int v = 0; v < V && !any; ++v) any = t->f_mask[v] != 0;
+    if (!any)
+        for (int i = 0; i < m; ++i) t->f_mask[t->f_ids[i]] = 1;
+    std::vector<int> &rows = t->f_keep_h;
+    rows.clear();
+    for (int v = 0; v < V; ++v)
+        if (t->f_mask[v]) rows.push_back(v);
+    const int mk = (int)rows.size();
+    /* 3. softmax over the kept rows and the draw, on the device */
+    CU(cudaMemcpyAsync(t->f_cand_i, rows.data(), 4ull * mk, cudaMemcpyHostToDevice, t->stream));
+    FinishParams f;
+    memset(&f, 0, sizeof(f));
+    f.cand_val = nullptr;
+    f.logits = t->logits + (size_t)b * t->nrows;
+    f.cand_idx = t->f_cand_i;
+    f.keep = nullptr;
+    f.variant = VARIANT_GPT2;
+    f.m = mk;
+    f.temperature = t->h_temp[b];
+    f.vocab = V;
+    f.u = t->f_u;
+    f.prefix = t->f_prefix;
+    f.diag = t->f_diag;
+    f.token = t->f_tok;
+    f.expf_x = t->ds->d_expf_x;
+    f.expf_y = t->ds->d_expf_y;
+    f.expf_n = t->ds->expf_n;
+    f.expf_bits = t->ds->d_expf_bits;
+    f.expf_off = t->ds->d_expf_off;
+    f.phase = 0;
+    CU(launch_finish(f, t->stream));
+    /* gpt2_server.c:2996: one draw every step, after the filter */
+    const float u = t->draw ? t->draw(t->draw_ctx) : u_fallback;
+    CU(cudaMemcpyAsync(t->f_u, &u, 4, cudaMemcpyHostToDevice, t->stream));
+    f.phase = 1;
+    CU(launch_finish(f, t->stream));
+    int tok = -1;
+    CU(cudaMemcpyAsync(&tok, t->f_tok, 4, cudaMemcpyDeviceToHost, t->stream));
+    CU(cudaStreamSynchronize(t->stream));
+    /* 4. the history push (FIFO at history_cap) */
+    if (t->cfg.history_cap > 0) {
+        const int pos = n < hc ? n : head;
+        const int n2 = n < hc ? n + 1 : n, head2 = n < hc ? head : (head + 1) % hc;
+        CU(cudaMemcpy(t->hist_ids + (size_t)b * hc + pos, &tok, 4, cudaMemcpyHostToDevice));
+        CU(cudaMemcpy(t->hist_n + b, &n2, 4, cudaMemcpyHostToDevice));
+        CU(cudaMemcpy(t->hist_head + b, &head2, 4, cudaMemcpyHostToDevice));
+    }
+    *token_out = tok;
+    return LAL_TAIL_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -1692,7 +1797,23 @@ int lal_tail_step(lal_tail *t, const float *hidden, int n_streams, const float *
         if (t->n_set < n_streams)
             return fail(LAL_TAIL_ERR_STATE, "sampling parameters not set for %d streams", n_streams);
         CHECK(lal_tail_stage_inputs(t, hidden, n_streams, u));
+        const int Bmax = t->cfg.max_streams;
         for (int b = 0; b < n_streams; ++b) {
+            if (t->cfg.sampler == LAL_SAMPLER_GPT2) {
+                if (t->h_temp[b] <= 0.0f || t->h_topk[b] <= 0) {
+                    /* greedy: argmax, no penalty, no filter (gpt2_server.c:3005) */
+                    CHECK(enqueue_gpt2(t, b, t->io_in, t->io_in + (size_t)Bmax * t->cfg.n_embd,
+                                       t->io_out));
+                    CU(cudaMemcpyAsync(tokens_out + b, t->io_out + b, 4, cudaMemcpyDeviceToHost,
+                                       t->stream));
+                    CHECK(lal_tail_sync(t));
+                } else {
+                    CHECK(gpt2_filtered_step(t, b, t->io_in,
+                                             t->io_in + (size_t)Bmax * t->cfg.n_embd, u[b],
+                                             tokens_out + b));
+                }
+                continue;
+            }
             if (t->h_temp[b] <= 0.0f || t->h_topk[b] <= 0) {
                 /* greedy: penalty then argmax, no filter (qwen7b_server.c:233-234) */
                 CHECK(enqueue_one(t, b));
@@ -2048,9 +2169,10 @@ int lal_tail_set_filter(lal_tail *t, lal_filter_topk_fn filter, lal_token_decode
         t->draw_ctx = nullptr;
         return LAL_TAIL_OK;
     }
-    if (t->cfg.sampler != LAL_SAMPLER_SERVER || t->cfg.shard_count != 1)
+    if ((t->cfg.sampler != LAL_SAMPLER_SERVER && t->cfg.sampler != LAL_SAMPLER_GPT2) ||
+        t->cfg.shard_count != 1)
         return fail(LAL_TAIL_ERR_UNSUPPORTED,
-                    "set_filter: the filter hook needs the server sampler and one shard");
+                    "set_filter: the filter hook needs the server or GPT-2 sampler and one shard");
     if (!t->f_cand_v) {
         const size_t r = (size_t)t->nrows;
         CU(cudaMalloc(&t->f_cand_v, 4 * r));

@@ -407,6 +407,39 @@ __host__ __device__ constexpr size_t gpt2_finish_bytes(int cap, int h_slots) {
                : (size_t)wide_area_bytes(cap);
 }
 
+/* The nucleus marks of a pool the wide path exported (the filter hook's
+ * first half): every row kept without top-p; with it, the pool's weights over
+ * its largest value and gpt2_nucleus, for a pool of at most kGpt2RerankN rows
+ * (a larger one -- ties across most of the vocabulary -- reports
+ * DEV_CAPACITY). */
+__device__ __noinline__ void gpt2_pool_nucleus(const Gpt2Finish &f, uint8_t *smem, Misc *ms) {
+    const int tid = threadIdx.x;
+    __syncthreads();
+    const int m = min(f.diag->n_cand, f.pool_cap);
+    const bool nucleus = f.top_p > 0.0f && f.top_p < 1.0f;
+    if (!nucleus) {
+        for (int i = tid; i < m; i += NT) f.pool_keep[i] = 1;
+        return;
+    }
+    if (m > kGpt2RerankN) {
+        if (tid == 0) atomicCAS(f.status, 0, (int)DEV_CAPACITY);
+        return;
+    }
+    float *Ce = reinterpret_cast<float *>(smem);
+    float *P = Ce + kGpt2RerankN, *Q = P + kGpt2RerankN;
+    int *R = reinterpret_cast<int *>(Q + kGpt2RerankN);
+    float mx = -1e30f;
+    for (int i = tid; i < m; i += NT) mx = fmaxf(mx, __ldcg(f.pool_val + i));
+    const float max_l = block_max_f(mx, ms);
+    const ExpfTables ex{f.expf_x, f.expf_y, f.expf_bits, f.expf_off, f.expf_hash,
+                        f.expf_hash_probe};
+    const float temp = f.temperature[0];
+    for (int i = tid; i < m; i += NT) Ce[i] = ex.weight(__ldcg(f.pool_val + i), max_l, temp);
+    __syncthreads();
+    const int n_keep = gpt2_nucleus(f.top_p, m, Ce, P, R, Q, ms);
+    for (int i = tid; i < m; i += NT) f.pool_keep[i] = R[i] < n_keep ? 1 : 0;
+}
+
 /* The server's sampler (gpt2_server.c:2862-3013) after the re-score, by one
  * CTA.  Every row the heap left out has an int8 logit <= the bound B (the
  * heap kept every row above it), and the repetition penalty never raises a
@@ -571,8 +604,15 @@ __device__ __noinline__ void gpt2_finish(const Gpt2Finish &f, uint8_t *smem, Mis
         a.hn = hn;
         a.hhead = hhead;
         a.top_p = f.top_p;
+        if (f.candidates_only) {
+            a.candidates_only = 1;
+            a.cand_val = f.pool_val;
+            a.cand_idx = f.pool_idx;
+            a.cand_cap = f.pool_cap;
+        }
         __syncthreads();
         wide_dense(a, smem, ms);
+        if (f.candidates_only) gpt2_pool_nucleus(f, smem, ms);
         return;
     }
     StreamDiag dg;
@@ -660,7 +700,24 @@ __device__ __noinline__ void gpt2_finish(const Gpt2Finish &f, uint8_t *smem, Mis
         }
         __syncthreads();
         int n_cand = m;
-        if (f.top_p > 0.0f && f.top_p < 1.0f) n_cand = gpt2_nucleus(f.top_p, m, Ce, P, Rk, Q, ms);
+        const bool nucleus = f.top_p > 0.0f && f.top_p < 1.0f;
+        if (nucleus) n_cand = gpt2_nucleus(f.top_p, m, Ce, P, Rk, Q, ms);
+        if (f.candidates_only) {
+            /* the filter hook's pool: every candidate, the nucleus's mark */
+            for (int i = tid; i < m && i < f.pool_cap; i += NT) {
+                f.pool_val[i] = Ov[i];
+                f.pool_idx[i] = Oi[i];
+                f.pool_keep[i] = !nucleus || Rk[i] < n_cand ? 1 : 0;
+            }
+            if (tid == 0) {
+                dg.threshold = key2f(T);
+                dg.max_l = max_l;
+                dg.n_cand = m;
+                dg.token = -1;
+                *f.diag = dg;
+            }
+            return;
+        }
         if (tid == 0) {
             float acc = 0.0f;
             for (int i = 0; i < m; ++i) {

@@ -103,6 +103,13 @@ struct Gpt2Finish {
     int h_slots;  /* history hash slots: a power of two >= 2 * hist_cap */
     unsigned *ticket;
     int *status;
+    /* the level-2 filter hook's first half: no draw; the top-k pool {l >= T}
+     * in ascending rows (values, rows, 1 where the top-p nucleus keeps the
+     * row) and its size in diag->n_cand */
+    int candidates_only;
+    float *pool_val;
+    int *pool_idx, *pool_keep;
+    int pool_cap;
 };
 
 /* Vocab-sharded step: the candidate record one shard exports per stream.
@@ -276,9 +283,11 @@ struct TailParams {
  * phase 0 computes max, weights, running sums and the argmax fallback over
  * the kept candidates; phase 1 draws with u. */
 struct FinishParams {
-    const float *cand_val;
+    const float *cand_val;   /* or null: the values are logits[cand_idx[i]]     */
+    const float *logits;
     const int *cand_idx;
-    const int *keep;
+    const int *keep;         /* or null: every entry is kept                   */
+    int variant;             /* VARIANT_GPT2: a draw of exactly 0 takes row 0   */
     int m;
     float temperature;
     int vocab;

@@ -1460,26 +1460,31 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const float *W, int 
 __global__ void __launch_bounds__(NT) finish_kernel(const FinishParams f) {
     __shared__ Misc ms;
     const int tid = threadIdx.x;
+    auto val = [&](int i) { return f.cand_val ? f.cand_val[i] : __ldcg(f.logits + f.cand_idx[i]); };
+    auto kept = [&](int i) { return f.keep == nullptr || f.keep[i] != 0; };
     if (f.phase == 0) {
+        /* the largest kept value with '>' from -1e30f (max over equal values
+         * is the same as fmaxf's) */
         float mx = -1e30f;
         for (int i = tid; i < f.m; i += NT)
-            if (f.keep[i]) mx = fmaxf(mx, f.cand_val[i]);
+            if (kept(i)) mx = fmaxf(mx, val(i));
         const float max_l = block_max_f(mx, &ms);
         for (int i = tid; i < f.m; i += NT)
-            f.prefix[i] = f.keep[i] ? sampler_expf(__fdiv_rn(__fsub_rn(f.cand_val[i], max_l),
-                                                             f.temperature),
-                                                   f.expf_x, f.expf_y, f.expf_bits, f.expf_off)
-                                    : 0.0f;
+            f.prefix[i] = kept(i) ? sampler_expf(__fdiv_rn(__fsub_rn(val(i), max_l),
+                                                           f.temperature),
+                                                 f.expf_x, f.expf_y, f.expf_bits, f.expf_off)
+                                  : 0.0f;
         __syncthreads();
         if (tid == 0) {
             float acc = 0.0f, bv = -1e30f;
             int best = 0;
             for (int i = 0; i < f.m; ++i) {
-                if (!f.keep[i]) continue;
+                if (!kept(i)) continue;
                 acc = __fadd_rn(acc, f.prefix[i]);
                 f.prefix[i] = acc;
-                if (f.cand_val[i] > bv) {
-                    bv = f.cand_val[i];
+                const float v = val(i);
+                if (v > bv) {
+                    bv = v;
                     best = f.cand_idx[i];
                 }
             }
@@ -1493,14 +1498,17 @@ __global__ void __launch_bounds__(NT) finish_kernel(const FinishParams f) {
         const float r = __fmul_rn(f.u[0], f.diag->sum);
         int first = 0x7fffffff;
         for (int i = tid; i < f.m; i += NT)
-            if (f.keep[i] && r <= f.prefix[i]) {
+            if (kept(i) && r <= f.prefix[i]) {
                 first = i;
                 break;
             }
         if (first != 0x7fffffff) atomicMin(&ms.found, first);
         __syncthreads();
         if (tid == 0) {
-            const int tok = ms.found != 0x7fffffff ? f.cand_idx[ms.found] : f.vocab - 1;
+            int tok = ms.found != 0x7fffffff ? f.cand_idx[ms.found] : f.vocab - 1;
+            /* gpt2_server.c:2996-3001 walks every row: a draw of exactly 0
+             * stops at row 0 */
+            if (f.variant == VARIANT_GPT2 && r == 0.0f) tok = 0;
             f.diag->r = r;
             f.diag->drew = 1;
             f.diag->token = tok;

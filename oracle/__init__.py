@@ -77,6 +77,10 @@ def port():
         lib.orc_gpt2_sample_p.argtypes = [_f32p, C.c_int, C.c_float, C.c_int, C.c_float,
                                           C.c_float, C.c_void_p, C.c_int, C.c_float,
                                           C.POINTER(SampleInfo)]
+        lib.orc_gpt2_sample_f.restype = C.c_int
+        lib.orc_gpt2_sample_f.argtypes = [_f32p, C.c_int, C.c_float, C.c_int, C.c_float,
+                                          C.c_float, C.c_void_p, C.c_int, C.c_void_p,
+                                          C.c_void_p, C.c_float, C.POINTER(SampleInfo)]
         lib.orc_quantize_x_int8.restype = C.c_float
         lib.orc_quantize_x_int8.argtypes = [_f32p, _i8p, C.c_int]
         lib.orc_compute_abs_xq.argtypes = [_i8p, _u8p, C.c_int]
@@ -204,15 +208,28 @@ def gpt2_lm_head(x: np.ndarray, wq: np.ndarray, sw: np.ndarray, lib: str = "port
     return logits, None
 
 
-def gpt2_sample(logits, temperature, top_k, rep_penalty, recent, u, top_p=0.0):
-    """gpt2_server.c:2862-3013 (top-p branch when 0 < top_p < 1, no filter)
-    on a copy: (token, info, penalised logits)."""
+def gpt2_sample(logits, temperature, top_k, rep_penalty, recent, u, top_p=0.0, filt=None,
+                decode=None):
+    """gpt2_server.c:2862-3013 (top-p branch when 0 < top_p < 1; the level-2
+    filter hook when filt is given) on a copy: (token, info, penalised
+    logits)."""
     lg = np.ascontiguousarray(logits, np.float32).copy()
     rec = None if recent is None or len(recent) == 0 else np.ascontiguousarray(recent, np.int32)
     info = SampleInfo()
-    tok = port().orc_gpt2_sample_p(lg, lg.size, np.float32(temperature), int(top_k),
+    if filt is None and decode is None:
+        tok = port().orc_gpt2_sample_p(lg, lg.size, np.float32(temperature), int(top_k),
+                                       np.float32(top_p), np.float32(rep_penalty), _ptr(rec),
+                                       0 if rec is None else rec.size, np.float32(u),
+                                       C.byref(info))
+        return tok, info, lg
+    cf = FILTER_FN(filt) if filt is not None else None
+    cd = DECODE_FN(decode) if decode is not None else None
+    tok = port().orc_gpt2_sample_f(lg, lg.size, np.float32(temperature), int(top_k),
                                    np.float32(top_p), np.float32(rep_penalty), _ptr(rec),
-                                   0 if rec is None else rec.size, np.float32(u), C.byref(info))
+                                   0 if rec is None else rec.size,
+                                   C.cast(cf, C.c_void_p) if cf else None,
+                                   C.cast(cd, C.c_void_p) if cd else None, np.float32(u),
+                                   C.byref(info))
     return tok, info, lg
 
 
@@ -221,8 +238,10 @@ class Gpt2PortLoop:
     sampler, then the recent-token ring (gpt2_server.c:3347-3348 as a FIFO of
     hist_cap)."""
 
-    def __init__(self, wq, sw, hist0, hist_cap, temperature, top_k, rep_penalty, top_p=0.0):
+    def __init__(self, wq, sw, hist0, hist_cap, temperature, top_k, rep_penalty, top_p=0.0,
+                 filt=None):
         self.top_p = top_p
+        self.filt = filt
         self.wq = np.ascontiguousarray(wq, np.int8)
         self.sw = np.ascontiguousarray(sw, np.float32)
         self.cap = max(1, hist_cap)
@@ -236,7 +255,8 @@ class Gpt2PortLoop:
     def step(self, x, u):
         logits, self.kept = gpt2_lm_head(x, self.wq, self.sw)
         tok, info, self.logits = gpt2_sample(logits, self.T, self.k, self.p,
-                                             self.rec[:self.n.value], u, self.top_p)
+                                             self.rec[:self.n.value], u, self.top_p,
+                                             filt=self.filt)
         port().orc_recent_push(self.rec, C.byref(self.n), self.cap, int(tok))
         return tok, info
 

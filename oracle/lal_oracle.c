@@ -506,6 +506,19 @@ int orc_gpt2_sample(float *logits, int vocab_size, float temperature, int top_k,
 int orc_gpt2_sample_p(float *logits, int vocab_size, float temperature, int top_k, float top_p,
                       float rep_penalty, const int *recent, int n_recent, float u,
                       orc_sample_info *info) {
+    return orc_gpt2_sample_f(logits, vocab_size, temperature, top_k, top_p, rep_penalty, recent,
+                             n_recent, NULL, NULL, u, info);
+}
+
+/* The same with the server's level-2 filter hook (gpt2_server.c:2962-2978):
+ * after the top-k (and top-p) keep mask, filter(keep_mask, V, last token,
+ * recent, n_recent, decode) may change any entry; if no entry is left, the
+ * top-k pool {l >= threshold} is restored.  The softmax and the draw then
+ * run over every row the mask keeps (gpt2_server.c:2981-3002). */
+int orc_gpt2_sample_f(float *logits, int vocab_size, float temperature, int top_k, float top_p,
+                      float rep_penalty, const int *recent, int n_recent,
+                      orc_filter_fn filter, orc_decode_fn decode, float u,
+                      orc_sample_info *info) {
     orc_sample_info loc;
     if (!info) info = &loc;
     memset(info, 0, sizeof(*info));
@@ -530,7 +543,7 @@ int orc_gpt2_sample_p(float *logits, int vocab_size, float temperature, int top_
             threshold = max_val;
             copy[max_v] = -1e30f;
         }
-        unsigned char *keep = (unsigned char *)calloc((size_t)vocab_size, 1);
+        int *keep = (int *)calloc((size_t)vocab_size, sizeof(int));
         if (top_p > 0.0f && top_p < 1.0f) {
             int *top_idx = (int *)malloc(sizeof(int) * (size_t)vocab_size);
             float *top_val = (float *)malloc(sizeof(float) * (size_t)vocab_size);
@@ -574,6 +587,15 @@ int orc_gpt2_sample_p(float *logits, int vocab_size, float temperature, int top_
         } else {
             for (int v = 0; v < vocab_size; v++)
                 if (logits[v] >= threshold) keep[v] = 1;
+        }
+        if (filter) {
+            const int last = n_recent > 0 ? recent[n_recent - 1] : -1;
+            (void)filter(keep, vocab_size, last, recent, n_recent, decode);
+            int any = 0;
+            for (int v = 0; v < vocab_size && !any; v++) any = keep[v] != 0;
+            if (!any)
+                for (int v = 0; v < vocab_size; v++)
+                    if (logits[v] >= threshold) keep[v] = 1;
         }
         float actual_max = -1e30f;
         int n_cand = 0;

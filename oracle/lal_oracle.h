@@ -101,6 +101,10 @@ int   orc_sample_token_filtered(float *logits, int vocab_size, float temperature
                                 int n_recent, orc_filter_fn filter,
                                 orc_decode_fn decode, orc_draw_fn draw,
                                 void *draw_ctx, orc_sample_info *info);
+int   orc_gpt2_sample_f(float *logits, int vocab_size, float temperature, int top_k,
+                        float top_p, float rep_penalty, const int *recent, int n_recent,
+                        orc_filter_fn filter, orc_decode_fn decode, float u,
+                        orc_sample_info *info);
 
 /* glibc expf element-wise (runtime/lal_sampling.h:112,120 call expf). */
 void  orc_expf_batch(const float *x, float *y, long n);

@@ -191,3 +191,65 @@ def test_gpt2_top_p_over_an_all_tied_vocabulary():
             assert tok == ptok, (top_p, u)
             assert t.diag(0)["n_cand"] == info.n_cand, (top_p, u)
     t.close()
+
+
+def _drop_last_and_even(keep, n_vocab, last, recent, n_recent, decode):
+    """The reference's test filter (tests/verify_qwen7b_lal.c:45-67): drops
+    the last token and every even row."""
+    ks = np.ctypeslib.as_array(keep, shape=(n_vocab,))
+    dropped = int(ks[::2].sum())
+    ks[::2] = 0
+    if 0 <= last < n_vocab and ks[last]:
+        ks[last] = 0
+        dropped += 1
+    return dropped
+
+
+def _ban_all(keep, n_vocab, last, recent, n_recent, decode):
+    np.ctypeslib.as_array(keep, shape=(n_vocab,))[:] = 0
+    return n_vocab
+
+
+def _add_rows(keep, n_vocab, last, recent, n_recent, decode):
+    """A filter that also keeps rows outside the top-k pool: the server's
+    softmax then runs over them too (gpt2_server.c:2981-2994)."""
+    ks = np.ctypeslib.as_array(keep, shape=(n_vocab,))
+    ks[7] = 1
+    ks[n_vocab - 3] = 1
+    return 0
+
+
+@pytest.mark.parametrize("top_p", [0.0, 0.9])
+def test_gpt2_filter_hook_loop_matches_oracle(top_p):
+    """The GPT-2 server's level-2 filter call (gpt2_server.c:2962-2978) inside
+    the GPT-2 context (lal_tail_set_filter): a C1 loop whose filter drops the
+    last token and every even row, one step where it empties the mask (the
+    top-k pool is restored), one where it adds rows, greedy steps (no
+    filter): tokens and history against the restatement."""
+    cfg = synth.CONFIGS["c1_gpt2"]
+    W = synth.lm_head_f32(cfg)
+    q, s = oracle.quantize_rows(W, "port")
+    hist0 = synth.history(cfg, 0)
+    t = gpt2_tail(q, s, cfg)
+    t.set_top_p(top_p)
+    t.set_history(0, hist0)
+    port = oracle.Gpt2PortLoop(q, s, hist0, cfg.hist, cfg.temperature, cfg.top_k,
+                               cfg.rep_penalty, top_p=top_p)
+    us = draws(12, 21)
+    for step in range(12):
+        filt = {4: _ban_all, 7: _add_rows}.get(step, _drop_last_and_even)
+        temp = 0.0 if step == 9 else cfg.temperature
+        t.set_sampling([temp], [cfg.top_k], [cfg.rep_penalty])
+        port.T = temp
+        t.set_filter(filt)
+        port.filt = filt
+        x = synth.hidden(cfg, step)
+        tok = int(t.step(x, us[step:step + 1])[0])
+        ptok, info = port.step(x[0], us[step])
+        assert tok == ptok, (top_p, step)
+        if filt is _drop_last_and_even and temp > 0:
+            assert tok % 2 == 1 or us[step] == 0.0
+        np.testing.assert_array_equal(bits(t.logits(0)), bits(port.logits), err_msg=str(step))
+    np.testing.assert_array_equal(t.get_history(0), port.history())
+    t.set_filter(None)
+    t.close()
