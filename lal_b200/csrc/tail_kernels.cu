@@ -1665,8 +1665,30 @@ __device__ __noinline__ void merge_small(const MergeParams &mp, int b, int M, co
     if (k > mp.vocab) k = mp.vocab;
     if (k > M) k = M;
     if (k < 1) k = 1;
+    /* the largest key first (max_l, runtime/lal_sampling.h:107-109): every
+     * entry's weight table load then goes out before the threshold count,
+     * which hides its latency */
+    {
+        const uint32_t wmx = __reduce_max_sync(0xffffffffu, max(me[0], me[1]));
+        if (lane == 0) ms->wmax[warp] = wmx;
+    }
+    __syncthreads();
+    uint32_t mx = ms->wmax[0];
+    for (int w = 1; w < NWARP; ++w) mx = max(mx, ms->wmax[w]);
+    const float max_l = fmaxf(-1e30f, key2f(mx));
+    float xw[2] = {0.0f, 0.0f}, yr[2] = {0.0f, 0.0f};
+    uint4 hp[2] = {make_uint4(0u, 0u, 0u, 0u), make_uint4(0u, 0u, 0u, 0u)};
+    const bool early_w = !greedy && mp.expf_hash != nullptr;
+    if (early_w)
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+            if (have[h]) {
+                xw[h] = __fdiv_rn(__fsub_rn(key2f(me[h]), max_l), temp);
+                hp[h] = expf_hash_load(xw[h], mp.expf_hash);
+                yr[h] = lal_expf_rounded(xw[h]);
+            }
     /* T = min{ key : #{keys > key} < k } (the k-th largest with
-     * multiplicity), and the largest key (max_l) */
+     * multiplicity) */
     int gt[2] = {0, 0};
     {
         const uint4 *K4 = reinterpret_cast<const uint4 *>(Mk);
@@ -1687,20 +1709,12 @@ __device__ __noinline__ void merge_small(const MergeParams &mp, int b, int M, co
     for (int h = 0; h < 2; ++h)
         if (have[h] && gt[h] < k) best = min(best, me[h]);
     best = __reduce_min_sync(0xffffffffu, best);
-    const uint32_t wmx = __reduce_max_sync(0xffffffffu, max(me[0], me[1]));
-    if (lane == 0) {
-        ms->scan[warp] = best;
-        ms->wmax[warp] = wmx;
-    }
+    if (lane == 0) ms->scan[warp] = best;
     if (tid == 0) ms->found = -1;
     __syncthreads();
-    uint32_t T = ms->scan[0], mx = ms->wmax[0];
-    for (int w = 1; w < NWARP; ++w) {
-        T = min(T, ms->scan[w]);
-        mx = max(mx, ms->wmax[w]);
-    }
+    uint32_t T = ms->scan[0];
+    for (int w = 1; w < NWARP; ++w) T = min(T, ms->scan[w]);
     mstamp(0);
-    const float max_l = fmaxf(-1e30f, key2f(mx));
     /* candidates {l >= T} and their places; each one's weight
      * expf((l - max_l) / T) (runtime/lal_sampling.h:107-112) */
     const ExpfTables ex{mp.expf_x, mp.expf_y, mp.expf_bits, mp.expf_off, mp.expf_hash,
@@ -1713,7 +1727,9 @@ __device__ __noinline__ void merge_small(const MergeParams &mp, int b, int M, co
         cand[h] = have[h] && me[h] >= T;
         bal[h] = __ballot_sync(0xffffffffu, cand[h]);
         if (lane == 0) ms->hist[h * NWARP + warp] = (uint32_t)__popc(bal[h]);
-        w[h] = cand[h] && !greedy ? ex.weight(key2f(me[h]), max_l, temp) : 0.0f;
+        w[h] = !cand[h] || greedy ? 0.0f
+               : early_w ? expf_hash_resolve(xw[h], yr[h], hp[h], mp.expf_hash, mp.expf_hash_probe)
+                         : ex.weight(key2f(me[h]), max_l, temp);
     }
     __syncthreads();
     int off[2] = {0, 0}, m = 0;
