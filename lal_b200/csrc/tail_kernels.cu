@@ -57,9 +57,6 @@ constexpr int kMergeHead = (int)((sizeof(MergeHead) + 15) / 16 * 16);
 template <class Load>
 __device__ void merge_sample(const MergeParams &mp, int b, uint8_t *area, Misc *ms, Load load);
 
-__device__ __forceinline__ void st_relaxed_sys_u64(uint64_t *p, uint64_t v) {
-    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
 __device__ __forceinline__ uint64_t ld_relaxed_sys_u64(const uint64_t *p) {
     uint64_t v;
     asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
@@ -1035,6 +1032,9 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
             for (int t = tid; t < S; t += NT) {
                 const uint32_t me = Sk[t];
                 int gt = 0;
+                /* four 16-byte loads in flight: the loop is bound by their
+                 * latency, not by the compares */
+#pragma unroll 4
                 for (int j = 0; j < S4 / 4; ++j) {
                     const uint4 v = K4[j];
                     gt += (v.x > me) + (v.y > me) + (v.z > me) + (v.w > me);
@@ -1068,6 +1068,7 @@ __global__ void __launch_bounds__(NT, 1) tail_kernel(const __grid_constant__ Tai
                 const int mi = Si[tid];
                 const int4 *I4 = reinterpret_cast<const int4 *>(Si);
                 int r = 0;
+#pragma unroll 4
                 for (int j = 0; j < S4 / 4; ++j) {
                     const uint4 v = K4[j];
                     const int4 ix = I4[j];
@@ -1694,6 +1695,7 @@ __device__ __noinline__ void merge_small(const MergeParams &mp, int b, int M, co
         const uint4 *K4 = reinterpret_cast<const uint4 *>(Mk);
         int j = 0;
         if ((reinterpret_cast<uintptr_t>(Mk) & 15u) == 0)
+#pragma unroll 4
             for (; j + 4 <= M; j += 4) {
                 const uint4 v = K4[j >> 2];
 #pragma unroll
