@@ -675,13 +675,26 @@ __global__ void __launch_bounds__(NT, 1) batch_select_kernel(const __grid_consta
             }
         }
         __syncthreads();
+        uint32_t gtop = 0u;
         for (int g0 = 0; g0 < p.n_groups; g0 += NT) {
             const int g = g0 + tid;
-            hist_add(hist, g < p.n_groups ? Gk[g] >> 20 : 0u, counts(g));
+            const uint32_t key = g < p.n_groups ? Gk[g] : 0u;
+            gtop = max(gtop, key);
+            hist_add(hist, key >> 20, counts(g));
+        }
+        gtop = __reduce_max_sync(0xffffffffu, gtop);
+        if ((tid & 31) == 0) ms->wmax[tid >> 5] = gtop;
+        __syncthreads();
+        /* one warp, down from the largest maximum's bin (the answer is near
+         * the top: kp of thousands of groups) */
+        if (tid < 32) {
+            uint32_t top = ms->wmax[0];
+            for (int w = 1; w < NWARP; ++w) top = max(top, ms->wmax[w]);
+            const uint32_t bin = warp_boundary_bin_4096(hist, top >> 20, (uint32_t)kp);
+            if (tid == 0) ms->sh[0] = bin;
         }
         __syncthreads();
-        uint32_t gab, gcnt;
-        L = boundary_bin(hist, 4096, (uint32_t)kp, ms, &gab, &gcnt) << 20;
+        L = ms->sh[0] << 20;
         for (int i = tid; i < 4096; i += NT) hist[i] = 0u; /* for the fallback */
         /* the candidate groups, listed in Gl */
         if (tid == 0) s_count = 0;
@@ -842,6 +855,27 @@ __global__ void __launch_bounds__(NT, 1) batch_select_kernel(const __grid_consta
     __syncthreads();
     }  /* full pass */
 
+    /* Early weights (a superset of at most NT keys: one a thread): the
+     * superset holds every candidate and the largest logit, so max_l
+     * (runtime/lal_sampling.h:107-109) is known before T, and each key's
+     * weight-table loads go out now and land during the select of T. */
+    const bool early = !greedy && S <= NT;
+    float max_l_e = -1e30f, xw = 0.0f;
+    uint32_t bw = 0u, olo = 0u, ohi = 0u;
+    if (early) {
+        uint32_t mk = tid < S ? Sk[tid] : 0u;
+        mk = __reduce_max_sync(0xffffffffu, mk);
+        if ((tid & 31) == 0) ms->wmax[tid >> 5] = mk;
+        __syncthreads();
+        for (int w = 0; w < NWARP; ++w) mk = max(mk, ms->wmax[w]);
+        max_l_e = fmaxf(-1e30f, key2f(mk));
+        if (tid < S) {
+            xw = __fdiv_rn(__fsub_rn(key2f(Sk[tid]), max_l_e), temp);
+            bw = expf_bitmap_word(xw, p.expf_bits);
+            expf_offsets(xw, p.expf_off, &olo, &ohi);
+        }
+        __syncthreads(); /* wmax is read before anything reuses it */
+    }
     /* 4. T exactly: the k-th largest key of the superset (counting for a
      * small superset: T = min{ key : #{keys > key} < k }) */
     uint32_t T;
@@ -893,21 +927,32 @@ __global__ void __launch_bounds__(NT, 1) batch_select_kernel(const __grid_consta
         batch_wide(p, b, k, greedy, temp, u0, hn, hhead, bsm, ms);
         return;
     }
+    /* the candidates with their weights when early (Ce in the list's order;
+     * with S <= NT the thread of superset entry e holds its loads) */
     for (int e = e0; e < e1; ++e)
         if (Sk[e] >= T) {
             Cv[pos] = key2f(Sk[e]);
             Ci[pos] = p.row_base + Si[e];
+            if (early) Ce[pos] = expf_with_range(xw, bw, olo, ohi, p.expf_x, p.expf_y);
             ++pos;
         }
     __syncthreads();
-    /* ascending vocab order */
+    /* ascending vocab order (the early weights move with their rows) */
     if (m <= 64) {
-        for (int i = tid; i < m; i += NT) {
-            const int me = Ci[i];
-            int r = 0;
+        int me = 0, r = 0;
+        float mv = 0.0f, mw = 0.0f;
+        if (tid < m) {
+            me = Ci[tid];
+            mv = Cv[tid];
+            mw = early ? Ce[tid] : 0.0f;
+#pragma unroll 8
             for (int j = 0; j < m; ++j) r += Ci[j] < me;
+        }
+        __syncthreads();
+        if (tid < m) {
             Oi[r] = me;
-            Ov[r] = Cv[i];
+            Ov[r] = mv;
+            if (early) Ce[r] = mw;
         }
     } else {
         int n2 = 1;
@@ -915,6 +960,7 @@ __global__ void __launch_bounds__(NT, 1) batch_select_kernel(const __grid_consta
         for (int i = tid; i < n2; i += NT) {
             Oi[i] = i < m ? Ci[i] : 0x7fffffff;
             Ov[i] = i < m ? Cv[i] : 0.0f;
+            if (early && i >= m) Ce[i] = 0.0f;
         }
         __syncthreads();
         for (int size = 2; size <= n2; size <<= 1)
@@ -927,9 +973,14 @@ __global__ void __launch_bounds__(NT, 1) batch_select_kernel(const __grid_consta
                     if ((a > bb) == asc) {
                         Oi[lo] = bb;
                         Oi[hi] = a;
-                        const float t = Ov[lo];
+                        float t = Ov[lo];
                         Ov[lo] = Ov[hi];
                         Ov[hi] = t;
+                        if (early) {
+                            t = Ce[lo];
+                            Ce[lo] = Ce[hi];
+                            Ce[hi] = t;
+                        }
                     }
                 }
                 __syncthreads();
@@ -959,18 +1010,22 @@ __global__ void __launch_bounds__(NT, 1) batch_select_kernel(const __grid_consta
 
     /* 5. max over candidates floored at -1e30 (runtime/lal_sampling.h:107-109),
      * weights expf((l - max_l)/T), sequential sums in vocab order, draw */
-    float mx = -1e30f;
-    for (int i = tid; i < m; i += NT) mx = fmaxf(mx, Ov[i]);
-    const float max_l = block_max_f(mx, ms);
+    float max_l = max_l_e;
+    if (!early) {
+        float mx = -1e30f;
+        for (int i = tid; i < m; i += NT) mx = fmaxf(mx, Ov[i]);
+        max_l = block_max_f(mx, ms);
+    }
     dg.max_l = max_l;
     int token;
     if (greedy) {
         token = Oi[0];
     } else {
-        for (int i = tid; i < m; i += NT) {
-            const float x = __fdiv_rn(__fsub_rn(Ov[i], max_l), temp);
-            Ce[i] = sampler_expf(x, p.expf_x, p.expf_y, p.expf_bits, p.expf_off);
-        }
+        if (!early)
+            for (int i = tid; i < m; i += NT) {
+                const float x = __fdiv_rn(__fsub_rn(Ov[i], max_l), temp);
+                Ce[i] = sampler_expf(x, p.expf_x, p.expf_y, p.expf_bits, p.expf_off);
+            }
         __syncthreads();
         if (tid == 0) {
             /* values fetched eight at a time, the adds in order */
