@@ -835,6 +835,8 @@ struct lal_tail {
     int8_t *xq_b = nullptr;
     float *sx_b = nullptr;
     uint32_t *gmax_b = nullptr;
+    int *ksplit_b = nullptr; /* the GEMM's split tiles' partial dots */
+    size_t ksplit_bytes = 0;
     BatchPlan bplan;
     /* peer exchange of the sharded step: this rank's receive buffer
      * [2][shard_count][rec_bytes] (exported by IPC handle), the device array
@@ -900,7 +902,7 @@ void destroy_ctx(lal_tail *t) {
     free_copies(t);
     void *bufs[] = {t->W, t->sw, t->io_in, t->io_out, t->logits, t->temp, t->topk, t->pen,
                     t->hist_ids, t->hist_n, t->hist_head, t->diag, t->phase_ts,
-                    t->x_send, t->x_recv, t->xq_b, t->sx_b, t->gmax_b, t->x_peer, t->d_peer,
+                    t->x_send, t->x_recv, t->xq_b, t->sx_b, t->gmax_b, t->ksplit_b, t->x_peer, t->d_peer,
                     t->f_cand_v, t->f_prefix, t->f_u, t->f_cand_i, t->f_keep, t->f_tok,
                     t->f_diag, t->d_norm_w, t->g2_cand_i, t->g2_count,
                     t->g2_bound, t->g2_ticket, t->g2_kept_v};
@@ -1108,8 +1110,10 @@ int ctx_alloc(lal_tail *t) {
         CU(cudaMemset(t->xq_b, 0, (size_t)256 * t->ld));
         CU(cudaMalloc(&t->sx_b, 4ull * 256));
         CU(cudaMalloc(&t->gmax_b, 4ull * 256 * batch_groups(t->nrows)));
+        t->ksplit_bytes = batch_split_bytes(t->nrows, t->ld, t->ds->num_sms, B);
+        if (t->ksplit_bytes) CU(cudaMalloc(&t->ksplit_b, t->ksplit_bytes));
         t->batch_ok = batch_plan(t->bplan, t->W, t->sw, t->nrows, t->ld, t->ds->num_sms, t->xq_b,
-                                 t->sx_b, t->gmax_b, B, c.history_cap,
+                                 t->sx_b, t->gmax_b, t->ksplit_b, B, c.history_cap,
                                  std::min(c.max_top_k, c.vocab_size)) == 0;
     }
     return LAL_TAIL_OK;

@@ -22,7 +22,14 @@
  *                          Two accumulator buffers let the epilogue of one
  *                          tile overlap the MMAs of the next.  int8 products
  *                          accumulate exactly in int32, so the logits equal
- *                          the reference's bit for bit.
+ *                          the reference's bit for bit.  The tiles left over
+ *                          after the last whole wave (4 of Qwen's 1188 on 148
+ *                          SMs) would cost a whole extra wave: they are split
+ *                          along K instead, one chunk a CTA after its own
+ *                          tiles, each chunk's int32 partial dots stored to
+ *                          its own slot (still in L2 when the select runs);
+ *                          the select adds a stream's slots (exact in any
+ *                          order) into its logits.
  *   batch_select_kernel    one CTA per stream: the repetition penalty
  *                          (runtime/lal_sampling.h:59-67; occurrences counted
  *                          in a shared-memory hash of the history), a key
@@ -56,6 +63,8 @@ constexpr int kGemmStagesMax = 8;
 constexpr int kGemmSmemLimit = 232448;
 constexpr int kStageGroups = 512;  /* 32-row logit groups staged a round (select) */
 constexpr int kPenGroupWords = 512; /* bitmap words of groups holding a penalised row */
+constexpr int kSplitChunksMax = 32; /* K chunks of a split tile (the select keeps a row's in registers) */
+constexpr int kSplitGroupsMax = 4 * 74; /* 32-row groups of the split tiles (>= 2 chunks a tile, 148 SMs) */
 
 /* ------------------------------------------------------------ PTX --- */
 __device__ __forceinline__ uint64_t policy_evict_last() {
@@ -193,7 +202,31 @@ struct GemmParams {
     int n_groups;
     int rows, B, N, kblocks, stages, stage_bytes, tmem_cols;
     int *status;
+    /* tiles [0, reg_end) whole, tile t by CTA t mod grid; tiles [reg_end,
+     * n_tiles) in split_chunks K chunks of split_cb boxes, chunk c of tile
+     * reg_end + u / split_chunks by CTA u < split_units */
+    int reg_end, split_units, split_chunks, split_cb;
+    int *split_part; /* [n_tiles - reg_end][split_chunks][N][128] int32 partial dots */
 };
+
+/* logits and group maxima of 32 streams (c0 ..) of one warp's 32 rows from
+ * their int32 dots r[j] (stream c0 + j, this lane's row) */
+__device__ __forceinline__ void emit_logits32(const GemmParams &p, const float *sx, float sw,
+                                              int row, int group, int c0, const uint32_t (&r)[32],
+                                              int lane) {
+    uint32_t mine = 0u;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+        const int b = c0 + j;
+        /* runtime/lal_q8_kernel.h:489: scale_x*scale_w[v]*(float)dot */
+        const float l = __fmul_rn(__fmul_rn(sx[b], sw), __int2float_rn((int)r[j]));
+        if (row < p.rows && b < p.B) p.logits[(size_t)b * p.rows + row] = l;
+        /* the group maximum of stream b, kept by lane j */
+        const uint32_t gm = __reduce_max_sync(0xffffffffu, row < p.rows ? f2key(l) : 0u);
+        if (lane == j) mine = gm;
+    }
+    if (c0 + lane < p.B) p.gmax[(size_t)(c0 + lane) * p.n_groups + group] = mine;
+}
 
 __device__ __forceinline__ bool bwait(uint64_t *b, uint32_t parity, volatile int *abort_flag) {
     return mbar_wait(b, parity, abort_flag);
@@ -215,8 +248,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_i8_kernel(const __grid_c
      * copy or MMA may be in flight when the CTA leaves */
     volatile int *never = reinterpret_cast<int *>(tholder + 2);
     float *sx = reinterpret_cast<float *>(tholder + 4);
-    const int n_tiles = (p.rows + kBM - 1) / kBM;
-
     if (threadIdx.x == 0) {
         for (int s = 0; s < p.stages; ++s) {
             mbar_init(&full[s], 1);
@@ -251,14 +282,33 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_i8_kernel(const __grid_c
      * ring of W first cost 5 us a launch at B=64). */
     const uint32_t bytes = (uint32_t)(kBM * kBK + p.N * kBK);
     const uint64_t pol_w = policy_evict_first(), pol_x = policy_evict_last();
-    const int my_iters = ((n_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1) * p.kblocks;
+    /* this CTA's work: its whole tiles, then its K chunk of a split tile (u_n
+     * boxes) as accumulator round a = n_reg when there is one */
+    const int G = (int)gridDim.x, bid = (int)blockIdx.x;
+    const bool has_unit = bid < p.split_units;
+    const int u_tile = has_unit ? p.reg_end + bid / p.split_chunks : 0;
+    const int u_kb0 = has_unit ? (bid % p.split_chunks) * p.split_cb : 0;
+    const int u_n = has_unit ? min(p.kblocks, u_kb0 + p.split_cb) - u_kb0 : 0;
+    const int n_reg = bid < p.reg_end ? (p.reg_end - 1 - bid) / G + 1 : 0;
+    const int n_acc = (u_n > 0 ? 1 : 0) + n_reg;
+    const int my_iters = u_n + n_reg * p.kblocks;
+    auto coord = [&](int it, int &tile, int &kb) {
+        if (it < n_reg * p.kblocks) {
+            tile = bid + (it / p.kblocks) * G;
+            kb = it % p.kblocks;
+        } else {
+            tile = u_tile;
+            kb = u_kb0 + (it - n_reg * p.kblocks);
+        }
+    };
     const int pre = min(2, my_iters);
     if (warp == 0 && lane == 0)
         for (int it = 0; it < pre; ++it) {
-            const int tile = blockIdx.x + (it / p.kblocks) * (int)gridDim.x;
+            int tile, kb;
+            coord(it, tile, kb);
             mbar_expect_tx(&full[it], bytes);
-            tma_load_2d(gsm + (size_t)it * p.stage_bytes, &p.tmW, (it % p.kblocks) * kBK,
-                        tile * kBM, &full[it], pol_w);
+            tma_load_2d(gsm + (size_t)it * p.stage_bytes, &p.tmW, kb * kBK, tile * kBM, &full[it],
+                        pol_w);
         }
     grid_dep_wait();
     grid_dep_launch_dependents();
@@ -270,25 +320,24 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_i8_kernel(const __grid_c
             /* producer: one W box and one X box per stage (the first `pre`
              * stages' W boxes are on their way already) */
             int it = 0;
-            bool ok = true;
-            for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x)
-                for (int kb = 0; kb < p.kblocks; ++kb, ++it) {
-                    const int s = it % p.stages;
-                    const uint32_t use = (uint32_t)(it / p.stages);
-                    uint8_t *st = gsm + (size_t)s * p.stage_bytes;
-                    if (it < pre) {
-                        tma_load_2d(st + kBM * kBK, &p.tmX, kb * kBK, 0, &full[s], pol_x);
-                        continue;
-                    }
-                    if (!bwait(&empty[s], (use & 1u) ^ 1u, abort_flag)) {
-                        *abort_flag = 1;
-                        ok = false;
-                        break;
-                    }
-                    mbar_expect_tx(&full[s], bytes);
-                    tma_load_2d(st, &p.tmW, kb * kBK, tile * kBM, &full[s], pol_w);
+            for (; it < my_iters; ++it) {
+                int tile, kb;
+                coord(it, tile, kb);
+                const int s = it % p.stages;
+                const uint32_t use = (uint32_t)(it / p.stages);
+                uint8_t *st = gsm + (size_t)s * p.stage_bytes;
+                if (it < pre) {
                     tma_load_2d(st + kBM * kBK, &p.tmX, kb * kBK, 0, &full[s], pol_x);
+                    continue;
                 }
+                if (!bwait(&empty[s], (use & 1u) ^ 1u, abort_flag)) {
+                    *abort_flag = 1;
+                    break;
+                }
+                mbar_expect_tx(&full[s], bytes);
+                tma_load_2d(st, &p.tmW, kb * kBK, tile * kBM, &full[s], pol_w);
+                tma_load_2d(st + kBM * kBK, &p.tmX, kb * kBK, 0, &full[s], pol_x);
+            }
             /* no copy may be in flight when the CTA exits */
             for (int q = max(0, it - p.stages); q < it; ++q)
                 bwait(&full[q % p.stages], (uint32_t)(q / p.stages) & 1u, never);
@@ -297,18 +346,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_i8_kernel(const __grid_c
         if (lane == 0) {
             /* MMA issuer */
             const uint32_t idesc = idesc_i8(kBM, p.N);
-            int it = 0, tcount = 0;
+            int it = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x, ++tcount) {
-                const int acc = tcount & 1;
-                const uint32_t ause = (uint32_t)(tcount >> 1);
-                if (tcount >= 2 && !bwait(&tempty[acc], (ause & 1u) ^ 1u, abort_flag)) {
+            for (int a = 0; a < n_acc && ok; ++a) {
+                const int acc = a & 1;
+                const uint32_t ause = (uint32_t)(a >> 1);
+                if (a >= 2 && !bwait(&tempty[acc], (ause & 1u) ^ 1u, abort_flag)) {
                     *abort_flag = 1;
                     break;
                 }
                 tc_fence_after();
                 const uint32_t d_tmem = tbase + (uint32_t)(acc * p.N);
-                for (int kb = 0; kb < p.kblocks; ++kb, ++it) {
+                const int nkb = a == n_reg ? u_n : p.kblocks;
+                for (int kb = 0; kb < nkb; ++kb, ++it) {
                     const int s = it % p.stages;
                     if (!bwait(&full[s], (uint32_t)(it / p.stages) & 1u, abort_flag)) {
                         *abort_flag = 1;
@@ -334,34 +384,42 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_i8_kernel(const __grid_c
         /* epilogue (warps 2-5): warp w reads tensor-memory lanes
          * 32*(w%4) .. +31 */
         const int q = warp & 3;
-        int tcount = 0;
-        for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++tcount) {
-            const int acc = tcount & 1;
-            const uint32_t ause = (uint32_t)(tcount >> 1);
+        for (int a = 0; a < n_acc; ++a) {
+            const int acc = a & 1;
+            const uint32_t ause = (uint32_t)(a >> 1);
             if (!bwait(&tfull[acc], ause & 1u, abort_flag)) {
                 *abort_flag = 1;
                 break;
             }
             tc_fence_after();
+            const bool part = a == n_reg;
+            const int tile = part ? u_tile : bid + a * G;
             const int row = tile * kBM + q * 32 + lane;
             const float sw = row < p.rows ? __ldg(p.scale_w + row) : 0.0f;
             const int group = tile * 4 + q; /* this warp's 32 rows */
+            if (part) {
+                /* a K chunk: its partial dots into its own slot, for the
+                 * select to add up */
+                const int slot = (tile - p.reg_end) * p.split_chunks + bid % p.split_chunks;
+                int *dst = p.split_part + (size_t)slot * p.N * kBM + q * 32 + lane;
+                for (int c0 = 0; c0 < p.N; c0 += 32) {
+                    uint32_t r[32];
+                    tmem_ld32(tbase + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * p.N + c0), r);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        if (c0 + j < p.B) dst[(size_t)(c0 + j) * kBM] = (int)r[j];
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tempty[acc]);
+                continue;
+            }
             for (int c0 = 0; c0 < p.N; c0 += 32) {
                 uint32_t r[32];
                 tmem_ld32(tbase + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * p.N + c0), r);
                 tmem_ld_wait();
-                uint32_t mine = 0u;
-#pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const int b = c0 + j;
-                    /* runtime/lal_q8_kernel.h:489: scale_x*scale_w[v]*(float)dot */
-                    const float l = __fmul_rn(__fmul_rn(sx[b], sw), __int2float_rn((int)r[j]));
-                    if (row < p.rows && b < p.B) p.logits[(size_t)b * p.rows + row] = l;
-                    /* the group maximum of stream b, kept by lane j */
-                    const uint32_t gm = __reduce_max_sync(0xffffffffu, row < p.rows ? f2key(l) : 0u);
-                    if (lane == j) mine = gm;
-                }
-                if (c0 + lane < p.B) p.gmax[(size_t)(c0 + lane) * p.n_groups + group] = mine;
+                emit_logits32(p, sx, sw, row, group, c0, r, lane);
             }
             tc_fence_before();
             __syncwarp();
@@ -398,8 +456,13 @@ struct BatchSelectParams {
     uint8_t *shard_out; /* [B][rec_bytes] records, or null */
     int rec_cap, rec_bytes;
     int s_cap, c_cap, h_slots; /* superset, candidate and hash capacities */
-    const uint32_t *gmax;      /* [B][n_groups] raw group maxima (GEMM) */
+    uint32_t *gmax;            /* [B][n_groups] raw group maxima (GEMM) */
     int n_groups;
+    /* the GEMM's split tiles (rows [split_row0, split_row0 + 128 * split_rem)):
+     * int32 partial dots [split_rem][split_chunks][split_n][128], or null */
+    const int *split_part;
+    int split_rem, split_chunks, split_n, split_row0;
+    const float *scale_w, *scale_x;
     int wide_cap;              /* explicit rows of the wide path (>= max k - 1) */
     unsigned long long *host_tok; /* [B] completion words in mapped host memory, or null */
     const unsigned *seq_in;
@@ -546,6 +609,48 @@ __global__ void __launch_bounds__(NT, 1) batch_select_kernel(const __grid_consta
         for (int j = 0; j < kGroupRegs; ++j) {
             const int g = j * NT + tid;
             gpre[j] = g < p.n_groups ? __ldcg(gm + g) : 0u;
+        }
+    }
+    /* the GEMM's split tiles: this stream's rows of them are the sums of
+     * their K chunks' partial dots (int32, exact in any order), scaled like
+     * every other logit (runtime/lal_q8_kernel.h:489), with their groups'
+     * maxima (which replace the ones just loaded); before the penalty,
+     * which may change them */
+    if (p.split_part != nullptr) {
+        __shared__ uint32_t s_split_gmax[kSplitGroupsMax];
+        const int R = p.split_rem * kBM; /* a multiple of 32, as NT: whole warps */
+        const int g0 = p.split_row0 >> 5;
+        const float sxb = __ldcg(p.scale_x + b);
+        const size_t cstride = (size_t)p.split_n * kBM;
+        for (int i = tid; i < R; i += NT) {
+            const int *src = p.split_part +
+                             ((size_t)(i >> 7) * p.split_chunks * p.split_n + b) * kBM + (i & 127);
+            /* every chunk's load in flight at once */
+            int v[kSplitChunksMax];
+#pragma unroll
+            for (int c = 0; c < kSplitChunksMax; ++c)
+                v[c] = c < p.split_chunks ? __ldcg(src + c * cstride) : 0;
+            int dot = 0;
+#pragma unroll
+            for (int c = 0; c < kSplitChunksMax; ++c) dot += v[c];
+            const int row = p.split_row0 + i;
+            const bool in = row < p.rows;
+            const float sw = in ? __ldg(p.scale_w + row) : 0.0f;
+            const float l = __fmul_rn(__fmul_rn(sxb, sw), __int2float_rn(dot));
+            if (in) lg[row] = l;
+            const uint32_t gm = __reduce_max_sync(0xffffffffu, in ? f2key(l) : 0u);
+            if ((tid & 31) == 0) {
+                p.gmax[(size_t)b * p.n_groups + (row >> 5)] = gm;
+                s_split_gmax[(row >> 5) - g0] = gm;
+            }
+        }
+        __syncthreads();
+        if (gpre_ok) {
+#pragma unroll
+            for (int j = 0; j < kGroupRegs; ++j) {
+                const int g = j * NT + tid;
+                if (g >= g0 && g < g0 + 4 * p.split_rem) gpre[j] = s_split_gmax[g - g0];
+            }
         }
     }
     if (use_pen) {
@@ -1146,10 +1251,48 @@ bool encode_i8(CUtensorMap *m, const void *base, int dim0, int dim1, int pitch, 
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+/* The tiles left over after the GEMM's last whole wave, split along K: rem
+ * tiles in `chunks` chunks of `cb` boxes, one chunk a CTA (rem * chunks <=
+ * grid), so the slowest CTA streams cb boxes more than the others instead
+ * of a whole tile (kblocks boxes) more.  The partial dots, rem * chunks *
+ * 128 * N ints, are kept to about 2^20 by longer chunks at large N: the
+ * select adds each stream's share.  rem = 0: nothing is split. */
+constexpr long kSplitPartsMax = 1l << 20;
+struct SplitShape {
+    int rem, chunks, cb;
+};
+SplitShape split_shape(int rows, int kblocks, int num_sms, int N) {
+    const int n_tiles = (rows + kBM - 1) / kBM;
+    const int grid = std::min(n_tiles, num_sms);
+    SplitShape sh = {0, 0, 0};
+    const int rem = grid > 0 ? n_tiles % grid : 0;
+    if (rem == 0) return sh;
+    const long per_chunk = (long)rem * kBM * std::max(1, N);
+    const int by_adds = (int)std::min<long>(kblocks, std::max<long>(2, kSplitPartsMax / per_chunk));
+    const int want = std::min({grid / rem, by_adds, kSplitChunksMax});
+    if (want < 2) return sh;
+    const int cb = (kblocks + want - 1) / want;
+    const int chunks = (kblocks + cb - 1) / cb;
+    if (chunks < 2 || rem * chunks > grid || 4 * rem > kSplitGroupsMax) return sh;
+    sh.rem = rem;
+    sh.chunks = chunks;
+    sh.cb = cb;
+    return sh;
+}
+
 }  // namespace
 
 /* ---- the batched step, as seen by tail_api.cu ---- */
 int batch_n_for(int B) { return (B + 31) / 32 * 32; }
+
+size_t batch_split_bytes(int rows, int ld, int num_sms, int max_B) {
+    size_t ints = 0;
+    for (int N = 32; N <= batch_n_for(max_B); N += 32) {
+        const SplitShape sh = split_shape(rows, (ld + kBK - 1) / kBK, num_sms, N);
+        ints = std::max(ints, (size_t)sh.rem * sh.chunks * N * kBM);
+    }
+    return 4 * ints;
+}
 
 size_t batch_select_smem(int s_cap, int c_cap, int h_slots, int n_groups) {
     const size_t fixed = 4ull * 4096 + 8ull * s_cap + 20ull * c_cap + 4ull * n_groups;
@@ -1157,8 +1300,8 @@ size_t batch_select_smem(int s_cap, int c_cap, int h_slots, int n_groups) {
 }
 
 int batch_plan(BatchPlan &bp, const int8_t *W, const float *scale_w, int rows, int ld,
-               int num_sms, int8_t *xq, float *sx, uint32_t *gmax, int max_B, int hist_cap,
-               int max_top_k) {
+               int num_sms, int8_t *xq, float *sx, uint32_t *gmax, int *split_scratch,
+               int max_B, int hist_cap, int max_top_k) {
     memset(&bp, 0, sizeof(bp));
     if (!encoder()) return -3;
     if (ld < kBK || ld % 16 != 0 || max_B < 2 || max_B > 256 || rows < 1) return -1;
@@ -1172,6 +1315,11 @@ int batch_plan(BatchPlan &bp, const int8_t *W, const float *scale_w, int rows, i
     bp.n_groups = batch_groups(rows);
     bp.num_sms = num_sms;
     bp.kblocks = (ld + kBK - 1) / kBK;
+    if (split_scratch != nullptr) {
+        bp.split_part = split_scratch;
+        bp.split_ints = batch_split_bytes(rows, ld, num_sms, max_B) / 4;
+        bp.split_rem = split_shape(rows, bp.kblocks, num_sms, 32).rem;
+    }
     /* select capacities: superset, candidates, history hash (>= 2x the
      * history, a power of two) */
     /* superset >= the group maxima and 8x the largest k; candidates k plus
@@ -1239,6 +1387,16 @@ cudaError_t batch_launch(BatchPlan &bp, const BatchStep &s, cudaStream_t st) {
     if (e != cudaSuccess) return e;
     const int n_tiles = (bp.rows + kBM - 1) / kBM;
     const int grid = std::min(n_tiles, bp.num_sms);
+    g.reg_end = n_tiles;
+    const SplitShape sh = split_shape(bp.rows, bp.kblocks, bp.num_sms, N);
+    if (bp.split_part != nullptr && sh.rem > 0 && sh.rem == bp.split_rem &&
+        (size_t)sh.rem * sh.chunks * N * kBM <= bp.split_ints) {
+        g.reg_end = n_tiles - sh.rem;
+        g.split_units = sh.rem * sh.chunks;
+        g.split_chunks = sh.chunks;
+        g.split_cb = sh.cb;
+        g.split_part = bp.split_part;
+    }
     if (s.gemm_ev0) {
         e = cudaEventRecord(s.gemm_ev0, st);
         if (e != cudaSuccess) return e;
@@ -1289,6 +1447,15 @@ cudaError_t batch_launch(BatchPlan &bp, const BatchStep &s, cudaStream_t st) {
     q.wide_cap = bp.wide_cap;
     q.host_tok = s.shard_out ? nullptr : s.host_tok;
     q.seq_in = s.seq_in;
+    if (g.split_part != nullptr) {
+        q.split_part = g.split_part;
+        q.split_rem = n_tiles - g.reg_end;
+        q.split_chunks = g.split_chunks;
+        q.split_n = N;
+        q.split_row0 = g.reg_end * kBM;
+        q.scale_w = bp.scale_w;
+        q.scale_x = bp.sx;
+    }
     const size_t ssmem = batch_select_smem(bp.s_cap, bp.c_cap, bp.h_slots, bp.n_groups);
     e = raise_smem((const void *)batch_select_kernel, kGemmSmemLimit - 8192);
     if (e != cudaSuccess) return e;

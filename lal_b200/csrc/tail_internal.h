@@ -355,6 +355,11 @@ struct BatchPlan {
     alignas(64) unsigned char tm_x[8][128];
     unsigned x_ready;
     int w_ready;
+    /* the GEMM's split tiles (those left over after its last whole wave):
+     * int32 partial dots [rem][chunks][N][128] of a launch, or null */
+    int *split_part;
+    int split_rem;
+    size_t split_ints;
 };
 struct BatchStep {
     const float *hidden;
@@ -385,8 +390,11 @@ struct BatchStep {
 };
 /* 0 when the shape takes the batched path (d >= 128, 2 <= max_B <= 256). */
 int batch_plan(BatchPlan &bp, const int8_t *W, const float *scale_w, int rows, int ld,
-               int num_sms, int8_t *xq, float *sx, uint32_t *gmax, int max_B, int hist_cap,
-               int max_top_k);
+               int num_sms, int8_t *xq, float *sx, uint32_t *gmax, int *split_scratch,
+               int max_B, int hist_cap, int max_top_k);
+/* bytes of the GEMM's split scratch for this shape and up to max_B streams
+ * (0: no tile is split); each launch writes what it reads */
+size_t batch_split_bytes(int rows, int ld, int num_sms, int max_B);
 /* 32-row groups of a slice of `rows` rows (the gmax buffer holds 256 streams of them) */
 inline int batch_groups(int rows) { return (rows + 127) / 128 * 4; }
 cudaError_t batch_launch(BatchPlan &bp, const BatchStep &s, cudaStream_t st);
