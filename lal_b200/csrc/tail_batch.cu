@@ -701,6 +701,7 @@ __global__ void __launch_bounds__(NT, 1) batch_select_kernel(const __grid_consta
     };
     uint32_t L = 0u;
     int S = -1;
+    bool ordered = false; /* the superset is in vocab order (the group path) */
     /* with the penalised groups marked, only the groups free of penalised
      * rows count towards the bound: their maxima are unchanged logits of k
      * distinct rows, so the k-th largest of them is <= T; otherwise every
@@ -801,25 +802,20 @@ __global__ void __launch_bounds__(NT, 1) batch_select_kernel(const __grid_consta
         __syncthreads();
         L = ms->sh[0] << 20;
         for (int i = tid; i < 4096; i += NT) hist[i] = 0u; /* for the fallback */
-        /* the candidate groups, listed in Gl */
-        if (tid == 0) s_count = 0;
+        /* the candidate groups, listed in Gl in ascending order (a thread a
+         * contiguous run of groups: count, one scan, write), so that the
+         * superset gathered from them, and the candidates, are in vocab
+         * order without a sort */
+        const int gper = (p.n_groups + NT - 1) / NT;
+        const int ga = min(p.n_groups, tid * gper), gb = min(p.n_groups, ga + gper);
+        uint32_t gc = 0;
+        for (int g = ga; g < gb; ++g) gc += Gk[g] >= L;
+        uint32_t ngt;
+        uint32_t gpos = block_scan_excl(gc, ms, &ngt);
+        for (int g = ga; g < gb; ++g)
+            if (Gk[g] >= L) Gl[gpos++] = g;
         __syncthreads();
-        /* one shared-memory atomic per warp and round */
-        for (int g0 = 0; g0 < p.n_groups; g0 += NT) {
-            const int g = g0 + tid;
-            const bool hit = g < p.n_groups && Gk[g] >= L;
-            const unsigned bal = __ballot_sync(0xffffffffu, hit);
-            if (bal) {
-                const int lane = tid & 31;
-                int base = 0;
-                if (lane == 0) base = atomicAdd(&s_count, __popc(bal));
-                base = __shfl_sync(0xffffffffu, base, 0);
-                if (hit) Gl[base + __popc(bal & ((1u << lane) - 1u))] = g;
-            }
-        }
-        __syncthreads();
-        const int ng = s_count;
-        __syncthreads();
+        const int ng = (int)ngt;
         if (ng <= p.n_groups / 2) {
             if (tid == 0) s_count = 0;
             /* gather the groups' keys >= L (32 consecutive rows a group):
@@ -873,6 +869,7 @@ __global__ void __launch_bounds__(NT, 1) batch_select_kernel(const __grid_consta
                 batch_wide(p, b, k, greedy, temp, u0, hn, hhead, bsm, ms);
                 return;
             }
+            ordered = true;
         }
     }
     if (S < 0) {
@@ -1043,7 +1040,12 @@ __global__ void __launch_bounds__(NT, 1) batch_select_kernel(const __grid_consta
         }
     __syncthreads();
     /* ascending vocab order (the early weights move with their rows) */
-    if (m <= 64) {
+    if (ordered) {
+        for (int i = tid; i < m; i += NT) {
+            Oi[i] = Ci[i];
+            Ov[i] = Cv[i];
+        }
+    } else if (m <= 64) {
         int me = 0, r = 0;
         float mv = 0.0f, mw = 0.0f;
         if (tid < m) {
