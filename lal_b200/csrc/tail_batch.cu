@@ -62,6 +62,11 @@ constexpr int kGemmThreads = 192;  /* warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
 constexpr int kGemmStagesMax = 8;
 constexpr int kGemmSmemLimit = 232448;
 constexpr int kStageGroups = 512;  /* 32-row logit groups staged a round (select) */
+/* the smallest round tried when a step has more streams than SMs (the
+ * largest round, in steps of 32 groups, with which two select CTAs fit on
+ * one SM, so that every stream's CTA is resident at once instead of a
+ * second wave waiting for the first) */
+constexpr int kStageGroupsMin = 64;
 constexpr int kPenGroupWords = 512; /* bitmap words of groups holding a penalised row */
 constexpr int kSplitChunksMax = 32; /* K chunks of a split tile (the select keeps a row's in registers) */
 constexpr int kSplitGroupsMax = 4 * 74; /* 32-row groups of the split tiles (>= 2 chunks a tile, 148 SMs) */
@@ -464,6 +469,7 @@ struct BatchSelectParams {
     int split_rem, split_chunks, split_n, split_row0;
     const float *scale_w, *scale_x;
     int wide_cap;              /* explicit rows of the wide path (>= max k - 1) */
+    int stage_groups;          /* candidate groups staged a round */
     unsigned long long *host_tok; /* [B] completion words in mapped host memory, or null */
     const unsigned *seq_in;
 };
@@ -527,8 +533,8 @@ __global__ void __launch_bounds__(NT, 1) batch_select_kernel(const __grid_consta
     float *Ce = reinterpret_cast<float *>(Oi + p.c_cap);           /* weights, sums    */
     int *Gl = reinterpret_cast<int *>(Ce + p.c_cap);               /* candidate groups */
     /* one 16-byte aligned region, used twice: the history hash of the
-     * penalty (step 1), then the staging of kStageGroups candidate groups'
-     * 32 logits (step 3) */
+     * penalty (step 1), then the staging of p.stage_groups candidate groups'
+     * 32 logits a round (step 3) */
     uint8_t *shared2 = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(Gl + p.n_groups) + 15) & ~static_cast<uintptr_t>(15));
     uint32_t *hkey = reinterpret_cast<uint32_t *>(shared2);        /* history hash     */
@@ -819,13 +825,13 @@ __global__ void __launch_bounds__(NT, 1) batch_select_kernel(const __grid_consta
         if (ng <= p.n_groups / 2) {
             if (tid == 0) s_count = 0;
             /* gather the groups' keys >= L (32 consecutive rows a group):
-             * each round copies up to kStageGroups groups into shared memory
+             * each round copies up to p.stage_groups groups into shared memory
              * with 16-byte asynchronous copies, all in flight together (a
              * piece that is misaligned or crosses the slice end is read one
              * value at a time), then a warp takes a group a ballot */
             const bool al16 = (reinterpret_cast<uintptr_t>(lg) & 15u) == 0;
-            for (int c0 = 0; c0 < ng; c0 += kStageGroups) {
-                const int cn = min(kStageGroups, ng - c0);
+            for (int c0 = 0; c0 < ng; c0 += p.stage_groups) {
+                const int cn = min(p.stage_groups, ng - c0);
                 __syncthreads(); /* the previous round's staging is consumed */
                 for (int e = tid; e < cn * 8; e += NT) {
                     const int r = Gl[c0 + (e >> 3)] * 32 + (e & 7) * 4;
@@ -1296,9 +1302,10 @@ size_t batch_split_bytes(int rows, int ld, int num_sms, int max_B) {
     return 4 * ints;
 }
 
-size_t batch_select_smem(int s_cap, int c_cap, int h_slots, int n_groups) {
+size_t batch_select_smem(int s_cap, int c_cap, int h_slots, int n_groups,
+                         int stage_groups = kStageGroups) {
     const size_t fixed = 4ull * 4096 + 8ull * s_cap + 20ull * c_cap + 4ull * n_groups;
-    return (fixed + 15) / 16 * 16 + std::max(8ull * h_slots, 128ull * kStageGroups);
+    return (fixed + 15) / 16 * 16 + std::max(8ull * h_slots, 128ull * stage_groups);
 }
 
 int batch_plan(BatchPlan &bp, const int8_t *W, const float *scale_w, int rows, int ld,
@@ -1458,9 +1465,31 @@ cudaError_t batch_launch(BatchPlan &bp, const BatchStep &s, cudaStream_t st) {
         q.scale_w = bp.scale_w;
         q.scale_x = bp.sx;
     }
-    const size_t ssmem = batch_select_smem(bp.s_cap, bp.c_cap, bp.h_slots, bp.n_groups);
     e = raise_smem((const void *)batch_select_kernel, kGemmSmemLimit - 8192);
     if (e != cudaSuccess) return e;
+    /* one select CTA a stream: with more streams than SMs, the largest
+     * staging round that lets two CTAs share an SM, if any (decided once) */
+    if (s.B > bp.num_sms && bp.stage_groups_many == 0) {
+        bp.stage_groups_many = kStageGroups;
+        for (int sg = kStageGroups; sg >= kStageGroupsMin; sg -= 32) {
+            const size_t sm_bytes =
+                batch_select_smem(bp.s_cap, bp.c_cap, bp.h_slots, bp.n_groups, sg);
+            if (sm_bytes < (size_t)wide_area_bytes(bp.wide_cap)) break;
+            int per_sm = 0;
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+                    &per_sm, (const void *)batch_select_kernel, NT, sm_bytes) != cudaSuccess) {
+                (void)cudaGetLastError(); /* the failed query leaves no error behind */
+                break;
+            }
+            if (per_sm >= 2) {
+                bp.stage_groups_many = sg;
+                break;
+            }
+        }
+    }
+    q.stage_groups = s.B > bp.num_sms ? bp.stage_groups_many : kStageGroups;
+    const size_t ssmem =
+        batch_select_smem(bp.s_cap, bp.c_cap, bp.h_slots, bp.n_groups, q.stage_groups);
     void *args[] = {&q};
     return launch_dependent((const void *)batch_select_kernel, s.B, NT, ssmem, st, args);
 }

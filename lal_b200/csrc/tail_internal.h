@@ -350,6 +350,10 @@ struct BatchPlan {
     int n_groups;
     int s_cap, c_cap, h_slots;
     int wide_cap; /* explicit rows of the select's wide path */
+    /* candidate groups the select stages a round when a step has more
+     * streams than SMs (0 = not chosen yet): the smaller round that lets two
+     * select CTAs share an SM, when they fit */
+    int stage_groups_many;
     /* TMA descriptors (CUtensorMap, 128 bytes each): W, and X for N = 32..256 */
     alignas(64) unsigned char tm_w[128];
     alignas(64) unsigned char tm_x[8][128];
