@@ -603,6 +603,9 @@ def run_ours(args, cfg):
         if world > 1 and not peer:
             launches_per_step += 1  # the merge (the NCCL all-gather is not ours)
         achieved = alg / (kern_ms * 1e-3) / 1e9
+        # lal_tail_step hands the token back through a mapped completion word
+        # (the library's own samplers, unsharded or peer-exchange steps)
+        notified = not gpt2 and (world == 1 or peer)
         peak = float(peaks["hbm_gbs"])
         traffic = load_traffic(cfg.name, world)
         tokens = K * B
@@ -614,12 +617,14 @@ def run_ours(args, cfg):
             "config": {**workload(cfg, world),
                        **({"sampler": args.sampler} if args.sampler != "library" else {})},
             "e2e": {"value": round(tokens / (e2e_ms * 1e-3), 3), "unit": "tokens/s",
-                    # unsharded: hidden + draws + the step number pulled from
-                    # pinned memory, one 8-byte completion word per stream
-                    # written back; sharded: the copies of lal_tail_step
+                    # unsharded, or one stream on peer-connected shards:
+                    # hidden + draws + the step number pulled from pinned
+                    # memory, one 8-byte completion word per stream written
+                    # back; otherwise copies of hidden + draws up and of the
+                    # tokens + status word down
                     "h2d_bytes_per_step": int(hid[0].nbytes + us[0].nbytes
-                                              + (4 if world == 1 else 0)),
-                    "d2h_bytes_per_step": int(8 * B if world == 1 else 4 * B + 4),
+                                              + (4 if notified else 0)),
+                    "d2h_bytes_per_step": int(8 * B if notified else 4 * B + 4),
                     "path": "lal_tail_step (C ABI) from host arrays" if c_step is not None
                             else "ShardedDecodeTail.step (stage, select, NCCL all-gather, "
                                  "merge, fetch)"},

@@ -1737,7 +1737,8 @@ int step_status_error(lal_tail *t, int status) {
                                                : "candidate set above the built capacity");
 }
 
-/* lal_tail_step of an unsharded context: the inputs are staged in mapped
+/* lal_tail_step of an unsharded context, or of one stream on a vocab shard
+ * connected to its peers: the inputs are staged in mapped
  * pinned memory and pulled onto the device by a small kernel (the step's
  * kernel begins streaming the LM head meanwhile), and each stream's kernel
  * stores [step number | token] into a mapped completion word that this
@@ -1831,7 +1832,11 @@ int lal_tail_step(lal_tail *t, const float *hidden, int n_streams, const float *
         return LAL_TAIL_OK;
     }
     const int B = t->cfg.max_streams, d = t->cfg.n_embd;
-    if (t->cfg.shard_count == 1 && t->cfg.sampler != LAL_SAMPLER_GPT2)
+    /* unsharded steps, and single-stream steps of a vocab shard connected to
+     * its peers (one kernel per rank draws the token): inputs pulled from
+     * mapped memory, the token handed back through the completion word */
+    if (t->cfg.sampler != LAL_SAMPLER_GPT2 &&
+        (t->cfg.shard_count == 1 || (t->p2p && n_streams == 1)))
         return notified_step(t, hidden, n_streams, u, tokens_out);
     CHECK(upload_inputs(t, hidden, n_streams, u));
     CHECK(enqueue_step(t, t->io_in, n_streams, t->io_in + (size_t)B * d, t->io_out));

@@ -203,8 +203,13 @@ struct PeerRecords {
 
 /* The peer exchange's merge of this step (the fused kernel's last CTA, after
  * it published its record): wait for every rank's record, merge and draw
- * like merge_kernel. */
+ * like merge_kernel.  With a host waiting on the step's completion word
+ * (lal_tail_step), thread 0 -- the thread that writes the token on every
+ * path of the merge -- then hands it the token, or -1 when the step failed
+ * (the host then reads the status); the token slot is set to -1 first, so
+ * no path can pass on an earlier step's token. */
 __device__ __noinline__ void peer_merge(const TailParams &p, uint8_t *smem, Misc *ms) {
+    if (threadIdx.x == 0 && p.host_tok != nullptr) p.tokens[0] = -1;
     MergeParams mp;
     mp.recv = p.peer_recv[p.rank] + (size_t)(p.seq & 1u) * p.n_ranks * p.rec_bytes;
     mp.rank_stride = p.rec_bytes;
@@ -234,6 +239,8 @@ __device__ __noinline__ void peer_merge(const TailParams &p, uint8_t *smem, Misc
     mp.smem_cap = (p.area_bytes - kMergeHead - kWideWalkBytes) / 24;
     mp.phase_ts = p.phase_ts ? p.phase_ts + ((size_t)gridDim.x + 1) * 8 : nullptr;
     merge_sample(mp, 0, smem, ms, PeerRecords{p, ms});
+    if (threadIdx.x == 0 && p.host_tok != nullptr)
+        notify_host(p.host_tok, __ldcg(p.seq_in), p.tokens[0]);
 }
 
 /* The wide path (tail_wide.cuh) of a launch whose candidates did not fit the
