@@ -227,7 +227,11 @@ int lal_tail_sync(lal_tail *t);
 /* Host staging of one step's inputs (pinned copy, then one H2D into the
  * context's device buffers, see lal_tail_device_buffers) and the matching
  * read of the tokens (D2H + wait + status check).  lal_tail_step is
- * stage_inputs + the step on the device buffers + fetch_tokens. */
+ * stage_inputs + the step on the device buffers + fetch_tokens for GPT-2
+ * sampler contexts and for shards that are not peer-connected; otherwise
+ * (unsharded, or one stream on peer-connected shards) a small kernel pulls
+ * the inputs from mapped pinned memory and the token comes back in a mapped
+ * completion word that the calling thread waits on. */
 int lal_tail_stage_inputs(lal_tail *t, const float *hidden, int n_streams, const float *u);
 int lal_tail_fetch_tokens(lal_tail *t, int n_streams, int *tokens_out);
 
