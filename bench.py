@@ -71,6 +71,12 @@ def algorithmic_bytes(cfg, B, rows=None):
     return V * cfg.n_embd + 4 * V + B * (4 * cfg.n_embd + 4 * cfg.hist + 4)
 
 
+def cpu_gbs(cfg, tokens_per_s):
+    """A CPU rate as the algorithmic bytes of the whole vocabulary it streams:
+    (V*d + 4V + B*(4d + 4H + 4)) per step of B tokens, in GB/s."""
+    return round(tokens_per_s / cfg.streams * algorithmic_bytes(cfg, cfg.streams) / 1e9, 3)
+
+
 INT8_DENSE_TOPS_NOMINAL = 4500.0  # B200 dense int8 (no measured int8 figure)
 
 
@@ -323,7 +329,7 @@ def run_reference_arm(args, cfg):
         "config": {**workload(cfg, args.gpus),
                    **({"sampler": args.sampler} if args.sampler != "library" else {})},
         "cpu_baseline": {"value": round(val, 3), "unit": "tokens/s", "cores": cores,
-                         "kind": kind, "host": host_cpu(),
+                         "kind": kind, "host": host_cpu(), "gbs": cpu_gbs(cfg, val),
                          "sample": f"{done} full decode-tail steps of {cfg.name} "
                                    + ("(gpt2_server.c's lm_head_int8_parallel and the "
                                       "restated sampler of :2862-3013)"
@@ -658,11 +664,11 @@ def run_ours(args, cfg):
                                           args.cpu_seconds, args.sampler)
         val1, _, done1, _ = cpu_tail(cfg, q, s, 10_000, 1, args.cpu_seconds / 2, args.sampler)
         out["cpu_baseline"] = {"value": round(val, 3), "unit": "tokens/s", "cores": cores,
-                               "kind": kind,
+                               "kind": kind, "gbs": cpu_gbs(cfg, val),
                                "sample": f"{done} decode-tail steps of {cfg.name} "
                                          f"(~{args.cpu_seconds:.0f} s bound)",
                                "one_thread": {"value": round(val1, 3), "unit": "tokens/s",
-                                              "cores": 1,
+                                              "cores": 1, "gbs": cpu_gbs(cfg, val1),
                                               "sample": f"{done1} steps "
                                                         f"(~{args.cpu_seconds / 2:.0f} s bound)"},
                                "host": host_cpu()}
