@@ -252,3 +252,31 @@ def test_port_matches_reference_on_exact_ties():
                 g = synth.GlibcStream(seed, private=False)
                 got_s, _, _ = oracle.sample_filtered(lg, temp, 40, 1.1, rec, draw=g.next_u)
                 assert got_s == want_s, (seed, temp)
+
+
+@pytest.mark.skipif(not oracle.have_ref(), reason="oracle/_ref not built (no reference checkout)")
+def test_port_matches_reference_at_extreme_temperatures_and_scales():
+    """Temperatures from 1e-3 (every weight but the largest underflows to 0 or a
+    subnormal) to 1e3 (all weights near 1), and logits from 1e-30 to 1e30 in
+    magnitude: the restatement's weights, sums and draws are the reference's
+    (runtime/lal_sampling.h:106-124), for both samplers."""
+    R = oracle.ref()
+    rng = np.random.default_rng(99)
+    trial = 0
+    for scale in (1e-30, 1e-3, 1.0, 1e4, 1e30):
+        for T in (1e-3, 0.05, 0.7, 30.0, 1e3):
+            V = int(rng.integers(50, 3000))
+            k = int(rng.integers(1, 65))
+            lg = (rng.standard_normal(V) * scale).astype(np.float32)
+            rec = rng.integers(0, V, size=64).astype(np.int32)
+            for filt in (False, True):
+                R.ref_srand(trial)
+                tr, lr = oracle.ref_sample(lg, T, k, 1.1, rec, filtered=filt)
+                g = synth.GlibcStream(trial, private=False)
+                if filt:
+                    tp, lp, _ = oracle.sample_filtered(lg, T, k, 1.1, rec, draw=g.next_u)
+                else:
+                    tp, lp, _ = oracle.sample(lg, T, k, 1.1, rec, g.next_u())
+                assert tr == tp, (scale, T, filt)
+                np.testing.assert_array_equal(bits(lr), bits(lp))
+            trial += 1
