@@ -327,11 +327,23 @@ int registry_get(const int8_t *wte_q, const float *scale_w, int rows_needed, int
     h.ld = ld_for(d);
     h.rows = rows_needed;
     h.host_scale = scale_w;
-    CU(cudaMalloc(&h.W, (size_t)h.rows * h.ld));
-    CU(cudaMalloc(&h.sw, sizeof(float) * (size_t)h.rows));
-    CHECK(upload_rows(wte_q, h.rows, d, h.ld, h.W, 0));
-    CU(cudaMemcpy(h.sw, scale_w, sizeof(float) * (size_t)h.rows, cudaMemcpyHostToDevice));
-    CU(cudaDeviceSynchronize());
+    /* on any failure the new buffers are freed, the old entry stays */
+    int rc = LAL_TAIL_OK;
+    cudaError_t e = cudaMalloc(&h.W, (size_t)h.rows * h.ld);
+    if (e == cudaSuccess) e = cudaMalloc(&h.sw, sizeof(float) * (size_t)h.rows);
+    if (e == cudaSuccess) rc = upload_rows(wte_q, h.rows, d, h.ld, h.W, 0);
+    if (e == cudaSuccess && rc == LAL_TAIL_OK)
+        e = cudaMemcpy(h.sw, scale_w, sizeof(float) * (size_t)h.rows, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess && rc == LAL_TAIL_OK) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess || rc != LAL_TAIL_OK) {
+        if (e != cudaSuccess)
+            rc = fail(LAL_TAIL_ERR_CUDA, "LM head registry: %s", cudaGetErrorString(e));
+        cudaDeviceSynchronize(); /* no copy into the buffers may be in flight */
+        if (h.W) cudaFree(h.W);
+        if (h.sw) cudaFree(h.sw);
+        (void)cudaGetLastError(); /* reported through rc; leave no stale error behind */
+        return rc;
+    }
     if (it != g_reg.end()) {
         g_retired.push_back(it->second.W);
         g_retired.push_back(it->second.sw);
